@@ -1,0 +1,28 @@
+/* b200_compiler.h — compile-only entry point of the B200 plugin's StableHLO compiler.
+ *
+ * No counterpart in the reference (its compiler, src/jam/jam.cc:8-24, is reachable only through
+ * PJRT_Client_Compile).  It runs the same parse -> lower -> NVRTC pipeline as PJRT_Client_Compile
+ * without creating a client or touching a GPU, and reports the plan, so the compiler can be tested
+ * on hosts with no GPU.
+ */
+#ifndef B200_COMPILER_H_
+#define B200_COMPILER_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Compiles StableHLO MLIR text for `num_processes` ranks.  Writes a NUL-terminated report into
+ * out[0..out_size): on success the plan dump ("plan: ...\n" then one line per step); on failure
+ * "error: <message>".  Returns 0 on success, 1 on a compile error, -1 if `out` is too small.
+ * `nvrtc` = 0 skips the NVRTC step (parse + lower only). */
+__attribute__((visibility("default"))) int b200_compile_report(const char* text, size_t size, int num_processes,
+                                                               int nvrtc, char* out, size_t out_size);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_COMPILER_H_ */

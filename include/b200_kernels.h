@@ -1,0 +1,59 @@
+/* b200_kernels.h — direct C-ABI entry points to the plugin's hand-written sm_100a kernels.
+ *
+ * The drop-in boundary is `GetPjrtApi()` (include/pjrt_b200.h); these entry points expose the same
+ * kernels that PJRT_LoadedExecutable_Execute launches, on caller-owned device memory and a caller
+ * stream, so that tests and benchmarks can time one kernel on HBM-resident inputs.  They have no
+ * counterpart in the reference (whose kernels are MPSGraph nodes chosen inside Apple's framework);
+ * each comment names the reference call site whose work the kernel performs.
+ *
+ * All pointers are device pointers; `stream` is a cudaStream_t (NULL = legacy default stream).
+ * Element types use the PJRT_Buffer_Type codes below.  Functions return 0 on success, a negative
+ * code on invalid arguments or launch failure; asynchronous kernel faults are reported by
+ * b200_take_device_error().
+ */
+#ifndef B200_KERNELS_H_
+#define B200_KERNELS_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_API __attribute__((visibility("default")))
+
+#define B200_DT_F16 10  /* PJRT_Buffer_Type_F16 */
+#define B200_DT_F32 11  /* PJRT_Buffer_Type_F32 */
+#define B200_DT_BF16 13 /* PJRT_Buffer_Type_BF16 */
+#define B200_DT_S32 4   /* PJRT_Buffer_Type_S32 */
+#define B200_DT_S64 5   /* PJRT_Buffer_Type_S64 */
+
+/* C[b] = A[b] . B[b]^T : A [batch, M, K] and B [batch, N, K] row-major (K contiguous), C [batch, M, N].
+ * ab_type in {BF16, F16, F32}; out_type in {F32, BF16, F16}.  bf16/f16 with K % 8 == 0 run on the
+ * tcgen05 tensor-core kernel; other cases on a SIMT kernel.
+ * Replaces: DotGeneral's matmulWithPrimaryTensor, src/jam/ops/linalg.mm:47-105 (call at :98). */
+B200_API int b200_gemm(const void* A, const void* B, void* C, int64_t batch, int64_t M, int64_t N, int64_t K,
+              int ab_type, int out_type, void* stream);
+
+/* O = softmax(scale * Q K^T [causal mask]) V, fp32 softmax, for bf16 Q, K, V, O of shape [B, H, S, D]
+ * (D contiguous), D in {64, 128}, S a multiple of 128.  Fused flash-style kernel on tcgen05.
+ * Replaces: the dot_general -> softMaxWithTensor -> dot_general chain, src/jam/ops/linalg.mm:98 and
+ * src/jam/ops/elementwise.mm:71-89 (TrySoftmax). */
+B200_API int b200_attention_fwd(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D,
+                       int causal, float scale, void* stream);
+
+/* out[idx[i], :] += upd[i, :] for i < n_upd (rows of length row_len; out has `rows` rows; indices
+ * outside [0, rows) are skipped).  dtype in {F32, BF16}; idx_type in {S32, S64}.
+ * Replaces: Scatter (add region), src/jam/ops/gather_scatter.mm:262-335. */
+B200_API int b200_scatter_add_rows(const void* idx, const void* upd, void* out, int64_t n_upd, int64_t row_len, int64_t rows,
+                          int dtype, int idx_type, void* stream);
+
+/* Returns and clears the first error code recorded by a bounded wait inside a tensor-core kernel on
+ * the current device (0 = none).  Synchronizes the device. */
+B200_API int b200_take_device_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_KERNELS_H_ */

@@ -1,0 +1,46 @@
+// comm.h — the collective backend: NCCL over NVLink / NVSwitch, one rank per device.
+//
+// Replaces the reference's libmccl wrapper (src/mccl/collective/comm.h:14-40, collectives.h:33-56):
+// the same Create(n, rank) / typed AllReduce / AllGather / ReduceScatter surface, returning a status
+// string instead of aborting.  Bootstrap exchanges the NCCL unique id through a key-value callback
+// (the PJRT client's kv_put / kv_get, which the reference ignores, src/pjrt/api/pjrt_c_api.cc:239-266)
+// and initialises non-blocking so that a rank that never joins ends in a deadline error, not a hang.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <functional>
+#include <memory>
+#include <string>
+
+#include "../jam/ir.h"
+
+namespace b200 {
+
+struct KvStore {
+  std::function<std::string(const std::string& key, const std::string& value)> put;   // "" on success
+  std::function<std::string(const std::string& key, int timeout_ms, std::string* value)> get;
+};
+
+class Comm {
+ public:
+  // Creates the communicator of `world` ranks; every rank must call it.  `timeout_ms` bounds the
+  // wait for the other ranks.  On failure returns null and sets *err.
+  static std::unique_ptr<Comm> Create(int world, int rank, int device, const KvStore& kv, int timeout_ms,
+                                      std::string* err);
+  ~Comm();
+
+  int rank() const { return rank_; }
+  int world() const { return world_; }
+
+  std::string AllReduce(const void* send, void* recv, size_t count, DT dt, ReduceKind op, cudaStream_t st);
+  std::string AllGather(const void* send, void* recv, size_t send_count, DT dt, cudaStream_t st);
+  std::string ReduceScatter(const void* send, void* recv, size_t recv_count, DT dt, ReduceKind op, cudaStream_t st);
+
+ private:
+  Comm() = default;
+  void* comm_ = nullptr;  // ncclComm_t
+  int rank_ = 0, world_ = 1;
+};
+
+}  // namespace b200

@@ -1,0 +1,1384 @@
+// lower.cc — StableHLO graph -> B200 plan: pattern matching, fusion decisions and CUDA C codegen.
+//
+// Follows the reference's lowering walk (src/jam/lower.mm:208-314, :460-566) in what it accepts and
+// how it treats shard_map and collectives, but emits different work:
+//   * `dot_general` -> a GemmStep (tcgen05 GEMM; operands brought to K-major [batch, rows, K] first,
+//     the canonicalisation of src/jam/ops/linalg.mm:68-104);
+//   * the dot_general -> (scale) -> (causal select) -> softmax -> dot_general chain -> one fused
+//     AttentionStep (the reference only matches the softmax, src/jam/ops/elementwise.mm:71-89);
+//   * chains of elementwise / broadcast / convert / index-map ops -> generated loop kernels, and
+//     `reduce` -> generated row / column reduction kernels with the producer chain inlined;
+//   * all_reduce / all_gather / reduce_scatter -> CollectiveSteps (NCCL); with one rank they are
+//     identities (lower.mm:346-352); all_gather / reduce_scatter only along dim 0 (lower.mm:391-410).
+// An op outside the supported set fails compilation with its name (lower.mm:309).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <functional>
+#include <set>
+#include <sstream>
+#include <unordered_map>
+#include <unordered_set>
+
+#include "plan.h"
+
+namespace b200 {
+namespace {
+
+struct LowerError {
+  std::string msg;
+};
+
+// ------------------------------------------------------------------------------------ op classes
+const std::unordered_set<std::string> kBinary = {
+    "add", "subtract", "multiply", "divide", "maximum", "minimum", "power", "remainder",
+    "atan2", "and", "or", "xor", "shift_left", "shift_right_logical", "shift_right_arithmetic"};
+const std::unordered_set<std::string> kUnary = {
+    "negate", "exponential", "exponential_minus_one", "log", "log_plus_one", "tanh", "sqrt",
+    "rsqrt", "cbrt", "abs", "sine", "cosine", "tan", "floor", "ceil", "sign", "round_nearest_even",
+    "round_nearest_afz", "logistic", "not", "is_finite", "popcnt"};
+const std::unordered_set<std::string> kIndexMap = {
+    "broadcast_in_dim", "reshape", "transpose", "slice", "concatenate", "pad", "iota",
+    "constant", "convert", "bitcast_convert", "gather", "reverse"};
+const std::unordered_set<std::string> kAliasCustom = {"Sharding", "SPMDFullToShardShape", "SPMDShardToFullShape"};
+
+bool IsElementwise(const Op* op) {
+  return kBinary.count(op->name) || kUnary.count(op->name) || kIndexMap.count(op->name) ||
+         op->name == "compare" || op->name == "select" || op->name == "clamp";
+}
+bool IsAlias(const Op* op) {
+  if (op->name == "custom_call") {
+    auto it = op->strs.find("call_target_name");
+    return it != op->strs.end() && kAliasCustom.count(it->second);
+  }
+  return op->name == "optimization_barrier";
+}
+
+// ------------------------------------------------------------------------------------ C helpers
+std::string CType(DT t) {   // register ("compute") type
+  switch (t) {
+    case DT::kPred: return "bool";
+    case DT::kS8: case DT::kS16: case DT::kS32: return "int";
+    case DT::kS64: return "long long";
+    case DT::kU8: case DT::kU16: case DT::kU32: return "unsigned";
+    case DT::kU64: return "unsigned long long";
+    case DT::kF16: case DT::kBF16: case DT::kF32: return "float";
+    case DT::kF64: return "double";
+    default: return "void";
+  }
+}
+std::string MemType(DT t) {  // storage type
+  switch (t) {
+    case DT::kPred: return "unsigned char";
+    case DT::kS8: return "signed char";
+    case DT::kS16: return "short";
+    case DT::kS32: return "int";
+    case DT::kS64: return "long long";
+    case DT::kU8: return "unsigned char";
+    case DT::kU16: return "unsigned short";
+    case DT::kU32: return "unsigned";
+    case DT::kU64: return "unsigned long long";
+    case DT::kF16: case DT::kBF16: return "unsigned short";
+    case DT::kF32: return "float";
+    case DT::kF64: return "double";
+    default: return "void";
+  }
+}
+std::string LoadExpr(DT t, const std::string& ptr, const std::string& idx) {
+  std::string raw = ptr + "[" + idx + "]";
+  if (t == DT::kBF16) return "bf2f(" + raw + ")";
+  if (t == DT::kF16) return "h2f(" + raw + ")";
+  if (t == DT::kPred) return "(" + raw + " != 0)";
+  return "(" + CType(t) + ")" + raw;
+}
+std::string StoreExpr(DT t, const std::string& v) {
+  if (t == DT::kBF16) return "f2bf(" + v + ")";
+  if (t == DT::kF16) return "f2h(" + v + ")";
+  if (t == DT::kPred) return "(unsigned char)(" + v + ")";
+  return "(" + MemType(t) + ")(" + v + ")";
+}
+
+std::string FloatLit(double d) {
+  float f = (float)d;
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  char buf[48];
+  std::snprintf(buf, sizeof(buf), "__int_as_float(0x%08x)", u);
+  return buf;
+}
+std::string DoubleLit(double d) {
+  uint64_t u;
+  std::memcpy(&u, &d, 8);
+  char buf[64];
+  std::snprintf(buf, sizeof(buf), "__longlong_as_double(0x%016llxLL)", (unsigned long long)u);
+  return buf;
+}
+std::string Literal(DT t, double v) {
+  if (t == DT::kF32 || t == DT::kBF16 || t == DT::kF16) return FloatLit(v);
+  if (t == DT::kF64) return DoubleLit(v);
+  if (t == DT::kPred) return v != 0 ? "true" : "false";
+  if (DTIsUnsigned(t)) return std::to_string((unsigned long long)v) + "ULL";
+  return "(" + CType(t) + ")(" + std::to_string((long long)v) + "LL)";
+}
+
+const char* kPrelude = R"(
+// ---- generated by the B200 PJRT plugin (sm_100a) ----
+__device__ __forceinline__ float bf2f(unsigned short h) { return __uint_as_float(((unsigned)h) << 16); }
+__device__ __forceinline__ unsigned short f2bf(float f) {
+  unsigned short r; asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(f)); return r; }
+__device__ __forceinline__ float h2f(unsigned short h) {
+  float f; asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h)); return f; }
+__device__ __forceinline__ unsigned short f2h(float f) {
+  unsigned short r; asm("cvt.rn.f16.f32 %0, %1;" : "=h"(r) : "f"(f)); return r; }
+__device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
+__device__ __forceinline__ float rhf(float f) { return h2f(f2h(f)); }
+__device__ __forceinline__ float fmax_n(float a, float b) { return (a != a || b != b) ? __int_as_float(0x7fc00000) : fmaxf(a, b); }
+__device__ __forceinline__ float fmin_n(float a, float b) { return (a != a || b != b) ? __int_as_float(0x7fc00000) : fminf(a, b); }
+__device__ __forceinline__ double dmax_n(double a, double b) { return (a != a || b != b) ? __longlong_as_double(0x7ff8000000000000LL) : fmax(a, b); }
+__device__ __forceinline__ double dmin_n(double a, double b) { return (a != a || b != b) ? __longlong_as_double(0x7ff8000000000000LL) : fmin(a, b); }
+template <typename T> __device__ __forceinline__ T imax(T a, T b) { return a > b ? a : b; }
+template <typename T> __device__ __forceinline__ T imin(T a, T b) { return a < b ? a : b; }
+__device__ __forceinline__ float fsign(float x) { return x > 0.f ? 1.f : (x < 0.f ? -1.f : x); }
+__device__ __forceinline__ float frne(float x) { return rintf(x); }
+__device__ __forceinline__ float fafz(float x) { return roundf(x); }
+__device__ __forceinline__ float flogistic(float x) { return 1.f / (1.f + expf(-x)); }
+__device__ __forceinline__ float warp_sum(float v) { for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o); return v; }
+__device__ __forceinline__ double warp_sum(double v) { for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o); return v; }
+)";
+
+// ------------------------------------------------------------------------------------ codegen
+// Emits the per-element expression of a fusion: values that are not materialized are computed
+// inline from their operands; materialized values are loaded from their slot.
+struct Gen {
+  const std::vector<int>* slot_of;        // value id -> slot (-1 if not materialized)
+  std::vector<int> in_slots;              // kernel input params (slots)
+  std::unordered_map<int, int> param_of;  // slot -> param index
+  std::unordered_map<std::string, std::string> cse;
+  std::unordered_map<int, std::string> group_regs;  // slot of a group member -> its register
+  std::vector<std::string> identity;      // loop index names of the current group shape
+  std::vector<int64_t> group_dims;
+  bool conflict = false;
+  std::ostringstream body;
+  int tmp = 0;
+  std::string indent = "    ";
+
+  std::string Var(DT t, const std::string& expr) {
+    std::string n = "t" + std::to_string(tmp++);
+    body << indent << CType(t) << " " << n << " = " << expr << ";\n";
+    return n;
+  }
+
+  std::string Param(int slot) {
+    auto it = param_of.find(slot);
+    if (it != param_of.end()) return "in" + std::to_string(it->second);
+    int k = (int)in_slots.size();
+    in_slots.push_back(slot);
+    param_of[slot] = k;
+    return "in" + std::to_string(k);
+  }
+
+  static std::string Linear(const std::vector<std::string>& idx, const std::vector<int64_t>& dims) {
+    if (dims.empty()) return "0";
+    std::string s;
+    for (size_t k = 0; k < dims.size(); ++k) {
+      if (k == 0) s = "(long long)(" + idx[0] + ")";
+      else if (dims[k] == 1) s = "(" + s + ")";
+      else s = "(" + s + ")*" + std::to_string(dims[k]) + "LL+(" + idx[k] + ")";
+    }
+    return s;
+  }
+
+  std::string Round(DT t, const std::string& v) {
+    if (t == DT::kBF16) return Var(t, "rbf(" + v + ")");
+    if (t == DT::kF16) return Var(t, "rhf(" + v + ")");
+    return v;
+  }
+
+  std::string Emit(const Value* v, const std::vector<std::string>& idx) {
+    std::string key = std::to_string(v->id);
+    for (auto& s : idx) key += "|" + s;
+    auto hit = cse.find(key);
+    if (hit != cse.end()) return hit->second;
+    std::string r = EmitUncached(v, idx);
+    cse[key] = r;
+    return r;
+  }
+
+  std::string EmitUncached(const Value* v, const std::vector<std::string>& idx) {
+    const TensorType& ty = v->type;
+    int slot = (*slot_of)[v->id];
+    if (slot >= 0) {
+      auto g = group_regs.find(slot);
+      if (g != group_regs.end()) {
+        if (idx == identity && ty.dims == group_dims) return g->second;
+        conflict = true;
+      }
+      return Var(ty.dt, LoadExpr(ty.dt, Param(slot), Linear(idx, ty.dims)));
+    }
+    const Op* op = v->def;
+    if (!op) throw LowerError{"internal: unmaterialized argument"};
+    const std::string& n = op->name;
+    auto opnd = [&](int k, const std::vector<std::string>& i) { return Emit(op->operands[k], i); };
+    if (IsAlias(op)) return opnd(0, idx);
+    if (n == "constant") {
+      if (!op->splat) throw LowerError{"internal: non-splat constant not materialized"};
+      return Literal(ty.dt, ConstScalar(op));
+    }
+    if (n == "iota") {
+      int d = (int)op->ints.at("dim")[0];
+      return Var(ty.dt, "(" + CType(ty.dt) + ")(" + idx[d] + ")");
+    }
+    if (n == "broadcast_in_dim") {
+      const auto& dims = op->ints.at("dims");
+      const auto& in = op->operands[0]->type.dims;
+      std::vector<std::string> j(in.size());
+      for (size_t k = 0; k < in.size(); ++k) j[k] = (in[k] == 1 && ty.dims[dims[k]] != 1) ? "0" : idx[dims[k]];
+      return opnd(0, j);
+    }
+    if (n == "reshape" || (n == "bitcast_convert" && DTBytes(ty.dt) == DTBytes(op->operands[0]->type.dt) && false)) {
+      return opnd(0, Reindex(idx, ty.dims, op->operands[0]->type.dims));
+    }
+    if (n == "transpose") {
+      const auto& perm = op->ints.at("dims");
+      std::vector<std::string> j(perm.size());
+      for (size_t k = 0; k < perm.size(); ++k) j[perm[k]] = idx[k];
+      return opnd(0, j);
+    }
+    if (n == "reverse") {
+      const auto& dims = op->ints.at("dimensions");
+      std::vector<std::string> j = idx;
+      for (int64_t d : dims) j[d] = "(" + std::to_string(ty.dims[d] - 1) + "-(" + idx[d] + "))";
+      return opnd(0, j);
+    }
+    if (n == "slice") {
+      const auto& st = op->ints.at("start_indices");
+      const auto& sd = op->ints.at("strides");
+      std::vector<std::string> j(idx.size());
+      for (size_t k = 0; k < idx.size(); ++k)
+        j[k] = "(" + std::to_string(st[k]) + "+(" + idx[k] + ")*" + std::to_string(sd[k]) + ")";
+      return opnd(0, j);
+    }
+    if (n == "convert") {
+      DT from = op->operands[0]->type.dt, to = ty.dt;
+      std::string x = opnd(0, idx);
+      if (to == DT::kPred) return Var(to, "(" + x + " != 0)");
+      if (DTIsFloat(from) && !DTIsFloat(to)) {
+        // float -> int: truncate toward zero, NaN -> 0, saturate (cvt.rzi semantics)
+        if (from == DT::kF64) return Var(to, "(" + CType(to) + ")(" + x + ")");
+        return Var(to, "(" + CType(to) + ")(" + x + ")");
+      }
+      std::string c = "(" + CType(to) + ")(" + x + ")";
+      if (from == DT::kF64 && (to == DT::kBF16 || to == DT::kF16)) c = "(float)(" + x + ")";  // double rounding accepted
+      return Round(to, Var(to, c));
+    }
+    if (n == "compare") {
+      DT t = op->operands[0]->type.dt;
+      std::string a = opnd(0, idx), b = opnd(1, idx);
+      std::string d = op->strs.at("comparison_direction");
+      auto ct = op->strs.find("compare_type");
+      if (ct != op->strs.end() && ct->second == "UNSIGNED" && DTIsSigned(t)) {
+        std::string u = t == DT::kS64 ? "(unsigned long long)" : "(unsigned)";
+        a = u + a;
+        b = u + b;
+      }
+      static const std::map<std::string, std::string> sym = {
+          {"EQ", "=="}, {"NE", "!="}, {"LT", "<"}, {"LE", "<="}, {"GT", ">"}, {"GE", ">="}};
+      return Var(DT::kPred, "(" + a + " " + sym.at(d) + " " + b + ")");
+    }
+    if (n == "select") {
+      const auto& pd = op->operands[0]->type.dims;
+      std::string p = Emit(op->operands[0], pd.empty() ? std::vector<std::string>{} : idx);
+      std::string a = opnd(1, idx), b = opnd(2, idx);
+      return Var(ty.dt, "(" + p + " ? " + a + " : " + b + ")");
+    }
+    if (n == "clamp") {
+      auto sc = [&](int k) { return op->operands[k]->type.dims.empty() ? std::vector<std::string>{} : idx; };
+      std::string lo = Emit(op->operands[0], sc(0)), x = opnd(1, idx), hi = Emit(op->operands[2], sc(2));
+      if (DTIsFloat(ty.dt)) return Var(ty.dt, "fmin_n(fmax_n(" + x + ", " + lo + "), " + hi + ")");
+      return Var(ty.dt, "imin(imax(" + x + ", " + lo + "), " + hi + ")");
+    }
+    if (n == "concatenate") {
+      int d = (int)op->ints.at("dim")[0];
+      std::string r = "t" + std::to_string(tmp++);
+      body << indent << CType(ty.dt) << " " << r << ";\n";
+      int64_t off = 0;
+      std::string save = indent;
+      for (size_t k = 0; k < op->operands.size(); ++k) {
+        int64_t len = op->operands[k]->type.dims[d];
+        std::vector<std::string> j = idx;
+        j[d] = "((" + idx[d] + ")-" + std::to_string(off) + ")";
+        body << indent << (k ? "else " : "") << "if ((" << idx[d] << ") < " << off + len << ") {\n";
+        indent += "  ";
+        auto saved = cse;          // values computed inside a branch are not visible outside
+        std::string x = Emit(op->operands[k], j);
+        cse = saved;
+        body << indent << r << " = " << x << ";\n";
+        indent = save;
+        body << indent << "}\n";
+        off += len;
+      }
+      return r;
+    }
+    if (n == "pad") {
+      const auto& lo = op->ints.at("edge_padding_low");
+      const auto& it = op->ints.at("interior_padding");
+      std::string pv = Emit(op->operands[1], {});
+      std::string r = "t" + std::to_string(tmp++);
+      body << indent << CType(ty.dt) << " " << r << " = " << pv << ";\n";
+      const auto& in = op->operands[0]->type.dims;
+      std::string cond = "true";
+      std::vector<std::string> j(idx.size());
+      for (size_t k = 0; k < idx.size(); ++k) {
+        std::string q = "((" + idx[k] + ")-(" + std::to_string(lo[k]) + "))";
+        int64_t s = it[k] + 1;
+        cond += " && " + q + " >= 0 && " + q + " < " + std::to_string((in[k] - 1) * s + 1);
+        if (s > 1) cond += " && " + q + " % " + std::to_string(s) + " == 0";
+        j[k] = s > 1 ? "(" + q + "/" + std::to_string(s) + ")" : q;
+      }
+      body << indent << "if (" << cond << ") {\n";
+      std::string save = indent;
+      indent += "  ";
+      auto saved = cse;
+      std::string x = Emit(op->operands[0], j);
+      cse = saved;
+      body << indent << r << " = " << x << ";\n";
+      indent = save;
+      body << indent << "}\n";
+      return r;
+    }
+    if (n == "gather") {
+      // row take: table[V, D...] indexed by ids at the batch positions (see CheckGather)
+      const Value* table = op->operands[0];
+      const Value* ids = op->operands[1];
+      const auto& offset_dims = op->ints.at("offset_dims");
+      std::vector<std::string> bidx;
+      for (size_t k = 0; k < idx.size(); ++k)
+        if (std::find(offset_dims.begin(), offset_dims.end(), (int64_t)k) == offset_dims.end()) bidx.push_back(idx[k]);
+      bidx.push_back("0");   // index_vector_dim (size 1)
+      std::string id = Emit(ids, bidx);
+      int64_t V = table->type.dims[0];
+      std::string row = Var(DT::kS64, "(long long)(" + id + ") < 0 ? 0LL : ((long long)(" + id + ") > " +
+                                          std::to_string(V - 1) + "LL ? " + std::to_string(V - 1) + "LL : (long long)(" + id + "))");
+      std::vector<std::string> t{row};
+      for (size_t k = 0; k < offset_dims.size(); ++k) t.push_back(idx[offset_dims[k]]);
+      return Emit(table, t);
+    }
+    if (kUnary.count(n)) {
+      std::string x = opnd(0, idx);
+      DT t = ty.dt;
+      bool f = DTIsFloat(t), d = t == DT::kF64;
+      std::string e;
+      if (n == "negate") e = "-" + x;
+      else if (n == "abs") e = f ? (d ? "fabs(" + x + ")" : "fabsf(" + x + ")") : "(" + x + " < 0 ? -" + x + " : " + x + ")";
+      else if (n == "not") e = t == DT::kPred ? "!" + x : "~" + x;
+      else if (n == "is_finite") e = "isfinite(" + opnd(0, idx) + ")";
+      else if (n == "sign") e = d ? "(double)((" + x + " > 0) - (" + x + " < 0))" : f ? "fsign(" + x + ")" : "((" + x + " > 0) - (" + x + " < 0))";
+      else if (n == "popcnt") e = "__popc(" + x + ")";
+      else {
+        static const std::map<std::string, std::pair<std::string, std::string>> fn = {
+            {"exponential", {"expf", "exp"}}, {"exponential_minus_one", {"expm1f", "expm1"}},
+            {"log", {"logf", "log"}}, {"log_plus_one", {"log1pf", "log1p"}}, {"tanh", {"tanhf", "tanh"}},
+            {"sqrt", {"sqrtf", "sqrt"}}, {"rsqrt", {"rsqrtf", "rsqrt"}}, {"cbrt", {"cbrtf", "cbrt"}},
+            {"sine", {"sinf", "sin"}}, {"cosine", {"cosf", "cos"}}, {"tan", {"tanf", "tan"}},
+            {"floor", {"floorf", "floor"}}, {"ceil", {"ceilf", "ceil"}},
+            {"round_nearest_even", {"frne", "rint"}}, {"round_nearest_afz", {"fafz", "round"}},
+            {"logistic", {"flogistic", "flogistic"}}};
+        auto it = fn.find(n);
+        if (it == fn.end() || !f) throw LowerError{"unsupported elementwise op '" + n + "' for " + DTName(t)};
+        e = (d ? it->second.second : it->second.first) + "(" + x + ")";
+      }
+      if (n == "is_finite") return Var(DT::kPred, e);
+      return Round(t, Var(t, e));
+    }
+    if (kBinary.count(n)) {
+      std::string a = opnd(0, idx), b = opnd(1, idx);
+      DT t = ty.dt;
+      bool f = DTIsFloat(t), d = t == DT::kF64;
+      std::string e;
+      if (n == "add") e = a + " + " + b;
+      else if (n == "subtract") e = a + " - " + b;
+      else if (n == "multiply") e = t == DT::kPred ? a + " && " + b : a + " * " + b;
+      else if (n == "divide") e = f ? a + " / " + b : "(" + b + " == 0 ? (" + CType(t) + ")-1 : " + a + " / " + b + ")";
+      else if (n == "remainder") e = f ? (d ? "fmod(" : "fmodf(") + a + ", " + b + ")" : "(" + b + " == 0 ? " + a + " : " + a + " % " + b + ")";
+      else if (n == "maximum") e = f ? (d ? "dmax_n(" : "fmax_n(") + a + ", " + b + ")" : "imax(" + a + ", " + b + ")";
+      else if (n == "minimum") e = f ? (d ? "dmin_n(" : "fmin_n(") + a + ", " + b + ")" : "imin(" + a + ", " + b + ")";
+      else if (n == "power") e = f ? (d ? "pow(" : "powf(") + a + ", " + b + ")" : "";
+      else if (n == "atan2") e = (d ? "atan2(" : "atan2f(") + a + ", " + b + ")";
+      else if (n == "and") e = t == DT::kPred ? a + " && " + b : a + " & " + b;
+      else if (n == "or") e = t == DT::kPred ? a + " || " + b : a + " | " + b;
+      else if (n == "xor") e = t == DT::kPred ? a + " != " + b : a + " ^ " + b;
+      else if (n == "shift_left") e = a + " << " + b;
+      else if (n == "shift_right_logical") e = "(" + CType(t) + ")((unsigned" + std::string(DTBytes(t) == 8 ? " long long" : "") + ")" + a + " >> " + b + ")";
+      else if (n == "shift_right_arithmetic") e = a + " >> " + b;
+      if (e.empty()) throw LowerError{"unsupported op '" + n + "' for " + DTName(t)};
+      return Round(t, Var(t, e));
+    }
+    throw LowerError{"unsupported op '" + n + "' inside a fusion"};
+  }
+
+  // Index of a reshape operand from the index of its result (row-major linearisation).
+  std::vector<std::string> Reindex(const std::vector<std::string>& idx, const std::vector<int64_t>& out,
+                                   const std::vector<int64_t>& in) {
+    // fast path: only unit dims inserted/removed
+    std::vector<int> on, inn;
+    for (size_t k = 0; k < out.size(); ++k) if (out[k] != 1) on.push_back((int)k);
+    for (size_t k = 0; k < in.size(); ++k) if (in[k] != 1) inn.push_back((int)k);
+    bool same = on.size() == inn.size();
+    for (size_t k = 0; same && k < on.size(); ++k) same = out[on[k]] == in[inn[k]];
+    std::vector<std::string> j(in.size(), "0");
+    if (same) {
+      for (size_t k = 0; k < inn.size(); ++k) j[inn[k]] = idx[on[k]];
+      return j;
+    }
+    std::string lin = Var(DT::kS64, Linear(idx, out));
+    int64_t stride = 1;
+    for (int k = (int)in.size() - 1; k >= 0; --k) {
+      std::string e = "(int)((" + lin + " / " + std::to_string(stride) + "LL) % " + std::to_string(in[k]) + "LL)";
+      if (k == 0) e = "(int)(" + lin + " / " + std::to_string(stride) + "LL)";
+      j[k] = Var(DT::kS32, e);
+      stride *= in[k];
+    }
+    return j;
+  }
+};
+
+std::string KernelParams(const std::vector<int>& ins, int n_out, bool scratch) {
+  std::string s;
+  for (size_t k = 0; k < ins.size(); ++k) s += (k ? ", " : "") + std::string("const void* __restrict__ p") + std::to_string(k);
+  for (int k = 0; k < n_out; ++k) s += (s.empty() ? "" : ", ") + std::string("void* __restrict__ q") + std::to_string(k);
+  if (scratch) s += (s.empty() ? "" : ", ") + std::string("void* __restrict__ scratch");
+  return s;
+}
+
+std::string ParamCasts(const std::vector<int>& ins, const std::vector<DT>& in_dts, const std::vector<DT>& out_dts) {
+  std::ostringstream o;
+  for (size_t k = 0; k < ins.size(); ++k)
+    o << "  const " << MemType(in_dts[k]) << "* __restrict__ in" << k << " = (const " << MemType(in_dts[k]) << "*)p" << k << ";\n";
+  for (size_t k = 0; k < out_dts.size(); ++k)
+    o << "  " << MemType(out_dts[k]) << "* __restrict__ out" << k << " = (" << MemType(out_dts[k]) << "*)q" << k << ";\n";
+  return o.str();
+}
+
+// Delinearises loop variable `lin` over `dims` into named indices; returns the names.
+std::vector<std::string> Delinearize(std::ostringstream& o, const std::string& lin, const std::vector<int64_t>& dims,
+                                     const std::string& prefix, const std::string& ind, bool wide) {
+  std::vector<std::string> names(dims.size());
+  std::string it = wide ? "long long" : "unsigned";
+  std::string cur = prefix + "r";
+  o << ind << it << " " << cur << " = (" << it << ")(" << lin << ");\n";
+  for (int k = (int)dims.size() - 1; k >= 0; --k) {
+    names[k] = prefix + std::to_string(k);
+    if (k == 0) {
+      o << ind << "int " << names[k] << " = (int)" << cur << ";\n";
+    } else if (dims[k] == 1) {
+      o << ind << "const int " << names[k] << " = 0;\n";
+    } else {
+      o << ind << "int " << names[k] << " = (int)(" << cur << " % " << dims[k] << (wide ? "LL" : "u") << "); "
+        << cur << " /= " << dims[k] << (wide ? "LL" : "u") << ";\n";
+    }
+  }
+  return names;
+}
+
+// ------------------------------------------------------------------------------------ lowering
+class Lowerer {
+ public:
+  Lowerer(Graph& g, const CompileOptions& opt, Plan* p) : g_(g), opt_(opt), p_(p) {}
+
+  void Run() {
+    slot_of_.assign(g_.values.size(), -1);
+    dead_.assign(g_.ops.size(), false);
+    Retype();
+    if (opt_.fuse_attention) MatchAttention();
+    DecideMaterialization();
+    BindLeaves();
+    EmitSteps();
+    BindOutputs();
+    ComputeLastUse();
+    p_->cuda_source = std::string(kPrelude) + src_.str();
+    p_->num_partitions = g_.num_partitions;
+  }
+
+ private:
+  Graph& g_;
+  const CompileOptions& opt_;
+  Plan* p_;
+  std::vector<int> slot_of_;
+  std::vector<bool> dead_;
+  std::vector<bool> need_;                 // value must be materialized
+  std::unordered_map<int, AttentionStep> attn_;  // result value id of the 2nd dot -> matched attention
+  std::unordered_map<int, std::array<const Value*, 3>> attn_in_;
+  std::ostringstream src_;
+  int kcount_ = 0;
+
+  int NewSlot(int64_t bytes) {
+    p_->slots.push_back(Slot());
+    p_->slots.back().bytes = std::max<int64_t>(bytes, 0);
+    return (int)p_->slots.size() - 1;
+  }
+
+  const Value* Resolve(const Value* v) const {
+    while (v->def && IsAlias(v->def)) {
+      const Op* op = v->def;
+      size_t k = 0;
+      for (; k < op->results.size(); ++k) if (op->results[k] == v) break;
+      v = op->operands[std::min(k, op->operands.size() - 1)];
+    }
+    return v;
+  }
+
+  // shard_map: an argument that reaches SPMDFullToShardShape is passed per device at shard shape
+  // (the reference retypes the placeholder, src/jam/lower.mm:273-289).
+  void Retype() {
+    p_->arg_types.clear();
+    for (Value* a : g_.args) p_->arg_types.push_back(a->type);
+    for (auto& op : g_.ops) {
+      if (op->name != "custom_call" || op->strs["call_target_name"] != "SPMDFullToShardShape") continue;
+      const Value* src = Resolve(op->operands[0]);
+      if (src->arg_index >= 0) p_->arg_types[src->arg_index] = op->result()->type;
+    }
+  }
+
+  // ---------------------------------------------------------------- attention pattern
+  // dot(Q,K^T) [* scale] [select(causal, ., -inf)] -> max -> exp(x - max) -> sum -> div -> [convert] -> dot(., V)
+  static const Value* Through(const Value* v) {   // skip reshapes / broadcasts that only add unit dims
+    while (v->def && (v->def->name == "reshape" || v->def->name == "broadcast_in_dim") &&
+           v->def->operands[0]->type.numel() == v->type.numel())
+      v = v->def->operands[0];
+    return v;
+  }
+  static const Value* RowBroadcastOf(const Value* v) {  // broadcast_in_dim(x, dims=[0..r-2]) of a row vector
+    if (!v->def || v->def->name != "broadcast_in_dim") return nullptr;
+    const Value* x = Through(v->def->operands[0]);
+    return x;
+  }
+  static bool IsScalarConst(const Value* v, double* out) {
+    while (v->def && v->def->name == "broadcast_in_dim") v = v->def->operands[0];
+    if (!v->def || v->def->name != "constant" || !v->def->splat) return false;
+    *out = ConstScalar(v->def);
+    return true;
+  }
+  bool SingleUse(const Value* v) const { return v->users.size() == 1; }
+
+  void MatchAttention() {
+    for (auto& opp : g_.ops) {
+      Op* d2 = opp.get();
+      if (d2->name != "dot_general" || d2->operands.size() != 2) continue;
+      auto ints = [&](const Op* o, const char* k) {
+        auto it = o->ints.find(k);
+        return it == o->ints.end() ? std::vector<int64_t>{} : it->second;
+      };
+      const std::vector<int64_t> b01 = {0, 1};
+      if (ints(d2, "batching_dims.lhs") != b01 || ints(d2, "batching_dims.rhs") != b01) continue;
+      if (ints(d2, "contracting_dims.lhs") != std::vector<int64_t>{3} ||
+          ints(d2, "contracting_dims.rhs") != std::vector<int64_t>{2})
+        continue;
+      std::vector<const Op*> chain{d2};
+      const Value* p = d2->operands[0];
+      const Value* V = d2->operands[1];
+      if (p->def && p->def->name == "convert") { chain.push_back(p->def); if (!SingleUse(p)) continue; p = p->def->operands[0]; }
+      if (!p->def || p->def->name != "divide" || !SingleUse(p)) continue;
+      const Op* div = p->def;
+      chain.push_back(div);
+      const Value* e = div->operands[0];
+      const Value* sumb = div->operands[1];
+      if (!e->def || e->def->name != "exponential") continue;
+      // sum = reduce_add(e, dims=[3]) seen through reshapes/broadcasts
+      const Value* sum = RowBroadcastOf(sumb);
+      if (!sum || !sum->def || sum->def->name != "reduce" || sum->def->reduce != ReduceKind::kAdd) continue;
+      if (sum->def->operands[0] != e || ints(sum->def, "dimensions") != std::vector<int64_t>{3}) continue;
+      if (e->users.size() != 2) continue;
+      chain.push_back(e->def);
+      chain.push_back(sum->def);
+      for (const Value* x = sumb; x != sum; x = x->def->operands[0]) { if (x->users.size() != 1) goto next; chain.push_back(x->def); }
+      {
+        const Value* sub = e->def->operands[0];
+        if (!sub->def || sub->def->name != "subtract" || !SingleUse(sub)) continue;
+        chain.push_back(sub->def);
+        const Value* x = sub->def->operands[0];
+        const Value* maxb = sub->def->operands[1];
+        const Value* mx = RowBroadcastOf(maxb);
+        if (!mx || !mx->def || mx->def->name != "reduce" || mx->def->reduce != ReduceKind::kMax) continue;
+        if (mx->def->operands[0] != x || ints(mx->def, "dimensions") != std::vector<int64_t>{3}) continue;
+        if (x->users.size() != 2) continue;
+        chain.push_back(mx->def);
+        for (const Value* y = maxb; y != mx; y = y->def->operands[0]) { if (y->users.size() != 1) goto next; chain.push_back(y->def); }
+        bool causal = false;
+        double scale = 1.0;
+        const Value* s = x;
+        if (s->def && s->def->name == "select") {
+          // select(broadcast(compare(iota0 GE iota1)), s, -inf)
+          const Op* sel = s->def;
+          double ninf;
+          if (!IsScalarConst(sel->operands[2], &ninf) || !(std::isinf(ninf) && ninf < 0)) continue;
+          const Value* m = Through(sel->operands[0]);
+          if (m->def && m->def->name == "broadcast_in_dim") m = m->def->operands[0];
+          if (!m->def || m->def->name != "compare") continue;
+          const Op* cmp = m->def;
+          const Value* l = cmp->operands[0];
+          const Value* r = cmp->operands[1];
+          auto iota_dim = [](const Value* v) -> int {
+            while (v->def && v->def->name == "broadcast_in_dim") v = v->def->operands[0];
+            return (v->def && v->def->name == "iota") ? (int)v->def->ints.at("dim")[0] : -1;
+          };
+          std::string dir = cmp->strs.at("comparison_direction");
+          int li = iota_dim(l), ri = iota_dim(r);
+          if (!((dir == "GE" && li == 0 && ri == 1) || (dir == "LE" && li == 1 && ri == 0))) continue;
+          if (m->type.rank() != 2) continue;
+          causal = true;
+          chain.push_back(sel);
+          if (!SingleUse(s)) {}
+          s = sel->operands[1];
+          if (!SingleUse(s)) continue;
+        }
+        if (s->def && s->def->name == "multiply") {
+          double c;
+          const Op* mul = s->def;
+          const Value* other = nullptr;
+          if (IsScalarConst(mul->operands[1], &c)) other = mul->operands[0];
+          else if (IsScalarConst(mul->operands[0], &c)) other = mul->operands[1];
+          if (!other || (s != x && !SingleUse(s))) continue;
+          scale = c;
+          chain.push_back(mul);
+          s = other;
+        }
+        if (!s->def || s->def->name != "dot_general" || (s != x && !SingleUse(s))) continue;
+        const Op* d1 = s->def;
+        if (ints(d1, "batching_dims.lhs") != b01 || ints(d1, "batching_dims.rhs") != b01 ||
+            ints(d1, "contracting_dims.lhs") != std::vector<int64_t>{3} ||
+            ints(d1, "contracting_dims.rhs") != std::vector<int64_t>{3})
+          continue;
+        const Value* Q = d1->operands[0];
+        const Value* K = d1->operands[1];
+        if (Q->type.dt != DT::kBF16 || K->type.dt != DT::kBF16 || V->type.dt != DT::kBF16) continue;
+        if (d2->result()->type.dt != DT::kBF16) continue;
+        if (!(Q->type.dims == K->type.dims && Q->type.dims == V->type.dims)) continue;
+        if (s->type.dt != DT::kF32) continue;
+        int Dh = (int)Q->type.dims[3];
+        if (Dh != 64 && Dh != 128) continue;
+        if (Q->type.dims[2] % 128 != 0) continue;
+        chain.push_back(d1);
+        AttentionStep a;
+        a.B = (int)Q->type.dims[0];
+        a.H = (int)Q->type.dims[1];
+        a.S = (int)Q->type.dims[2];
+        a.D = Dh;
+        a.causal = causal;
+        a.scale = (float)scale;
+        attn_[d2->result()->id] = a;
+        attn_in_[d2->result()->id] = {Q, K, V};
+        for (const Op* o : chain) if (o != d2) dead_[o->index] = true;
+      }
+    next:;
+    }
+  }
+
+  // ---------------------------------------------------------------- materialization
+  bool IsHeavy(const Op* op) const {
+    const std::string& n = op->name;
+    return n == "dot_general" || n == "dot" || n == "scatter" || n == "all_reduce" || n == "all_gather" ||
+           n == "reduce_scatter" || n == "reduce";
+  }
+  bool Cheap(const Value* v) const {
+    const Op* op = v->def;
+    if (!op) return true;
+    if (IsAlias(op)) return Cheap(op->operands[0]);
+    const std::string& n = op->name;
+    if (n == "constant" || n == "iota") return true;
+    if (n == "broadcast_in_dim" || n == "reshape" || n == "transpose" || n == "slice" || n == "convert" || n == "reverse")
+      return true;
+    if (n == "compare" || n == "select" || n == "and" || n == "or" || n == "not") {
+      for (const Value* o : op->operands) if (!IndexOnly(o)) return false;
+      return true;
+    }
+    return false;
+  }
+  bool IndexOnly(const Value* v) const {   // a pure function of the element index (masks)
+    const Op* op = v->def;
+    if (!op) return false;
+    const std::string& n = op->name;
+    if (n == "constant") return op->splat;
+    if (n == "iota") return true;
+    if (n == "broadcast_in_dim" || n == "reshape" || n == "transpose" || n == "convert" || n == "compare" ||
+        n == "and" || n == "or" || n == "not" || n == "select") {
+      for (const Value* o : op->operands) if (!IndexOnly(o)) return false;
+      return true;
+    }
+    return false;
+  }
+
+  void DecideMaterialization() {
+    size_t nv = g_.values.size();
+    need_.assign(nv, false);
+    // consumer "kernels" of each value: -1 means "needs a buffer"
+    std::vector<std::set<int>> cons(nv);
+    for (Value* o : g_.outputs) need_[o->id] = true;
+    for (auto& kv : attn_in_) for (const Value* v : kv.second) need_[v->id] = true;
+    for (int i = (int)g_.ops.size() - 1; i >= 0; --i) {
+      Op* op = g_.ops[i].get();
+      if (dead_[i]) continue;
+      for (Value* r : op->results) {
+        std::set<int> c;
+        for (Op* u : r->users) {
+          if (dead_[u->index]) continue;
+          if (IsHeavy(u) && u->name != "reduce") { need_[r->id] = true; continue; }
+          if (u->name == "reduce") {
+            if (u->operands[0] == r) c.insert(u->result()->id);
+            continue;                       // the init value is folded into the reduction kernel
+
+          }
+          if (IsAlias(u)) {
+            // an alias of r: consumers of the alias are consumers of r
+            for (Value* ur : u->results) {
+              if (need_[ur->id]) c.insert(ur->id);
+              else c.insert(cons[ur->id].begin(), cons[ur->id].end());
+            }
+            continue;
+          }
+          Value* ur = u->result();
+          if (need_[ur->id]) c.insert(ur->id);
+          else c.insert(cons[ur->id].begin(), cons[ur->id].end());
+        }
+        if (attn_.count(r->id)) need_[r->id] = true;
+        cons[r->id] = c;
+        if (IsHeavy(op)) need_[r->id] = true;
+        if (!op->results.empty() && op->name == "constant" && !op->splat) need_[r->id] = true;
+        if (!need_[r->id] && IsElementwise(op) && c.size() >= 2 && !Cheap(r)) need_[r->id] = true;
+        if (IsAlias(op) && need_[r->id]) {
+          // the alias source carries the buffer
+          need_[op->operands[0]->id] = true;
+        }
+      }
+    }
+    for (Value* a : g_.args) need_[a->id] = true;
+  }
+
+  // ---------------------------------------------------------------- slots for args / constants
+  void BindLeaves() {
+    p_->arg_slots.clear();
+    for (size_t k = 0; k < g_.args.size(); ++k) {
+      int s = NewSlot(p_->arg_types[k].bytes());
+      p_->slots[s].arg_index = (int)k;
+      slot_of_[g_.args[k]->id] = s;
+      p_->arg_slots.push_back(s);
+    }
+  }
+
+  int SlotFor(const Value* v) {
+    v = Resolve(v);
+    if (slot_of_[v->id] < 0) slot_of_[v->id] = NewSlot(v->type.bytes());
+    return slot_of_[v->id];
+  }
+
+  // ---------------------------------------------------------------- step emission
+  struct LoopGroup {
+    std::vector<const Value*> roots;
+    std::vector<int64_t> dims;
+    DT dummy = DT::kF32;
+  };
+
+  void EmitSteps() {
+    std::vector<const Value*> pending;   // loop roots of the open group
+    auto flush = [&]() {
+      if (!pending.empty()) EmitLoopGroup(pending);
+      pending.clear();
+    };
+    for (auto& opp : g_.ops) {
+      Op* op = opp.get();
+      if (dead_[op->index]) continue;
+      const std::string& n = op->name;
+      if (IsAlias(op)) {
+        for (size_t k = 0; k < op->results.size(); ++k) {
+          const Value* src = Resolve(op->results[k]);
+          if (slot_of_[src->id] >= 0) slot_of_[op->results[k]->id] = slot_of_[src->id];
+        }
+        continue;
+      }
+      Value* r = op->result();
+      if (attn_.count(r->id)) { flush(); EmitAttention(op); continue; }
+      if (n == "constant") {
+        if (!op->splat || need_[r->id]) {
+          int s = NewSlot(r->type.bytes());
+          p_->consts.push_back(ConstBlob());
+          auto& blob = p_->consts.back().bytes;
+          if (op->splat) {
+            for (int64_t e = 0; e < r->type.numel(); ++e) blob.insert(blob.end(), op->data.begin(), op->data.end());
+          } else {
+            blob = op->data;
+          }
+          p_->slots[s].const_index = (int)p_->consts.size() - 1;
+          slot_of_[r->id] = s;
+        }
+        continue;
+      }
+      if (n == "dot_general" || n == "dot") { flush(); EmitDot(op); continue; }
+      if (n == "reduce") { flush(); EmitReduce(op); continue; }
+      if (n == "scatter") { flush(); EmitScatter(op); continue; }
+      if (n == "all_reduce" || n == "all_gather" || n == "reduce_scatter") { flush(); EmitCollective(op); continue; }
+      if (n == "custom_call") throw LowerError{"unsupported custom_call @" + op->strs["call_target_name"]};
+      if (n == "partition_id" || n == "replica_id") throw LowerError{"unsupported op '" + n + "'"};
+      if (!IsElementwise(op)) throw LowerError{"unsupported op '" + n + "'"};
+      if (n == "gather") CheckGather(op);
+      if (!need_[r->id]) continue;
+      if (n == "reshape" && slot_of_[Resolve(op->operands[0])->id] >= 0 && need_[op->operands[0]->id]) {
+        slot_of_[r->id] = slot_of_[Resolve(op->operands[0])->id];   // contiguous reshape: same buffer
+        continue;
+      }
+      if (!pending.empty() && (pending[0]->type.dims != r->type.dims)) flush();
+      pending.push_back(r);
+    }
+    flush();
+  }
+
+  void CheckGather(const Op* op) {
+    // supported: row take — operand rank >= 1, collapsed_slice_dims=[0], start_index_map=[0],
+    // index_vector_dim = last index dim of size 1, slice_sizes = [1, full rest]
+    auto get = [&](const char* k) { auto it = op->ints.find(k); return it == op->ints.end() ? std::vector<int64_t>{} : it->second; };
+    const Value* t = op->operands[0];
+    const Value* ids = op->operands[1];
+    bool ok = get("collapsed_slice_dims") == std::vector<int64_t>{0} && get("start_index_map") == std::vector<int64_t>{0};
+    auto ivd = get("index_vector_dim");
+    ok = ok && ivd.size() == 1 && ivd[0] == ids->type.rank() - 1 && ids->type.dims.back() == 1;
+    auto ss = get("slice_sizes");
+    ok = ok && (int)ss.size() == t->type.rank() && ss[0] == 1;
+    for (int k = 1; ok && k < t->type.rank(); ++k) ok = ss[k] == t->type.dims[k];
+    auto od = get("offset_dims");
+    ok = ok && (int)od.size() == t->type.rank() - 1;
+    for (size_t k = 0; ok && k < od.size(); ++k) ok = od[k] == (int64_t)(ids->type.rank() - 1 + k);
+    if (!ok) throw LowerError{"unsupported gather form (only row take along dim 0 is supported)"};
+  }
+
+  std::string KName() { return "k" + std::to_string(kcount_++); }
+
+  static std::vector<DT> SlotDts(const std::vector<int>& slots, const std::unordered_map<int, DT>& dt_of) {
+    std::vector<DT> out;
+    for (int s : slots) out.push_back(dt_of.at(s));
+    return out;
+  }
+
+  // A group of loop roots with one shape -> one kernel with several outputs.
+  void EmitLoopGroup(const std::vector<const Value*>& roots) {
+    // greedily split where a later root reads an earlier one at a non-identity index
+    size_t start = 0;
+    while (start < roots.size()) {
+      size_t end = start + 1;
+      while (end < roots.size() && TryLoop(std::vector<const Value*>(roots.begin() + start, roots.begin() + end + 1), true)) ++end;
+      TryLoop(std::vector<const Value*>(roots.begin() + start, roots.begin() + end), false);
+      start = end;
+    }
+  }
+
+  bool TryLoop(const std::vector<const Value*>& roots, bool dry) {
+    const auto& dims = roots[0]->type.dims;
+    int64_t n = roots[0]->type.numel();
+    bool wide = n >= (1LL << 31);
+    std::vector<int> out_slots;
+    std::vector<DT> out_dts;
+    std::vector<int> saved(slot_of_);
+    size_t saved_slots = p_->slots.size();
+    for (const Value* r : roots) {
+      out_slots.push_back(SlotFor(r));
+      out_dts.push_back(r->type.dt);
+    }
+    Gen gen;
+    gen.slot_of = &slot_of_;
+    gen.group_dims = dims;
+    std::ostringstream pre;
+    std::string ind = "    ";
+    gen.identity = Delinearize(pre, "i", dims, "i", ind, wide);
+    gen.body << pre.str();
+    std::vector<std::string> regs;
+    for (size_t k = 0; k < roots.size(); ++k) {
+      // a root is computed from its defining op (not loaded from its own slot)
+      int s = slot_of_[roots[k]->id];
+      slot_of_[roots[k]->id] = -1;
+      std::string v = gen.Emit(roots[k], gen.identity);
+      slot_of_[roots[k]->id] = s;
+      gen.group_regs[s] = v;
+      regs.push_back(v);
+    }
+    if (dry) {
+      bool ok = !gen.conflict;
+      slot_of_ = saved;
+      p_->slots.resize(saved_slots);
+      return ok;
+    }
+    if (gen.conflict) throw LowerError{"internal: fusion conflict"};
+    std::unordered_map<int, DT> dt_of;
+    for (size_t k = 0; k < p_->slots.size(); ++k) {}
+    std::vector<DT> in_dts;
+    for (int s : gen.in_slots) in_dts.push_back(SlotDt(s));
+    std::string fn = KName();
+    src_ << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "("
+         << KernelParams(gen.in_slots, (int)out_slots.size(), false) << ") {\n"
+         << ParamCasts(gen.in_slots, in_dts, out_dts)
+         << "  for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < " << n << "LL; i += (long long)gridDim.x * 256) {\n"
+         << gen.body.str();
+    for (size_t k = 0; k < roots.size(); ++k)
+      src_ << "    out" << k << "[i] = " << StoreExpr(out_dts[k], regs[k]) << ";\n";
+    src_ << "  }\n}\n";
+    Launch L;
+    L.fn = fn;
+    L.in_slots = gen.in_slots;
+    L.out_slots = out_slots;
+    L.block = 256;
+    L.grid_x = std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 16));
+    Step st;
+    st.kind = StepKind::kFusion;
+    st.launches.push_back(L);
+    st.label = "loop" + std::string(" ") + roots[0]->type.str() + " x" + std::to_string(roots.size());
+    p_->steps.push_back(st);
+    for (size_t k = 0; k < roots.size(); ++k) RecordDt(out_slots[k], out_dts[k]);
+    return true;
+  }
+
+  std::unordered_map<int, DT> slot_dt_;
+  void RecordDt(int s, DT t) { slot_dt_[s] = t; }
+  DT SlotDt(int s) {
+    auto it = slot_dt_.find(s);
+    if (it != slot_dt_.end()) return it->second;
+    // find a value bound to this slot
+    for (auto& v : g_.values)
+      if (slot_of_[v->id] == s) return v->type.dt;
+    throw LowerError{"internal: slot without dtype"};
+  }
+
+  // ---------------------------------------------------------------- reductions
+  void EmitReduce(Op* op) {
+    if (op->results.size() != 1) throw LowerError{"variadic reduce (argmax/argmin) is not supported yet"};
+    const Value* x = op->operands[0];
+    const Value* init = op->operands[1];
+    Value* r = op->result();
+    std::vector<int64_t> rd = op->ints.at("dimensions");
+    std::sort(rd.begin(), rd.end());
+    const auto& xd = x->type.dims;
+    std::vector<int64_t> kept, red;
+    std::vector<int> kept_ax, red_ax;
+    for (int k = 0; k < (int)xd.size(); ++k) {
+      if (std::binary_search(rd.begin(), rd.end(), (int64_t)k)) { red.push_back(xd[k]); red_ax.push_back(k); }
+      else { kept.push_back(xd[k]); kept_ax.push_back(k); }
+    }
+    int64_t n_out = r->type.numel(), L = 1;
+    for (int64_t d : red) L *= d;
+    ReduceKind kind = op->reduce;
+    if (kind == ReduceKind::kNone) throw LowerError{"reduce with an unrecognised reducer body"};
+    DT odt = r->type.dt;
+    DT acc_dt = odt == DT::kF64 ? DT::kF64 : DTIsFloat(odt) ? DT::kF32 : odt;
+    std::string acc_t = CType(acc_dt);
+    auto combine = [&](const std::string& a, const std::string& b) -> std::string {
+      bool f = DTIsFloat(acc_dt), d = acc_dt == DT::kF64;
+      switch (kind) {
+        case ReduceKind::kAdd: return a + " + " + b;
+        case ReduceKind::kMul: return a + " * " + b;
+        case ReduceKind::kMax: return f ? (d ? "dmax_n(" : "fmax_n(") + a + ", " + b + ")" : "imax(" + a + ", " + b + ")";
+        case ReduceKind::kMin: return f ? (d ? "dmin_n(" : "fmin_n(") + a + ", " + b + ")" : "imin(" + a + ", " + b + ")";
+        case ReduceKind::kAnd: return acc_dt == DT::kPred ? a + " && " + b : a + " & " + b;
+        case ReduceKind::kOr: return acc_dt == DT::kPred ? a + " || " + b : a + " | " + b;
+        default: return a;
+      }
+    };
+    bool inner = !red_ax.empty() && red_ax.back() == (int)xd.size() - 1;  // reduces the contiguous dim
+    int out_slot = SlotFor(r);
+    Gen gen;
+    gen.slot_of = &slot_of_;
+    std::ostringstream pre;
+    // init value (scalar expression)
+    std::string init_expr;
+    {
+      Gen ig;
+      ig.slot_of = &slot_of_;
+      ig.tmp = 1000000;
+      std::string iv = ig.Emit(init, {});
+      if (!ig.in_slots.empty()) throw LowerError{"reduce init must be a constant"};
+      init_expr = "(" + acc_t + ")(" + iv + ")";
+      if (!ig.body.str().empty()) throw LowerError{"reduce init must be a splat constant"};
+    }
+    std::string fn = KName();
+    std::ostringstream k;
+    Step st;
+    st.kind = StepKind::kFusion;
+    st.label = "reduce " + x->type.str() + " -> " + r->type.str();
+    bool wide = x->type.numel() >= (1LL << 31);
+    const std::string shfl_red = R"(    for (int o = 16; o; o >>= 1) { )" + acc_t + " oth = __shfl_xor_sync(0xffffffffu, acc, o); acc = " +
+                                 combine("acc", "oth") + "; }\n";
+    if (inner && L >= 16 && (n_out >= 148 * 4 || L < 8192)) {
+      // warp or block per output row; reduced index split into (kept, reduced) dims
+      bool block_per_row = L >= 4096;
+      int threads = block_per_row ? 512 : 256;
+      gen.indent = "      ";
+      std::ostringstream ob;
+      // element index: kept part from `row`, reduced part from `j`
+      auto names_k = Delinearize(ob, "row", kept, "a", "    ", wide);
+      std::ostringstream inner_pre;
+      auto names_r = Delinearize(inner_pre, "j", red, "b", "      ", wide);
+      std::vector<std::string> idx(xd.size());
+      for (size_t q = 0; q < kept_ax.size(); ++q) idx[kept_ax[q]] = names_k[q];
+      for (size_t q = 0; q < red_ax.size(); ++q) idx[red_ax[q]] = names_r[q];
+      gen.body << inner_pre.str();
+      // cse entries made inside the loop must not leak outside: emit everything inside the loop
+      std::string v = gen.Emit(x, idx);
+      std::vector<DT> in_dts;
+      for (int s : gen.in_slots) in_dts.push_back(SlotDt(s));
+      k << "extern \"C\" __global__ void __launch_bounds__(" << threads << ") " << fn << "("
+        << KernelParams(gen.in_slots, 1, false) << ") {\n" << ParamCasts(gen.in_slots, in_dts, {odt});
+      if (block_per_row) {
+        k << "  __shared__ " << acc_t << " red[32];\n"
+          << "  for (long long row = blockIdx.x; row < " << n_out << "LL; row += gridDim.x) {\n"
+          << ob.str() << "    " << acc_t << " acc = " << init_expr << ";\n"
+          << "    for (long long j = threadIdx.x; j < " << L << "LL; j += " << threads << ") {\n"
+          << gen.body.str() << "      acc = " << combine("acc", "(" + acc_t + ")(" + v + ")") << ";\n    }\n"
+          << shfl_red
+          << "    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;\n    __syncthreads();\n"
+          << "    if (threadIdx.x < 32) {\n      acc = threadIdx.x < " << threads / 32 << " ? red[threadIdx.x] : " << init_expr << ";\n"
+          << "  " << shfl_red
+          << "      if (threadIdx.x == 0) out0[row] = " << StoreExpr(odt, "acc") << ";\n    }\n    __syncthreads();\n  }\n}\n";
+        Launch Lc;
+        Lc.fn = fn;
+        Lc.in_slots = gen.in_slots;
+        Lc.out_slots = {out_slot};
+        Lc.block = threads;
+        Lc.grid_x = std::max<int64_t>(1, std::min<int64_t>(n_out, 148 * 8));
+        st.launches.push_back(Lc);
+      } else {
+        k << "  const int lane = threadIdx.x & 31;\n"
+          << "  for (long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); row < " << n_out << "LL; row += (long long)gridDim.x * 8) {\n"
+          << ob.str() << "    " << acc_t << " acc = " << init_expr << ";\n"
+          << "    for (long long j = lane; j < " << L << "LL; j += 32) {\n"
+          << gen.body.str() << "      acc = " << combine("acc", "(" + acc_t + ")(" + v + ")") << ";\n    }\n"
+          << shfl_red << "    if (lane == 0) out0[row] = " << StoreExpr(odt, "acc") << ";\n  }\n}\n";
+        Launch Lc;
+        Lc.fn = fn;
+        Lc.in_slots = gen.in_slots;
+        Lc.out_slots = {out_slot};
+        Lc.block = 256;
+        Lc.grid_x = std::max<int64_t>(1, std::min<int64_t>((n_out + 7) / 8, 148 * 16));
+        st.launches.push_back(Lc);
+      }
+    } else {
+      // thread per output, reduced range split over `chunks` blocks in y; partials to scratch, then
+      // a second kernel combines the chunks.  The output index space is the kept dims in order.
+      int64_t chunks = 1;
+      int64_t want_threads = 148LL * 2048;
+      if (n_out < want_threads && L > 64) chunks = std::min<int64_t>((want_threads + n_out - 1) / n_out, std::max<int64_t>(1, L / 32));
+      chunks = std::max<int64_t>(1, std::min<int64_t>(chunks, 1024));
+      int64_t per = (L + chunks - 1) / chunks;
+      gen.indent = "      ";
+      std::ostringstream ob;
+      auto names_k = Delinearize(ob, "o", kept, "a", "    ", wide);
+      std::ostringstream inner_pre;
+      auto names_r = Delinearize(inner_pre, "j", red, "b", "      ", wide);
+      std::vector<std::string> idx(xd.size());
+      for (size_t q = 0; q < kept_ax.size(); ++q) idx[kept_ax[q]] = names_k[q];
+      for (size_t q = 0; q < red_ax.size(); ++q) idx[red_ax[q]] = names_r[q];
+      gen.body << inner_pre.str();
+      std::string v = gen.Emit(x, idx);
+      std::vector<DT> in_dts;
+      for (int s : gen.in_slots) in_dts.push_back(SlotDt(s));
+      int scratch = -1;
+      if (chunks > 1) scratch = NewSlot(chunks * n_out * DTBytes(acc_dt));
+      k << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "("
+        << KernelParams(gen.in_slots, 1, chunks > 1) << ") {\n" << ParamCasts(gen.in_slots, in_dts, {odt})
+        << "  long long o = (long long)blockIdx.x * 256 + threadIdx.x;\n  if (o >= " << n_out << "LL) return;\n"
+        << ob.str() << "  " << acc_t << " acc = " << (chunks > 1 ? "(" + acc_t + ")(" + IdentityOf(kind, acc_dt) + ")" : init_expr) << ";\n"
+        << "    long long j0 = (long long)blockIdx.y * " << per << "LL;\n"
+        << "    long long j1 = j0 + " << per << "LL < " << L << "LL ? j0 + " << per << "LL : " << L << "LL;\n"
+        << "    for (long long j = j0; j < j1; ++j) {\n"
+        << gen.body.str() << "      acc = " << combine("acc", "(" + acc_t + ")(" + v + ")") << ";\n    }\n";
+      if (chunks > 1) k << "  ((" << acc_t << "*)scratch)[(long long)blockIdx.y * " << n_out << "LL + o] = acc;\n}\n";
+      else k << "  out0[o] = " << StoreExpr(odt, "acc") << ";\n}\n";
+      Launch L1;
+      L1.fn = fn;
+      L1.in_slots = gen.in_slots;
+      L1.out_slots = chunks > 1 ? std::vector<int>{} : std::vector<int>{out_slot};
+      L1.scratch = scratch;
+      L1.block = 256;
+      L1.grid_x = (n_out + 255) / 256;
+      L1.grid_y = chunks;
+      if (chunks > 1) {
+        // stage 1 writes no output; patch signature: it declares one output param q0, pass scratch as q0 too
+        L1.out_slots = {scratch};
+      }
+      st.launches.push_back(L1);
+      if (chunks > 1) {
+        std::string fn2 = KName();
+        k << "extern \"C\" __global__ void __launch_bounds__(256) " << fn2 << "(const void* __restrict__ p0, void* __restrict__ q0) {\n"
+          << "  const " << acc_t << "* part = (const " << acc_t << "*)p0;\n  " << MemType(odt) << "* out0 = (" << MemType(odt) << "*)q0;\n"
+          << "  long long o = (long long)blockIdx.x * 256 + threadIdx.x;\n  if (o >= " << n_out << "LL) return;\n"
+          << "  " << acc_t << " acc = " << init_expr << ";\n"
+          << "  for (int c = 0; c < " << chunks << "; ++c) acc = " << combine("acc", "part[(long long)c * " + std::to_string(n_out) + "LL + o]") << ";\n"
+          << "  out0[o] = " << StoreExpr(odt, "acc") << ";\n}\n";
+        Launch L2;
+        L2.fn = fn2;
+        L2.in_slots = {scratch};
+        L2.out_slots = {out_slot};
+        L2.block = 256;
+        L2.grid_x = (n_out + 255) / 256;
+        st.launches.push_back(L2);
+        RecordDt(scratch, acc_dt);
+      }
+    }
+    src_ << k.str();
+    RecordDt(out_slot, odt);
+    p_->steps.push_back(st);
+  }
+
+  static std::string IdentityOf(ReduceKind k, DT t) {
+    bool f = DTIsFloat(t);
+    switch (k) {
+      case ReduceKind::kAdd: return "0";
+      case ReduceKind::kMul: return "1";
+      case ReduceKind::kMax: return f ? "-__int_as_float(0x7f800000)" : (t == DT::kS64 ? "(-9223372036854775807LL-1)" : DTIsUnsigned(t) ? "0" : "(-2147483647-1)");
+      case ReduceKind::kMin: return f ? "__int_as_float(0x7f800000)" : (t == DT::kS64 ? "9223372036854775807LL" : DTIsUnsigned(t) ? "0xffffffffu" : "2147483647");
+      case ReduceKind::kAnd: return t == DT::kPred ? "true" : "-1";
+      case ReduceKind::kOr: return t == DT::kPred ? "false" : "0";
+      default: return "0";
+    }
+  }
+
+  // ---------------------------------------------------------------- dot_general
+  // Materialises `v` permuted by `perm` (and optionally converted) into a new slot.
+  int EmitPermute(const Value* v, const std::vector<int>& perm, const std::vector<int64_t>& out_dims, DT out_dt) {
+    int src = SlotFor(v);
+    int64_t n = 1;
+    for (int64_t d : out_dims) n *= d;
+    int dst = NewSlot(n * DTBytes(out_dt));
+    std::ostringstream body;
+    auto names = Delinearize(body, "i", out_dims, "i", "    ", n >= (1LL << 31));
+    // out index k corresponds to source dim perm[k]
+    std::vector<std::string> sidx(v->type.rank());
+    for (size_t k = 0; k < perm.size(); ++k) sidx[perm[k]] = names[k];
+    std::string fn = KName();
+    DT in_dt = v->type.dt;
+    src_ << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const void* __restrict__ p0, void* __restrict__ q0) {\n"
+         << "  const " << MemType(in_dt) << "* in0 = (const " << MemType(in_dt) << "*)p0;\n"
+         << "  " << MemType(out_dt) << "* out0 = (" << MemType(out_dt) << "*)q0;\n"
+         << "  for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < " << n << "LL; i += (long long)gridDim.x * 256) {\n"
+         << body.str() << "    out0[i] = " << StoreExpr(out_dt, LoadExpr(in_dt, "in0", Gen::Linear(sidx, v->type.dims))) << ";\n  }\n}\n";
+    Launch L;
+    L.fn = fn;
+    L.in_slots = {src};
+    L.out_slots = {dst};
+    L.grid_x = std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 16));
+    Step st;
+    st.kind = StepKind::kFusion;
+    st.launches.push_back(L);
+    st.label = "transpose " + v->type.str();
+    p_->steps.push_back(st);
+    RecordDt(dst, out_dt);
+    return dst;
+  }
+
+  void EmitDot(Op* op) {
+    const Value* a = op->operands[0];
+    const Value* b = op->operands[1];
+    Value* r = op->result();
+    auto get = [&](const char* k) { auto it = op->ints.find(k); return it == op->ints.end() ? std::vector<int64_t>{} : it->second; };
+    std::vector<int64_t> lb = get("batching_dims.lhs"), rb = get("batching_dims.rhs");
+    std::vector<int64_t> lc = get("contracting_dims.lhs"), rc = get("contracting_dims.rhs");
+    if (op->name == "dot") { lc = {a->type.rank() - 1}; rc = {0}; }
+    std::vector<int64_t> lf, rf;
+    for (int k = 0; k < a->type.rank(); ++k)
+      if (std::find(lb.begin(), lb.end(), k) == lb.end() && std::find(lc.begin(), lc.end(), k) == lc.end()) lf.push_back(k);
+    for (int k = 0; k < b->type.rank(); ++k)
+      if (std::find(rb.begin(), rb.end(), k) == rb.end() && std::find(rc.begin(), rc.end(), k) == rc.end()) rf.push_back(k);
+    auto prod = [](const Value* v, const std::vector<int64_t>& ax) { int64_t p = 1; for (int64_t k : ax) p *= v->type.dims[k]; return p; };
+    GemmStep g;
+    g.batch = prod(a, lb);
+    g.M = prod(a, lf);
+    g.N = prod(b, rf);
+    g.K = prod(a, lc);
+    DT at = a->type.dt, bt = b->type.dt;
+    if (!DTIsFloat(at) || !DTIsFloat(bt)) throw LowerError{"dot_general on non-float operands is not supported"};
+    DT ab = (at == DT::kF32 || bt == DT::kF32 || at == DT::kF64 || bt == DT::kF64) ? DT::kF32 : at;
+    if (at != bt && ab != DT::kF32) ab = DT::kF32;
+    if (ab == DT::kF16 || ab == DT::kBF16 || ab == DT::kF32) {} else ab = DT::kF32;
+    g.ab = ab;
+    g.out = r->type.dt;
+    if (g.out != DT::kF32 && g.out != DT::kBF16 && g.out != DT::kF16) throw LowerError{"dot_general result type not supported"};
+    // A as [batch, M, K]: permutation lb + lf + lc of a's dims
+    auto operand = [&](const Value* v, std::vector<int64_t> order, DT want, const std::vector<int64_t>& shape3) {
+      std::vector<int> perm(order.begin(), order.end());
+      bool ident = true;
+      for (size_t k = 0; k < perm.size(); ++k) ident = ident && perm[k] == (int)k;
+      if (ident && v->type.dt == want) return SlotFor(v);
+      std::vector<int64_t> od;
+      for (int q : perm) od.push_back(v->type.dims[q]);
+      (void)shape3;
+      return EmitPermute(v, perm, od, want);
+    };
+    std::vector<int64_t> aord = lb;
+    aord.insert(aord.end(), lf.begin(), lf.end());
+    aord.insert(aord.end(), lc.begin(), lc.end());
+    std::vector<int64_t> bord = rb;
+    bord.insert(bord.end(), rf.begin(), rf.end());
+    bord.insert(bord.end(), rc.begin(), rc.end());
+    g.a = operand(a, aord, ab, {});
+    g.b = operand(b, bord, ab, {});
+    g.c = SlotFor(r);
+    Step st;
+    st.kind = StepKind::kGemm;
+    st.gemm = g;
+    st.label = "gemm b" + std::to_string(g.batch) + " " + std::to_string(g.M) + "x" + std::to_string(g.N) + "x" + std::to_string(g.K);
+    p_->steps.push_back(st);
+    RecordDt(g.c, g.out);
+  }
+
+  void EmitAttention(Op* d2) {
+    AttentionStep a = attn_.at(d2->result()->id);
+    auto ins = attn_in_.at(d2->result()->id);
+    a.q = SlotFor(ins[0]);
+    a.k = SlotFor(ins[1]);
+    a.v = SlotFor(ins[2]);
+    a.o = SlotFor(d2->result());
+    a.dt = DT::kBF16;
+    Step st;
+    st.kind = StepKind::kAttention;
+    st.attn = a;
+    st.label = std::string("attention ") + (a.causal ? "causal " : "") + ins[0]->type.str();
+    p_->steps.push_back(st);
+    RecordDt(a.o, DT::kBF16);
+  }
+
+  // ---------------------------------------------------------------- scatter (embedding VJP)
+  void EmitScatter(Op* op) {
+    if (op->operands.size() != 3 || op->reduce != ReduceKind::kAdd)
+      throw LowerError{"unsupported scatter (only scatter-add of rows is supported)"};
+    const Value* base = op->operands[0];
+    const Value* idx = op->operands[1];
+    const Value* upd = op->operands[2];
+    auto get = [&](const char* k) { auto it = op->ints.find(k); return it == op->ints.end() ? std::vector<int64_t>{} : it->second; };
+    if (base->type.rank() != 2 || get("inserted_window_dims") != std::vector<int64_t>{0} ||
+        get("scatter_dims_to_operand_dims") != std::vector<int64_t>{0} || idx->type.dims.back() != 1 ||
+        get("update_window_dims") != std::vector<int64_t>{upd->type.rank() - 1})
+      throw LowerError{"unsupported scatter form (only row scatter-add along dim 0)"};
+    ScatterStep s;
+    s.rows = base->type.dims[0];
+    s.row_len = base->type.dims[1];
+    s.n_upd = upd->type.numel() / s.row_len;
+    s.dt = base->type.dt;
+    s.idx_dt = idx->type.dt;
+    if (s.dt != DT::kF32 && s.dt != DT::kBF16) throw LowerError{"scatter-add supports f32 / bf16 rows"};
+    if (s.idx_dt != DT::kS32 && s.idx_dt != DT::kS64) throw LowerError{"scatter indices must be s32/s64"};
+    s.base = SlotFor(base);
+    s.idx = SlotFor(idx);
+    s.upd = SlotFor(upd);
+    s.out = SlotFor(op->result());
+    Step st;
+    st.kind = StepKind::kScatterAdd;
+    st.scatter = s;
+    st.label = "scatter_add " + base->type.str();
+    p_->steps.push_back(st);
+    RecordDt(s.out, s.dt);
+  }
+
+  // ---------------------------------------------------------------- collectives
+  void EmitCollective(Op* op) {
+    const Value* x = op->operands[0];
+    Value* r = op->result();
+    if (op->operands.size() != 1 || op->results.size() != 1) throw LowerError{"variadic collectives not yet supported"};
+    const std::string& n = op->name;
+    if (n != "all_reduce") {
+      const char* key = n == "all_gather" ? "all_gather_dim" : "scatter_dimension";
+      auto it = op->ints.find(key);
+      if (it != op->ints.end() && !it->second.empty() && it->second[0] != 0)
+        throw LowerError{n + " only supported along dim 0"};
+    }
+    if (opt_.num_processes <= 1 && x->type.dims == r->type.dims) {
+      // one rank: identity (the reference does the same, src/jam/lower.mm:346-352)
+      slot_of_[r->id] = SlotFor(x);
+      return;
+    }
+    CollectiveStep c;
+    c.op = n == "all_reduce" ? CollKind::kAllReduce : n == "all_gather" ? CollKind::kAllGather : CollKind::kReduceScatter;
+    c.reduce = op->reduce == ReduceKind::kNone ? ReduceKind::kAdd : op->reduce;
+    if (c.op != CollKind::kAllGather && op->reduce == ReduceKind::kNone)
+      throw LowerError{n + " reducer is not a recognized add/max/min/multiply"};
+    c.in = SlotFor(x);
+    c.out = SlotFor(r);
+    c.send_count = x->type.numel();
+    c.recv_count = r->type.numel();
+    c.dt = x->type.dt;
+    Step st;
+    st.kind = StepKind::kCollective;
+    st.coll = c;
+    st.label = n + " " + x->type.str();
+    p_->steps.push_back(st);
+    RecordDt(c.out, c.dt);
+  }
+
+  // ---------------------------------------------------------------- outputs
+  void BindOutputs() {
+    p_->out_slots.clear();
+    p_->out_types.clear();
+    std::set<int> used;
+    for (Value* o : g_.outputs) {
+      const Value* v = Resolve(o);
+      int s = slot_of_[v->id];
+      if (s < 0) s = slot_of_[o->id];
+      if (s < 0) throw LowerError{"internal: output not materialized"};
+      TensorType t = o->type;
+      // shard_map outputs stay per-device shards (src/jam/lower.mm:290-298)
+      if (o->def && IsAlias(o->def)) t.dims = v->type.dims, t = v->type;
+      const Slot& sl = p_->slots[s];
+      if (sl.arg_index >= 0 || sl.const_index >= 0 || used.count(s)) {
+        int d = NewSlot(sl.bytes);
+        Step st;
+        st.kind = StepKind::kCopy;
+        st.copy.src = s;
+        st.copy.dst = d;
+        st.copy.bytes = sl.bytes;
+        st.label = "copy output";
+        p_->steps.push_back(st);
+        s = d;
+      }
+      used.insert(s);
+      p_->slots[s].output = true;
+      p_->out_slots.push_back(s);
+      p_->out_types.push_back(t);
+    }
+  }
+
+  void ComputeLastUse() {
+    auto touch = [&](int s, int i) { if (s >= 0) p_->slots[s].last_use = std::max(p_->slots[s].last_use, i); };
+    for (int i = 0; i < (int)p_->steps.size(); ++i) {
+      const Step& st = p_->steps[i];
+      switch (st.kind) {
+        case StepKind::kFusion:
+          for (auto& L : st.launches) {
+            for (int s : L.in_slots) touch(s, i);
+            for (int s : L.out_slots) touch(s, i);
+            touch(L.scratch, i);
+          }
+          break;
+        case StepKind::kGemm: touch(st.gemm.a, i); touch(st.gemm.b, i); touch(st.gemm.c, i); break;
+        case StepKind::kAttention: touch(st.attn.q, i); touch(st.attn.k, i); touch(st.attn.v, i); touch(st.attn.o, i); break;
+        case StepKind::kScatterAdd: touch(st.scatter.base, i); touch(st.scatter.idx, i); touch(st.scatter.upd, i); touch(st.scatter.out, i); break;
+        case StepKind::kCollective: touch(st.coll.in, i); touch(st.coll.out, i); break;
+        case StepKind::kCopy: touch(st.copy.src, i); touch(st.copy.dst, i); break;
+      }
+    }
+  }
+};
+
+}  // namespace
+
+std::string Plan::dump() const {
+  std::ostringstream o;
+  o << "plan: " << slots.size() << " slots, " << steps.size() << " steps, " << consts.size() << " constants\n";
+  for (size_t i = 0; i < steps.size(); ++i) o << "  [" << i << "] " << steps[i].label << "\n";
+  return o.str();
+}
+
+std::string Lower(Graph& g, const CompileOptions& opt, Plan* plan) {
+  try {
+    Lowerer l(g, opt, plan);
+    l.Run();
+  } catch (const LowerError& e) {
+    return e.msg;
+  } catch (const std::exception& e) {
+    return std::string("lowering failed: ") + e.what();
+  }
+  return "";
+}
+
+}  // namespace b200

@@ -1,0 +1,109 @@
+// plan.h — the compiled form of a StableHLO program: buffer slots + an ordered list of device steps.
+//
+// The reference compiles `@main` into MPSGraph "segments" separated by collective steps and binds
+// values to numbered slots (src/jam/program_impl.h:14-51, src/jam/lower.mm:460-566).  Here a program
+// becomes a flat list of B200 steps — generated fused kernels (NVRTC, sm_100a), tcgen05 GEMMs, the
+// fused attention kernel, scatter-add, NCCL collectives and copies — over slots that the runtime
+// allocates stream-ordered on first definition and frees after last use.
+#pragma once
+
+#include <string>
+#include <vector>
+
+#include "ir.h"
+
+namespace b200 {
+
+struct Slot {
+  int64_t bytes = 0;
+  int arg_index = -1;          // bound to @main argument k (not owned)
+  int const_index = -1;        // bound to uploaded constant k (owned by the executable)
+  bool output = false;         // handed to the caller as an output buffer
+  int last_use = -1;           // index of the last step that reads it (-1: never read)
+};
+
+enum class StepKind { kFusion, kGemm, kAttention, kScatterAdd, kCollective, kCopy };
+
+// One generated kernel launch (loop fusion, or one stage of a reduction).
+struct Launch {
+  std::string fn;              // kernel name inside the NVRTC module
+  std::vector<int> in_slots;   // pointer params first, in this order
+  std::vector<int> out_slots;  // then output pointers
+  int scratch = -1;            // scratch slot appended as the last pointer (-1: none)
+  int64_t grid_x = 1, grid_y = 1;
+  int block = 256;
+  int smem = 0;
+};
+
+struct GemmStep {
+  int a = -1, b = -1, c = -1;  // A[batch,M,K], B[batch,N,K] (K-major), C[batch,M,N] row-major
+  int64_t batch = 1, M = 0, N = 0, K = 0;
+  DT ab = DT::kBF16, out = DT::kF32;
+};
+
+struct AttentionStep {
+  int q = -1, k = -1, v = -1, o = -1;   // [B,H,S,D] each, D contiguous
+  int B = 0, H = 0, S = 0, D = 0;
+  bool causal = false;
+  float scale = 1.f;
+  DT dt = DT::kBF16;
+};
+
+struct ScatterStep {           // out = base; out[idx[i], :] += upd[i, :]
+  int base = -1, idx = -1, upd = -1, out = -1;
+  int64_t rows = 0, row_len = 0, n_upd = 0;
+  DT dt = DT::kF32, idx_dt = DT::kS32;
+};
+
+enum class CollKind { kAllReduce, kAllGather, kReduceScatter };
+
+struct CollectiveStep {
+  CollKind op = CollKind::kAllReduce;
+  ReduceKind reduce = ReduceKind::kAdd;
+  int in = -1, out = -1;
+  int64_t send_count = 0, recv_count = 0;
+  DT dt = DT::kF32;
+};
+
+struct CopyStep {
+  int src = -1, dst = -1;
+  int64_t bytes = 0;
+};
+
+struct Step {
+  StepKind kind;
+  std::vector<Launch> launches;      // kFusion: one or two (reduction stage 2) launches
+  GemmStep gemm;
+  AttentionStep attn;
+  ScatterStep scatter;
+  CollectiveStep coll;
+  CopyStep copy;
+  std::string label;                 // for dumps / timing
+};
+
+struct ConstBlob {
+  std::vector<uint8_t> bytes;
+};
+
+struct Plan {
+  std::vector<Slot> slots;
+  std::vector<Step> steps;
+  std::vector<ConstBlob> consts;
+  std::string cuda_source;           // every generated kernel, one NVRTC module
+  std::vector<int> arg_slots;        // per @main argument
+  std::vector<TensorType> arg_types; // after shard_map retyping
+  std::vector<int> out_slots;        // per @main result
+  std::vector<TensorType> out_types;
+  int num_partitions = 1;
+  std::string dump() const;
+};
+
+struct CompileOptions {
+  int num_processes = 1;             // ranks in the communicator (1: collectives are identities)
+  bool fuse_attention = true;        // B200_NO_FLASH=1 turns the attention pattern match off
+};
+
+// Lowers a parsed graph into a plan.  Returns "" on success, else the error (unsupported op ...).
+std::string Lower(Graph& g, const CompileOptions& opt, Plan* plan);
+
+}  // namespace b200

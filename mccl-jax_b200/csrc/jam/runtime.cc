@@ -1,0 +1,332 @@
+// runtime.cc — plan execution on a device (see runtime.h).
+#include "runtime.h"
+
+#include <cuda.h>
+#include <nvrtc.h>
+
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+
+#include "../../../include/b200_kernels.h"
+#include "../comm/comm.h"
+
+namespace b200k {
+int AttentionFwdWithVt(const void* q, const void* k, const void* v, void* vt, void* o, int B, int H, int S, int D,
+                       int causal, float scale, cudaStream_t st);
+}
+
+namespace b200 {
+namespace {
+
+// ---- driver API through the runtime's entry points (the plugin does not link libcuda) ----
+typedef CUresult (*FnModuleLoadData)(CUmodule*, const void*);
+typedef CUresult (*FnModuleGetFunction)(CUfunction*, CUmodule, const char*);
+typedef CUresult (*FnLaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
+                                   CUstream, void**, void**);
+typedef CUresult (*FnModuleUnload)(CUmodule);
+
+struct Driver {
+  FnModuleLoadData load = nullptr;
+  FnModuleGetFunction get = nullptr;
+  FnLaunchKernel launch = nullptr;
+  FnModuleUnload unload = nullptr;
+  bool ok = false;
+};
+
+const Driver& Drv() {
+  static Driver d;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    auto sym = [](const char* name) -> void* {
+      void* p = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+        return nullptr;
+      return p;
+    };
+    d.load = (FnModuleLoadData)sym("cuModuleLoadData");
+    d.get = (FnModuleGetFunction)sym("cuModuleGetFunction");
+    d.launch = (FnLaunchKernel)sym("cuLaunchKernel");
+    d.unload = (FnModuleUnload)sym("cuModuleUnload");
+    d.ok = d.load && d.get && d.launch && d.unload;
+  });
+  return d;
+}
+
+std::string Nvrtc(const std::string& src, std::vector<char>* cubin) {
+  nvrtcProgram prog;
+  nvrtcResult r = nvrtcCreateProgram(&prog, src.c_str(), "b200_fusions.cu", 0, nullptr, nullptr);
+  if (r != NVRTC_SUCCESS) return std::string("nvrtcCreateProgram: ") + nvrtcGetErrorString(r);
+  const char* opts[] = {"--gpu-architecture=sm_100a", "--std=c++17", "-default-device", "-lineinfo", "--fmad=true"};
+  r = nvrtcCompileProgram(prog, 5, opts);
+  if (r != NVRTC_SUCCESS) {
+    size_t n = 0;
+    nvrtcGetProgramLogSize(prog, &n);
+    std::string log(n, '\0');
+    nvrtcGetProgramLog(prog, &log[0]);
+    nvrtcDestroyProgram(&prog);
+    if (const char* dump = std::getenv("B200_DUMP_CUDA")) std::ofstream(dump) << src;
+    return "NVRTC compile of generated kernels failed: " + log.substr(0, 4000);
+  }
+  size_t n = 0;
+  nvrtcGetCUBINSize(prog, &n);
+  cubin->resize(n);
+  nvrtcGetCUBIN(prog, cubin->data());
+  nvrtcDestroyProgram(&prog);
+  return "";
+}
+
+int PjrtType(DT t) {
+  switch (t) {
+    case DT::kF32: return B200_DT_F32;
+    case DT::kBF16: return B200_DT_BF16;
+    case DT::kF16: return B200_DT_F16;
+    case DT::kS32: return B200_DT_S32;
+    case DT::kS64: return B200_DT_S64;
+    default: return -1;
+  }
+}
+
+struct StepTimer {
+  bool on = std::getenv("B200_TIME") != nullptr;
+  std::map<std::string, double> ms;
+  int runs = 0;
+};
+
+}  // namespace
+
+std::string DeviceAlloc(size_t bytes, cudaStream_t stream, void** out) {
+  *out = nullptr;
+  cudaError_t e = cudaMallocAsync(out, bytes < 16 ? 16 : bytes, stream);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return std::string("device allocation of ") + std::to_string(bytes) + " bytes failed: " + cudaGetErrorString(e);
+  }
+  return "";
+}
+
+void DeviceFree(void* p, cudaStream_t stream) {
+  if (p) cudaFreeAsync(p, stream);
+}
+
+std::string Executable::Build(const char* text, size_t n, const CompileOptions& opt, std::unique_ptr<Executable>* out) {
+  std::unique_ptr<Executable> ex(new Executable());
+  Graph g;
+  std::string err = ParseModule(text, n, &g);
+  if (!err.empty()) return err;
+  err = Lower(g, opt, &ex->plan_);
+  if (!err.empty()) return err;
+  ex->name_ = g.name.empty() ? "b200.main" : g.name;
+  if (std::getenv("B200_DUMP_PLAN")) std::fprintf(stderr, "%s", ex->plan_.dump().c_str());
+  if (const char* dump = std::getenv("B200_DUMP_CUDA")) std::ofstream(dump) << ex->plan_.cuda_source;
+  bool any_fusion = false;
+  for (const Step& s : ex->plan_.steps) any_fusion |= s.kind == StepKind::kFusion;
+  if (any_fusion) {
+    err = Nvrtc(ex->plan_.cuda_source, &ex->cubin_);
+    if (!err.empty()) return err;
+  }
+  *out = std::move(ex);
+  return "";
+}
+
+Executable::~Executable() {
+  const Driver& d = Drv();
+  for (auto& kv : per_dev_) {
+    cudaSetDevice(kv.first);
+    for (void* p : kv.second.consts) cudaFree(p);
+    if (kv.second.module && d.ok) d.unload((CUmodule)kv.second.module);
+  }
+}
+
+std::string Executable::Load(DeviceState& dev, PerDevice** pd) {
+  std::lock_guard<std::mutex> lock(mu_);
+  auto it = per_dev_.find(dev.ordinal);
+  if (it != per_dev_.end()) { *pd = &it->second; return ""; }
+  PerDevice p;
+  if (!cubin_.empty()) {
+    const Driver& d = Drv();
+    if (!d.ok) return "CUDA driver entry points unavailable";
+    CUmodule m;
+    CUresult r = d.load(&m, cubin_.data());
+    if (r != CUDA_SUCCESS) return "cuModuleLoadData failed (" + std::to_string((int)r) + ")";
+    p.module = m;
+    for (const Step& s : plan_.steps)
+      for (const Launch& L : s.launches) {
+        if (p.fns.count(L.fn)) continue;
+        CUfunction f;
+        if (d.get(&f, m, L.fn.c_str()) != CUDA_SUCCESS) return "generated kernel " + L.fn + " not found";
+        p.fns[L.fn] = f;
+      }
+  }
+  for (const ConstBlob& c : plan_.consts) {
+    void* ptr = nullptr;
+    if (cudaMalloc(&ptr, c.bytes.empty() ? 16 : c.bytes.size()) != cudaSuccess) return "constant upload: out of memory";
+    if (!c.bytes.empty()) cudaMemcpy(ptr, c.bytes.data(), c.bytes.size(), cudaMemcpyHostToDevice);
+    p.consts.push_back(ptr);
+  }
+  per_dev_[dev.ordinal] = std::move(p);
+  *pd = &per_dev_[dev.ordinal];
+  return "";
+}
+
+std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& args, std::vector<void*>* outs, Comm* comm) {
+  cudaSetDevice(dev.ordinal);
+  PerDevice* pd = nullptr;
+  std::string err = Load(dev, &pd);
+  if (!err.empty()) return err;
+  const Plan& P = plan_;
+  if (args.size() != P.arg_slots.size()) return "wrong number of arguments";
+  std::vector<void*> ptr(P.slots.size(), nullptr);
+  std::vector<bool> owned(P.slots.size(), false);
+  for (size_t k = 0; k < args.size(); ++k) ptr[P.arg_slots[k]] = const_cast<void*>(args[k]);
+  for (size_t s = 0; s < P.slots.size(); ++s)
+    if (P.slots[s].const_index >= 0) ptr[s] = pd->consts[P.slots[s].const_index];
+  cudaStream_t st = dev.stream;
+  auto slot = [&](int s) -> std::string {
+    if (s < 0 || ptr[s]) return "";
+    std::string e = DeviceAlloc((size_t)P.slots[s].bytes, st, &ptr[s]);
+    if (e.empty()) owned[s] = true;
+    return e;
+  };
+  auto fail = [&](const std::string& e) {
+    for (size_t s = 0; s < ptr.size(); ++s)
+      if (owned[s]) DeviceFree(ptr[s], st);
+    return e;
+  };
+  static StepTimer timer;
+  std::vector<cudaEvent_t> evs;
+  if (timer.on) {
+    evs.resize(P.steps.size() + 1);
+    for (auto& e : evs) cudaEventCreate(&e);
+    cudaEventRecord(evs[0], st);
+  }
+  const Driver& drv = Drv();
+  for (size_t i = 0; i < P.steps.size(); ++i) {
+    const Step& S = P.steps[i];
+    switch (S.kind) {
+      case StepKind::kFusion: {
+        for (const Launch& L : S.launches) {
+          std::vector<void*> vals;
+          for (int s : L.in_slots) { err = slot(s); if (!err.empty()) return fail(err); vals.push_back(ptr[s]); }
+          for (int s : L.out_slots) { err = slot(s); if (!err.empty()) return fail(err); vals.push_back(ptr[s]); }
+          if (L.scratch >= 0) { err = slot(L.scratch); if (!err.empty()) return fail(err); vals.push_back(ptr[L.scratch]); }
+          std::vector<void*> params;
+          for (void*& v : vals) params.push_back(&v);
+          CUresult r = drv.launch((CUfunction)pd->fns.at(L.fn), (unsigned)L.grid_x, (unsigned)L.grid_y, 1, L.block, 1, 1,
+                                  L.smem, (CUstream)st, params.data(), nullptr);
+          if (r != CUDA_SUCCESS) return fail("launch of " + L.fn + " failed (" + std::to_string((int)r) + ")");
+        }
+        break;
+      }
+      case StepKind::kGemm: {
+        const GemmStep& g = S.gemm;
+        for (int s : {g.a, g.b, g.c}) { err = slot(s); if (!err.empty()) return fail(err); }
+        int rc = b200_gemm(ptr[g.a], ptr[g.b], ptr[g.c], g.batch, g.M, g.N, g.K, PjrtType(g.ab), PjrtType(g.out), st);
+        if (rc != 0) return fail("gemm launch failed (" + std::to_string(rc) + ") for " + S.label);
+        break;
+      }
+      case StepKind::kAttention: {
+        const AttentionStep& a = S.attn;
+        for (int s : {a.q, a.k, a.v, a.o}) { err = slot(s); if (!err.empty()) return fail(err); }
+        void* vt = nullptr;
+        err = DeviceAlloc((size_t)a.B * a.H * a.S * a.D * 2, st, &vt);
+        if (!err.empty()) return fail(err);
+        int rc = b200k::AttentionFwdWithVt(ptr[a.q], ptr[a.k], ptr[a.v], vt, ptr[a.o], a.B, a.H, a.S, a.D, a.causal, a.scale, st);
+        DeviceFree(vt, st);
+        if (rc != 0) return fail("attention launch failed (" + std::to_string(rc) + ")");
+        break;
+      }
+      case StepKind::kScatterAdd: {
+        const ScatterStep& s = S.scatter;
+        for (int q : {s.base, s.idx, s.upd, s.out}) { err = slot(q); if (!err.empty()) return fail(err); }
+        size_t bytes = (size_t)s.rows * s.row_len * DTBytes(s.dt);
+        if (ptr[s.out] != ptr[s.base]) cudaMemcpyAsync(ptr[s.out], ptr[s.base], bytes, cudaMemcpyDeviceToDevice, st);
+        int rc = b200_scatter_add_rows(ptr[s.idx], ptr[s.upd], ptr[s.out], s.n_upd, s.row_len, s.rows, PjrtType(s.dt),
+                                       PjrtType(s.idx_dt), st);
+        if (rc != 0) return fail("scatter-add launch failed");
+        break;
+      }
+      case StepKind::kCollective: {
+        const CollectiveStep& c = S.coll;
+        for (int q : {c.in, c.out}) { err = slot(q); if (!err.empty()) return fail(err); }
+        if (!comm) return fail("collective in a single-process program without a communicator");
+        if (c.op == CollKind::kAllReduce) err = comm->AllReduce(ptr[c.in], ptr[c.out], c.send_count, c.dt, c.reduce, st);
+        else if (c.op == CollKind::kAllGather) err = comm->AllGather(ptr[c.in], ptr[c.out], c.send_count, c.dt, st);
+        else err = comm->ReduceScatter(ptr[c.in], ptr[c.out], c.recv_count, c.dt, c.reduce, st);
+        if (!err.empty()) return fail(err);
+        break;
+      }
+      case StepKind::kCopy: {
+        for (int q : {S.copy.src, S.copy.dst}) { err = slot(q); if (!err.empty()) return fail(err); }
+        cudaMemcpyAsync(ptr[S.copy.dst], ptr[S.copy.src], (size_t)S.copy.bytes, cudaMemcpyDeviceToDevice, st);
+        break;
+      }
+    }
+    if (timer.on) cudaEventRecord(evs[i + 1], st);
+    // release temporaries after their last use (stream-ordered)
+    for (size_t s = 0; s < P.slots.size(); ++s) {
+      const Slot& sl = P.slots[s];
+      if (owned[s] && !sl.output && sl.last_use == (int)i) {
+        DeviceFree(ptr[s], st);
+        ptr[s] = nullptr;
+        owned[s] = false;
+      }
+    }
+  }
+  outs->clear();
+  for (int s : P.out_slots) {
+    if (!ptr[s]) { err = slot(s); if (!err.empty()) return fail(err); }
+    outs->push_back(ptr[s]);
+    owned[s] = false;
+  }
+  for (size_t s = 0; s < P.slots.size(); ++s)
+    if (owned[s]) DeviceFree(ptr[s], st);
+  cudaError_t ce = cudaGetLastError();
+  if (ce != cudaSuccess) return std::string("CUDA error during execute: ") + cudaGetErrorString(ce);
+  if (timer.on) {
+    cudaEventSynchronize(evs.back());
+    for (size_t i = 0; i < P.steps.size(); ++i) {
+      float ms = 0;
+      cudaEventElapsedTime(&ms, evs[i], evs[i + 1]);
+      timer.ms[P.steps[i].label.substr(0, 48)] += ms;
+    }
+    for (auto& e : evs) cudaEventDestroy(e);
+    if (++timer.runs % 20 == 0) {
+      std::fprintf(stderr, "[b200 timing] %s: per-run ms by step label (avg over %d runs)\n", name_.c_str(), timer.runs);
+      for (auto& kv : timer.ms) std::fprintf(stderr, "  %10.4f  %s\n", kv.second / timer.runs, kv.first.c_str());
+    }
+  }
+  return "";
+}
+
+}  // namespace b200
+
+// ------------------------------------------------------------------------------------------------
+#include "../../../include/b200_compiler.h"
+
+extern "C" int b200_compile_report(const char* text, size_t size, int num_processes, int nvrtc, char* out, size_t out_size) {
+  std::string report;
+  int rc = 0;
+  b200::CompileOptions opt;
+  opt.num_processes = num_processes;
+  opt.fuse_attention = std::getenv("B200_NO_FLASH") == nullptr;
+  if (nvrtc) {
+    std::unique_ptr<b200::Executable> ex;
+    std::string err = b200::Executable::Build(text, size, opt, &ex);
+    if (!err.empty()) { report = "error: " + err; rc = 1; }
+    else report = ex->plan().dump();
+  } else {
+    b200::Graph g;
+    b200::Plan plan;
+    std::string err = b200::ParseModule(text, size, &g);
+    if (err.empty()) err = b200::Lower(g, opt, &plan);
+    if (!err.empty()) { report = "error: " + err; rc = 1; }
+    else report = plan.dump();
+  }
+  if (report.size() + 1 > out_size) return -1;
+  std::memcpy(out, report.c_str(), report.size() + 1);
+  return rc;
+}

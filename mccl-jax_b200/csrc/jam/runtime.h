@@ -1,0 +1,64 @@
+// runtime.h — executes a compiled plan on one device: the B200 counterpart of the reference's
+// segmented MPSGraph runner (src/jam/jam_run.mm:130-344, Run :346-419).
+//
+// Differences that matter on B200: every step is enqueued asynchronously on the device's stream
+// (the reference runs each segment synchronously, jam_run.mm:305); slot memory comes from CUDA's
+// stream-ordered pool (cudaMallocAsync / cudaFreeAsync after the last use) instead of a size-keyed
+// buffer pool (jam_run.mm:74-112); generated kernels are compiled once per executable with NVRTC for
+// sm_100a and loaded per device.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "plan.h"
+
+namespace b200 {
+
+class Comm;
+
+struct DeviceState {
+  int ordinal = 0;
+  cudaStream_t stream = nullptr;
+};
+
+class Executable {
+ public:
+  // Parses, lowers and NVRTC-compiles a StableHLO text module.  Returns "" or the error.
+  static std::string Build(const char* text, size_t n, const CompileOptions& opt, std::unique_ptr<Executable>* out);
+  ~Executable();
+
+  const Plan& plan() const { return plan_; }
+  const std::string& name() const { return name_; }
+
+  // Enqueues one execution on `dev`.  `args` are device pointers of the argument buffers (sizes were
+  // checked against plan().arg_types by the caller); on success `outs` receives newly allocated
+  // device buffers (stream-ordered on dev.stream) that the caller owns.
+  std::string Run(DeviceState& dev, const std::vector<const void*>& args, std::vector<void*>* outs, Comm* comm);
+
+ private:
+  struct PerDevice {
+    void* module = nullptr;                  // CUmodule
+    std::map<std::string, void*> fns;        // CUfunction by kernel name
+    std::vector<void*> consts;               // uploaded constants
+  };
+  std::string Load(DeviceState& dev, PerDevice** pd);
+
+  Plan plan_;
+  std::string name_;
+  std::vector<char> cubin_;
+  std::mutex mu_;
+  std::map<int, PerDevice> per_dev_;
+};
+
+// Frees memory allocated by Run / the allocator on `stream` (stream-ordered).
+void DeviceFree(void* p, cudaStream_t stream);
+// Allocates `bytes` stream-ordered from the device pool (never returns null for bytes == 0).
+std::string DeviceAlloc(size_t bytes, cudaStream_t stream, void** out);
+
+}  // namespace b200

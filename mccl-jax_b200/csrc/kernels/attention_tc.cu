@@ -1,0 +1,412 @@
+// attention_tc.cu — fused softmax(scale * Q K^T [causal]) V on the B200 tensor cores, bf16 in/out,
+// fp32 scores / softmax / accumulation.
+//
+// The reference runs attention as three MPSGraph ops with the full S x S score matrix in memory:
+// DotGeneral (src/jam/ops/linalg.mm:98), the softmax pattern match (src/jam/ops/elementwise.mm:71-89)
+// and a second DotGeneral.  Here the whole chain is one kernel and the scores never leave the SM.
+//
+// CTA = two 128-row query tiles of one (batch, head) = 256 queries; KV tiles of 128 keys.
+//   warps 0-3   softmax warpgroup for query tile 0 (thread i owns query row i)
+//   warps 4-7   softmax warpgroup for query tile 1
+//   warp 8      TMA loads: Q0, Q1 once; K_j and V^T_j through two-stage rings
+//   warp 9      allocates 512 TMEM columns; one thread issues every tcgen05.mma
+// TMEM: S_t (128 x 128 f32) at column 128 t, PV_t (128 x D f32) at column 256 + D t.
+// Per KV tile j and query tile t:  S_t = Q_t K_j^T  ->  softmax warps read S_t, update the running
+// max / sum, write P_t (bf16) into 128-byte-swizzled shared memory  ->  PV_t = P_t V_j  ->  the
+// softmax warps fold PV_t into their register accumulator O (O = O * alpha + PV).  The MMA thread
+// interleaves PV_0(j), S_0(j+1), PV_1(j), S_1(j+1) so each warpgroup's next scores are computed
+// while the other warpgroup is still in its softmax.
+// V is consumed as V^T [B*H, D, S] (K-major for the PV product); b200_attention_fwd transposes it
+// into a scratch buffer first.
+#include <cuda_bf16.h>
+#include <mutex>
+
+#include "tc_common.cuh"
+#include "../../../include/b200_kernels.h"
+
+namespace b200k {
+
+static __device__ int g_tc_error_attn;
+
+namespace {
+
+constexpr int TQ = 128, TK = 128;
+
+template <int D>
+struct ACfg {
+  static constexpr int kQBytes = TQ * D * 2;          // one query tile
+  static constexpr int kKBytes = TK * D * 2;          // one key tile
+  static constexpr int kVBytes = D * TK * 2;          // one V^T tile (D rows x 128 keys)
+  static constexpr int kPBytes = TQ * TK * 2;         // one P tile
+  static constexpr int kQOff = 0;
+  static constexpr int kKOff = 2 * kQBytes;
+  static constexpr int kVOff = kKOff + 2 * kKBytes;
+  static constexpr int kPOff = kVOff + 2 * kVBytes;
+  static constexpr int kBarOff = kPOff + 2 * kPBytes;
+  static constexpr int kSmem = kBarOff + 256 + 1024;
+  static constexpr int kPVCol = 256;
+};
+
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// barrier indices inside the barrier block
+enum { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kSFree = 11, kPFull = 13, kPVFull = 15,
+       kNumBars = 17 };
+
+template <int D, bool CAUSAL>
+__global__ void __launch_bounds__(320, 1)
+attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmVt, __nv_bfloat16* __restrict__ O, int H, int S, float scale_log2) {
+  using C = ACfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = (uint64_t*)(smem + C::kBarOff);
+  uint32_t* tmem_slot = (uint32_t*)(bars + kNumBars);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qblk = S / (2 * TQ);
+  // heavy (late) query blocks first for the causal case
+  const int qb = CAUSAL ? (n_qblk - 1 - (int)(blockIdx.x % n_qblk)) : (int)(blockIdx.x % n_qblk);
+  const int bh = blockIdx.x / n_qblk;
+  const int q0 = qb * 2 * TQ;
+  const int n_kv = CAUSAL ? (q0 + 2 * TQ) / TK : S / TK;
+  const long long row_base = (long long)bh * S;  // row of (bh, 0) in the [B*H*S, D] views
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[kQFull], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[kKFull + i], 1);
+      mbar_init(&bars[kKEmpty + i], 1);
+      mbar_init(&bars[kVFull + i], 1);
+      mbar_init(&bars[kVEmpty + i], 1);
+      mbar_init(&bars[kSFull + i], 1);
+      mbar_init(&bars[kSFree + i], 128);
+      mbar_init(&bars[kPFull + i], 128);
+      mbar_init(&bars[kPVFull + i], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 9) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  int* err = &g_tc_error_attn;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmVt);
+      mbar_arrive_expect_tx(&bars[kQFull], 2 * C::kQBytes);
+      tma_load_2d(&tmQ, &bars[kQFull], smem + C::kQOff, 0, (int)(row_base + q0));
+      tma_load_2d(&tmQ, &bars[kQFull], smem + C::kQOff + C::kQBytes, 0, (int)(row_base + q0 + TQ));
+      bool ok = true;
+      uint32_t kpar = 0, vpar = 0, kiss = 0, viss = 0;
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&bars[kKEmpty + st], ph ^ 1, kErrTimeoutEmpty, err)) { ok = false; break; }
+        mbar_arrive_expect_tx(&bars[kKFull + st], C::kKBytes);
+        tma_load_2d(&tmK, &bars[kKFull + st], smem + C::kKOff + st * C::kKBytes, 0, (int)(row_base + j * TK));
+        kiss |= 1u << st;
+        kpar = (kpar & ~(1u << st)) | (ph << st);
+        if (!mbar_wait(&bars[kVEmpty + st], ph ^ 1, kErrTimeoutEmpty, err)) { ok = false; break; }
+        mbar_arrive_expect_tx(&bars[kVFull + st], C::kVBytes);
+        uint8_t* vdst = smem + C::kVOff + st * C::kVBytes;
+        // V^T rows (bh*D + d), keys j*128 + [0,64) and + [64,128): two 64-key blocks of D rows
+        tma_load_2d(&tmVt, &bars[kVFull + st], vdst, j * TK, bh * D);
+        tma_load_2d(&tmVt, &bars[kVFull + st], vdst + D * 128, j * TK + 64, bh * D);
+        viss |= 1u << st;
+        vpar = (vpar & ~(1u << st)) | (ph << st);
+      }
+      mbar_wait(&bars[kQFull], 0, kErrTimeoutOther, err);
+      for (int s = 0; s < 2; ++s) {
+        if (kiss & (1u << s)) mbar_wait(&bars[kKFull + s], (kpar >> s) & 1, kErrTimeoutOther, err);
+        if (viss & (1u << s)) mbar_wait(&bars[kVFull + s], (vpar >> s) & 1, kErrTimeoutOther, err);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t id_s = idesc_f16(1, TQ, TK);
+      const uint32_t id_pv = idesc_f16(1, TQ, D);
+      const uint32_t q_addr = smem_u32(smem + C::kQOff);
+      const uint32_t k_addr = smem_u32(smem + C::kKOff);
+      const uint32_t v_addr = smem_u32(smem + C::kVOff);
+      const uint32_t p_addr = smem_u32(smem + C::kPOff);
+      bool ok = mbar_wait(&bars[kQFull], 0, kErrTimeoutFull, err);
+      auto issue_s = [&](int t, int j) {
+        const int st = j & 1;
+        const uint32_t qa = q_addr + t * C::kQBytes, ka = k_addr + st * C::kKBytes;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          // K-major, D = 64: one 128-byte swizzle block; D = 128: two blocks of 128 rows
+          const uint32_t off_q = (k / 4) * (TQ * 128) + (k % 4) * 32;
+          const uint32_t off_k = (k / 4) * (TK * 128) + (k % 4) * 32;
+          mma_f16_ss(tmem + t * 128, sw128_desc(qa + off_q), sw128_desc(ka + off_k), id_s, k != 0);
+        }
+        mma_commit(&bars[kSFull + t]);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const int st = j & 1;
+        const uint32_t pa = p_addr + t * C::kPBytes, va = v_addr + st * C::kVBytes;
+#pragma unroll
+        for (int k = 0; k < TK / 16; ++k) {
+          const uint32_t off_p = (k / 4) * (TQ * 128) + (k % 4) * 32;
+          const uint32_t off_v = (k / 4) * (D * 128) + (k % 4) * 32;
+          mma_f16_ss(tmem + C::kPVCol + t * D, sw128_desc(pa + off_p), sw128_desc(va + off_v), id_pv, k != 0);
+        }
+        mma_commit(&bars[kPVFull + t]);
+      };
+      if (ok) ok = mbar_wait(&bars[kKFull + 0], 0, kErrTimeoutFull, err);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        mma_commit(&bars[kKEmpty + 0]);
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&bars[kVFull + st], ph, kErrTimeoutFull, err)) break;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!mbar_wait(&bars[kPFull + t], j & 1, kErrTimeoutFull, err)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(t, j);
+          if (t == 1) mma_commit(&bars[kVEmpty + st]);
+          if (j + 1 < n_kv) {
+            const int ns = (j + 1) & 1;
+            if (t == 0 && !mbar_wait(&bars[kKFull + ns], ((j + 1) >> 1) & 1, kErrTimeoutFull, err)) { ok = false; break; }
+            if (!mbar_wait(&bars[kSFree + t], j & 1, kErrTimeoutFull, err)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(t, j + 1);
+            if (t == 1) mma_commit(&bars[kKEmpty + ns]);
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax warpgroups
+    const int t = warp >> 2;                 // query tile 0 / 1
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;       // row inside the tile == TMEM lane
+    const int qrow = q0 + t * TQ + r;        // query index inside the head
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_col = tmem + t * 128 + lane_off;
+    const uint32_t pv_col = tmem + C::kPVCol + t * D + lane_off;
+    uint8_t* p_tile = smem + C::kPOff + t * C::kPBytes;
+    float o[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) o[i] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!mbar_wait(&bars[kSFull + t], j & 1, kErrTimeoutAcc, err)) { ok = false; break; }
+      tc_fence_after();
+      const int key0 = j * TK;
+      const bool need_mask = CAUSAL && (key0 + TK - 1 > q0 + t * TQ);
+      // pass 1: row max of the scaled scores (log2 domain)
+      float mx = -INFINITY;
+#pragma unroll 2
+      for (int c = 0; c < TK; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(s_col + c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float s = __uint_as_float(v[e]) * scale_log2;
+          if (need_mask && key0 + c + e > qrow) s = -INFINITY;
+          mx = fmaxf(mx, s);
+        }
+      }
+      const float m_new = fmaxf(m, mx);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;   // fully masked so far: keep p = 0
+      const float alpha = ex2(m - m_use);
+      // fold the previous P V into the register accumulator (its MMA has released P smem)
+      if (j > 0) {
+        if (!mbar_wait(&bars[kPVFull + t], (j - 1) & 1, kErrTimeoutAcc, err)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D; c += 16) {
+          uint32_t v[16];
+          tmem_ld16(pv_col + c, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) o[c + e] = fmaf(o[c + e], alpha_prev, __uint_as_float(v[e]));
+        }
+      }
+      // pass 2: P = exp2(s - m) -> bf16 into the swizzled P tile; row sum
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < TK; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(s_col + c, v);
+        tmem_wait_ld();
+        float p[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float s = __uint_as_float(v[e]) * scale_log2;
+          if (need_mask && key0 + c + e > qrow) s = -INFINITY;
+          p[e] = ex2(s - m_use);
+          sum += p[e];
+        }
+        uint32_t pk[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) pk[e] = pack_bf16(p[2 * e], p[2 * e + 1]);
+        // keys c .. c+15 = two 16-byte chunks; 64-key blocks of 128 rows x 128 B, 128-byte swizzle
+        const int blk = c >> 6;
+        const int ch0 = (c & 63) >> 3;
+        uint8_t* rowp = p_tile + blk * (TQ * 128) + r * 128;
+        *(uint4*)(rowp + (((ch0) ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *(uint4*)(rowp + (((ch0 + 1) ^ (r & 7)) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      }
+      tc_fence_before();
+      mbar_arrive(&bars[kSFree + t]);
+      fence_async_smem();
+      mbar_arrive(&bars[kPFull + t]);
+      l = l * alpha + sum;
+      m = m_new;
+      alpha_prev = alpha;
+    }
+    if (ok && mbar_wait(&bars[kPVFull + t], (n_kv - 1) & 1, kErrTimeoutAcc, err)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+      for (int c = 0; c < D; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(pv_col + c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) o[c + e] = fmaf(o[c + e], alpha_prev, __uint_as_float(v[e])) * inv;
+      }
+      __nv_bfloat16* orow = O + (row_base + qrow) * D;
+#pragma unroll
+      for (int c = 0; c < D; c += 8) {
+        uint4 w = make_uint4(pack_bf16(o[c], o[c + 1]), pack_bf16(o[c + 2], o[c + 3]), pack_bf16(o[c + 4], o[c + 5]),
+                             pack_bf16(o[c + 6], o[c + 7]));
+        *(uint4*)(orow + c) = w;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// V [BH, S, D] -> V^T [BH, D, S], 64 x 64 tiles through shared memory.
+__global__ void __launch_bounds__(256) transpose_v_kernel(const uint16_t* __restrict__ v, uint16_t* __restrict__ vt, int S, int D) {
+  __shared__ uint16_t tile[64][65];
+  const int bh = blockIdx.z, s0 = blockIdx.x * 64, d0 = blockIdx.y * 64;
+  const uint16_t* src = v + (long long)bh * S * D;
+  uint16_t* dst = vt + (long long)bh * S * D;
+  for (int i = threadIdx.x; i < 64 * 64; i += 256) {
+    int rs = i / 64, cd = i % 64;
+    tile[rs][cd] = src[(long long)(s0 + rs) * D + d0 + cd];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 64 * 64; i += 256) {
+    int rd = i / 64, cs = i % 64;
+    dst[(long long)(d0 + rd) * S + s0 + cs] = tile[cs][rd];
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+}  // namespace
+
+EncodeTiledFn GetEncodeTiled();
+
+static bool Map2D(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn enc = GetEncodeTiled();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int D, bool CAUSAL>
+static int LaunchAttn(const void* q, const void* k, const void* vt, void* o, int B, int H, int S, float scale, cudaStream_t st) {
+  using Cf = ACfg<D>;
+  static std::once_flag once[8];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 7], [] {
+    cudaFuncSetAttribute(attn_fwd_kernel<D, CAUSAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmem);
+  });
+  CUtensorMap mq, mk, mv;
+  const uint64_t rows = (uint64_t)B * H * S;
+  if (D == 64) {
+    if (!Map2D(&mq, q, D, rows, 64, TQ) || !Map2D(&mk, k, D, rows, 64, TK)) return -2;
+  } else {
+    return -1;  // D = 128 needs a 3-D map splitting D into two 64-wide blocks; not built yet
+  }
+  if (!Map2D(&mv, vt, (uint64_t)S, (uint64_t)B * H * D, 64, D)) return -2;
+  const float scale_log2 = scale * 1.4426950408889634f;
+  dim3 grid((unsigned)(B * H * (S / (2 * TQ))));
+  attn_fwd_kernel<D, CAUSAL><<<grid, 320, Cf::kSmem, st>>>(mq, mk, mv, (__nv_bfloat16*)o, H, S, scale_log2);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int AttentionFwdWithVt(const void* q, const void* k, const void* v, void* vt, void* o, int B, int H, int S, int D,
+                       int causal, float scale, cudaStream_t st) {
+  if (B <= 0 || H <= 0 || S <= 0) return 0;
+  if (D != 64 || S % (2 * TQ) != 0) return -1;
+  if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)vt | (uintptr_t)o) % 16) return -1;
+  if ((long long)B * H * S > INT32_MAX) return -1;
+  dim3 tg(S / 64, D / 64, B * H);
+  transpose_v_kernel<<<tg, 256, 0, st>>>((const uint16_t*)v, (uint16_t*)vt, S, D);
+  if (causal) return LaunchAttn<64, true>(q, k, vt, o, B, H, S, scale, st);
+  return LaunchAttn<64, false>(q, k, vt, o, B, H, S, scale, st);
+}
+
+int TakeAttnError() {
+  int v = 0, z = 0;
+  cudaMemcpyFromSymbol(&v, g_tc_error_attn, sizeof(int));
+  if (v) cudaMemcpyToSymbol(g_tc_error_attn, &z, sizeof(int));
+  return v;
+}
+
+}  // namespace b200k
+
+extern "C" int b200_attention_fwd(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D,
+                                  int causal, float scale, void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  if (B <= 0 || H <= 0 || S <= 0) return 0;
+  if (D != 64 || S % 256 != 0) return -1;
+  size_t bytes = (size_t)B * H * S * D * 2;
+  void* vt = nullptr;
+  if (cudaMallocAsync(&vt, bytes, st) != cudaSuccess) return -4;
+  int rc = b200k::AttentionFwdWithVt(q, k, v, vt, o, B, H, S, D, causal, scale, st);
+  cudaFreeAsync(vt, st);
+  return rc;
+}

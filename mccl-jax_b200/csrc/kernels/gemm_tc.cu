@@ -1,0 +1,352 @@
+// gemm_tc.cu — dot_general on the B200 tensor cores: C[b] = A[b] . B[b]^T with A[b] (M x K) and
+// B[b] (N x K) K-major (bf16 or f16), fp32 accumulation in TMEM, f32 / bf16 / f16 result.
+//
+// This replaces the reference's MPSGraph matmul call (src/jam/ops/linalg.mm:98, reached from
+// DotGeneral linalg.mm:47-105 after its [batch, free, contract] canonicalisation).
+//
+// Design (one CTA per SM, persistent over output tiles of 128 x BN):
+//   warp 0     TMA producer: 128x64 A and BNx64 B tiles (128-byte swizzle) into a kStages ring;
+//   warp 1     allocates TMEM (2 x BN columns: double-buffered accumulator) and one thread issues
+//              tcgen05.mma (M=128, N=BN, K=16) x4 per stage, committing stage release / acc-ready;
+//   warps 2-5  epilogue: tcgen05.ld 32 lanes x 16 columns, convert, store; release the accumulator
+//              so the next tile's MMAs overlap this tile's stores.
+// Tails in M / N / K are handled by TMA zero fill and predicated stores.
+#include <cuda_bf16.h>
+#include <cstdio>
+#include <mutex>
+
+#include "tc_common.cuh"
+#include "../../../include/b200_kernels.h"
+
+namespace b200k {
+
+static __device__ int g_tc_error_gemm;
+
+namespace {
+
+constexpr int BM = 128, BK = 64;
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStage = kABytes + kBBytes;
+  static constexpr int kSmem = kStages * kStage + 1024 + 256;
+  static constexpr int kTmemCols = 2 * BN;
+};
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// OUT: 0 f32, 1 bf16, 2 f16
+template <int BN, int OUT>
+__global__ void __launch_bounds__(192, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* __restrict__ C,
+               int M, int N, int K, int batch, int fmt) {
+  using CF = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = (uint64_t*)(smem + CF::kStages * CF::kStage);
+  uint64_t* empty = full + CF::kStages;
+  uint64_t* acc_full = empty + CF::kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mb = (M + BM - 1) / BM, nb = (N + BN - 1) / BN;
+  const int per_batch = mb * nb, num_tiles = per_batch * batch;
+  const int kbs = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < CF::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, CF::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmA);
+      prefetch_tmap(&tmB);
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued = 0;  // bit s: stage s has a fill in flight of parity (ph_of_fill[s])
+      uint32_t fill_par = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int b = t / per_batch, r = t % per_batch;
+        const int m_blk = r % mb, n_blk = r / mb;
+        for (int kb = 0; kb < kbs; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, kErrTimeoutEmpty, &g_tc_error_gemm)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], CF::kStage);
+          uint8_t* sa = smem + s * CF::kStage;
+          tma_load_3d(&tmA, &full[s], sa, kb * BK, m_blk * BM, b);
+          tma_load_3d(&tmB, &full[s], sa + CF::kABytes, kb * BK, n_blk * BN, b);
+          issued |= 1u << s;
+          fill_par = (fill_par & ~(1u << s)) | (ph << s);
+          if (++s == CF::kStages) { s = 0; ph ^= 1; }
+        }
+      }
+      // never leave with TMA writes in flight: wait (bounded) for the last fill of every stage
+      for (int q = 0; q < CF::kStages; ++q)
+        if (issued & (1u << q)) mbar_wait(&full[q], (fill_par >> q) & 1, kErrTimeoutOther, &g_tc_error_gemm);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(fmt, BM, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+        const int a = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[a], aph ^ 1, kErrTimeoutAccEmpty, &g_tc_error_gemm)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + a * BN;
+        for (int kb = 0; kb < kbs; ++kb) {
+          if (!mbar_wait(&full[s], ph, kErrTimeoutFull, &g_tc_error_gemm)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * CF::kStage);
+          const uint32_t b_addr = a_addr + CF::kABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_f16_ss(d, sw128_desc(a_addr + k * 32), sw128_desc(b_addr + k * 32), idesc, (kb | k) != 0);
+          mma_commit(&empty[s]);
+          if (++s == CF::kStages) { s = 0; ph ^= 1; }
+        }
+        if (ok) mma_commit(&acc_full[a]);
+      }
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      const int a = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[a], aph, kErrTimeoutAcc, &g_tc_error_gemm)) break;
+      tc_fence_after();
+      const int b = t / per_batch, r = t % per_batch;
+      const int m_blk = r % mb, n_blk = r / mb;
+      const int row = m_blk * BM + row_in_tile;
+      const uint32_t taddr = tmem_base + a * BN + ((uint32_t)(q * 32) << 16);
+      const long long crow = ((long long)b * M + row) * (long long)N;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(taddr + c, v);
+        tmem_wait_ld();
+        const int col = n_blk * BN + c;
+        if (row < M && col < N) {
+          if (OUT == 0) {
+            float* out = (float*)C + crow + col;
+            if (col + 16 <= N && (N & 3) == 0) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4)
+                *(float4*)(out + j) = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                                  __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+            } else {
+              for (int j = 0; j < 16 && col + j < N; ++j) out[j] = __uint_as_float(v[j]);
+            }
+          } else {
+            uint16_t* out = (uint16_t*)C + crow + col;
+            if (col + 16 <= N && (N & 7) == 0) {
+              uint32_t p[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                p[j] = OUT == 1 ? pack_bf16(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]))
+                                : pack_f16(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+              *(uint4*)out = make_uint4(p[0], p[1], p[2], p[3]);
+              *(uint4*)(out + 8) = make_uint4(p[4], p[5], p[6], p[7]);
+            } else {
+              for (int j = 0; j < 16 && col + j < N; ++j) {
+                uint32_t pk = OUT == 1 ? pack_bf16(__uint_as_float(v[j]), 0.f) : pack_f16(__uint_as_float(v[j]), 0.f);
+                out[j] = (uint16_t)(pk & 0xffff);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[a]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, CF::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------- SIMT fallback
+// fp32 (or any) inputs, K-major A[b] (M x K) and B[b] (N x K): 128x128 tiles, 8x8 per thread.
+template <typename T, int OUT>
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A, const T* __restrict__ B, void* __restrict__ C,
+                                                        int M, int N, int K) {
+  __shared__ float As[16][128 + 4];
+  __shared__ float Bs[16][128 + 4];
+  const int b = blockIdx.z;
+  const int m0 = blockIdx.y * 128, n0 = blockIdx.x * 128;
+  const T* Ab = A + (long long)b * M * K;
+  const T* Bb = B + (long long)b * N * K;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    // 128 rows x 16 k per operand = 2048 elements; 256 threads x 8
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      int idx = threadIdx.x + e * 256;
+      int row = idx >> 4, kk = idx & 15;
+      int gk = k0 + kk;
+      int gm = m0 + row, gn = n0 + row;
+      As[kk][row] = (gm < M && gk < K) ? (float)Ab[(long long)gm * K + gk] : 0.f;
+      Bs[kk][row] = (gn < N && gk < K) ? (float)Bb[(long long)gn * K + gk] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float av[8], bv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) av[i] = As[kk][ty * 8 + i];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bv[j] = Bs[kk][tx * 8 + j];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int gm = m0 + ty * 8 + i;
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      int gn = n0 + tx * 8 + j;
+      if (gn >= N) continue;
+      long long o = ((long long)b * M + gm) * N + gn;
+      if (OUT == 0) ((float*)C)[o] = acc[i][j];
+      else if (OUT == 1) ((__nv_bfloat16*)C)[o] = __float2bfloat16_rn(acc[i][j]);
+      else ((__half*)C)[o] = __float2half_rn(acc[i][j]);
+    }
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+}  // namespace
+
+EncodeTiledFn GetEncodeTiled();
+
+// 3-D K-major operand map: dims {K, rows, batch}, box {64, box_rows, 1}, 128-byte swizzle.
+bool MakeOperandMap(CUtensorMap* map, const void* ptr, int K, int rows, int batch, int box_rows, bool f16like) {
+  EncodeTiledFn enc = GetEncodeTiled();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)K * 2 * rows};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, f16like ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr),
+                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int NumSMs() {
+  int dev = 0, n = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+template <int BN, int OUT>
+static int LaunchTc(const void* A, const void* B, void* C, int batch, int M, int N, int K, int fmt, cudaStream_t st) {
+  using CF = Cfg<BN>;
+  static std::once_flag once[8];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 7], [] {
+    cudaFuncSetAttribute(gemm_tc_kernel<BN, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kSmem);
+  });
+  CUtensorMap ta, tb;
+  if (!MakeOperandMap(&ta, A, K, M, batch, BM, fmt == 0) || !MakeOperandMap(&tb, B, K, N, batch, BN, fmt == 0))
+    return -2;
+  int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
+  int grid = std::min(tiles, NumSMs());
+  gemm_tc_kernel<BN, OUT><<<grid, 192, CF::kSmem, st>>>(ta, tb, C, M, N, K, batch, fmt);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+template <typename T>
+static int LaunchSimt(const void* A, const void* B, void* C, int batch, int M, int N, int K, int out, cudaStream_t st) {
+  dim3 grid((N + 127) / 128, (M + 127) / 128, batch);
+  if (out == 0) gemm_simt_kernel<T, 0><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K);
+  else if (out == 1) gemm_simt_kernel<T, 1><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K);
+  else gemm_simt_kernel<T, 2><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int TakeGemmError() {
+  int v = 0, z = 0;
+  cudaMemcpyFromSymbol(&v, g_tc_error_gemm, sizeof(int));
+  if (v) cudaMemcpyToSymbol(g_tc_error_gemm, &z, sizeof(int));
+  return v;
+}
+
+}  // namespace b200k
+
+using namespace b200k;
+
+extern "C" int b200_gemm(const void* A, const void* B, void* C, int64_t batch, int64_t M, int64_t N, int64_t K,
+                         int ab_type, int out_type, void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  if (batch <= 0 || M <= 0 || N <= 0) return 0;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || batch > 65535) return -1;
+  int out = out_type == B200_DT_F32 ? 0 : out_type == B200_DT_BF16 ? 1 : out_type == B200_DT_F16 ? 2 : -1;
+  if (out < 0) return -1;
+  if (K == 0) {
+    size_t bytes = (size_t)batch * M * N * (out == 0 ? 4 : 2);
+    return cudaMemsetAsync(C, 0, bytes, st) == cudaSuccess ? 0 : -3;
+  }
+  bool tc_ok = (ab_type == B200_DT_BF16 || ab_type == B200_DT_F16) && (K % 8) == 0 &&
+               ((uintptr_t)A % 16) == 0 && ((uintptr_t)B % 16) == 0 && !getenv("B200_GEMM_SIMT");
+  if (tc_ok) {
+    int fmt = ab_type == B200_DT_BF16 ? 1 : 0;
+    bool wide = N >= 256;
+    if (out == 0) return wide ? LaunchTc<256, 0>(A, B, C, batch, M, N, K, fmt, st) : LaunchTc<128, 0>(A, B, C, batch, M, N, K, fmt, st);
+    if (out == 1) return wide ? LaunchTc<256, 1>(A, B, C, batch, M, N, K, fmt, st) : LaunchTc<128, 1>(A, B, C, batch, M, N, K, fmt, st);
+    return wide ? LaunchTc<256, 2>(A, B, C, batch, M, N, K, fmt, st) : LaunchTc<128, 2>(A, B, C, batch, M, N, K, fmt, st);
+  }
+  if (ab_type == B200_DT_F32) return LaunchSimt<float>(A, B, C, batch, M, N, K, out, st);
+  if (ab_type == B200_DT_BF16) return LaunchSimt<__nv_bfloat16>(A, B, C, batch, M, N, K, out, st);
+  if (ab_type == B200_DT_F16) return LaunchSimt<__half>(A, B, C, batch, M, N, K, out, st);
+  return -1;
+}

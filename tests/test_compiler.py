@@ -1,0 +1,99 @@
+"""The plugin's StableHLO compiler without a GPU (b200_compile_report): parsing, pattern matching,
+fusion planning, NVRTC compilation of generated kernels, and compile-time errors, which name the
+unsupported op like the reference's lowering does (src/jam/lower.mm:309)."""
+import ctypes
+import os
+
+import pytest
+
+from pjrt_b200 import configs
+from pjrt_b200.shlo import Builder
+
+
+def report(lib_path, text, nprocs=1, nvrtc=1):
+    lib = ctypes.CDLL(lib_path)
+    buf = ctypes.create_string_buffer(1 << 20)
+    t = text.encode()
+    rc = lib.b200_compile_report(t, len(t), nprocs, nvrtc, buf, len(buf))
+    return rc, buf.value.decode()
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_chain_becomes_one_fused_step(lib_path, causal):
+    p = configs.attention_program(B=4, H=16, S=1024, causal=causal, with_inputs=False)
+    rc, rep = report(lib_path, p.text)
+    assert rc == 0, rep
+    steps = [l for l in rep.splitlines() if l.startswith("  [")]
+    assert len(steps) == 1 and "attention" in steps[0] and (("causal" in steps[0]) == causal), rep
+
+
+def test_attention_unfused_when_disabled(lib_path, monkeypatch):
+    monkeypatch.setenv("B200_NO_FLASH", "1")
+    p = configs.attention_program(B=1, H=2, S=256, causal=True, with_inputs=False)
+    rc, rep = report(lib_path, p.text)
+    assert rc == 0, rep
+    assert "attention" not in rep and rep.count("gemm") == 2 and "reduce" in rep
+
+
+def test_mlp_step_compiles_with_generated_kernels(lib_path):
+    rc, rep = report(lib_path, configs.mlp_program(with_inputs=False).text)
+    assert rc == 0, rep
+    assert rep.count("gemm") == 5 and "reduce" in rep and "loop" in rep
+
+
+def test_gemm_and_batched_gemm_plans(lib_path):
+    rc, rep = report(lib_path, configs.gemm_program(1024, 1024, 1024, with_inputs=False).text)
+    assert rc == 0 and "gemm b1 1024x1024x1024" in rep, rep
+    rc, rep = report(lib_path, configs.gemm_program(2048, 2048, 2048, batch=16, with_inputs=False).text)
+    assert rc == 0 and "gemm b16 2048x2048x2048" in rep, rep
+
+
+def test_psum_is_identity_on_one_rank_and_a_collective_on_many(lib_path):
+    p = configs.psum_program(1024, 2, with_inputs=False)
+    rc, rep = report(lib_path, p.text, nprocs=1)
+    assert rc == 0 and "all_reduce" not in rep, rep
+    rc, rep = report(lib_path, p.text, nprocs=2)
+    assert rc == 0 and "all_reduce tensor<1024xf32>" in rep, rep
+
+
+def test_unsupported_op_fails_at_compile_time_with_its_name(lib_path):
+    text = """
+module @m {
+  func.func public @main(%arg0: tensor<8xf32>) -> (tensor<8xf32>) {
+    %0 = stablehlo.fft %arg0, type = FFT, length = [8] : (tensor<8xf32>) -> tensor<8xf32>
+    return %0 : tensor<8xf32>
+  }
+}
+"""
+    rc, rep = report(lib_path, text)
+    assert rc == 1 and "fft" in rep, rep
+
+
+def test_all_gather_only_along_dim0(lib_path):
+    b = Builder("jit_ag", num_partitions=2)
+    x = b.arg((4, 6), "f32")
+    y = b.all_gather(x, 2, dim=1)
+    rc, rep = report(lib_path, b.text([y]), nprocs=2)
+    assert rc == 1 and "dim 0" in rep, rep
+
+
+def test_malformed_text_is_a_compile_error(lib_path):
+    rc, rep = report(lib_path, "module @m { func.func public @main(%arg0: tensor<4xf32>) -> ")
+    assert rc == 1 and rep.startswith("error:"), rep
+    rc, rep = report(lib_path, "")
+    assert rc == 1
+
+
+def test_generated_kernels_compile_with_nvrtc_for_sm100a(lib_path):
+    """Elementwise / broadcast / convert / compare / select / iota / reduce chains -> NVRTC."""
+    b = Builder("jit_mix")
+    x = b.arg((64, 96), "bf16")
+    y = b.arg((96,), "f32")
+    xf = b.convert(x, "f32")
+    z = b.tanh(xf * 0.5 + y) - b.exp(b.sqrt(b.maximum(xf, 0.0)))
+    m = b.compare(b.iota((64, 96), 0), b.iota((64, 96), 1), "LT")
+    w = b.select(m, z, b.const(0.0, "f32", (64, 96)))
+    r1 = b.sum(w, 1)
+    r0 = b.max(w, 0)
+    rc, rep = report(lib_path, b.text([b.convert(w, "bf16"), r1, r0]))
+    assert rc == 0, rep

@@ -1,0 +1,98 @@
+"""Hand-written sm_100a kernels through their C-ABI entry points (include/b200_kernels.h) on
+HBM-resident inputs, against fp32 PyTorch references of the same op."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import RTOL_BF16, RTOL_F32, rel_err
+
+pytestmark = pytest.mark.gpu
+
+BF16, F16, F32, S32, S64 = 13, 10, 11, 4, 5
+
+
+@pytest.fixture(scope="module")
+def lib(lib_path, cuda):
+    l = ctypes.CDLL(lib_path)
+    l.b200_gemm.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 4 + [ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    l.b200_attention_fwd.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_void_p]
+    l.b200_scatter_add_rows.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 3 + [ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    return l
+
+
+def stream(torch):
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def check_device_error(lib):
+    assert lib.b200_take_device_error() == 0
+
+
+@pytest.mark.parametrize("batch,M,N,K", [(1, 128, 256, 64), (1, 1024, 1024, 1024), (1, 200, 300, 136),
+                                         (3, 256, 128, 512), (1, 77, 50, 8), (2, 1000, 520, 1000)])
+@pytest.mark.parametrize("out", [F32, BF16])
+def test_gemm_bf16_tensor_cores(lib, cuda, batch, M, N, K, out):
+    torch = cuda
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
+    a = (torch.randn(batch, M, K, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
+    b = (torch.randn(batch, N, K, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
+    c = torch.empty(batch, M, N, device="cuda", dtype=torch.float32 if out == F32 else torch.bfloat16)
+    rc = lib.b200_gemm(a.data_ptr(), b.data_ptr(), c.data_ptr(), batch, M, N, K, BF16, out, stream(torch))
+    assert rc == 0
+    torch.cuda.synchronize()
+    check_device_error(lib)
+    ref = torch.bmm(a.float(), b.float().transpose(1, 2))
+    e = rel_err(c.float().cpu().numpy(), ref.cpu().numpy())
+    assert e <= (RTOL_F32 * 10 if out == F32 else RTOL_BF16), e
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (300, 200, 100), (64, 10, 784)])
+def test_gemm_f32_simt(lib, cuda, M, N, K):
+    torch = cuda
+    a = torch.randn(1, M, K, device="cuda", dtype=torch.float64).float()
+    b = torch.randn(1, N, K, device="cuda", dtype=torch.float64).float()
+    c = torch.empty(1, M, N, device="cuda")
+    assert lib.b200_gemm(a.data_ptr(), b.data_ptr(), c.data_ptr(), 1, M, N, K, F32, F32, stream(torch)) == 0
+    ref = (a.double() @ b.double().transpose(1, 2)).cpu().numpy()
+    assert rel_err(c.cpu().numpy(), ref) <= RTOL_F32
+
+
+@pytest.mark.parametrize("B,H,S", [(1, 1, 256), (2, 3, 512), (1, 2, 1024)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_fwd(lib, cuda, B, H, S, causal):
+    torch = cuda
+    D = 64
+    g = torch.Generator(device="cuda").manual_seed(S + H + causal)
+    q, k, v = (torch.randn(B, H, S, D, device="cuda", generator=g).to(torch.bfloat16) for _ in range(3))
+    o = torch.empty_like(q)
+    rc = lib.b200_attention_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, H, S, D, int(causal),
+                                1.0 / 8.0, stream(torch))
+    assert rc == 0
+    torch.cuda.synchronize()
+    check_device_error(lib)
+    ref = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float(), is_causal=causal)
+    assert rel_err(o.float().cpu().numpy(), ref.cpu().numpy()) <= RTOL_BF16
+
+
+def test_attention_rejects_unsupported_shapes(lib, cuda):
+    torch = cuda
+    q = torch.zeros(1, 1, 200, 64, device="cuda", dtype=torch.bfloat16)
+    assert lib.b200_attention_fwd(q.data_ptr(), q.data_ptr(), q.data_ptr(), q.data_ptr(), 1, 1, 200, 64, 0, 1.0,
+                                  stream(torch)) != 0
+
+
+@pytest.mark.parametrize("dtype", [F32, BF16])
+def test_scatter_add_rows(lib, cuda, dtype):
+    torch = cuda
+    tdt = torch.float32 if dtype == F32 else torch.bfloat16
+    rows, L, n = 50, 24, 300
+    idx = torch.randint(-3, rows + 3, (n,), device="cuda", dtype=torch.int32)
+    upd = torch.randn(n, L, device="cuda").to(tdt)
+    out = torch.zeros(rows, L, device="cuda", dtype=tdt)
+    assert lib.b200_scatter_add_rows(idx.data_ptr(), upd.data_ptr(), out.data_ptr(), n, L, rows, dtype, S32,
+                                     stream(torch)) == 0
+    ref = torch.zeros(rows, L, device="cuda", dtype=torch.float64)
+    keep = (idx >= 0) & (idx < rows)
+    ref.index_add_(0, idx[keep].long(), upd[keep].double())
+    assert rel_err(out.float().cpu().numpy(), ref.cpu().numpy()) <= (RTOL_F32 * 10 if dtype == F32 else RTOL_BF16)

@@ -1,0 +1,116 @@
+"""Pins the CPU oracle (oracle/interp.py) before it is trusted as the parity checker:
+  * against the golden fixtures (tests/golden/make_golden.py, PyTorch CPU) for attention, the MLP
+    train step and the GEMMs;
+  * against the reference's own known-answer collective tests: src/mccl/collective/smoke.cc:24-40
+    (one rank: in-place all-reduce of [1, 2, 3, 4] is the identity) and smoke_multi.cc:32-48 (rank r
+    contributes r+1 in each of 1024 floats; every rank reads n(n+1)/2).
+"""
+import os
+
+import ml_dtypes
+import numpy as np
+import pytest
+
+from conftest import RTOL_BF16, RTOL_F32, ROOT, assert_close
+from oracle.interp import parse_dense, run, run_spmd
+from oracle.shlo_parse import TType, parse_module
+from pjrt_b200 import configs
+from pjrt_b200.shlo import Builder
+
+G = os.path.join(ROOT, "tests", "golden")
+
+
+def bf(u16):
+    return u16.view(ml_dtypes.bfloat16)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_oracle_attention_matches_golden(causal):
+    d = np.load(os.path.join(G, f"attention_{'causal' if causal else 'full'}.npz"))
+    p = configs.attention_program(B=1, H=2, S=256, D=64, causal=causal, with_inputs=False)
+    out = run(p.text, [bf(d["q"]), bf(d["k"]), bf(d["v"])])[0]
+    assert out.dtype == ml_dtypes.bfloat16
+    assert_close(out.astype(np.float32), d["out"], RTOL_BF16, "attention")
+
+
+def test_oracle_mlp_step_matches_golden():
+    d = np.load(os.path.join(G, "mlp_step.npz"))
+    p = configs.mlp_program(batch=32, din=64, hidden=48, classes=10, lr=0.01, with_inputs=False)
+    outs = run(p.text, [d[f"in{i}"] for i in range(6)])
+    for i, o in enumerate(outs):
+        assert_close(o, d[f"out{i}"], RTOL_F32, f"mlp out{i}")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_oracle_gemm_matches_golden(dtype):
+    d = np.load(os.path.join(G, f"gemm_{dtype}.npz"))
+    p = configs.gemm_program(M=96, N=80, K=64, dtype=dtype, with_inputs=False)
+    a, b = (bf(d["a"]), bf(d["b"])) if dtype == "bf16" else (d["a"], d["b"])
+    out = run(p.text, [a, b])[0]
+    assert_close(out, d["out"], RTOL_F32, "gemm")
+
+
+def test_oracle_allreduce_known_answer_single_rank():
+    """smoke.cc:24-40: with one rank the all-reduce leaves [1, 2, 3, 4] unchanged."""
+    p = configs.psum_program(4, 1, with_inputs=False)
+    out = run(p.text, [np.array([1, 2, 3, 4], np.float32)])[0]
+    np.testing.assert_array_equal(out, [1, 2, 3, 4])
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_oracle_allreduce_known_answer_multi_rank(n):
+    """smoke_multi.cc:32-48: rank r contributes r+1 across 1024 floats; all read n(n+1)/2."""
+    p = configs.psum_program(1024, n, with_inputs=False)
+    res = run_spmd(p.text, [[np.full(1024, r + 1, np.float32)] for r in range(n)])
+    for r in range(n):
+        np.testing.assert_array_equal(res[r][0], np.full(1024, n * (n + 1) / 2, np.float32))
+
+
+def test_oracle_integer_compare_iota_bit_exact():
+    b = Builder("jit_ints")
+    x = b.arg((6, 5), "i32")
+    io = b.iota((6, 5), 1)
+    m = b.compare(x, io, "GE")
+    s = b.select(m, x, io)
+    r = b.reduce(s, [1], "max")
+    text = b.text([m, s, r])
+    xv = np.arange(30, dtype=np.int32).reshape(6, 5) % 7 - 2
+    m_o, s_o, r_o = run(text, [xv])
+    iov = np.broadcast_to(np.arange(5, dtype=np.int32), (6, 5))
+    np.testing.assert_array_equal(m_o, xv >= iov)
+    np.testing.assert_array_equal(s_o, np.where(xv >= iov, xv, iov))
+    np.testing.assert_array_equal(r_o, np.where(xv >= iov, xv, iov).max(1))
+
+
+def test_dense_literal_forms():
+    assert parse_dense("dense<0xFF800000>", TType((), "f32"))[()] == -np.inf
+    np.testing.assert_array_equal(parse_dense("dense<[[1, 2], [3, 4]]>", TType((2, 2), "i32")), [[1, 2], [3, 4]])
+    v = parse_dense("dense<1.000000e-01>", TType((3,), "bf16"))
+    assert v.dtype == ml_dtypes.bfloat16 and float(v[0]) == float(ml_dtypes.bfloat16(0.1))
+    raw = np.array([1.5, -2.0], np.float32).tobytes().hex().upper()
+    np.testing.assert_array_equal(parse_dense(f'dense<"0x{raw}">', TType((2,), "f32")), [1.5, -2.0])
+
+
+def test_parser_handles_generic_reduce_and_call_forms():
+    text = """
+module @m {
+  func.func public @main(%arg0: tensor<4x3xf32>) -> (tensor<4xf32>) {
+    %0 = call @inner(%arg0) : (tensor<4x3xf32>) -> tensor<4x3xf32>
+    %cst = stablehlo.constant dense<0.000000e+00> : tensor<f32>
+    %1 = stablehlo.reduce(%0 init: %cst) across dimensions = [1] : (tensor<4x3xf32>, tensor<f32>) -> tensor<4xf32>
+     reducer(%a: tensor<f32>, %b: tensor<f32>)  {
+      %2 = stablehlo.add %a, %b : tensor<f32>
+      stablehlo.return %2 : tensor<f32>
+    }
+    return %1 : tensor<4xf32>
+  }
+  func.func private @inner(%x: tensor<4x3xf32>) -> tensor<4x3xf32> {
+    %0 = stablehlo.multiply %x, %x : tensor<4x3xf32>
+    return %0 : tensor<4x3xf32>
+  }
+}
+"""
+    m = parse_module(text)
+    assert set(m.funcs) == {"main", "inner"}
+    x = np.arange(12, dtype=np.float32).reshape(4, 3)
+    np.testing.assert_allclose(run(text, [x])[0], (x * x).sum(1))

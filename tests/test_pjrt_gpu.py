@@ -1,0 +1,188 @@
+"""End-to-end through the PJRT C API on a B200, checked against the CPU oracle on the same module
+text and the same seeded inputs — the flow of the reference's src/pjrt/pjrt_e2e.cc:60-181."""
+import os
+
+import ml_dtypes
+import numpy as np
+import pytest
+
+from conftest import RTOL_BF16, RTOL_F32, ROOT, assert_close
+from oracle.interp import run as oracle_run
+from pjrt_b200 import configs, pjrt
+from pjrt_b200.shlo import Builder
+
+pytestmark = pytest.mark.gpu
+G = os.path.join(ROOT, "tests", "golden")
+
+
+def test_client_identity(client):
+    assert client.platform_name() == "b200"
+    assert "PJRT 0.55" in client.platform_version()
+    devs = client.devices(addressable=True)
+    assert len(devs) == 1
+    assert "B200" in client.device_kind(devs[0])
+
+
+@pytest.mark.parametrize("dt", [np.float32, np.int32, np.bool_, ml_dtypes.bfloat16, np.float16, np.int8])
+def test_buffer_roundtrip(client, dt):
+    x = (np.arange(3 * 5 * 7) % 11 - 4).reshape(3, 5, 7).astype(dt)
+    b = client.buffer_from_host(x)
+    assert b.shape() == (3, 5, 7)
+    np.testing.assert_array_equal(b.to_numpy(), x)
+    b.delete()
+
+
+def test_empty_buffer(client):
+    x = np.zeros((0, 4), np.float32)
+    b = client.buffer_from_host(x)
+    assert b.shape() == (0, 4)
+    assert b.to_numpy().shape == (0, 4)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_golden_through_pjrt(client, causal):
+    d = np.load(os.path.join(G, f"attention_{'causal' if causal else 'full'}.npz"))
+    p = configs.attention_program(B=1, H=2, S=256, D=64, causal=causal, with_inputs=False)
+    ins = [d[k].view(ml_dtypes.bfloat16) for k in ("q", "k", "v")]
+    out = client.run(p.text, ins)[0]
+    assert out.dtype == ml_dtypes.bfloat16
+    assert_close(out.astype(np.float32), d["out"], RTOL_BF16, "attention vs golden")
+    ref = oracle_run(p.text, ins)[0]
+    assert_close(out.astype(np.float32), ref.astype(np.float32), RTOL_BF16, "attention vs oracle")
+
+
+@pytest.mark.parametrize("S,causal", [(512, False), (512, True), (1024, True)])
+def test_attention_config_shapes_vs_oracle(client, S, causal):
+    p = configs.attention_program(B=2, H=4, S=S, D=64, causal=causal, seed=S)
+    out = client.run(p.text, p.inputs)[0]
+    ref = oracle_run(p.text, p.inputs)[0]
+    assert_close(out.astype(np.float32), ref.astype(np.float32), RTOL_BF16, "attention")
+
+
+def test_attention_unfused_path_vs_oracle(client, monkeypatch):
+    monkeypatch.setenv("B200_NO_FLASH", "1")
+    p = configs.attention_program(B=1, H=2, S=256, D=64, causal=True, seed=11)
+    out = client.run(p.text, p.inputs)[0]
+    ref = oracle_run(p.text, p.inputs)[0]
+    assert_close(out.astype(np.float32), ref.astype(np.float32), RTOL_BF16, "unfused attention")
+
+
+def test_mlp_step_golden(client):
+    d = np.load(os.path.join(G, "mlp_step.npz"))
+    p = configs.mlp_program(batch=32, din=64, hidden=48, classes=10, lr=0.01, with_inputs=False)
+    outs = client.run(p.text, [d[f"in{i}"] for i in range(6)])
+    for i, o in enumerate(outs):
+        assert_close(o, d[f"out{i}"], RTOL_F32, f"mlp out{i}")
+
+
+def test_mlp_step_config1_vs_oracle(client):
+    p = configs.mlp_program()  # [128,784] -> 512 -> 10
+    outs = client.run(p.text, p.inputs)
+    refs = oracle_run(p.text, p.inputs)
+    for i, (o, r) in enumerate(zip(outs, refs)):
+        assert_close(o, r, RTOL_F32, f"mlp out{i}")
+
+
+@pytest.mark.parametrize("dtype,M,N,K,batch", [("bf16", 1024, 1024, 1024, 0), ("f32", 256, 192, 320, 0),
+                                               ("bf16", 256, 256, 256, 4), ("bf16", 96, 80, 64, 0)])
+def test_gemm_vs_oracle(client, dtype, M, N, K, batch):
+    p = configs.gemm_program(M, N, K, batch=batch, dtype=dtype, seed=M + K)
+    out = client.run(p.text, p.inputs)[0]
+    ref = oracle_run(p.text, p.inputs)[0]
+    assert_close(out, ref, RTOL_F32 if dtype == "f32" else RTOL_F32 * 10, "gemm")
+
+
+def test_psum_single_rank_known_answer(client):
+    """smoke.cc:24-40: one rank, all-reduce of [1,2,3,4] is the identity."""
+    p = configs.psum_program(4, 1, with_inputs=False)
+    out = client.run(p.text, [np.array([1, 2, 3, 4], np.float32)])[0]
+    np.testing.assert_array_equal(out, [1, 2, 3, 4])
+
+
+def test_integer_index_work_bit_exact(client):
+    b = Builder("jit_ints")
+    x = b.arg((64, 33), "i32")
+    io = b.iota((64, 33), 1)
+    m = b.compare(x, io, "GE")
+    s = b.select(m, x, io)
+    r = b.reduce(s, [1], "max")
+    c = b.reduce(b.convert(m, "i32"), [0], "add")
+    text = b.text([m, s, r, c])
+    xv = (np.arange(64 * 33, dtype=np.int32).reshape(64, 33) * 7919) % 61 - 20
+    outs = client.run(text, [xv])
+    refs = oracle_run(text, [xv])
+    for o, rr in zip(outs, refs):
+        assert o.dtype == rr.dtype
+        np.testing.assert_array_equal(o, rr)
+
+
+def test_elementwise_and_reductions_vs_oracle(client):
+    b = Builder("jit_mix")
+    x = b.arg((64, 96), "bf16")
+    y = b.arg((96,), "f32")
+    xf = b.convert(x, "f32")
+    z = b.tanh(xf * 0.5 + y) - b.exp(b.sqrt(b.maximum(xf, 0.0)))
+    m = b.compare(b.iota((64, 96), 0), b.iota((64, 96), 1), "LT")
+    w = b.select(m, z, b.const(0.0, "f32", (64, 96)))
+    text = b.text([b.convert(w, "bf16"), b.sum(w, 1), b.max(w, 0), b.sum(w, [0, 1])])
+    rng = np.random.default_rng(1)
+    ins = [rng.standard_normal((64, 96)).astype(ml_dtypes.bfloat16), rng.standard_normal(96).astype(np.float32)]
+    outs = client.run(text, ins)
+    refs = oracle_run(text, ins)
+    assert_close(outs[0].astype(np.float32), refs[0].astype(np.float32), RTOL_BF16, "bf16 out")
+    for o, r in zip(outs[1:], refs[1:]):
+        assert_close(o, r, RTOL_F32, "reduction")
+
+
+def test_embedding_take_and_scatter_add(client):
+    b = Builder("jit_embed")
+    table = b.arg((100, 16), "f32")
+    ids = b.arg((4, 8), "i32")
+    g = b.take(table, ids)                     # [4, 8, 16]
+    base = b.const(0.0, "f32", (100, 16))
+    s = b.scatter_add(base, ids, g * 2.0)
+    text = b.text([g, s])
+    rng = np.random.default_rng(2)
+    ins = [rng.standard_normal((100, 16)).astype(np.float32), rng.integers(0, 100, (4, 8)).astype(np.int32)]
+    outs = client.run(text, ins)
+    refs = oracle_run(text, ins)
+    np.testing.assert_array_equal(outs[0], refs[0])
+    assert_close(outs[1], refs[1], RTOL_F32, "scatter")
+
+
+def test_wrong_argument_shape_is_invalid_argument(client):
+    exe = client.compile(configs.gemm_program(64, 64, 64, dtype="f32", with_inputs=False).text)
+    bad = client.buffer_from_host(np.zeros((64, 32), np.float32))
+    good = client.buffer_from_host(np.zeros((64, 64), np.float32))
+    with pytest.raises(pjrt.PjrtError) as e:
+        exe.execute([bad, good])
+    assert e.value.code_name == "INVALID_ARGUMENT"
+    with pytest.raises(pjrt.PjrtError) as e:
+        exe.execute([good])
+    assert e.value.code_name == "INVALID_ARGUMENT"
+    exe.destroy()
+
+
+def test_compile_error_names_the_op(client):
+    text = """
+module @m {
+  func.func public @main(%arg0: tensor<8xf32>) -> (tensor<8xf32>) {
+    %0 = stablehlo.fft %arg0, type = FFT, length = [8] : (tensor<8xf32>) -> tensor<8xf32>
+    return %0 : tensor<8xf32>
+  }
+}
+"""
+    with pytest.raises(pjrt.PjrtError) as e:
+        client.compile(text)
+    assert e.value.code_name == "INVALID_ARGUMENT" and "jam compile" in e.value.message and "fft" in e.value.message
+
+
+def test_repeated_execution_reuses_executable(client):
+    p = configs.attention_program(B=1, H=2, S=256, causal=False, seed=4)
+    exe = client.compile(p.text)
+    bufs = [client.buffer_from_host(x) for x in p.inputs]
+    first = exe.execute(bufs)[0].to_numpy()
+    for _ in range(5):
+        again = exe.execute(bufs)[0].to_numpy()
+        np.testing.assert_array_equal(again.view(np.uint16), first.view(np.uint16))
+    exe.destroy()
