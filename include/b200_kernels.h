@@ -36,11 +36,17 @@ B200_API int b200_gemm(const void* A, const void* B, void* C, int64_t batch, int
               int ab_type, int out_type, void* stream);
 
 /* O = softmax(scale * Q K^T [causal mask]) V, fp32 softmax, for bf16 Q, K, V, O of shape [B, H, S, D]
- * (D contiguous), D in {64, 128}, S a multiple of 128.  Fused flash-style kernel on tcgen05.
+ * (D contiguous), D = 64, S a multiple of 256.  Fused flash-style kernel on tcgen05; allocates nothing.
  * Replaces: the dot_general -> softMaxWithTensor -> dot_general chain, src/jam/ops/linalg.mm:98 and
  * src/jam/ops/elementwise.mm:71-89 (TrySoftmax). */
 B200_API int b200_attention_fwd(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D,
                        int causal, float scale, void* stream);
+
+/* The same attention with V first transposed into the caller's scratch `vt` (B*H*S*D bf16 elements)
+ * and consumed K-major: an independent operand layout for cross-checking b200_attention_fwd.
+ * No counterpart in the reference. */
+B200_API int b200_attention_fwd_vt(const void* q, const void* k, const void* v, void* vt, void* o, int B, int H, int S,
+                                   int D, int causal, float scale, void* stream);
 
 /* out[idx[i], :] += upd[i, :] for i < n_upd (rows of length row_len; out has `rows` rows; indices
  * outside [0, rows) are skipped).  dtype in {F32, BF16}; idx_type in {S32, S64}.

@@ -1319,7 +1319,7 @@ class Lowerer {
       TensorType t = o->type;
       // shard_map outputs stay per-device shards (src/jam/lower.mm:290-298)
       if (o->def && IsAlias(o->def)) t.dims = v->type.dims, t = v->type;
-      const Slot& sl = p_->slots[s];
+      const Slot sl = p_->slots[s];   // by value: NewSlot below may reallocate the slot vector
       if (sl.arg_index >= 0 || sl.const_index >= 0 || used.count(s)) {
         int d = NewSlot(sl.bytes);
         Step st;

@@ -14,8 +14,8 @@
 #include "../comm/comm.h"
 
 namespace b200k {
-int AttentionFwdWithVt(const void* q, const void* k, const void* v, void* vt, void* o, int B, int H, int S, int D,
-                       int causal, float scale, cudaStream_t st);
+int AttentionFwd(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D, int causal, float scale,
+                 cudaStream_t st);
 }
 
 namespace b200 {
@@ -231,11 +231,7 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
       case StepKind::kAttention: {
         const AttentionStep& a = S.attn;
         for (int s : {a.q, a.k, a.v, a.o}) { err = slot(s); if (!err.empty()) return fail(err); }
-        void* vt = nullptr;
-        err = DeviceAlloc((size_t)a.B * a.H * a.S * a.D * 2, st, &vt);
-        if (!err.empty()) return fail(err);
-        int rc = b200k::AttentionFwdWithVt(ptr[a.q], ptr[a.k], ptr[a.v], vt, ptr[a.o], a.B, a.H, a.S, a.D, a.causal, a.scale, st);
-        DeviceFree(vt, st);
+        int rc = b200k::AttentionFwd(ptr[a.q], ptr[a.k], ptr[a.v], ptr[a.o], a.B, a.H, a.S, a.D, a.causal, a.scale, st);
         if (rc != 0) return fail("attention launch failed (" + std::to_string(rc) + ")");
         break;
       }

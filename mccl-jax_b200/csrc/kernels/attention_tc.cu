@@ -6,18 +6,22 @@
 // and a second DotGeneral.  Here the whole chain is one kernel and the scores never leave the SM.
 //
 // CTA = two 128-row query tiles of one (batch, head) = 256 queries; KV tiles of 128 keys.
-//   warps 0-3   softmax warpgroup for query tile 0 (thread i owns query row i)
+//   warps 0-3   softmax warpgroup for query tile 0 (thread i owns query row i = TMEM lane i)
 //   warps 4-7   softmax warpgroup for query tile 1
-//   warp 8      TMA loads: Q0, Q1 once; K_j and V^T_j through two-stage rings
+//   warp 8      TMA loads: Q0, Q1 once; K_j and V_j through two-stage rings
 //   warp 9      allocates 512 TMEM columns; one thread issues every tcgen05.mma
-// TMEM: S_t (128 x 128 f32) at column 128 t, PV_t (128 x D f32) at column 256 + D t.
-// Per KV tile j and query tile t:  S_t = Q_t K_j^T  ->  softmax warps read S_t, update the running
-// max / sum, write P_t (bf16) into 128-byte-swizzled shared memory  ->  PV_t = P_t V_j  ->  the
-// softmax warps fold PV_t into their register accumulator O (O = O * alpha + PV).  The MMA thread
-// interleaves PV_0(j), S_0(j+1), PV_1(j), S_1(j+1) so each warpgroup's next scores are computed
-// while the other warpgroup is still in its softmax.
-// V is consumed as V^T [B*H, D, S] (K-major for the PV product); b200_attention_fwd transposes it
-// into a scratch buffer first.
+// TMEM: S_t (128 x 128 f32) at column 128 t, O_t (128 x D f32) at column 256 + D t.
+// Per KV tile j and query tile t:
+//   S_t = Q_t K_j^T (tensor core)  ->  softmax warps load their S row once (one wait), release S_t,
+//   update the running max, write P_t = exp2(s - m) as bf16 into 128-byte-swizzled shared memory
+//   ->  O_t += P_t V_j (tensor core, accumulating in TMEM).
+// The running max used for P only moves when the true row max exceeds it by more than 2^8
+// (lazy rescaling): then the warp rescales its O row in TMEM (ld / scale / st) before the next
+// P V product; otherwise O is never touched by the CUDA cores until the final 1 / l.
+// The MMA thread issues S_t(j+1) as soon as warpgroup t has read S_t(j), before PV_t(j), so the
+// tensor core computes the next scores while the softmax runs.
+// V is read in place ([B*H, S, D], D contiguous) as the MN-major B operand of the P V product; the
+// VT variant (V pre-transposed to [B*H, D, S], K-major) is kept as a cross-check.
 #include <cuda_bf16.h>
 #include <mutex>
 
@@ -31,12 +35,13 @@ static __device__ int g_tc_error_attn;
 namespace {
 
 constexpr int TQ = 128, TK = 128;
+constexpr float kRescaleThreshold = 8.0f;   // log2 units: P entries stay <= 256
 
 template <int D>
 struct ACfg {
   static constexpr int kQBytes = TQ * D * 2;          // one query tile
   static constexpr int kKBytes = TK * D * 2;          // one key tile
-  static constexpr int kVBytes = D * TK * 2;          // one V^T tile (D rows x 128 keys)
+  static constexpr int kVBytes = TK * D * 2;          // one value tile
   static constexpr int kPBytes = TQ * TK * 2;         // one P tile
   static constexpr int kQOff = 0;
   static constexpr int kKOff = 2 * kQBytes;
@@ -44,7 +49,7 @@ struct ACfg {
   static constexpr int kPOff = kVOff + 2 * kVBytes;
   static constexpr int kBarOff = kPOff + 2 * kPBytes;
   static constexpr int kSmem = kBarOff + 256 + 1024;
-  static constexpr int kPVCol = 256;
+  static constexpr int kOCol = 256;
 };
 
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1) {
@@ -68,14 +73,26 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// barrier indices inside the barrier block
+// MN-major operand in the 128-byte swizzle layout: rows of 128 B along K (here: keys), the 64-element
+// MN extent inside one row; SBO = 1024 B between 8-row groups along K.
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)(8192 >> 4) << 16;     // LBO: next 64-element MN block (unused for MN extent 64)
+  d |= (uint64_t)(1024 >> 4) << 32;     // SBO
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
 enum { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kSFree = 11, kPFull = 13, kPVFull = 15,
        kNumBars = 17 };
 
-template <int D, bool CAUSAL>
+// 320 threads: the compiler caps registers at 168 per thread (one CTA per SM); 200 does not launch.
+template <int D, bool CAUSAL, bool VT>
 __global__ void __launch_bounds__(320, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                const __grid_constant__ CUtensorMap tmVt, __nv_bfloat16* __restrict__ O, int H, int S, float scale_log2) {
+                const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int H, int S, float scale_log2) {
   using C = ACfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -117,26 +134,30 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     if (lane == 0) {
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
-      prefetch_tmap(&tmVt);
+      prefetch_tmap(&tmV);
       mbar_arrive_expect_tx(&bars[kQFull], 2 * C::kQBytes);
       tma_load_2d(&tmQ, &bars[kQFull], smem + C::kQOff, 0, (int)(row_base + q0));
       tma_load_2d(&tmQ, &bars[kQFull], smem + C::kQOff + C::kQBytes, 0, (int)(row_base + q0 + TQ));
-      bool ok = true;
       uint32_t kpar = 0, vpar = 0, kiss = 0, viss = 0;
-      for (int j = 0; j < n_kv && ok; ++j) {
+      for (int j = 0; j < n_kv; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&bars[kKEmpty + st], ph ^ 1, kErrTimeoutEmpty, err)) { ok = false; break; }
+        if (!mbar_wait(&bars[kKEmpty + st], ph ^ 1, kErrTimeoutEmpty, err)) break;
         mbar_arrive_expect_tx(&bars[kKFull + st], C::kKBytes);
         tma_load_2d(&tmK, &bars[kKFull + st], smem + C::kKOff + st * C::kKBytes, 0, (int)(row_base + j * TK));
         kiss |= 1u << st;
         kpar = (kpar & ~(1u << st)) | (ph << st);
-        if (!mbar_wait(&bars[kVEmpty + st], ph ^ 1, kErrTimeoutEmpty, err)) { ok = false; break; }
+        if (!mbar_wait(&bars[kVEmpty + st], ph ^ 1, kErrTimeoutEmpty, err)) break;
         mbar_arrive_expect_tx(&bars[kVFull + st], C::kVBytes);
         uint8_t* vdst = smem + C::kVOff + st * C::kVBytes;
-        // V^T rows (bh*D + d), keys j*128 + [0,64) and + [64,128): two 64-key blocks of D rows
-        tma_load_2d(&tmVt, &bars[kVFull + st], vdst, j * TK, bh * D);
-        tma_load_2d(&tmVt, &bars[kVFull + st], vdst + D * 128, j * TK + 64, bh * D);
+        if (VT) {
+          // V^T rows (bh*D + d), keys j*128 + [0,64) and + [64,128): two 64-key blocks of D rows
+          tma_load_2d(&tmV, &bars[kVFull + st], vdst, j * TK, bh * D);
+          tma_load_2d(&tmV, &bars[kVFull + st], vdst + D * 128, j * TK + 64, bh * D);
+        } else {
+          // V rows (keys) j*128 .. +128, the D = 64 values of a key in one 128-byte row
+          tma_load_2d(&tmV, &bars[kVFull + st], vdst, 0, (int)(row_base + j * TK));
+        }
         viss |= 1u << st;
         vpar = (vpar & ~(1u << st)) | (ph << st);
       }
@@ -150,22 +171,17 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t id_s = idesc_f16(1, TQ, TK);
-      const uint32_t id_pv = idesc_f16(1, TQ, D);
+      const uint32_t id_pv = idesc_f16(1, TQ, D, !VT);
       const uint32_t q_addr = smem_u32(smem + C::kQOff);
       const uint32_t k_addr = smem_u32(smem + C::kKOff);
       const uint32_t v_addr = smem_u32(smem + C::kVOff);
       const uint32_t p_addr = smem_u32(smem + C::kPOff);
-      bool ok = mbar_wait(&bars[kQFull], 0, kErrTimeoutFull, err);
       auto issue_s = [&](int t, int j) {
         const int st = j & 1;
         const uint32_t qa = q_addr + t * C::kQBytes, ka = k_addr + st * C::kKBytes;
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          // K-major, D = 64: one 128-byte swizzle block; D = 128: two blocks of 128 rows
-          const uint32_t off_q = (k / 4) * (TQ * 128) + (k % 4) * 32;
-          const uint32_t off_k = (k / 4) * (TK * 128) + (k % 4) * 32;
-          mma_f16_ss(tmem + t * 128, sw128_desc(qa + off_q), sw128_desc(ka + off_k), id_s, k != 0);
-        }
+        for (int k = 0; k < D / 16; ++k)
+          mma_f16_ss(tmem + t * 128, sw128_desc(qa + k * 32), sw128_desc(ka + k * 32), id_s, k != 0);
         mma_commit(&bars[kSFull + t]);
       };
       auto issue_pv = [&](int t, int j) {
@@ -174,11 +190,13 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 #pragma unroll
         for (int k = 0; k < TK / 16; ++k) {
           const uint32_t off_p = (k / 4) * (TQ * 128) + (k % 4) * 32;
-          const uint32_t off_v = (k / 4) * (D * 128) + (k % 4) * 32;
-          mma_f16_ss(tmem + C::kPVCol + t * D, sw128_desc(pa + off_p), sw128_desc(va + off_v), id_pv, k != 0);
+          const uint64_t bdesc = VT ? sw128_desc(va + (k / 4) * (D * 128) + (k % 4) * 32)
+                                    : sw128_mn_desc(va + k * 16 * 128);
+          mma_f16_ss(tmem + C::kOCol + t * D, sw128_desc(pa + off_p), bdesc, id_pv, (j | k) != 0);
         }
         mma_commit(&bars[kPVFull + t]);
       };
+      bool ok = mbar_wait(&bars[kQFull], 0, kErrTimeoutFull, err);
       if (ok) ok = mbar_wait(&bars[kKFull + 0], 0, kErrTimeoutFull, err);
       if (ok) {
         tc_fence_after();
@@ -189,20 +207,20 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       for (int j = 0; j < n_kv && ok; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&bars[kVFull + st], ph, kErrTimeoutFull, err)) break;
+        const int ns = (j + 1) & 1;
         for (int t = 0; t < 2 && ok; ++t) {
-          if (!mbar_wait(&bars[kPFull + t], j & 1, kErrTimeoutFull, err)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(t, j);
-          if (t == 1) mma_commit(&bars[kVEmpty + st]);
           if (j + 1 < n_kv) {
-            const int ns = (j + 1) & 1;
             if (t == 0 && !mbar_wait(&bars[kKFull + ns], ((j + 1) >> 1) & 1, kErrTimeoutFull, err)) { ok = false; break; }
             if (!mbar_wait(&bars[kSFree + t], j & 1, kErrTimeoutFull, err)) { ok = false; break; }
             tc_fence_after();
             issue_s(t, j + 1);
             if (t == 1) mma_commit(&bars[kKEmpty + ns]);
           }
+          if (t == 0 && !mbar_wait(&bars[kVFull + st], ph, kErrTimeoutFull, err)) { ok = false; break; }
+          if (!mbar_wait(&bars[kPFull + t], j & 1, kErrTimeoutFull, err)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(t, j);
+          if (t == 1) mma_commit(&bars[kVEmpty + st]);
         }
       }
     }
@@ -214,98 +232,97 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     const int qrow = q0 + t * TQ + r;        // query index inside the head
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t s_col = tmem + t * 128 + lane_off;
-    const uint32_t pv_col = tmem + C::kPVCol + t * D + lane_off;
-    uint8_t* p_tile = smem + C::kPOff + t * C::kPBytes;
-    float o[D];
-#pragma unroll
-    for (int i = 0; i < D; ++i) o[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    const uint32_t o_col = tmem + C::kOCol + t * D + lane_off;
+    uint8_t* p_row = smem + C::kPOff + t * C::kPBytes + r * 128;
+    float m_use = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!mbar_wait(&bars[kSFull + t], j & 1, kErrTimeoutAcc, err)) { ok = false; break; }
+      if (!mbar_wait_warp(&bars[kSFull + t], j & 1, kErrTimeoutAcc, err)) { ok = false; break; }
       tc_fence_after();
+      uint32_t sv[TK];
+#pragma unroll
+      for (int c = 0; c < TK; c += 16) tmem_ld16(s_col + c, *reinterpret_cast<uint32_t(*)[16]>(sv + c));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bars[kSFree + t]);        // S_t may be overwritten by the next Q K^T
       const int key0 = j * TK;
       const bool need_mask = CAUSAL && (key0 + TK - 1 > q0 + t * TQ);
-      // pass 1: row max of the scaled scores (log2 domain)
       float mx = -INFINITY;
-#pragma unroll 2
-      for (int c = 0; c < TK; c += 16) {
-        uint32_t v[16];
-        tmem_ld16(s_col + c, v);
-        tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float s = __uint_as_float(v[e]) * scale_log2;
-          if (need_mask && key0 + c + e > qrow) s = -INFINITY;
-          mx = fmaxf(mx, s);
-        }
+      for (int e = 0; e < TK; ++e) {
+        float s = __uint_as_float(sv[e]) * scale_log2;
+        if (need_mask && key0 + e > qrow) s = -INFINITY;
+        sv[e] = __float_as_uint(s);
+        mx = fmaxf(mx, s);
       }
-      const float m_new = fmaxf(m, mx);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;   // fully masked so far: keep p = 0
-      const float alpha = ex2(m - m_use);
-      // fold the previous P V into the register accumulator (its MMA has released P smem)
-      if (j > 0) {
-        if (!mbar_wait(&bars[kPVFull + t], (j - 1) & 1, kErrTimeoutAcc, err)) { ok = false; break; }
-        tc_fence_after();
+      // P smem and the O accumulator are free once the previous P V product has completed
+      if (j > 0 && !mbar_wait_warp(&bars[kPVFull + t], (j - 1) & 1, kErrTimeoutAcc, err)) { ok = false; break; }
+      tc_fence_after();
+      // Lazy rescale.  The decision is per row, but tcgen05.ld / st are warp-collective
+      // (.sync.aligned): the whole warp takes the TMEM path when any of its rows needs it, and rows
+      // that do not rescale multiply by 1.
+      const bool mine = mx > m_use + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, mine)) {
+        const float m_new = mine ? mx : m_use;
+        if (j > 0) {
+          const float f = mine ? ex2(m_use - m_new) : 1.f;
+          l *= f;
 #pragma unroll
-        for (int c = 0; c < D; c += 16) {
-          uint32_t v[16];
-          tmem_ld16(pv_col + c, v);
-          tmem_wait_ld();
+          for (int c = 0; c < D; c += 16) {
+            uint32_t v[16];
+            tmem_ld16(o_col + c, v);
+            tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) o[c + e] = fmaf(o[c + e], alpha_prev, __uint_as_float(v[e]));
+            for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * f);
+            tmem_st16(o_col + c, v);
+          }
+          tmem_wait_st();
         }
+        m_use = m_new;
       }
-      // pass 2: P = exp2(s - m) -> bf16 into the swizzled P tile; row sum
       float sum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < TK; c += 16) {
-        uint32_t v[16];
-        tmem_ld16(s_col + c, v);
-        tmem_wait_ld();
-        float p[16];
+      const float mu = m_use == -INFINITY ? 0.f : m_use;   // a row masked so far contributes p = 0
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float s = __uint_as_float(v[e]) * scale_log2;
-          if (need_mask && key0 + c + e > qrow) s = -INFINITY;
-          p[e] = ex2(s - m_use);
-          sum += p[e];
-        }
+      for (int c = 0; c < TK; c += 16) {
         uint32_t pk[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) pk[e] = pack_bf16(p[2 * e], p[2 * e + 1]);
-        // keys c .. c+15 = two 16-byte chunks; 64-key blocks of 128 rows x 128 B, 128-byte swizzle
+        for (int e = 0; e < 8; ++e) {
+          const float p0 = ex2(__uint_as_float(sv[c + 2 * e]) - mu);
+          const float p1 = ex2(__uint_as_float(sv[c + 2 * e + 1]) - mu);
+          sum += p0 + p1;
+          pk[e] = pack_bf16(p0, p1);
+        }
+        // keys c .. c+15 = two 16-byte chunks of row r in the 64-key block c / 64 (128-byte swizzle)
         const int blk = c >> 6;
         const int ch0 = (c & 63) >> 3;
-        uint8_t* rowp = p_tile + blk * (TQ * 128) + r * 128;
-        *(uint4*)(rowp + (((ch0) ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        uint8_t* rowp = p_row + blk * (TQ * 128);
+        *(uint4*)(rowp + ((ch0 ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         *(uint4*)(rowp + (((ch0 + 1) ^ (r & 7)) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
+      l += sum;
       tc_fence_before();
-      mbar_arrive(&bars[kSFree + t]);
       fence_async_smem();
       mbar_arrive(&bars[kPFull + t]);
-      l = l * alpha + sum;
-      m = m_new;
-      alpha_prev = alpha;
     }
-    if (ok && mbar_wait(&bars[kPVFull + t], (n_kv - 1) & 1, kErrTimeoutAcc, err)) {
+    if (ok && mbar_wait_warp(&bars[kPVFull + t], (n_kv - 1) & 1, kErrTimeoutAcc, err)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = O + (row_base + qrow) * D;
 #pragma unroll
       for (int c = 0; c < D; c += 16) {
         uint32_t v[16];
-        tmem_ld16(pv_col + c, v);
+        tmem_ld16(o_col + c, v);
         tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 16; ++e) o[c + e] = fmaf(o[c + e], alpha_prev, __uint_as_float(v[e])) * inv;
-      }
-      __nv_bfloat16* orow = O + (row_base + qrow) * D;
-#pragma unroll
-      for (int c = 0; c < D; c += 8) {
-        uint4 w = make_uint4(pack_bf16(o[c], o[c + 1]), pack_bf16(o[c + 2], o[c + 3]), pack_bf16(o[c + 4], o[c + 5]),
-                             pack_bf16(o[c + 6], o[c + 7]));
-        *(uint4*)(orow + c) = w;
+        uint4 w0 = make_uint4(pack_bf16(__uint_as_float(v[0]) * inv, __uint_as_float(v[1]) * inv),
+                              pack_bf16(__uint_as_float(v[2]) * inv, __uint_as_float(v[3]) * inv),
+                              pack_bf16(__uint_as_float(v[4]) * inv, __uint_as_float(v[5]) * inv),
+                              pack_bf16(__uint_as_float(v[6]) * inv, __uint_as_float(v[7]) * inv));
+        uint4 w1 = make_uint4(pack_bf16(__uint_as_float(v[8]) * inv, __uint_as_float(v[9]) * inv),
+                              pack_bf16(__uint_as_float(v[10]) * inv, __uint_as_float(v[11]) * inv),
+                              pack_bf16(__uint_as_float(v[12]) * inv, __uint_as_float(v[13]) * inv),
+                              pack_bf16(__uint_as_float(v[14]) * inv, __uint_as_float(v[15]) * inv));
+        *(uint4*)(orow + c) = w0;
+        *(uint4*)(orow + c + 8) = w1;
       }
     }
   }
@@ -317,7 +334,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   }
 }
 
-// V [BH, S, D] -> V^T [BH, D, S], 64 x 64 tiles through shared memory.
+// V [BH, S, D] -> V^T [BH, D, S], 64 x 64 tiles through shared memory (VT variant only).
 __global__ void __launch_bounds__(256) transpose_v_kernel(const uint16_t* __restrict__ v, uint16_t* __restrict__ vt, int S, int D) {
   __shared__ uint16_t tile[64][65];
   const int bh = blockIdx.z, s0 = blockIdx.x * 64, d0 = blockIdx.y * 64;
@@ -354,39 +371,51 @@ static bool Map2D(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t ou
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int D, bool CAUSAL>
-static int LaunchAttn(const void* q, const void* k, const void* vt, void* o, int B, int H, int S, float scale, cudaStream_t st) {
+template <int D, bool CAUSAL, bool VT>
+static int LaunchAttn(const void* q, const void* k, const void* v, void* o, int B, int H, int S, float scale, cudaStream_t st) {
   using Cf = ACfg<D>;
   static std::once_flag once[8];
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 7], [] {
-    cudaFuncSetAttribute(attn_fwd_kernel<D, CAUSAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmem);
+    cudaFuncSetAttribute(attn_fwd_kernel<D, CAUSAL, VT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmem);
   });
   CUtensorMap mq, mk, mv;
   const uint64_t rows = (uint64_t)B * H * S;
-  if (D == 64) {
-    if (!Map2D(&mq, q, D, rows, 64, TQ) || !Map2D(&mk, k, D, rows, 64, TK)) return -2;
+  if (!Map2D(&mq, q, D, rows, 64, TQ) || !Map2D(&mk, k, D, rows, 64, TK)) return -2;
+  if (VT) {
+    if (!Map2D(&mv, v, (uint64_t)S, (uint64_t)B * H * D, 64, D)) return -2;
   } else {
-    return -1;  // D = 128 needs a 3-D map splitting D into two 64-wide blocks; not built yet
+    if (!Map2D(&mv, v, D, rows, 64, TK)) return -2;
   }
-  if (!Map2D(&mv, vt, (uint64_t)S, (uint64_t)B * H * D, 64, D)) return -2;
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid((unsigned)(B * H * (S / (2 * TQ))));
-  attn_fwd_kernel<D, CAUSAL><<<grid, 320, Cf::kSmem, st>>>(mq, mk, mv, (__nv_bfloat16*)o, H, S, scale_log2);
+  attn_fwd_kernel<D, CAUSAL, VT><<<grid, 320, Cf::kSmem, st>>>(mq, mk, mv, (__nv_bfloat16*)o, H, S, scale_log2);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
+bool AttentionShapeOk(int B, int H, int S, int D) {
+  return B > 0 && H > 0 && D == 64 && S > 0 && S % (2 * TQ) == 0 && (long long)B * H * S <= INT32_MAX;
+}
+
+// V read in place (MN-major operand); no scratch memory.
+int AttentionFwd(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D, int causal, float scale,
+                 cudaStream_t st) {
+  if (!AttentionShapeOk(B, H, S, D)) return -1;
+  if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)o) % 16) return -1;
+  if (causal) return LaunchAttn<64, true, false>(q, k, v, o, B, H, S, scale, st);
+  return LaunchAttn<64, false, false>(q, k, v, o, B, H, S, scale, st);
+}
+
+// Cross-check variant: V transposed into `vt` (B*H*S*D bf16 scratch) and read K-major.
 int AttentionFwdWithVt(const void* q, const void* k, const void* v, void* vt, void* o, int B, int H, int S, int D,
                        int causal, float scale, cudaStream_t st) {
-  if (B <= 0 || H <= 0 || S <= 0) return 0;
-  if (D != 64 || S % (2 * TQ) != 0) return -1;
+  if (!AttentionShapeOk(B, H, S, D)) return -1;
   if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)vt | (uintptr_t)o) % 16) return -1;
-  if ((long long)B * H * S > INT32_MAX) return -1;
   dim3 tg(S / 64, D / 64, B * H);
   transpose_v_kernel<<<tg, 256, 0, st>>>((const uint16_t*)v, (uint16_t*)vt, S, D);
-  if (causal) return LaunchAttn<64, true>(q, k, vt, o, B, H, S, scale, st);
-  return LaunchAttn<64, false>(q, k, vt, o, B, H, S, scale, st);
+  if (causal) return LaunchAttn<64, true, true>(q, k, vt, o, B, H, S, scale, st);
+  return LaunchAttn<64, false, true>(q, k, vt, o, B, H, S, scale, st);
 }
 
 int TakeAttnError() {
@@ -400,13 +429,12 @@ int TakeAttnError() {
 
 extern "C" int b200_attention_fwd(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D,
                                   int causal, float scale, void* stream) {
-  cudaStream_t st = (cudaStream_t)stream;
-  if (B <= 0 || H <= 0 || S <= 0) return 0;
-  if (D != 64 || S % 256 != 0) return -1;
-  size_t bytes = (size_t)B * H * S * D * 2;
-  void* vt = nullptr;
-  if (cudaMallocAsync(&vt, bytes, st) != cudaSuccess) return -4;
-  int rc = b200k::AttentionFwdWithVt(q, k, v, vt, o, B, H, S, D, causal, scale, st);
-  cudaFreeAsync(vt, st);
-  return rc;
+  if (B == 0 || H == 0 || S == 0) return 0;
+  return b200k::AttentionFwd(q, k, v, o, B, H, S, D, causal, scale, (cudaStream_t)stream);
+}
+
+extern "C" int b200_attention_fwd_vt(const void* q, const void* k, const void* v, void* vt, void* o, int B, int H, int S,
+                                     int D, int causal, float scale, void* stream) {
+  if (B == 0 || H == 0 || S == 0) return 0;
+  return b200k::AttentionFwdWithVt(q, k, v, vt, o, B, H, S, D, causal, scale, (cudaStream_t)stream);
 }

@@ -144,7 +144,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int a = local & 1;
       const uint32_t aph = (local >> 1) & 1;
-      if (!mbar_wait(&acc_full[a], aph, kErrTimeoutAcc, &g_tc_error_gemm)) break;
+      if (!mbar_wait_warp(&acc_full[a], aph, kErrTimeoutAcc, &g_tc_error_gemm)) break;
       tc_fence_after();
       const int b = t / per_batch, r = t % per_batch;
       const int m_blk = r % mb, n_blk = r / mb;

@@ -68,6 +68,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
   }
 }
 
+// Warp-uniform form of mbar_wait for warps that go on to warp-collective (.sync.aligned) tcgen05
+// instructions: every lane returns the same answer, so a timeout seen by one lane cannot leave the
+// warp diverged in front of a tcgen05.ld / st.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int code, int* flag) {
+  const bool ok = mbar_wait(bar, parity, code, flag);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ---- TMA (tiled, no multicast) ----------------------------------------------------------------
 __device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1, int c2) {
   asm volatile(

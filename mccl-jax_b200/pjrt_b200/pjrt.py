@@ -230,9 +230,10 @@ class Buffer:
         return out
 
     def delete(self):
-        if self.h:
+        # a buffer outliving its client is dropped without a call: the client freed the device
+        if self.h and self.client.h:
             self.api.call("Buffer_Destroy", BufferArgs(buffer=self.h))
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:
@@ -271,9 +272,15 @@ class Executable:
         return outs
 
     def destroy(self):
-        if self.h:
+        if self.h and self.client.h:
             self.client.api.call("LoadedExecutable_Destroy", LoadedArgs(executable=self.h))
-            self.h = None
+        self.h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
 
 
 class Client:
@@ -369,14 +376,16 @@ class Client:
 
     def run(self, text_or_exe, inputs: Sequence[np.ndarray]) -> List[np.ndarray]:
         exe = self.compile(text_or_exe) if isinstance(text_or_exe, str) else text_or_exe
-        bufs = [self.buffer_from_host(x) for x in inputs]
-        outs = exe.execute(bufs)
-        res = [o.to_numpy() for o in outs]
-        for b in bufs + outs:
-            b.delete()
-        if isinstance(text_or_exe, str):
-            exe.destroy()
-        return res
+        bufs, outs = [], []
+        try:
+            bufs = [self.buffer_from_host(x) for x in inputs]
+            outs = exe.execute(bufs)
+            return [o.to_numpy() for o in outs]
+        finally:
+            for b in bufs + outs:
+                b.delete()
+            if isinstance(text_or_exe, str):
+                exe.destroy()
 
     def close(self):
         if self.h:

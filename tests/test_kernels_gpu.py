@@ -75,6 +75,45 @@ def test_attention_fwd(lib, cuda, B, H, S, causal):
     assert rel_err(o.float().cpu().numpy(), ref.cpu().numpy()) <= RTOL_BF16
 
 
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_vt_variant_agrees(lib, cuda, causal):
+    """V read MN-major in place vs V transposed first and read K-major: two operand layouts."""
+    torch = cuda
+    B, H, S, D = 2, 2, 512, 64
+    g = torch.Generator(device="cuda").manual_seed(99)
+    q, k, v = (torch.randn(B, H, S, D, device="cuda", generator=g).to(torch.bfloat16) for _ in range(3))
+    o1, o2, vt = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
+    lib.b200_attention_fwd_vt.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_void_p]
+    assert lib.b200_attention_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o1.data_ptr(), B, H, S, D, int(causal),
+                                  0.125, stream(torch)) == 0
+    assert lib.b200_attention_fwd_vt(q.data_ptr(), k.data_ptr(), v.data_ptr(), vt.data_ptr(), o2.data_ptr(), B, H, S, D,
+                                     int(causal), 0.125, stream(torch)) == 0
+    torch.cuda.synchronize()
+    check_device_error(lib)
+    assert rel_err(o1.float().cpu().numpy(), o2.float().cpu().numpy()) <= 1e-2
+    ref = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float(), is_causal=causal)
+    assert rel_err(o2.float().cpu().numpy(), ref.cpu().numpy()) <= RTOL_BF16
+
+
+def test_attention_large_logits_rescale(lib, cuda):
+    """Scores spread over hundreds of units exercise the lazy O rescaling (max moves by > 2^8)."""
+    torch = cuda
+    B, H, S, D = 1, 2, 1024, 64
+    g = torch.Generator(device="cuda").manual_seed(5)
+    q = (torch.randn(B, H, S, D, device="cuda", generator=g) * 4).to(torch.bfloat16)
+    k = (torch.randn(B, H, S, D, device="cuda", generator=g) * 4).to(torch.bfloat16)
+    ramp = torch.linspace(0, 3, S, device="cuda").view(1, 1, S, 1)
+    k = (k.float() * (1 + ramp)).to(torch.bfloat16)            # later keys dominate: the max keeps rising
+    v = torch.randn(B, H, S, D, device="cuda", generator=g).to(torch.bfloat16)
+    o = torch.empty_like(q)
+    assert lib.b200_attention_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, H, S, D, 0, 0.125,
+                                  stream(torch)) == 0
+    torch.cuda.synchronize()
+    check_device_error(lib)
+    ref = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float(), scale=0.125)
+    assert rel_err(o.float().cpu().numpy(), ref.cpu().numpy()) <= RTOL_BF16
+
+
 def test_attention_rejects_unsupported_shapes(lib, cuda):
     torch = cuda
     q = torch.zeros(1, 1, 200, 64, device="cuda", dtype=torch.bfloat16)
