@@ -73,6 +73,43 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// Packed f32x2 arithmetic (sm_100): two fp32 lanes in one 64-bit register pair per instruction.
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t pack2u(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ float lo_f(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo;
+}
+__device__ __forceinline__ float hi_f(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return hi;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // MN-major operand in the 128-byte swizzle layout: rows of 128 B along K (here: keys), the 64-element
 // MN extent inside one row; SBO = 1024 B between 8-row groups along K.
 __device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t addr) {
@@ -246,15 +283,17 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       tc_fence_before();
       mbar_arrive(&bars[kSFree + t]);        // S_t may be overwritten by the next Q K^T
       const int key0 = j * TK;
-      const bool need_mask = CAUSAL && (key0 + TK - 1 > q0 + t * TQ);
-      float mx = -INFINITY;
+      if (CAUSAL && key0 + TK - 1 > q0 + t * TQ) {   // diagonal tile: keys after the query are -inf
 #pragma unroll
-      for (int e = 0; e < TK; ++e) {
-        float s = __uint_as_float(sv[e]) * scale_log2;
-        if (need_mask && key0 + e > qrow) s = -INFINITY;
-        sv[e] = __float_as_uint(s);
-        mx = fmaxf(mx, s);
+        for (int e = 0; e < TK; ++e)
+          if (key0 + e > qrow) sv[e] = 0xff800000u;
       }
+      // row max of the raw scores (scale > 0 commutes with max), three at a time
+      float mx = __uint_as_float(sv[0]);
+#pragma unroll
+      for (int e = 1; e + 1 < TK; e += 2) mx = fmax3(mx, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
+      mx = fmaxf(mx, __uint_as_float(sv[TK - 1]));
+      mx *= scale_log2;
       // P smem and the O accumulator are free once the previous P V product has completed
       if (j > 0 && !mbar_wait_warp(&bars[kPVFull + t], (j - 1) & 1, kErrTimeoutAcc, err)) { ok = false; break; }
       tc_fence_after();
@@ -280,16 +319,18 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         }
         m_use = m_new;
       }
-      float sum = 0.f;
       const float mu = m_use == -INFINITY ? 0.f : m_use;   // a row masked so far contributes p = 0
+      // p = 2^(s * scale_log2 - m): one packed FMA per two scores, packed adds for the row sum
+      const uint64_t sc2 = pack2(scale_log2, scale_log2), nm2 = pack2(-mu, -mu);
+      uint64_t sum2 = pack2(0.f, 0.f);
 #pragma unroll
       for (int c = 0; c < TK; c += 16) {
         uint32_t pk[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float p0 = ex2(__uint_as_float(sv[c + 2 * e]) - mu);
-          const float p1 = ex2(__uint_as_float(sv[c + 2 * e + 1]) - mu);
-          sum += p0 + p1;
+          const uint64_t x2 = ffma2(pack2u(sv[c + 2 * e], sv[c + 2 * e + 1]), sc2, nm2);
+          const float p0 = ex2(lo_f(x2)), p1 = ex2(hi_f(x2));
+          sum2 = fadd2(sum2, pack2(p0, p1));
           pk[e] = pack_bf16(p0, p1);
         }
         // keys c .. c+15 = two 16-byte chunks of row r in the 64-key block c / 64 (128-byte swizzle)
@@ -299,7 +340,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         *(uint4*)(rowp + ((ch0 ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         *(uint4*)(rowp + (((ch0 + 1) ^ (r & 7)) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
-      l += sum;
+      l += lo_f(sum2) + hi_f(sum2);
       tc_fence_before();
       fence_async_smem();
       mbar_arrive(&bars[kPFull + t]);
