@@ -211,6 +211,10 @@ def main():
     ap.add_argument("--H", type=int, default=HEAD["H"])
     ap.add_argument("--S", type=int, default=HEAD["S"])
     ap.add_argument("--causal", action="store_true")
+    ap.add_argument("--workload", default="attention", choices=["attention", "dp", "gemm", "psum"],
+                    help="attention (headline); dp = GPT-2 DP train step; gemm = dot_general sweep; "
+                         "psum = all_reduce bandwidth sweep")
+    ap.add_argument("--layers", type=int, default=12, help="dp: decoder layers")
     a = ap.parse_args()
     HEAD.update(B=a.B, H=a.H, S=a.S, causal=a.causal)
     a.warmup = max(a.warmup, 3)
@@ -218,6 +222,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if a.impl == "b200" and a.workload != "attention":
+        import workloads  # mccl-jax_b200/workloads.py
+        return workloads.run(a, world, rank, local)
 
     if a.impl == "reference":
         if rank != 0:

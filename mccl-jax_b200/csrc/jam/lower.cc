@@ -320,8 +320,9 @@ struct Gen {
       return r;
     }
     if (n == "pad") {
-      const auto& lo = op->ints.at("edge_padding_low");
-      const auto& it = op->ints.at("interior_padding");
+      // pretty form: low / high / interior; generic form: edge_padding_low / interior_padding
+      const auto& lo = op->ints.count("low") ? op->ints.at("low") : op->ints.at("edge_padding_low");
+      const auto& it = op->ints.count("interior") ? op->ints.at("interior") : op->ints.at("interior_padding");
       std::string pv = Emit(op->operands[1], {});
       std::string r = "t" + std::to_string(tmp++);
       body << indent << CType(ty.dt) << " " << r << " = " << pv << ";\n";
@@ -495,7 +496,10 @@ class Lowerer {
     EmitSteps();
     BindOutputs();
     ComputeLastUse();
-    p_->cuda_source = std::string(kPrelude) + src_.str();
+    EndKernel();
+    p_->cuda_prelude = kPrelude;
+    p_->cuda_source = kPrelude;
+    for (const auto& k : p_->kernel_sources) p_->cuda_source += k;
     p_->num_partitions = g_.num_partitions;
   }
 
@@ -509,6 +513,13 @@ class Lowerer {
   std::unordered_map<int, AttentionStep> attn_;  // result value id of the 2nd dot -> matched attention
   std::unordered_map<int, std::array<const Value*, 3>> attn_in_;
   std::ostringstream src_;
+  // Each finished kernel's source becomes its own unit so NVRTC can compile them in parallel.
+  void EndKernel() {
+    std::string k = src_.str();
+    if (!k.empty()) p_->kernel_sources.push_back(k);
+    src_.str("");
+    src_.clear();
+  }
   int kcount_ = 0;
 
   int NewSlot(int64_t bytes) {
@@ -909,14 +920,37 @@ class Lowerer {
     std::vector<DT> in_dts;
     for (int s : gen.in_slots) in_dts.push_back(SlotDt(s));
     std::string fn = KName();
-    src_ << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "("
-         << KernelParams(gen.in_slots, (int)out_slots.size(), false) << ") {\n"
-         << ParamCasts(gen.in_slots, in_dts, out_dts)
-         << "  for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < " << n << "LL; i += (long long)gridDim.x * 256) {\n"
+    // The per-element body is an inlined device function; the grid-stride loop calls it for four
+    // independent elements per iteration so each thread keeps four loads in flight (one 4-byte load
+    // per thread cannot cover HBM latency: Little's law caps that near 1.5 TB/s on 148 SMs).
+    std::string args_decl, args_use;
+    for (size_t k = 0; k < gen.in_slots.size(); ++k) {
+      args_decl += ", const " + MemType(in_dts[k]) + "* __restrict__ in" + std::to_string(k);
+      args_use += ", in" + std::to_string(k);
+    }
+    for (size_t k = 0; k < out_dts.size(); ++k) {
+      args_decl += ", " + MemType(out_dts[k]) + "* __restrict__ out" + std::to_string(k);
+      args_use += ", out" + std::to_string(k);
+    }
+    src_ << "static __device__ __forceinline__ void " << fn << "_elem(long long i" << args_decl << ") {\n"
          << gen.body.str();
     for (size_t k = 0; k < roots.size(); ++k)
       src_ << "    out" << k << "[i] = " << StoreExpr(out_dts[k], regs[k]) << ";\n";
-    src_ << "  }\n}\n";
+    src_ << "}\n";
+    src_ << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "("
+         << KernelParams(gen.in_slots, (int)out_slots.size(), false) << ") {\n"
+         << ParamCasts(gen.in_slots, in_dts, out_dts)
+         << "  const long long st = (long long)gridDim.x * 256;\n"
+         << "  long long i = (long long)blockIdx.x * 256 + threadIdx.x;\n"
+         << "  for (; i + 3 * st < " << n << "LL; i += 4 * st) {\n"
+         << "    " << fn << "_elem(i" << args_use << ");\n"
+         << "    " << fn << "_elem(i + st" << args_use << ");\n"
+         << "    " << fn << "_elem(i + 2 * st" << args_use << ");\n"
+         << "    " << fn << "_elem(i + 3 * st" << args_use << ");\n"
+         << "  }\n"
+         << "  for (; i < " << n << "LL; i += st) " << fn << "_elem(i" << args_use << ");\n"
+         << "}\n";
+    EndKernel();
     Launch L;
     L.fn = fn;
     L.in_slots = gen.in_slots;
@@ -1025,7 +1059,7 @@ class Lowerer {
         k << "  __shared__ " << acc_t << " red[32];\n"
           << "  for (long long row = blockIdx.x; row < " << n_out << "LL; row += gridDim.x) {\n"
           << ob.str() << "    " << acc_t << " acc = " << init_expr << ";\n"
-          << "    for (long long j = threadIdx.x; j < " << L << "LL; j += " << threads << ") {\n"
+          << "#pragma unroll 4\n    for (long long j = threadIdx.x; j < " << L << "LL; j += " << threads << ") {\n"
           << gen.body.str() << "      acc = " << combine("acc", "(" + acc_t + ")(" + v + ")") << ";\n    }\n"
           << shfl_red
           << "    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;\n    __syncthreads();\n"
@@ -1043,7 +1077,7 @@ class Lowerer {
         k << "  const int lane = threadIdx.x & 31;\n"
           << "  for (long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); row < " << n_out << "LL; row += (long long)gridDim.x * 8) {\n"
           << ob.str() << "    " << acc_t << " acc = " << init_expr << ";\n"
-          << "    for (long long j = lane; j < " << L << "LL; j += 32) {\n"
+          << "#pragma unroll 4\n    for (long long j = lane; j < " << L << "LL; j += 32) {\n"
           << gen.body.str() << "      acc = " << combine("acc", "(" + acc_t + ")(" + v + ")") << ";\n    }\n"
           << shfl_red << "    if (lane == 0) out0[row] = " << StoreExpr(odt, "acc") << ";\n  }\n}\n";
         Launch Lc;
@@ -1082,7 +1116,7 @@ class Lowerer {
         << ob.str() << "  " << acc_t << " acc = " << (chunks > 1 ? "(" + acc_t + ")(" + IdentityOf(kind, acc_dt) + ")" : init_expr) << ";\n"
         << "    long long j0 = (long long)blockIdx.y * " << per << "LL;\n"
         << "    long long j1 = j0 + " << per << "LL < " << L << "LL ? j0 + " << per << "LL : " << L << "LL;\n"
-        << "    for (long long j = j0; j < j1; ++j) {\n"
+        << "#pragma unroll 4\n    for (long long j = j0; j < j1; ++j) {\n"
         << gen.body.str() << "      acc = " << combine("acc", "(" + acc_t + ")(" + v + ")") << ";\n    }\n";
       if (chunks > 1) k << "  ((" << acc_t << "*)scratch)[(long long)blockIdx.y * " << n_out << "LL + o] = acc;\n}\n";
       else k << "  out0[o] = " << StoreExpr(odt, "acc") << ";\n}\n";
@@ -1118,6 +1152,7 @@ class Lowerer {
       }
     }
     src_ << k.str();
+    EndKernel();
     RecordDt(out_slot, odt);
     p_->steps.push_back(st);
   }
@@ -1137,11 +1172,85 @@ class Lowerer {
 
   // ---------------------------------------------------------------- dot_general
   // Materialises `v` permuted by `perm` (and optionally converted) into a new slot.
-  int EmitPermute(const Value* v, const std::vector<int>& perm, const std::vector<int64_t>& out_dims, DT out_dt) {
+  // A permutation that moves the innermost dim: 32 x 32 tiles through shared memory so both the
+  // reads (along the source's innermost dim) and the writes (along the output's) are coalesced.
+  // Output dim q holds the source's innermost dim; the output's innermost dim is source dim perm[r-1].
+  void EmitTiledTranspose(const Value* v, const std::vector<int>& perm, const std::vector<int64_t>& od, DT out_dt,
+                          int64_t pitch, int src, int dst) {
+    const int r = (int)perm.size();
+    const auto& sd = v->type.dims;
+    std::vector<int64_t> sstr(r, 1), ostr(r, 1);
+    for (int k = r - 2; k >= 0; --k) sstr[k] = sstr[k + 1] * sd[k + 1];
+    ostr[r - 1] = 1;
+    if (r >= 2) ostr[r - 2] = pitch;
+    for (int k = r - 3; k >= 0; --k) ostr[k] = ostr[k + 1] * od[k + 1];
+    int q = 0;
+    for (int k = 0; k < r; ++k) if (perm[k] == r - 1) q = k;
+    const int64_t A = od[q], Bn = od[r - 1];
+    const int64_t S_in = sstr[perm[r - 1]];      // source stride of the output's innermost dim
+    const int64_t O_q = ostr[q];                 // output stride of dim q
+    std::vector<int> rest_dims;
+    int64_t R = 1;
+    for (int k = 0; k < r; ++k)
+      if (k != q && k != r - 1) { rest_dims.push_back(k); R *= od[k]; }
+    DT in_dt = v->type.dt;
+    std::string fn = KName();
+    std::ostringstream o;
+    o << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const void* __restrict__ p0, void* __restrict__ q0) {\n"
+      << "  const " << MemType(in_dt) << "* __restrict__ in0 = (const " << MemType(in_dt) << "*)p0;\n"
+      << "  " << MemType(out_dt) << "* __restrict__ out0 = (" << MemType(out_dt) << "*)q0;\n"
+      << "  __shared__ " << CType(in_dt) << " tile[32][33];\n"
+      << "  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;\n"
+      << "  const long long a0 = (long long)blockIdx.y * 32, b0 = (long long)blockIdx.x * 32;\n"
+      << "  for (long long rr = blockIdx.z; rr < " << R << "LL; rr += gridDim.z) {\n"
+      << "    long long rem = rr, soff = 0, ooff = 0;\n";
+    for (int k = (int)rest_dims.size() - 1; k >= 0; --k) {
+      int d = rest_dims[k];
+      o << "    { long long ix = rem % " << od[d] << "LL; rem /= " << od[d] << "LL; soff += ix * " << sstr[perm[d]]
+        << "LL; ooff += ix * " << ostr[d] << "LL; }\n";
+    }
+    o << "#pragma unroll\n    for (int j = 0; j < 4; ++j) {\n"
+      << "      const long long a = a0 + tx, bb = b0 + ty + 8 * j;\n"
+      << "      if (a < " << A << "LL && bb < " << Bn << "LL) tile[ty + 8 * j][tx] = " << LoadExpr(in_dt, "in0", "soff + a + bb * " + std::to_string(S_in) + "LL") << ";\n"
+      << "    }\n    __syncthreads();\n"
+      << "#pragma unroll\n    for (int j = 0; j < 4; ++j) {\n"
+      << "      const long long bb = b0 + tx, a = a0 + ty + 8 * j;\n"
+      << "      if (a < " << A << "LL && bb < " << Bn << "LL) out0[ooff + a * " << O_q << "LL + bb] = " << StoreExpr(out_dt, "tile[tx][ty + 8 * j]") << ";\n"
+      << "    }\n    __syncthreads();\n  }\n}\n";
+    src_ << o.str();
+    EndKernel();
+    Launch L;
+    L.fn = fn;
+    L.in_slots = {src};
+    L.out_slots = {dst};
+    L.block = 256;
+    L.grid_x = (Bn + 31) / 32;
+    L.grid_y = (A + 31) / 32;
+    L.grid_z = std::max<int64_t>(1, std::min<int64_t>(R, 65535));
+    Step st;
+    st.kind = StepKind::kFusion;
+    st.launches.push_back(L);
+    st.label = "transpose " + v->type.str();
+    p_->steps.push_back(st);
+    RecordDt(dst, out_dt);
+  }
+
+  // Materialises `v` permuted by `perm` (and converted to out_dt) into a new slot.  With
+  // `inner_pitch` > 0 the innermost dim is stored with that row pitch (elements), leaving the pad
+  // columns unwritten: used to give TMA a 16-byte-aligned row stride.
+  int EmitPermute(const Value* v, const std::vector<int>& perm, const std::vector<int64_t>& out_dims, DT out_dt,
+                  int64_t inner_pitch = 0) {
     int src = SlotFor(v);
     int64_t n = 1;
     for (int64_t d : out_dims) n *= d;
-    int dst = NewSlot(n * DTBytes(out_dt));
+    const int64_t inner = out_dims.empty() ? 1 : out_dims.back();
+    const int64_t pitch = inner_pitch > 0 ? inner_pitch : inner;
+    int dst = NewSlot(n / std::max<int64_t>(inner, 1) * pitch * DTBytes(out_dt));
+    const int rank = (int)perm.size();
+    if (rank >= 2 && perm.back() != rank - 1 && n > 0) {
+      EmitTiledTranspose(v, perm, out_dims, out_dt, pitch, src, dst);
+      return dst;
+    }
     std::ostringstream body;
     auto names = Delinearize(body, "i", out_dims, "i", "    ", n >= (1LL << 31));
     // out index k corresponds to source dim perm[k]
@@ -1149,11 +1258,14 @@ class Lowerer {
     for (size_t k = 0; k < perm.size(); ++k) sidx[perm[k]] = names[k];
     std::string fn = KName();
     DT in_dt = v->type.dt;
+    std::string oidx = pitch == inner ? "i" : "(i / " + std::to_string(inner) + "LL) * " + std::to_string(pitch) +
+                                                 "LL + i % " + std::to_string(inner) + "LL";
     src_ << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const void* __restrict__ p0, void* __restrict__ q0) {\n"
          << "  const " << MemType(in_dt) << "* in0 = (const " << MemType(in_dt) << "*)p0;\n"
          << "  " << MemType(out_dt) << "* out0 = (" << MemType(out_dt) << "*)q0;\n"
          << "  for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < " << n << "LL; i += (long long)gridDim.x * 256) {\n"
-         << body.str() << "    out0[i] = " << StoreExpr(out_dt, LoadExpr(in_dt, "in0", Gen::Linear(sidx, v->type.dims))) << ";\n  }\n}\n";
+         << body.str() << "    out0[" << oidx << "] = " << StoreExpr(out_dt, LoadExpr(in_dt, "in0", Gen::Linear(sidx, v->type.dims))) << ";\n  }\n}\n";
+    EndKernel();
     Launch L;
     L.fn = fn;
     L.in_slots = {src};
@@ -1189,22 +1301,32 @@ class Lowerer {
     g.K = prod(a, lc);
     DT at = a->type.dt, bt = b->type.dt;
     if (!DTIsFloat(at) || !DTIsFloat(bt)) throw LowerError{"dot_general on non-float operands is not supported"};
-    DT ab = (at == DT::kF32 || bt == DT::kF32 || at == DT::kF64 || bt == DT::kF64) ? DT::kF32 : at;
-    if (at != bt && ab != DT::kF32) ab = DT::kF32;
-    if (ab == DT::kF16 || ab == DT::kBF16 || ab == DT::kF32) {} else ab = DT::kF32;
+    // Operand type of the GEMM: both f32 (or f64) -> f32 SIMT (the f32 precision bar); otherwise a
+    // 16-bit type on the tensor cores.  A 16-bit operand times an f32 one (the cotangent of an f32
+    // dot result meeting bf16 weights in a backward pass) runs in the 16-bit type: the f32 operand is
+    // rounded once, the result keeps f32 accumulation (B200_DOT_MIXED_F32=1 keeps such dots in f32).
+    auto wide = [](DT t) { return t == DT::kF32 || t == DT::kF64; };
+    DT ab;
+    if (wide(at) && wide(bt)) ab = DT::kF32;
+    else if (!wide(at) && !wide(bt)) ab = at == bt ? at : DT::kBF16;
+    else ab = std::getenv("B200_DOT_MIXED_F32") ? DT::kF32 : (wide(at) ? bt : at);
+    if (ab != DT::kF16 && ab != DT::kBF16 && ab != DT::kF32) ab = DT::kF32;
     g.ab = ab;
     g.out = r->type.dt;
     if (g.out != DT::kF32 && g.out != DT::kBF16 && g.out != DT::kF16) throw LowerError{"dot_general result type not supported"};
+    // TMA needs 16-byte row strides: a 16-bit operand with K % 8 != 0 is copied with a padded pitch
+    const int64_t pitch = (ab != DT::kF32 && g.K % 8 != 0) ? (g.K + 7) / 8 * 8 : 0;
+    g.lda = g.ldb = pitch ? pitch : g.K;
     // A as [batch, M, K]: permutation lb + lf + lc of a's dims
     auto operand = [&](const Value* v, std::vector<int64_t> order, DT want, const std::vector<int64_t>& shape3) {
       std::vector<int> perm(order.begin(), order.end());
       bool ident = true;
       for (size_t k = 0; k < perm.size(); ++k) ident = ident && perm[k] == (int)k;
-      if (ident && v->type.dt == want) return SlotFor(v);
+      if (ident && v->type.dt == want && !pitch) return SlotFor(v);
       std::vector<int64_t> od;
       for (int q : perm) od.push_back(v->type.dims[q]);
       (void)shape3;
-      return EmitPermute(v, perm, od, want);
+      return EmitPermute(v, perm, od, want, pitch);
     };
     std::vector<int64_t> aord = lb;
     aord.insert(aord.end(), lf.begin(), lf.end());

@@ -30,7 +30,7 @@ struct Launch {
   std::vector<int> in_slots;   // pointer params first, in this order
   std::vector<int> out_slots;  // then output pointers
   int scratch = -1;            // scratch slot appended as the last pointer (-1: none)
-  int64_t grid_x = 1, grid_y = 1;
+  int64_t grid_x = 1, grid_y = 1, grid_z = 1;
   int block = 256;
   int smem = 0;
 };
@@ -38,6 +38,7 @@ struct Launch {
 struct GemmStep {
   int a = -1, b = -1, c = -1;  // A[batch,M,K], B[batch,N,K] (K-major), C[batch,M,N] row-major
   int64_t batch = 1, M = 0, N = 0, K = 0;
+  int64_t lda = 0, ldb = 0;    // row pitch of A / B in elements (>= K; K rounded up to 8 for TMA)
   DT ab = DT::kBF16, out = DT::kF32;
 };
 
@@ -89,7 +90,9 @@ struct Plan {
   std::vector<Slot> slots;
   std::vector<Step> steps;
   std::vector<ConstBlob> consts;
-  std::string cuda_source;           // every generated kernel, one NVRTC module
+  std::string cuda_prelude;          // helpers every generated kernel uses
+  std::vector<std::string> kernel_sources;  // one entry per generated kernel (or reduction pair)
+  std::string cuda_source;           // prelude + every kernel (for dumps)
   std::vector<int> arg_slots;        // per @main argument
   std::vector<TensorType> arg_types; // after shard_map retyping
   std::vector<int> out_slots;        // per @main result

@@ -9,11 +9,14 @@
 #include <cstdlib>
 #include <cstring>
 #include <fstream>
+#include <thread>
 
 #include "../../../include/b200_kernels.h"
 #include "../comm/comm.h"
 
 namespace b200k {
+int Gemm(const void* A, long long lda, const void* B, long long ldb, void* C, int64_t batch, int64_t M, int64_t N,
+         int64_t K, int ab_type, int out_type, cudaStream_t st);
 int AttentionFwd(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D, int causal, float scale,
                  cudaStream_t st);
 }
@@ -96,6 +99,38 @@ struct StepTimer {
   int runs = 0;
 };
 
+// Execution timer (b200_exec_timer): a start event recorded by the first execution after a reset
+// and an end event re-recorded by every execution, both on the device stream.
+struct ExecTimer {
+  std::mutex mu;
+  bool armed = false, started = false;
+  int device = -1;
+  cudaEvent_t start = nullptr, end = nullptr;
+};
+ExecTimer& GetExecTimer() {
+  static ExecTimer t;
+  return t;
+}
+
+void ExecTimerMarkStart(int device, cudaStream_t st) {
+  ExecTimer& t = GetExecTimer();
+  std::lock_guard<std::mutex> lock(t.mu);
+  if (!t.armed || t.started) return;
+  if (!t.start) {
+    cudaEventCreate(&t.start);
+    cudaEventCreate(&t.end);
+  }
+  cudaEventRecord(t.start, st);
+  t.device = device;
+  t.started = true;
+}
+
+void ExecTimerMarkEnd(int device, cudaStream_t st) {
+  ExecTimer& t = GetExecTimer();
+  std::lock_guard<std::mutex> lock(t.mu);
+  if (t.armed && t.started && t.device == device) cudaEventRecord(t.end, st);
+}
+
 }  // namespace
 
 std::string DeviceAlloc(size_t bytes, cudaStream_t stream, void** out) {
@@ -122,11 +157,30 @@ std::string Executable::Build(const char* text, size_t n, const CompileOptions& 
   ex->name_ = g.name.empty() ? "b200.main" : g.name;
   if (std::getenv("B200_DUMP_PLAN")) std::fprintf(stderr, "%s", ex->plan_.dump().c_str());
   if (const char* dump = std::getenv("B200_DUMP_CUDA")) std::ofstream(dump) << ex->plan_.cuda_source;
-  bool any_fusion = false;
-  for (const Step& s : ex->plan_.steps) any_fusion |= s.kind == StepKind::kFusion;
-  if (any_fusion) {
-    err = Nvrtc(ex->plan_.cuda_source, &ex->cubin_);
-    if (!err.empty()) return err;
+  // NVRTC: the generated kernels are split into groups compiled as separate modules on parallel
+  // threads (one large module of a train step takes tens of seconds on one thread).
+  const auto& ks = ex->plan_.kernel_sources;
+  if (!ks.empty()) {
+    unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    size_t groups = std::min<size_t>(std::min<size_t>(hw, 32), (ks.size() + 7) / 8);
+    groups = std::max<size_t>(groups, 1);
+    std::vector<std::string> srcs(groups, ex->plan_.cuda_prelude);
+    size_t total = 0;
+    for (const auto& k : ks) total += k.size();
+    size_t per = total / groups + 1, g = 0, acc = 0;
+    for (const auto& k : ks) {
+      if (acc > per && g + 1 < groups) { ++g; acc = 0; }
+      srcs[g] += k;
+      acc += k.size();
+    }
+    ex->cubins_.assign(groups, {});
+    std::vector<std::string> errs(groups);
+    std::vector<std::thread> th;
+    for (size_t i = 0; i < groups; ++i)
+      th.emplace_back([&, i] { errs[i] = Nvrtc(srcs[i], &ex->cubins_[i]); });
+    for (auto& t : th) t.join();
+    for (auto& e : errs)
+      if (!e.empty()) return e;
   }
   *out = std::move(ex);
   return "";
@@ -137,7 +191,8 @@ Executable::~Executable() {
   for (auto& kv : per_dev_) {
     cudaSetDevice(kv.first);
     for (void* p : kv.second.consts) cudaFree(p);
-    if (kv.second.module && d.ok) d.unload((CUmodule)kv.second.module);
+    if (d.ok)
+      for (void* m : kv.second.modules) d.unload((CUmodule)m);
   }
 }
 
@@ -146,18 +201,22 @@ std::string Executable::Load(DeviceState& dev, PerDevice** pd) {
   auto it = per_dev_.find(dev.ordinal);
   if (it != per_dev_.end()) { *pd = &it->second; return ""; }
   PerDevice p;
-  if (!cubin_.empty()) {
+  if (!cubins_.empty()) {
     const Driver& d = Drv();
     if (!d.ok) return "CUDA driver entry points unavailable";
-    CUmodule m;
-    CUresult r = d.load(&m, cubin_.data());
-    if (r != CUDA_SUCCESS) return "cuModuleLoadData failed (" + std::to_string((int)r) + ")";
-    p.module = m;
+    for (const auto& cubin : cubins_) {
+      CUmodule m;
+      CUresult r = d.load(&m, cubin.data());
+      if (r != CUDA_SUCCESS) return "cuModuleLoadData failed (" + std::to_string((int)r) + ")";
+      p.modules.push_back(m);
+    }
     for (const Step& s : plan_.steps)
       for (const Launch& L : s.launches) {
         if (p.fns.count(L.fn)) continue;
-        CUfunction f;
-        if (d.get(&f, m, L.fn.c_str()) != CUDA_SUCCESS) return "generated kernel " + L.fn + " not found";
+        CUfunction f = nullptr;
+        for (void* m : p.modules)
+          if (d.get(&f, (CUmodule)m, L.fn.c_str()) == CUDA_SUCCESS) break;
+        if (!f) return "generated kernel " + L.fn + " not found";
         p.fns[L.fn] = f;
       }
   }
@@ -196,6 +255,7 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
       if (owned[s]) DeviceFree(ptr[s], st);
     return e;
   };
+  ExecTimerMarkStart(dev.ordinal, st);
   static StepTimer timer;
   std::vector<cudaEvent_t> evs;
   if (timer.on) {
@@ -215,7 +275,7 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
           if (L.scratch >= 0) { err = slot(L.scratch); if (!err.empty()) return fail(err); vals.push_back(ptr[L.scratch]); }
           std::vector<void*> params;
           for (void*& v : vals) params.push_back(&v);
-          CUresult r = drv.launch((CUfunction)pd->fns.at(L.fn), (unsigned)L.grid_x, (unsigned)L.grid_y, 1, L.block, 1, 1,
+          CUresult r = drv.launch((CUfunction)pd->fns.at(L.fn), (unsigned)L.grid_x, (unsigned)L.grid_y, (unsigned)L.grid_z, L.block, 1, 1,
                                   L.smem, (CUstream)st, params.data(), nullptr);
           if (r != CUDA_SUCCESS) return fail("launch of " + L.fn + " failed (" + std::to_string((int)r) + ")");
         }
@@ -224,7 +284,8 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
       case StepKind::kGemm: {
         const GemmStep& g = S.gemm;
         for (int s : {g.a, g.b, g.c}) { err = slot(s); if (!err.empty()) return fail(err); }
-        int rc = b200_gemm(ptr[g.a], ptr[g.b], ptr[g.c], g.batch, g.M, g.N, g.K, PjrtType(g.ab), PjrtType(g.out), st);
+        int rc = b200k::Gemm(ptr[g.a], g.lda ? g.lda : g.K, ptr[g.b], g.ldb ? g.ldb : g.K, ptr[g.c], g.batch, g.M, g.N,
+                             g.K, PjrtType(g.ab), PjrtType(g.out), st);
         if (rc != 0) return fail("gemm launch failed (" + std::to_string(rc) + ") for " + S.label);
         break;
       }
@@ -280,6 +341,7 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
   }
   for (size_t s = 0; s < P.slots.size(); ++s)
     if (owned[s]) DeviceFree(ptr[s], st);
+  ExecTimerMarkEnd(dev.ordinal, st);
   cudaError_t ce = cudaGetLastError();
   if (ce != cudaSuccess) return std::string("CUDA error during execute: ") + cudaGetErrorString(ce);
   if (timer.on) {
@@ -325,4 +387,20 @@ extern "C" int b200_compile_report(const char* text, size_t size, int num_proces
   if (report.size() + 1 > out_size) return -1;
   std::memcpy(out, report.c_str(), report.size() + 1);
   return rc;
+}
+
+extern "C" double b200_exec_timer(int action) {
+  b200::ExecTimer& t = b200::GetExecTimer();
+  std::lock_guard<std::mutex> lock(t.mu);
+  if (action == 0) {
+    t.armed = true;
+    t.started = false;
+    return 0.0;
+  }
+  if (!t.armed || !t.started) return -1.0;
+  cudaSetDevice(t.device);
+  cudaEventSynchronize(t.end);
+  float ms = 0.f;
+  if (cudaEventElapsedTime(&ms, t.start, t.end) != cudaSuccess) return -1.0;
+  return ms;
 }

@@ -43,7 +43,7 @@ class Executable {
 
  private:
   struct PerDevice {
-    void* module = nullptr;                  // CUmodule
+    std::vector<void*> modules;              // CUmodule per NVRTC group
     std::map<std::string, void*> fns;        // CUfunction by kernel name
     std::vector<void*> consts;               // uploaded constants
   };
@@ -51,7 +51,7 @@ class Executable {
 
   Plan plan_;
   std::string name_;
-  std::vector<char> cubin_;
+  std::vector<std::vector<char>> cubins_;
   std::mutex mu_;
   std::map<int, PerDevice> per_dev_;
 };

@@ -32,7 +32,8 @@ struct Cfg {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStage = kABytes + kBBytes;
-  static constexpr int kSmem = kStages * kStage + 1024 + 256;
+  static constexpr int kStageOut = 4 * 32 * 33 * 4;   // epilogue staging: 4 warps x 32 x 33 f32
+  static constexpr int kSmem = kStages * kStage + 1024 + 256 + kStageOut;
   static constexpr int kTmemCols = 2 * BN;
 };
 
@@ -60,6 +61,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint64_t* acc_full = empty + CF::kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
+  float* stage_base = (float*)(smem + CF::kStages * CF::kStage + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mb = (M + BM - 1) / BM, nb = (N + BN - 1) / BN;
@@ -151,40 +153,55 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int row = m_blk * BM + row_in_tile;
       const uint32_t taddr = tmem_base + a * BN + ((uint32_t)(q * 32) << 16);
       const long long crow = ((long long)b * M + row) * (long long)N;
+      // full 32-column chunks of an aligned row go straight out as 16-byte vectors; otherwise (N not
+      // a multiple of 8 / 4, or the ragged last chunk) the warp stages 32 rows x 32 columns in shared
+      // memory and writes them row by row, coalesced, with bounds checks
+      const bool aligned = OUT == 0 ? (N & 3) == 0 : (N & 7) == 0;
+      float* stage = stage_base + (warp - 2) * 32 * 33;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t v[16];
-        tmem_ld16(taddr + c, v);
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tmem_ld16(taddr + c, *reinterpret_cast<uint32_t(*)[16]>(v));
+        tmem_ld16(taddr + c + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
         tmem_wait_ld();
         const int col = n_blk * BN + c;
-        if (row < M && col < N) {
-          if (OUT == 0) {
-            float* out = (float*)C + crow + col;
-            if (col + 16 <= N && (N & 3) == 0) {
+        if (col >= N) continue;                        // warp-uniform
+        if (aligned && col + 32 <= N) {
+          if (row < M) {
+            if (OUT == 0) {
+              float* out = (float*)C + crow + col;
 #pragma unroll
-              for (int j = 0; j < 16; j += 4)
+              for (int j = 0; j < 32; j += 4)
                 *(float4*)(out + j) = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
                                                   __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
             } else {
-              for (int j = 0; j < 16 && col + j < N; ++j) out[j] = __uint_as_float(v[j]);
-            }
-          } else {
-            uint16_t* out = (uint16_t*)C + crow + col;
-            if (col + 16 <= N && (N & 7) == 0) {
-              uint32_t p[8];
+              uint16_t* out = (uint16_t*)C + crow + col;
+              uint32_t p[16];
 #pragma unroll
-              for (int j = 0; j < 8; ++j)
+              for (int j = 0; j < 16; ++j)
                 p[j] = OUT == 1 ? pack_bf16(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]))
                                 : pack_f16(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-              *(uint4*)out = make_uint4(p[0], p[1], p[2], p[3]);
-              *(uint4*)(out + 8) = make_uint4(p[4], p[5], p[6], p[7]);
-            } else {
-              for (int j = 0; j < 16 && col + j < N; ++j) {
-                uint32_t pk = OUT == 1 ? pack_bf16(__uint_as_float(v[j]), 0.f) : pack_f16(__uint_as_float(v[j]), 0.f);
-                out[j] = (uint16_t)(pk & 0xffff);
-              }
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) *(uint4*)(out + 2 * j) = make_uint4(p[j], p[j + 1], p[j + 2], p[j + 3]);
             }
           }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) stage[lane * 33 + j] = __uint_as_float(v[j]);
+          __syncwarp();
+          const int gcol = col + lane;
+#pragma unroll 4
+          for (int rr = 0; rr < 32; ++rr) {
+            const int grow = m_blk * BM + q * 32 + rr;
+            if (grow < M && gcol < N) {
+              const float x = stage[rr * 33 + lane];
+              const long long o = ((long long)b * M + grow) * (long long)N + gcol;
+              if (OUT == 0) ((float*)C)[o] = x;
+              else if (OUT == 1) ((uint16_t*)C)[o] = (uint16_t)(pack_bf16(x, 0.f) & 0xffff);
+              else ((uint16_t*)C)[o] = (uint16_t)(pack_f16(x, 0.f) & 0xffff);
+            }
+          }
+          __syncwarp();
         }
       }
       tc_fence_before();
@@ -200,16 +217,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 }
 
 // ---------------------------------------------------------------------------- SIMT fallback
-// fp32 (or any) inputs, K-major A[b] (M x K) and B[b] (N x K): 128x128 tiles, 8x8 per thread.
+// fp32 (or any) inputs, K-major A[b] (M x K, row pitch lda) and B[b] (N x K, pitch ldb): 128x128
+// tiles, 8x8 outputs per thread.
 template <typename T, int OUT>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A, const T* __restrict__ B, void* __restrict__ C,
-                                                        int M, int N, int K) {
+                                                        int M, int N, int K, long long lda, long long ldb) {
   __shared__ float As[16][128 + 4];
   __shared__ float Bs[16][128 + 4];
   const int b = blockIdx.z;
   const int m0 = blockIdx.y * 128, n0 = blockIdx.x * 128;
-  const T* Ab = A + (long long)b * M * K;
-  const T* Bb = B + (long long)b * N * K;
+  const T* Ab = A + (long long)b * M * lda;
+  const T* Bb = B + (long long)b * N * ldb;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   float acc[8][8];
 #pragma unroll
@@ -224,8 +242,8 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
       int row = idx >> 4, kk = idx & 15;
       int gk = k0 + kk;
       int gm = m0 + row, gn = n0 + row;
-      As[kk][row] = (gm < M && gk < K) ? (float)Ab[(long long)gm * K + gk] : 0.f;
-      Bs[kk][row] = (gn < N && gk < K) ? (float)Bb[(long long)gn * K + gk] : 0.f;
+      As[kk][row] = (gm < M && gk < K) ? (float)Ab[(long long)gm * lda + gk] : 0.f;
+      Bs[kk][row] = (gn < N && gk < K) ? (float)Bb[(long long)gn * ldb + gk] : 0.f;
     }
     __syncthreads();
 #pragma unroll
@@ -266,12 +284,14 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 
 EncodeTiledFn GetEncodeTiled();
 
-// 3-D K-major operand map: dims {K, rows, batch}, box {64, box_rows, 1}, 128-byte swizzle.
-bool MakeOperandMap(CUtensorMap* map, const void* ptr, int K, int rows, int batch, int box_rows, bool f16like) {
+// 3-D K-major operand map: dims {K, rows, batch} with row pitch `ld` elements (ld * 2 % 16 == 0),
+// box {64, box_rows, 1}, 128-byte swizzle.  Columns K .. ld-1 are never read (zero fill past K).
+bool MakeOperandMap(CUtensorMap* map, const void* ptr, int K, long long ld, int rows, int batch, int box_rows,
+                    bool f16like) {
   EncodeTiledFn enc = GetEncodeTiled();
   if (!enc) return false;
   cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)K * 2 * rows};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)ld * 2 * rows};
   cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, f16like ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr),
@@ -288,7 +308,8 @@ int NumSMs() {
 }
 
 template <int BN, int OUT>
-static int LaunchTc(const void* A, const void* B, void* C, int batch, int M, int N, int K, int fmt, cudaStream_t st) {
+static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, void* C, int batch, int M, int N, int K,
+                    int fmt, cudaStream_t st) {
   using CF = Cfg<BN>;
   static std::once_flag once[8];
   int dev = 0;
@@ -297,7 +318,7 @@ static int LaunchTc(const void* A, const void* B, void* C, int batch, int M, int
     cudaFuncSetAttribute(gemm_tc_kernel<BN, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kSmem);
   });
   CUtensorMap ta, tb;
-  if (!MakeOperandMap(&ta, A, K, M, batch, BM, fmt == 0) || !MakeOperandMap(&tb, B, K, N, batch, BN, fmt == 0))
+  if (!MakeOperandMap(&ta, A, K, lda, M, batch, BM, fmt == 0) || !MakeOperandMap(&tb, B, K, ldb, N, batch, BN, fmt == 0))
     return -2;
   int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
   int grid = std::min(tiles, NumSMs());
@@ -306,11 +327,12 @@ static int LaunchTc(const void* A, const void* B, void* C, int batch, int M, int
 }
 
 template <typename T>
-static int LaunchSimt(const void* A, const void* B, void* C, int batch, int M, int N, int K, int out, cudaStream_t st) {
+static int LaunchSimt(const void* A, long long lda, const void* B, long long ldb, void* C, int batch, int M, int N, int K,
+                      int out, cudaStream_t st) {
   dim3 grid((N + 127) / 128, (M + 127) / 128, batch);
-  if (out == 0) gemm_simt_kernel<T, 0><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K);
-  else if (out == 1) gemm_simt_kernel<T, 1><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K);
-  else gemm_simt_kernel<T, 2><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K);
+  if (out == 0) gemm_simt_kernel<T, 0><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K, lda, ldb);
+  else if (out == 1) gemm_simt_kernel<T, 1><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K, lda, ldb);
+  else gemm_simt_kernel<T, 2><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K, lda, ldb);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -321,32 +343,36 @@ int TakeGemmError() {
   return v;
 }
 
-}  // namespace b200k
-
-using namespace b200k;
-
-extern "C" int b200_gemm(const void* A, const void* B, void* C, int64_t batch, int64_t M, int64_t N, int64_t K,
-                         int ab_type, int out_type, void* stream) {
-  cudaStream_t st = (cudaStream_t)stream;
+// C[b] = A[b] . B[b]^T with row pitches lda / ldb (elements) for A [batch, M, >=K] and B [batch, N, >=K].
+int Gemm(const void* A, long long lda, const void* B, long long ldb, void* C, int64_t batch, int64_t M, int64_t N,
+         int64_t K, int ab_type, int out_type, cudaStream_t st) {
   if (batch <= 0 || M <= 0 || N <= 0) return 0;
-  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || batch > 65535) return -1;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || batch > 65535 || lda < K || ldb < K) return -1;
   int out = out_type == B200_DT_F32 ? 0 : out_type == B200_DT_BF16 ? 1 : out_type == B200_DT_F16 ? 2 : -1;
   if (out < 0) return -1;
   if (K == 0) {
     size_t bytes = (size_t)batch * M * N * (out == 0 ? 4 : 2);
     return cudaMemsetAsync(C, 0, bytes, st) == cudaSuccess ? 0 : -3;
   }
-  bool tc_ok = (ab_type == B200_DT_BF16 || ab_type == B200_DT_F16) && (K % 8) == 0 &&
+  bool tc_ok = (ab_type == B200_DT_BF16 || ab_type == B200_DT_F16) && (lda % 8) == 0 && (ldb % 8) == 0 &&
                ((uintptr_t)A % 16) == 0 && ((uintptr_t)B % 16) == 0 && !getenv("B200_GEMM_SIMT");
   if (tc_ok) {
     int fmt = ab_type == B200_DT_BF16 ? 1 : 0;
     bool wide = N >= 256;
-    if (out == 0) return wide ? LaunchTc<256, 0>(A, B, C, batch, M, N, K, fmt, st) : LaunchTc<128, 0>(A, B, C, batch, M, N, K, fmt, st);
-    if (out == 1) return wide ? LaunchTc<256, 1>(A, B, C, batch, M, N, K, fmt, st) : LaunchTc<128, 1>(A, B, C, batch, M, N, K, fmt, st);
-    return wide ? LaunchTc<256, 2>(A, B, C, batch, M, N, K, fmt, st) : LaunchTc<128, 2>(A, B, C, batch, M, N, K, fmt, st);
+    int b = (int)batch, m = (int)M, n = (int)N, k = (int)K;
+    if (out == 0) return wide ? LaunchTc<256, 0>(A, lda, B, ldb, C, b, m, n, k, fmt, st) : LaunchTc<128, 0>(A, lda, B, ldb, C, b, m, n, k, fmt, st);
+    if (out == 1) return wide ? LaunchTc<256, 1>(A, lda, B, ldb, C, b, m, n, k, fmt, st) : LaunchTc<128, 1>(A, lda, B, ldb, C, b, m, n, k, fmt, st);
+    return wide ? LaunchTc<256, 2>(A, lda, B, ldb, C, b, m, n, k, fmt, st) : LaunchTc<128, 2>(A, lda, B, ldb, C, b, m, n, k, fmt, st);
   }
-  if (ab_type == B200_DT_F32) return LaunchSimt<float>(A, B, C, batch, M, N, K, out, st);
-  if (ab_type == B200_DT_BF16) return LaunchSimt<__nv_bfloat16>(A, B, C, batch, M, N, K, out, st);
-  if (ab_type == B200_DT_F16) return LaunchSimt<__half>(A, B, C, batch, M, N, K, out, st);
+  if (ab_type == B200_DT_F32) return LaunchSimt<float>(A, lda, B, ldb, C, batch, M, N, K, out, st);
+  if (ab_type == B200_DT_BF16) return LaunchSimt<__nv_bfloat16>(A, lda, B, ldb, C, batch, M, N, K, out, st);
+  if (ab_type == B200_DT_F16) return LaunchSimt<__half>(A, lda, B, ldb, C, batch, M, N, K, out, st);
   return -1;
+}
+
+}  // namespace b200k
+
+extern "C" int b200_gemm(const void* A, const void* B, void* C, int64_t batch, int64_t M, int64_t N, int64_t K,
+                         int ab_type, int out_type, void* stream) {
+  return b200k::Gemm(A, K, B, K, C, batch, M, N, K, ab_type, out_type, (cudaStream_t)stream);
 }

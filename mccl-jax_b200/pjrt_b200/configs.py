@@ -129,3 +129,144 @@ def psum_program(n_elems, world, seed_rank=0, with_inputs=True):
         rng = np.random.default_rng(1000 + seed_rank)
         inputs = [rng.standard_normal(n_elems, dtype=np.float32)]
     return Program(b.name, b.text([o]), inputs, bytes=4.0 * n_elems, meta=dict(n=n_elems, world=world))
+
+
+# ----------------------------------------------------------------------------- C4 GPT-2 DP train step
+GPT2_SMALL = dict(layers=12, d=768, heads=12, mlp=3072, vocab=50257, seq=1024)
+
+
+def gpt2_param_shapes(layers, d, heads, mlp, vocab, seq):
+    shapes = [("wte", (vocab, d)), ("wpe", (seq, d))]
+    for l in range(layers):
+        shapes += [(f"h{l}.ln1_g", (d,)), (f"h{l}.ln1_b", (d,)), (f"h{l}.w_qkv", (d, 3 * d)), (f"h{l}.b_qkv", (3 * d,)),
+                   (f"h{l}.w_proj", (d, d)), (f"h{l}.b_proj", (d,)), (f"h{l}.ln2_g", (d,)), (f"h{l}.ln2_b", (d,)),
+                   (f"h{l}.w_fc", (d, mlp)), (f"h{l}.b_fc", (mlp,)), (f"h{l}.w_fc2", (mlp, d)), (f"h{l}.b_fc2", (d,))]
+    shapes += [("lnf_g", (d,)), ("lnf_b", (d,))]
+    return shapes
+
+
+def gpt2_program(layers=12, d=768, heads=12, mlp=3072, vocab=50257, seq=1024, batch=8, world=1,
+                 lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1, seed=0, rank=0, with_inputs=True):
+    """One data-parallel AdamW step of a GPT-2-style decoder (pre-LN, GELU(tanh) MLP, tied LM head).
+
+    Params bf16 (replicated), AdamW moments f32; the batch [world*batch, seq] of token ids is sharded
+    over ranks with shard_map (SPMDFullToShardShape); gradients are psum'd (all_reduce) and divided by
+    the world size (pmean), as temp/dp_train.py:80-83 does.  Adam bias corrections come in as host
+    scalars (dp_train.py:74-76).  Returns (new params..., new m..., new v..., pmean loss).
+    """
+    b = Builder("jit_gpt2_dp_step", num_partitions=world)
+    shapes = gpt2_param_shapes(layers, d, heads, mlp, vocab, seq)
+    P = {n: b.arg(s, "bf16") for n, s in shapes}
+    M = {n: b.arg(s, "f32") for n, s in shapes}
+    V = {n: b.arg(s, "f32") for n, s in shapes}
+    ids_full = b.arg((world * batch, seq), "i32")
+    tgt_full = b.arg((world * batch, seq), "i32")
+    bc1 = b.arg((), "f32")
+    bc2 = b.arg((), "f32")
+    ids = b.shard(ids_full, (batch, seq)) if world > 1 else ids_full
+    tgt = b.shard(tgt_full, (batch, seq)) if world > 1 else tgt_full
+    Dh = d // heads
+    ntok = batch * seq
+
+    def layernorm(x, g, bias):
+        xf = b.convert(x, "f32")
+        mu = b.mean(xf, -1, keepdims=True)
+        xc = xf - b.broadcast_to(mu, xf.shape)
+        var = b.mean(xc * xc, -1, keepdims=True)
+        inv = b.rsqrt(var + 1e-5)
+        y = xc * b.broadcast_to(inv, xf.shape) * b.broadcast_to(b.convert(g, "f32"), xf.shape) \
+            + b.broadcast_to(b.convert(bias, "f32"), xf.shape)
+        return b.convert(y, "bf16")
+
+    def linear(x2, w, bias):                       # x2 [ntok, din] bf16 -> [ntok, dout] bf16
+        y = b.dot_general(x2, w, contract=([1], [0]), out_dtype="bf16")
+        return y + b.broadcast_to(bias, y.shape)
+
+    def gelu(x):                                   # tanh approximation, in f32
+        xf = b.convert(x, "f32")
+        inner = (xf + 0.044715 * (xf * xf * xf)) * math.sqrt(2.0 / math.pi)
+        return b.convert(0.5 * xf * (1.0 + b.tanh(inner)), "bf16")
+
+    x = b.take(P["wte"], ids) + b.broadcast_to(P["wpe"], (batch, seq, d))   # [B, S, d] bf16
+    x = b.reshape(x, (ntok, d))
+    for l in range(layers):
+        p = lambda n: P[f"h{l}.{n}"]
+        h = layernorm(x, p("ln1_g"), p("ln1_b"))
+        qkv = linear(h, p("w_qkv"), p("b_qkv"))                             # [ntok, 3d]
+        heads_of = []
+        for i in range(3):
+            part = b.slice(qkv, [0, i * d], [ntok, (i + 1) * d])
+            heads_of.append(b.transpose(b.reshape(part, (batch, seq, heads, Dh)), (0, 2, 1, 3)))   # [B,H,S,Dh]
+        q, k, v = heads_of
+        s = b.dot_general(q, k, batch=([0, 1], [0, 1]), contract=([3], [3]), out_dtype="f32")
+        s = s * (1.0 / math.sqrt(Dh))
+        mask = b.broadcast_in_dim(b.compare(b.iota((seq, seq), 0), b.iota((seq, seq), 1), "GE"), s.shape, [2, 3])
+        s = b.select(mask, s, b.const(-np.inf, "f32", s.shape))
+        m = b.stop_gradient(b.max(s, 3, keepdims=True))
+        e = b.exp(s - b.broadcast_to(m, s.shape))
+        pr = e / b.broadcast_to(b.sum(e, 3, keepdims=True), s.shape)
+        o = b.dot_general(b.convert(pr, "bf16"), v, batch=([0, 1], [0, 1]), contract=([3], [2]), out_dtype="bf16")
+        o = b.reshape(b.transpose(o, (0, 2, 1, 3)), (ntok, d))
+        x = x + linear(o, p("w_proj"), p("b_proj"))
+        h = layernorm(x, p("ln2_g"), p("ln2_b"))
+        x = x + linear(gelu(linear(h, p("w_fc"), p("b_fc"))), p("w_fc2"), p("b_fc2"))
+    x = layernorm(x, P["lnf_g"], P["lnf_b"])
+    logits = b.dot_general(x, P["wte"], contract=([1], [1]), out_dtype="f32")      # tied head [ntok, V]
+    mx = b.stop_gradient(b.max(logits, 1, keepdims=True))
+    z = logits - b.broadcast_to(mx, logits.shape)
+    lse = b.log(b.sum(b.exp(z), 1, keepdims=True))
+    t2 = b.reshape(tgt, (ntok,))
+    onehot = b.compare(b.broadcast_in_dim(t2, (ntok, vocab), [0]), b.iota((ntok, vocab), 1), "EQ")
+    picked = b.sum(b.select(onehot, z, b.const(0.0, "f32", z.shape)), 1, keepdims=True)
+    loss = b.mean(lse - picked, [0, 1])
+    names = [n for n, _ in shapes]
+    grads = grad(b, loss, [P[n] for n in names])
+    outs_p, outs_m, outs_v = [], [], []
+    inv_world = 1.0 / world
+    for n, g in zip(names, grads):
+        if world > 1:
+            g = b.all_reduce(g, world)
+        gf = b.convert(g, "f32") * inv_world
+        m1 = b1 * M[n] + (1.0 - b1) * gf
+        v1 = b2 * V[n] + (1.0 - b2) * (gf * gf)
+        pf = b.convert(P[n], "f32")
+        mhat = m1 / b.broadcast_to(bc1, m1.shape)
+        vhat = v1 / b.broadcast_to(bc2, v1.shape)
+        decay = wd if P[n].ndim == 2 else 0.0
+        upd = mhat / (b.sqrt(vhat) + eps) + (decay * pf if decay else 0.0)
+        outs_p.append(b.convert(pf - lr * upd, "bf16"))
+        outs_m.append(m1)
+        outs_v.append(v1)
+    lo = b.all_reduce(loss, world) * inv_world if world > 1 else loss
+    text = b.text(outs_p + outs_m + outs_v + [lo])
+    inputs = []
+    if with_inputs:
+        inputs = gpt2_inputs(shapes, batch, seq, vocab, seed=seed, rank=rank)
+    n_params = sum(int(np.prod(s)) for _, s in shapes)
+    flops_per_token = 6 * (12 * layers * d * d + d * vocab) + 12 * layers * seq * d
+    return Program(b.name, text, inputs, flops=float(flops_per_token) * ntok,
+                   meta=dict(n_params=n_params, tokens=ntok, n_tensors=len(shapes), layers=layers, d=d,
+                             vocab=vocab, seq=seq, batch=batch, world=world))
+
+
+def gpt2_inputs(shapes, batch, seq, vocab, seed=0, rank=0, step=1, b1=0.9, b2=0.95):
+    """Params ~N(0, 0.02) bf16 (LN gains 1, biases 0) from `seed` (same on every rank); zero moments;
+    token ids / targets uniform in [0, vocab) from seed 1000 + rank (dp_train.py:50)."""
+    rng = np.random.default_rng(seed)
+    params, ms, vs = [], [], []
+    for n, s in shapes:
+        if n.endswith("_g"):
+            a = np.ones(s, np.float32)
+        elif len(s) == 1:
+            a = np.zeros(s, np.float32)
+        else:
+            a = rng.standard_normal(s, dtype=np.float32) * 0.02
+        params.append(a.astype(BF16))
+        ms.append(np.zeros(s, np.float32))
+        vs.append(np.zeros(s, np.float32))
+    brng = np.random.default_rng(1000 + rank)
+    ids = brng.integers(0, vocab, (batch, seq)).astype(np.int32)
+    tgt = brng.integers(0, vocab, (batch, seq)).astype(np.int32)
+    bc1 = np.array(1 - b1 ** step, np.float32)
+    bc2 = np.array(1 - b2 ** step, np.float32)
+    return params + ms + vs + [ids, tgt, bc1, bc2]

@@ -267,8 +267,9 @@ class Executable:
         outs = [Buffer(self.client, out_arr[i]) for i in range(self.num_outputs)]
         if wait:
             api.await_event(evs[0])
-        else:
-            self.last_event = evs[0]
+        elif evs[0]:
+            # asynchronous: the outputs carry their own ready events; drop the completion event
+            api.call("Event_Destroy", EventArgs(event=evs[0]))
         return outs
 
     def destroy(self):
@@ -366,7 +367,7 @@ class Client:
         return Executable(self, a.executable)
 
     def buffer_from_host(self, x: np.ndarray, device=None, semantics: int = 1) -> Buffer:
-        x = np.ascontiguousarray(x)
+        x = np.ascontiguousarray(x).reshape(np.shape(x))   # (ascontiguousarray turns 0-d into 1-d)
         dims = (C.c_int64 * max(1, x.ndim))(*x.shape)
         a = self.api.call("Client_BufferFromHostBuffer", FromHostArgs(
             client=self.h, data=x.ctypes.data, type=np_type_code(x), dims=dims, num_dims=x.ndim,

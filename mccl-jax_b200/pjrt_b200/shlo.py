@@ -245,6 +245,19 @@ class Builder:
         sl = ", ".join(f"{s}:{l}" + (f":{st}" if st != 1 else "") for s, l, st in zip(start, limit, strides))
         return self._emit(t, f"{t.name} = stablehlo.slice {x.name} [{sl}] : ({x.type}) -> {t.type}")
 
+    def pad(self, x, value, low, high, interior=None):
+        interior = interior or [0] * x.ndim
+        shape = tuple(x.shape[i] + low[i] + high[i] + max(x.shape[i] - 1, 0) * interior[i] for i in range(x.ndim))
+        v = value if isinstance(value, T) else self.const(value, x.dtype)
+        t = T(self, self._fresh(), shape, x.dtype, op="pad", inputs=(x, v),
+              attrs={"low": tuple(low), "high": tuple(high), "interior": tuple(interior)})
+        return self._emit(t, f"{t.name} = stablehlo.pad {x.name}, {v.name}, low = {_dims(low)}, high = {_dims(high)}, "
+                             f"interior = {_dims(interior)} : ({x.type}, {v.type}) -> {t.type}")
+
+    def stop_gradient(self, x):
+        """Same value, no gradient (jax.lax.stop_gradient lowers to nothing in StableHLO)."""
+        return T(self, x.name, x.shape, x.dtype, op="stop_gradient", inputs=(x,))
+
     def concatenate(self, xs, dim):
         shape = list(xs[0].shape)
         shape[dim] = sum(x.shape[dim] for x in xs)
@@ -409,7 +422,7 @@ class Builder:
         sig = ", ".join(f"{a.name}: {a.type}" for a in self.args)
         res = ", ".join(f"{o.type}" for o in outs)
         attrs = f"mhlo.num_partitions = {self.num_partitions} : i32, mhlo.num_replicas = {self.num_replicas} : i32"
-        body = [f"    {self.lines[id(t)]}".replace("\n", "\n    ") for t in self.ops if id(t) in live]
+        body = [f"    {self.lines[id(t)]}".replace("\n", "\n    ") for t in self.ops if id(t) in live and id(t) in self.lines]
         ret = f"    return {', '.join(o.name for o in outs)} : {', '.join(o.type for o in outs)}"
         return (f"module @{self.name} attributes {{{attrs}}} {{\n"
                 f"  func.func public @main({sig}) -> ({res}) {{\n" + "\n".join(body) + "\n" + ret + "\n  }\n}\n")
@@ -465,7 +478,16 @@ def _unbroadcast_bid(b, g, x, dims):
 
 def _vjp(b: Builder, t: T, g: T, acc):
     op, ins = t.op, t.inputs
-    if op in ("arg", "constant", "iota", "compare"):
+    if op in ("arg", "constant", "iota", "compare", "stop_gradient"):
+        return
+    if op == "slice":
+        x = ins[0]
+        st, li, sd = t.attrs["start"], t.attrs["limit"], t.attrs["strides"]
+        low = list(st)
+        interior = [s - 1 for s in sd]
+        high = [x.shape[i] - (st[i] + (t.shape[i] - 1) * sd[i] + 1) if t.shape[i] else x.shape[i] - st[i]
+                for i in range(x.ndim)]
+        acc(x, b.pad(g, 0.0, low, high, interior))
         return
     if op == "add":
         acc(ins[0], g); acc(ins[1], g)

@@ -92,6 +92,23 @@ def test_gemm_vs_oracle(client, dtype, M, N, K, batch):
     assert_close(out, ref, RTOL_F32 if dtype == "f32" else RTOL_F32 * 10, "gemm")
 
 
+@pytest.mark.parametrize("K,N,out", [(50, 70, "f32"), (50257 // 41, 333, "bf16"), (768, 1001, "f32")])
+def test_dot_mixed_precision_and_unaligned_shapes(client, K, N, out):
+    """bf16 x f32 operands (a backward-pass cotangent meeting bf16 weights) run on the tensor cores in
+    bf16; K % 8 != 0 takes the padded-pitch operand copy; N % 8 != 0 the staged epilogue."""
+    b = Builder("jit_mixed_dot")
+    x = b.arg((200, K), "bf16")
+    w = b.arg((K, N), "f32")
+    y = b.dot_general(x, w, contract=([1], [0]), out_dtype=out)
+    text = b.text([y])
+    rng = np.random.default_rng(K + N)
+    ins = [(rng.standard_normal((200, K)) / np.sqrt(K)).astype(ml_dtypes.bfloat16),
+           rng.standard_normal((K, N)).astype(np.float32)]
+    got = client.run(text, ins)[0]
+    ref = oracle_run(text, ins)[0]
+    assert_close(np.asarray(got, np.float32), np.asarray(ref, np.float32), 1e-2, "mixed dot")
+
+
 def test_psum_single_rank_known_answer(client):
     """smoke.cc:24-40: one rank, all-reduce of [1,2,3,4] is the identity."""
     p = configs.psum_program(4, 1, with_inputs=False)
