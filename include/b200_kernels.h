@@ -48,6 +48,22 @@ B200_API int b200_attention_fwd(const void* q, const void* k, const void* v, voi
 B200_API int b200_attention_fwd_vt(const void* q, const void* k, const void* v, void* vt, void* o, int B, int H, int S,
                                    int D, int causal, float scale, void* stream);
 
+/* b200_attention_fwd_vt without the caller-provided scratch: for callers that cannot allocate device
+ * memory — code running under a framework whose caching allocator owns the whole device budget, or
+ * a latency-critical path where cudaMalloc / cudaFree (which can synchronize the device) are not
+ * allowed.  No counterpart in the reference.
+ * The transposed V goes to a static 32 MiB device array built into the library; the function calls
+ * no cudaMalloc, cudaFree or other allocating routine.  Limit: B*H*S*D*2 bytes <= 32 MiB (e.g.
+ * [4,16,4096,64]); larger problems return -5 without launching anything.  The array's device address
+ * is looked up on the first call on each device (with that device current), so make that first call
+ * before any stream capture.  All calls share the one array and it keeps the previous call's
+ * contents (each call overwrites the part it uses before reading it): calls that overlap on the GPU
+ * (different streams, or different host threads on one device) race on it and must be serialized by
+ * the caller.  Returns 0, -1 (bad shape), -5 (too large for the scratch), -6 (scratch address lookup
+ * failed), or the attention kernel's launch codes. */
+B200_API int b200_attention_fwd_noalloc(const void* q, const void* k, const void* v, void* o, int B, int H, int S,
+                                        int D, int causal, float scale, void* stream);
+
 /* out[idx[i], :] += upd[i, :] for i < n_upd (rows of length row_len; out has `rows` rows; indices
  * outside [0, rows) are skipped).  dtype in {F32, BF16}; idx_type in {S32, S64}.
  * Replaces: Scatter (add region), src/jam/ops/gather_scatter.mm:262-335. */

@@ -479,3 +479,50 @@ extern "C" int b200_attention_fwd_vt(const void* q, const void* k, const void* v
   if (B == 0 || H == 0 || S == 0) return 0;
   return b200k::AttentionFwdWithVt(q, k, v, vt, o, B, H, S, D, causal, scale, (cudaStream_t)stream);
 }
+
+// ------------------------------------------------------------------------------------------------
+// Allocation-free variant of b200_attention_fwd_vt.  Its scratch (the transposed V) lives in this
+// file-scope device array instead of memory the caller passes in.  The array is part of the
+// library's device image: every GPU that loads this module holds it (32 MiB) until the process
+// exits.  In host code `g_vt_noalloc_scratch` only names a host-side stand-in, so the device address
+// is taken once per device with cudaGetSymbolAddress (with that device current) and cached.
+namespace b200k {
+
+constexpr size_t kNoAllocScratchBytes = 32u << 20;   // fits V^T for B*H*S*D <= 16 Mi bf16 elements
+
+static __device__ __align__(256) unsigned char g_vt_noalloc_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64];
+
+// Device address of the scratch array for the current device; resolved on the first call per device.
+static int NoAllocScratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -6;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_vt_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return -6;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+}  // namespace b200k
+
+extern "C" int b200_attention_fwd_noalloc(const void* q, const void* k, const void* v, void* o, int B, int H, int S,
+                                          int D, int causal, float scale, void* stream) {
+  if (B == 0 || H == 0 || S == 0) return 0;
+  if (B < 0 || H < 0 || S < 0 || D <= 0) return -1;
+  const size_t need = (size_t)B * H * S * D * 2;
+  if (need > b200k::kNoAllocScratchBytes) return -5;   // larger than the static scratch
+  void* vt = nullptr;
+  int rc = b200k::NoAllocScratch(&vt);
+  if (rc != 0) return rc;
+  return b200k::AttentionFwdWithVt(q, k, v, vt, o, B, H, S, D, causal, scale, (cudaStream_t)stream);
+}
