@@ -211,10 +211,11 @@ def main():
     ap.add_argument("--H", type=int, default=HEAD["H"])
     ap.add_argument("--S", type=int, default=HEAD["S"])
     ap.add_argument("--causal", action="store_true")
-    ap.add_argument("--workload", default="attention", choices=["attention", "dp", "gemm", "psum"],
-                    help="attention (headline); dp = GPT-2 DP train step; gemm = dot_general sweep; "
+    ap.add_argument("--workload", default="attention", choices=["attention", "dp", "gemm", "psum", "fused"],
+                    help="attention (headline); dp = GPT-2 DP train step; gemm = dot_general sweep; fused = HBM-bound chains; "
                          "psum = all_reduce bandwidth sweep")
     ap.add_argument("--layers", type=int, default=12, help="dp: decoder layers")
+    ap.add_argument("--only", default="", help="fused: run only the chains whose name contains this text")
     a = ap.parse_args()
     HEAD.update(B=a.B, H=a.H, S=a.S, causal=a.causal)
     a.warmup = max(a.warmup, 3)

@@ -204,14 +204,100 @@ struct Gen {
     return r;
   }
 
+  // Vector mode (loop kernels whose innermost extent is a multiple of 4): the element function
+  // handles 4 consecutive elements; lane v's innermost loop index is named `vinner_v`.  A leaf read
+  // whose innermost index is exactly that name (and whose other indices do not depend on it) is
+  // contiguous and 4-aligned across the lanes, so lane 0 issues one vector load for all four.
+  bool vec = false;
+  std::string vinner;
+  int branch_depth = 0;                                   // inside concatenate / pad branches
+  std::unordered_map<std::string, std::string> vloads;    // leaf base -> vector register
+  std::vector<std::vector<std::string>> lane_identity;   // identity index per lane (vector mode)
+  std::unordered_map<int, std::vector<std::string>> lane_group_regs;
+
+  int LaneOf(const std::vector<std::string>& idx) const {
+    if (!vec || idx.empty()) return -1;
+    const std::string& last = idx.back();
+    if (last.size() != vinner.size() + 2 || last.compare(0, vinner.size() + 1, vinner + "_") != 0) return -1;
+    for (size_t k = 0; k + 1 < idx.size(); ++k)
+      if (idx[k].find(vinner + "_") != std::string::npos) return -1;
+    return last.back() - '0';
+  }
+
+  std::string VecLoad(DT dt, int slot, const std::vector<std::string>& idx, int lane) {
+    std::vector<std::string> base = idx;
+    base.back() = vinner + "_0";
+    std::string key = std::to_string(slot);
+    for (auto& s : base) key += "|" + s;
+    auto it = vloads.find(key);
+    std::string name;
+    if (it == vloads.end()) {
+      name = "v" + std::to_string(tmp++);
+      if (dt == DT::kF32) body << indent << "const float4 " << name << " = *(const float4*)(" << Param(slot) << " + (" << LinearDims(base) << "));\n";
+      else body << indent << "const uint2 " << name << " = *(const uint2*)(" << Param(slot) << " + (" << LinearDims(base) << "));\n";
+      vloads[key] = name;
+    } else {
+      name = it->second;
+    }
+    if (dt == DT::kF32) {
+      static const char* c[] = {".x", ".y", ".z", ".w"};
+      return name + c[lane];
+    }
+    // 4 x 16-bit: .x = lanes 0,1 (low half first), .y = lanes 2,3
+    std::string word = name + (lane < 2 ? ".x" : ".y");
+    std::string half = (lane & 1) ? "(unsigned short)(" + word + " >> 16)" : "(unsigned short)(" + word + " & 0xffffu)";
+    return Var(dt, dt == DT::kBF16 ? "bf2f(" + half + ")" : "h2f(" + half + ")");
+  }
+  std::vector<int64_t> cur_dims;   // dims of the leaf being vector-loaded (set by the caller)
+  std::string LinearDims(const std::vector<std::string>& idx) const { return Linear(idx, cur_dims); }
+
+  // Row-group mode: values already reduced or computed for the current row live in registers and
+  // may only be read at the row's own index (`row_ident`; unit dims may read index 0).
+  std::unordered_map<int, std::string> fixed;   // value id -> register
+  std::vector<std::string> row_ident;
+  std::vector<int64_t> row_dims;
+  // idx (over dims) names the current row: its non-unit entries are the row's non-unit indices
+  // (an index into a unit dim can only be 0)
+  bool SameRow(const std::vector<std::string>& idx, const std::vector<int64_t>& dims) const {
+    std::vector<std::string> a, b;
+    for (size_t k = 0; k < dims.size(); ++k) if (dims[k] != 1) a.push_back(idx[k]);
+    for (size_t k = 0; k < row_dims.size(); ++k) if (row_dims[k] != 1) b.push_back(row_ident[k]);
+    return a == b;
+  }
+  // the index of the current row in a row-shaped value of shape dims
+  std::vector<std::string> RowIndex(const std::vector<int64_t>& dims) const {
+    std::vector<std::string> b, out;
+    for (size_t k = 0; k < row_dims.size(); ++k) if (row_dims[k] != 1) b.push_back(row_ident[k]);
+    size_t q = 0;
+    for (int64_t d : dims) out.push_back(d != 1 && q < b.size() ? b[q++] : "0");
+    return out;
+  }
+
   std::string EmitUncached(const Value* v, const std::vector<std::string>& idx) {
     const TensorType& ty = v->type;
+    auto fx = fixed.find(v->id);
+    if (fx != fixed.end()) {
+      if (!SameRow(idx, ty.dims)) conflict = true;
+      return fx->second;
+    }
     int slot = (*slot_of)[v->id];
     if (slot >= 0) {
       auto g = group_regs.find(slot);
       if (g != group_regs.end()) {
         if (idx == identity && ty.dims == group_dims) return g->second;
+        if (vec && ty.dims == group_dims) {
+          auto lg = lane_group_regs.find(slot);
+          for (size_t l = 0; lg != lane_group_regs.end() && l < lane_identity.size(); ++l)
+            if (idx == lane_identity[l] && l < lg->second.size()) return lg->second[l];
+        }
         conflict = true;
+      }
+      const int lane = branch_depth == 0 ? LaneOf(idx) : -1;
+      if (lane >= 0 && (ty.dt == DT::kF32 || ty.dt == DT::kBF16 || ty.dt == DT::kF16) && !ty.dims.empty() &&
+          ty.dims.back() % 4 == 0) {
+        cur_dims = ty.dims;
+        std::string r = VecLoad(ty.dt, slot, idx, lane);
+        return ty.dt == DT::kF32 ? Var(ty.dt, r) : r;
       }
       return Var(ty.dt, LoadExpr(ty.dt, Param(slot), Linear(idx, ty.dims)));
     }
@@ -310,7 +396,9 @@ struct Gen {
         body << indent << (k ? "else " : "") << "if ((" << idx[d] << ") < " << off + len << ") {\n";
         indent += "  ";
         auto saved = cse;          // values computed inside a branch are not visible outside
+        ++branch_depth;
         std::string x = Emit(op->operands[k], j);
+        --branch_depth;
         cse = saved;
         body << indent << r << " = " << x << ";\n";
         indent = save;
@@ -340,7 +428,9 @@ struct Gen {
       std::string save = indent;
       indent += "  ";
       auto saved = cse;
+      ++branch_depth;
       std::string x = Emit(op->operands[0], j);
+      --branch_depth;
       cse = saved;
       body << indent << r << " = " << x << ";\n";
       indent = save;
@@ -510,6 +600,8 @@ class Lowerer {
   std::vector<int> slot_of_;
   std::vector<bool> dead_;
   std::vector<bool> need_;                 // value must be materialized
+  std::vector<bool> ext_use_;              // read by a program output, a library step or attention
+  std::vector<std::set<int>> cons_;        // materialized consumers of each value
   std::unordered_map<int, AttentionStep> attn_;  // result value id of the 2nd dot -> matched attention
   std::unordered_map<int, std::array<const Value*, 3>> attn_in_;
   std::ostringstream src_;
@@ -721,10 +813,12 @@ class Lowerer {
   void DecideMaterialization() {
     size_t nv = g_.values.size();
     need_.assign(nv, false);
-    // consumer "kernels" of each value: -1 means "needs a buffer"
-    std::vector<std::set<int>> cons(nv);
-    for (Value* o : g_.outputs) need_[o->id] = true;
-    for (auto& kv : attn_in_) for (const Value* v : kv.second) need_[v->id] = true;
+    ext_use_.assign(nv, false);
+    // materialized consumers of each value (reached through unmaterialized chains)
+    cons_.assign(nv, {});
+    auto& cons = cons_;
+    for (Value* o : g_.outputs) need_[o->id] = ext_use_[o->id] = true;
+    for (auto& kv : attn_in_) for (const Value* v : kv.second) need_[v->id] = ext_use_[v->id] = true;
     for (int i = (int)g_.ops.size() - 1; i >= 0; --i) {
       Op* op = g_.ops[i].get();
       if (dead_[i]) continue;
@@ -732,7 +826,7 @@ class Lowerer {
         std::set<int> c;
         for (Op* u : r->users) {
           if (dead_[u->index]) continue;
-          if (IsHeavy(u) && u->name != "reduce") { need_[r->id] = true; continue; }
+          if (IsHeavy(u) && u->name != "reduce") { need_[r->id] = ext_use_[r->id] = true; continue; }
           if (u->name == "reduce") {
             if (u->operands[0] == r) c.insert(u->result()->id);
             continue;                       // the init value is folded into the reduction kernel
@@ -790,9 +884,23 @@ class Lowerer {
 
   void EmitSteps() {
     std::vector<const Value*> pending;   // loop roots of the open group
+    std::vector<const Value*> row;       // members of the open row group
+    std::vector<int64_t> row_x;          // its row space X = [rows..., L]
     auto flush = [&]() {
+      if (!row.empty()) TryRow(row, row_x, false);
+      row.clear();
       if (!pending.empty()) EmitLoopGroup(pending);
       pending.clear();
+    };
+    // true if r joined the open row group
+    auto join_row = [&](const Value* r) {
+      if (row.empty()) return false;
+      if (r->type.dims != row_x && !RowShaped(r->type.dims, row_x)) return false;
+      std::vector<const Value*> cand = row;
+      cand.push_back(r);
+      if (!TryRow(cand, row_x, true)) return false;
+      row = cand;
+      return true;
     };
     for (auto& opp : g_.ops) {
       Op* op = opp.get();
@@ -823,7 +931,30 @@ class Lowerer {
         continue;
       }
       if (n == "dot_general" || n == "dot") { flush(); EmitDot(op); continue; }
-      if (n == "reduce") { flush(); EmitReduce(op); continue; }
+      if (n == "reduce") {
+        if (RowReducible(op)) {
+          const auto& X = op->operands[0]->type.dims;
+          if (!row.empty() && row_x == X && join_row(r)) continue;
+          // the loop roots just before it (e.g. masked scores) join when they have its shape
+          if (row.empty() && !pending.empty() && pending[0]->type.dims == X) {
+            std::vector<const Value*> cand = pending;
+            cand.push_back(r);
+            if (TryRow(cand, X, true)) {
+              pending.clear();
+              row = cand;
+              row_x = X;
+              continue;
+            }
+          }
+          flush();
+          row = {r};
+          row_x = X;
+          continue;
+        }
+        flush();
+        EmitReduce(op);
+        continue;
+      }
       if (n == "scatter") { flush(); EmitScatter(op); continue; }
       if (n == "all_reduce" || n == "all_gather" || n == "reduce_scatter") { flush(); EmitCollective(op); continue; }
       if (n == "custom_call") throw LowerError{"unsupported custom_call @" + op->strs["call_target_name"]};
@@ -834,6 +965,10 @@ class Lowerer {
       if (n == "reshape" && slot_of_[Resolve(op->operands[0])->id] >= 0 && need_[op->operands[0]->id]) {
         slot_of_[r->id] = slot_of_[Resolve(op->operands[0])->id];   // contiguous reshape: same buffer
         continue;
+      }
+      if (!row.empty()) {
+        if (join_row(r)) continue;
+        flush();
       }
       if (!pending.empty() && (pending[0]->type.dims != r->type.dims)) flush();
       pending.push_back(r);
@@ -896,17 +1031,46 @@ class Lowerer {
     gen.group_dims = dims;
     std::ostringstream pre;
     std::string ind = "    ";
-    gen.identity = Delinearize(pre, "i", dims, "i", ind, wide);
-    gen.body << pre.str();
-    std::vector<std::string> regs;
-    for (size_t k = 0; k < roots.size(); ++k) {
-      // a root is computed from its defining op (not loaded from its own slot)
-      int s = slot_of_[roots[k]->id];
-      slot_of_[roots[k]->id] = -1;
-      std::string v = gen.Emit(roots[k], gen.identity);
-      slot_of_[roots[k]->id] = s;
-      gen.group_regs[s] = v;
-      regs.push_back(v);
+    // vector mode: four consecutive elements per call (innermost extent a multiple of 4)
+    const bool vec = !dims.empty() && dims.back() % 4 == 0 && n % 4 == 0 && !std::getenv("B200_NO_VEC");
+    std::vector<std::string> regs;                     // scalar mode: one register per root
+    std::vector<std::vector<std::string>> lregs;       // vector mode: four registers per root
+    if (!vec) {
+      gen.identity = Delinearize(pre, "i", dims, "i", ind, wide);
+      gen.body << pre.str();
+      for (size_t k = 0; k < roots.size(); ++k) {
+        // a root is computed from its defining op (not loaded from its own slot)
+        int s = slot_of_[roots[k]->id];
+        slot_of_[roots[k]->id] = -1;
+        std::string v = gen.Emit(roots[k], gen.identity);
+        slot_of_[roots[k]->id] = s;
+        gen.group_regs[s] = v;
+        regs.push_back(v);
+      }
+    } else {
+      std::vector<std::string> names = Delinearize(pre, "i", dims, "i", ind, wide);
+      const std::string inner = names.back();
+      pre << ind << "const int " << inner << "_0 = " << inner << ", " << inner << "_1 = " << inner << " + 1, " << inner
+          << "_2 = " << inner << " + 2, " << inner << "_3 = " << inner << " + 3;\n";
+      gen.body << pre.str();
+      gen.vec = true;
+      gen.vinner = inner;
+      for (int l = 0; l < 4; ++l) {
+        std::vector<std::string> id = names;
+        id.back() = inner + "_" + std::to_string(l);
+        gen.lane_identity.push_back(id);
+      }
+      gen.identity = gen.lane_identity[0];
+      for (size_t k = 0; k < roots.size(); ++k) {
+        int s = slot_of_[roots[k]->id];
+        slot_of_[roots[k]->id] = -1;
+        std::vector<std::string> rl;
+        for (int l = 0; l < 4; ++l) rl.push_back(gen.Emit(roots[k], gen.lane_identity[l]));
+        slot_of_[roots[k]->id] = s;
+        gen.group_regs[s] = rl[0];
+        gen.lane_group_regs[s] = rl;
+        lregs.push_back(rl);
+      }
     }
     if (dry) {
       bool ok = !gen.conflict;
@@ -915,8 +1079,6 @@ class Lowerer {
       return ok;
     }
     if (gen.conflict) throw LowerError{"internal: fusion conflict"};
-    std::unordered_map<int, DT> dt_of;
-    for (size_t k = 0; k < p_->slots.size(); ++k) {}
     std::vector<DT> in_dts;
     for (int s : gen.in_slots) in_dts.push_back(SlotDt(s));
     std::string fn = KName();
@@ -932,23 +1094,40 @@ class Lowerer {
       args_decl += ", " + MemType(out_dts[k]) + "* __restrict__ out" + std::to_string(k);
       args_use += ", out" + std::to_string(k);
     }
-    src_ << "static __device__ __forceinline__ void " << fn << "_elem(long long i" << args_decl << ") {\n"
-         << gen.body.str();
-    for (size_t k = 0; k < roots.size(); ++k)
-      src_ << "    out" << k << "[i] = " << StoreExpr(out_dts[k], regs[k]) << ";\n";
+    // In vector mode the element function's argument is the vector index t (elements 4t .. 4t+3).
+    const int64_t trip = vec ? n / 4 : n;
+    src_ << "static __device__ __forceinline__ void " << fn << "_elem(long long " << (vec ? "t" : "i") << args_decl << ") {\n";
+    if (vec) src_ << "    const long long i = t * 4;\n";
+    src_ << gen.body.str();
+    for (size_t k = 0; k < roots.size(); ++k) {
+      if (!vec) {
+        src_ << "    out" << k << "[i] = " << StoreExpr(out_dts[k], regs[k]) << ";\n";
+        continue;
+      }
+      const auto& r4 = lregs[k];
+      if (out_dts[k] == DT::kF32) {
+        src_ << "    *(float4*)(out" << k << " + i) = make_float4(" << r4[0] << ", " << r4[1] << ", " << r4[2] << ", " << r4[3] << ");\n";
+      } else if (out_dts[k] == DT::kBF16 || out_dts[k] == DT::kF16) {
+        auto h = [&](int l) { return "(unsigned)" + StoreExpr(out_dts[k], r4[l]); };
+        src_ << "    *(uint2*)(out" << k << " + i) = make_uint2(" << h(0) << " | (" << h(1) << " << 16), " << h(2) << " | ("
+             << h(3) << " << 16));\n";
+      } else {
+        for (int l = 0; l < 4; ++l) src_ << "    out" << k << "[i + " << l << "] = " << StoreExpr(out_dts[k], r4[l]) << ";\n";
+      }
+    }
     src_ << "}\n";
     src_ << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "("
          << KernelParams(gen.in_slots, (int)out_slots.size(), false) << ") {\n"
          << ParamCasts(gen.in_slots, in_dts, out_dts)
          << "  const long long st = (long long)gridDim.x * 256;\n"
          << "  long long i = (long long)blockIdx.x * 256 + threadIdx.x;\n"
-         << "  for (; i + 3 * st < " << n << "LL; i += 4 * st) {\n"
+         << "  for (; i + 3 * st < " << trip << "LL; i += 4 * st) {\n"
          << "    " << fn << "_elem(i" << args_use << ");\n"
          << "    " << fn << "_elem(i + st" << args_use << ");\n"
          << "    " << fn << "_elem(i + 2 * st" << args_use << ");\n"
          << "    " << fn << "_elem(i + 3 * st" << args_use << ");\n"
          << "  }\n"
-         << "  for (; i < " << n << "LL; i += st) " << fn << "_elem(i" << args_use << ");\n"
+         << "  for (; i < " << trip << "LL; i += st) " << fn << "_elem(i" << args_use << ");\n"
          << "}\n";
     EndKernel();
     Launch L;
@@ -956,7 +1135,8 @@ class Lowerer {
     L.in_slots = gen.in_slots;
     L.out_slots = out_slots;
     L.block = 256;
-    L.grid_x = std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 16));
+    L.grid_x = std::max<int64_t>(1, (trip + 255) / 256);
+    L.grid_stride = true;
     Step st;
     st.kind = StepKind::kFusion;
     st.launches.push_back(L);
@@ -975,6 +1155,227 @@ class Lowerer {
     for (auto& v : g_.values)
       if (slot_of_[v->id] == s) return v->type.dt;
     throw LowerError{"internal: slot without dtype"};
+  }
+
+  // ---------------------------------------------------------------- row groups
+  // A reduction over the trailing axis of X = [rows..., L] opens a row group.  Later materialized
+  // values of shape X ("full" members) or of the row shape ("row scalars"), and further trailing
+  // reductions over the same X, join it while every read of a member stays inside its own row.  The
+  // group is one kernel: a warp (a block, for long rows) owns a row and walks it once per member in
+  // program order.  Reduction results and row scalars live in registers; full members are
+  // recomputed by the members that read them and stored only when something outside the group reads
+  // them.  Re-walks of a row hit L1/L2, so DRAM sees each input once (LayerNorm, softmax and
+  // logsumexp each become one kernel).
+  bool RowReducible(const Op* op) const {
+    if (op->results.size() != 1 || op->reduce == ReduceKind::kNone || std::getenv("B200_NO_ROWFUSE")) return false;
+    const auto& xd = op->operands[0]->type.dims;
+    const auto& rd = op->ints.at("dimensions");
+    if (xd.size() < 2 || rd.size() != 1 || rd[0] != (int64_t)xd.size() - 1) return false;
+    DT odt = op->result()->type.dt;
+    if (!(DTIsFloat(odt) || odt == DT::kS32 || odt == DT::kS64)) return false;
+    int64_t L = xd.back(), rows = op->result()->type.numel();
+    return L >= 32 && L < (1LL << 30) && (rows >= 148 * 4 || L < 8192);
+  }
+  // dims has the row shape of X = [rows..., L] up to unit dims
+  static bool RowShaped(const std::vector<int64_t>& dims, const std::vector<int64_t>& X) {
+    std::vector<int64_t> a, b;
+    for (int64_t d : dims) if (d != 1) a.push_back(d);
+    for (size_t k = 0; k + 1 < X.size(); ++k) if (X[k] != 1) b.push_back(X[k]);
+    return a == b;
+  }
+  static std::string Combine(ReduceKind kind, DT acc_dt, const std::string& a, const std::string& b) {
+    bool f = DTIsFloat(acc_dt), d = acc_dt == DT::kF64;
+    switch (kind) {
+      case ReduceKind::kAdd: return a + " + " + b;
+      case ReduceKind::kMul: return a + " * " + b;
+      case ReduceKind::kMax: return f ? (d ? "dmax_n(" : "fmax_n(") + a + ", " + b + ")" : "imax(" + a + ", " + b + ")";
+      case ReduceKind::kMin: return f ? (d ? "dmin_n(" : "fmin_n(") + a + ", " + b + ")" : "imin(" + a + ", " + b + ")";
+      case ReduceKind::kAnd: return acc_dt == DT::kPred ? a + " && " + b : a + " & " + b;
+      case ReduceKind::kOr: return acc_dt == DT::kPred ? a + " || " + b : a + " | " + b;
+      default: return a;
+    }
+  }
+  static DT AccDt(DT odt) { return odt == DT::kF64 ? DT::kF64 : DTIsFloat(odt) ? DT::kF32 : odt; }
+  // register value of a reduction result held in the accumulator type (rounded like a stored value)
+  static std::string FromAcc(DT odt, const std::string& e) {
+    if (odt == DT::kBF16) return "rbf(" + e + ")";
+    if (odt == DT::kF16) return "rhf(" + e + ")";
+    return "(" + CType(odt) + ")(" + e + ")";
+  }
+  std::string InitExpr(const Value* init, DT acc_dt) {
+    Gen ig;
+    ig.slot_of = &slot_of_;
+    ig.tmp = 1000000;
+    std::string iv = ig.Emit(init, {});
+    if (!ig.in_slots.empty()) throw LowerError{"reduce init must be a constant"};
+    if (!ig.body.str().empty()) throw LowerError{"reduce init must be a splat constant"};
+    return "(" + CType(acc_dt) + ")(" + iv + ")";
+  }
+
+  bool TryRow(const std::vector<const Value*>& members, const std::vector<int64_t>& X, bool dry) {
+    const std::vector<int64_t> kept(X.begin(), X.end() - 1);
+    const int64_t L = X.back();
+    int64_t rows = 1;
+    for (int64_t d : kept) rows *= d;
+    const bool wide = rows * L >= (1LL << 31);
+    const bool block_mode = L > 2048;
+    const int T = block_mode ? 512 : 32;          // threads that share a row
+    const bool vec = L % 4 == 0 && !std::getenv("B200_NO_VEC");
+    const int V = vec ? 4 : 1;
+    std::vector<int> saved(slot_of_);
+    size_t saved_slots = p_->slots.size();
+    std::set<int> ids;
+    for (const Value* m : members) ids.insert(m->id);
+    std::vector<int> out_slots, out_of(members.size(), -1);
+    std::vector<DT> out_dts;
+    for (size_t k = 0; k < members.size(); ++k) {
+      const Value* m = members[k];
+      bool ext = ext_use_[m->id];
+      for (int c : cons_[m->id]) if (!ids.count(c)) ext = true;
+      if (!ext) continue;
+      out_of[k] = (int)out_slots.size();
+      out_slots.push_back(SlotFor(m));
+      out_dts.push_back(m->type.dt);
+    }
+    std::vector<int> member_slot;
+    for (const Value* m : members) {
+      member_slot.push_back(slot_of_[m->id]);
+      slot_of_[m->id] = -1;                     // members are recomputed or held in registers
+    }
+    Gen gen;
+    gen.slot_of = &slot_of_;
+    gen.group_dims = X;
+    std::ostringstream ob, body;
+    gen.row_ident = Delinearize(ob, "row", kept, "a", "    ", wide);
+    gen.row_dims = kept;
+    std::vector<std::string> ident = gen.row_ident;
+    ident.push_back("j");
+    std::vector<std::vector<std::string>> lanes;
+    for (int l = 0; l < 4; ++l) {
+      lanes.push_back(gen.row_ident);
+      lanes.back().push_back("j_" + std::to_string(l));
+    }
+    const std::string loop_head = "#pragma unroll 4\n    for (int j = lt * " + std::to_string(V) + "; j < " + std::to_string(L) +
+                                  "; j += " + std::to_string(T * V) + ") {\n" +
+                                  (vec ? "      const int j_0 = j, j_1 = j + 1, j_2 = j + 2, j_3 = j + 3;\n" : "") +
+                                  "      const long long e = (long long)row * " + std::to_string(L) + "LL + j;\n";
+    // a phase over the row: element values of `v` (one per lane in vector mode)
+    auto row_phase = [&](const Value* v) {
+      gen.cse.clear();
+      gen.vloads.clear();
+      gen.body.str("");
+      gen.body.clear();
+      gen.indent = "      ";
+      gen.vec = vec;
+      gen.vinner = "j";
+      gen.lane_identity = lanes;
+      gen.identity = vec ? lanes[0] : ident;
+      std::vector<std::string> vals;
+      if (vec) for (int l = 0; l < 4; ++l) vals.push_back(gen.Emit(v, lanes[l]));
+      else vals.push_back(gen.Emit(v, ident));
+      return vals;
+    };
+    std::vector<std::pair<std::string, std::string>> shared;   // block mode: (type, name)
+    for (size_t k = 0; k < members.size(); ++k) {
+      const Value* m = members[k];
+      const Op* op = m->def;
+      const std::string rk = "r" + std::to_string(k);
+      const std::string o = out_of[k] >= 0 ? "out" + std::to_string(out_of[k]) : "";
+      if (op && op->name == "reduce") {
+        DT odt = m->type.dt, acc_dt = AccDt(odt);
+        std::string acc_t = CType(acc_dt), acc = "acc" + std::to_string(k);
+        std::string init = InitExpr(op->operands[1], acc_dt);
+        std::vector<std::string> vals = row_phase(op->operands[0]);
+        body << "    " << acc_t << " " << acc << " = (" << acc_t << ")(" << IdentityOf(op->reduce, acc_dt) << ");\n"
+             << loop_head << gen.body.str();
+        for (const auto& v : vals) body << "      " << acc << " = " << Combine(op->reduce, acc_dt, acc, "(" + acc_t + ")(" + v + ")") << ";\n";
+        body << "    }\n"
+             << "    for (int o = 16; o; o >>= 1) { " << acc_t << " oth = __shfl_xor_sync(0xffffffffu, " << acc << ", o); "
+             << acc << " = " << Combine(op->reduce, acc_dt, acc, "oth") << "; }\n";
+        if (block_mode) {
+          std::string red = "red" + std::to_string(k);
+          shared.push_back({acc_t, red});
+          body << "    if ((threadIdx.x & 31) == 0) " << red << "[threadIdx.x >> 5] = " << acc << ";\n    __syncthreads();\n"
+               << "    " << acc << " = " << red << "[0];\n"
+               << "    for (int w = 1; w < " << T / 32 << "; ++w) " << acc << " = " << Combine(op->reduce, acc_dt, acc, red + "[w]") << ";\n"
+               << "    __syncthreads();\n";
+        }
+        body << "    const " << CType(odt) << " " << rk << " = " << FromAcc(odt, Combine(op->reduce, acc_dt, init, acc)) << ";\n";
+        if (!o.empty()) body << "    if (lt == 0) " << o << "[row] = " << StoreExpr(odt, rk) << ";\n";
+        gen.fixed[m->id] = rk;
+      } else if (m->type.dims == X) {
+        if (o.empty()) continue;                // internal: the members that read it recompute it
+        std::vector<std::string> vals = row_phase(m);
+        body << loop_head << gen.body.str();
+        DT dt = m->type.dt;
+        if (!vec) {
+          body << "      " << o << "[e] = " << StoreExpr(dt, vals[0]) << ";\n";
+        } else if (dt == DT::kF32) {
+          body << "      *(float4*)(" << o << " + e) = make_float4(" << vals[0] << ", " << vals[1] << ", " << vals[2] << ", " << vals[3] << ");\n";
+        } else if (dt == DT::kBF16 || dt == DT::kF16) {
+          auto h = [&](int l) { return "(unsigned)" + StoreExpr(dt, vals[l]); };
+          body << "      *(uint2*)(" << o << " + e) = make_uint2(" << h(0) << " | (" << h(1) << " << 16), " << h(2) << " | (" << h(3) << " << 16));\n";
+        } else {
+          for (int l = 0; l < 4; ++l) body << "      " << o << "[e + " << l << "] = " << StoreExpr(dt, vals[l]) << ";\n";
+        }
+        body << "    }\n";
+      } else {
+        // row scalar: every thread of the row computes it
+        gen.cse.clear();
+        gen.body.str("");
+        gen.body.clear();
+        gen.indent = "    ";
+        gen.vec = false;
+        gen.identity = gen.row_ident;
+        std::string v = gen.Emit(m, gen.RowIndex(m->type.dims));
+        body << gen.body.str() << "    const " << CType(m->type.dt) << " " << rk << " = " << v << ";\n";
+        if (!o.empty()) body << "    if (lt == 0) " << o << "[row] = " << StoreExpr(m->type.dt, rk) << ";\n";
+        gen.fixed[m->id] = rk;
+      }
+    }
+    if (dry || gen.conflict) {
+      bool ok = !gen.conflict;
+      slot_of_ = saved;
+      p_->slots.resize(saved_slots);
+      if (!dry) throw LowerError{"internal: row fusion conflict"};
+      return ok;
+    }
+    for (size_t k = 0; k < members.size(); ++k) slot_of_[members[k]->id] = member_slot[k];
+    std::vector<DT> in_dts;
+    for (int s : gen.in_slots) in_dts.push_back(SlotDt(s));
+    std::string fn = KName();
+    const int threads = block_mode ? 512 : 256;
+    src_ << "extern \"C\" __global__ void __launch_bounds__(" << threads << ") " << fn << "("
+         << KernelParams(gen.in_slots, (int)out_slots.size(), false) << ") {\n"
+         << ParamCasts(gen.in_slots, in_dts, out_dts);
+    for (const auto& s : shared) src_ << "  __shared__ " << s.first << " " << s.second << "[32];\n";
+    if (block_mode)
+      src_ << "  const int lt = threadIdx.x;\n"
+           << "  for (long long row = blockIdx.x; row < " << rows << "LL; row += gridDim.x) {\n";
+    else
+      src_ << "  const int lt = threadIdx.x & 31;\n"
+           << "  for (long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); row < " << rows
+           << "LL; row += (long long)gridDim.x * 8) {\n";
+    src_ << ob.str() << body.str() << "  }\n}\n";
+    EndKernel();
+    Launch Lc;
+    Lc.fn = fn;
+    Lc.in_slots = gen.in_slots;
+    Lc.out_slots = out_slots;
+    Lc.block = threads;
+    Lc.grid_x = block_mode ? std::max<int64_t>(1, rows) : std::max<int64_t>(1, (rows + 7) / 8);
+    Lc.grid_stride = true;
+    Step st;
+    st.kind = StepKind::kFusion;
+    st.launches.push_back(Lc);
+    for (const Value* m : members)
+      if (m->def && m->def->name == "reduce") {
+        st.label = "row " + m->def->operands[0]->type.str() + " x" + std::to_string(members.size());
+        break;
+      }
+    p_->steps.push_back(st);
+    for (size_t k = 0; k < out_slots.size(); ++k) RecordDt(out_slots[k], out_dts[k]);
+    return true;
   }
 
   // ---------------------------------------------------------------- reductions
@@ -1058,34 +1459,36 @@ class Lowerer {
       if (block_per_row) {
         k << "  __shared__ " << acc_t << " red[32];\n"
           << "  for (long long row = blockIdx.x; row < " << n_out << "LL; row += gridDim.x) {\n"
-          << ob.str() << "    " << acc_t << " acc = " << init_expr << ";\n"
+          << ob.str() << "    " << acc_t << " acc = " << "(" + acc_t + ")(" + IdentityOf(kind, acc_dt) + ")" << ";\n"
           << "#pragma unroll 4\n    for (long long j = threadIdx.x; j < " << L << "LL; j += " << threads << ") {\n"
           << gen.body.str() << "      acc = " << combine("acc", "(" + acc_t + ")(" + v + ")") << ";\n    }\n"
           << shfl_red
           << "    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;\n    __syncthreads();\n"
-          << "    if (threadIdx.x < 32) {\n      acc = threadIdx.x < " << threads / 32 << " ? red[threadIdx.x] : " << init_expr << ";\n"
+          << "    if (threadIdx.x < 32) {\n      acc = threadIdx.x < " << threads / 32 << " ? red[threadIdx.x] : (" << acc_t << ")(" << IdentityOf(kind, acc_dt) << ");\n"
           << "  " << shfl_red
-          << "      if (threadIdx.x == 0) out0[row] = " << StoreExpr(odt, "acc") << ";\n    }\n    __syncthreads();\n  }\n}\n";
+          << "      if (threadIdx.x == 0) out0[row] = " << StoreExpr(odt, combine(init_expr, "acc")) << ";\n    }\n    __syncthreads();\n  }\n}\n";
         Launch Lc;
         Lc.fn = fn;
         Lc.in_slots = gen.in_slots;
         Lc.out_slots = {out_slot};
         Lc.block = threads;
-        Lc.grid_x = std::max<int64_t>(1, std::min<int64_t>(n_out, 148 * 8));
+        Lc.grid_x = std::max<int64_t>(1, n_out);
+        Lc.grid_stride = true;
         st.launches.push_back(Lc);
       } else {
         k << "  const int lane = threadIdx.x & 31;\n"
           << "  for (long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); row < " << n_out << "LL; row += (long long)gridDim.x * 8) {\n"
-          << ob.str() << "    " << acc_t << " acc = " << init_expr << ";\n"
+          << ob.str() << "    " << acc_t << " acc = " << "(" + acc_t + ")(" + IdentityOf(kind, acc_dt) + ")" << ";\n"
           << "#pragma unroll 4\n    for (long long j = lane; j < " << L << "LL; j += 32) {\n"
           << gen.body.str() << "      acc = " << combine("acc", "(" + acc_t + ")(" + v + ")") << ";\n    }\n"
-          << shfl_red << "    if (lane == 0) out0[row] = " << StoreExpr(odt, "acc") << ";\n  }\n}\n";
+          << shfl_red << "    if (lane == 0) out0[row] = " << StoreExpr(odt, combine(init_expr, "acc")) << ";\n  }\n}\n";
         Launch Lc;
         Lc.fn = fn;
         Lc.in_slots = gen.in_slots;
         Lc.out_slots = {out_slot};
         Lc.block = 256;
-        Lc.grid_x = std::max<int64_t>(1, std::min<int64_t>((n_out + 7) / 8, 148 * 16));
+        Lc.grid_x = std::max<int64_t>(1, (n_out + 7) / 8);
+        Lc.grid_stride = true;
         st.launches.push_back(Lc);
       }
     } else {

@@ -33,6 +33,7 @@ struct Launch {
   int64_t grid_x = 1, grid_y = 1, grid_z = 1;
   int block = 256;
   int smem = 0;
+  bool grid_stride = false;    // any grid size is correct: launched with at most one wave of CTAs
 };
 
 struct GemmStep {

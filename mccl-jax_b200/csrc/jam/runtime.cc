@@ -30,12 +30,14 @@ typedef CUresult (*FnModuleGetFunction)(CUfunction*, CUmodule, const char*);
 typedef CUresult (*FnLaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
                                    CUstream, void**, void**);
 typedef CUresult (*FnModuleUnload)(CUmodule);
+typedef CUresult (*FnOccupancy)(int*, CUfunction, int, size_t);
 
 struct Driver {
   FnModuleLoadData load = nullptr;
   FnModuleGetFunction get = nullptr;
   FnLaunchKernel launch = nullptr;
   FnModuleUnload unload = nullptr;
+  FnOccupancy occupancy = nullptr;
   bool ok = false;
 };
 
@@ -54,7 +56,8 @@ const Driver& Drv() {
     d.get = (FnModuleGetFunction)sym("cuModuleGetFunction");
     d.launch = (FnLaunchKernel)sym("cuLaunchKernel");
     d.unload = (FnModuleUnload)sym("cuModuleUnload");
-    d.ok = d.load && d.get && d.launch && d.unload;
+    d.occupancy = (FnOccupancy)sym("cuOccupancyMaxActiveBlocksPerMultiprocessor");
+    d.ok = d.load && d.get && d.launch && d.unload && d.occupancy;
   });
   return d;
 }
@@ -218,6 +221,13 @@ std::string Executable::Load(DeviceState& dev, PerDevice** pd) {
           if (d.get(&f, (CUmodule)m, L.fn.c_str()) == CUDA_SUCCESS) break;
         if (!f) return "generated kernel " + L.fn + " not found";
         p.fns[L.fn] = f;
+        if (L.grid_stride) {
+          // one full wave: a grid-stride kernel gains nothing from CTAs that wait for a free SM
+          int per_sm = 0, sms = 0;
+          cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev.ordinal);
+          if (d.occupancy(&per_sm, f, L.block, (size_t)L.smem) == CUDA_SUCCESS && per_sm > 0 && sms > 0)
+            p.wave[L.fn] = (int64_t)per_sm * sms;
+        }
       }
   }
   for (const ConstBlob& c : plan_.consts) {
@@ -275,7 +285,12 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
           if (L.scratch >= 0) { err = slot(L.scratch); if (!err.empty()) return fail(err); vals.push_back(ptr[L.scratch]); }
           std::vector<void*> params;
           for (void*& v : vals) params.push_back(&v);
-          CUresult r = drv.launch((CUfunction)pd->fns.at(L.fn), (unsigned)L.grid_x, (unsigned)L.grid_y, (unsigned)L.grid_z, L.block, 1, 1,
+          int64_t gx = L.grid_x;
+          if (L.grid_stride) {
+            auto w = pd->wave.find(L.fn);
+            if (w != pd->wave.end()) gx = std::max<int64_t>(1, std::min(gx, w->second));
+          }
+          CUresult r = drv.launch((CUfunction)pd->fns.at(L.fn), (unsigned)gx, (unsigned)L.grid_y, (unsigned)L.grid_z, L.block, 1, 1,
                                   L.smem, (CUstream)st, params.data(), nullptr);
           if (r != CUDA_SUCCESS) return fail("launch of " + L.fn + " failed (" + std::to_string((int)r) + ")");
         }

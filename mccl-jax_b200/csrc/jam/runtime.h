@@ -45,6 +45,7 @@ class Executable {
   struct PerDevice {
     std::vector<void*> modules;              // CUmodule per NVRTC group
     std::map<std::string, void*> fns;        // CUfunction by kernel name
+    std::map<std::string, int64_t> wave;     // grid-stride kernels: resident CTAs on the device
     std::vector<void*> consts;               // uploaded constants
   };
   std::string Load(DeviceState& dev, PerDevice** pd);

@@ -32,7 +32,7 @@ def test_attention_unfused_when_disabled(lib_path, monkeypatch):
     p = configs.attention_program(B=1, H=2, S=256, causal=True, with_inputs=False)
     rc, rep = report(lib_path, p.text)
     assert rc == 0, rep
-    assert "attention" not in rep and rep.count("gemm") == 2 and "reduce" in rep
+    assert "attention" not in rep and rep.count("gemm") == 2 and ("reduce" in rep or "row" in rep)
 
 
 def test_mlp_step_compiles_with_generated_kernels(lib_path):
