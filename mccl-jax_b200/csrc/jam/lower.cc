@@ -91,11 +91,19 @@ std::string LoadExpr(DT t, const std::string& ptr, const std::string& idx) {
   if (t == DT::kPred) return "(" + raw + " != 0)";
   return "(" + CType(t) + ")" + raw;
 }
+// A bf16-typed register always holds a value that bf16 represents exactly (loads are exact and
+// every op that makes a bf16 value rounds it), so storing it is a shift, not a conversion.
 std::string StoreExpr(DT t, const std::string& v) {
-  if (t == DT::kBF16) return "f2bf(" + v + ")";
+  if (t == DT::kBF16) return "bf_bits(" + v + ")";
   if (t == DT::kF16) return "f2h(" + v + ")";
   if (t == DT::kPred) return "(unsigned char)(" + v + ")";
   return "(" + MemType(t) + ")(" + v + ")";
+}
+
+// two 16-bit float values packed into one 32-bit word, the first in the low half
+std::string Pack16(DT t, const std::string& a, const std::string& b) {
+  if (t == DT::kBF16) return "((__float_as_uint(" + a + ") >> 16) | (__float_as_uint(" + b + ") & 0xffff0000u))";
+  return "((unsigned)f2h(" + a + ") | ((unsigned)f2h(" + b + ") << 16))";
 }
 
 std::string FloatLit(double d) {
@@ -113,8 +121,19 @@ std::string DoubleLit(double d) {
   std::snprintf(buf, sizeof(buf), "__longlong_as_double(0x%016llxLL)", (unsigned long long)u);
   return buf;
 }
+// round-to-nearest-even of a float to bf16 precision (host side, for literals)
+float RoundBf16(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return f;   // NaN stays NaN
+  u = (u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
 std::string Literal(DT t, double v) {
-  if (t == DT::kF32 || t == DT::kBF16 || t == DT::kF16) return FloatLit(v);
+  if (t == DT::kBF16) return FloatLit(RoundBf16((float)v));
+  if (t == DT::kF32 || t == DT::kF16) return FloatLit(v);
   if (t == DT::kF64) return DoubleLit(v);
   if (t == DT::kPred) return v != 0 ? "true" : "false";
   if (DTIsUnsigned(t)) return std::to_string((unsigned long long)v) + "ULL";
@@ -131,6 +150,7 @@ __device__ __forceinline__ float h2f(unsigned short h) {
 __device__ __forceinline__ unsigned short f2h(float f) {
   unsigned short r; asm("cvt.rn.f16.f32 %0, %1;" : "=h"(r) : "f"(f)); return r; }
 __device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
+__device__ __forceinline__ unsigned short bf_bits(float f) { return (unsigned short)(__float_as_uint(f) >> 16); }
 __device__ __forceinline__ float rhf(float f) { return h2f(f2h(f)); }
 __device__ __forceinline__ float fmax_n(float a, float b) { return (a != a || b != b) ? __int_as_float(0x7fc00000) : fmaxf(a, b); }
 __device__ __forceinline__ float fmin_n(float a, float b) { return (a != a || b != b) ? __int_as_float(0x7fc00000) : fminf(a, b); }
@@ -312,7 +332,7 @@ struct Gen {
     }
     if (n == "iota") {
       int d = (int)op->ints.at("dim")[0];
-      return Var(ty.dt, "(" + CType(ty.dt) + ")(" + idx[d] + ")");
+      return Round(ty.dt, Var(ty.dt, "(" + CType(ty.dt) + ")(" + idx[d] + ")"));
     }
     if (n == "broadcast_in_dim") {
       const auto& dims = op->ints.at("dims");
@@ -1108,9 +1128,8 @@ class Lowerer {
       if (out_dts[k] == DT::kF32) {
         src_ << "    *(float4*)(out" << k << " + i) = make_float4(" << r4[0] << ", " << r4[1] << ", " << r4[2] << ", " << r4[3] << ");\n";
       } else if (out_dts[k] == DT::kBF16 || out_dts[k] == DT::kF16) {
-        auto h = [&](int l) { return "(unsigned)" + StoreExpr(out_dts[k], r4[l]); };
-        src_ << "    *(uint2*)(out" << k << " + i) = make_uint2(" << h(0) << " | (" << h(1) << " << 16), " << h(2) << " | ("
-             << h(3) << " << 16));\n";
+        src_ << "    *(uint2*)(out" << k << " + i) = make_uint2(" << Pack16(out_dts[k], r4[0], r4[1]) << ", "
+             << Pack16(out_dts[k], r4[2], r4[3]) << ");\n";
       } else {
         for (int l = 0; l < 4; ++l) src_ << "    out" << k << "[i + " << l << "] = " << StoreExpr(out_dts[k], r4[l]) << ";\n";
       }
@@ -1212,6 +1231,33 @@ class Lowerer {
     return "(" + CType(acc_dt) + ")(" + iv + ")";
   }
 
+  // rmax = max(A) over the row (identity init) and rsum = sum(exp(A - rmax)) (identity init), both
+  // f32, where the subtracted value reads rmax at the current row: one online walk computes both.
+  bool OnlinePair(const Value* rmax, const Value* rsum, const Gen& g) const {
+    const Op* a = rmax->def;
+    const Op* b = rsum->def;
+    if (!a || !b || a->name != "reduce" || b->name != "reduce" || a->reduce != ReduceKind::kMax || b->reduce != ReduceKind::kAdd)
+      return false;
+    if (rmax->type.dt != DT::kF32 || rsum->type.dt != DT::kF32 || a->operands[0]->type.dt != DT::kF32) return false;
+    double ia = 0, ib = 1;
+    if (!IsScalarConst(a->operands[1], &ia) || !IsScalarConst(b->operands[1], &ib) || !(std::isinf(ia) && ia < 0) || ib != 0)
+      return false;
+    const Value* e = b->operands[0];
+    if (!e->def || e->def->name != "exponential") return false;
+    const Value* d = e->def->operands[0];
+    if (!d->def || d->def->name != "subtract" || d->def->operands[0] != a->operands[0]) return false;
+    // the subtrahend must be rmax of this row: emit it with rmax as a marked register
+    Gen probe;
+    probe.slot_of = &slot_of_;
+    probe.row_ident = g.row_ident;
+    probe.row_dims = g.row_dims;
+    probe.fixed[rmax->id] = "RMAX";
+    std::vector<std::string> id = g.row_ident;
+    id.push_back("j");
+    std::string r = probe.Emit(d->def->operands[1], id);
+    return !probe.conflict && r == "RMAX" && probe.in_slots.empty();
+  }
+
   bool TryRow(const std::vector<const Value*>& members, const std::vector<int64_t>& X, bool dry) {
     const std::vector<int64_t> kept(X.begin(), X.end() - 1);
     const int64_t L = X.back();
@@ -1220,8 +1266,10 @@ class Lowerer {
     const bool wide = rows * L >= (1LL << 31);
     const bool block_mode = L > 2048;
     const int T = block_mode ? 512 : 32;          // threads that share a row
+    // Each thread takes four elements per step: consecutive ones with vector loads when L % 4 == 0,
+    // else four T-strided ones (coalesced scalar loads) whose indices are clamped into the row and
+    // whose lanes past the end (ok_l false) contribute nothing.
     const bool vec = L % 4 == 0 && !std::getenv("B200_NO_VEC");
-    const int V = vec ? 4 : 1;
     std::vector<int> saved(slot_of_);
     size_t saved_slots = p_->slots.size();
     std::set<int> ids;
@@ -1255,10 +1303,17 @@ class Lowerer {
       lanes.push_back(gen.row_ident);
       lanes.back().push_back("j_" + std::to_string(l));
     }
-    const std::string loop_head = "#pragma unroll 4\n    for (int j = lt * " + std::to_string(V) + "; j < " + std::to_string(L) +
-                                  "; j += " + std::to_string(T * V) + ") {\n" +
-                                  (vec ? "      const int j_0 = j, j_1 = j + 1, j_2 = j + 2, j_3 = j + 3;\n" : "") +
-                                  "      const long long e = (long long)row * " + std::to_string(L) + "LL + j;\n";
+    const std::string Ls = std::to_string(L), Ts = std::to_string(T), last = std::to_string(L - 1);
+    const std::string loop_head =
+        vec ? "#pragma unroll 4\n    for (int j = lt * 4; j < " + Ls + "; j += " + std::to_string(4 * T) + ") {\n" +
+                  "      const int j_0 = j, j_1 = j + 1, j_2 = j + 2, j_3 = j + 3;\n"
+            : "#pragma unroll 2\n    for (int j = lt; j < " + Ls + "; j += " + std::to_string(4 * T) + ") {\n" +
+                  "      const bool ok_1 = j + " + Ts + " < " + Ls + ", ok_2 = j + " + std::to_string(2 * T) + " < " + Ls +
+                  ", ok_3 = j + " + std::to_string(3 * T) + " < " + Ls + ";\n" +
+                  "      const int j_0 = j, j_1 = ok_1 ? j + " + Ts + " : " + last + ", j_2 = ok_2 ? j + " + std::to_string(2 * T) +
+                  " : " + last + ", j_3 = ok_3 ? j + " + std::to_string(3 * T) + " : " + last + ";\n";
+    auto ok = [&](int l) { return vec || l == 0 ? std::string() : "ok_" + std::to_string(l); };
+    auto elem_index = [&](int l) { return "(long long)row * " + Ls + "LL + j_" + std::to_string(l); };
     // a phase over the row: element values of `v` (one per lane in vector mode)
     auto row_phase = [&](const Value* v) {
       gen.cse.clear();
@@ -1269,18 +1324,70 @@ class Lowerer {
       gen.vec = vec;
       gen.vinner = "j";
       gen.lane_identity = lanes;
-      gen.identity = vec ? lanes[0] : ident;
+      gen.identity = lanes[0];
       std::vector<std::string> vals;
-      if (vec) for (int l = 0; l < 4; ++l) vals.push_back(gen.Emit(v, lanes[l]));
-      else vals.push_back(gen.Emit(v, ident));
+      for (int l = 0; l < 4; ++l) vals.push_back(gen.Emit(v, lanes[l]));
       return vals;
     };
     std::vector<std::pair<std::string, std::string>> shared;   // block mode: (type, name)
+    std::vector<bool> done(members.size(), false);
     for (size_t k = 0; k < members.size(); ++k) {
+      if (done[k]) continue;
       const Value* m = members[k];
       const Op* op = m->def;
       const std::string rk = "r" + std::to_string(k);
       const std::string o = out_of[k] >= 0 ? "out" + std::to_string(out_of[k]) : "";
+      // the next reduction, past full members only (they read at most this row's earlier results)
+      size_t k2 = k + 1;
+      while (k2 < members.size() && members[k2]->type.dims == X && !(members[k2]->def && members[k2]->def->name == "reduce")) ++k2;
+      if (op && op->name == "reduce" && k2 < members.size() && OnlinePair(m, members[k2], gen)) {
+        // max(x) then sum(exp(x - max)) in one walk of the row: (mx, s) with s = sum exp(x_i - mx)
+        // over the elements seen so far, rescaled when mx grows.  Edge cases match the two-pass
+        // form: a NaN makes both NaN; an all -inf row or a +inf element makes the sum NaN.
+        const std::string k1 = std::to_string(k), kk = std::to_string(k2);
+        const std::string mx = "mx" + k1, s = "sx" + k1, bad = "bad" + k1, NINF = "(-__int_as_float(0x7f800000))";
+        std::vector<std::string> vals = row_phase(op->operands[0]);
+        body << "    float " << mx << " = " << NINF << ", " << s << " = 0.f;\n    int " << bad << " = 0;\n"
+             << loop_head << gen.body.str();
+        body << "      {\n";
+        for (int l = 0; l < 4; ++l)
+          body << "        const float c" << l << " = " << (ok(l).empty() ? vals[l] : ok(l) + " ? " + vals[l] + " : " + NINF) << ";\n";
+        body << "        " << bad << " |= (c0 != c0) | (c1 != c1) | (c2 != c2) | (c3 != c3);\n"
+             << "        const float c = fmaxf(fmaxf(c0, c1), fmaxf(c2, c3));\n"
+             << "        if (c > " << mx << ") { " << s << " *= expf(" << mx << " - c); " << mx << " = c; }\n"
+             << "        if (" << mx << " > " << NINF << ") " << s << " += (expf(c0 - " << mx << ") + expf(c1 - " << mx
+             << ")) + (expf(c2 - " << mx << ") + expf(c3 - " << mx << "));\n      }\n";
+        body << "    }\n";
+        auto merge = [&](const std::string& om, const std::string& os) {
+          return "{ const float nm = fmaxf(" + mx + ", " + om + "); " + s + " = (" + mx + " == " + NINF + " ? 0.f : " + s +
+                 " * expf(" + mx + " - nm)) + (" + om + " == " + NINF + " ? 0.f : " + os + " * expf(" + om + " - nm)); " + mx +
+                 " = nm; }";
+        };
+        body << "    for (int o = 16; o; o >>= 1) { const float om = __shfl_xor_sync(0xffffffffu, " << mx
+             << ", o), os = __shfl_xor_sync(0xffffffffu, " << s << ", o); " << bad << " |= __shfl_xor_sync(0xffffffffu, " << bad
+             << ", o); " << merge("om", "os") << " }\n";
+        if (block_mode) {
+          std::string rm = "redm" + k1, rs = "reds" + k1, rb = "redb" + k1;
+          shared.push_back({"float", rm});
+          shared.push_back({"float", rs});
+          shared.push_back({"int", rb});
+          body << "    if ((threadIdx.x & 31) == 0) { " << rm << "[threadIdx.x >> 5] = " << mx << "; " << rs << "[threadIdx.x >> 5] = "
+               << s << "; " << rb << "[threadIdx.x >> 5] = " << bad << "; }\n    __syncthreads();\n"
+               << "    " << mx << " = " << rm << "[0]; " << s << " = " << rs << "[0]; " << bad << " = " << rb << "[0];\n"
+               << "    for (int w = 1; w < " << T / 32 << "; ++w) { " << bad << " |= " << rb << "[w]; " << merge(rm + "[w]", rs + "[w]")
+               << " }\n    __syncthreads();\n";
+        }
+        body << "    if (" << bad << ") { " << mx << " = __int_as_float(0x7fc00000); " << s << " = " << mx << "; } else if (isinf(" << mx
+             << ")) " << s << " = __int_as_float(0x7fc00000);\n"
+             << "    const float r" << k1 << " = " << mx << ", r" << kk << " = " << s << ";\n";
+        for (size_t q : {k, k2}) {
+          if (out_of[q] >= 0)
+            body << "    if (lt == 0) out" << out_of[q] << "[row] = r" << q << ";\n";
+          gen.fixed[members[q]->id] = "r" + std::to_string(q);
+        }
+        done[k2] = true;
+        continue;
+      }
       if (op && op->name == "reduce") {
         DT odt = m->type.dt, acc_dt = AccDt(odt);
         std::string acc_t = CType(acc_dt), acc = "acc" + std::to_string(k);
@@ -1288,7 +1395,11 @@ class Lowerer {
         std::vector<std::string> vals = row_phase(op->operands[0]);
         body << "    " << acc_t << " " << acc << " = (" << acc_t << ")(" << IdentityOf(op->reduce, acc_dt) << ");\n"
              << loop_head << gen.body.str();
-        for (const auto& v : vals) body << "      " << acc << " = " << Combine(op->reduce, acc_dt, acc, "(" + acc_t + ")(" + v + ")") << ";\n";
+        for (int l = 0; l < 4; ++l) {
+          std::string x = "(" + acc_t + ")(" + vals[l] + ")";
+          if (!ok(l).empty()) x = "(" + ok(l) + " ? " + x + " : (" + acc_t + ")(" + IdentityOf(op->reduce, acc_dt) + "))";
+          body << "      " << acc << " = " << Combine(op->reduce, acc_dt, acc, x) << ";\n";
+        }
         body << "    }\n"
              << "    for (int o = 16; o; o >>= 1) { " << acc_t << " oth = __shfl_xor_sync(0xffffffffu, " << acc << ", o); "
              << acc << " = " << Combine(op->reduce, acc_dt, acc, "oth") << "; }\n";
@@ -1309,14 +1420,14 @@ class Lowerer {
         body << loop_head << gen.body.str();
         DT dt = m->type.dt;
         if (!vec) {
-          body << "      " << o << "[e] = " << StoreExpr(dt, vals[0]) << ";\n";
+          for (int l = 0; l < 4; ++l)
+            body << "      " << (ok(l).empty() ? "" : "if (" + ok(l) + ") ") << o << "[" << elem_index(l) << "] = " << StoreExpr(dt, vals[l]) << ";\n";
         } else if (dt == DT::kF32) {
-          body << "      *(float4*)(" << o << " + e) = make_float4(" << vals[0] << ", " << vals[1] << ", " << vals[2] << ", " << vals[3] << ");\n";
+          body << "      *(float4*)(" << o << " + " << elem_index(0) << ") = make_float4(" << vals[0] << ", " << vals[1] << ", " << vals[2] << ", " << vals[3] << ");\n";
         } else if (dt == DT::kBF16 || dt == DT::kF16) {
-          auto h = [&](int l) { return "(unsigned)" + StoreExpr(dt, vals[l]); };
-          body << "      *(uint2*)(" << o << " + e) = make_uint2(" << h(0) << " | (" << h(1) << " << 16), " << h(2) << " | (" << h(3) << " << 16));\n";
+          body << "      *(uint2*)(" << o << " + " << elem_index(0) << ") = make_uint2(" << Pack16(dt, vals[0], vals[1]) << ", " << Pack16(dt, vals[2], vals[3]) << ");\n";
         } else {
-          for (int l = 0; l < 4; ++l) body << "      " << o << "[e + " << l << "] = " << StoreExpr(dt, vals[l]) << ";\n";
+          for (int l = 0; l < 4; ++l) body << "      " << o << "[" << elem_index(l) << "] = " << StoreExpr(dt, vals[l]) << ";\n";
         }
         body << "    }\n";
       } else {
@@ -1466,7 +1577,7 @@ class Lowerer {
           << "    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;\n    __syncthreads();\n"
           << "    if (threadIdx.x < 32) {\n      acc = threadIdx.x < " << threads / 32 << " ? red[threadIdx.x] : (" << acc_t << ")(" << IdentityOf(kind, acc_dt) << ");\n"
           << "  " << shfl_red
-          << "      if (threadIdx.x == 0) out0[row] = " << StoreExpr(odt, combine(init_expr, "acc")) << ";\n    }\n    __syncthreads();\n  }\n}\n";
+          << "      if (threadIdx.x == 0) out0[row] = " << StoreExpr(odt, FromAcc(odt, combine(init_expr, "acc"))) << ";\n    }\n    __syncthreads();\n  }\n}\n";
         Launch Lc;
         Lc.fn = fn;
         Lc.in_slots = gen.in_slots;
@@ -1481,7 +1592,7 @@ class Lowerer {
           << ob.str() << "    " << acc_t << " acc = " << "(" + acc_t + ")(" + IdentityOf(kind, acc_dt) + ")" << ";\n"
           << "#pragma unroll 4\n    for (long long j = lane; j < " << L << "LL; j += 32) {\n"
           << gen.body.str() << "      acc = " << combine("acc", "(" + acc_t + ")(" + v + ")") << ";\n    }\n"
-          << shfl_red << "    if (lane == 0) out0[row] = " << StoreExpr(odt, combine(init_expr, "acc")) << ";\n  }\n}\n";
+          << shfl_red << "    if (lane == 0) out0[row] = " << StoreExpr(odt, FromAcc(odt, combine(init_expr, "acc"))) << ";\n  }\n}\n";
         Launch Lc;
         Lc.fn = fn;
         Lc.in_slots = gen.in_slots;
@@ -1522,7 +1633,7 @@ class Lowerer {
         << "#pragma unroll 4\n    for (long long j = j0; j < j1; ++j) {\n"
         << gen.body.str() << "      acc = " << combine("acc", "(" + acc_t + ")(" + v + ")") << ";\n    }\n";
       if (chunks > 1) k << "  ((" << acc_t << "*)scratch)[(long long)blockIdx.y * " << n_out << "LL + o] = acc;\n}\n";
-      else k << "  out0[o] = " << StoreExpr(odt, "acc") << ";\n}\n";
+      else k << "  out0[o] = " << StoreExpr(odt, FromAcc(odt, "acc")) << ";\n}\n";
       Launch L1;
       L1.fn = fn;
       L1.in_slots = gen.in_slots;
@@ -1543,7 +1654,7 @@ class Lowerer {
           << "  long long o = (long long)blockIdx.x * 256 + threadIdx.x;\n  if (o >= " << n_out << "LL) return;\n"
           << "  " << acc_t << " acc = " << init_expr << ";\n"
           << "  for (int c = 0; c < " << chunks << "; ++c) acc = " << combine("acc", "part[(long long)c * " + std::to_string(n_out) + "LL + o]") << ";\n"
-          << "  out0[o] = " << StoreExpr(odt, "acc") << ";\n}\n";
+          << "  out0[o] = " << StoreExpr(odt, FromAcc(odt, "acc")) << ";\n}\n";
         Launch L2;
         L2.fn = fn2;
         L2.in_slots = {scratch};

@@ -184,3 +184,28 @@ def test_integer_row_max_is_bit_exact(client):
     refs = oracle_run(text, [xv])
     for o, r in zip(outs, refs):
         np.testing.assert_array_equal(o, r)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [1000, 5003])
+def test_online_max_sum_edge_rows_match_two_pass(client, n):
+    """max and sum(exp(x - max)) share one walk of the row; rows holding -inf (masked), all -inf,
+    +inf or NaN must come out as the two-pass definition gives them."""
+    b = Builder("jit_lse_edge")
+    x = b.arg((8, n), "f32")
+    m = b.max(x, 1, keepdims=True)
+    s = b.sum(b.exp(x - b.broadcast_to(m, x.shape)), 1)
+    text = b.text([s, b.reshape(m, (8,))])
+    xv = np.random.default_rng(11).standard_normal((8, n)).astype(np.float32)
+    xv[1, n // 2:] = -np.inf          # causal-style mask
+    xv[2, :7] = -np.inf               # masked head of the row
+    xv[3, :] = -np.inf                # fully masked
+    xv[4, 17] = np.inf
+    xv[5, 3] = np.nan
+    xv[6] *= 30.0                     # large spread: many rescales
+    outs = client.run(text, [xv])
+    refs = oracle_run(text, [xv])
+    for o, r in zip(outs, refs):
+        np.testing.assert_array_equal(np.isnan(o), np.isnan(r))
+        ok = ~np.isnan(r)
+        np.testing.assert_allclose(o[ok], r[ok], rtol=RTOL_F32)
