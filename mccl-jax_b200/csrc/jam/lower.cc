@@ -602,6 +602,7 @@ class Lowerer {
     Retype();
     if (opt_.fuse_attention) MatchAttention();
     DecideMaterialization();
+    DecideStoredTypes();
     BindLeaves();
     EmitSteps();
     BindOutputs();
@@ -622,6 +623,92 @@ class Lowerer {
   std::vector<bool> need_;                 // value must be materialized
   std::vector<bool> ext_use_;              // read by a program output, a library step or attention
   std::vector<std::set<int>> cons_;        // materialized consumers of each value
+  std::unordered_map<int, DT> demote_;     // value id -> narrower type its buffer holds
+
+  // An f32 value read only by dots whose other operand is 16-bit is rounded to that type when the
+  // dot runs; its producing kernel stores it rounded instead (half the bytes, no conversion pass).
+  void DecideStoredTypes() {
+    if (std::getenv("B200_DOT_MIXED_F32")) return;
+    std::unordered_set<int> outs;
+    for (Value* o : g_.outputs) outs.insert(o->id);
+    for (auto& opp : g_.ops) {
+      const Op* op = opp.get();
+      if (dead_[op->index] || op->results.size() != 1 || !IsElementwise(op) || IsAlias(op) || op->name == "constant") continue;
+      const Value* r = op->result();
+      if (!need_[r->id] || r->type.dt != DT::kF32 || outs.count(r->id) || attn_.count(r->id)) continue;
+      bool any_attn = false;
+      for (auto& kv : attn_in_) for (const Value* v : kv.second) any_attn = any_attn || v == r;
+      if (any_attn) continue;
+      DT narrow = DT::kF32;
+      bool ok = !r->users.empty();
+      // a padded row pitch lets every dot read it in place when its innermost extent is not a
+      // multiple of 8 (TMA row strides are multiples of 16 bytes): allowed when each dot uses the
+      // innermost dim alone as its contracting or free dim, with the operand otherwise in order
+      const int rank = r->type.rank();
+      bool pitch_ok = rank >= 2 && r->type.dims.back() % 8 != 0;
+      for (const Op* u : r->users) {
+        if (dead_[u->index]) continue;
+        if (u->name != "dot_general" && u->name != "dot") { ok = false; break; }
+        const Value* other = u->operands[0] == r ? u->operands[1] : u->operands[0];
+        if (u->operands[0] == r && u->operands[1] == r) { ok = false; break; }
+        DT t = other->type.dt;
+        if (t != DT::kBF16 && t != DT::kF16) { ok = false; break; }
+        if (narrow != DT::kF32 && narrow != t) { ok = false; break; }
+        narrow = t;
+        std::vector<int64_t> bat, fr, ct;
+        DotDims(u, u->operands[0] == r ? 0 : 1, &bat, &fr, &ct);
+        auto in_order = [&](std::vector<int64_t> o, const std::vector<int64_t>& y, const std::vector<int64_t>& z) {
+          o.insert(o.end(), y.begin(), y.end());
+          o.insert(o.end(), z.begin(), z.end());
+          for (size_t k = 0; k < o.size(); ++k) if (o[k] != (int64_t)k) return false;
+          return true;
+        };
+        const std::vector<int64_t> last{rank - 1};
+        pitch_ok = pitch_ok && ((ct == last && in_order(bat, fr, ct)) || (fr == last && in_order(bat, ct, fr)));
+      }
+      if (ok && narrow != DT::kF32) {
+        demote_[r->id] = narrow;
+        if (pitch_ok) pitch_[r->id] = (r->type.dims.back() + 7) / 8 * 8;
+      }
+    }
+  }
+  // batch / free / contracting dims of operand `side` (0 lhs, 1 rhs) of a dot
+  static void DotDims(const Op* op, int side, std::vector<int64_t>* bat, std::vector<int64_t>* fr, std::vector<int64_t>* ct) {
+    auto get = [&](const char* k) { auto it = op->ints.find(k); return it == op->ints.end() ? std::vector<int64_t>{} : it->second; };
+    const Value* v = op->operands[side];
+    *bat = get(side ? "batching_dims.rhs" : "batching_dims.lhs");
+    *ct = get(side ? "contracting_dims.rhs" : "contracting_dims.lhs");
+    if (op->name == "dot") *ct = {side ? 0 : v->type.rank() - 1};
+    fr->clear();
+    for (int k = 0; k < v->type.rank(); ++k)
+      if (std::find(bat->begin(), bat->end(), k) == bat->end() && std::find(ct->begin(), ct->end(), k) == ct->end()) fr->push_back(k);
+  }
+  std::unordered_map<int, int64_t> pitch_;   // value id -> padded innermost row pitch (elements)
+  int64_t StoredPitch(const Value* v) const {
+    auto it = pitch_.find(v->id);
+    return it == pitch_.end() ? 0 : it->second;
+  }
+  int64_t StoredBytes(const Value* v) const {
+    const int64_t p = StoredPitch(v), n = v->type.numel();
+    if (!p) return n * DTBytes(StoredDt(v));
+    return n / v->type.dims.back() * p * DTBytes(StoredDt(v));
+  }
+  // element offset of linear index `i` in the buffer of v (padded pitch when it has one)
+  std::string StoredIndex(const Value* v, const std::string& i) const {
+    const int64_t p = StoredPitch(v);
+    if (!p) return i;
+    const std::string inner = std::to_string(v->type.dims.back());
+    return "((" + i + ") / " + inner + "LL * " + std::to_string(p) + "LL + (" + i + ") % " + inner + "LL)";
+  }
+  DT StoredDt(const Value* v) const {
+    auto it = demote_.find(v->id);
+    return it == demote_.end() ? v->type.dt : it->second;
+  }
+  // the value to store for root v into a buffer of type `dt` (rounded when the buffer is narrower)
+  static std::string StoreVal(const Value* v, DT dt, const std::string& x) {
+    if (dt == v->type.dt) return x;
+    return dt == DT::kBF16 ? "rbf(" + x + ")" : "rhf(" + x + ")";
+  }
   std::unordered_map<int, AttentionStep> attn_;  // result value id of the 2nd dot -> matched attention
   std::unordered_map<int, std::array<const Value*, 3>> attn_in_;
   std::ostringstream src_;
@@ -891,7 +978,7 @@ class Lowerer {
 
   int SlotFor(const Value* v) {
     v = Resolve(v);
-    if (slot_of_[v->id] < 0) slot_of_[v->id] = NewSlot(v->type.bytes());
+    if (slot_of_[v->id] < 0) slot_of_[v->id] = NewSlot(StoredBytes(v));
     return slot_of_[v->id];
   }
 
@@ -1044,7 +1131,7 @@ class Lowerer {
     size_t saved_slots = p_->slots.size();
     for (const Value* r : roots) {
       out_slots.push_back(SlotFor(r));
-      out_dts.push_back(r->type.dt);
+      out_dts.push_back(StoredDt(r));
     }
     Gen gen;
     gen.slot_of = &slot_of_;
@@ -1121,17 +1208,18 @@ class Lowerer {
     src_ << gen.body.str();
     for (size_t k = 0; k < roots.size(); ++k) {
       if (!vec) {
-        src_ << "    out" << k << "[i] = " << StoreExpr(out_dts[k], regs[k]) << ";\n";
+        src_ << "    out" << k << "[" << StoredIndex(roots[k], "i") << "] = " << StoreExpr(out_dts[k], StoreVal(roots[k], out_dts[k], regs[k])) << ";\n";
         continue;
       }
-      const auto& r4 = lregs[k];
+      std::vector<std::string> r4 = lregs[k];
+      for (auto& x : r4) x = StoreVal(roots[k], out_dts[k], x);
       if (out_dts[k] == DT::kF32) {
-        src_ << "    *(float4*)(out" << k << " + i) = make_float4(" << r4[0] << ", " << r4[1] << ", " << r4[2] << ", " << r4[3] << ");\n";
+        src_ << "    *(float4*)(out" << k << " + " << StoredIndex(roots[k], "i") << ") = make_float4(" << r4[0] << ", " << r4[1] << ", " << r4[2] << ", " << r4[3] << ");\n";
       } else if (out_dts[k] == DT::kBF16 || out_dts[k] == DT::kF16) {
-        src_ << "    *(uint2*)(out" << k << " + i) = make_uint2(" << Pack16(out_dts[k], r4[0], r4[1]) << ", "
+        src_ << "    *(uint2*)(out" << k << " + " << StoredIndex(roots[k], "i") << ") = make_uint2(" << Pack16(out_dts[k], r4[0], r4[1]) << ", "
              << Pack16(out_dts[k], r4[2], r4[3]) << ");\n";
       } else {
-        for (int l = 0; l < 4; ++l) src_ << "    out" << k << "[i + " << l << "] = " << StoreExpr(out_dts[k], r4[l]) << ";\n";
+        for (int l = 0; l < 4; ++l) src_ << "    out" << k << "[" << StoredIndex(roots[k], "i") << " + " << l << "] = " << StoreExpr(out_dts[k], r4[l]) << ";\n";
       }
     }
     src_ << "}\n";
@@ -1283,7 +1371,7 @@ class Lowerer {
       if (!ext) continue;
       out_of[k] = (int)out_slots.size();
       out_slots.push_back(SlotFor(m));
-      out_dts.push_back(m->type.dt);
+      out_dts.push_back(StoredDt(m));
     }
     std::vector<int> member_slot;
     for (const Value* m : members) {
@@ -1313,7 +1401,10 @@ class Lowerer {
                   "      const int j_0 = j, j_1 = ok_1 ? j + " + Ts + " : " + last + ", j_2 = ok_2 ? j + " + std::to_string(2 * T) +
                   " : " + last + ", j_3 = ok_3 ? j + " + std::to_string(3 * T) + " : " + last + ";\n";
     auto ok = [&](int l) { return vec || l == 0 ? std::string() : "ok_" + std::to_string(l); };
-    auto elem_index = [&](int l) { return "(long long)row * " + Ls + "LL + j_" + std::to_string(l); };
+    auto elem_index = [&](const Value* m, int l) {
+      const int64_t p = StoredPitch(m);
+      return "(long long)row * " + (p ? std::to_string(p) : Ls) + "LL + j_" + std::to_string(l);
+    };
     // a phase over the row: element values of `v` (one per lane in vector mode)
     auto row_phase = [&](const Value* v) {
       gen.cse.clear();
@@ -1418,16 +1509,17 @@ class Lowerer {
         if (o.empty()) continue;                // internal: the members that read it recompute it
         std::vector<std::string> vals = row_phase(m);
         body << loop_head << gen.body.str();
-        DT dt = m->type.dt;
+        DT dt = StoredDt(m);
+        for (auto& x : vals) x = StoreVal(m, dt, x);
         if (!vec) {
           for (int l = 0; l < 4; ++l)
-            body << "      " << (ok(l).empty() ? "" : "if (" + ok(l) + ") ") << o << "[" << elem_index(l) << "] = " << StoreExpr(dt, vals[l]) << ";\n";
+            body << "      " << (ok(l).empty() ? "" : "if (" + ok(l) + ") ") << o << "[" << elem_index(m, l) << "] = " << StoreExpr(dt, vals[l]) << ";\n";
         } else if (dt == DT::kF32) {
-          body << "      *(float4*)(" << o << " + " << elem_index(0) << ") = make_float4(" << vals[0] << ", " << vals[1] << ", " << vals[2] << ", " << vals[3] << ");\n";
+          body << "      *(float4*)(" << o << " + " << elem_index(m, 0) << ") = make_float4(" << vals[0] << ", " << vals[1] << ", " << vals[2] << ", " << vals[3] << ");\n";
         } else if (dt == DT::kBF16 || dt == DT::kF16) {
-          body << "      *(uint2*)(" << o << " + " << elem_index(0) << ") = make_uint2(" << Pack16(dt, vals[0], vals[1]) << ", " << Pack16(dt, vals[2], vals[3]) << ");\n";
+          body << "      *(uint2*)(" << o << " + " << elem_index(m, 0) << ") = make_uint2(" << Pack16(dt, vals[0], vals[1]) << ", " << Pack16(dt, vals[2], vals[3]) << ");\n";
         } else {
-          for (int l = 0; l < 4; ++l) body << "      " << o << "[" << elem_index(l) << "] = " << StoreExpr(dt, vals[l]) << ";\n";
+          for (int l = 0; l < 4; ++l) body << "      " << o << "[" << elem_index(m, l) << "] = " << StoreExpr(dt, vals[l]) << ";\n";
         }
         body << "    }\n";
       } else {
@@ -1440,7 +1532,7 @@ class Lowerer {
         gen.identity = gen.row_ident;
         std::string v = gen.Emit(m, gen.RowIndex(m->type.dims));
         body << gen.body.str() << "    const " << CType(m->type.dt) << " " << rk << " = " << v << ";\n";
-        if (!o.empty()) body << "    if (lt == 0) " << o << "[row] = " << StoreExpr(m->type.dt, rk) << ";\n";
+        if (!o.empty()) body << "    if (lt == 0) " << o << "[row] = " << StoreExpr(StoredDt(m), StoreVal(m, StoredDt(m), rk)) << ";\n";
         gen.fixed[m->id] = rk;
       }
     }
@@ -1707,7 +1799,7 @@ class Lowerer {
     int64_t R = 1;
     for (int k = 0; k < r; ++k)
       if (k != q && k != r - 1) { rest_dims.push_back(k); R *= od[k]; }
-    DT in_dt = v->type.dt;
+    DT in_dt = StoredDt(v);
     std::string fn = KName();
     std::ostringstream o;
     o << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const void* __restrict__ p0, void* __restrict__ q0) {\n"
@@ -1771,7 +1863,7 @@ class Lowerer {
     std::vector<std::string> sidx(v->type.rank());
     for (size_t k = 0; k < perm.size(); ++k) sidx[perm[k]] = names[k];
     std::string fn = KName();
-    DT in_dt = v->type.dt;
+    DT in_dt = StoredDt(v);
     std::string oidx = pitch == inner ? "i" : "(i / " + std::to_string(inner) + "LL) * " + std::to_string(pitch) +
                                                  "LL + i % " + std::to_string(inner) + "LL";
     src_ << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const void* __restrict__ p0, void* __restrict__ q0) {\n"
@@ -1813,7 +1905,7 @@ class Lowerer {
     g.M = prod(a, lf);
     g.N = prod(b, rf);
     g.K = prod(a, lc);
-    DT at = a->type.dt, bt = b->type.dt;
+    DT at = StoredDt(a), bt = StoredDt(b);
     if (!DTIsFloat(at) || !DTIsFloat(bt)) throw LowerError{"dot_general on non-float operands is not supported"};
     // Operand type of the GEMM: both f32 (or f64) -> f32 SIMT (the f32 precision bar); otherwise a
     // 16-bit type on the tensor cores.  A 16-bit operand times an f32 one (the cotangent of an f32
@@ -1828,33 +1920,57 @@ class Lowerer {
     g.ab = ab;
     g.out = r->type.dt;
     if (g.out != DT::kF32 && g.out != DT::kBF16 && g.out != DT::kF16) throw LowerError{"dot_general result type not supported"};
-    // TMA needs 16-byte row strides: a 16-bit operand with K % 8 != 0 is copied with a padded pitch
-    const int64_t pitch = (ab != DT::kF32 && g.K % 8 != 0) ? (g.K + 7) / 8 * 8 : 0;
-    g.lda = g.ldb = pitch ? pitch : g.K;
-    // A as [batch, M, K]: permutation lb + lf + lc of a's dims
-    auto operand = [&](const Value* v, std::vector<int64_t> order, DT want, const std::vector<int64_t>& shape3) {
-      std::vector<int> perm(order.begin(), order.end());
-      bool ident = true;
-      for (size_t k = 0; k < perm.size(); ++k) ident = ident && perm[k] == (int)k;
-      if (ident && v->type.dt == want && !pitch) return SlotFor(v);
+    // Each operand is used where it lies when its dims are [batch, rows, K] (K-major) or [batch, K,
+    // rows] (MN-major) in order; otherwise it is copied K-major.  The tensor cores read either form
+    // through TMA, which needs 16-byte row strides: rows % 8 == 0 for MN-major, and a 16-bit K-major
+    // copy with K % 8 != 0 gets a padded pitch.
+    const bool tc = ab != DT::kF32;
+    struct Opnd { int slot; bool mn; int64_t ld; };
+    auto identity = [](const std::vector<int64_t>& o) {
+      for (size_t k = 0; k < o.size(); ++k) if (o[k] != (int64_t)k) return false;
+      return true;
+    };
+    auto cat = [](std::vector<int64_t> x, const std::vector<int64_t>& y, const std::vector<int64_t>& z) {
+      x.insert(x.end(), y.begin(), y.end());
+      x.insert(x.end(), z.begin(), z.end());
+      return x;
+    };
+    auto operand = [&](const Value* v, const std::vector<int64_t>& bat, const std::vector<int64_t>& fr,
+                       const std::vector<int64_t>& ct, int64_t rows) -> Opnd {
+      const std::vector<int64_t> kord = cat(bat, fr, ct), mord = cat(bat, ct, fr);
+      const DT held = StoredDt(v);
+      if (const int64_t p = StoredPitch(v)) {      // stored with a padded pitch for exactly this use
+        const std::vector<int64_t> last{v->type.rank() - 1};
+        if (identity(kord) && ct == last) return {SlotFor(v), false, p};
+        if (identity(mord) && fr == last) return {SlotFor(v), true, p};
+        throw LowerError{"internal: padded operand used out of place"};
+      }
+      if (identity(kord) && held == ab && !(tc && g.K % 8)) return {SlotFor(v), false, g.K};
+      if (identity(mord) && (!tc || rows % 8 == 0) && !std::getenv("B200_GEMM_NO_MN")) {
+        if (held == ab) return {SlotFor(v), true, rows};
+        std::vector<int> same(v->type.rank());
+        for (int k = 0; k < v->type.rank(); ++k) same[k] = k;
+        return {EmitPermute(v, same, v->type.dims, ab), true, rows};   // convert only
+      }
+      const int64_t pitch = (tc && g.K % 8 != 0) ? (g.K + 7) / 8 * 8 : 0;
+      std::vector<int> perm(kord.begin(), kord.end());
       std::vector<int64_t> od;
       for (int q : perm) od.push_back(v->type.dims[q]);
-      (void)shape3;
-      return EmitPermute(v, perm, od, want, pitch);
+      return {EmitPermute(v, perm, od, ab, pitch), false, pitch ? pitch : g.K};
     };
-    std::vector<int64_t> aord = lb;
-    aord.insert(aord.end(), lf.begin(), lf.end());
-    aord.insert(aord.end(), lc.begin(), lc.end());
-    std::vector<int64_t> bord = rb;
-    bord.insert(bord.end(), rf.begin(), rf.end());
-    bord.insert(bord.end(), rc.begin(), rc.end());
-    g.a = operand(a, aord, ab, {});
-    g.b = operand(b, bord, ab, {});
+    Opnd oa = operand(a, lb, lf, lc, g.M), ob = operand(b, rb, rf, rc, g.N);
+    g.a = oa.slot;
+    g.a_mn = oa.mn;
+    g.lda = oa.ld;
+    g.b = ob.slot;
+    g.b_mn = ob.mn;
+    g.ldb = ob.ld;
     g.c = SlotFor(r);
     Step st;
     st.kind = StepKind::kGemm;
     st.gemm = g;
-    st.label = "gemm b" + std::to_string(g.batch) + " " + std::to_string(g.M) + "x" + std::to_string(g.N) + "x" + std::to_string(g.K);
+    st.label = "gemm b" + std::to_string(g.batch) + " " + std::to_string(g.M) + "x" + std::to_string(g.N) + "x" + std::to_string(g.K) +
+               (g.a_mn || g.b_mn ? std::string(" ") + (g.a_mn ? "m" : "k") + (g.b_mn ? "n" : "k") : "");
     p_->steps.push_back(st);
     RecordDt(g.c, g.out);
   }

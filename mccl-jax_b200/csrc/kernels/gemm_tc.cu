@@ -1,11 +1,13 @@
 // gemm_tc.cu — dot_general on the B200 tensor cores: C[b] = A[b] . B[b]^T with A[b] (M x K) and
-// B[b] (N x K) K-major (bf16 or f16), fp32 accumulation in TMEM, f32 / bf16 / f16 result.
+// B[b] (N x K), each stored K-major ([rows, K], K contiguous) or MN-major ([K, rows], rows
+// contiguous), bf16 or f16, fp32 accumulation in TMEM, f32 / bf16 / f16 result.
 //
 // This replaces the reference's MPSGraph matmul call (src/jam/ops/linalg.mm:98, reached from
 // DotGeneral linalg.mm:47-105 after its [batch, free, contract] canonicalisation).
 //
 // Design (one CTA per SM, persistent over output tiles of 128 x BN):
-//   warp 0     TMA producer: 128x64 A and BNx64 B tiles (128-byte swizzle) into a kStages ring;
+//   warp 0     TMA producer: 128x64 A and BNx64 B tiles (128-byte swizzle) into a kStages ring; an
+//              MN-major operand arrives as 64(MN) x 64(K) boxes, 8 KB apart (the descriptor's LBO);
 //   warp 1     allocates TMEM (2 x BN columns: double-buffered accumulator) and one thread issues
 //              tcgen05.mma (M=128, N=BN, K=16) x4 per stage, committing stage release / acc-ready;
 //   warps 2-5  epilogue: tcgen05.ld 32 lanes x 16 columns, convert, store; release the accumulator
@@ -48,8 +50,8 @@ __device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
   return r;
 }
 
-// OUT: 0 f32, 1 bf16, 2 f16
-template <int BN, int OUT>
+// OUT: 0 f32, 1 bf16, 2 f16; AMN / BMN: operand stored MN-major
+template <int BN, int OUT, bool AMN, bool BMN>
 __global__ void __launch_bounds__(192, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* __restrict__ C,
                int M, int N, int K, int batch, int fmt) {
@@ -101,8 +103,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (!mbar_wait(&empty[s], ph ^ 1, kErrTimeoutEmpty, &g_tc_error_gemm)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], CF::kStage);
           uint8_t* sa = smem + s * CF::kStage;
-          tma_load_3d(&tmA, &full[s], sa, kb * BK, m_blk * BM, b);
-          tma_load_3d(&tmB, &full[s], sa + CF::kABytes, kb * BK, n_blk * BN, b);
+          if (AMN) {
+#pragma unroll
+            for (int i = 0; i < BM / 64; ++i) tma_load_3d(&tmA, &full[s], sa + i * 8192, m_blk * BM + 64 * i, kb * BK, b);
+          } else {
+            tma_load_3d(&tmA, &full[s], sa, kb * BK, m_blk * BM, b);
+          }
+          if (BMN) {
+#pragma unroll
+            for (int i = 0; i < BN / 64; ++i)
+              tma_load_3d(&tmB, &full[s], sa + CF::kABytes + i * 8192, n_blk * BN + 64 * i, kb * BK, b);
+          } else {
+            tma_load_3d(&tmB, &full[s], sa + CF::kABytes, kb * BK, n_blk * BN, b);
+          }
           issued |= 1u << s;
           fill_par = (fill_par & ~(1u << s)) | (ph << s);
           if (++s == CF::kStages) { s = 0; ph ^= 1; }
@@ -114,7 +127,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(fmt, BM, BN);
+      const uint32_t idesc = idesc_f16(fmt, BM, BN, BMN, AMN);
       int s = 0;
       uint32_t ph = 0;
       int local = 0;
@@ -132,7 +145,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const uint32_t b_addr = a_addr + CF::kABytes;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            mma_f16_ss(d, sw128_desc(a_addr + k * 32), sw128_desc(b_addr + k * 32), idesc, (kb | k) != 0);
+            mma_f16_ss(d, AMN ? sw128_mn_desc_lbo(a_addr + k * 2048, 8192) : sw128_desc(a_addr + k * 32),
+                       BMN ? sw128_mn_desc_lbo(b_addr + k * 2048, 8192) : sw128_desc(b_addr + k * 32), idesc, (kb | k) != 0);
           mma_commit(&empty[s]);
           if (++s == CF::kStages) { s = 0; ph ^= 1; }
         }
@@ -217,17 +231,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 }
 
 // ---------------------------------------------------------------------------- SIMT fallback
-// fp32 (or any) inputs, K-major A[b] (M x K, row pitch lda) and B[b] (N x K, pitch ldb): 128x128
-// tiles, 8x8 outputs per thread.
-template <typename T, int OUT>
+// fp32 (or any) inputs, A[b] (M x K) and B[b] (N x K), each K-major (row pitch ld) or MN-major ([K,
+// rows], pitch ld): 128x128 tiles, 8x8 outputs per thread.
+template <typename T, int OUT, bool AMN, bool BMN>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A, const T* __restrict__ B, void* __restrict__ C,
                                                         int M, int N, int K, long long lda, long long ldb) {
   __shared__ float As[16][128 + 4];
   __shared__ float Bs[16][128 + 4];
   const int b = blockIdx.z;
   const int m0 = blockIdx.y * 128, n0 = blockIdx.x * 128;
-  const T* Ab = A + (long long)b * M * lda;
-  const T* Bb = B + (long long)b * N * ldb;
+  const T* Ab = A + (long long)b * (AMN ? K : M) * lda;
+  const T* Bb = B + (long long)b * (BMN ? K : N) * ldb;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   float acc[8][8];
 #pragma unroll
@@ -239,11 +253,16 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       int idx = threadIdx.x + e * 256;
-      int row = idx >> 4, kk = idx & 15;
-      int gk = k0 + kk;
-      int gm = m0 + row, gn = n0 + row;
-      As[kk][row] = (gm < M && gk < K) ? (float)Ab[(long long)gm * lda + gk] : 0.f;
-      Bs[kk][row] = (gn < N && gk < K) ? (float)Bb[(long long)gn * ldb + gk] : 0.f;
+      {
+        int row = AMN ? idx & 127 : idx >> 4, kk = AMN ? idx >> 7 : idx & 15;
+        int gk = k0 + kk, gm = m0 + row;
+        As[kk][row] = (gm < M && gk < K) ? (float)Ab[AMN ? (long long)gk * lda + gm : (long long)gm * lda + gk] : 0.f;
+      }
+      {
+        int row = BMN ? idx & 127 : idx >> 4, kk = BMN ? idx >> 7 : idx & 15;
+        int gk = k0 + kk, gn = n0 + row;
+        Bs[kk][row] = (gn < N && gk < K) ? (float)Bb[BMN ? (long long)gk * ldb + gn : (long long)gn * ldb + gk] : 0.f;
+      }
     }
     __syncthreads();
 #pragma unroll
@@ -300,6 +319,21 @@ bool MakeOperandMap(CUtensorMap* map, const void* ptr, int K, long long ld, int 
   return r == CUDA_SUCCESS;
 }
 
+// 3-D MN-major operand map: dims {rows, K, batch} with K-row pitch `ld` elements (ld * 2 % 16 == 0),
+// box {64, 64, 1} (64 MN elements = one 128-byte swizzle row, 64 k), 128-byte swizzle.
+bool MakeOperandMapMN(CUtensorMap* map, const void* ptr, int K, long long ld, int rows, int batch, bool f16like) {
+  EncodeTiledFn enc = GetEncodeTiled();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)rows, (cuuint64_t)K, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)ld * 2 * K};
+  cuuint32_t box[3] = {64, 64, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, f16like ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr),
+                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int NumSMs() {
   int dev = 0, n = 148;
   cudaGetDevice(&dev);
@@ -307,7 +341,7 @@ int NumSMs() {
   return n;
 }
 
-template <int BN, int OUT>
+template <int BN, int OUT, bool AMN, bool BMN>
 static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, void* C, int batch, int M, int N, int K,
                     int fmt, cudaStream_t st) {
   using CF = Cfg<BN>;
@@ -315,25 +349,44 @@ static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, 
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 7], [] {
-    cudaFuncSetAttribute(gemm_tc_kernel<BN, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kSmem);
+    cudaFuncSetAttribute(gemm_tc_kernel<BN, OUT, AMN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kSmem);
   });
   CUtensorMap ta, tb;
-  if (!MakeOperandMap(&ta, A, K, lda, M, batch, BM, fmt == 0) || !MakeOperandMap(&tb, B, K, ldb, N, batch, BN, fmt == 0))
-    return -2;
+  bool ok = AMN ? MakeOperandMapMN(&ta, A, K, lda, M, batch, fmt == 0) : MakeOperandMap(&ta, A, K, lda, M, batch, BM, fmt == 0);
+  ok = ok && (BMN ? MakeOperandMapMN(&tb, B, K, ldb, N, batch, fmt == 0) : MakeOperandMap(&tb, B, K, ldb, N, batch, BN, fmt == 0));
+  if (!ok) return -2;
   int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
   int grid = std::min(tiles, NumSMs());
-  gemm_tc_kernel<BN, OUT><<<grid, 192, CF::kSmem, st>>>(ta, tb, C, M, N, K, batch, fmt);
+  gemm_tc_kernel<BN, OUT, AMN, BMN><<<grid, 192, CF::kSmem, st>>>(ta, tb, C, M, N, K, batch, fmt);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+template <int BN, int OUT>
+static int LaunchTcMajor(bool amn, bool bmn, const void* A, long long lda, const void* B, long long ldb, void* C, int batch,
+                         int M, int N, int K, int fmt, cudaStream_t st) {
+  if (amn && bmn) return LaunchTc<BN, OUT, true, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st);
+  if (amn) return LaunchTc<BN, OUT, true, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st);
+  if (bmn) return LaunchTc<BN, OUT, false, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st);
+  return LaunchTc<BN, OUT, false, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st);
+}
+
+template <typename T, bool AMN, bool BMN>
+static int LaunchSimtT(const void* A, long long lda, const void* B, long long ldb, void* C, int batch, int M, int N, int K,
+                       int out, cudaStream_t st) {
+  dim3 grid((N + 127) / 128, (M + 127) / 128, batch);
+  if (out == 0) gemm_simt_kernel<T, 0, AMN, BMN><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K, lda, ldb);
+  else if (out == 1) gemm_simt_kernel<T, 1, AMN, BMN><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K, lda, ldb);
+  else gemm_simt_kernel<T, 2, AMN, BMN><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K, lda, ldb);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
 template <typename T>
-static int LaunchSimt(const void* A, long long lda, const void* B, long long ldb, void* C, int batch, int M, int N, int K,
-                      int out, cudaStream_t st) {
-  dim3 grid((N + 127) / 128, (M + 127) / 128, batch);
-  if (out == 0) gemm_simt_kernel<T, 0><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K, lda, ldb);
-  else if (out == 1) gemm_simt_kernel<T, 1><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K, lda, ldb);
-  else gemm_simt_kernel<T, 2><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K, lda, ldb);
-  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+static int LaunchSimt(bool amn, bool bmn, const void* A, long long lda, const void* B, long long ldb, void* C, int batch,
+                      int M, int N, int K, int out, cudaStream_t st) {
+  if (amn && bmn) return LaunchSimtT<T, true, true>(A, lda, B, ldb, C, batch, M, N, K, out, st);
+  if (amn) return LaunchSimtT<T, true, false>(A, lda, B, ldb, C, batch, M, N, K, out, st);
+  if (bmn) return LaunchSimtT<T, false, true>(A, lda, B, ldb, C, batch, M, N, K, out, st);
+  return LaunchSimtT<T, false, false>(A, lda, B, ldb, C, batch, M, N, K, out, st);
 }
 
 int TakeGemmError() {
@@ -343,11 +396,13 @@ int TakeGemmError() {
   return v;
 }
 
-// C[b] = A[b] . B[b]^T with row pitches lda / ldb (elements) for A [batch, M, >=K] and B [batch, N, >=K].
-int Gemm(const void* A, long long lda, const void* B, long long ldb, void* C, int64_t batch, int64_t M, int64_t N,
-         int64_t K, int ab_type, int out_type, cudaStream_t st) {
+// C[b] = A[b] . B[b]^T.  A is [batch, M, >=K] (K-major, row pitch lda) or, with a_mn, [batch, K, >=M]
+// (MN-major, pitch lda); B likewise with N, ldb and b_mn.
+int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C, int64_t batch, int64_t M,
+         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st) {
   if (batch <= 0 || M <= 0 || N <= 0) return 0;
-  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || batch > 65535 || lda < K || ldb < K) return -1;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || batch > 65535 || lda < (a_mn ? M : K) || ldb < (b_mn ? N : K))
+    return -1;
   int out = out_type == B200_DT_F32 ? 0 : out_type == B200_DT_BF16 ? 1 : out_type == B200_DT_F16 ? 2 : -1;
   if (out < 0) return -1;
   if (K == 0) {
@@ -360,14 +415,25 @@ int Gemm(const void* A, long long lda, const void* B, long long ldb, void* C, in
     int fmt = ab_type == B200_DT_BF16 ? 1 : 0;
     bool wide = N >= 256;
     int b = (int)batch, m = (int)M, n = (int)N, k = (int)K;
-    if (out == 0) return wide ? LaunchTc<256, 0>(A, lda, B, ldb, C, b, m, n, k, fmt, st) : LaunchTc<128, 0>(A, lda, B, ldb, C, b, m, n, k, fmt, st);
-    if (out == 1) return wide ? LaunchTc<256, 1>(A, lda, B, ldb, C, b, m, n, k, fmt, st) : LaunchTc<128, 1>(A, lda, B, ldb, C, b, m, n, k, fmt, st);
-    return wide ? LaunchTc<256, 2>(A, lda, B, ldb, C, b, m, n, k, fmt, st) : LaunchTc<128, 2>(A, lda, B, ldb, C, b, m, n, k, fmt, st);
+    if (out == 0)
+      return wide ? LaunchTcMajor<256, 0>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st)
+                  : LaunchTcMajor<128, 0>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st);
+    if (out == 1)
+      return wide ? LaunchTcMajor<256, 1>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st)
+                  : LaunchTcMajor<128, 1>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st);
+    return wide ? LaunchTcMajor<256, 2>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st)
+                : LaunchTcMajor<128, 2>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st);
   }
-  if (ab_type == B200_DT_F32) return LaunchSimt<float>(A, lda, B, ldb, C, batch, M, N, K, out, st);
-  if (ab_type == B200_DT_BF16) return LaunchSimt<__nv_bfloat16>(A, lda, B, ldb, C, batch, M, N, K, out, st);
-  if (ab_type == B200_DT_F16) return LaunchSimt<__half>(A, lda, B, ldb, C, batch, M, N, K, out, st);
+  int b = (int)batch, m = (int)M, n = (int)N, k = (int)K;
+  if (ab_type == B200_DT_F32) return LaunchSimt<float>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, out, st);
+  if (ab_type == B200_DT_BF16) return LaunchSimt<__nv_bfloat16>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, out, st);
+  if (ab_type == B200_DT_F16) return LaunchSimt<__half>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, out, st);
   return -1;
+}
+
+int Gemm(const void* A, long long lda, const void* B, long long ldb, void* C, int64_t batch, int64_t M, int64_t N,
+         int64_t K, int ab_type, int out_type, cudaStream_t st) {
+  return Gemm(A, lda, false, B, ldb, false, C, batch, M, N, K, ab_type, out_type, st);
 }
 
 }  // namespace b200k

@@ -166,11 +166,24 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
   return d;
 }
 
-// Instruction descriptor, kind::f16: f32 accumulate, A/B = bf16 (fmt 1) or f16 (fmt 0), both K-major
-// unless b_mn_major, M x N tile.
-__host__ __device__ constexpr uint32_t idesc_f16(int fmt, int M, int N, bool b_mn_major = false) {
-  return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) |
-         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// Shared-memory matrix descriptor for an MN-major operand in the 128-byte swizzle layout: each
+// 128-byte row holds 64 consecutive MN elements of one k; 8-row groups along K are SBO = 1024 B apart
+// and consecutive 64-element MN blocks are `lbo` bytes apart.
+__device__ __forceinline__ uint64_t sw128_mn_desc_lbo(uint32_t addr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16: f32 accumulate, A/B = bf16 (fmt 1) or f16 (fmt 0), K-major
+// unless a_mn_major / b_mn_major, M x N tile.
+__host__ __device__ constexpr uint32_t idesc_f16(int fmt, int M, int N, bool b_mn_major = false, bool a_mn_major = false) {
+  return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | ((a_mn_major ? 1u : 0u) << 15) |
+         ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 }  // namespace b200k

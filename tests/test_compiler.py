@@ -48,6 +48,32 @@ def test_gemm_and_batched_gemm_plans(lib_path):
     assert rc == 0 and "gemm b16 2048x2048x2048" in rep, rep
 
 
+def test_dot_reads_mn_major_operands_in_place(lib_path):
+    """x @ W with W [K, N] and x^T @ dy read their operands where they lie (no transpose step)."""
+    b = Builder("jit_mn")
+    x = b.arg((512, 256), "bf16")
+    w = b.arg((256, 384), "bf16")
+    dy = b.arg((512, 384), "bf16")
+    y = b.dot_general(x, w, contract=([1], [0]), out_dtype="f32")
+    dw = b.dot_general(x, dy, contract=([0], [0]), out_dtype="f32")
+    rc, rep = report(lib_path, b.text([y, dw]))
+    assert rc == 0, rep
+    assert "transpose" not in rep and "gemm b1 512x384x256 kn" in rep and "gemm b1 256x384x512 mn" in rep, rep
+
+
+def test_f32_dot_operand_is_stored_narrow_and_read_in_place(lib_path):
+    b = Builder("jit_cot")
+    x = b.arg((256, 96), "bf16")
+    w = b.arg((1001, 96), "bf16")
+    z = b.arg((256, 1001), "f32")
+    g = b.exp(z) - z
+    dx = b.dot_general(g, w, contract=([1], [0]), out_dtype="f32")
+    dw = b.dot_general(g, x, contract=([0], [0]), out_dtype="f32")
+    rc, rep = report(lib_path, b.text([dx, dw]))
+    assert rc == 0, rep
+    assert "transpose" not in rep and rep.count("gemm") == 2 and "loop" in rep, rep
+
+
 def test_psum_is_identity_on_one_rank_and_a_collective_on_many(lib_path):
     p = configs.psum_program(1024, 2, with_inputs=False)
     rc, rep = report(lib_path, p.text, nprocs=1)

@@ -109,6 +109,67 @@ def test_dot_mixed_precision_and_unaligned_shapes(client, K, N, out):
     assert_close(np.asarray(got, np.float32), np.asarray(ref, np.float32), 1e-2, "mixed dot")
 
 
+@pytest.mark.parametrize("lhs_c,rhs_c", [(1, 0), (0, 0), (1, 1), (0, 1)])
+@pytest.mark.parametrize("dtype,M,N,K", [("bf16", 384, 512, 320), ("bf16", 200, 136, 72), ("bf16", 90, 70, 50),
+                                         ("f32", 72, 40, 56)])
+def test_dot_operand_layouts(client, lhs_c, rhs_c, dtype, M, N, K):
+    """Each operand is read where it lies when it is [rows, K] (K-major) or [K, rows] (MN-major, rows
+    a multiple of 8); other layouts are copied.  All four contraction placements against the oracle."""
+    b = Builder("jit_layouts")
+    x = b.arg((M, K) if lhs_c == 1 else (K, M), dtype)
+    w = b.arg((N, K) if rhs_c == 1 else (K, N), dtype)
+    y = b.dot_general(x, w, contract=([lhs_c], [rhs_c]), out_dtype="f32")
+    text = b.text([y])
+    rng = np.random.default_rng(M * 7 + N + lhs_c * 2 + rhs_c)
+    npdt = ml_dtypes.bfloat16 if dtype == "bf16" else np.float32
+    ins = [(rng.standard_normal(x.shape) / np.sqrt(K)).astype(npdt), rng.standard_normal(w.shape).astype(npdt)]
+    got = client.run(text, ins)[0]
+    ref = oracle_run(text, ins)[0]
+    assert_close(got, ref, RTOL_F32 if dtype == "f32" else RTOL_F32 * 10, "dot layouts")
+
+
+@pytest.mark.parametrize("V", [1001, 1000, 1024])
+def test_f32_cotangent_feeding_two_dots(client, V):
+    """An f32 value read only by dots with bf16 partners (the logits cotangent of an LM head) is stored
+    rounded to bf16, with a padded row pitch when V % 8 != 0, and both dots (dX = g W^T, dW = x^T g)
+    read it in place."""
+    b = Builder("jit_cotangent")
+    x = b.arg((256, 96), "bf16")
+    w = b.arg((V, 96), "bf16")
+    z = b.arg((256, V), "f32")
+    g = b.exp(z) * 0.5 - z                       # f32 [256, V], produced by a loop kernel
+    dx = b.dot_general(g, w, contract=([1], [0]), out_dtype="f32")
+    dw = b.dot_general(g, x, contract=([0], [0]), out_dtype="f32")
+    text = b.text([dx, dw])
+    rng = np.random.default_rng(V)
+    ins = [(rng.standard_normal((256, 96)) * 0.3).astype(ml_dtypes.bfloat16),
+           (rng.standard_normal((V, 96)) * 0.3).astype(ml_dtypes.bfloat16),
+           (rng.standard_normal((256, V)) * 0.5).astype(np.float32)]
+    outs = client.run(text, ins)
+    refs = oracle_run(text, ins)
+    for o, r, name in zip(outs, refs, ("dx", "dw")):
+        assert_close(o, r, 1e-2, name)
+
+
+@pytest.mark.parametrize("mn", [True, False])
+def test_batched_dot_mn_major_operands(client, mn, monkeypatch):
+    """Batched A^T B with both operands MN-major ([b, K, M] and [b, K, N]) against the oracle, and the
+    same program with MN-major reads disabled (operands copied K-major)."""
+    if not mn:
+        monkeypatch.setenv("B200_GEMM_NO_MN", "1")
+    b = Builder("jit_bmn")
+    x = b.arg((6, 192, 136), "bf16")
+    w = b.arg((6, 192, 264), "bf16")
+    y = b.dot_general(x, w, batch=([0], [0]), contract=([1], [1]), out_dtype="f32")
+    text = b.text([y])
+    rng = np.random.default_rng(5)
+    ins = [(rng.standard_normal((6, 192, 136)) / 14).astype(ml_dtypes.bfloat16),
+           rng.standard_normal((6, 192, 264)).astype(ml_dtypes.bfloat16)]
+    got = client.run(text, ins)[0]
+    ref = oracle_run(text, ins)[0]
+    assert_close(got, ref, RTOL_F32 * 10, "batched mn dot")
+
+
 def test_psum_single_rank_known_answer(client):
     """smoke.cc:24-40: one rank, all-reduce of [1,2,3,4] is the identity."""
     p = configs.psum_program(4, 1, with_inputs=False)
