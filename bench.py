@@ -215,7 +215,8 @@ def main():
                     help="attention (headline); dp = GPT-2 DP train step; gemm = dot_general sweep; fused = HBM-bound chains; "
                          "psum = all_reduce bandwidth sweep")
     ap.add_argument("--layers", type=int, default=12, help="dp: decoder layers")
-    ap.add_argument("--only", default="", help="fused: run only the chains whose name contains this text")
+    ap.add_argument("--only", default="", help="fused: run only the chains whose name contains this text; "
+                                               "gemm: run only one size, e.g. b1-8192-bf16")
     a = ap.parse_args()
     HEAD.update(B=a.B, H=a.H, S=a.S, causal=a.causal)
     a.warmup = max(a.warmup, 3)

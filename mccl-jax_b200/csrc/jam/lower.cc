@@ -150,6 +150,8 @@ __device__ __forceinline__ float h2f(unsigned short h) {
 __device__ __forceinline__ unsigned short f2h(float f) {
   unsigned short r; asm("cvt.rn.f16.f32 %0, %1;" : "=h"(r) : "f"(f)); return r; }
 __device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
+__device__ __forceinline__ float fmax_nan(float a, float b) { float r; asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b)); return r; }
+__device__ __forceinline__ float ex2a(float x) { float r; asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
 __device__ __forceinline__ unsigned short bf_bits(float f) { return (unsigned short)(__float_as_uint(f) >> 16); }
 __device__ __forceinline__ float rhf(float f) { return h2f(f2h(f)); }
 __device__ __forceinline__ float fmax_n(float a, float b) { return (a != a || b != b) ? __int_as_float(0x7fc00000) : fmaxf(a, b); }
@@ -1223,7 +1225,7 @@ class Lowerer {
       }
     }
     src_ << "}\n";
-    src_ << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "("
+    src_ << "extern \"C\" __global__ void __launch_bounds__(256, 4) " << fn << "("
          << KernelParams(gen.in_slots, (int)out_slots.size(), false) << ") {\n"
          << ParamCasts(gen.in_slots, in_dts, out_dts)
          << "  const long long st = (long long)gridDim.x * 256;\n"
@@ -1438,17 +1440,21 @@ class Lowerer {
         const std::string k1 = std::to_string(k), kk = std::to_string(k2);
         const std::string mx = "mx" + k1, s = "sx" + k1, bad = "bad" + k1, NINF = "(-__int_as_float(0x7f800000))";
         std::vector<std::string> vals = row_phase(op->operands[0]);
-        body << "    float " << mx << " = " << NINF << ", " << s << " = 0.f;\n    int " << bad << " = 0;\n"
+        body << "    float " << mx << " = " << NINF << ", " << s << " = 0.f, nmx" << k1 << " = " << NINF << ";\n    int " << bad << " = 0;\n"
              << loop_head << gen.body.str();
         body << "      {\n";
         for (int l = 0; l < 4; ++l)
           body << "        const float c" << l << " = " << (ok(l).empty() ? vals[l] : ok(l) + " ? " + vals[l] + " : " + NINF) << ";\n";
-        body << "        " << bad << " |= (c0 != c0) | (c1 != c1) | (c2 != c2) | (c3 != c3);\n"
+        // exp(d) as 2^(d log2 e) on the SFU: d = c_l - mx is formed first so the scaling only rounds
+        // the (small) exponent; NaN inputs are seen by a NaN-propagating max kept beside mx
+        const std::string nmx = "nmx" + k1;
+        body << "        " << nmx << " = fmax_nan(" << nmx << ", fmax_nan(fmax_nan(c0, c1), fmax_nan(c2, c3)));\n"
              << "        const float c = fmaxf(fmaxf(c0, c1), fmaxf(c2, c3));\n"
-             << "        if (c > " << mx << ") { " << s << " *= expf(" << mx << " - c); " << mx << " = c; }\n"
-             << "        if (" << mx << " > " << NINF << ") " << s << " += (expf(c0 - " << mx << ") + expf(c1 - " << mx
-             << ")) + (expf(c2 - " << mx << ") + expf(c3 - " << mx << "));\n      }\n";
-        body << "    }\n";
+             << "        if (c > " << mx << ") { " << s << " *= ex2a((" << mx << " - c) * 1.4426950408889634f); " << mx << " = c; }\n"
+             << "        if (" << mx << " > " << NINF << ") " << s << " += (ex2a((c0 - " << mx << ") * 1.4426950408889634f) + ex2a((c1 - " << mx
+             << ") * 1.4426950408889634f)) + (ex2a((c2 - " << mx << ") * 1.4426950408889634f) + ex2a((c3 - " << mx
+             << ") * 1.4426950408889634f));\n      }\n";
+        body << "    }\n    " << bad << " = nmx" << k1 << " != nmx" << k1 << ";\n";
         auto merge = [&](const std::string& om, const std::string& os) {
           return "{ const float nm = fmaxf(" + mx + ", " + om + "); " + s + " = (" + mx + " == " + NINF + " ? 0.f : " + s +
                  " * expf(" + mx + " - nm)) + (" + om + " == " + NINF + " ? 0.f : " + os + " * expf(" + om + " - nm)); " + mx +
@@ -1548,7 +1554,7 @@ class Lowerer {
     for (int s : gen.in_slots) in_dts.push_back(SlotDt(s));
     std::string fn = KName();
     const int threads = block_mode ? 512 : 256;
-    src_ << "extern \"C\" __global__ void __launch_bounds__(" << threads << ") " << fn << "("
+    src_ << "extern \"C\" __global__ void __launch_bounds__(" << threads << ", " << (block_mode ? 2 : 4) << ") " << fn << "("
          << KernelParams(gen.in_slots, (int)out_slots.size(), false) << ") {\n"
          << ParamCasts(gen.in_slots, in_dts, out_dts);
     for (const auto& s : shared) src_ << "  __shared__ " << s.first << " " << s.second << "[32];\n";

@@ -50,6 +50,18 @@ __device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
   return r;
 }
 
+// Output tile order within a batch: bands of kGroupM row blocks, column-major inside a band.  The
+// CTAs working at the same time (consecutive tile indices) then share a few A row blocks and B
+// column blocks, which stay in L2, instead of streaming all of A once per B column block.
+constexpr int kGroupM = 16;
+__device__ __forceinline__ void tile_coords(int r, int mb, int nb, int* m_blk, int* n_blk) {
+  const int band = r / (kGroupM * nb), first = band * kGroupM;
+  const int rows = min(mb - first, kGroupM);
+  const int q = r - band * kGroupM * nb;
+  *m_blk = first + q % rows;
+  *n_blk = q / rows;
+}
+
 // OUT: 0 f32, 1 bf16, 2 f16; AMN / BMN: operand stored MN-major
 template <int BN, int OUT, bool AMN, bool BMN>
 __global__ void __launch_bounds__(192, 1)
@@ -98,7 +110,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         const int b = t / per_batch, r = t % per_batch;
-        const int m_blk = r % mb, n_blk = r / mb;
+        int m_blk, n_blk;
+        tile_coords(r, mb, nb, &m_blk, &n_blk);
         for (int kb = 0; kb < kbs; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, kErrTimeoutEmpty, &g_tc_error_gemm)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], CF::kStage);
@@ -163,7 +176,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (!mbar_wait_warp(&acc_full[a], aph, kErrTimeoutAcc, &g_tc_error_gemm)) break;
       tc_fence_after();
       const int b = t / per_batch, r = t % per_batch;
-      const int m_blk = r % mb, n_blk = r / mb;
+      int m_blk, n_blk;
+      tile_coords(r, mb, nb, &m_blk, &n_blk);
       const int row = m_blk * BM + row_in_tile;
       const uint32_t taddr = tmem_base + a * BN + ((uint32_t)(q * 32) << 16);
       const long long crow = ((long long)b * M + row) * (long long)N;
