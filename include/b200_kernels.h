@@ -42,6 +42,25 @@ B200_API int b200_gemm(const void* A, const void* B, void* C, int64_t batch, int
 B200_API int b200_attention_fwd(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D,
                        int causal, float scale, void* stream);
 
+/* b200_attention_fwd that also writes lse2 [B, H, S] (f32): per query row, log2 of sum_j
+ * 2^(scale * log2(e) * s_j) over the keys it sees, which the backward uses to recompute P.
+ * Replaces: the forward half of the same chain when its intermediates feed a backward pass
+ * (reference: softmax and dot_general VJPs as separate MPSGraph ops, src/jam/ops/linalg.mm:47-105,
+ * src/jam/ops/elementwise.mm:71-123). */
+B200_API int b200_attention_fwd_lse(const void* q, const void* k, const void* v, void* o, float* lse2, int B, int H,
+                                    int S, int D, int causal, float scale, void* stream);
+
+/* dQ, dK, dV of O = softmax(scale * Q K^T [causal]) V from Q, K, V, O, dO (bf16 [B, H, S, D]) and
+ * the forward's lse2, D = 64, S a multiple of 128.  Scores are recomputed per 128 x 128 tile on
+ * tcgen05; dQ accumulates in the caller's f32 scratch dq_acc [B, H, S, D]; delta [B, H, S] f32 is
+ * scratch too.  Allocates nothing.
+ * Replaces: the VJP of the attention chain, which the reference runs as the transposed
+ * dot_generals (src/jam/ops/linalg.mm:47-105) and the elementwise softmax VJP ops
+ * (src/jam/ops/elementwise.mm:91-191, src/jam/ops/reduce.mm:45-109) over full S x S tensors. */
+B200_API int b200_attention_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                                const float* lse2, void* dq, void* dk, void* dv, float* dq_acc, float* delta, int B,
+                                int H, int S, int D, int causal, float scale, void* stream);
+
 /* The same attention with V first transposed into the caller's scratch `vt` (B*H*S*D bf16 elements)
  * and consumed K-major: an independent operand layout for cross-checking b200_attention_fwd.
  * No counterpart in the reference. */

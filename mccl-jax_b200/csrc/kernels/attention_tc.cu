@@ -129,7 +129,8 @@ enum { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9,
 template <int D, bool CAUSAL, bool VT>
 __global__ void __launch_bounds__(320, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int H, int S, float scale_log2) {
+                const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, float* __restrict__ lse2, int H,
+                int S, float scale_log2) {
   using C = ACfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -365,6 +366,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         *(uint4*)(orow + c) = w0;
         *(uint4*)(orow + c + 8) = w1;
       }
+      // log2-sum-exp of the scaled row (the backward recomputes P = 2^(s * scale_log2 - lse2))
+      if (lse2) lse2[row_base + qrow] = l > 0.f ? (m_use == -INFINITY ? 0.f : m_use) + log2f(l) : -INFINITY;
     }
   }
   tc_fence_before();
@@ -413,7 +416,8 @@ static bool Map2D(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t ou
 }
 
 template <int D, bool CAUSAL, bool VT>
-static int LaunchAttn(const void* q, const void* k, const void* v, void* o, int B, int H, int S, float scale, cudaStream_t st) {
+static int LaunchAttn(const void* q, const void* k, const void* v, void* o, int B, int H, int S, float scale, cudaStream_t st,
+                      float* lse2 = nullptr) {
   using Cf = ACfg<D>;
   static std::once_flag once[8];
   int dev = 0;
@@ -431,7 +435,7 @@ static int LaunchAttn(const void* q, const void* k, const void* v, void* o, int 
   }
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid((unsigned)(B * H * (S / (2 * TQ))));
-  attn_fwd_kernel<D, CAUSAL, VT><<<grid, 320, Cf::kSmem, st>>>(mq, mk, mv, (__nv_bfloat16*)o, H, S, scale_log2);
+  attn_fwd_kernel<D, CAUSAL, VT><<<grid, 320, Cf::kSmem, st>>>(mq, mk, mv, (__nv_bfloat16*)o, lse2, H, S, scale_log2);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -446,6 +450,15 @@ int AttentionFwd(const void* q, const void* k, const void* v, void* o, int B, in
   if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)o) % 16) return -1;
   if (causal) return LaunchAttn<64, true, false>(q, k, v, o, B, H, S, scale, st);
   return LaunchAttn<64, false, false>(q, k, v, o, B, H, S, scale, st);
+}
+
+// Training form: also writes lse2[B*H*S] (f32, log2 units of the scaled scores) for the backward.
+int AttentionFwdLse(const void* q, const void* k, const void* v, void* o, float* lse2, int B, int H, int S, int D,
+                    int causal, float scale, cudaStream_t st) {
+  if (!AttentionShapeOk(B, H, S, D)) return -1;
+  if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)o | (uintptr_t)lse2) % 16) return -1;
+  if (causal) return LaunchAttn<64, true, false>(q, k, v, o, B, H, S, scale, st, lse2);
+  return LaunchAttn<64, false, false>(q, k, v, o, B, H, S, scale, st, lse2);
 }
 
 // Cross-check variant: V transposed into `vt` (B*H*S*D bf16 scratch) and read K-major.
@@ -472,6 +485,12 @@ extern "C" int b200_attention_fwd(const void* q, const void* k, const void* v, v
                                   int causal, float scale, void* stream) {
   if (B == 0 || H == 0 || S == 0) return 0;
   return b200k::AttentionFwd(q, k, v, o, B, H, S, D, causal, scale, (cudaStream_t)stream);
+}
+
+extern "C" int b200_attention_fwd_lse(const void* q, const void* k, const void* v, void* o, float* lse2, int B, int H,
+                                      int S, int D, int causal, float scale, void* stream) {
+  if (B == 0 || H == 0 || S == 0) return 0;
+  return b200k::AttentionFwdLse(q, k, v, o, lse2, B, H, S, D, causal, scale, (cudaStream_t)stream);
 }
 
 extern "C" int b200_attention_fwd_vt(const void* q, const void* k, const void* v, void* vt, void* o, int B, int H, int S,

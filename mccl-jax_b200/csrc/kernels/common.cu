@@ -31,6 +31,7 @@ EncodeTiledFn GetEncodeTiled() {
 
 int TakeGemmError();
 int TakeAttnError();
+int TakeAttnBwdError();
 
 template <typename T, typename I>
 __global__ void __launch_bounds__(256) scatter_add_rows_kernel(const I* __restrict__ idx, const T* __restrict__ upd, T* __restrict__ out,
@@ -50,7 +51,8 @@ extern "C" int b200_take_device_error(void) {
   cudaDeviceSynchronize();
   int e = b200k::TakeGemmError();
   int a = b200k::TakeAttnError();
-  return e ? e : a;
+  int b = b200k::TakeAttnBwdError();
+  return e ? e : a ? a : b;
 }
 
 extern "C" int b200_scatter_add_rows(const void* idx, const void* upd, void* out, int64_t n_upd, int64_t row_len,

@@ -135,3 +135,47 @@ def test_scatter_add_rows(lib, cuda, dtype):
     keep = (idx >= 0) & (idx < rows)
     ref.index_add_(0, idx[keep].long(), upd[keep].double())
     assert rel_err(out.float().cpu().numpy(), ref.cpu().numpy()) <= (RTOL_F32 * 10 if dtype == F32 else RTOL_BF16)
+
+
+def _attention_ref(torch, q, k, v, do, causal, scale):
+    """fp32 autograd reference: O, log2-sum-exp of the scaled scores, dQ, dK, dV."""
+    qf, kf, vf = (t.float().requires_grad_(True) for t in (q, k, v))
+    s = (qf @ kf.transpose(-1, -2)) * scale
+    if causal:
+        S = q.shape[2]
+        mask = torch.ones(S, S, device="cuda", dtype=torch.bool).tril()
+        s = s.masked_fill(~mask, float("-inf"))
+    lse2 = torch.logsumexp(s, -1) / np.log(2.0)
+    o = torch.softmax(s, -1) @ vf
+    o.backward(do.float())
+    return o.detach(), lse2.detach(), qf.grad, kf.grad, vf.grad
+
+
+@pytest.mark.parametrize("B,H,S,causal", [(1, 2, 256, True), (2, 3, 512, False), (2, 2, 1024, True), (1, 1, 256, False)])
+def test_attention_backward_vs_autograd(lib, cuda, B, H, S, causal):
+    """Forward with lse2 output, then dQ, dK, dV from the backward kernel (recomputed scores, atomics
+    into an f32 dQ accumulator), against fp32 autograd of the same attention."""
+    torch = cuda
+    lib.b200_attention_fwd_lse.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_void_p]
+    lib.b200_attention_bwd.argtypes = [ctypes.c_void_p] * 11 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_void_p]
+    g = torch.Generator(device="cuda").manual_seed(S + B + H + causal)
+    q, k, v, do = (torch.randn(B, H, S, 64, device="cuda", generator=g).to(torch.bfloat16) for _ in range(4))
+    scale = 0.125
+    o = torch.empty_like(q)
+    lse2 = torch.empty(B, H, S, device="cuda")
+    assert lib.b200_attention_fwd_lse(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse2.data_ptr(),
+                                      B, H, S, 64, int(causal), scale, stream(torch)) == 0
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
+    dq_acc = torch.empty(B, H, S, 64, device="cuda")
+    delta = torch.empty(B, H, S, device="cuda")
+    assert lib.b200_attention_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), lse2.data_ptr(),
+                                  dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dq_acc.data_ptr(), delta.data_ptr(),
+                                  B, H, S, 64, int(causal), scale, stream(torch)) == 0
+    torch.cuda.synchronize()
+    check_device_error(lib)
+    ro, rl, rdq, rdk, rdv = _attention_ref(torch, q, k, v, do, causal, scale)
+    assert rel_err(o.float().cpu().numpy(), ro.cpu().numpy()) <= RTOL_BF16
+    np.testing.assert_allclose(lse2.cpu().numpy(), rl.cpu().numpy(), rtol=1e-4, atol=1e-3)
+    for got, ref, name in ((dq, rdq, "dq"), (dk, rdk, "dk"), (dv, rdv, "dv")):
+        e = rel_err(got.float().cpu().numpy(), ref.cpu().numpy())
+        assert e <= RTOL_BF16, (name, e)
