@@ -15,6 +15,7 @@
 #include <cmath>
 #include <cstring>
 #include <functional>
+#include <map>
 #include <set>
 #include <sstream>
 #include <unordered_map>
@@ -772,118 +773,388 @@ class Lowerer {
   }
   bool SingleUse(const Value* v) const { return v->users.size() == 1; }
 
+  // The forward chain ending at d2 = dot(P', V).  strict: every intermediate has the single use the
+  // inference form gives it (the chain can simply disappear); otherwise intermediates may also feed
+  // a backward pass, which MatchAttentionTraining accounts for.
+  struct FwdChain {
+    const Value *Q = nullptr, *K = nullptr, *V = nullptr, *S = nullptr, *x = nullptr, *P = nullptr, *P16 = nullptr;
+    std::vector<const Op*> ops;   // the chain's ops other than d2
+    bool causal = false;
+    double scale = 1.0;
+  };
+  bool MatchFwdChain(const Op* d2, bool strict, FwdChain* fc) const {
+    auto ints = [&](const Op* o, const char* k) {
+      auto it = o->ints.find(k);
+      return it == o->ints.end() ? std::vector<int64_t>{} : it->second;
+    };
+    auto single = [&](const Value* v) { return !strict || SingleUse(v); };
+    if (d2->name != "dot_general" || d2->operands.size() != 2) return false;
+    const std::vector<int64_t> b01 = {0, 1};
+    if (ints(d2, "batching_dims.lhs") != b01 || ints(d2, "batching_dims.rhs") != b01) return false;
+    if (ints(d2, "contracting_dims.lhs") != std::vector<int64_t>{3} || ints(d2, "contracting_dims.rhs") != std::vector<int64_t>{2})
+      return false;
+    std::vector<const Op*> chain;
+    const Value* p = d2->operands[0];
+    const Value* V = d2->operands[1];
+    fc->P16 = p;
+    if (p->def && p->def->name == "convert") {
+      chain.push_back(p->def);
+      if (!single(p)) return false;
+      p = p->def->operands[0];
+    }
+    fc->P = p;
+    if (!p->def || p->def->name != "divide" || !single(p)) return false;
+    const Op* div = p->def;
+    chain.push_back(div);
+    const Value* e = div->operands[0];
+    const Value* sumb = div->operands[1];
+    if (!e->def || e->def->name != "exponential") return false;
+    // sum = reduce_add(e, dims=[3]) seen through reshapes/broadcasts
+    const Value* sum = RowBroadcastOf(sumb);
+    if (!sum || !sum->def || sum->def->name != "reduce" || sum->def->reduce != ReduceKind::kAdd) return false;
+    if (sum->def->operands[0] != e || ints(sum->def, "dimensions") != std::vector<int64_t>{3}) return false;
+    if (strict && e->users.size() != 2) return false;
+    chain.push_back(e->def);
+    chain.push_back(sum->def);
+    for (const Value* y = sumb; y != sum; y = y->def->operands[0]) {
+      if (strict && y->users.size() != 1) return false;
+      chain.push_back(y->def);
+    }
+    const Value* sub = e->def->operands[0];
+    if (!sub->def || sub->def->name != "subtract" || !single(sub)) return false;
+    chain.push_back(sub->def);
+    const Value* x = sub->def->operands[0];
+    const Value* maxb = sub->def->operands[1];
+    const Value* mx = RowBroadcastOf(maxb);
+    if (!mx || !mx->def || mx->def->name != "reduce" || mx->def->reduce != ReduceKind::kMax) return false;
+    if (mx->def->operands[0] != x || ints(mx->def, "dimensions") != std::vector<int64_t>{3}) return false;
+    if (strict && x->users.size() != 2) return false;
+    chain.push_back(mx->def);
+    for (const Value* y = maxb; y != mx; y = y->def->operands[0]) {
+      if (strict && y->users.size() != 1) return false;
+      chain.push_back(y->def);
+    }
+    fc->x = x;
+    const Value* s = x;
+    if (s->def && s->def->name == "select") {
+      // select(broadcast(compare(iota0 GE iota1)), s, -inf)
+      const Op* sel = s->def;
+      double ninf;
+      if (!IsScalarConst(sel->operands[2], &ninf) || !(std::isinf(ninf) && ninf < 0)) return false;
+      const Value* m = Through(sel->operands[0]);
+      if (m->def && m->def->name == "broadcast_in_dim") m = m->def->operands[0];
+      if (!m->def || m->def->name != "compare") return false;
+      const Op* cmp = m->def;
+      auto iota_dim = [](const Value* v) -> int {
+        while (v->def && v->def->name == "broadcast_in_dim") v = v->def->operands[0];
+        return (v->def && v->def->name == "iota") ? (int)v->def->ints.at("dim")[0] : -1;
+      };
+      std::string dir = cmp->strs.at("comparison_direction");
+      int li = iota_dim(cmp->operands[0]), ri = iota_dim(cmp->operands[1]);
+      if (!((dir == "GE" && li == 0 && ri == 1) || (dir == "LE" && li == 1 && ri == 0))) return false;
+      if (m->type.rank() != 2) return false;
+      fc->causal = true;
+      chain.push_back(sel);
+      s = sel->operands[1];
+      if (!single(s)) return false;
+    }
+    if (s->def && s->def->name == "multiply") {
+      double c;
+      const Op* mul = s->def;
+      const Value* other = nullptr;
+      if (IsScalarConst(mul->operands[1], &c)) other = mul->operands[0];
+      else if (IsScalarConst(mul->operands[0], &c)) other = mul->operands[1];
+      if (!other || (s != x && !single(s))) return false;
+      fc->scale = c;
+      chain.push_back(mul);
+      s = other;
+    }
+    if (!s->def || s->def->name != "dot_general" || (s != x && !single(s))) return false;
+    const Op* d1 = s->def;
+    if (ints(d1, "batching_dims.lhs") != b01 || ints(d1, "batching_dims.rhs") != b01 ||
+        ints(d1, "contracting_dims.lhs") != std::vector<int64_t>{3} || ints(d1, "contracting_dims.rhs") != std::vector<int64_t>{3})
+      return false;
+    const Value* Q = d1->operands[0];
+    const Value* K = d1->operands[1];
+    if (Q->type.dt != DT::kBF16 || K->type.dt != DT::kBF16 || V->type.dt != DT::kBF16) return false;
+    if (d2->result()->type.dt != DT::kBF16) return false;
+    if (!(Q->type.dims == K->type.dims && Q->type.dims == V->type.dims)) return false;
+    if (s->type.dt != DT::kF32) return false;
+    const int Dh = (int)Q->type.dims[3];
+    if (Dh != 64 || Q->type.dims[2] % 256 != 0 || fc->scale <= 0) return false;
+    chain.push_back(d1);
+    fc->Q = Q;
+    fc->K = K;
+    fc->V = V;
+    fc->S = s;
+    fc->ops = chain;
+    return true;
+  }
+
+  void RegisterAttention(const Op* d2, const FwdChain& fc) {
+    AttentionStep a;
+    a.B = (int)fc.Q->type.dims[0];
+    a.H = (int)fc.Q->type.dims[1];
+    a.S = (int)fc.Q->type.dims[2];
+    a.D = (int)fc.Q->type.dims[3];
+    a.causal = fc.causal;
+    a.scale = (float)fc.scale;
+    attn_[d2->result()->id] = a;
+    attn_in_[d2->result()->id] = {fc.Q, fc.K, fc.V};
+    for (const Op* o : fc.ops) dead_[o->index] = true;
+  }
+
   void MatchAttention() {
     for (auto& opp : g_.ops) {
-      Op* d2 = opp.get();
-      if (d2->name != "dot_general" || d2->operands.size() != 2) continue;
-      auto ints = [&](const Op* o, const char* k) {
-        auto it = o->ints.find(k);
-        return it == o->ints.end() ? std::vector<int64_t>{} : it->second;
-      };
-      const std::vector<int64_t> b01 = {0, 1};
-      if (ints(d2, "batching_dims.lhs") != b01 || ints(d2, "batching_dims.rhs") != b01) continue;
-      if (ints(d2, "contracting_dims.lhs") != std::vector<int64_t>{3} ||
-          ints(d2, "contracting_dims.rhs") != std::vector<int64_t>{2})
-        continue;
-      std::vector<const Op*> chain{d2};
-      const Value* p = d2->operands[0];
-      const Value* V = d2->operands[1];
-      if (p->def && p->def->name == "convert") { chain.push_back(p->def); if (!SingleUse(p)) continue; p = p->def->operands[0]; }
-      if (!p->def || p->def->name != "divide" || !SingleUse(p)) continue;
-      const Op* div = p->def;
-      chain.push_back(div);
-      const Value* e = div->operands[0];
-      const Value* sumb = div->operands[1];
-      if (!e->def || e->def->name != "exponential") continue;
-      // sum = reduce_add(e, dims=[3]) seen through reshapes/broadcasts
-      const Value* sum = RowBroadcastOf(sumb);
-      if (!sum || !sum->def || sum->def->name != "reduce" || sum->def->reduce != ReduceKind::kAdd) continue;
-      if (sum->def->operands[0] != e || ints(sum->def, "dimensions") != std::vector<int64_t>{3}) continue;
-      if (e->users.size() != 2) continue;
-      chain.push_back(e->def);
-      chain.push_back(sum->def);
-      for (const Value* x = sumb; x != sum; x = x->def->operands[0]) { if (x->users.size() != 1) goto next; chain.push_back(x->def); }
-      {
-        const Value* sub = e->def->operands[0];
-        if (!sub->def || sub->def->name != "subtract" || !SingleUse(sub)) continue;
-        chain.push_back(sub->def);
-        const Value* x = sub->def->operands[0];
-        const Value* maxb = sub->def->operands[1];
-        const Value* mx = RowBroadcastOf(maxb);
-        if (!mx || !mx->def || mx->def->name != "reduce" || mx->def->reduce != ReduceKind::kMax) continue;
-        if (mx->def->operands[0] != x || ints(mx->def, "dimensions") != std::vector<int64_t>{3}) continue;
-        if (x->users.size() != 2) continue;
-        chain.push_back(mx->def);
-        for (const Value* y = maxb; y != mx; y = y->def->operands[0]) { if (y->users.size() != 1) goto next; chain.push_back(y->def); }
-        bool causal = false;
-        double scale = 1.0;
-        const Value* s = x;
-        if (s->def && s->def->name == "select") {
-          // select(broadcast(compare(iota0 GE iota1)), s, -inf)
-          const Op* sel = s->def;
-          double ninf;
-          if (!IsScalarConst(sel->operands[2], &ninf) || !(std::isinf(ninf) && ninf < 0)) continue;
-          const Value* m = Through(sel->operands[0]);
-          if (m->def && m->def->name == "broadcast_in_dim") m = m->def->operands[0];
-          if (!m->def || m->def->name != "compare") continue;
-          const Op* cmp = m->def;
-          const Value* l = cmp->operands[0];
-          const Value* r = cmp->operands[1];
-          auto iota_dim = [](const Value* v) -> int {
-            while (v->def && v->def->name == "broadcast_in_dim") v = v->def->operands[0];
-            return (v->def && v->def->name == "iota") ? (int)v->def->ints.at("dim")[0] : -1;
-          };
-          std::string dir = cmp->strs.at("comparison_direction");
-          int li = iota_dim(l), ri = iota_dim(r);
-          if (!((dir == "GE" && li == 0 && ri == 1) || (dir == "LE" && li == 1 && ri == 0))) continue;
-          if (m->type.rank() != 2) continue;
-          causal = true;
-          chain.push_back(sel);
-          if (!SingleUse(s)) {}
-          s = sel->operands[1];
-          if (!SingleUse(s)) continue;
-        }
-        if (s->def && s->def->name == "multiply") {
-          double c;
-          const Op* mul = s->def;
-          const Value* other = nullptr;
-          if (IsScalarConst(mul->operands[1], &c)) other = mul->operands[0];
-          else if (IsScalarConst(mul->operands[0], &c)) other = mul->operands[1];
-          if (!other || (s != x && !SingleUse(s))) continue;
-          scale = c;
-          chain.push_back(mul);
-          s = other;
-        }
-        if (!s->def || s->def->name != "dot_general" || (s != x && !SingleUse(s))) continue;
-        const Op* d1 = s->def;
-        if (ints(d1, "batching_dims.lhs") != b01 || ints(d1, "batching_dims.rhs") != b01 ||
-            ints(d1, "contracting_dims.lhs") != std::vector<int64_t>{3} ||
-            ints(d1, "contracting_dims.rhs") != std::vector<int64_t>{3})
-          continue;
-        const Value* Q = d1->operands[0];
-        const Value* K = d1->operands[1];
-        if (Q->type.dt != DT::kBF16 || K->type.dt != DT::kBF16 || V->type.dt != DT::kBF16) continue;
-        if (d2->result()->type.dt != DT::kBF16) continue;
-        if (!(Q->type.dims == K->type.dims && Q->type.dims == V->type.dims)) continue;
-        if (s->type.dt != DT::kF32) continue;
-        int Dh = (int)Q->type.dims[3];
-        if (Dh != 64 && Dh != 128) continue;
-        if (Q->type.dims[2] % 128 != 0) continue;
-        chain.push_back(d1);
-        AttentionStep a;
-        a.B = (int)Q->type.dims[0];
-        a.H = (int)Q->type.dims[1];
-        a.S = (int)Q->type.dims[2];
-        a.D = Dh;
-        a.causal = causal;
-        a.scale = (float)scale;
-        attn_[d2->result()->id] = a;
-        attn_in_[d2->result()->id] = {Q, K, V};
-        for (const Op* o : chain) if (o != d2) dead_[o->index] = true;
-      }
-    next:;
+      const Op* d2 = opp.get();
+      FwdChain fc;
+      if (MatchFwdChain(d2, true, &fc)) RegisterAttention(d2, fc);
+      else if (MatchFwdChain(d2, false, &fc) && !std::getenv("B200_NO_FLASH_BWD")) MatchAttentionTraining(d2, fc);
     }
   }
+
+  // ---------------------------------------------------------------- attention in training
+  // The forward chain's intermediates also feed its VJP.  Recognised by anchors: dV = dot(P', G)
+  // contracting the query dim, dP = dot(G, V) contracting the head dim, and one value T read by
+  // dQ = dot(T, K) and dK = dot(Q, T) (or dot(T, Q)).  T is accepted when it evaluates, on sample
+  // rows of random scores and cotangents, to scale * mask * P * (dP - rowsum(P * dP)) -- whatever
+  // elementwise / row-reduction ops compute it.  Then the forward runs as the flash forward (also
+  // writing lse2) and the three dots as one flash-backward step; the S x S intermediates vanish.
+  struct BwdMatch {
+    int d2 = -1;                                     // forward result value id (O)
+    const Value *Q = nullptr, *K = nullptr, *V = nullptr, *O = nullptr, *G = nullptr;
+    const Value *dq = nullptr, *dk = nullptr, *dv = nullptr;
+    bool dk_t = false;                               // dK delivered as [B, H, D, S]
+    bool emitted = false;
+  };
+  std::vector<BwdMatch> bwd_;
+  std::unordered_map<int, int> bwd_of_;              // dq / dk / dv dot result id -> bwd_ index
+  std::unordered_set<int> bwd_in_;                   // values the backward step reads (G)
+
+  // Row evaluator: the value of `v` at a full index, in double precision, for the ops a softmax VJP
+  // is made of; `leaf` supplies the scores S and the cotangent dP.  Returns false for other ops.
+  struct RowEval {
+    std::function<bool(const Value*, const std::vector<int64_t>&, double*)> leaf;
+    std::map<std::pair<int, std::vector<int64_t>>, double> memo;
+    int budget = 4000000;
+    bool At(const Value* v, const std::vector<int64_t>& idx, double* out) {
+      if (--budget < 0) return false;
+      if (leaf(v, idx, out)) return true;
+      auto key = std::make_pair(v->id, idx);
+      auto it = memo.find(key);
+      if (it != memo.end()) { *out = it->second; return true; }
+      const Op* op = v->def;
+      if (!op) return false;
+      const std::string& n = op->name;
+      double r = 0;
+      auto at = [&](int k, const std::vector<int64_t>& j, double* o) { return At(op->operands[k], j, o); };
+      if (n == "constant") {
+        if (!op->splat) return false;
+        r = ConstScalar(op);
+      } else if (n == "iota") {
+        r = (double)idx[op->ints.at("dim")[0]];
+      } else if (n == "broadcast_in_dim") {
+        const auto& dims = op->ints.at("dims");
+        const auto& in = op->operands[0]->type.dims;
+        std::vector<int64_t> j(in.size());
+        for (size_t k = 0; k < in.size(); ++k) j[k] = in[k] == 1 ? 0 : idx[dims[k]];
+        if (!at(0, j, &r)) return false;
+      } else if (n == "reshape" || IsAlias(op)) {
+        const auto& od = v->type.dims;
+        const auto& in = op->operands[0]->type.dims;
+        int64_t lin = 0;
+        for (size_t k = 0; k < od.size(); ++k) lin = lin * od[k] + idx[k];
+        std::vector<int64_t> j(in.size());
+        for (int k = (int)in.size() - 1; k >= 0; --k) { j[k] = in[k] ? lin % in[k] : 0; lin = in[k] ? lin / in[k] : 0; }
+        if (!at(0, j, &r)) return false;
+      } else if (n == "transpose") {
+        const auto& perm = op->ints.at("dims");
+        std::vector<int64_t> j(perm.size());
+        for (size_t k = 0; k < perm.size(); ++k) j[perm[k]] = idx[k];
+        if (!at(0, j, &r)) return false;
+      } else if (n == "convert") {
+        if (!at(0, idx, &r)) return false;
+        if (v->type.dt == DT::kBF16) r = RoundBf16((float)r);
+        else if (v->type.dt == DT::kF32) r = (float)r;
+        else if (v->type.dt == DT::kPred) r = r != 0;
+        else if (!DTIsFloat(v->type.dt)) r = std::trunc(r);
+      } else if (n == "compare") {
+        double a, b;
+        if (!at(0, idx, &a) || !at(1, idx, &b)) return false;
+        const std::string& d = op->strs.at("comparison_direction");
+        r = d == "EQ" ? a == b : d == "NE" ? a != b : d == "LT" ? a < b : d == "LE" ? a <= b : d == "GT" ? a > b : a >= b;
+      } else if (n == "select") {
+        double c;
+        const auto& pd = op->operands[0]->type.dims;
+        if (!At(op->operands[0], pd.empty() ? std::vector<int64_t>{} : idx, &c)) return false;
+        if (!at(c != 0 ? 1 : 2, idx, &r)) return false;
+      } else if (n == "negate" || n == "exponential" || n == "log" || n == "sqrt" || n == "rsqrt" || n == "tanh") {
+        double a;
+        if (!at(0, idx, &a)) return false;
+        r = n == "negate" ? -a : n == "exponential" ? std::exp(a) : n == "log" ? std::log(a) : n == "sqrt" ? std::sqrt(a)
+            : n == "rsqrt" ? 1.0 / std::sqrt(a) : std::tanh(a);
+      } else if (n == "add" || n == "subtract" || n == "multiply" || n == "divide" || n == "maximum" || n == "minimum") {
+        double a, b;
+        if (!at(0, idx, &a) || !at(1, idx, &b)) return false;
+        r = n == "add" ? a + b : n == "subtract" ? a - b : n == "multiply" ? a * b : n == "divide" ? a / b
+            : n == "maximum" ? std::max(a, b) : std::min(a, b);
+      } else if (n == "reduce" && (op->reduce == ReduceKind::kAdd || op->reduce == ReduceKind::kMax) && op->results.size() == 1) {
+        std::vector<int64_t> rd = op->ints.at("dimensions");
+        std::sort(rd.begin(), rd.end());
+        const auto& xd = op->operands[0]->type.dims;
+        double init;
+        if (!At(op->operands[1], {}, &init)) return false;
+        std::vector<int64_t> j(xd.size());
+        size_t q = 0;
+        for (size_t k = 0; k < xd.size(); ++k) if (!std::binary_search(rd.begin(), rd.end(), (int64_t)k)) j[k] = idx[q++];
+        int64_t total = 1;
+        for (int64_t d : rd) total *= xd[d];
+        r = init;
+        for (int64_t t = 0; t < total; ++t) {
+          int64_t rem = t;
+          for (int k = (int)rd.size() - 1; k >= 0; --k) { j[rd[k]] = rem % xd[rd[k]]; rem /= xd[rd[k]]; }
+          double x;
+          if (!at(0, j, &x)) return false;
+          r = op->reduce == ReduceKind::kAdd ? r + x : std::max(r, x);
+        }
+      } else {
+        return false;
+      }
+      memo[key] = r;
+      *out = r;
+      return true;
+    }
+  };
+
+  // deterministic pseudo-random value in [-1, 1) for an index
+  static double Hash01(uint64_t a, uint64_t b, uint64_t salt) {
+    uint64_t h = a * 0x9E3779B97F4A7C15ULL ^ (b + salt) * 0xC2B2AE3D27D4EB4FULL;
+    h ^= h >> 29;
+    h *= 0xBF58476D1CE4E5B9ULL;
+    h ^= h >> 32;
+    return (double)(h >> 11) / (double)(1ULL << 52) - 1.0;
+  }
+
+  // T == scale * mask * P * (dP - rowsum(P * dP)) on sample rows of random S and dP?
+  bool VerifySoftmaxVjp(const Value* T, const Value* S, const Value* dP, const FwdChain& fc) const {
+    const auto& d = T->type.dims;
+    if (d.size() != 4 || S->type.dims != d || dP->type.dims != d) return false;
+    const int64_t n = d[3];
+    for (int64_t q : {n / 2 + 3, n - 1, (int64_t)1}) {
+      if (q >= d[2]) continue;
+      RowEval ev;
+      ev.leaf = [&](const Value* v, const std::vector<int64_t>& idx, double* out) {
+        if (v == S) { *out = 3.0 * Hash01(idx[2], idx[3], 1); return true; }
+        if (v == dP) { *out = RoundBf16((float)Hash01(idx[2], idx[3], 2)); return true; }
+        return false;
+      };
+      // reference row in double
+      std::vector<double> x(n), pr(n), dp(n);
+      double mx = -INFINITY;
+      for (int64_t k = 0; k < n; ++k) {
+        const bool keep = !fc.causal || k <= q;
+        x[k] = keep ? fc.scale * 3.0 * Hash01(q, k, 1) : -INFINITY;
+        mx = std::max(mx, x[k]);
+        dp[k] = RoundBf16((float)Hash01(q, k, 2));
+      }
+      double sum = 0, dot = 0;
+      for (int64_t k = 0; k < n; ++k) { pr[k] = std::exp(x[k] - mx); sum += pr[k]; }
+      for (int64_t k = 0; k < n; ++k) { pr[k] /= sum; dot += pr[k] * dp[k]; }
+      double worst = 0, big = 1e-30;
+      for (int64_t k = 0; k < n; ++k) {
+        const double ref = fc.scale * pr[k] * (dp[k] - dot);
+        double got;
+        if (!ev.At(T, {1 % d[0], 1 % d[1], q, k}, &got)) return false;
+        worst = std::max(worst, std::fabs(got - ref));
+        big = std::max(big, std::fabs(ref));
+      }
+      if (!(worst <= 2e-2 * big)) return false;
+    }
+    return true;
+  }
+
+  void MatchAttentionTraining(const Op* d2, const FwdChain& fc) {
+    auto ints = [&](const Op* o, const char* k) {
+      auto it = o->ints.find(k);
+      return it == o->ints.end() ? std::vector<int64_t>{} : it->second;
+    };
+    auto is_dot = [&](const Op* o, const Value* l, const Value* r, int64_t lc, int64_t rc) {
+      return o->name == "dot_general" && o->operands.size() == 2 && o->operands[0] == l && (!r || o->operands[1] == r) &&
+             ints(o, "batching_dims.lhs") == std::vector<int64_t>{0, 1} && ints(o, "batching_dims.rhs") == std::vector<int64_t>{0, 1} &&
+             ints(o, "contracting_dims.lhs") == std::vector<int64_t>{lc} && ints(o, "contracting_dims.rhs") == std::vector<int64_t>{rc} &&
+             o->result()->type.dt == DT::kBF16;
+    };
+    // dV = dot(P', G) contracting the query dim
+    const Op* dv_op = nullptr;
+    for (const Op* u : fc.P16->users)
+      if (u != d2 && is_dot(u, fc.P16, nullptr, 2, 2)) dv_op = u;
+    if (!dv_op) return;
+    const Value* G = dv_op->operands[1];
+    if (G->type.dims != fc.Q->type.dims || G->type.dt != DT::kBF16) return;
+    // dP = dot(G, V) contracting the head dim
+    const Op* dp_op = nullptr;
+    for (const Op* u : G->users)
+      if (is_dot(u, G, fc.V, 3, 3)) dp_op = u;
+    if (!dp_op) return;
+    // dQ = dot(T, K) [3 x 2]; dK = dot(Q, T) [2 x 2] or dot(T, Q) [2 x 2]
+    const Op* dq_op = nullptr;
+    for (const Op* u : fc.K->users)
+      if (u->name == "dot_general" && u->operands.size() == 2 && u->operands[1] == fc.K && is_dot(u, u->operands[0], fc.K, 3, 2) &&
+          u->operands[0]->type.dims == fc.S->type.dims)
+        dq_op = u;
+    if (!dq_op) return;
+    const Value* T = dq_op->operands[0];
+    const Op* dk_op = nullptr;
+    bool dk_t = false;
+    for (const Op* u : T->users) {
+      if (is_dot(u, fc.Q, T, 2, 2)) { dk_op = u; dk_t = true; }
+      else if (is_dot(u, T, fc.Q, 2, 2)) { dk_op = u; dk_t = false; }
+    }
+    if (!dk_op || T->users.size() != 2) return;
+    if (!VerifySoftmaxVjp(T, fc.S, dp_op->result(), fc)) return;
+    // the ops that compute T from S, dP and the forward intermediates
+    std::unordered_set<const Op*> kill(fc.ops.begin(), fc.ops.end());
+    kill.insert(dp_op);
+    std::vector<const Value*> stack{T};
+    while (!stack.empty()) {
+      const Value* v = stack.back();
+      stack.pop_back();
+      if (!v->def || v == fc.S || IndexOnly(v) || kill.count(v->def)) continue;
+      if (v == dp_op->result()) continue;
+      const std::string& n = v->def->name;
+      if (!(IsElementwise(v->def) || n == "reduce") || n == "dot_general") return;
+      kill.insert(v->def);
+      for (const Value* o : v->def->operands) stack.push_back(o);
+    }
+    // nothing outside may read what is about to disappear
+    std::unordered_set<const Op*> ok_users(kill.begin(), kill.end());
+    for (const Op* o : {d2, dv_op, dq_op, dk_op}) ok_users.insert(o);
+    for (const Op* o : kill)
+      for (const Value* r : o->results)
+        for (const Op* u : r->users)
+          if (!dead_[u->index] && !ok_users.count(u)) return;
+    FwdChain keep = fc;
+    keep.ops.clear();
+    RegisterAttention(d2, keep);
+    for (const Op* o : kill) dead_[o->index] = true;
+    BwdMatch m;
+    m.d2 = d2->result()->id;
+    m.Q = fc.Q;
+    m.K = fc.K;
+    m.V = fc.V;
+    m.O = d2->result();
+    m.G = G;
+    m.dq = dq_op->result();
+    m.dk = dk_op->result();
+    m.dv = dv_op->result();
+    m.dk_t = dk_t;
+    const int idx = (int)bwd_.size();
+    bwd_.push_back(m);
+    for (const Value* r : {m.dq, m.dk, m.dv}) bwd_of_[r->id] = idx;
+    bwd_in_.insert(G->id);
+    lse_for_[m.d2] = -1;
+  }
+  std::unordered_map<int, int> lse_for_;   // forward result id -> lse2 slot (training forward)
 
   // ---------------------------------------------------------------- materialization
   bool IsHeavy(const Op* op) const {
@@ -928,6 +1199,8 @@ class Lowerer {
     auto& cons = cons_;
     for (Value* o : g_.outputs) need_[o->id] = ext_use_[o->id] = true;
     for (auto& kv : attn_in_) for (const Value* v : kv.second) need_[v->id] = ext_use_[v->id] = true;
+    for (const BwdMatch& m : bwd_)
+      for (const Value* v : {m.Q, m.K, m.V, m.O, m.G}) need_[v->id] = ext_use_[v->id] = true;
     for (int i = (int)g_.ops.size() - 1; i >= 0; --i) {
       Op* op = g_.ops[i].get();
       if (dead_[i]) continue;
@@ -935,6 +1208,7 @@ class Lowerer {
         std::set<int> c;
         for (Op* u : r->users) {
           if (dead_[u->index]) continue;
+          if (u->results.size() == 1 && bwd_of_.count(u->result()->id)) continue;   // run by the attention backward
           if (IsHeavy(u) && u->name != "reduce") { need_[r->id] = ext_use_[r->id] = true; continue; }
           if (u->name == "reduce") {
             if (u->operands[0] == r) c.insert(u->result()->id);
@@ -1037,6 +1311,11 @@ class Lowerer {
           p_->slots[s].const_index = (int)p_->consts.size() - 1;
           slot_of_[r->id] = s;
         }
+        continue;
+      }
+      if (bwd_of_.count(r->id)) {
+        BwdMatch& m = bwd_[bwd_of_.at(r->id)];
+        if (!m.emitted) { flush(); EmitAttentionBwd(m); m.emitted = true; }
         continue;
       }
       if (n == "dot_general" || n == "dot") { flush(); EmitDot(op); continue; }
@@ -1989,12 +2268,52 @@ class Lowerer {
     a.v = SlotFor(ins[2]);
     a.o = SlotFor(d2->result());
     a.dt = DT::kBF16;
+    auto lf = lse_for_.find(d2->result()->id);
+    if (lf != lse_for_.end()) {                  // training: the backward needs lse2
+      a.lse = NewSlot((int64_t)a.B * a.H * a.S * 4);
+      lf->second = a.lse;
+      RecordDt(a.lse, DT::kF32);
+    }
     Step st;
     st.kind = StepKind::kAttention;
     st.attn = a;
-    st.label = std::string("attention ") + (a.causal ? "causal " : "") + ins[0]->type.str();
+    st.label = std::string("attention ") + (a.causal ? "causal " : "") + (a.lse >= 0 ? "+lse " : "") + ins[0]->type.str();
     p_->steps.push_back(st);
     RecordDt(a.o, DT::kBF16);
+  }
+
+  void EmitAttentionBwd(const BwdMatch& m) {
+    const AttentionStep& a = attn_.at(m.d2);
+    AttentionBwdStep b;
+    b.B = a.B;
+    b.H = a.H;
+    b.S = a.S;
+    b.D = a.D;
+    b.causal = a.causal;
+    b.scale = a.scale;
+    b.q = SlotFor(m.Q);
+    b.k = SlotFor(m.K);
+    b.v = SlotFor(m.V);
+    b.o = SlotFor(m.O);
+    b.dout = SlotFor(m.G);
+    b.lse = lse_for_.at(m.d2);
+    if (b.lse < 0) throw LowerError{"internal: attention backward before its forward"};
+    b.dq = SlotFor(m.dq);
+    b.dk = SlotFor(m.dk);
+    b.dv = SlotFor(m.dv);
+    const int64_t rows = (int64_t)a.B * a.H * a.S;
+    b.dq_acc = NewSlot(rows * a.D * 4);
+    b.delta = NewSlot(rows * 4);
+    b.dk_t = m.dk_t;
+    if (m.dk_t) b.dk_tmp = NewSlot(rows * a.D * 2);
+    for (int s : {b.dq, b.dk, b.dv}) RecordDt(s, DT::kBF16);
+    for (int s : {b.dq_acc, b.delta}) RecordDt(s, DT::kF32);
+    if (b.dk_tmp >= 0) RecordDt(b.dk_tmp, DT::kBF16);
+    Step st;
+    st.kind = StepKind::kAttentionBwd;
+    st.bwd = b;
+    st.label = std::string("attention_bwd ") + (a.causal ? "causal " : "") + m.Q->type.str();
+    p_->steps.push_back(st);
   }
 
   // ---------------------------------------------------------------- scatter (embedding VJP)
@@ -2109,7 +2428,14 @@ class Lowerer {
           }
           break;
         case StepKind::kGemm: touch(st.gemm.a, i); touch(st.gemm.b, i); touch(st.gemm.c, i); break;
-        case StepKind::kAttention: touch(st.attn.q, i); touch(st.attn.k, i); touch(st.attn.v, i); touch(st.attn.o, i); break;
+        case StepKind::kAttention:
+          touch(st.attn.q, i); touch(st.attn.k, i); touch(st.attn.v, i); touch(st.attn.o, i); touch(st.attn.lse, i);
+          break;
+        case StepKind::kAttentionBwd:
+          for (int s : {st.bwd.q, st.bwd.k, st.bwd.v, st.bwd.o, st.bwd.dout, st.bwd.lse, st.bwd.dq, st.bwd.dk, st.bwd.dv,
+                        st.bwd.dq_acc, st.bwd.delta, st.bwd.dk_tmp})
+            touch(s, i);
+          break;
         case StepKind::kScatterAdd: touch(st.scatter.base, i); touch(st.scatter.idx, i); touch(st.scatter.upd, i); touch(st.scatter.out, i); break;
         case StepKind::kCollective: touch(st.coll.in, i); touch(st.coll.out, i); break;
         case StepKind::kCopy: touch(st.copy.src, i); touch(st.copy.dst, i); break;

@@ -22,7 +22,7 @@ struct Slot {
   int last_use = -1;           // index of the last step that reads it (-1: never read)
 };
 
-enum class StepKind { kFusion, kGemm, kAttention, kScatterAdd, kCollective, kCopy };
+enum class StepKind { kFusion, kGemm, kAttention, kAttentionBwd, kScatterAdd, kCollective, kCopy };
 
 // One generated kernel launch (loop fusion, or one stage of a reduction).
 struct Launch {
@@ -50,6 +50,18 @@ struct AttentionStep {
   bool causal = false;
   float scale = 1.f;
   DT dt = DT::kBF16;
+  int lse = -1;                          // training forward: lse2 [B*H*S] f32 for the backward
+};
+
+// dQ, dK, dV of an attention whose forward ran as an AttentionStep with lse.
+struct AttentionBwdStep {
+  int q = -1, k = -1, v = -1, o = -1, dout = -1, lse = -1;   // inputs, [B,H,S,D] bf16 (lse [B*H*S] f32)
+  int dq = -1, dk = -1, dv = -1;                            // outputs bf16; dk is [B,H,D,S] when dk_t
+  int dq_acc = -1, delta = -1, dk_tmp = -1;                 // scratch
+  bool dk_t = false;
+  int B = 0, H = 0, S = 0, D = 0;
+  bool causal = false;
+  float scale = 1.f;
 };
 
 struct ScatterStep {           // out = base; out[idx[i], :] += upd[i, :]
@@ -78,6 +90,7 @@ struct Step {
   std::vector<Launch> launches;      // kFusion: one or two (reduction stage 2) launches
   GemmStep gemm;
   AttentionStep attn;
+  AttentionBwdStep bwd;
   ScatterStep scatter;
   CollectiveStep coll;
   CopyStep copy;

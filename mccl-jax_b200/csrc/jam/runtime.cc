@@ -21,6 +21,12 @@ int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, 
          int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st);
 int AttentionFwd(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D, int causal, float scale,
                  cudaStream_t st);
+int AttentionFwdLse(const void* q, const void* k, const void* v, void* o, float* lse2, int B, int H, int S, int D,
+                    int causal, float scale, cudaStream_t st);
+int AttentionBwd(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse2,
+                 void* dq, void* dk, void* dv, float* dq_acc, float* delta, int B, int H, int S, int D, int causal,
+                 float scale, cudaStream_t st);
+int TransposeRowsCols(const void* x, void* y, int n, int R, int C, cudaStream_t st);
 }
 
 namespace b200 {
@@ -309,9 +315,25 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
       }
       case StepKind::kAttention: {
         const AttentionStep& a = S.attn;
-        for (int s : {a.q, a.k, a.v, a.o}) { err = slot(s); if (!err.empty()) return fail(err); }
-        int rc = b200k::AttentionFwd(ptr[a.q], ptr[a.k], ptr[a.v], ptr[a.o], a.B, a.H, a.S, a.D, a.causal, a.scale, st);
+        for (int s : {a.q, a.k, a.v, a.o, a.lse}) { err = slot(s); if (!err.empty()) return fail(err); }
+        int rc = a.lse >= 0 ? b200k::AttentionFwdLse(ptr[a.q], ptr[a.k], ptr[a.v], ptr[a.o], (float*)ptr[a.lse], a.B, a.H, a.S,
+                                                     a.D, a.causal, a.scale, st)
+                            : b200k::AttentionFwd(ptr[a.q], ptr[a.k], ptr[a.v], ptr[a.o], a.B, a.H, a.S, a.D, a.causal, a.scale, st);
         if (rc != 0) return fail("attention launch failed (" + std::to_string(rc) + ")");
+        break;
+      }
+      case StepKind::kAttentionBwd: {
+        const AttentionBwdStep& b = S.bwd;
+        for (int s : {b.q, b.k, b.v, b.o, b.dout, b.lse, b.dq, b.dk, b.dv, b.dq_acc, b.delta, b.dk_tmp}) {
+          err = slot(s);
+          if (!err.empty()) return fail(err);
+        }
+        void* dk = b.dk_t ? ptr[b.dk_tmp] : ptr[b.dk];
+        int rc = b200k::AttentionBwd(ptr[b.q], ptr[b.k], ptr[b.v], ptr[b.o], ptr[b.dout], (const float*)ptr[b.lse], ptr[b.dq], dk,
+                                     ptr[b.dv], (float*)ptr[b.dq_acc], (float*)ptr[b.delta], b.B, b.H, b.S, b.D, b.causal,
+                                     b.scale, st);
+        if (rc == 0 && b.dk_t) rc = b200k::TransposeRowsCols(dk, ptr[b.dk], b.B * b.H, b.S, b.D, st);
+        if (rc != 0) return fail("attention backward launch failed (" + std::to_string(rc) + ")");
         break;
       }
       case StepKind::kScatterAdd: {

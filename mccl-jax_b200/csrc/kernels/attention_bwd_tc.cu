@@ -327,6 +327,20 @@ __global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* __restric
   }
 }
 
+// [n, R, C] -> [n, C, R] bf16 through 32 x 32 shared-memory tiles (dK for a caller that wants it
+// head-dim-major).
+__global__ void __launch_bounds__(256) transpose_rc_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int R, int C) {
+  __shared__ uint16_t tile[32][34];
+  const long long base = (long long)blockIdx.z * R * C;
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int j = ty; j < 32; j += 8)
+    if (r0 + j < R && c0 + tx < C) tile[j][tx] = x[base + (long long)(r0 + j) * C + c0 + tx];
+  __syncthreads();
+  for (int j = ty; j < 32; j += 8)
+    if (c0 + j < C && r0 + tx < R) y[base + (long long)(c0 + j) * R + r0 + tx] = tile[tx][j];
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -385,6 +399,13 @@ int AttentionBwd(const void* q, const void* k, const void* v, const void* o, con
                                                          (__nv_bfloat16*)dv, S, scale, scale_log2);
   const long long n4 = rows * HD / 4;
   f32_to_bf16_kernel<<<(unsigned)std::min<long long>((n4 + 255) / 256, 148 * 8), 256, 0, st>>>(dq_acc, (__nv_bfloat16*)dq, n4);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int TransposeRowsCols(const void* x, void* y, int n, int R, int C, cudaStream_t st) {
+  if (n <= 0 || R <= 0 || C <= 0) return 0;
+  dim3 grid((C + 31) / 32, (R + 31) / 32, n);
+  transpose_rc_kernel<<<grid, 256, 0, st>>>((const uint16_t*)x, (uint16_t*)y, R, C);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
