@@ -544,11 +544,18 @@ struct Gen {
       for (size_t k = 0; k < inn.size(); ++k) j[inn[k]] = idx[on[k]];
       return j;
     }
-    std::string lin = Var(DT::kS64, Linear(idx, out));
+    // general reshape: through the row-major linear index (32-bit arithmetic when it fits: division
+    // by a constant is a multiply-high, far cheaper than the 64-bit sequence)
+    int64_t total = 1;
+    for (int64_t d : in) total *= d;
+    const bool narrow = total < (1LL << 31);
+    std::string lin = narrow ? Var(DT::kU32, "(unsigned)(" + Linear(idx, out) + ")") : Var(DT::kS64, Linear(idx, out));
+    const std::string suf = narrow ? "u" : "LL";
     int64_t stride = 1;
     for (int k = (int)in.size() - 1; k >= 0; --k) {
-      std::string e = "(int)((" + lin + " / " + std::to_string(stride) + "LL) % " + std::to_string(in[k]) + "LL)";
-      if (k == 0) e = "(int)(" + lin + " / " + std::to_string(stride) + "LL)";
+      std::string e = "(int)((" + lin + " / " + std::to_string(stride) + suf + ") % " + std::to_string(in[k]) + suf + ")";
+      if (k == 0) e = "(int)(" + lin + " / " + std::to_string(stride) + suf + ")";
+      if (stride == 1 && k != 0) e = "(int)(" + lin + " % " + std::to_string(in[k]) + suf + ")";
       j[k] = Var(DT::kS32, e);
       stride *= in[k];
     }
@@ -696,12 +703,15 @@ class Lowerer {
     if (!p) return n * DTBytes(StoredDt(v));
     return n / v->type.dims.back() * p * DTBytes(StoredDt(v));
   }
-  // element offset of linear index `i` in the buffer of v (padded pitch when it has one)
-  std::string StoredIndex(const Value* v, const std::string& i) const {
+  // element offset of linear index `i` (whose per-dim indices are `names`) in the buffer of v: with
+  // a padded pitch, the outer dims' linear index times the pitch plus the innermost index
+  std::string StoredIndex(const Value* v, const std::string& i, const std::vector<std::string>& names) const {
     const int64_t p = StoredPitch(v);
     if (!p) return i;
-    const std::string inner = std::to_string(v->type.dims.back());
-    return "((" + i + ") / " + inner + "LL * " + std::to_string(p) + "LL + (" + i + ") % " + inner + "LL)";
+    const auto& d = v->type.dims;
+    std::vector<std::string> outer(names.begin(), names.end() - 1);
+    std::vector<int64_t> od(d.begin(), d.end() - 1);
+    return "(" + Gen::Linear(outer, od) + " * " + std::to_string(p) + "LL + (" + names.back() + "))";
   }
   DT StoredDt(const Value* v) const {
     auto it = demote_.find(v->id);
@@ -1190,6 +1200,40 @@ class Lowerer {
     return false;
   }
 
+  // A value read by several fusion kernels is stored once unless recomputing it in each reader is
+  // cheaper: its expression (down to arguments, reductions and other non-elementwise results) has a
+  // few ops and reads at most one tensor of its own size, the rest being small broadcast operands
+  // (row statistics, labels, biases).  Each reader then reads that one tensor instead of the stored
+  // copy: the same bytes, minus the store.  (exp(z - max) and one-hot(labels) of a cross entropy,
+  // x - mean of a LayerNorm, x + bias before an activation.)
+  bool Recomputable(const Value* v) const {
+    if (std::getenv("B200_NO_RECOMPUTE")) return false;
+    const int64_t n = v->type.numel();
+    int ops = 0;
+    std::unordered_set<int> big, seen;
+    std::vector<const Value*> stack{v};
+    while (!stack.empty()) {
+      const Value* x = stack.back();
+      stack.pop_back();
+      if (!seen.insert(x->id).second) continue;
+      const Op* op = x->def;
+      const bool leaf = !op || !IsElementwise(op) || op->name == "gather" || (op->name == "constant" && !op->splat);
+      if (leaf || (op->name == "constant") || op->name == "iota") {
+        if (op && (op->name == "constant" || op->name == "iota")) continue;
+        if (x->type.numel() * 16 > n) big.insert(x->id);
+        if (big.size() > 1) return false;
+        continue;
+      }
+      if (IsAlias(op) || op->name == "broadcast_in_dim" || op->name == "reshape" || op->name == "convert") {
+        // free in the generated code
+      } else if (++ops > 12) {
+        return false;
+      }
+      for (const Value* o : op->operands) stack.push_back(o);
+    }
+    return true;
+  }
+
   void DecideMaterialization() {
     size_t nv = g_.values.size();
     need_.assign(nv, false);
@@ -1231,7 +1275,7 @@ class Lowerer {
         cons[r->id] = c;
         if (IsHeavy(op)) need_[r->id] = true;
         if (!op->results.empty() && op->name == "constant" && !op->splat) need_[r->id] = true;
-        if (!need_[r->id] && IsElementwise(op) && c.size() >= 2 && !Cheap(r)) need_[r->id] = true;
+        if (!need_[r->id] && IsElementwise(op) && c.size() >= 2 && !Cheap(r) && !Recomputable(r)) need_[r->id] = true;
         if (IsAlias(op) && need_[r->id]) {
           // the alias source carries the buffer
           need_[op->operands[0]->id] = true;
@@ -1390,8 +1434,20 @@ class Lowerer {
     return out;
   }
 
-  // A group of loop roots with one shape -> one kernel with several outputs.
+  // A group of loop roots with one shape -> one kernel with several outputs.  Wide rows (inner extent
+  // >= 512, enough rows to fill the GPU) run as a row kernel: the row's index math and its row-shaped
+  // operands (statistics, labels) are computed once per row instead of once per element.
   void EmitLoopGroup(const std::vector<const Value*>& roots) {
+    const auto& X = roots[0]->type.dims;
+    if (X.size() >= 2 && X.back() >= 512 && !std::getenv("B200_NO_ROWLOOP")) {
+      int64_t rows = 1;
+      for (size_t k = 0; k + 1 < X.size(); ++k) rows *= X[k];
+      const bool enough = X.back() > 8192 ? rows >= 148 * 4 : rows >= 148 * 32;
+      if (enough && TryRow(roots, X, true)) {
+        TryRow(roots, X, false);
+        return;
+      }
+    }
     // greedily split where a later root reads an earlier one at a non-identity index
     size_t start = 0;
     while (start < roots.size()) {
@@ -1489,18 +1545,18 @@ class Lowerer {
     src_ << gen.body.str();
     for (size_t k = 0; k < roots.size(); ++k) {
       if (!vec) {
-        src_ << "    out" << k << "[" << StoredIndex(roots[k], "i") << "] = " << StoreExpr(out_dts[k], StoreVal(roots[k], out_dts[k], regs[k])) << ";\n";
+        src_ << "    out" << k << "[" << StoredIndex(roots[k], "i", vec ? gen.lane_identity[0] : gen.identity) << "] = " << StoreExpr(out_dts[k], StoreVal(roots[k], out_dts[k], regs[k])) << ";\n";
         continue;
       }
       std::vector<std::string> r4 = lregs[k];
       for (auto& x : r4) x = StoreVal(roots[k], out_dts[k], x);
       if (out_dts[k] == DT::kF32) {
-        src_ << "    *(float4*)(out" << k << " + " << StoredIndex(roots[k], "i") << ") = make_float4(" << r4[0] << ", " << r4[1] << ", " << r4[2] << ", " << r4[3] << ");\n";
+        src_ << "    *(float4*)(out" << k << " + " << StoredIndex(roots[k], "i", vec ? gen.lane_identity[0] : gen.identity) << ") = make_float4(" << r4[0] << ", " << r4[1] << ", " << r4[2] << ", " << r4[3] << ");\n";
       } else if (out_dts[k] == DT::kBF16 || out_dts[k] == DT::kF16) {
-        src_ << "    *(uint2*)(out" << k << " + " << StoredIndex(roots[k], "i") << ") = make_uint2(" << Pack16(out_dts[k], r4[0], r4[1]) << ", "
+        src_ << "    *(uint2*)(out" << k << " + " << StoredIndex(roots[k], "i", vec ? gen.lane_identity[0] : gen.identity) << ") = make_uint2(" << Pack16(out_dts[k], r4[0], r4[1]) << ", "
              << Pack16(out_dts[k], r4[2], r4[3]) << ");\n";
       } else {
-        for (int l = 0; l < 4; ++l) src_ << "    out" << k << "[" << StoredIndex(roots[k], "i") << " + " << l << "] = " << StoreExpr(out_dts[k], r4[l]) << ";\n";
+        for (int l = 0; l < 4; ++l) src_ << "    out" << k << "[" << StoredIndex(roots[k], "i", vec ? gen.lane_identity[0] : gen.identity) << " + " << l << "] = " << StoreExpr(out_dts[k], r4[l]) << ";\n";
       }
     }
     src_ << "}\n";
@@ -1633,7 +1689,7 @@ class Lowerer {
     int64_t rows = 1;
     for (int64_t d : kept) rows *= d;
     const bool wide = rows * L >= (1LL << 31);
-    const bool block_mode = L > 2048;
+    const bool block_mode = L > 8192;
     const int T = block_mode ? 512 : 32;          // threads that share a row
     // Each thread takes four elements per step: consecutive ones with vector loads when L % 4 == 0,
     // else four T-strided ones (coalesced scalar loads) whose indices are clamped into the row and
@@ -1687,7 +1743,7 @@ class Lowerer {
       return "(long long)row * " + (p ? std::to_string(p) : Ls) + "LL + j_" + std::to_string(l);
     };
     // a phase over the row: element values of `v` (one per lane in vector mode)
-    auto row_phase = [&](const Value* v) {
+    auto phase_begin = [&]() {
       gen.cse.clear();
       gen.vloads.clear();
       gen.body.str("");
@@ -1697,9 +1753,15 @@ class Lowerer {
       gen.vinner = "j";
       gen.lane_identity = lanes;
       gen.identity = lanes[0];
+    };
+    auto phase_vals = [&](const Value* v) {
       std::vector<std::string> vals;
       for (int l = 0; l < 4; ++l) vals.push_back(gen.Emit(v, lanes[l]));
       return vals;
+    };
+    auto row_phase = [&](const Value* v) {
+      phase_begin();
+      return phase_vals(v);
     };
     std::vector<std::pair<std::string, std::string>> shared;   // block mode: (type, name)
     std::vector<bool> done(members.size(), false);
@@ -1791,20 +1853,38 @@ class Lowerer {
         if (!o.empty()) body << "    if (lt == 0) " << o << "[row] = " << StoreExpr(odt, rk) << ";\n";
         gen.fixed[m->id] = rk;
       } else if (m->type.dims == X) {
-        if (o.empty()) continue;                // internal: the members that read it recompute it
-        std::vector<std::string> vals = row_phase(m);
+        // a run of consecutive full members shares one walk of the row; internal ones are not
+        // stored (the members that read them recompute them)
+        size_t k_end = k;
+        while (k_end < members.size() && !done[k_end] && members[k_end]->type.dims == X &&
+               !(members[k_end]->def && members[k_end]->def->name == "reduce"))
+          ++k_end;
+        std::vector<std::pair<size_t, std::vector<std::string>>> outs;
+        phase_begin();
+        for (size_t q = k; q < k_end; ++q) {
+          done[q] = true;
+          if (out_of[q] < 0) continue;
+          outs.push_back({q, phase_vals(members[q])});
+        }
+        k = k_end - 1;
+        if (outs.empty()) continue;
         body << loop_head << gen.body.str();
-        DT dt = StoredDt(m);
-        for (auto& x : vals) x = StoreVal(m, dt, x);
-        if (!vec) {
-          for (int l = 0; l < 4; ++l)
-            body << "      " << (ok(l).empty() ? "" : "if (" + ok(l) + ") ") << o << "[" << elem_index(m, l) << "] = " << StoreExpr(dt, vals[l]) << ";\n";
-        } else if (dt == DT::kF32) {
-          body << "      *(float4*)(" << o << " + " << elem_index(m, 0) << ") = make_float4(" << vals[0] << ", " << vals[1] << ", " << vals[2] << ", " << vals[3] << ");\n";
-        } else if (dt == DT::kBF16 || dt == DT::kF16) {
-          body << "      *(uint2*)(" << o << " + " << elem_index(m, 0) << ") = make_uint2(" << Pack16(dt, vals[0], vals[1]) << ", " << Pack16(dt, vals[2], vals[3]) << ");\n";
-        } else {
-          for (int l = 0; l < 4; ++l) body << "      " << o << "[" << elem_index(m, l) << "] = " << StoreExpr(dt, vals[l]) << ";\n";
+        for (auto& ov : outs) {
+          const Value* mq = members[ov.first];
+          const std::string oq = "out" + std::to_string(out_of[ov.first]);
+          std::vector<std::string>& vals = ov.second;
+          DT dt = StoredDt(mq);
+          for (auto& x : vals) x = StoreVal(mq, dt, x);
+          if (!vec) {
+            for (int l = 0; l < 4; ++l)
+              body << "      " << (ok(l).empty() ? "" : "if (" + ok(l) + ") ") << oq << "[" << elem_index(mq, l) << "] = " << StoreExpr(dt, vals[l]) << ";\n";
+          } else if (dt == DT::kF32) {
+            body << "      *(float4*)(" << oq << " + " << elem_index(mq, 0) << ") = make_float4(" << vals[0] << ", " << vals[1] << ", " << vals[2] << ", " << vals[3] << ");\n";
+          } else if (dt == DT::kBF16 || dt == DT::kF16) {
+            body << "      *(uint2*)(" << oq << " + " << elem_index(mq, 0) << ") = make_uint2(" << Pack16(dt, vals[0], vals[1]) << ", " << Pack16(dt, vals[2], vals[3]) << ");\n";
+          } else {
+            for (int l = 0; l < 4; ++l) body << "      " << oq << "[" << elem_index(mq, l) << "] = " << StoreExpr(dt, vals[l]) << ";\n";
+          }
         }
         body << "    }\n";
       } else {
@@ -1856,6 +1936,7 @@ class Lowerer {
     Step st;
     st.kind = StepKind::kFusion;
     st.launches.push_back(Lc);
+    st.label = "rowloop " + members[0]->type.str() + " x" + std::to_string(members.size());
     for (const Value* m : members)
       if (m->def && m->def->name == "reduce") {
         st.label = "row " + m->def->operands[0]->type.str() + " x" + std::to_string(members.size());

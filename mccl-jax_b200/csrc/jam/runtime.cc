@@ -107,6 +107,7 @@ int PjrtType(DT t) {
 struct StepTimer {
   bool on = std::getenv("B200_TIME") != nullptr;
   std::map<std::string, double> ms;
+  double host_ms = 0;          // time the host spends enqueueing one execution
   int runs = 0;
 };
 
@@ -275,6 +276,7 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
   };
   ExecTimerMarkStart(dev.ordinal, st);
   static StepTimer timer;
+  const auto host_t0 = std::chrono::steady_clock::now();
   std::vector<cudaEvent_t> evs;
   if (timer.on) {
     evs.resize(P.steps.size() + 1);
@@ -385,6 +387,7 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
   cudaError_t ce = cudaGetLastError();
   if (ce != cudaSuccess) return std::string("CUDA error during execute: ") + cudaGetErrorString(ce);
   if (timer.on) {
+    timer.host_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - host_t0).count();
     cudaEventSynchronize(evs.back());
     for (size_t i = 0; i < P.steps.size(); ++i) {
       float ms = 0;
@@ -393,7 +396,8 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     }
     for (auto& e : evs) cudaEventDestroy(e);
     if (++timer.runs % 20 == 0) {
-      std::fprintf(stderr, "[b200 timing] %s: per-run ms by step label (avg over %d runs)\n", name_.c_str(), timer.runs);
+      std::fprintf(stderr, "[b200 timing] %s: per-run ms by step label (avg over %d runs); host enqueue %.3f ms\n",
+                   name_.c_str(), timer.runs, timer.host_ms / timer.runs);
       for (auto& kv : timer.ms) std::fprintf(stderr, "  %10.4f  %s\n", kv.second / timer.runs, kv.first.c_str());
     }
   }
