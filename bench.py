@@ -211,7 +211,7 @@ def main():
     ap.add_argument("--H", type=int, default=HEAD["H"])
     ap.add_argument("--S", type=int, default=HEAD["S"])
     ap.add_argument("--causal", action="store_true")
-    ap.add_argument("--workload", default="attention", choices=["attention", "dp", "gemm", "psum", "fused"],
+    ap.add_argument("--workload", default="attention", choices=["attention", "dp", "gemm", "psum", "fused", "attn_bwd"],
                     help="attention (headline); dp = GPT-2 DP train step; gemm = dot_general sweep; fused = HBM-bound chains; "
                          "psum = all_reduce bandwidth sweep")
     ap.add_argument("--layers", type=int, default=12, help="dp: decoder layers")

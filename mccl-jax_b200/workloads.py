@@ -328,6 +328,64 @@ def run_fused(a, world, rank, local):
     return 0
 
 
+def run_attn_bwd(a, world, rank, local):
+    """Flash-attention training kernels through the C ABI: forward with lse2, then the backward
+    (delta, dQ/dK/dV, dQ rounding), device time with CUDA events, L2 flushed before each step."""
+    import torch
+    lib = ctypes.CDLL(LIB)
+    lib.b200_attention_fwd_lse.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_void_p]
+    lib.b200_attention_bwd.argtypes = [ctypes.c_void_p] * 11 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_void_p]
+    torch.cuda.set_device(local)
+    st = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(st.cuda_stream)
+    flush = torch.empty(64 * 1024 * 1024, device="cuda")
+    pk, src = _peaks()
+    rows = []
+    for B, H, S, causal in [(8, 12, 1024, True), (4, 16, 4096, True), (4, 16, 4096, False)]:
+        name = f"{B}x{H}x{S}-{'causal' if causal else 'full'}"
+        if getattr(a, "only", "") and a.only != name:
+            continue
+        g = torch.Generator(device="cuda").manual_seed(S)
+        q, k, v, do = (torch.randn(B, H, S, 64, device="cuda", generator=g).to(torch.bfloat16) for _ in range(4))
+        o, dq, dk, dv = (torch.empty_like(q) for _ in range(4))
+        lse = torch.empty(B, H, S, device="cuda")
+        dq_acc = torch.empty(B, H, S, 64, device="cuda")
+        delta = torch.empty(B, H, S, device="cuda")
+        fwd = lambda: lib.b200_attention_fwd_lse(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+                                                 B, H, S, 64, int(causal), 0.125, sp)
+        bwd = lambda: lib.b200_attention_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(),
+                                             lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dq_acc.data_ptr(),
+                                             delta.data_ptr(), B, H, S, 64, int(causal), 0.125, sp)
+        for _ in range(a.warmup):
+            assert fwd() == 0 and bwd() == 0
+        tf, tb = [], []
+        for _ in range(a.steps):
+            flush.zero_()
+            e = [torch.cuda.Event(True) for _ in range(3)]
+            e[0].record(st)
+            fwd()
+            e[1].record(st)
+            bwd()
+            e[2].record(st)
+            e[2].synchronize()
+            tf.append(e[0].elapsed_time(e[1]))
+            tb.append(e[1].elapsed_time(e[2]))
+        mf, mb = sorted(tf)[len(tf) // 2], sorted(tb)[len(tb) // 2]
+        fl = 4.0 * B * H * S * S * 64 * (0.5 if causal else 1.0)      # forward; the backward is 2.5x
+        rows.append({"shape": name, "fwd_ms": round(mf, 4), "fwd_tflops": round(fl / mf / 1e9, 1),
+                     "bwd_ms": round(mb, 4), "bwd_tflops": round(2.5 * fl / mb / 1e9, 1)})
+    head = rows[0]
+    print(json.dumps({"metric": "attention backward TFLOP/s (bf16 [8,12,1024,64] causal, GPT-2 training shape)",
+                      "value": head["bwd_tflops"], "unit": "TFLOP/s", "n_gpus": 1, "higher_is_better": True,
+                      "dtype": "bf16", "data": "synthetic N(0,1)",
+                      "config": {"workload": "flash attention fwd(+lse2) and bwd", "l2": "flushed before every step",
+                                 "flops": "bwd = 2.5 x fwd = 10 B H S^2 d (half causal)"},
+                      "roofline": {"bound": "tensor", "achieved": head["bwd_tflops"], "peak": pk["bf16_tflops"],
+                                   "frac": round(head["bwd_tflops"] / pk["bf16_tflops"], 3), "peak_source": src},
+                      "sweep": rows}))
+    return 0
+
+
 def run(a, world, rank, local):
     import torch
     torch.cuda.set_device(local)
@@ -335,7 +393,8 @@ def run(a, world, rank, local):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     try:
-        return {"dp": run_dp, "gemm": run_gemm, "psum": run_psum, "fused": run_fused}[a.workload](a, world, rank, local)
+        return {"dp": run_dp, "gemm": run_gemm, "psum": run_psum, "fused": run_fused,
+                "attn_bwd": run_attn_bwd}[a.workload](a, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist
