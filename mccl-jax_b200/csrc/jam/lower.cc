@@ -23,6 +23,10 @@
 
 #include "plan.h"
 
+namespace b200k {
+int GemmSplitK(int64_t batch, int64_t M, int64_t N, int64_t K, int sms);
+}
+
 namespace b200 {
 namespace {
 
@@ -2332,6 +2336,10 @@ class Lowerer {
     g.b_mn = ob.mn;
     g.ldb = ob.ld;
     g.c = SlotFor(r);
+    if (tc && g.out != DT::kF32 && b200k::GemmSplitK(g.batch, g.M, g.N, g.K, 148) > 1) {
+      g.ws = NewSlot(g.batch * g.M * g.N * 4);   // split-K partial sums
+      RecordDt(g.ws, DT::kF32);
+    }
     Step st;
     st.kind = StepKind::kGemm;
     st.gemm = g;
@@ -2508,7 +2516,7 @@ class Lowerer {
             touch(L.scratch, i);
           }
           break;
-        case StepKind::kGemm: touch(st.gemm.a, i); touch(st.gemm.b, i); touch(st.gemm.c, i); break;
+        case StepKind::kGemm: touch(st.gemm.a, i); touch(st.gemm.b, i); touch(st.gemm.c, i); touch(st.gemm.ws, i); break;
         case StepKind::kAttention:
           touch(st.attn.q, i); touch(st.attn.k, i); touch(st.attn.v, i); touch(st.attn.o, i); touch(st.attn.lse, i);
           break;

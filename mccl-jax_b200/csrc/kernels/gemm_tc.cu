@@ -34,8 +34,10 @@ struct Cfg {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStage = kABytes + kBBytes;
-  static constexpr int kStageOut = 4 * 32 * 33 * 4;   // epilogue staging: 4 warps x 32 x 33 f32
-  static constexpr int kSmem = kStages * kStage + 1024 + 256 + kStageOut;
+  // epilogue staging (1024-byte aligned): 4 warps x 32 x 33 f32 for the bounds-checked path, or 4 x
+  // 4 KB swizzled boxes for the TMA-store path
+  static constexpr int kStageOut = 4 * 32 * 33 * 4;
+  static constexpr int kSmem = kStages * kStage + 1024 + 1024 + kStageOut;
   static constexpr int kTmemCols = 2 * BN;
 };
 
@@ -49,6 +51,16 @@ __device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+               ::"l"(map), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Output tile order within a batch: bands of kGroupM row blocks, column-major inside a band.  The
 // CTAs working at the same time (consecutive tile indices) then share a few A row blocks and B
@@ -65,8 +77,9 @@ __device__ __forceinline__ void tile_coords(int r, int mb, int nb, int* m_blk, i
 // OUT: 0 f32, 1 bf16, 2 f16; AMN / BMN: operand stored MN-major
 template <int BN, int OUT, bool AMN, bool BMN>
 __global__ void __launch_bounds__(192, 1)
-gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* __restrict__ C,
-               int M, int N, int K, int batch, int fmt) {
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmC, void* __restrict__ C, int M, int N, int K, int batch, int fmt,
+               int splits, float* __restrict__ ws, int tma_store) {
   using CF = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -75,12 +88,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint64_t* acc_full = empty + CF::kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
-  float* stage_base = (float*)(smem + CF::kStages * CF::kStage + 256);
+  float* stage_base = (float*)(smem + CF::kStages * CF::kStage + 1024);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mb = (M + BM - 1) / BM, nb = (N + BN - 1) / BN;
   const int per_batch = mb * nb, num_tiles = per_batch * batch;
   const int kbs = (K + BK - 1) / BK;
+  // split-K: work unit u = (tile u / splits, K slice u % splits); slices are non-empty by construction
+  // (host side), partial sums go to the f32 workspace through atomics
+  const int kps = (kbs + splits - 1) / splits;
+  const int num_units = num_tiles * splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < CF::kStages; ++s) {
@@ -108,11 +125,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t issued = 0;  // bit s: stage s has a fill in flight of parity (ph_of_fill[s])
       uint32_t fill_par = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int t = u / splits, sp = u % splits;
         const int b = t / per_batch, r = t % per_batch;
         int m_blk, n_blk;
         tile_coords(r, mb, nb, &m_blk, &n_blk);
-        for (int kb = 0; kb < kbs; ++kb) {
+        const int kb1 = min(kbs, (sp + 1) * kps);
+        for (int kb = sp * kps; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, kErrTimeoutEmpty, &g_tc_error_gemm)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], CF::kStage);
           uint8_t* sa = smem + s * CF::kStage;
@@ -145,13 +164,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t ph = 0;
       int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
         const int a = local & 1;
         const uint32_t aph = (local >> 1) & 1;
         if (!mbar_wait(&acc_empty[a], aph ^ 1, kErrTimeoutAccEmpty, &g_tc_error_gemm)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + a * BN;
-        for (int kb = 0; kb < kbs; ++kb) {
+        const int sp = u % splits, kb0 = sp * kps, kb1 = min(kbs, (sp + 1) * kps);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[s], ph, kErrTimeoutFull, &g_tc_error_gemm)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + s * CF::kStage);
@@ -159,7 +179,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             mma_f16_ss(d, AMN ? sw128_mn_desc_lbo(a_addr + k * 2048, 8192) : sw128_desc(a_addr + k * 32),
-                       BMN ? sw128_mn_desc_lbo(b_addr + k * 2048, 8192) : sw128_desc(b_addr + k * 32), idesc, (kb | k) != 0);
+                       BMN ? sw128_mn_desc_lbo(b_addr + k * 2048, 8192) : sw128_desc(b_addr + k * 32), idesc,
+                       ((kb - kb0) | k) != 0);
           mma_commit(&empty[s]);
           if (++s == CF::kStages) { s = 0; ph ^= 1; }
         }
@@ -170,7 +191,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
     int local = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
+      const int t = u / splits;
       const int a = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       if (!mbar_wait_warp(&acc_full[a], aph, kErrTimeoutAcc, &g_tc_error_gemm)) break;
@@ -186,6 +208,41 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       // memory and writes them row by row, coalesced, with bounds checks
       const bool aligned = OUT == 0 ? (N & 3) == 0 : (N & 7) == 0;
       float* stage = stage_base + (warp - 2) * 32 * 33;
+      if (tma_store) {
+        // 128-byte rows (32 f32 or 64 16-bit columns) into a 128-byte-swizzled 32-row box, written out
+        // by one TMA store per chunk (full-line writes; M / N tails clipped by the tensor map)
+        uint8_t* box = (uint8_t*)stage_base + (warp - 2) * 4096;
+        constexpr int CW = OUT == 0 ? 32 : 64;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += CW) {
+          uint32_t v[CW];
+#pragma unroll
+          for (int j = 0; j < CW; j += 16) tmem_ld16(taddr + c + j, *reinterpret_cast<uint32_t(*)[16]>(v + j));
+          tmem_wait_ld();
+          const int col = n_blk * BN + c;
+          if (col >= N) continue;                      // warp-uniform
+          uint32_t w[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            w[j] = OUT == 0 ? v[j]
+                 : OUT == 1 ? pack_bf16(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]))
+                            : pack_f16(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+          if (lane == 0) bulk_wait_read0();            // the previous store has read the box
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *(uint4*)(box + lane * 128 + ((i ^ (lane & 7)) << 4)) = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmC, box, col, m_blk * BM + q * 32, b);
+            bulk_commit();
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[a]);
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t v[32];
@@ -194,7 +251,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         tmem_wait_ld();
         const int col = n_blk * BN + c;
         if (col >= N) continue;                        // warp-uniform
-        if (aligned && col + 32 <= N) {
+        if (splits > 1) {
+          // partial sum of one K slice: f32 atomics into the workspace, coalesced through the stage
+#pragma unroll
+          for (int j = 0; j < 32; ++j) stage[lane * 33 + j] = __uint_as_float(v[j]);
+          __syncwarp();
+          const int gcol = col + lane;
+#pragma unroll 4
+          for (int rr = 0; rr < 32; ++rr) {
+            const int grow = m_blk * BM + q * 32 + rr;
+            if (grow < M && gcol < N) atomicAdd(ws + ((long long)b * M + grow) * (long long)N + gcol, stage[rr * 33 + lane]);
+          }
+          __syncwarp();
+        } else if (aligned && col + 32 <= N) {
           if (row < M) {
             if (OUT == 0) {
               float* out = (float*)C + crow + col;
@@ -236,6 +305,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       mbar_arrive(&acc_empty[a]);
     }
   }
+  if (warp >= 2 && lane == 0) bulk_wait_all();    // TMA stores complete before the CTA's smem goes away
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -348,6 +418,22 @@ bool MakeOperandMapMN(CUtensorMap* map, const void* ptr, int K, long long ld, in
   return r == CUDA_SUCCESS;
 }
 
+// 3-D output map for the TMA-store epilogue: dims {N, M, batch}, box {128 bytes of columns, 32 rows, 1},
+// 128-byte swizzle.  Rows must be 16-byte multiples.
+bool MakeOutputMap(CUtensorMap* map, void* C, int M, int N, int batch, int out) {
+  EncodeTiledFn enc = GetEncodeTiled();
+  if (!enc) return false;
+  const int esz = out == 0 ? 4 : 2;
+  cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)N * esz, (cuuint64_t)N * esz * M};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / esz), 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUtensorMapDataType t = out == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : out == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(map, t, 3, C, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int NumSMs() {
   int dev = 0, n = 148;
   cudaGetDevice(&dev);
@@ -357,7 +443,7 @@ int NumSMs() {
 
 template <int BN, int OUT, bool AMN, bool BMN>
 static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, void* C, int batch, int M, int N, int K,
-                    int fmt, cudaStream_t st) {
+                    int fmt, cudaStream_t st, int splits, float* ws) {
   using CF = Cfg<BN>;
   static std::once_flag once[8];
   int dev = 0;
@@ -365,23 +451,34 @@ static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, 
   std::call_once(once[dev & 7], [] {
     cudaFuncSetAttribute(gemm_tc_kernel<BN, OUT, AMN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kSmem);
   });
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tc;
   bool ok = AMN ? MakeOperandMapMN(&ta, A, K, lda, M, batch, fmt == 0) : MakeOperandMap(&ta, A, K, lda, M, batch, BM, fmt == 0);
   ok = ok && (BMN ? MakeOperandMapMN(&tb, B, K, ldb, N, batch, fmt == 0) : MakeOperandMap(&tb, B, K, ldb, N, batch, BN, fmt == 0));
   if (!ok) return -2;
+  // TMA-store epilogue when C's rows are 16-byte multiples (else the bounds-checked staged path)
+  const int esz = OUT == 0 ? 4 : 2;
+  int tma_store = splits == 1 && ((long long)N * esz) % 16 == 0 && ((uintptr_t)C % 16) == 0 && !getenv("B200_GEMM_NO_TMA_STORE");
+  if (tma_store) tma_store = MakeOutputMap(&tc, C, M, N, batch, OUT);
+  if (!tma_store) tc = ta;                                  // unused
   int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
-  int grid = std::min(tiles, NumSMs());
-  gemm_tc_kernel<BN, OUT, AMN, BMN><<<grid, 192, CF::kSmem, st>>>(ta, tb, C, M, N, K, batch, fmt);
+  int grid = std::min(tiles * splits, NumSMs());
+  gemm_tc_kernel<BN, OUT, AMN, BMN><<<grid, 192, CF::kSmem, st>>>(ta, tb, tc, C, M, N, K, batch, fmt, splits, ws, tma_store);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
 template <int BN, int OUT>
 static int LaunchTcMajor(bool amn, bool bmn, const void* A, long long lda, const void* B, long long ldb, void* C, int batch,
-                         int M, int N, int K, int fmt, cudaStream_t st) {
-  if (amn && bmn) return LaunchTc<BN, OUT, true, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st);
-  if (amn) return LaunchTc<BN, OUT, true, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st);
-  if (bmn) return LaunchTc<BN, OUT, false, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st);
-  return LaunchTc<BN, OUT, false, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st);
+                         int M, int N, int K, int fmt, cudaStream_t st, int splits, float* ws) {
+  if (amn && bmn) return LaunchTc<BN, OUT, true, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws);
+  if (amn) return LaunchTc<BN, OUT, true, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws);
+  if (bmn) return LaunchTc<BN, OUT, false, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws);
+  return LaunchTc<BN, OUT, false, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws);
+}
+
+__global__ void __launch_bounds__(256) ws_to_16bit_kernel(const float* __restrict__ ws, uint16_t* __restrict__ c, long long n,
+                                                           int f16) {
+  for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < n; i += (long long)gridDim.x * 256)
+    c[i] = (uint16_t)((f16 ? pack_f16(ws[i], 0.f) : pack_bf16(ws[i], 0.f)) & 0xffff);
 }
 
 template <typename T, bool AMN, bool BMN>
@@ -412,8 +509,35 @@ int TakeGemmError() {
 
 // C[b] = A[b] . B[b]^T.  A is [batch, M, >=K] (K-major, row pitch lda) or, with a_mn, [batch, K, >=M]
 // (MN-major, pitch lda); B likewise with N, ldb and b_mn.
+// K slices for a tensor-core GEMM: 1 when the output tiles fill the SMs well; otherwise the smallest
+// count (at most 8, each slice >= 4 K blocks) whose work units fill at least 85 % of the waves they
+// need.  Shared by the compiler (which sizes the workspace) and the launcher.
+int GemmSplitK(int64_t batch, int64_t M, int64_t N, int64_t K, int sms) {
+  if (std::getenv("B200_GEMM_NO_SPLITK") || K <= 0) return 1;
+  const int64_t bn = N >= 256 ? 256 : 128;
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn) * batch;
+  const int64_t kbs = (K + BK - 1) / BK;
+  auto eff = [&](int64_t s) {
+    const int64_t units = tiles * s;
+    return (double)units / (double)(((units + sms - 1) / sms) * sms);
+  };
+  // splitting pays only when the tiles leave SMs idle and each slice keeps a long K loop (the f32
+  // partials cost a zeroing pass and atomics)
+  if (eff(1) >= 0.85 || tiles * 2 > sms) return 1;
+  for (int64_t s = 2; s <= 8 && kbs / s >= 16; ++s) {
+    const int64_t kps = (kbs + s - 1) / s;
+    if ((s - 1) * kps >= kbs) continue;          // would leave an empty slice
+    if (eff(s) >= 0.85) return (int)s;
+  }
+  return 1;
+}
+
+// C[b] = A[b] . B[b]^T.  A is [batch, M, >=K] (K-major, row pitch lda) or, with a_mn, [batch, K, >=M]
+// (MN-major, pitch lda); B likewise with N, ldb and b_mn.  With `ws` (batch*M*N f32) a 16-bit result
+// may be computed split-K (partials added into ws, then rounded into C); an f32 result splits without
+// it (partials added into C).
 int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C, int64_t batch, int64_t M,
-         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st) {
+         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st, float* ws) {
   if (batch <= 0 || M <= 0 || N <= 0) return 0;
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || batch > 65535 || lda < (a_mn ? M : K) || ldb < (b_mn ? N : K))
     return -1;
@@ -429,14 +553,27 @@ int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, 
     int fmt = ab_type == B200_DT_BF16 ? 1 : 0;
     bool wide = N >= 256;
     int b = (int)batch, m = (int)M, n = (int)N, k = (int)K;
+    int splits = GemmSplitK(batch, M, N, K, NumSMs());
+    float* acc = out == 0 ? (float*)C : ws;
+    if (splits > 1 && !acc) splits = 1;
+    if (splits > 1 && cudaMemsetAsync(acc, 0, (size_t)batch * M * N * 4, st) != cudaSuccess) return -3;
+    int rc;
     if (out == 0)
-      return wide ? LaunchTcMajor<256, 0>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st)
-                  : LaunchTcMajor<128, 0>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st);
-    if (out == 1)
-      return wide ? LaunchTcMajor<256, 1>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st)
-                  : LaunchTcMajor<128, 1>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st);
-    return wide ? LaunchTcMajor<256, 2>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st)
-                : LaunchTcMajor<128, 2>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st);
+      rc = wide ? LaunchTcMajor<256, 0>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc)
+                : LaunchTcMajor<128, 0>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc);
+    else if (out == 1)
+      rc = wide ? LaunchTcMajor<256, 1>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc)
+                : LaunchTcMajor<128, 1>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc);
+    else
+      rc = wide ? LaunchTcMajor<256, 2>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc)
+                : LaunchTcMajor<128, 2>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc);
+    if (rc == 0 && splits > 1 && out != 0) {
+      const long long total = (long long)batch * M * N;
+      ws_to_16bit_kernel<<<(unsigned)std::min<long long>((total + 255) / 256, 148 * 8), 256, 0, st>>>(acc, (uint16_t*)C, total,
+                                                                                                     out == 2);
+      rc = cudaGetLastError() == cudaSuccess ? 0 : -3;
+    }
+    return rc;
   }
   int b = (int)batch, m = (int)M, n = (int)N, k = (int)K;
   if (ab_type == B200_DT_F32) return LaunchSimt<float>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, out, st);
@@ -445,9 +582,14 @@ int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, 
   return -1;
 }
 
+int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C, int64_t batch, int64_t M,
+         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st) {
+  return Gemm(A, lda, a_mn, B, ldb, b_mn, C, batch, M, N, K, ab_type, out_type, st, nullptr);
+}
+
 int Gemm(const void* A, long long lda, const void* B, long long ldb, void* C, int64_t batch, int64_t M, int64_t N,
          int64_t K, int ab_type, int out_type, cudaStream_t st) {
-  return Gemm(A, lda, false, B, ldb, false, C, batch, M, N, K, ab_type, out_type, st);
+  return Gemm(A, lda, false, B, ldb, false, C, batch, M, N, K, ab_type, out_type, st, nullptr);
 }
 
 }  // namespace b200k

@@ -141,15 +141,23 @@ def run_gemm(a, world, rank, local):
     flush = torch.empty(64 * 1024 * 1024, device="cuda")
     pk, src = _peaks()
     rows = []
-    for batch, n, ab in [(1, 1024, 13), (1, 4096, 13), (1, 8192, 13), (16, 2048, 13), (1, 1024, 11), (1, 4096, 11),
-                         (1, 8192, 11)]:
-        if getattr(a, "only", "") and a.only != f"b{batch}-{n}-{'bf16' if ab == 13 else 'f32'}":
+    shapes = [(1, 1024, 13), (1, 4096, 13), (1, 8192, 13), (16, 2048, 13), (1, 1024, 11), (1, 4096, 11), (1, 8192, 11)]
+    only = getattr(a, "only", "")
+    custom = None
+    if only.startswith("m"):                      # e.g. m8192n3072k768: one rectangular bf16 shape
+        import re
+        mm = re.fullmatch(r"m(\d+)n(\d+)k(\d+)", only)
+        custom = tuple(int(x) for x in mm.groups())
+        shapes = [(1, custom, 13)]
+    for batch, n, ab in shapes:
+        if only and custom is None and only != f"b{batch}-{n}-{'bf16' if ab == 13 else 'f32'}":
             continue
+        M, N, K = n if custom else (n, n, n)
         dt = torch.bfloat16 if ab == 13 else torch.float32
-        A = (torch.randn(batch, n, n, device="cuda") / math.sqrt(n)).to(dt)
-        B = (torch.randn(batch, n, n, device="cuda") / math.sqrt(n)).to(dt)
-        C = torch.empty(batch, n, n, device="cuda")
-        f = lambda: lib.b200_gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), batch, n, n, n, ab, 11,
+        A = (torch.randn(batch, M, K, device="cuda") / math.sqrt(K)).to(dt)
+        B = (torch.randn(batch, N, K, device="cuda") / math.sqrt(K)).to(dt)
+        C = torch.empty(batch, M, N, device="cuda")
+        f = lambda: lib.b200_gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), batch, M, N, K, ab, 11,
                                   ctypes.c_void_p(st.cuda_stream))
         for _ in range(a.warmup):
             f()
@@ -163,9 +171,9 @@ def run_gemm(a, world, rank, local):
             e1.synchronize()
             ts.append(e0.elapsed_time(e1))
         ms = sorted(ts)[len(ts) // 2]
-        tf = 2.0 * batch * n ** 3 / (ms * 1e-3) / 1e12
-        rows.append({"batch": batch, "M=N=K": n, "inputs": "bf16" if ab == 13 else "f32", "ms": round(ms, 4),
-                     "tflops": round(tf, 1), "frac_of_peak": round(tf / pk["bf16_tflops"], 3)})
+        tf = 2.0 * batch * M * N * K / (ms * 1e-3) / 1e12
+        rows.append({"batch": batch, "M=N=K": n if not custom else f"{M}x{N}x{K}", "inputs": "bf16" if ab == 13 else "f32",
+                     "ms": round(ms, 4), "tflops": round(tf, 1), "frac_of_peak": round(tf / pk["bf16_tflops"], 3)})
         del A, B, C
     heads = [r for r in rows if r["M=N=K"] == 8192 and r["inputs"] == "bf16"]
     head = heads[0] if heads else rows[0]

@@ -179,3 +179,19 @@ def test_attention_backward_vs_autograd(lib, cuda, B, H, S, causal):
     for got, ref, name in ((dq, rdq, "dq"), (dk, rdk, "dk"), (dv, rdv, "dv")):
         e = rel_err(got.float().cpu().numpy(), ref.cpu().numpy())
         assert e <= RTOL_BF16, (name, e)
+
+
+@pytest.mark.parametrize("batch,M,N,K", [(1, 256, 384, 8192), (2, 640, 768, 4096), (1, 768, 768, 8192)])
+def test_gemm_split_k_f32(lib, cuda, batch, M, N, K):
+    """Few output tiles and a long K: the K range is split across CTAs and the f32 partials are added
+    into C (zeroed first) with atomics."""
+    torch = cuda
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    a = (torch.randn(batch, M, K, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
+    b = torch.randn(batch, N, K, device="cuda", generator=g).to(torch.bfloat16)
+    c = torch.full((batch, M, N), 7.0, device="cuda")
+    assert lib.b200_gemm(a.data_ptr(), b.data_ptr(), c.data_ptr(), batch, M, N, K, BF16, F32, stream(torch)) == 0
+    torch.cuda.synchronize()
+    check_device_error(lib)
+    ref = torch.bmm(a.float(), b.float().transpose(1, 2))
+    assert rel_err(c.cpu().numpy(), ref.cpu().numpy()) <= RTOL_F32 * 10

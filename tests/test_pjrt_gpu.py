@@ -151,6 +151,25 @@ def test_f32_cotangent_feeding_two_dots(client, V):
         assert_close(o, r, 1e-2, name)
 
 
+@pytest.mark.parametrize("splitk", [True, False])
+def test_weight_gradient_dot_split_k(client, splitk, monkeypatch):
+    """dW = x^T dy with a bf16 result: few output tiles, K = 4096 rows, so the compiler gives the dot
+    an f32 split-K workspace (or, disabled, one CTA per tile)."""
+    if not splitk:
+        monkeypatch.setenv("B200_GEMM_NO_SPLITK", "1")
+    b = Builder("jit_dw")
+    x = b.arg((4096, 384), "bf16")
+    dy = b.arg((4096, 512), "bf16")
+    dw = b.dot_general(x, dy, contract=([0], [0]), out_dtype="bf16")
+    text = b.text([dw])
+    rng = np.random.default_rng(3)
+    ins = [(rng.standard_normal((4096, 384)) / 64).astype(ml_dtypes.bfloat16),
+           rng.standard_normal((4096, 512)).astype(ml_dtypes.bfloat16)]
+    got = client.run(text, ins)[0]
+    ref = oracle_run(text, ins)[0]
+    assert_close(np.asarray(got, np.float32), np.asarray(ref, np.float32), RTOL_BF16, "dW")
+
+
 @pytest.mark.parametrize("mn", [True, False])
 def test_batched_dot_mn_major_operands(client, mn, monkeypatch):
     """Batched A^T B with both operands MN-major ([b, K, M] and [b, K, N]) against the oracle, and the
