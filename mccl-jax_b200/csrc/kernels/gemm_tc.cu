@@ -58,6 +58,11 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
                ::"l"(map), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
                : "memory");
 }
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];"
+               ::"l"(map), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
@@ -208,6 +213,34 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       // memory and writes them row by row, coalesced, with bounds checks
       const bool aligned = OUT == 0 ? (N & 3) == 0 : (N & 7) == 0;
       float* stage = stage_base + (warp - 2) * 32 * 33;
+      if (tma_store == 2) {
+        // split-K partial sums: f32 boxes added into the workspace by TMA reduce-add (L2 atomics
+        // on whole lines instead of one per element)
+        uint8_t* box = (uint8_t*)stage_base + (warp - 2) * 4096;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tmem_ld16(taddr + c, *reinterpret_cast<uint32_t(*)[16]>(v));
+          tmem_ld16(taddr + c + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
+          tmem_wait_ld();
+          const int col = n_blk * BN + c;
+          if (col >= N) continue;                      // warp-uniform
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *(uint4*)(box + lane * 128 + ((i ^ (lane & 7)) << 4)) = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_reduce_add_3d(&tmC, box, col, m_blk * BM + q * 32, b);
+            bulk_commit();
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[a]);
+        continue;
+      }
       if (tma_store) {
         // 128-byte rows (32 f32 or 64 16-bit columns) into a 128-byte-swizzled 32-row box, written out
         // by one TMA store per chunk (full-line writes; M / N tails clipped by the tensor map)
@@ -455,10 +488,16 @@ static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, 
   bool ok = AMN ? MakeOperandMapMN(&ta, A, K, lda, M, batch, fmt == 0) : MakeOperandMap(&ta, A, K, lda, M, batch, BM, fmt == 0);
   ok = ok && (BMN ? MakeOperandMapMN(&tb, B, K, ldb, N, batch, fmt == 0) : MakeOperandMap(&tb, B, K, ldb, N, batch, BN, fmt == 0));
   if (!ok) return -2;
-  // TMA-store epilogue when C's rows are 16-byte multiples (else the bounds-checked staged path)
+  // TMA-store epilogue when C's rows are 16-byte multiples (else the bounds-checked staged path);
+  // split-K partials go to the f32 workspace by TMA reduce-add under the same condition
   const int esz = OUT == 0 ? 4 : 2;
-  int tma_store = splits == 1 && ((long long)N * esz) % 16 == 0 && ((uintptr_t)C % 16) == 0 && !getenv("B200_GEMM_NO_TMA_STORE");
-  if (tma_store) tma_store = MakeOutputMap(&tc, C, M, N, batch, OUT);
+  int tma_store = 0;
+  if (!getenv("B200_GEMM_NO_TMA_STORE")) {
+    if (splits == 1 && ((long long)N * esz) % 16 == 0 && ((uintptr_t)C % 16) == 0)
+      tma_store = MakeOutputMap(&tc, C, M, N, batch, OUT) ? 1 : 0;
+    else if (splits > 1 && ((long long)N * 4) % 16 == 0 && ((uintptr_t)ws % 16) == 0)
+      tma_store = MakeOutputMap(&tc, ws, M, N, batch, 0) ? 2 : 0;
+  }
   if (!tma_store) tc = ta;                                  // unused
   int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
   int grid = std::min(tiles * splits, NumSMs());
