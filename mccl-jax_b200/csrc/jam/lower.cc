@@ -620,6 +620,7 @@ class Lowerer {
     BindLeaves();
     EmitSteps();
     BindOutputs();
+    MarkAsyncCollectives();
     ComputeLastUse();
     EndKernel();
     p_->cuda_prelude = kPrelude;
@@ -1333,9 +1334,31 @@ class Lowerer {
       row = cand;
       return true;
     };
+    // Collectives are issued as soon as their operand exists (the reference hoists them too,
+    // src/jam/lower.mm:438-458): a gradient's all_reduce then overlaps the rest of the backward pass.
+    std::vector<std::pair<int, Op*>> hoist;   // (index of the operand's producer, collective)
+    std::unordered_set<const Op*> hoisted;
+    if (opt_.num_processes > 1 && !std::getenv("B200_NO_HOIST")) {
+      for (auto& opp : g_.ops) {
+        Op* op = opp.get();
+        if (dead_[op->index] || !(op->name == "all_reduce" || op->name == "all_gather" || op->name == "reduce_scatter")) continue;
+        if (op->operands.size() != 1) continue;
+        const Value* x = Resolve(op->operands[0]);
+        hoist.push_back({x->def ? x->def->index : -1, op});
+      }
+    }
+    size_t next_hoist = 0;
+    std::sort(hoist.begin(), hoist.end(), [](const auto& a, const auto& b) { return a.first < b.first; });
     for (auto& opp : g_.ops) {
       Op* op = opp.get();
-      if (dead_[op->index]) continue;
+      while (next_hoist < hoist.size() && hoist[next_hoist].first < op->index) {
+        Op* c = hoist[next_hoist++].second;
+        if (c->index <= op->index || hoisted.count(c)) continue;
+        flush();
+        EmitCollective(c);
+        hoisted.insert(c);
+      }
+      if (dead_[op->index] || hoisted.count(op)) continue;
       const std::string& n = op->name;
       if (IsAlias(op)) {
         for (size_t k = 0; k < op->results.size(); ++k) {
@@ -2504,6 +2527,44 @@ class Lowerer {
     }
   }
 
+  // slots a step reads
+  static std::vector<int> StepReads(const Step& st) {
+    std::vector<int> r;
+    switch (st.kind) {
+      case StepKind::kFusion:
+        for (auto& L : st.launches) r.insert(r.end(), L.in_slots.begin(), L.in_slots.end());
+        break;
+      case StepKind::kGemm: r = {st.gemm.a, st.gemm.b}; break;
+      case StepKind::kAttention: r = {st.attn.q, st.attn.k, st.attn.v}; break;
+      case StepKind::kAttentionBwd: r = {st.bwd.q, st.bwd.k, st.bwd.v, st.bwd.o, st.bwd.dout, st.bwd.lse}; break;
+      case StepKind::kScatterAdd: r = {st.scatter.base, st.scatter.idx, st.scatter.upd}; break;
+      case StepKind::kCollective: r = {st.coll.in}; break;
+      case StepKind::kCopy: r = {st.copy.src}; break;
+    }
+    return r;
+  }
+  // Collectives of a multi-process program run on the communication stream; the first step that
+  // reads a collective's result waits for it (later readers are ordered behind that step).
+  std::vector<int> coll_until_;   // step index -> step that waits for it (async collectives)
+  void MarkAsyncCollectives() {
+    coll_until_.assign(p_->steps.size(), -1);
+    if (opt_.num_processes <= 1 || std::getenv("B200_SYNC_COLLECTIVES")) return;
+    for (int k = 0; k < (int)p_->steps.size(); ++k) {
+      Step& c = p_->steps[k];
+      if (c.kind != StepKind::kCollective) continue;
+      c.async = true;
+      for (int j = k + 1; j < (int)p_->steps.size(); ++j) {
+        const std::vector<int> rd = StepReads(p_->steps[j]);
+        if (std::find(rd.begin(), rd.end(), c.coll.out) != rd.end()) {
+          p_->steps[j].wait_coll.push_back(k);
+          coll_until_[k] = j;
+          break;
+        }
+      }
+      if (coll_until_[k] < 0) coll_until_[k] = (int)p_->steps.size() - 1;   // waited for at the end
+    }
+  }
+
   void ComputeLastUse() {
     auto touch = [&](int s, int i) { if (s >= 0) p_->slots[s].last_use = std::max(p_->slots[s].last_use, i); };
     for (int i = 0; i < (int)p_->steps.size(); ++i) {
@@ -2526,7 +2587,13 @@ class Lowerer {
             touch(s, i);
           break;
         case StepKind::kScatterAdd: touch(st.scatter.base, i); touch(st.scatter.idx, i); touch(st.scatter.upd, i); touch(st.scatter.out, i); break;
-        case StepKind::kCollective: touch(st.coll.in, i); touch(st.coll.out, i); break;
+        case StepKind::kCollective: {
+          // an overlapped collective keeps its buffers until the step that waits for it
+          const int until = st.async && i < (int)coll_until_.size() ? std::max(i, coll_until_[i]) : i;
+          touch(st.coll.in, until);
+          touch(st.coll.out, until);
+          break;
+        }
         case StepKind::kCopy: touch(st.copy.src, i); touch(st.copy.dst, i); break;
       }
     }

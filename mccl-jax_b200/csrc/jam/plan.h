@@ -95,6 +95,8 @@ struct Step {
   ScatterStep scatter;
   CollectiveStep coll;
   CopyStep copy;
+  bool async = false;                // kCollective: runs on the communication stream
+  std::vector<int> wait_coll;        // async collective steps that must finish before this step
   std::string label;                 // for dumps / timing
 };
 

@@ -284,8 +284,15 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     cudaEventRecord(evs[0], st);
   }
   const Driver& drv = Drv();
+  std::vector<cudaEvent_t> coll_done(P.steps.size(), nullptr);   // async collectives in flight
+  auto release_events = [&]() {
+    for (auto& e : coll_done)
+      if (e) { cudaEventDestroy(e); e = nullptr; }
+  };
   for (size_t i = 0; i < P.steps.size(); ++i) {
     const Step& S = P.steps[i];
+    for (int k : S.wait_coll)
+      if (coll_done[k]) cudaStreamWaitEvent(st, coll_done[k], 0);
     switch (S.kind) {
       case StepKind::kFusion: {
         for (const Launch& L : S.launches) {
@@ -352,10 +359,26 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
         const CollectiveStep& c = S.coll;
         for (int q : {c.in, c.out}) { err = slot(q); if (!err.empty()) return fail(err); }
         if (!comm) return fail("collective in a single-process program without a communicator");
-        if (c.op == CollKind::kAllReduce) err = comm->AllReduce(ptr[c.in], ptr[c.out], c.send_count, c.dt, c.reduce, st);
-        else if (c.op == CollKind::kAllGather) err = comm->AllGather(ptr[c.in], ptr[c.out], c.send_count, c.dt, st);
-        else err = comm->ReduceScatter(ptr[c.in], ptr[c.out], c.recv_count, c.dt, c.reduce, st);
-        if (!err.empty()) return fail(err);
+        cudaStream_t cs = st;
+        if (S.async) {
+          // on the communication stream, after everything enqueued so far on the compute stream
+          if (!dev.comm_stream && cudaStreamCreateWithFlags(&dev.comm_stream, cudaStreamNonBlocking) != cudaSuccess)
+            return fail("cannot create the communication stream");
+          cudaEvent_t ready;
+          cudaEventCreateWithFlags(&ready, cudaEventDisableTiming);
+          cudaEventRecord(ready, st);
+          cudaStreamWaitEvent(dev.comm_stream, ready, 0);
+          cudaEventDestroy(ready);
+          cs = dev.comm_stream;
+        }
+        if (c.op == CollKind::kAllReduce) err = comm->AllReduce(ptr[c.in], ptr[c.out], c.send_count, c.dt, c.reduce, cs);
+        else if (c.op == CollKind::kAllGather) err = comm->AllGather(ptr[c.in], ptr[c.out], c.send_count, c.dt, cs);
+        else err = comm->ReduceScatter(ptr[c.in], ptr[c.out], c.recv_count, c.dt, c.reduce, cs);
+        if (!err.empty()) { release_events(); return fail(err); }
+        if (S.async) {
+          cudaEventCreateWithFlags(&coll_done[i], cudaEventDisableTiming);
+          cudaEventRecord(coll_done[i], cs);
+        }
         break;
       }
       case StepKind::kCopy: {
@@ -381,6 +404,10 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     outs->push_back(ptr[s]);
     owned[s] = false;
   }
+  // the execution completes on the compute stream only after its collectives
+  for (auto& e : coll_done)
+    if (e) cudaStreamWaitEvent(st, e, 0);
+  release_events();
   for (size_t s = 0; s < P.slots.size(); ++s)
     if (owned[s]) DeviceFree(ptr[s], st);
   ExecTimerMarkEnd(dev.ordinal, st);

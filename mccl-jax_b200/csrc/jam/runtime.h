@@ -25,6 +25,7 @@ class Comm;
 struct DeviceState {
   int ordinal = 0;
   cudaStream_t stream = nullptr;
+  cudaStream_t comm_stream = nullptr;   // collectives overlapped with compute (created on first use)
 };
 
 class Executable {

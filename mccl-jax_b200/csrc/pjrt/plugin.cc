@@ -176,13 +176,18 @@ struct PJRT_Client {
   std::unique_ptr<PJRT_TopologyDescription> topology;
   std::unique_ptr<b200::Comm> comm;
   ~PJRT_Client() {
+    // drain the compute and communication streams before the communicator goes away
+    for (PJRT_Device* d : addressable_devices) {
+      cudaSetDevice(d->state.ordinal);
+      if (d->state.stream) cudaStreamSynchronize(d->state.stream);
+      if (d->state.comm_stream) cudaStreamSynchronize(d->state.comm_stream);
+    }
     comm.reset();
-    for (PJRT_Device* d : addressable_devices)
-      if (d->state.stream) {
-        cudaSetDevice(d->state.ordinal);
-        cudaStreamSynchronize(d->state.stream);
-        cudaStreamDestroy(d->state.stream);
-      }
+    for (PJRT_Device* d : addressable_devices) {
+      cudaSetDevice(d->state.ordinal);
+      if (d->state.stream) cudaStreamDestroy(d->state.stream);
+      if (d->state.comm_stream) cudaStreamDestroy(d->state.comm_stream);
+    }
   }
 };
 
