@@ -1411,7 +1411,8 @@ class Lowerer {
           continue;
         }
         flush();
-        EmitReduce(op);
+        if (op->results.size() == 2) EmitArgReduce(op);
+        else EmitReduce(op);
         continue;
       }
       if (n == "scatter") { flush(); EmitScatter(op); continue; }
@@ -1972,6 +1973,100 @@ class Lowerer {
     p_->steps.push_back(st);
     for (size_t k = 0; k < out_slots.size(); ++k) RecordDt(out_slots[k], out_dts[k]);
     return true;
+  }
+
+  // ---------------------------------------------------------------- argmax / argmin
+  // The two-operand reduce jnp.argmax / argmin emit: (x, iota along the axis) with inits
+  // (-inf | +inf | int extreme, 0) and a reducer whose first comparison is GT (argmax) or LT (argmin),
+  // recognised as the reference's DetectArgReduce does (src/jam/ops/reduce.mm:29-43).  Result: the
+  // extreme value and the smallest index holding it; a NaN counts as the extreme (the first NaN
+  // wins), which is what the jnp reducer body computes when folded in index order.
+  void EmitArgReduce(Op* op) {
+    auto fail = [&]() { throw LowerError{"variadic reduce other than argmax / argmin is not supported"}; };
+    if (op->operands.size() != 4 || op->results.size() != 2) fail();
+    auto rc = op->strs.find("region_compare");
+    if (rc == op->strs.end() || (rc->second != "GT" && rc->second != "LT")) fail();
+    const bool is_max = rc->second == "GT";
+    const std::vector<int64_t> rd = op->ints.at("dimensions");
+    if (rd.size() != 1) fail();
+    const Value* x = op->operands[0];
+    const Value* io = op->operands[1];
+    const int ax = (int)rd[0];
+    if (!io->def || io->def->name != "iota" || io->def->ints.at("dim")[0] != ax || io->type.dims != x->type.dims) fail();
+    double i0 = 0;
+    if (!IsScalarConst(op->operands[3], &i0) || i0 != 0) fail();
+    const DT vdt = x->type.dt, idt = op->results[1]->type.dt;
+    if (!(DTIsFloat(vdt) || DTIsSigned(vdt)) || !(idt == DT::kS32 || idt == DT::kS64)) fail();
+    const bool fl = DTIsFloat(vdt);
+    const DT acc_dt = AccDt(vdt);
+    const std::string at = CType(acc_dt), it = CType(idt);
+    const auto& xd = x->type.dims;
+    std::vector<int64_t> kept;
+    for (int k = 0; k < (int)xd.size(); ++k) if (k != ax) kept.push_back(xd[k]);
+    const int64_t L = xd[ax];
+    int64_t n_out = 1;
+    for (int64_t d : kept) n_out *= d;
+    const bool wide = x->type.numel() >= (1LL << 31);
+    const bool inner = ax == (int)xd.size() - 1;
+    const int out_v = SlotFor(op->results[0]), out_i = SlotFor(op->results[1]);
+    std::string init = InitExpr(op->operands[2], acc_dt);
+    // better(a, b): a NaN beats any number (the smaller index among NaNs), else the larger (smaller)
+    // value, else the smaller index
+    const std::string cmp = is_max ? ">" : "<";
+    std::string better = "static __device__ __forceinline__ bool " + std::string("%FN%_better(") + at + " av, " + it + " ai, " + at +
+                         " bv, " + it + " bi) {\n";
+    if (fl) better += "  if (av != av) return bv == bv || ai < bi;\n  if (bv != bv) return false;\n";
+    better += "  if (av != bv) return av " + cmp + " bv;\n  return ai < bi;\n}\n";
+    Gen gen;
+    gen.slot_of = &slot_of_;
+    gen.indent = "      ";
+    std::ostringstream ob, jb;
+    auto names_k = Delinearize(ob, inner ? "row" : "o", kept, "a", "    ", wide);
+    std::vector<std::string> idx(xd.size());
+    for (int k = 0, q = 0; k < (int)xd.size(); ++k) idx[k] = k == ax ? "j" : names_k[q++];
+    std::string v = gen.Emit(x, idx);
+    std::vector<DT> in_dts;
+    for (int sl : gen.in_slots) in_dts.push_back(SlotDt(sl));
+    std::string fn = KName();
+    size_t pos;
+    while ((pos = better.find("%FN%")) != std::string::npos) better.replace(pos, 4, fn);
+    std::ostringstream k;
+    k << better << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(" << KernelParams(gen.in_slots, 2, false)
+      << ") {\n" << ParamCasts(gen.in_slots, in_dts, {vdt, idt});
+    const std::string scan = "      { const " + at + " cv = (" + at + ")(" + v + "); if (" + fn + "_better(cv, (" + it +
+                             ")j, bv, bi)) { bv = cv; bi = (" + it + ")j; } }\n";
+    Launch Lc;
+    Lc.fn = fn;
+    Lc.in_slots = gen.in_slots;
+    Lc.out_slots = {out_v, out_i};
+    Lc.block = 256;
+    Lc.grid_stride = true;
+    if (inner) {
+      k << "  const int lane = threadIdx.x & 31;\n"
+        << "  for (long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); row < " << n_out << "LL; row += (long long)gridDim.x * 8) {\n"
+        << ob.str() << "    " << at << " bv = " << init << "; " << it << " bi = 0;\n"
+        << "    for (long long j = lane; j < " << L << "LL; j += 32) {\n" << gen.body.str() << scan << "    }\n"
+        << "    for (int o = 16; o; o >>= 1) {\n"
+        << "      const " << at << " ov = __shfl_xor_sync(0xffffffffu, bv, o); const " << it << " oi = __shfl_xor_sync(0xffffffffu, bi, o);\n"
+        << "      if (" << fn << "_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }\n    }\n"
+        << "    if (lane == 0) { out0[row] = " << StoreExpr(vdt, FromAcc(vdt, "bv")) << "; out1[row] = bi; }\n  }\n}\n";
+      Lc.grid_x = std::max<int64_t>(1, (n_out + 7) / 8);
+    } else {
+      k << "  for (long long o = (long long)blockIdx.x * 256 + threadIdx.x; o < " << n_out << "LL; o += (long long)gridDim.x * 256) {\n"
+        << ob.str() << "    " << at << " bv = " << init << "; " << it << " bi = 0;\n"
+        << "    for (long long j = 0; j < " << L << "LL; ++j) {\n" << gen.body.str() << scan << "    }\n"
+        << "    out0[o] = " << StoreExpr(vdt, FromAcc(vdt, "bv")) << "; out1[o] = bi;\n  }\n}\n";
+      Lc.grid_x = std::max<int64_t>(1, (n_out + 255) / 256);
+    }
+    src_ << k.str();
+    EndKernel();
+    Step st;
+    st.kind = StepKind::kFusion;
+    st.launches.push_back(Lc);
+    st.label = std::string(is_max ? "argmax " : "argmin ") + x->type.str();
+    p_->steps.push_back(st);
+    RecordDt(out_v, vdt);
+    RecordDt(out_i, idt);
   }
 
   // ---------------------------------------------------------------- reductions

@@ -414,7 +414,15 @@ class Parser {
   }
 
   static void RegionSummary(OpAst& op, const std::vector<OpAst>& body) {
-    for (const OpAst& b : body) op.region_ops.push_back(b.name);
+    for (const OpAst& b : body) {
+      op.region_ops.push_back(b.name);
+      // the first comparison of a reducer body tells argmax (GT) from argmin (LT), as the
+      // reference's DetectArgReduce reads it (src/jam/ops/reduce.mm:29-43)
+      if (b.name == "stablehlo.compare" && !op.strs.count("region_compare")) {
+        auto it = b.strs.find("comparison_direction");
+        if (it != b.strs.end()) op.strs["region_compare"] = it->second;
+      }
+    }
   }
 
   OpAst Operation() {

@@ -280,6 +280,45 @@ class Builder:
         return self._emit(t, f"{t.name} = stablehlo.reduce({x.name} init: {c.name}) applies stablehlo.{body} across "
                              f"dimensions = {_dims(dims)} : ({x.type}, {c.type}) -> {t.type}")
 
+    def argreduce(self, x, axis, kind="max", index_dtype="i32"):
+        """(max|min over `axis`, its index) as jnp.argmax / argmin lower it: a two-operand reduce of
+        (x, iota) whose reducer keeps the larger (smaller) value, a NaN first, and on ties the smaller
+        index.  Returns the (value, index) pair."""
+        axis %= x.ndim
+        idx = self.iota(x.shape, axis, index_dtype)
+        fl = x.dtype in FLOATS
+        if fl:
+            vinit = -np.inf if kind == "max" else np.inf
+        else:
+            info = np.iinfo(np.dtype({"i8": "int8", "i16": "int16", "i32": "int32", "i64": "int64"}[x.dtype]))
+            vinit = info.min if kind == "max" else info.max
+        cv, ci = self.const(vinit, x.dtype), self.const(0, index_dtype)
+        name = self._fresh()
+        shape = tuple(s for i, s in enumerate(x.shape) if i != axis)
+        tv = T(self, name + "#0", shape, x.dtype, op="argreduce", inputs=(x, idx, cv, ci), attrs={"axis": axis})
+        ti = T(self, name + "#1", shape, index_dtype, op="argreduce", inputs=(x, idx, cv, ci), attrs={"axis": axis})
+        st, it = mlir_type((), x.dtype), mlir_type((), index_dtype)
+        ctype = "FLOAT" if fl else "SIGNED"
+        d = "GT" if kind == "max" else "LT"
+        nan = f"      %n = stablehlo.compare  NE, %a0, %a0,  {ctype} : ({st}, {st}) -> tensor<i1>\n" if fl else ""
+        pick = "stablehlo.or %g, %n" if fl else None
+        body = (f"{name}:2 = stablehlo.reduce({x.name} init: {cv.name}), ({idx.name} init: {ci.name}) across dimensions = "
+                f"[{axis}] : ({x.type}, {idx.type}, {st}, {it}) -> ({tv.type}, {ti.type})\n"
+                f"     reducer(%a0: {st}, %b0: {st}) (%a1: {it}, %b1: {it})  {{\n"
+                f"      %g = stablehlo.compare  {d}, %a0, %b0,  {ctype} : ({st}, {st}) -> tensor<i1>\n" + nan +
+                (f"      %p = {pick} : tensor<i1>\n" if fl else "      %p = stablehlo.or %g, %g : tensor<i1>\n") +
+                f"      %e = stablehlo.compare  EQ, %a0, %b0,  {ctype} : ({st}, {st}) -> tensor<i1>\n"
+                f"      %l = stablehlo.compare  LT, %a1, %b1,  SIGNED : ({it}, {it}) -> tensor<i1>\n"
+                f"      %q = stablehlo.and %e, %l : tensor<i1>\n"
+                f"      %r = stablehlo.or %p, %q : tensor<i1>\n"
+                f"      %v = stablehlo.select %p, %a0, %b0 : tensor<i1>, {st}\n"
+                f"      %w = stablehlo.select %r, %a1, %b1 : tensor<i1>, {it}\n"
+                f"      stablehlo.return %v, %w : {st}, {it}\n"
+                f"    }}")
+        self._emit(tv, body)
+        self.ops.append(ti)                     # second result of the same op (no line of its own)
+        return tv, ti
+
     def sum(self, x, axis, keepdims=False):
         return self._keep(self.reduce(x, _axes(axis, x.ndim), "add"), x, axis, keepdims)
 

@@ -385,7 +385,17 @@ class Interp:
             xs, inits = ins[:k], ins[k:]
             dims = a["dimensions"]
             if k != 1:
-                raise NotImplementedError("variadic reduce")
+                # general reducer body (argmax / argmin as jnp lowers them): fold it over the reduced
+                # positions in index order, accumulator as the left operands, element as the right
+                dims = sorted(dims)
+                flat = [np.moveaxis(x, dims, list(range(len(dims)))) for x in xs]
+                flat = [f.reshape((-1,) + f.shape[len(dims):]) for f in flat]
+                acc = [np.broadcast_to(np.asarray(i), flat[0].shape[1:]).astype(i.dtype) for i in inits]
+                blk = op.regions[0]
+                for j in range(flat[0].shape[0]):
+                    acc = yield from self.block(blk, blk.args, acc + [f[j] for f in flat])
+                    acc = [np.asarray(v) for v in acc]
+                return [_cast(np.asarray(v), t.dtype) for v, t in zip(acc, op.out_types)]
             kind = _reducer_kind(op.regions[0])
             return [_cast(_reduce_np(xs[0], dims, kind, inits[0]), ot.dtype)]
         if n == "stablehlo.gather":
