@@ -21,8 +21,10 @@
 //
 //   warp 0     TMA: K, V once; Q, dO tiles (+ lse2, delta slices) through a two-stage ring
 //   warp 1     TMEM allocation (512 columns) and the single MMA-issuing thread
-//   warps 2-5  P / dS: thread r owns key row r of the tile (TMEM lane r)
-//   warps 6-9  dQ readout and atomics: thread r owns query row r
+//   warps 2-9  P / dS: thread r of warps 2-5 (6-9) owns key row r of the tile (TMEM lane r) for
+//              queries 0-63 (64-127) of the step; each half signals its own barrier so the dV / dK
+//              products on the first half start while the second is still being computed
+//   warps 10-13 dQ readout and atomics: thread r owns query row r
 #include <cuda_bf16.h>
 #include <mutex>
 
@@ -52,8 +54,9 @@ struct BCfg {
   static constexpr int kSmem = kBarOff + 256 + 1024;
 };
 
-enum { kKVFull = 0, kQFull = 1, kQEmpty = 3, kSFull = 5, kSFree = 6, kPdSFull = 7, kPdSFree = 8, kdQFull = 9,
-       kdQFree = 10, kAccFull = 11, kNumBars = 12 };
+enum { kKVFull = 0, kQFull = 1, kQEmpty = 3, kSFull = 5, kSFree = 6, kPdSFull = 7 /* 2: per query half */, kPdSFree = 9,
+       kdQFull = 10, kdQFree = 11, kAccFull = 12, kNumBars = 13 };
+constexpr int kThreads = 14 * 32;   // TMA, MMA, 8 P / dS warps (two query halves), 4 dQ warps
 
 __device__ __forceinline__ float ex2f(float x) {
   float y;
@@ -78,7 +81,7 @@ __device__ __forceinline__ void store_row32(uint8_t* tile, int r, int c0, const 
 }
 
 template <bool CAUSAL>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(kThreads, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                 const float* __restrict__ lse2, const float* __restrict__ delta, float* __restrict__ dq_acc,
@@ -107,8 +110,9 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       mbar_init(&bars[kQEmpty + i], 1);
     }
     mbar_init(&bars[kSFull], 1);
-    mbar_init(&bars[kSFree], 128);
-    mbar_init(&bars[kPdSFull], 128);
+    mbar_init(&bars[kSFree], 256);
+    mbar_init(&bars[kPdSFull + 0], 128);
+    mbar_init(&bars[kPdSFull + 1], 128);
     mbar_init(&bars[kPdSFree], 1);
     mbar_init(&bars[kdQFull], 1);
     mbar_init(&bars[kdQFree], 128);
@@ -173,19 +177,20 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         for (int k = 0; k < HD / 16; ++k)
           mma_f16_ss(tmem + 128, sw128_desc(v_a + k * 32), sw128_desc(do_a + k * 32), id_s, k != 0);
         mma_commit(&bars[kSFull]);
-        if (!(ok = mbar_wait(&bars[kPdSFull], i & 1, kErrTimeoutFull, err))) break;
-        tc_fence_after();
-        // dV += P^T dO and dK += dS^T Q: K = 128 queries in steps of 16 (two 64-query blocks of A)
+        // dV += P^T dO and dK += dS^T Q: K = 128 queries in steps of 16, issued per 64-query half as
+        // soon as that half of P^T / dS^T is in shared memory (the other half is still being written)
+        for (int hh = 0; hh < 2 && ok; ++hh) {
+          if (!(ok = mbar_wait(&bars[kPdSFull + hh], i & 1, kErrTimeoutFull, err))) break;
+          tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < TB / 16; ++k) {
-          const uint32_t off = (k / 4) * (TB * 128) + (k % 4) * 32;
-          mma_f16_ss(tmem + 256, sw128_desc(p_a + off), sw128_mn_desc_lbo(do_a + k * 2048, 8192), id_kv, (i | k) != 0);
+          for (int kk = 0; kk < 4; ++kk) {
+            const int k = hh * 4 + kk;
+            const uint32_t off = hh * (TB * 128) + kk * 32;
+            mma_f16_ss(tmem + 256, sw128_desc(p_a + off), sw128_mn_desc_lbo(do_a + k * 2048, 8192), id_kv, (i | k) != 0);
+            mma_f16_ss(tmem + 320, sw128_desc(ds_a + off), sw128_mn_desc_lbo(q_a + k * 2048, 8192), id_kv, (i | k) != 0);
+          }
         }
-#pragma unroll
-        for (int k = 0; k < TB / 16; ++k) {
-          const uint32_t off = (k / 4) * (TB * 128) + (k % 4) * 32;
-          mma_f16_ss(tmem + 320, sw128_desc(ds_a + off), sw128_mn_desc_lbo(q_a + k * 2048, 8192), id_kv, (i | k) != 0);
-        }
+        if (!ok) break;
         // dQ_t = dS K: A = dS^T read MN-major (queries contiguous; the two 64-query blocks are the
         // 16 KB-apart MN atoms), K = 128 keys in steps of 16 rows
         if (i > 0 && !(ok = mbar_wait(&bars[kdQFree], (i - 1) & 1, kErrTimeoutFull, err))) break;
@@ -200,8 +205,10 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       }
       if (ok) mma_commit(&bars[kAccFull]);
     }
-  } else if (warp < 6) {
+  } else if (warp < 10) {
     // ------------------------------------------------------------------ P / dS (key rows)
+    // warps 2-5 take queries 0-63 of each step, warps 6-9 queries 64-127 (same key rows = TMEM lanes)
+    const int half = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;           // key row in the tile == TMEM lane
     const int key = k0 + r;
@@ -221,7 +228,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       tc_fence_after();
       const bool diag = CAUSAL && q0 == k0;
 #pragma unroll 1
-      for (int c = 0; c < TB; c += 32) {
+      for (int c = half * 64; c < half * 64 + 64; c += 32) {
         uint32_t sv[32], dv[32];
         tmem_ld16(tmem + lane_off + c, *reinterpret_cast<uint32_t(*)[16]>(sv));
         tmem_ld16(tmem + lane_off + c + 16, *reinterpret_cast<uint32_t(*)[16]>(sv + 16));
@@ -248,12 +255,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       tc_fence_before();
       mbar_arrive(&bars[kSFree]);                // S^T / dP^T may be recomputed for the next tile
       fence_async_shared();
-      mbar_arrive(&bars[kPdSFull]);
+      mbar_arrive(&bars[kPdSFull + half]);
     }
     // dV and dK rows of this key tile
     if (ok && mbar_wait_warp(&bars[kAccFull], 0, kErrTimeoutAcc, err)) {
       tc_fence_after();
-      for (int w = 0; w < 2; ++w) {
+      for (int w = half; w < half + 1; ++w) {  // half 0 writes dV, half 1 dK
         __nv_bfloat16* out = (w == 0 ? dV : dK) + (row_base + key) * HD;
         const uint32_t col = tmem + lane_off + 256 + w * 64;
 #pragma unroll
@@ -392,10 +399,10 @@ int AttentionBwd(const void* q, const void* k, const void* v, const void* o, con
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid((unsigned)(B * H * (S / TB)));
   if (causal)
-    attn_bwd_kernel<true><<<grid, 320, C::kSmem, st>>>(mq, mk, mv, mdo, lse2, delta, dq_acc, (__nv_bfloat16*)dk,
+    attn_bwd_kernel<true><<<grid, kThreads, C::kSmem, st>>>(mq, mk, mv, mdo, lse2, delta, dq_acc, (__nv_bfloat16*)dk,
                                                         (__nv_bfloat16*)dv, S, scale, scale_log2);
   else
-    attn_bwd_kernel<false><<<grid, 320, C::kSmem, st>>>(mq, mk, mv, mdo, lse2, delta, dq_acc, (__nv_bfloat16*)dk,
+    attn_bwd_kernel<false><<<grid, kThreads, C::kSmem, st>>>(mq, mk, mv, mdo, lse2, delta, dq_acc, (__nv_bfloat16*)dk,
                                                          (__nv_bfloat16*)dv, S, scale, scale_log2);
   const long long n4 = rows * HD / 4;
   f32_to_bf16_kernel<<<(unsigned)std::min<long long>((n4 + 255) / 256, 148 * 8), 256, 0, st>>>(dq_acc, (__nv_bfloat16*)dq, n4);
