@@ -2229,18 +2229,25 @@ class Lowerer {
       st.launches.push_back(L1);
       if (chunks > 1) {
         std::string fn2 = KName();
+        // second pass: a warp per output, its lanes striding over the chunk partials (independent
+        // loads in flight), then a shuffle tree; one thread per output would wait out one L2
+        // round trip per chunk
         k << "extern \"C\" __global__ void __launch_bounds__(256) " << fn2 << "(const void* __restrict__ p0, void* __restrict__ q0) {\n"
           << "  const " << acc_t << "* part = (const " << acc_t << "*)p0;\n  " << MemType(odt) << "* out0 = (" << MemType(odt) << "*)q0;\n"
-          << "  long long o = (long long)blockIdx.x * 256 + threadIdx.x;\n  if (o >= " << n_out << "LL) return;\n"
-          << "  " << acc_t << " acc = " << init_expr << ";\n"
-          << "  for (int c = 0; c < " << chunks << "; ++c) acc = " << combine("acc", "part[(long long)c * " + std::to_string(n_out) + "LL + o]") << ";\n"
-          << "  out0[o] = " << StoreExpr(odt, FromAcc(odt, "acc")) << ";\n}\n";
+          << "  const int lane = threadIdx.x & 31;\n"
+          << "  for (long long o = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); o < " << n_out << "LL; o += (long long)gridDim.x * 8) {\n"
+          << "    " << acc_t << " acc = (" << acc_t << ")(" << IdentityOf(kind, acc_dt) << ");\n"
+          << "#pragma unroll 4\n"
+          << "    for (int c = lane; c < " << chunks << "; c += 32) acc = " << combine("acc", "part[(long long)c * " + std::to_string(n_out) + "LL + o]") << ";\n"
+          << "  " << shfl_red
+          << "    if (lane == 0) out0[o] = " << StoreExpr(odt, FromAcc(odt, combine(init_expr, "acc"))) << ";\n  }\n}\n";
         Launch L2;
         L2.fn = fn2;
         L2.in_slots = {scratch};
         L2.out_slots = {out_slot};
         L2.block = 256;
-        L2.grid_x = (n_out + 255) / 256;
+        L2.grid_x = std::max<int64_t>(1, (n_out + 7) / 8);
+        L2.grid_stride = true;
         st.launches.push_back(L2);
         RecordDt(scratch, acc_dt);
       }

@@ -94,9 +94,11 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_t = S / TB;
-  // heavy key tiles (early keys see the most queries when causal) first
-  const int kt = (int)(blockIdx.x % n_t);
-  const int bh = (int)(blockIdx.x / n_t);
+  // key-tile-major block order: every (batch, head)'s heaviest key tile (the early keys see the most
+  // queries when causal) is dispatched before any lighter one, so the last wave holds short CTAs
+  const int n_bh = (int)(gridDim.x / n_t);
+  const int kt = (int)(blockIdx.x / n_bh);
+  const int bh = (int)(blockIdx.x % n_bh);
   const int k0 = kt * TB;
   const int qt0 = CAUSAL ? kt : 0;
   const int n_it = n_t - qt0;

@@ -139,9 +139,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qblk = S / (2 * TQ);
-  // heavy (late) query blocks first for the causal case
-  const int qb = CAUSAL ? (n_qblk - 1 - (int)(blockIdx.x % n_qblk)) : (int)(blockIdx.x % n_qblk);
-  const int bh = blockIdx.x / n_qblk;
+  // query-block-major order: for the causal case every (batch, head)'s heaviest (last) query block
+  // is dispatched before any lighter one, so the last wave holds short CTAs
+  const int n_bh = (int)(gridDim.x / n_qblk);
+  const int qi = (int)(blockIdx.x / n_bh);
+  const int qb = CAUSAL ? (n_qblk - 1 - qi) : qi;
+  const int bh = (int)(blockIdx.x % n_bh);
   const int q0 = qb * 2 * TQ;
   const int n_kv = CAUSAL ? (q0 + 2 * TQ) / TK : S / TK;
   const long long row_base = (long long)bh * S;  // row of (bh, 0) in the [B*H*S, D] views
