@@ -2518,11 +2518,9 @@ class Lowerer {
     const int64_t rows = (int64_t)a.B * a.H * a.S;
     b.dq_acc = NewSlot(rows * a.D * 4);
     b.delta = NewSlot(rows * 4);
-    b.dk_t = m.dk_t;
-    if (m.dk_t) b.dk_tmp = NewSlot(rows * a.D * 2);
+    b.dk_t = m.dk_t;                             // the kernel writes dK in the dot's [B, H, D, S] layout
     for (int s : {b.dq, b.dk, b.dv}) RecordDt(s, DT::kBF16);
     for (int s : {b.dq_acc, b.delta}) RecordDt(s, DT::kF32);
-    if (b.dk_tmp >= 0) RecordDt(b.dk_tmp, DT::kBF16);
     Step st;
     st.kind = StepKind::kAttentionBwd;
     st.bwd = b;
@@ -2685,7 +2683,7 @@ class Lowerer {
           break;
         case StepKind::kAttentionBwd:
           for (int s : {st.bwd.q, st.bwd.k, st.bwd.v, st.bwd.o, st.bwd.dout, st.bwd.lse, st.bwd.dq, st.bwd.dk, st.bwd.dv,
-                        st.bwd.dq_acc, st.bwd.delta, st.bwd.dk_tmp})
+                        st.bwd.dq_acc, st.bwd.delta})
             touch(s, i);
           break;
         case StepKind::kScatterAdd: touch(st.scatter.base, i); touch(st.scatter.idx, i); touch(st.scatter.upd, i); touch(st.scatter.out, i); break;

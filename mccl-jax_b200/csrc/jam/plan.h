@@ -58,7 +58,7 @@ struct AttentionStep {
 struct AttentionBwdStep {
   int q = -1, k = -1, v = -1, o = -1, dout = -1, lse = -1;   // inputs, [B,H,S,D] bf16 (lse [B*H*S] f32)
   int dq = -1, dk = -1, dv = -1;                            // outputs bf16; dk is [B,H,D,S] when dk_t
-  int dq_acc = -1, delta = -1, dk_tmp = -1;                 // scratch
+  int dq_acc = -1, delta = -1;                 // scratch
   bool dk_t = false;
   int B = 0, H = 0, S = 0, D = 0;
   bool causal = false;

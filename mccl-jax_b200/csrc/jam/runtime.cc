@@ -25,8 +25,7 @@ int AttentionFwdLse(const void* q, const void* k, const void* v, void* o, float*
                     int causal, float scale, cudaStream_t st);
 int AttentionBwd(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse2,
                  void* dq, void* dk, void* dv, float* dq_acc, float* delta, int B, int H, int S, int D, int causal,
-                 float scale, cudaStream_t st);
-int TransposeRowsCols(const void* x, void* y, int n, int R, int C, cudaStream_t st);
+                 float scale, cudaStream_t st, int dk_t);
 }
 
 namespace b200 {
@@ -333,15 +332,13 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
       }
       case StepKind::kAttentionBwd: {
         const AttentionBwdStep& b = S.bwd;
-        for (int s : {b.q, b.k, b.v, b.o, b.dout, b.lse, b.dq, b.dk, b.dv, b.dq_acc, b.delta, b.dk_tmp}) {
+        for (int s : {b.q, b.k, b.v, b.o, b.dout, b.lse, b.dq, b.dk, b.dv, b.dq_acc, b.delta}) {
           err = slot(s);
           if (!err.empty()) return fail(err);
         }
-        void* dk = b.dk_t ? ptr[b.dk_tmp] : ptr[b.dk];
-        int rc = b200k::AttentionBwd(ptr[b.q], ptr[b.k], ptr[b.v], ptr[b.o], ptr[b.dout], (const float*)ptr[b.lse], ptr[b.dq], dk,
-                                     ptr[b.dv], (float*)ptr[b.dq_acc], (float*)ptr[b.delta], b.B, b.H, b.S, b.D, b.causal,
-                                     b.scale, st);
-        if (rc == 0 && b.dk_t) rc = b200k::TransposeRowsCols(dk, ptr[b.dk], b.B * b.H, b.S, b.D, st);
+        int rc = b200k::AttentionBwd(ptr[b.q], ptr[b.k], ptr[b.v], ptr[b.o], ptr[b.dout], (const float*)ptr[b.lse], ptr[b.dq],
+                                     ptr[b.dk], ptr[b.dv], (float*)ptr[b.dq_acc], (float*)ptr[b.delta], b.B, b.H, b.S, b.D,
+                                     b.causal, b.scale, st, b.dk_t ? 1 : 0);
         if (rc != 0) return fail("attention backward launch failed (" + std::to_string(rc) + ")");
         break;
       }

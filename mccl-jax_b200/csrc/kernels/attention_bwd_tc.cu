@@ -85,7 +85,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                 const float* __restrict__ lse2, const float* __restrict__ delta, float* __restrict__ dq_acc,
-                __nv_bfloat16* __restrict__ dK, __nv_bfloat16* __restrict__ dV, int S, float scale, float scale_log2) {
+                __nv_bfloat16* __restrict__ dK, __nv_bfloat16* __restrict__ dV, int S, float scale, float scale_log2,
+                int dk_t) {
   using C = BCfg;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -265,6 +266,20 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       for (int w = half; w < half + 1; ++w) {  // half 0 writes dV, half 1 dK
         __nv_bfloat16* out = (w == 0 ? dV : dK) + (row_base + key) * HD;
         const uint32_t col = tmem + lane_off + 256 + w * 64;
+        if (w == 1 && dk_t) {
+          // dK as [B*H, D, S] (the layout a dot_general(Q, dS) result has): for each d the warp's 32
+          // consecutive keys form one 64-byte store
+          __nv_bfloat16* outt = dK + (long long)bh * HD * S + key;
+#pragma unroll 1
+          for (int c = 0; c < HD; c += 16) {
+            uint32_t v[16];
+            tmem_ld16(col + c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) outt[(long long)(c + e) * S] = __float2bfloat16_rn(__uint_as_float(v[e]));
+          }
+          continue;
+        }
 #pragma unroll
         for (int c = 0; c < HD; c += 16) {
           uint32_t v[16];
@@ -336,20 +351,6 @@ __global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* __restric
   }
 }
 
-// [n, R, C] -> [n, C, R] bf16 through 32 x 32 shared-memory tiles (dK for a caller that wants it
-// head-dim-major).
-__global__ void __launch_bounds__(256) transpose_rc_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int R, int C) {
-  __shared__ uint16_t tile[32][34];
-  const long long base = (long long)blockIdx.z * R * C;
-  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  for (int j = ty; j < 32; j += 8)
-    if (r0 + j < R && c0 + tx < C) tile[j][tx] = x[base + (long long)(r0 + j) * C + c0 + tx];
-  __syncthreads();
-  for (int j = ty; j < 32; j += 8)
-    if (c0 + j < C && r0 + tx < R) y[base + (long long)(c0 + j) * R + r0 + tx] = tile[tx][j];
-}
-
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -376,9 +377,10 @@ bool AttentionBwdShapeOk(int B, int H, int S, int D) {
 }
 
 // Scratch: dq_acc (B*H*S*D f32) and delta (B*H*S f32), caller-owned.  Allocates nothing.
+// dk_t: dK is written as [B, H, D, S] instead of [B, H, S, D].
 int AttentionBwd(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse2,
                  void* dq, void* dk, void* dv, float* dq_acc, float* delta, int B, int H, int S, int D, int causal,
-                 float scale, cudaStream_t st) {
+                 float scale, cudaStream_t st, int dk_t = 0) {
   if (!AttentionBwdShapeOk(B, H, S, D)) return -1;
   if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)o | (uintptr_t)dout | (uintptr_t)dq | (uintptr_t)dk |
        (uintptr_t)dv | (uintptr_t)lse2 | (uintptr_t)dq_acc | (uintptr_t)delta) % 16)
@@ -402,19 +404,12 @@ int AttentionBwd(const void* q, const void* k, const void* v, const void* o, con
   dim3 grid((unsigned)(B * H * (S / TB)));
   if (causal)
     attn_bwd_kernel<true><<<grid, kThreads, C::kSmem, st>>>(mq, mk, mv, mdo, lse2, delta, dq_acc, (__nv_bfloat16*)dk,
-                                                        (__nv_bfloat16*)dv, S, scale, scale_log2);
+                                                        (__nv_bfloat16*)dv, S, scale, scale_log2, dk_t);
   else
     attn_bwd_kernel<false><<<grid, kThreads, C::kSmem, st>>>(mq, mk, mv, mdo, lse2, delta, dq_acc, (__nv_bfloat16*)dk,
-                                                         (__nv_bfloat16*)dv, S, scale, scale_log2);
+                                                         (__nv_bfloat16*)dv, S, scale, scale_log2, dk_t);
   const long long n4 = rows * HD / 4;
   f32_to_bf16_kernel<<<(unsigned)std::min<long long>((n4 + 255) / 256, 148 * 8), 256, 0, st>>>(dq_acc, (__nv_bfloat16*)dq, n4);
-  return cudaGetLastError() == cudaSuccess ? 0 : -3;
-}
-
-int TransposeRowsCols(const void* x, void* y, int n, int R, int C, cudaStream_t st) {
-  if (n <= 0 || R <= 0 || C <= 0) return 0;
-  dim3 grid((C + 31) / 32, (R + 31) / 32, n);
-  transpose_rc_kernel<<<grid, 256, 0, st>>>((const uint16_t*)x, (uint16_t*)y, R, C);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
