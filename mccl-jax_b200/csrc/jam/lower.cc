@@ -169,6 +169,12 @@ __device__ __forceinline__ float fsign(float x) { return x > 0.f ? 1.f : (x < 0.
 __device__ __forceinline__ float frne(float x) { return rintf(x); }
 __device__ __forceinline__ float fafz(float x) { return roundf(x); }
 __device__ __forceinline__ float flogistic(float x) { return 1.f / (1.f + expf(-x)); }
+// 1 / (1 + e^(-2u)) = (1 + tanh(u)) / 2, with the exponential and the reciprocal on the SFU
+__device__ __forceinline__ float fsig2(float u) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + ex2a(u * -2.88539008177792681f)));  // -2 log2(e)
+  return r;
+}
 __device__ __forceinline__ float warp_sum(float v) { for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o); return v; }
 __device__ __forceinline__ double warp_sum(double v) { for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o); return v; }
 )";
@@ -241,6 +247,11 @@ struct Gen {
   std::unordered_map<std::string, std::string> vloads;    // leaf base -> vector register
   std::vector<std::vector<std::string>> lane_identity;   // identity index per lane (vector mode)
   std::unordered_map<int, std::vector<std::string>> lane_group_regs;
+  // Ragged-row walks (non-empty shift_dims): the lanes' four elements are 16-byte aligned only in
+  // tensors of exactly these dims read at the current row (index prefix shift_prefix); other reads
+  // are scalar.
+  std::vector<int64_t> shift_dims;
+  std::vector<std::string> shift_prefix;
 
   int LaneOf(const std::vector<std::string>& idx) const {
     if (!vec || idx.empty()) return -1;
@@ -300,6 +311,28 @@ struct Gen {
     return out;
   }
 
+  static bool SplatIs(const Value* v, double want) {
+    while (v->def && v->def->name == "broadcast_in_dim") v = v->def->operands[0];
+    return v->def && v->def->name == "constant" && v->def->splat && ConstScalar(v->def) == want;
+  }
+  // v = (0.5 * h) * (1 + tanh(u)), operands of each product and sum in either order, all f32
+  static bool GeluTanhForm(const Value* v, const Value** h, const Value** u) {
+    const Op* m = v->def;
+    if (!m || m->name != "multiply" || m->operands.size() != 2) return false;
+    for (int s = 0; s < 2; ++s) {
+      const Op* half = m->operands[s]->def;
+      const Op* sum = m->operands[1 - s]->def;
+      if (!half || !sum || half->name != "multiply" || sum->name != "add") continue;
+      const Value* hv = SplatIs(half->operands[0], 0.5) ? half->operands[1] : SplatIs(half->operands[1], 0.5) ? half->operands[0] : nullptr;
+      const Value* tv = SplatIs(sum->operands[0], 1.0) ? sum->operands[1] : SplatIs(sum->operands[1], 1.0) ? sum->operands[0] : nullptr;
+      if (!hv || !tv || !tv->def || tv->def->name != "tanh" || hv->type.dt != DT::kF32 || tv->type.dt != DT::kF32) continue;
+      *h = hv;
+      *u = tv->def->operands[0];
+      return true;
+    }
+    return false;
+  }
+
   std::string EmitUncached(const Value* v, const std::vector<std::string>& idx) {
     const TensorType& ty = v->type;
     auto fx = fixed.find(v->id);
@@ -320,8 +353,11 @@ struct Gen {
         conflict = true;
       }
       const int lane = branch_depth == 0 ? LaneOf(idx) : -1;
-      if (lane >= 0 && (ty.dt == DT::kF32 || ty.dt == DT::kBF16 || ty.dt == DT::kF16) && !ty.dims.empty() &&
-          ty.dims.back() % 4 == 0) {
+      const bool aligned4 = shift_dims.empty()
+                                ? !ty.dims.empty() && ty.dims.back() % 4 == 0
+                                : ty.dims == shift_dims && idx.size() == shift_prefix.size() + 1 &&
+                                      std::equal(shift_prefix.begin(), shift_prefix.end(), idx.begin());
+      if (lane >= 0 && (ty.dt == DT::kF32 || ty.dt == DT::kBF16 || ty.dt == DT::kF16) && aligned4) {
         cur_dims = ty.dims;
         std::string r = VecLoad(ty.dt, slot, idx, lane);
         return ty.dt == DT::kF32 ? Var(ty.dt, r) : r;
@@ -507,6 +543,15 @@ struct Gen {
       }
       if (n == "is_finite") return Var(DT::kPred, e);
       return Round(t, Var(t, e));
+    }
+    if (n == "multiply" && ty.dt == DT::kF32) {
+      // (0.5 h) (1 + tanh u), the tanh form of GELU, as h / (1 + e^(-2u)): the same function
+      // without the cancellation in 1 + tanh(u) for u < 0, in five instructions instead of ~20
+      const Value *h = nullptr, *u = nullptr;
+      if (GeluTanhForm(v, &h, &u)) {
+        std::string hs = Emit(h, idx), us = Emit(u, idx);
+        return Var(DT::kF32, hs + " * fsig2(" + us + ")");
+      }
     }
     if (kBinary.count(n)) {
       std::string a = opnd(0, idx), b = opnd(1, idx);
@@ -1757,15 +1802,37 @@ class Lowerer {
       lanes.back().push_back("j_" + std::to_string(l));
     }
     const std::string Ls = std::to_string(L), Ts = std::to_string(T), last = std::to_string(L - 1);
+    // A short row that splits evenly over the threads is walked by a fully unrolled loop: every
+    // phase then reads the same addresses, so the row's loads are issued together once and the
+    // later phases reuse the registers instead of re-reading L1.
+    const int64_t n_it = vec && L % (4 * T) == 0 ? L / (4 * T) : 0;
     const std::string loop_head =
-        vec ? "#pragma unroll 4\n    for (int j = lt * 4; j < " + Ls + "; j += " + std::to_string(4 * T) + ") {\n" +
+        vec && n_it > 0 && n_it <= 8
+            ? "#pragma unroll\n    for (int jj = 0; jj < " + std::to_string(n_it) + "; ++jj) {\n      const int j = lt * 4 + jj * " +
+                  std::to_string(4 * T) + ";\n      const int j_0 = j, j_1 = j + 1, j_2 = j + 2, j_3 = j + 3;\n"
+        : vec ? "#pragma unroll 4\n    for (int j = lt * 4; j < " + Ls + "; j += " + std::to_string(4 * T) + ") {\n" +
                   "      const int j_0 = j, j_1 = j + 1, j_2 = j + 2, j_3 = j + 3;\n"
             : "#pragma unroll 2\n    for (int j = lt; j < " + Ls + "; j += " + std::to_string(4 * T) + ") {\n" +
                   "      const bool ok_1 = j + " + Ts + " < " + Ls + ", ok_2 = j + " + std::to_string(2 * T) + " < " + Ls +
                   ", ok_3 = j + " + std::to_string(3 * T) + " < " + Ls + ";\n" +
                   "      const int j_0 = j, j_1 = ok_1 ? j + " + Ts + " : " + last + ", j_2 = ok_2 ? j + " + std::to_string(2 * T) +
                   " : " + last + ", j_3 = ok_3 ? j + " + std::to_string(3 * T) + " : " + last + ";\n";
-    auto ok = [&](int l) { return vec || l == 0 ? std::string() : "ok_" + std::to_string(l); };
+    // Rows of a ragged length (L % 4 != 0) start at varying alignments.  Each row is then walked in
+    // two loops: four-element groups from the row's first 16-byte aligned element (hd), where the
+    // reads and writes of [rows..., L] tensors are vector accesses, and a scalar loop over the at
+    // most six elements left at the two ends.
+    const bool shift = !vec && L >= 4 * T && !std::getenv("B200_NO_VEC");
+    if (shift)
+      ob << "    const int hd = (int)((4 - (int)((row * " << Ls << "LL) & 3)) & 3), nv = (" << Ls << " - hd) >> 2, nrem = " << Ls
+         << " - 4 * nv;\n";
+    const std::string shift_head = "#pragma unroll 4\n    for (int jv = lt; jv < nv; jv += " + Ts +
+                                   ") {\n      const int j = hd + 4 * jv;\n      const int j_0 = j, j_1 = j + 1, j_2 = j + 2, j_3 = j + 3;\n";
+    const std::string rem_head = "    for (int j = lt; j < nrem; j += " + Ts +
+                                 ") {\n      const bool ok_1 = false, ok_2 = false, ok_3 = false;\n"
+                                 "      const int j_0 = j < hd ? j : j + 4 * nv, j_1 = j_0, j_2 = j_0, j_3 = j_0;\n";
+    bool cur_vec = vec;        // the walk being emitted has four consecutive elements per thread
+    std::string cur_head = loop_head;
+    auto ok = [&](int l) { return cur_vec || l == 0 ? std::string() : "ok_" + std::to_string(l); };
     auto elem_index = [&](const Value* m, int l) {
       const int64_t p = StoredPitch(m);
       return "(long long)row * " + (p ? std::to_string(p) : Ls) + "LL + j_" + std::to_string(l);
@@ -1777,10 +1844,25 @@ class Lowerer {
       gen.body.str("");
       gen.body.clear();
       gen.indent = "      ";
-      gen.vec = vec;
+      gen.vec = cur_vec;
+      gen.shift_dims = shift && cur_vec ? X : std::vector<int64_t>{};
+      gen.shift_prefix = gen.row_ident;
       gen.vinner = "j";
       gen.lane_identity = lanes;
       gen.identity = lanes[0];
+    };
+    // the loops of one walk over the row; `lane_code` emits the phase's values and returns the code
+    // that consumes them
+    auto walk = [&](const std::function<std::string()>& lane_code) {
+      std::string out;
+      for (int pass = 0; pass < (shift ? 2 : 1); ++pass) {
+        cur_vec = shift ? pass == 0 : vec;
+        cur_head = shift ? (pass == 0 ? shift_head : rem_head) : loop_head;
+        const std::string tail = lane_code();
+        out += cur_head + gen.body.str() + tail + "    }\n";
+      }
+      cur_vec = vec;
+      return out;
     };
     auto phase_vals = [&](const Value* v) {
       std::vector<std::string> vals;
@@ -1808,22 +1890,25 @@ class Lowerer {
         // form: a NaN makes both NaN; an all -inf row or a +inf element makes the sum NaN.
         const std::string k1 = std::to_string(k), kk = std::to_string(k2);
         const std::string mx = "mx" + k1, s = "sx" + k1, bad = "bad" + k1, NINF = "(-__int_as_float(0x7f800000))";
-        std::vector<std::string> vals = row_phase(op->operands[0]);
-        body << "    float " << mx << " = " << NINF << ", " << s << " = 0.f, nmx" << k1 << " = " << NINF << ";\n    int " << bad << " = 0;\n"
-             << loop_head << gen.body.str();
-        body << "      {\n";
-        for (int l = 0; l < 4; ++l)
-          body << "        const float c" << l << " = " << (ok(l).empty() ? vals[l] : ok(l) + " ? " + vals[l] + " : " + NINF) << ";\n";
-        // exp(d) as 2^(d log2 e) on the SFU: d = c_l - mx is formed first so the scaling only rounds
-        // the (small) exponent; NaN inputs are seen by a NaN-propagating max kept beside mx
         const std::string nmx = "nmx" + k1;
-        body << "        " << nmx << " = fmax_nan(" << nmx << ", fmax_nan(fmax_nan(c0, c1), fmax_nan(c2, c3)));\n"
-             << "        const float c = fmaxf(fmaxf(c0, c1), fmaxf(c2, c3));\n"
-             << "        if (c > " << mx << ") { " << s << " *= ex2a((" << mx << " - c) * 1.4426950408889634f); " << mx << " = c; }\n"
-             << "        if (" << mx << " > " << NINF << ") " << s << " += (ex2a((c0 - " << mx << ") * 1.4426950408889634f) + ex2a((c1 - " << mx
-             << ") * 1.4426950408889634f)) + (ex2a((c2 - " << mx << ") * 1.4426950408889634f) + ex2a((c3 - " << mx
-             << ") * 1.4426950408889634f));\n      }\n";
-        body << "    }\n    " << bad << " = nmx" << k1 << " != nmx" << k1 << ";\n";
+        body << "    float " << mx << " = " << NINF << ", " << s << " = 0.f, " << nmx << " = " << NINF << ";\n    int " << bad << " = 0;\n";
+        body << walk([&]() {
+          std::vector<std::string> vals = row_phase(op->operands[0]);
+          std::ostringstream t;
+          t << "      {\n";
+          for (int l = 0; l < 4; ++l)
+            t << "        const float c" << l << " = " << (ok(l).empty() ? vals[l] : ok(l) + " ? " + vals[l] + " : " + NINF) << ";\n";
+          // exp(d) as 2^(d log2 e) on the SFU: d = c_l - mx is formed first so the scaling only
+          // rounds the (small) exponent; NaN inputs are seen by a NaN-propagating max kept beside mx
+          t << "        " << nmx << " = fmax_nan(" << nmx << ", fmax_nan(fmax_nan(c0, c1), fmax_nan(c2, c3)));\n"
+            << "        const float c = fmaxf(fmaxf(c0, c1), fmaxf(c2, c3));\n"
+            << "        if (c > " << mx << ") { " << s << " *= ex2a((" << mx << " - c) * 1.4426950408889634f); " << mx << " = c; }\n"
+            << "        if (" << mx << " > " << NINF << ") " << s << " += (ex2a((c0 - " << mx << ") * 1.4426950408889634f) + ex2a((c1 - " << mx
+            << ") * 1.4426950408889634f)) + (ex2a((c2 - " << mx << ") * 1.4426950408889634f) + ex2a((c3 - " << mx
+            << ") * 1.4426950408889634f));\n      }\n";
+          return t.str();
+        });
+        body << "    " << bad << " = " << nmx << " != " << nmx << ";\n";
         auto merge = [&](const std::string& om, const std::string& os) {
           return "{ const float nm = fmaxf(" + mx + ", " + om + "); " + s + " = (" + mx + " == " + NINF + " ? 0.f : " + s +
                  " * expf(" + mx + " - nm)) + (" + om + " == " + NINF + " ? 0.f : " + os + " * expf(" + om + " - nm)); " + mx +
@@ -1858,16 +1943,18 @@ class Lowerer {
         DT odt = m->type.dt, acc_dt = AccDt(odt);
         std::string acc_t = CType(acc_dt), acc = "acc" + std::to_string(k);
         std::string init = InitExpr(op->operands[1], acc_dt);
-        std::vector<std::string> vals = row_phase(op->operands[0]);
-        body << "    " << acc_t << " " << acc << " = (" << acc_t << ")(" << IdentityOf(op->reduce, acc_dt) << ");\n"
-             << loop_head << gen.body.str();
-        for (int l = 0; l < 4; ++l) {
-          std::string x = "(" + acc_t + ")(" + vals[l] + ")";
-          if (!ok(l).empty()) x = "(" + ok(l) + " ? " + x + " : (" + acc_t + ")(" + IdentityOf(op->reduce, acc_dt) + "))";
-          body << "      " << acc << " = " << Combine(op->reduce, acc_dt, acc, x) << ";\n";
-        }
-        body << "    }\n"
-             << "    for (int o = 16; o; o >>= 1) { " << acc_t << " oth = __shfl_xor_sync(0xffffffffu, " << acc << ", o); "
+        body << "    " << acc_t << " " << acc << " = (" << acc_t << ")(" << IdentityOf(op->reduce, acc_dt) << ");\n";
+        body << walk([&]() {
+          std::vector<std::string> vals = row_phase(op->operands[0]);
+          std::string t;
+          for (int l = 0; l < 4; ++l) {
+            std::string x = "(" + acc_t + ")(" + vals[l] + ")";
+            if (!ok(l).empty()) x = "(" + ok(l) + " ? " + x + " : (" + acc_t + ")(" + IdentityOf(op->reduce, acc_dt) + "))";
+            t += "      " + acc + " = " + Combine(op->reduce, acc_dt, acc, x) + ";\n";
+          }
+          return t;
+        });
+        body << "    for (int o = 16; o; o >>= 1) { " << acc_t << " oth = __shfl_xor_sync(0xffffffffu, " << acc << ", o); "
              << acc << " = " << Combine(op->reduce, acc_dt, acc, "oth") << "; }\n";
         if (block_mode) {
           std::string red = "red" + std::to_string(k);
@@ -1887,34 +1974,37 @@ class Lowerer {
         while (k_end < members.size() && !done[k_end] && members[k_end]->type.dims == X &&
                !(members[k_end]->def && members[k_end]->def->name == "reduce"))
           ++k_end;
-        std::vector<std::pair<size_t, std::vector<std::string>>> outs;
-        phase_begin();
+        std::vector<size_t> stored;
         for (size_t q = k; q < k_end; ++q) {
           done[q] = true;
-          if (out_of[q] < 0) continue;
-          outs.push_back({q, phase_vals(members[q])});
+          if (out_of[q] >= 0) stored.push_back(q);
         }
         k = k_end - 1;
-        if (outs.empty()) continue;
-        body << loop_head << gen.body.str();
-        for (auto& ov : outs) {
-          const Value* mq = members[ov.first];
-          const std::string oq = "out" + std::to_string(out_of[ov.first]);
-          std::vector<std::string>& vals = ov.second;
-          DT dt = StoredDt(mq);
-          for (auto& x : vals) x = StoreVal(mq, dt, x);
-          if (!vec) {
-            for (int l = 0; l < 4; ++l)
-              body << "      " << (ok(l).empty() ? "" : "if (" + ok(l) + ") ") << oq << "[" << elem_index(mq, l) << "] = " << StoreExpr(dt, vals[l]) << ";\n";
-          } else if (dt == DT::kF32) {
-            body << "      *(float4*)(" << oq << " + " << elem_index(mq, 0) << ") = make_float4(" << vals[0] << ", " << vals[1] << ", " << vals[2] << ", " << vals[3] << ");\n";
-          } else if (dt == DT::kBF16 || dt == DT::kF16) {
-            body << "      *(uint2*)(" << oq << " + " << elem_index(mq, 0) << ") = make_uint2(" << Pack16(dt, vals[0], vals[1]) << ", " << Pack16(dt, vals[2], vals[3]) << ");\n";
-          } else {
-            for (int l = 0; l < 4; ++l) body << "      " << oq << "[" << elem_index(mq, l) << "] = " << StoreExpr(dt, vals[l]) << ";\n";
+        if (stored.empty()) continue;
+        body << walk([&]() {
+          phase_begin();
+          std::vector<std::vector<std::string>> vals_of;
+          for (size_t q : stored) vals_of.push_back(phase_vals(members[q]));
+          std::ostringstream t;
+          for (size_t i = 0; i < stored.size(); ++i) {
+            const Value* mq = members[stored[i]];
+            const std::string oq = "out" + std::to_string(out_of[stored[i]]);
+            std::vector<std::string>& vals = vals_of[i];
+            DT dt = StoredDt(mq);
+            for (auto& x : vals) x = StoreVal(mq, dt, x);
+            // vector stores need the row's alignment: with a ragged row only an unpadded output has it
+            const bool vstore = cur_vec && (!shift || StoredPitch(mq) == 0);
+            if (!vstore || (dt != DT::kF32 && dt != DT::kBF16 && dt != DT::kF16)) {
+              for (int l = 0; l < 4; ++l)
+                t << "      " << (ok(l).empty() ? "" : "if (" + ok(l) + ") ") << oq << "[" << elem_index(mq, l) << "] = " << StoreExpr(dt, vals[l]) << ";\n";
+            } else if (dt == DT::kF32) {
+              t << "      *(float4*)(" << oq << " + " << elem_index(mq, 0) << ") = make_float4(" << vals[0] << ", " << vals[1] << ", " << vals[2] << ", " << vals[3] << ");\n";
+            } else {
+              t << "      *(uint2*)(" << oq << " + " << elem_index(mq, 0) << ") = make_uint2(" << Pack16(dt, vals[0], vals[1]) << ", " << Pack16(dt, vals[2], vals[3]) << ");\n";
+            }
           }
-        }
-        body << "    }\n";
+          return t.str();
+        });
       } else {
         // row scalar: every thread of the row computes it
         gen.cse.clear();

@@ -231,6 +231,23 @@ def test_elementwise_and_reductions_vs_oracle(client):
         assert_close(o, r, RTOL_F32, "reduction")
 
 
+def test_tanh_f32_within_4_ulp(client):
+    # the generated kernels' tanh (series below |x| = 0.55, SFU exponential above) over every
+    # binade from 2^-30 to 2^6, signed zeros, infinities and NaN
+    rng = np.random.default_rng(5)
+    mag = np.exp2(rng.uniform(-30, 6, 1 << 20))
+    x = (mag * rng.choice([-1.0, 1.0], mag.size)).astype(np.float32)
+    x[:6] = [0.0, -0.0, np.inf, -np.inf, np.nan, 0.55]
+    b = Builder("jit_tanh")
+    a = b.arg(x.shape, "f32")
+    y = client.run(b.text([b.tanh(a)]), [x])[0]
+    ref = np.tanh(x.astype(np.float64))
+    assert np.isnan(y[4]) and np.array_equal(np.signbit(y[:2]), [False, True]) and list(y[2:4]) == [1.0, -1.0]
+    fin = np.isfinite(ref)
+    ulp = np.abs(y[fin].astype(np.float64) - ref[fin]) / np.spacing(np.abs(ref[fin]).astype(np.float32))
+    assert ulp.max() <= 4.0, f"tanh max error {ulp.max():.2f} ulp"
+
+
 def test_embedding_take_and_scatter_add(client):
     b = Builder("jit_embed")
     table = b.arg((100, 16), "f32")

@@ -99,7 +99,8 @@ def _ln_inputs(rows, d, dt, seed=0):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("rows,d,dtype", [(1024, 768, "bf16"), (300, 96, "f32"), (77, 2056, "f32"), (40, 33, "f32")])
+@pytest.mark.parametrize("rows,d,dtype", [(1024, 768, "bf16"), (300, 96, "f32"), (77, 2056, "f32"), (40, 33, "f32"),
+                                        (37, 770, "bf16"), (9, 9001, "f32")])
 def test_layernorm_vs_oracle(client, rows, d, dtype):
     text = layernorm(rows, d, dtype)
     ins = _ln_inputs(rows, d, BF16 if dtype == "bf16" else np.float32)
@@ -120,7 +121,7 @@ def test_layernorm_intermediates_are_stored_when_read_outside(client):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("shape", [(2, 4, 128, 128), (64, 1000), (32, 5003), (16, 8192)])
+@pytest.mark.parametrize("shape", [(2, 4, 128, 128), (64, 1000), (32, 5003), (16, 8192), (3, 5, 2051)])
 def test_softmax_vs_oracle(client, shape):
     text = softmax(shape)
     x = (np.random.default_rng(5).standard_normal(shape) * 4).astype(np.float32)
