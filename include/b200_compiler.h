@@ -25,8 +25,10 @@ __attribute__((visibility("default"))) int b200_compile_report(const char* text,
  * segments with host clocks under MCCL_JAX_TIME, src/jam/jam_run.mm:114-126).
  * b200_exec_timer(0): reset — the next LoadedExecutable_Execute records a CUDA event on the device
  *   stream before its first step;
+ * b200_exec_timer(2): reset into per-execution mode — every execution records its own start and end;
  * b200_exec_timer(1): returns the device milliseconds from that event to the end of the most recent
- *   execution (waits for it), or -1 if nothing was recorded since the reset. */
+ *   execution (waits for it), or in per-execution mode the sum of the executions' own spans (the
+ *   gaps between executions left out), or -1 if nothing was recorded since the reset. */
 __attribute__((visibility("default"))) double b200_exec_timer(int action);
 
 #ifdef __cplusplus

@@ -1193,10 +1193,24 @@ class Lowerer {
       for (const Value* r : o->results)
         for (const Op* u : r->users)
           if (!dead_[u->index] && !ok_users.count(u)) return;
+    // dK = dot(Q, T) comes out [B, H, D, S]; when its one reader transposes it back to [B, H, S, D]
+    // the backward writes that transpose's value in its own layout and the dot disappears
+    const Value* dk_val = dk_op->result();
+    const Op* dk_dead = nullptr;
+    if (dk_t && dk_val->users.size() == 1 && std::find(g_.outputs.begin(), g_.outputs.end(), dk_val) == g_.outputs.end()) {
+      const Op* tr = dk_val->users[0];
+      auto pm = tr->ints.find("dims");
+      if (tr->name == "transpose" && pm != tr->ints.end() && pm->second == std::vector<int64_t>{0, 1, 3, 2}) {
+        dk_val = tr->result();
+        dk_t = false;
+        dk_dead = dk_op;
+      }
+    }
     FwdChain keep = fc;
     keep.ops.clear();
     RegisterAttention(d2, keep);
     for (const Op* o : kill) dead_[o->index] = true;
+    if (dk_dead) dead_[dk_dead->index] = true;
     BwdMatch m;
     m.d2 = d2->result()->id;
     m.Q = fc.Q;
@@ -1205,7 +1219,7 @@ class Lowerer {
     m.O = d2->result();
     m.G = G;
     m.dq = dq_op->result();
-    m.dk = dk_op->result();
+    m.dk = dk_val;
     m.dv = dv_op->result();
     m.dk_t = dk_t;
     const int idx = (int)bwd_.size();
@@ -1321,7 +1335,7 @@ class Lowerer {
           if (need_[ur->id]) c.insert(ur->id);
           else c.insert(cons[ur->id].begin(), cons[ur->id].end());
         }
-        if (attn_.count(r->id)) need_[r->id] = true;
+        if (attn_.count(r->id) || bwd_of_.count(r->id)) need_[r->id] = true;
         cons[r->id] = c;
         if (IsHeavy(op)) need_[r->id] = true;
         if (!op->results.empty() && op->name == "constant" && !op->splat) need_[r->id] = true;
@@ -1810,7 +1824,7 @@ class Lowerer {
         vec && n_it > 0 && n_it <= 8
             ? "#pragma unroll\n    for (int jj = 0; jj < " + std::to_string(n_it) + "; ++jj) {\n      const int j = lt * 4 + jj * " +
                   std::to_string(4 * T) + ";\n      const int j_0 = j, j_1 = j + 1, j_2 = j + 2, j_3 = j + 3;\n"
-        : vec ? "#pragma unroll 4\n    for (int j = lt * 4; j < " + Ls + "; j += " + std::to_string(4 * T) + ") {\n" +
+        : vec ? "#pragma unroll 8\n    for (int j = lt * 4; j < " + Ls + "; j += " + std::to_string(4 * T) + ") {\n" +
                   "      const int j_0 = j, j_1 = j + 1, j_2 = j + 2, j_3 = j + 3;\n"
             : "#pragma unroll 2\n    for (int j = lt; j < " + Ls + "; j += " + std::to_string(4 * T) + ") {\n" +
                   "      const bool ok_1 = j + " + Ts + " < " + Ls + ", ok_2 = j + " + std::to_string(2 * T) + " < " + Ls +
@@ -2795,7 +2809,11 @@ class Lowerer {
 std::string Plan::dump() const {
   std::ostringstream o;
   o << "plan: " << slots.size() << " slots, " << steps.size() << " steps, " << consts.size() << " constants\n";
-  for (size_t i = 0; i < steps.size(); ++i) o << "  [" << i << "] " << steps[i].label << "\n";
+  for (size_t i = 0; i < steps.size(); ++i) {
+    o << "  [" << i << "] " << steps[i].label;
+    for (size_t k = 0; k < steps[i].launches.size(); ++k) o << (k ? ", " : "  {") << steps[i].launches[k].fn;
+    o << (steps[i].launches.empty() ? "" : "}") << "\n";
+  }
   return o.str();
 }
 

@@ -111,12 +111,17 @@ struct StepTimer {
 };
 
 // Execution timer (b200_exec_timer): a start event recorded by the first execution after a reset
-// and an end event re-recorded by every execution, both on the device stream.
+// and an end event re-recorded by every execution, both on the device stream.  In per-execution
+// mode every execution records its own pair instead and the reading is the sum of their spans:
+// the device time of the executions without the gaps between them.
 struct ExecTimer {
   std::mutex mu;
-  bool armed = false, started = false;
+  bool armed = false, started = false, per_exec = false;
   int device = -1;
   cudaEvent_t start = nullptr, end = nullptr;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pairs;
+  size_t used = 0;
+  bool open = false;           // a pair's start is recorded and its end is not
 };
 ExecTimer& GetExecTimer() {
   static ExecTimer t;
@@ -126,6 +131,20 @@ ExecTimer& GetExecTimer() {
 void ExecTimerMarkStart(int device, cudaStream_t st) {
   ExecTimer& t = GetExecTimer();
   std::lock_guard<std::mutex> lock(t.mu);
+  if (t.armed && t.per_exec) {
+    if (t.started && t.device != device) return;
+    if (t.used == t.pairs.size()) {
+      cudaEvent_t a, b;
+      if (cudaEventCreate(&a) != cudaSuccess) return;
+      if (cudaEventCreate(&b) != cudaSuccess) { cudaEventDestroy(a); return; }
+      t.pairs.push_back({a, b});
+    }
+    cudaEventRecord(t.pairs[t.used].first, st);
+    t.device = device;
+    t.started = true;
+    t.open = true;
+    return;
+  }
   if (!t.armed || t.started) return;
   if (!t.start) {
     cudaEventCreate(&t.start);
@@ -139,6 +158,13 @@ void ExecTimerMarkStart(int device, cudaStream_t st) {
 void ExecTimerMarkEnd(int device, cudaStream_t st) {
   ExecTimer& t = GetExecTimer();
   std::lock_guard<std::mutex> lock(t.mu);
+  if (t.armed && t.per_exec) {
+    if (t.open && t.device == device) {
+      cudaEventRecord(t.pairs[t.used++].second, st);
+      t.open = false;
+    }
+    return;
+  }
   if (t.armed && t.started && t.device == device) cudaEventRecord(t.end, st);
 }
 
@@ -460,13 +486,27 @@ extern "C" int b200_compile_report(const char* text, size_t size, int num_proces
 extern "C" double b200_exec_timer(int action) {
   b200::ExecTimer& t = b200::GetExecTimer();
   std::lock_guard<std::mutex> lock(t.mu);
-  if (action == 0) {
+  if (action == 0 || action == 2) {   // 0: first start to last end; 2: sum over executions
     t.armed = true;
     t.started = false;
+    t.per_exec = action == 2;
+    t.used = 0;
+    t.open = false;
     return 0.0;
   }
   if (!t.armed || !t.started) return -1.0;
   cudaSetDevice(t.device);
+  if (t.per_exec) {
+    if (t.used == 0) return -1.0;
+    cudaEventSynchronize(t.pairs[t.used - 1].second);
+    double total = 0;
+    for (size_t i = 0; i < t.used; ++i) {
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, t.pairs[i].first, t.pairs[i].second) != cudaSuccess) return -1.0;
+      total += ms;
+    }
+    return total;
+  }
   cudaEventSynchronize(t.end);
   float ms = 0.f;
   if (cudaEventElapsedTime(&ms, t.start, t.end) != cudaSuccess) return -1.0;

@@ -14,8 +14,11 @@
 //              so the next tile's MMAs overlap this tile's stores.
 // Tails in M / N / K are handled by TMA zero fill and predicated stores.
 #include <cuda_bf16.h>
+#include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
+#include <type_traits>
 
 #include "tc_common.cuh"
 #include "../../../include/b200_kernels.h"
@@ -30,7 +33,7 @@ constexpr int BM = 128, BK = 64;
 
 template <int BN>
 struct Cfg {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kStages = BN == 256 ? 4 : BN == 192 ? 5 : 6;
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStage = kABytes + kBBytes;
@@ -38,7 +41,7 @@ struct Cfg {
   // 4 KB swizzled boxes for the TMA-store path
   static constexpr int kStageOut = 4 * 32 * 33 * 4;
   static constexpr int kSmem = kStages * kStage + 1024 + 1024 + kStageOut;
-  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kTmemCols = BN == 192 ? 512 : 2 * BN;   // allocations are powers of two
 };
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
@@ -548,27 +551,44 @@ int TakeGemmError() {
 
 // C[b] = A[b] . B[b]^T.  A is [batch, M, >=K] (K-major, row pitch lda) or, with a_mn, [batch, K, >=M]
 // (MN-major, pitch lda); B likewise with N, ldb and b_mn.
-// K slices for a tensor-core GEMM: 1 when the output tiles fill the SMs well; otherwise the smallest
-// count (at most 8, each slice >= 4 K blocks) whose work units fill at least 85 % of the waves they
-// need.  Shared by the compiler (which sizes the workspace) and the launcher.
-int GemmSplitK(int64_t batch, int64_t M, int64_t N, int64_t K, int sms) {
-  if (std::getenv("B200_GEMM_NO_SPLITK") || K <= 0) return 1;
-  const int64_t bn = N >= 256 ? 256 : 128;
-  const int64_t tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn) * batch;
-  const int64_t kbs = (K + BK - 1) / BK;
-  auto eff = [&](int64_t s) {
-    const int64_t units = tiles * s;
-    return (double)units / (double)(((units + sms - 1) / sms) * sms);
-  };
-  // splitting pays only when the tiles leave SMs idle and each slice keeps a long K loop (the f32
-  // partials cost a zeroing pass and atomics)
-  if (eff(1) >= 0.85 || tiles * 2 > sms) return 1;
-  for (int64_t s = 2; s <= 8 && kbs / s >= 16; ++s) {
-    const int64_t kps = (kbs + s - 1) / s;
-    if ((s - 1) * kps >= kbs) continue;          // would leave an empty slice
-    if (eff(s) >= 0.85) return (int)s;
+// Tile width and K slices for a tensor-core GEMM, chosen by a wave model: the time of a persistent
+// launch is the number of rounds of work units over the SMs times the time of one unit, which grows
+// with the tile width (BN = 256, 192 or 128 columns) and the unit's K blocks plus about two blocks of
+// fill and epilogue; narrower tiles pay a little for feeding the tensor cores more operand bytes
+// per FLOP.  K is split (at most 8 slices of >= 16 K blocks, none empty) only when the tiles leave
+// more than half the SMs idle: the f32 partials cost a zeroing pass, L2 reductions and a rounding
+// pass.  Shared by the compiler (which sizes the workspace) and the launcher.
+void GemmTile(int64_t batch, int64_t M, int64_t N, int64_t K, int sms, int* bn_out, int* splits_out) {
+  const int64_t kbs = std::max<int64_t>(1, (K + BK - 1) / BK), mb = (M + BM - 1) / BM;
+  const bool no_split = std::getenv("B200_GEMM_NO_SPLITK") != nullptr || K <= 0;
+  const char* force = std::getenv("B200_GEMM_BN");
+  double best = 1e300;
+  int best_bn = 256, best_s = 1;
+  for (int bn : {256, 192, 128}) {
+    if (force && std::atoi(force) != bn) continue;
+    if (!force && bn > 128 && N < bn) continue;
+    const int64_t tiles = mb * ((N + bn - 1) / bn) * batch;
+    const double width = bn / 256.0 * (bn == 128 ? 1.3 : bn == 192 ? 1.08 : 1.0);   // measured on B200
+    for (int64_t s = 1; s <= 8; ++s) {
+      if (s > 1 && (no_split || tiles * 2 > sms || kbs / s < 16)) break;
+      const int64_t kps = (kbs + s - 1) / s;
+      if (s > 1 && (s - 1) * kps >= kbs) continue;        // would leave an empty slice
+      const int64_t rounds = (tiles * s + sms - 1) / sms;
+      double t = (double)rounds * width * (double)(kps + 2);
+      // splitting: zero + reduce + round the f32 partials, ~10 bytes per output at HBM speed, in
+      // units of one 128 x 256 x 64 block step (~0.45 us)
+      if (s > 1) t += (double)batch * M * N * 10.0 / 6.5e12 / 0.45e-6;
+      if (t < best * 0.999) { best = t; best_bn = bn; best_s = (int)s; }
+    }
   }
-  return 1;
+  *bn_out = best_bn;
+  *splits_out = best_s;
+}
+
+int GemmSplitK(int64_t batch, int64_t M, int64_t N, int64_t K, int sms) {
+  int bn = 256, s = 1;
+  GemmTile(batch, M, N, K, sms, &bn, &s);
+  return s;
 }
 
 // C[b] = A[b] . B[b]^T.  A is [batch, M, >=K] (K-major, row pitch lda) or, with a_mn, [batch, K, >=M]
@@ -590,22 +610,21 @@ int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, 
                ((uintptr_t)A % 16) == 0 && ((uintptr_t)B % 16) == 0 && !getenv("B200_GEMM_SIMT");
   if (tc_ok) {
     int fmt = ab_type == B200_DT_BF16 ? 1 : 0;
-    bool wide = N >= 256;
     int b = (int)batch, m = (int)M, n = (int)N, k = (int)K;
-    int splits = GemmSplitK(batch, M, N, K, NumSMs());
+    int bn = 256, splits = 1;
+    GemmTile(batch, M, N, K, NumSMs(), &bn, &splits);
     float* acc = out == 0 ? (float*)C : ws;
     if (splits > 1 && !acc) splits = 1;
     if (splits > 1 && cudaMemsetAsync(acc, 0, (size_t)batch * M * N * 4, st) != cudaSuccess) return -3;
-    int rc;
-    if (out == 0)
-      rc = wide ? LaunchTcMajor<256, 0>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc)
-                : LaunchTcMajor<128, 0>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc);
-    else if (out == 1)
-      rc = wide ? LaunchTcMajor<256, 1>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc)
-                : LaunchTcMajor<128, 1>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc);
-    else
-      rc = wide ? LaunchTcMajor<256, 2>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc)
-                : LaunchTcMajor<128, 2>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc);
+    auto launch = [&](auto out_c) {
+      constexpr int O = decltype(out_c)::value;
+      if (bn == 256) return LaunchTcMajor<256, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc);
+      if (bn == 192) return LaunchTcMajor<192, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc);
+      return LaunchTcMajor<128, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc);
+    };
+    int rc = out == 0 ? launch(std::integral_constant<int, 0>{})
+           : out == 1 ? launch(std::integral_constant<int, 1>{})
+                      : launch(std::integral_constant<int, 2>{});
     if (rc == 0 && splits > 1 && out != 0) {
       const long long total = (long long)batch * M * N;
       ws_to_16bit_kernel<<<(unsigned)std::min<long long>((total + 255) / 256, 148 * 8), 256, 0, st>>>(acc, (uint16_t*)C, total,

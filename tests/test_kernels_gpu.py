@@ -47,6 +47,26 @@ def test_gemm_bf16_tensor_cores(lib, cuda, batch, M, N, K, out):
     assert e <= (RTOL_F32 * 10 if out == F32 else RTOL_BF16), e
 
 
+@pytest.mark.parametrize("bn", ["256", "192", "128"])
+@pytest.mark.parametrize("batch,M,N,K", [(1, 8192, 768, 768), (2, 300, 1000, 200), (1, 130, 200, 4096)])
+@pytest.mark.parametrize("out", [F32, BF16])
+def test_gemm_every_tile_width(lib, cuda, monkeypatch, bn, batch, M, N, K, out):
+    """The 256-, 192- and 128-column tile kernels (the launcher picks one per shape by a wave
+    model) on full and ragged shapes, B200_GEMM_BN forcing each."""
+    torch = cuda
+    monkeypatch.setenv("B200_GEMM_BN", bn)
+    g = torch.Generator(device="cuda").manual_seed(M + 3 * N + K)
+    a = (torch.randn(batch, M, K, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
+    b = (torch.randn(batch, N, K, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
+    c = torch.empty(batch, M, N, device="cuda", dtype=torch.float32 if out == F32 else torch.bfloat16)
+    assert lib.b200_gemm(a.data_ptr(), b.data_ptr(), c.data_ptr(), batch, M, N, K, BF16, out, stream(torch)) == 0
+    torch.cuda.synchronize()
+    check_device_error(lib)
+    ref = torch.bmm(a.float(), b.float().transpose(1, 2))
+    e = rel_err(c.float().cpu().numpy(), ref.cpu().numpy())
+    assert e <= (RTOL_F32 * 10 if out == F32 else RTOL_BF16), e
+
+
 @pytest.mark.parametrize("M,N,K", [(128, 128, 128), (300, 200, 100), (64, 10, 784)])
 def test_gemm_f32_simt(lib, cuda, M, N, K):
     torch = cuda
