@@ -31,6 +31,12 @@ __attribute__((visibility("default"))) int b200_compile_report(const char* text,
  *   gaps between executions left out), or -1 if nothing was recorded since the reset. */
 __attribute__((visibility("default"))) double b200_exec_timer(int action);
 
+/* CUDA-graph replay of executions (no counterpart in the reference): a program without collectives
+ * whose argument and output buffers sit at the addresses of an earlier execution is captured once
+ * and replayed as one graph (B200_NO_GRAPHS=1 turns this off).
+ * b200_graph_stats(0): graphs captured so far; b200_graph_stats(1): executions replayed from one. */
+__attribute__((visibility("default"))) long long b200_graph_stats(int which);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1820,10 +1820,28 @@ class Lowerer {
     // phase then reads the same addresses, so the row's loads are issued together once and the
     // later phases reuse the registers instead of re-reading L1.
     const int64_t n_it = vec && L % (4 * T) == 0 ? L / (4 * T) : 0;
+    const bool unrolled = vec && n_it > 0 && n_it <= 8;
+    // A row loop without reductions over too few rows to give every warp several: the rows are cut
+    // into segments (multiples of 128 elements) and the warps take (row, segment) items, which fill
+    // the GPU's rounds evenly.
+    bool any_reduce = false;
+    for (const Value* m : members) any_reduce = any_reduce || (m->def && m->def->name == "reduce");
+    int64_t nseg = 1, seg = L;
+    if (!any_reduce && !block_mode && vec && !unrolled) {
+      const int64_t warps = 148 * 32;
+      while (nseg < 8 && rows * nseg < warps * 4 && (L + nseg) / (nseg + 1) >= 256) ++nseg;
+      seg = ((L + nseg - 1) / nseg + 127) / 128 * 128;
+      nseg = (L + seg - 1) / seg;
+    }
+    if (nseg > 1)
+      ob << "    const int j_lo = sg * " << seg << ", j_hi = j_lo + " << seg << " < " << Ls << " ? j_lo + " << seg << " : " << Ls << ";\n";
     const std::string loop_head =
-        vec && n_it > 0 && n_it <= 8
+        unrolled
             ? "#pragma unroll\n    for (int jj = 0; jj < " + std::to_string(n_it) + "; ++jj) {\n      const int j = lt * 4 + jj * " +
                   std::to_string(4 * T) + ";\n      const int j_0 = j, j_1 = j + 1, j_2 = j + 2, j_3 = j + 3;\n"
+        : vec && nseg > 1
+            ? "#pragma unroll 8\n    for (int j = j_lo + lt * 4; j < j_hi; j += " + std::to_string(4 * T) + ") {\n" +
+                  "      const int j_0 = j, j_1 = j + 1, j_2 = j + 2, j_3 = j + 3;\n"
         : vec ? "#pragma unroll 8\n    for (int j = lt * 4; j < " + Ls + "; j += " + std::to_string(4 * T) + ") {\n" +
                   "      const int j_0 = j, j_1 = j + 1, j_2 = j + 2, j_3 = j + 3;\n"
             : "#pragma unroll 2\n    for (int j = lt; j < " + Ls + "; j += " + std::to_string(4 * T) + ") {\n" +
@@ -2052,6 +2070,11 @@ class Lowerer {
     if (block_mode)
       src_ << "  const int lt = threadIdx.x;\n"
            << "  for (long long row = blockIdx.x; row < " << rows << "LL; row += gridDim.x) {\n";
+    else if (nseg > 1)
+      src_ << "  const int lt = threadIdx.x & 31;\n"
+           << "  for (long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); w < " << rows * nseg
+           << "LL; w += (long long)gridDim.x * 8) {\n"
+           << "    const long long row = w / " << nseg << ";\n    const int sg = (int)(w % " << nseg << ");\n";
     else
       src_ << "  const int lt = threadIdx.x & 31;\n"
            << "  for (long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); row < " << rows
@@ -2063,7 +2086,7 @@ class Lowerer {
     Lc.in_slots = gen.in_slots;
     Lc.out_slots = out_slots;
     Lc.block = threads;
-    Lc.grid_x = block_mode ? std::max<int64_t>(1, rows) : std::max<int64_t>(1, (rows + 7) / 8);
+    Lc.grid_x = block_mode ? std::max<int64_t>(1, rows) : std::max<int64_t>(1, (rows * nseg + 7) / 8);
     Lc.grid_stride = true;
     Step st;
     st.kind = StepKind::kFusion;
@@ -2285,6 +2308,90 @@ class Lowerer {
         Lc.grid_x = std::max<int64_t>(1, (n_out + 7) / 8);
         Lc.grid_stride = true;
         st.launches.push_back(Lc);
+      }
+    } else if (!inner && !kept_ax.empty() && kept_ax.back() == (int)xd.size() - 1 && kept.back() % 4 == 0 &&
+               acc_dt == DT::kF32 && !std::getenv("B200_NO_VEC")) {
+      // Column reduction (the contiguous dim is kept): a thread owns four adjacent outputs and reads
+      // them with one vector load per reduced index; the reduced range is split over `chunks` blocks
+      // in y whose partials a second kernel combines.
+      const int64_t n4 = n_out / 4;
+      int64_t chunks = 1;
+      const int64_t want_threads = 148LL * 2048;
+      if (L > 16) chunks = std::min<int64_t>((want_threads + n4 - 1) / n4, std::max<int64_t>(1, L / 16));
+      chunks = std::max<int64_t>(1, std::min<int64_t>(chunks, 1024));
+      const int64_t per = (L + chunks - 1) / chunks;
+      chunks = (L + per - 1) / per;
+      const int bt = (int)std::min<int64_t>(256, (n4 + 31) / 32 * 32);
+      gen.indent = "      ";
+      std::ostringstream ob;
+      auto names_k = Delinearize(ob, "o4", kept, "a", "  ", wide);
+      std::ostringstream inner_pre;
+      auto names_r = Delinearize(inner_pre, "j", red, "b", "      ", wide);
+      const std::string vin = names_k.back();
+      std::vector<std::vector<std::string>> lanes(4, std::vector<std::string>(xd.size()));
+      for (int l = 0; l < 4; ++l) {
+        for (size_t q = 0; q < kept_ax.size(); ++q) lanes[l][kept_ax[q]] = names_k[q];
+        lanes[l][kept_ax.back()] = vin + "_" + std::to_string(l);
+        for (size_t q = 0; q < red_ax.size(); ++q) lanes[l][red_ax[q]] = names_r[q];
+      }
+      gen.vec = true;
+      gen.vinner = vin;
+      gen.lane_identity = lanes;
+      gen.identity = lanes[0];
+      gen.body << inner_pre.str();
+      std::vector<std::string> vals;
+      for (int l = 0; l < 4; ++l) vals.push_back(gen.Emit(x, lanes[l]));
+      std::vector<DT> in_dts;
+      for (int s : gen.in_slots) in_dts.push_back(SlotDt(s));
+      int scratch = -1;
+      if (chunks > 1) scratch = NewSlot(chunks * n_out * 4);
+      const std::string ident = "(" + acc_t + ")(" + IdentityOf(kind, acc_dt) + ")";
+      k << "extern \"C\" __global__ void __launch_bounds__(" << bt << ") " << fn << "("
+        << KernelParams(gen.in_slots, 1, false) << ") {\n" << ParamCasts(gen.in_slots, in_dts, {chunks > 1 ? DT::kF32 : odt})
+        << "  const long long o = (long long)blockIdx.x * " << bt << " + threadIdx.x;\n  if (o >= " << n4 << "LL) return;\n"
+        << "  const long long o4 = o * 4;\n" << ob.str()
+        << "  const int " << vin << "_0 = " << vin << ", " << vin << "_1 = " << vin << " + 1, " << vin << "_2 = " << vin << " + 2, "
+        << vin << "_3 = " << vin << " + 3;\n";
+      for (int l = 0; l < 4; ++l) k << "  " << acc_t << " acc" << l << " = " << (chunks > 1 ? ident : init_expr) << ";\n";
+      k << "  const long long j0 = (long long)blockIdx.y * " << per << "LL;\n"
+        << "  const long long j1 = j0 + " << per << "LL < " << L << "LL ? j0 + " << per << "LL : " << L << "LL;\n"
+        << "#pragma unroll 8\n  for (long long j = j0; j < j1; ++j) {\n" << gen.body.str();
+      for (int l = 0; l < 4; ++l)
+        k << "      acc" << l << " = " << combine("acc" + std::to_string(l), "(" + acc_t + ")(" + vals[l] + ")") << ";\n";
+      k << "  }\n";
+      if (chunks > 1)
+        k << "  *(float4*)(out0 + (long long)blockIdx.y * " << n_out << "LL + o4) = make_float4(acc0, acc1, acc2, acc3);\n}\n";
+      else
+        for (int l = 0; l < 4; ++l) k << "  out0[o4 + " << l << "] = " << StoreExpr(odt, FromAcc(odt, "acc" + std::to_string(l))) << ";\n";
+      if (chunks == 1) k << "}\n";
+      Launch L1;
+      L1.fn = fn;
+      L1.in_slots = gen.in_slots;
+      L1.out_slots = {chunks > 1 ? scratch : out_slot};
+      L1.block = bt;
+      L1.grid_x = (n4 + bt - 1) / bt;
+      L1.grid_y = chunks;
+      st.launches.push_back(L1);
+      if (chunks > 1) {
+        std::string fn2 = KName();
+        k << "extern \"C\" __global__ void __launch_bounds__(256) " << fn2 << "(const void* __restrict__ p0, void* __restrict__ q0) {\n"
+          << "  const float* part = (const float*)p0;\n  " << MemType(odt) << "* out0 = (" << MemType(odt) << "*)q0;\n"
+          << "  const int lane = threadIdx.x & 31;\n"
+          << "  for (long long o = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); o < " << n_out << "LL; o += (long long)gridDim.x * 8) {\n"
+          << "    " << acc_t << " acc = " << ident << ";\n"
+          << "#pragma unroll 4\n"
+          << "    for (int c = lane; c < " << chunks << "; c += 32) acc = " << combine("acc", "part[(long long)c * " + std::to_string(n_out) + "LL + o]") << ";\n"
+          << "  " << shfl_red
+          << "    if (lane == 0) out0[o] = " << StoreExpr(odt, FromAcc(odt, combine(init_expr, "acc"))) << ";\n  }\n}\n";
+        Launch L2;
+        L2.fn = fn2;
+        L2.in_slots = {scratch};
+        L2.out_slots = {out_slot};
+        L2.block = 256;
+        L2.grid_x = std::max<int64_t>(1, (n_out + 7) / 8);
+        L2.grid_stride = true;
+        st.launches.push_back(L2);
+        RecordDt(scratch, DT::kF32);
       }
     } else {
       // thread per output, reduced range split over `chunks` blocks in y; partials to scratch, then

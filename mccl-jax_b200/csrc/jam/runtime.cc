@@ -4,11 +4,14 @@
 #include <cuda.h>
 #include <nvrtc.h>
 
+#include <algorithm>
+#include <atomic>
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <fstream>
+#include <functional>
 #include <thread>
 
 #include "../../../include/b200_kernels.h"
@@ -109,6 +112,8 @@ struct StepTimer {
   double host_ms = 0;          // time the host spends enqueueing one execution
   int runs = 0;
 };
+
+std::atomic<long long> g_graph_captures{0}, g_graph_launches{0};
 
 // Execution timer (b200_exec_timer): a start event recorded by the first execution after a reset
 // and an end event re-recorded by every execution, both on the device stream.  In per-execution
@@ -223,10 +228,81 @@ std::string Executable::Build(const char* text, size_t n, const CompileOptions& 
   return "";
 }
 
+// The slots a step reads or writes.
+static void StepSlots(const Step& S, std::vector<int>* out) {
+  out->clear();
+  auto add = [&](std::initializer_list<int> l) { for (int s : l) if (s >= 0) out->push_back(s); };
+  switch (S.kind) {
+    case StepKind::kFusion:
+      for (const Launch& L : S.launches) {
+        for (int s : L.in_slots) add({s});
+        for (int s : L.out_slots) add({s});
+        add({L.scratch});
+      }
+      break;
+    case StepKind::kGemm: add({S.gemm.a, S.gemm.b, S.gemm.c, S.gemm.ws}); break;
+    case StepKind::kAttention: add({S.attn.q, S.attn.k, S.attn.v, S.attn.o, S.attn.lse}); break;
+    case StepKind::kAttentionBwd:
+      add({S.bwd.q, S.bwd.k, S.bwd.v, S.bwd.o, S.bwd.dout, S.bwd.lse, S.bwd.dq, S.bwd.dk, S.bwd.dv, S.bwd.dq_acc, S.bwd.delta});
+      break;
+    case StepKind::kScatterAdd: add({S.scatter.base, S.scatter.idx, S.scatter.upd, S.scatter.out}); break;
+    case StepKind::kCollective: add({S.coll.in, S.coll.out}); break;
+    case StepKind::kCopy: add({S.copy.src, S.copy.dst}); break;
+  }
+}
+
+// Arena layout: every intermediate slot (not an argument, constant or output) gets an offset such
+// that slots with overlapping live ranges [first step touching it, last step reading it] do not
+// share bytes.  Greedy: largest first, lowest offset that clears the placed slots it overlaps.
+static int64_t LayoutArena(const Plan& P, std::vector<int64_t>* off) {
+  const size_t n = P.slots.size();
+  std::vector<int> first(n, -1), last(n, -1);
+  std::vector<int> ss;
+  for (size_t i = 0; i < P.steps.size(); ++i) {
+    StepSlots(P.steps[i], &ss);
+    for (int s : ss) {
+      if (first[s] < 0) first[s] = (int)i;
+      last[s] = std::max(last[s], (int)i);
+    }
+  }
+  off->assign(n, -1);
+  std::vector<int> order;
+  for (size_t s = 0; s < n; ++s) {
+    const Slot& sl = P.slots[s];
+    if (sl.arg_index >= 0 || sl.const_index >= 0 || sl.output || first[s] < 0) continue;
+    last[s] = std::max(last[s], sl.last_use);
+    order.push_back((int)s);
+  }
+  std::sort(order.begin(), order.end(), [&](int a, int b) { return P.slots[a].bytes > P.slots[b].bytes; });
+  auto align = [](int64_t x) { return (x + 255) & ~(int64_t)255; };
+  int64_t total = 0;
+  std::vector<int> placed;
+  std::vector<std::pair<int64_t, int64_t>> busy;
+  for (int s : order) {
+    const int64_t sz = align(std::max<int64_t>(P.slots[s].bytes, 16));
+    busy.clear();
+    for (int q : placed)
+      if (first[q] <= last[s] && first[s] <= last[q]) busy.push_back({(*off)[q], (*off)[q] + align(std::max<int64_t>(P.slots[q].bytes, 16))});
+    std::sort(busy.begin(), busy.end());
+    int64_t at = 0;
+    for (auto& b : busy) {
+      if (at + sz <= b.first) break;
+      at = std::max(at, b.second);
+    }
+    (*off)[s] = at;
+    total = std::max(total, at + sz);
+    placed.push_back(s);
+  }
+  return total;
+}
+
 Executable::~Executable() {
   const Driver& d = Drv();
   for (auto& kv : per_dev_) {
     cudaSetDevice(kv.first);
+    for (auto& g : kv.second.graphs)
+      if (g.exec) cudaGraphExecDestroy(g.exec);
+    if (kv.second.arena) cudaFree(kv.second.arena);
     for (void* p : kv.second.consts) cudaFree(p);
     if (d.ok)
       for (void* m : kv.second.modules) d.unload((CUmodule)m);
@@ -264,6 +340,11 @@ std::string Executable::Load(DeviceState& dev, PerDevice** pd) {
         }
       }
   }
+  const int64_t arena_bytes = LayoutArena(plan_, &p.arena_off);
+  if (arena_bytes > 0 && cudaMalloc(&p.arena, (size_t)arena_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return "device allocation of the " + std::to_string(arena_bytes) + "-byte intermediate arena failed";
+  }
   for (const ConstBlob& c : plan_.consts) {
     void* ptr = nullptr;
     if (cudaMalloc(&ptr, c.bytes.empty() ? 16 : c.bytes.size()) != cudaSuccess) return "constant upload: out of memory";
@@ -285,8 +366,10 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
   std::vector<void*> ptr(P.slots.size(), nullptr);
   std::vector<bool> owned(P.slots.size(), false);
   for (size_t k = 0; k < args.size(); ++k) ptr[P.arg_slots[k]] = const_cast<void*>(args[k]);
-  for (size_t s = 0; s < P.slots.size(); ++s)
+  for (size_t s = 0; s < P.slots.size(); ++s) {
     if (P.slots[s].const_index >= 0) ptr[s] = pd->consts[P.slots[s].const_index];
+    else if (pd->arena_off[s] >= 0) ptr[s] = (char*)pd->arena + pd->arena_off[s];
+  }
   cudaStream_t st = dev.stream;
   auto slot = [&](int s) -> std::string {
     if (s < 0 || ptr[s]) return "";
@@ -294,7 +377,9 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     if (e.empty()) owned[s] = true;
     return e;
   };
+  std::function<void()> abort_capture;
   auto fail = [&](const std::string& e) {
+    if (abort_capture) abort_capture();
     for (size_t s = 0; s < ptr.size(); ++s)
       if (owned[s]) DeviceFree(ptr[s], st);
     return e;
@@ -314,113 +399,189 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     for (auto& e : coll_done)
       if (e) { cudaEventDestroy(e); e = nullptr; }
   };
-  for (size_t i = 0; i < P.steps.size(); ++i) {
-    const Step& S = P.steps[i];
-    for (int k : S.wait_coll)
-      if (coll_done[k]) cudaStreamWaitEvent(st, coll_done[k], 0);
-    switch (S.kind) {
-      case StepKind::kFusion: {
-        for (const Launch& L : S.launches) {
-          std::vector<void*> vals;
-          for (int s : L.in_slots) { err = slot(s); if (!err.empty()) return fail(err); vals.push_back(ptr[s]); }
-          for (int s : L.out_slots) { err = slot(s); if (!err.empty()) return fail(err); vals.push_back(ptr[s]); }
-          if (L.scratch >= 0) { err = slot(L.scratch); if (!err.empty()) return fail(err); vals.push_back(ptr[L.scratch]); }
-          std::vector<void*> params;
-          for (void*& v : vals) params.push_back(&v);
-          int64_t gx = L.grid_x;
-          if (L.grid_stride) {
-            auto w = pd->wave.find(L.fn);
-            if (w != pd->wave.end()) gx = std::max<int64_t>(1, std::min(gx, w->second));
-          }
-          CUresult r = drv.launch((CUfunction)pd->fns.at(L.fn), (unsigned)gx, (unsigned)L.grid_y, (unsigned)L.grid_z, L.block, 1, 1,
-                                  L.smem, (CUstream)st, params.data(), nullptr);
-          if (r != CUDA_SUCCESS) return fail("launch of " + L.fn + " failed (" + std::to_string((int)r) + ")");
-        }
-        break;
-      }
-      case StepKind::kGemm: {
-        const GemmStep& g = S.gemm;
-        for (int s : {g.a, g.b, g.c, g.ws}) { err = slot(s); if (!err.empty()) return fail(err); }
-        int rc = b200k::Gemm(ptr[g.a], g.lda ? g.lda : (g.a_mn ? g.M : g.K), g.a_mn, ptr[g.b], g.ldb ? g.ldb : (g.b_mn ? g.N : g.K),
-                             g.b_mn, ptr[g.c], g.batch, g.M, g.N,
-                             g.K, PjrtType(g.ab), PjrtType(g.out), st, g.ws >= 0 ? (float*)ptr[g.ws] : nullptr);
-        if (rc != 0) return fail("gemm launch failed (" + std::to_string(rc) + ") for " + S.label);
-        break;
-      }
-      case StepKind::kAttention: {
-        const AttentionStep& a = S.attn;
-        for (int s : {a.q, a.k, a.v, a.o, a.lse}) { err = slot(s); if (!err.empty()) return fail(err); }
-        int rc = a.lse >= 0 ? b200k::AttentionFwdLse(ptr[a.q], ptr[a.k], ptr[a.v], ptr[a.o], (float*)ptr[a.lse], a.B, a.H, a.S,
-                                                     a.D, a.causal, a.scale, st)
-                            : b200k::AttentionFwd(ptr[a.q], ptr[a.k], ptr[a.v], ptr[a.o], a.B, a.H, a.S, a.D, a.causal, a.scale, st);
-        if (rc != 0) return fail("attention launch failed (" + std::to_string(rc) + ")");
-        break;
-      }
-      case StepKind::kAttentionBwd: {
-        const AttentionBwdStep& b = S.bwd;
-        for (int s : {b.q, b.k, b.v, b.o, b.dout, b.lse, b.dq, b.dk, b.dv, b.dq_acc, b.delta}) {
-          err = slot(s);
-          if (!err.empty()) return fail(err);
-        }
-        int rc = b200k::AttentionBwd(ptr[b.q], ptr[b.k], ptr[b.v], ptr[b.o], ptr[b.dout], (const float*)ptr[b.lse], ptr[b.dq],
-                                     ptr[b.dk], ptr[b.dv], (float*)ptr[b.dq_acc], (float*)ptr[b.delta], b.B, b.H, b.S, b.D,
-                                     b.causal, b.scale, st, b.dk_t ? 1 : 0);
-        if (rc != 0) return fail("attention backward launch failed (" + std::to_string(rc) + ")");
-        break;
-      }
-      case StepKind::kScatterAdd: {
-        const ScatterStep& s = S.scatter;
-        for (int q : {s.base, s.idx, s.upd, s.out}) { err = slot(q); if (!err.empty()) return fail(err); }
-        size_t bytes = (size_t)s.rows * s.row_len * DTBytes(s.dt);
-        if (ptr[s.out] != ptr[s.base]) cudaMemcpyAsync(ptr[s.out], ptr[s.base], bytes, cudaMemcpyDeviceToDevice, st);
-        int rc = b200_scatter_add_rows(ptr[s.idx], ptr[s.upd], ptr[s.out], s.n_upd, s.row_len, s.rows, PjrtType(s.dt),
-                                       PjrtType(s.idx_dt), st);
-        if (rc != 0) return fail("scatter-add launch failed");
-        break;
-      }
-      case StepKind::kCollective: {
-        const CollectiveStep& c = S.coll;
-        for (int q : {c.in, c.out}) { err = slot(q); if (!err.empty()) return fail(err); }
-        if (!comm) return fail("collective in a single-process program without a communicator");
-        cudaStream_t cs = st;
-        if (S.async) {
-          // on the communication stream, after everything enqueued so far on the compute stream
-          if (!dev.comm_stream && cudaStreamCreateWithFlags(&dev.comm_stream, cudaStreamNonBlocking) != cudaSuccess)
-            return fail("cannot create the communication stream");
-          cudaEvent_t ready;
-          cudaEventCreateWithFlags(&ready, cudaEventDisableTiming);
-          cudaEventRecord(ready, st);
-          cudaStreamWaitEvent(dev.comm_stream, ready, 0);
-          cudaEventDestroy(ready);
-          cs = dev.comm_stream;
-        }
-        if (c.op == CollKind::kAllReduce) err = comm->AllReduce(ptr[c.in], ptr[c.out], c.send_count, c.dt, c.reduce, cs);
-        else if (c.op == CollKind::kAllGather) err = comm->AllGather(ptr[c.in], ptr[c.out], c.send_count, c.dt, cs);
-        else err = comm->ReduceScatter(ptr[c.in], ptr[c.out], c.recv_count, c.dt, c.reduce, cs);
-        if (!err.empty()) { release_events(); return fail(err); }
-        if (S.async) {
-          cudaEventCreateWithFlags(&coll_done[i], cudaEventDisableTiming);
-          cudaEventRecord(coll_done[i], cs);
-        }
-        break;
-      }
-      case StepKind::kCopy: {
-        for (int q : {S.copy.src, S.copy.dst}) { err = slot(q); if (!err.empty()) return fail(err); }
-        cudaMemcpyAsync(ptr[S.copy.dst], ptr[S.copy.src], (size_t)S.copy.bytes, cudaMemcpyDeviceToDevice, st);
-        break;
-      }
+  // CUDA graphs: a program without collectives whose arguments and outputs sit at the addresses
+  // of an earlier execution (intermediates are at fixed arena offsets) replays that execution's
+  // launches as one graph.  The first execution with a set of addresses runs eagerly (lazy set-up
+  // happens there), the second is captured, later ones launch the graph.
+  bool has_coll = false;
+  for (const Step& S : P.steps) has_coll = has_coll || S.kind == StepKind::kCollective;
+  // (a program of a few launches gains nothing from a graph and pays its launch latency)
+  size_t n_launch = 0;
+  for (const Step& S : P.steps) n_launch += S.kind == StepKind::kFusion ? S.launches.size() : 1;
+  const bool graphs = !has_coll && n_launch >= 8 && !timer.on && !std::getenv("B200_NO_GRAPHS");
+  GraphEntry* ge = nullptr;
+  bool capture = false;
+  if (graphs) {
+    for (int s : P.out_slots) {
+      err = slot(s);
+      if (!err.empty()) return fail(err);
     }
-    if (timer.on) cudaEventRecord(evs[i + 1], st);
-    // release temporaries after their last use (stream-ordered)
-    for (size_t s = 0; s < P.slots.size(); ++s) {
-      const Slot& sl = P.slots[s];
-      if (owned[s] && !sl.output && sl.last_use == (int)i) {
-        DeviceFree(ptr[s], st);
-        ptr[s] = nullptr;
-        owned[s] = false;
+    std::vector<void*> key;
+    for (int s : P.arg_slots) key.push_back(ptr[s]);
+    for (int s : P.out_slots) key.push_back(ptr[s]);
+    for (auto& g : pd->graphs)
+      if (g.key == key) ge = &g;
+    if (ge && ge->exec) {
+      if (cudaGraphLaunch(ge->exec, st) != cudaSuccess) return fail("graph launch failed");
+      g_graph_launches.fetch_add(1);
+      ge->last = ++pd->graph_clock;
+      outs->clear();
+      for (int s : P.out_slots) outs->push_back(ptr[s]);
+      ExecTimerMarkEnd(dev.ordinal, st);
+      cudaError_t ce = cudaGetLastError();
+      return ce == cudaSuccess ? std::string() : std::string("CUDA error during execute: ") + cudaGetErrorString(ce);
+    }
+    if (ge) {
+      if (!ge->no_graph) {
+        capture = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+        if (!capture) cudaGetLastError();
       }
+    } else {
+      if (pd->graphs.size() >= 4) {   // forget the least recently used address set
+        auto old = std::min_element(pd->graphs.begin(), pd->graphs.end(),
+                                    [](const GraphEntry& a, const GraphEntry& b) { return a.last < b.last; });
+        if (old->exec) cudaGraphExecDestroy(old->exec);
+        pd->graphs.erase(old);
+      }
+      pd->graphs.push_back(GraphEntry{key, nullptr, ++pd->graph_clock});
     }
   }
+  auto end_capture = [&]() {
+    if (!capture) return;
+    capture = false;
+    cudaGraph_t g = nullptr;
+    if (cudaStreamEndCapture(st, &g) == cudaSuccess && g) {
+      cudaGraphExec_t ex = nullptr;
+      if (cudaGraphInstantiate(&ex, g, 0) == cudaSuccess) {
+        ge->exec = ex;
+        g_graph_captures.fetch_add(1);
+      }
+      cudaGraphDestroy(g);
+    }
+    cudaGetLastError();
+  };
+  abort_capture = [&]() {
+    if (!capture) return;
+    capture = false;
+    cudaGraph_t g = nullptr;
+    cudaStreamEndCapture(st, &g);
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+  };
+  auto run_steps = [&]() -> std::string {
+    for (size_t i = 0; i < P.steps.size(); ++i) {
+      const Step& S = P.steps[i];
+      for (int k : S.wait_coll)
+        if (coll_done[k]) cudaStreamWaitEvent(st, coll_done[k], 0);
+      switch (S.kind) {
+        case StepKind::kFusion: {
+          for (const Launch& L : S.launches) {
+            std::vector<void*> vals;
+            for (int s : L.in_slots) { err = slot(s); if (!err.empty()) return fail(err); vals.push_back(ptr[s]); }
+            for (int s : L.out_slots) { err = slot(s); if (!err.empty()) return fail(err); vals.push_back(ptr[s]); }
+            if (L.scratch >= 0) { err = slot(L.scratch); if (!err.empty()) return fail(err); vals.push_back(ptr[L.scratch]); }
+            std::vector<void*> params;
+            for (void*& v : vals) params.push_back(&v);
+            int64_t gx = L.grid_x;
+            if (L.grid_stride) {
+              auto w = pd->wave.find(L.fn);
+              if (w != pd->wave.end()) gx = std::max<int64_t>(1, std::min(gx, w->second));
+            }
+            CUresult r = drv.launch((CUfunction)pd->fns.at(L.fn), (unsigned)gx, (unsigned)L.grid_y, (unsigned)L.grid_z, L.block, 1, 1,
+                                    L.smem, (CUstream)st, params.data(), nullptr);
+            if (r != CUDA_SUCCESS) return fail("launch of " + L.fn + " failed (" + std::to_string((int)r) + ")");
+          }
+          break;
+        }
+        case StepKind::kGemm: {
+          const GemmStep& g = S.gemm;
+          for (int s : {g.a, g.b, g.c, g.ws}) { err = slot(s); if (!err.empty()) return fail(err); }
+          int rc = b200k::Gemm(ptr[g.a], g.lda ? g.lda : (g.a_mn ? g.M : g.K), g.a_mn, ptr[g.b], g.ldb ? g.ldb : (g.b_mn ? g.N : g.K),
+                               g.b_mn, ptr[g.c], g.batch, g.M, g.N,
+                               g.K, PjrtType(g.ab), PjrtType(g.out), st, g.ws >= 0 ? (float*)ptr[g.ws] : nullptr);
+          if (rc != 0) return fail("gemm launch failed (" + std::to_string(rc) + ") for " + S.label);
+          break;
+        }
+        case StepKind::kAttention: {
+          const AttentionStep& a = S.attn;
+          for (int s : {a.q, a.k, a.v, a.o, a.lse}) { err = slot(s); if (!err.empty()) return fail(err); }
+          int rc = a.lse >= 0 ? b200k::AttentionFwdLse(ptr[a.q], ptr[a.k], ptr[a.v], ptr[a.o], (float*)ptr[a.lse], a.B, a.H, a.S,
+                                                       a.D, a.causal, a.scale, st)
+                              : b200k::AttentionFwd(ptr[a.q], ptr[a.k], ptr[a.v], ptr[a.o], a.B, a.H, a.S, a.D, a.causal, a.scale, st);
+          if (rc != 0) return fail("attention launch failed (" + std::to_string(rc) + ")");
+          break;
+        }
+        case StepKind::kAttentionBwd: {
+          const AttentionBwdStep& b = S.bwd;
+          for (int s : {b.q, b.k, b.v, b.o, b.dout, b.lse, b.dq, b.dk, b.dv, b.dq_acc, b.delta}) {
+            err = slot(s);
+            if (!err.empty()) return fail(err);
+          }
+          int rc = b200k::AttentionBwd(ptr[b.q], ptr[b.k], ptr[b.v], ptr[b.o], ptr[b.dout], (const float*)ptr[b.lse], ptr[b.dq],
+                                       ptr[b.dk], ptr[b.dv], (float*)ptr[b.dq_acc], (float*)ptr[b.delta], b.B, b.H, b.S, b.D,
+                                       b.causal, b.scale, st, b.dk_t ? 1 : 0);
+          if (rc != 0) return fail("attention backward launch failed (" + std::to_string(rc) + ")");
+          break;
+        }
+        case StepKind::kScatterAdd: {
+          const ScatterStep& s = S.scatter;
+          for (int q : {s.base, s.idx, s.upd, s.out}) { err = slot(q); if (!err.empty()) return fail(err); }
+          size_t bytes = (size_t)s.rows * s.row_len * DTBytes(s.dt);
+          if (ptr[s.out] != ptr[s.base]) cudaMemcpyAsync(ptr[s.out], ptr[s.base], bytes, cudaMemcpyDeviceToDevice, st);
+          int rc = b200_scatter_add_rows(ptr[s.idx], ptr[s.upd], ptr[s.out], s.n_upd, s.row_len, s.rows, PjrtType(s.dt),
+                                         PjrtType(s.idx_dt), st);
+          if (rc != 0) return fail("scatter-add launch failed");
+          break;
+        }
+        case StepKind::kCollective: {
+          const CollectiveStep& c = S.coll;
+          for (int q : {c.in, c.out}) { err = slot(q); if (!err.empty()) return fail(err); }
+          if (!comm) return fail("collective in a single-process program without a communicator");
+          cudaStream_t cs = st;
+          if (S.async) {
+            // on the communication stream, after everything enqueued so far on the compute stream
+            if (!dev.comm_stream && cudaStreamCreateWithFlags(&dev.comm_stream, cudaStreamNonBlocking) != cudaSuccess)
+              return fail("cannot create the communication stream");
+            cudaEvent_t ready;
+            cudaEventCreateWithFlags(&ready, cudaEventDisableTiming);
+            cudaEventRecord(ready, st);
+            cudaStreamWaitEvent(dev.comm_stream, ready, 0);
+            cudaEventDestroy(ready);
+            cs = dev.comm_stream;
+          }
+          if (c.op == CollKind::kAllReduce) err = comm->AllReduce(ptr[c.in], ptr[c.out], c.send_count, c.dt, c.reduce, cs);
+          else if (c.op == CollKind::kAllGather) err = comm->AllGather(ptr[c.in], ptr[c.out], c.send_count, c.dt, cs);
+          else err = comm->ReduceScatter(ptr[c.in], ptr[c.out], c.recv_count, c.dt, c.reduce, cs);
+          if (!err.empty()) { release_events(); return fail(err); }
+          if (S.async) {
+            cudaEventCreateWithFlags(&coll_done[i], cudaEventDisableTiming);
+            cudaEventRecord(coll_done[i], cs);
+          }
+          break;
+        }
+        case StepKind::kCopy: {
+          for (int q : {S.copy.src, S.copy.dst}) { err = slot(q); if (!err.empty()) return fail(err); }
+          cudaMemcpyAsync(ptr[S.copy.dst], ptr[S.copy.src], (size_t)S.copy.bytes, cudaMemcpyDeviceToDevice, st);
+          break;
+        }
+      }
+      if (timer.on) cudaEventRecord(evs[i + 1], st);
+    }
+    return std::string();
+  };
+  err = run_steps();
+  if (!err.empty()) return err;
+  if (capture) {
+    end_capture();
+    if (ge->exec) {
+      if (cudaGraphLaunch(ge->exec, st) != cudaSuccess) return fail("graph launch failed");
+    } else {
+      ge->no_graph = true;             // capture failed: this address set runs eagerly from now on
+      err = run_steps();
+      if (!err.empty()) return err;
+    }
+  }
+  abort_capture = nullptr;
   outs->clear();
   for (int s : P.out_slots) {
     if (!ptr[s]) { err = slot(s); if (!err.empty()) return fail(err); }
@@ -481,6 +642,10 @@ extern "C" int b200_compile_report(const char* text, size_t size, int num_proces
   if (report.size() + 1 > out_size) return -1;
   std::memcpy(out, report.c_str(), report.size() + 1);
   return rc;
+}
+
+extern "C" long long b200_graph_stats(int which) {
+  return which == 0 ? b200::g_graph_captures.load() : b200::g_graph_launches.load();
 }
 
 extern "C" double b200_exec_timer(int action) {

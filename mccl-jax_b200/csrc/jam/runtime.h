@@ -43,11 +43,24 @@ class Executable {
   std::string Run(DeviceState& dev, const std::vector<const void*>& args, std::vector<void*>* outs, Comm* comm);
 
  private:
+  struct GraphEntry {
+    std::vector<void*> key;                  // argument then output addresses
+    cudaGraphExec_t exec = nullptr;          // null until the second execution with these addresses
+    uint64_t last = 0;
+    bool no_graph = false;                   // capture failed once: run eagerly
+  };
   struct PerDevice {
     std::vector<void*> modules;              // CUmodule per NVRTC group
     std::map<std::string, void*> fns;        // CUfunction by kernel name
     std::map<std::string, int64_t> wave;     // grid-stride kernels: resident CTAs on the device
     std::vector<void*> consts;               // uploaded constants
+    // Intermediates live at fixed offsets in one arena allocated at load: slots whose live ranges
+    // (first to last step that touches them) do not overlap share bytes.  Executions on a device
+    // are stream-ordered, so each reuses the arena; only outputs are allocated per execution.
+    void* arena = nullptr;
+    std::vector<int64_t> arena_off;          // per slot, -1 when not in the arena
+    std::vector<GraphEntry> graphs;          // captured executions by argument / output addresses
+    uint64_t graph_clock = 0;
   };
   std::string Load(DeviceState& dev, PerDevice** pd);
 

@@ -300,3 +300,31 @@ def test_repeated_execution_reuses_executable(client):
         again = exe.execute(bufs)[0].to_numpy()
         np.testing.assert_array_equal(again.view(np.uint16), first.view(np.uint16))
     exe.destroy()
+
+
+def test_repeated_executions_replay_a_cuda_graph(client, lib_path):
+    """An execution whose buffers sit at the addresses of an earlier one is captured once and then
+    replayed as a CUDA graph; every replay gives the eager result and the oracle's."""
+    import ctypes
+    lib = ctypes.CDLL(lib_path)
+    lib.b200_graph_stats.restype = ctypes.c_longlong
+    p = configs.mlp_program(seed=3)
+    exe = client.compile(p.text)
+    bufs = [client.buffer_from_host(x) for x in p.inputs]
+    cap0, rep0 = lib.b200_graph_stats(0), lib.b200_graph_stats(1)
+    results = []
+    for _ in range(6):
+        outs = exe.execute(bufs)
+        results.append([o.to_numpy() for o in outs])
+        for o in outs:
+            o.delete()
+    assert lib.b200_graph_stats(0) > cap0 and lib.b200_graph_stats(1) > rep0
+    for r in results[1:]:
+        for a, b in zip(results[0], r):
+            np.testing.assert_array_equal(a, b)
+    refs = oracle_run(p.text, p.inputs)
+    for o, r in zip(results[-1], refs):
+        assert_close(np.asarray(o, np.float32), np.asarray(r, np.float32), RTOL_F32 * 10, "mlp step via graph")
+    for b in bufs:
+        b.delete()
+    exe.destroy()
