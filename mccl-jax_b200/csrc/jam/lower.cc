@@ -245,6 +245,7 @@ struct Gen {
   std::string vinner;
   int branch_depth = 0;                                   // inside concatenate / pad branches
   std::unordered_map<std::string, std::string> vloads;    // leaf base -> vector register
+  std::unordered_map<std::string, std::vector<std::string>> reindex_cse;   // vector-mode reshapes
   std::vector<std::vector<std::string>> lane_identity;   // identity index per lane (vector mode)
   std::unordered_map<int, std::vector<std::string>> lane_group_regs;
   // Ragged-row walks (non-empty shift_dims): the lanes' four elements are 16-byte aligned only in
@@ -253,18 +254,55 @@ struct Gen {
   std::vector<int64_t> shift_dims;
   std::vector<std::string> shift_prefix;
 
+  // Lane-affine index strings: the innermost index of lane l equals lane 0's (`base`) plus l.  The
+  // group's own lane names (vinner_l) are; reshapes, slices and pads that keep four consecutive
+  // elements consecutive produce more (canonical names, see Canon), each recorded here with whether
+  // its lane-0 value is a multiple of 4 (then lane 0 may issue one vector access for all four).
+  struct LaneIx {
+    std::string base;
+    int lane = 0;
+    bool al4 = false;
+  };
+  std::unordered_map<std::string, LaneIx> lane_ix;
+  bool LaneInfo(const std::string& s, LaneIx* out) const {
+    if (!vec) return false;
+    if (s.size() == vinner.size() + 2 && s.compare(0, vinner.size() + 1, vinner + "_") == 0 && s.back() >= '0' &&
+        s.back() <= '3') {
+      *out = LaneIx{vinner + "_0", s.back() - '0', shift_dims.empty()};
+      return true;
+    }
+    auto it = lane_ix.find(s);
+    if (it == lane_ix.end()) return false;
+    *out = it->second;
+    return true;
+  }
+  std::string Canon(const std::string& base, int l) const {
+    if (l == 0) return base;
+    if (base == vinner + "_0") return vinner + "_" + std::to_string(l);
+    return "(" + base + "+" + std::to_string(l) + ")";
+  }
+  // records the lane strings of a derived lane-0 index `b0` and returns lane l's
+  std::string DeriveLane(const std::string& b0, int l, bool al4) {
+    lane_ix[b0] = LaneIx{b0, 0, al4};
+    const std::string c = Canon(b0, l);
+    lane_ix[c] = LaneIx{b0, l, al4};
+    return c;
+  }
+
   int LaneOf(const std::vector<std::string>& idx) const {
     if (!vec || idx.empty()) return -1;
-    const std::string& last = idx.back();
-    if (last.size() != vinner.size() + 2 || last.compare(0, vinner.size() + 1, vinner + "_") != 0) return -1;
+    LaneIx li;
+    if (!LaneInfo(idx.back(), &li)) return -1;
     for (size_t k = 0; k + 1 < idx.size(); ++k)
-      if (idx[k].find(vinner + "_") != std::string::npos) return -1;
-    return last.back() - '0';
+      if (idx[k].find(vinner + "_") != std::string::npos || lane_ix.count(idx[k])) return -1;
+    return li.lane;
   }
 
   std::string VecLoad(DT dt, int slot, const std::vector<std::string>& idx, int lane) {
     std::vector<std::string> base = idx;
-    base.back() = vinner + "_0";
+    LaneIx li;
+    LaneInfo(idx.back(), &li);
+    base.back() = li.base;
     std::string key = std::to_string(slot);
     for (auto& s : base) key += "|" + s;
     auto it = vloads.find(key);
@@ -353,10 +391,12 @@ struct Gen {
         conflict = true;
       }
       const int lane = branch_depth == 0 ? LaneOf(idx) : -1;
-      const bool aligned4 = shift_dims.empty()
-                                ? !ty.dims.empty() && ty.dims.back() % 4 == 0
-                                : ty.dims == shift_dims && idx.size() == shift_prefix.size() + 1 &&
-                                      std::equal(shift_prefix.begin(), shift_prefix.end(), idx.begin());
+      LaneIx li;
+      const bool lane_ok = lane >= 0 && LaneInfo(idx.back(), &li);
+      const bool aligned4 = lane_ok && (shift_dims.empty()
+                                ? li.al4 && !ty.dims.empty() && ty.dims.back() % 4 == 0
+                                : ty.dims == shift_dims && idx.size() == shift_prefix.size() + 1 && li.base == vinner + "_0" &&
+                                      std::equal(shift_prefix.begin(), shift_prefix.end(), idx.begin()));
       if (lane >= 0 && (ty.dt == DT::kF32 || ty.dt == DT::kBF16 || ty.dt == DT::kF16) && aligned4) {
         cur_dims = ty.dims;
         std::string r = VecLoad(ty.dt, slot, idx, lane);
@@ -385,7 +425,25 @@ struct Gen {
       return opnd(0, j);
     }
     if (n == "reshape" || (n == "bitcast_convert" && DTBytes(ty.dt) == DTBytes(op->operands[0]->type.dt) && false)) {
-      return opnd(0, Reindex(idx, ty.dims, op->operands[0]->type.dims));
+      const auto& in = op->operands[0]->type.dims;
+      LaneIx li;
+      if (vec && !idx.empty() && !in.empty() && ty.dims.back() % 4 == 0 && in.back() % 4 == 0 && LaneInfo(idx.back(), &li) &&
+          li.al4) {
+        // four consecutive, 4-aligned elements of the result are four consecutive elements of the
+        // operand's innermost dim: lane l reads lane 0's operand index with the innermost + l
+        std::vector<std::string> idx0 = idx;
+        idx0.back() = li.base;
+        std::string key;
+        for (auto& q : idx0) key += q + "|";
+        for (int64_t d : in) key += std::to_string(d) + ",";
+        auto hit = reindex_cse.find(key);
+        std::vector<std::string> j0 = hit != reindex_cse.end() ? hit->second : Reindex(idx0, ty.dims, in);
+        reindex_cse[key] = j0;
+        std::vector<std::string> j = j0;
+        j.back() = DeriveLane(j0.back(), li.lane, true);
+        return opnd(0, j);
+      }
+      return opnd(0, Reindex(idx, ty.dims, in));
     }
     if (n == "transpose") {
       const auto& perm = op->ints.at("dims");
@@ -405,6 +463,9 @@ struct Gen {
       std::vector<std::string> j(idx.size());
       for (size_t k = 0; k < idx.size(); ++k)
         j[k] = "(" + std::to_string(st[k]) + "+(" + idx[k] + ")*" + std::to_string(sd[k]) + ")";
+      LaneIx li;
+      if (!idx.empty() && sd.back() == 1 && LaneInfo(idx.back(), &li))
+        j.back() = DeriveLane("(" + std::to_string(st.back()) + "+(" + li.base + ")*1)", li.lane, li.al4 && st.back() % 4 == 0);
       return opnd(0, j);
     }
     if (n == "convert") {
@@ -459,10 +520,12 @@ struct Gen {
         body << indent << (k ? "else " : "") << "if ((" << idx[d] << ") < " << off + len << ") {\n";
         indent += "  ";
         auto saved = cse;          // values computed inside a branch are not visible outside
+        auto saved_r = reindex_cse;
         ++branch_depth;
         std::string x = Emit(op->operands[k], j);
         --branch_depth;
         cse = saved;
+        reindex_cse = saved_r;
         body << indent << r << " = " << x << ";\n";
         indent = save;
         body << indent << "}\n";
@@ -474,6 +537,53 @@ struct Gen {
       // pretty form: low / high / interior; generic form: edge_padding_low / interior_padding
       const auto& lo = op->ints.count("low") ? op->ints.at("low") : op->ints.at("edge_padding_low");
       const auto& it = op->ints.count("interior") ? op->ints.at("interior") : op->ints.at("interior_padding");
+      const auto& ind = op->operands[0]->type.dims;
+      LaneIx li;
+      if (vec && branch_depth == 0 && !idx.empty() && LaneInfo(idx.back(), &li) && li.al4 && li.lane == 0 &&
+          lo.back() % 4 == 0 && it.back() == 0 && ind.back() % 4 == 0 && ty.dims.back() % 4 == 0) {
+        // the four lanes lie on the same side of every edge: one branch computes all four (their
+        // reads inside may then be one vector access) and lanes 1-3 are left in the value cache
+        std::string pv = Emit(op->operands[1], {});
+        std::vector<std::string> r(4), cond_parts;
+        for (int l = 0; l < 4; ++l) {
+          r[l] = "t" + std::to_string(tmp++);
+          body << indent << CType(ty.dt) << " " << r[l] << " = " << pv << ";\n";
+        }
+        std::string cond = "true";
+        std::vector<std::string> j(idx.size());
+        for (size_t k = 0; k < idx.size(); ++k) {
+          std::string q = "((" + idx[k] + ")-(" + std::to_string(lo[k]) + "))";
+          int64_t s = it[k] + 1;
+          cond += " && " + q + " >= 0 && " + q + " < " + std::to_string((ind[k] - 1) * s + 1);
+          if (s > 1) cond += " && " + q + " % " + std::to_string(s) + " == 0";
+          j[k] = s > 1 ? "(" + q + "/" + std::to_string(s) + ")" : q;
+        }
+        const std::string q0 = j.back();
+        body << indent << "if (" << cond << ") {\n";
+        std::string save = indent;
+        indent += "  ";
+        auto saved = cse;
+        auto saved_v = vloads;
+        auto saved_r = reindex_cse;
+        for (int l = 0; l < 4; ++l) {
+          std::vector<std::string> jl = j;
+          jl.back() = DeriveLane(q0, l, true);
+          const std::string x = Emit(op->operands[0], jl);
+          body << indent << r[l] << " = " << x << ";\n";
+        }
+        cse = saved;
+        vloads = saved_v;
+        reindex_cse = saved_r;
+        indent = save;
+        body << indent << "}\n";
+        for (int l = 1; l < 4; ++l) {
+          std::string key = std::to_string(v->id);
+          for (size_t k = 0; k + 1 < idx.size(); ++k) key += "|" + idx[k];
+          key += "|" + Canon(li.base, l);
+          cse[key] = r[l];
+        }
+        return r[0];
+      }
       std::string pv = Emit(op->operands[1], {});
       std::string r = "t" + std::to_string(tmp++);
       body << indent << CType(ty.dt) << " " << r << " = " << pv << ";\n";
@@ -491,10 +601,12 @@ struct Gen {
       std::string save = indent;
       indent += "  ";
       auto saved = cse;
+      auto saved_r = reindex_cse;
       ++branch_depth;
       std::string x = Emit(op->operands[0], j);
       --branch_depth;
       cse = saved;
+      reindex_cse = saved_r;
       body << indent << r << " = " << x << ";\n";
       indent = save;
       body << indent << "}\n";
@@ -1873,6 +1985,7 @@ class Lowerer {
     auto phase_begin = [&]() {
       gen.cse.clear();
       gen.vloads.clear();
+      gen.reindex_cse.clear();
       gen.body.str("");
       gen.body.clear();
       gen.indent = "      ";
@@ -2040,6 +2153,7 @@ class Lowerer {
       } else {
         // row scalar: every thread of the row computes it
         gen.cse.clear();
+        gen.reindex_cse.clear();
         gen.body.str("");
         gen.body.clear();
         gen.indent = "    ";

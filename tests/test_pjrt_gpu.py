@@ -328,3 +328,29 @@ def test_repeated_executions_replay_a_cuda_graph(client, lib_path):
     for b in bufs:
         b.delete()
     exe.destroy()
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f32"])
+def test_head_gradients_assembled_into_rows(client, dt):
+    """The attention backward's dq / dk / dv ([B, H, S, D]) transposed to [B*S, H*D] and placed side
+    by side by pad + add (what autodiff of a slice produces), plus a sliced, offset read: the
+    vectorised walk reads four consecutive elements per lane through reshape / transpose / pad /
+    slice.  Pure data movement, so bit-exact against the oracle."""
+    B, H, S, D = 2, 3, 64, 32
+    b = Builder("jit_assemble")
+    parts = [b.arg((B, H, S, D), dt) for _ in range(3)]
+    rows = []
+    for i, p in enumerate(parts):
+        r = b.reshape(b.transpose(p, (0, 2, 1, 3)), (B * S, H * D))
+        rows.append(b.pad(r, 0.0, [0, i * H * D], [0, (2 - i) * H * D]))
+    out = rows[0] + rows[1] + rows[2]
+    shifted = b.slice(out, [0, 4], [B * S, 3 * H * D - 4])           # aligned offset
+    odd = b.slice(out, [0, 1], [B * S, 3 * H * D - 7])               # unaligned offset
+    text = b.text([out, shifted * 2.0, odd])
+    rng = np.random.default_rng(9)
+    npdt = ml_dtypes.bfloat16 if dt == "bf16" else np.float32
+    ins = [rng.standard_normal((B, H, S, D)).astype(npdt) for _ in range(3)]
+    outs = client.run(text, ins)
+    refs = oracle_run(text, ins)
+    for o, r in zip(outs, refs):
+        np.testing.assert_array_equal(np.asarray(o, np.float32), np.asarray(r, np.float32))
