@@ -50,8 +50,11 @@ struct BCfg {
   static constexpr int kdSOff = kPOff + 2 * kTile;    // dS^T, same layout
   static constexpr int kLseOff = kdSOff + 2 * kTile;  // 2 stages x 128 f32
   static constexpr int kDeltaOff = kLseOff + 2 * TB * 4;
-  static constexpr int kBarOff = kDeltaOff + 2 * TB * 4;
+  // dQ staging: per dQ warp two 32-row x 32-column f32 boxes (128-byte swizzled, 4 KB each)
+  static constexpr int kdQOff = kDeltaOff + 2 * TB * 4;
+  static constexpr int kBarOff = kdQOff + 4 * 2 * 4096;
   static constexpr int kSmem = kBarOff + 256 + 1024;
+  static_assert(kdQOff % 1024 == 0, "swizzled boxes need 1024-byte alignment");
 };
 
 enum { kKVFull = 0, kQFull = 1, kQEmpty = 3, kSFull = 5, kSFree = 6, kPdSFull = 7 /* 2: per query half */, kPdSFree = 9,
@@ -69,6 +72,15 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return r;
 }
 __device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// f32 box added element-wise into global memory by the TMA unit (an L2 reduction per line)
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(map), "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_group_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // 32 consecutive keys-by-query values of row r, as bf16, into a 128-byte-swizzled K-major tile made
 // of two 64-column blocks (column c0 .. c0+31).
@@ -84,6 +96,7 @@ template <bool CAUSAL>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                const __grid_constant__ CUtensorMap tmdQ,
                 const float* __restrict__ lse2, const float* __restrict__ delta, float* __restrict__ dq_acc,
                 __nv_bfloat16* __restrict__ dK, __nv_bfloat16* __restrict__ dV, int S, float scale, float scale_log2,
                 int dk_t) {
@@ -300,26 +313,41 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
   } else {
     // ------------------------------------------------------------------ dQ readout (query rows)
+    // each warp's 32 query rows leave as two 32 x 32 f32 boxes added into dq_acc by TMA reductions
+    // (whole 128-byte lines per L2 operation instead of one 16-byte atomic per row and chunk)
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    uint8_t* boxes = smem + C::kdQOff + quarter * 8192;
     for (int i = 0; i < n_it; ++i) {
       if (!mbar_wait_warp(&bars[kdQFull], i & 1, kErrTimeoutAcc, err)) break;
       tc_fence_after();
-      float* out = dq_acc + (row_base + (long long)(qt0 + i) * TB + r) * HD;
-#pragma unroll
-      for (int c = 0; c < HD; c += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem + lane_off + 384 + c, v);
+      const int row0 = (int)(row_base + (long long)(qt0 + i) * TB + quarter * 32);
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        uint32_t v[32];
+        tmem_ld16(tmem + lane_off + 384 + h * 32, *reinterpret_cast<uint32_t(*)[16]>(v));
+        tmem_ld16(tmem + lane_off + 384 + h * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
         tmem_wait_ld();
+        if (h == 1) {                             // both columns read: the MMA may overwrite dQ_t
+          tc_fence_before();
+          mbar_arrive(&bars[kdQFree]);
+        }
+        uint8_t* box = boxes + h * 4096;
+        if (lane == 0) bulk_wait_group_read0();   // this box's previous reduction has read it
+        __syncwarp();
 #pragma unroll
-        for (int e = 0; e < 16; e += 4)
-          atomicAdd((float4*)(out + c + e), make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]),
-                                                        __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3])));
+        for (int q = 0; q < 8; ++q)
+          *(uint4*)(box + lane * 128 + ((q ^ (lane & 7)) << 4)) = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_2d(&tmdQ, box, h * 32, row0);
+          bulk_commit_group();
+        }
       }
-      tc_fence_before();
-      mbar_arrive(&bars[kdQFree]);
     }
+    if (lane == 0) bulk_wait_group0();            // reductions complete before the CTA exits
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -329,18 +357,34 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   }
 }
 
-// delta[row] = sum_d dO[row, d] * O[row, d] (f32), one warp per row, two elements per lane.
+// delta = rowsum(dO * O): eight threads per 64-element row, one 16-byte load of each operand per
+// thread, a three-step shuffle; a warp covers four rows per step (512 contiguous bytes per load)
 __global__ void __launch_bounds__(256) attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ O,
                                                              const __nv_bfloat16* __restrict__ dO, float* __restrict__ delta,
                                                              long long rows) {
-  const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const int lane = threadIdx.x & 31;
-  const __nv_bfloat162 o = ((const __nv_bfloat162*)(O + row * HD))[lane];
-  const __nv_bfloat162 g = ((const __nv_bfloat162*)(dO + row * HD))[lane];
-  float s = __bfloat162float(o.x) * __bfloat162float(g.x) + __bfloat162float(o.y) * __bfloat162float(g.y);
-  for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if (lane == 0) delta[row] = s;
+  const int sub = threadIdx.x & 7, lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * 8;
+  // warp-uniform loop over groups of four rows; a row past the end contributes nothing
+  for (long long r4 = ((long long)blockIdx.x * 256 + threadIdx.x) >> 5; r4 * 4 < rows; r4 += warps) {
+    const long long row = r4 * 4 + (lane >> 3);
+    float s = 0.f;
+    if (row < rows) {
+      const uint4 o = ((const uint4*)(O + row * HD))[sub];
+      const uint4 g = ((const uint4*)(dO + row * HD))[sub];
+      const __nv_bfloat162* o2 = (const __nv_bfloat162*)&o;
+      const __nv_bfloat162* g2 = (const __nv_bfloat162*)&g;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 a = __bfloat1622float2(o2[e]), b = __bfloat1622float2(g2[e]);
+        s = fmaf(a.x, b.x, s);
+        s = fmaf(a.y, b.y, s);
+      }
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    if (sub == 0 && row < rows) delta[row] = s;
+  }
 }
 
 __global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y,
@@ -360,6 +404,19 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 EncodeTiledFn GetEncodeTiled();
 
 // [rows, 64] bf16, 128 x 64 boxes, 128-byte swizzle.
+// dq_acc rows (64 f32) as 32 x 32 boxes, 128-byte swizzled, for the TMA reductions
+static bool MapRowsF32(CUtensorMap* map, const void* ptr, uint64_t rows) {
+  EncodeTiledFn enc = GetEncodeTiled();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {HD, rows};
+  cuuint64_t strides[1] = {HD * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static bool MapRows64(CUtensorMap* map, const void* ptr, uint64_t rows) {
   EncodeTiledFn enc = GetEncodeTiled();
   if (!enc) return false;
@@ -395,18 +452,20 @@ int AttentionBwd(const void* q, const void* k, const void* v, const void* o, con
   });
   const long long rows = (long long)B * H * S;
   CUtensorMap mq, mk, mv, mdo;
-  if (!MapRows64(&mq, q, rows) || !MapRows64(&mk, k, rows) || !MapRows64(&mv, v, rows) || !MapRows64(&mdo, dout, rows))
+  CUtensorMap mdq;
+  if (!MapRows64(&mq, q, rows) || !MapRows64(&mk, k, rows) || !MapRows64(&mv, v, rows) || !MapRows64(&mdo, dout, rows) ||
+      !MapRowsF32(&mdq, dq_acc, rows))
     return -2;
   if (cudaMemsetAsync(dq_acc, 0, (size_t)rows * HD * 4, st) != cudaSuccess) return -3;
-  attn_bwd_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>((const __nv_bfloat16*)o, (const __nv_bfloat16*)dout,
-                                                                    delta, rows);
+  attn_bwd_delta_kernel<<<(unsigned)std::min<long long>((rows + 31) / 32, 148 * 8), 256, 0, st>>>(
+      (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, delta, rows);
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid((unsigned)(B * H * (S / TB)));
   if (causal)
-    attn_bwd_kernel<true><<<grid, kThreads, C::kSmem, st>>>(mq, mk, mv, mdo, lse2, delta, dq_acc, (__nv_bfloat16*)dk,
+    attn_bwd_kernel<true><<<grid, kThreads, C::kSmem, st>>>(mq, mk, mv, mdo, mdq, lse2, delta, dq_acc, (__nv_bfloat16*)dk,
                                                         (__nv_bfloat16*)dv, S, scale, scale_log2, dk_t);
   else
-    attn_bwd_kernel<false><<<grid, kThreads, C::kSmem, st>>>(mq, mk, mv, mdo, lse2, delta, dq_acc, (__nv_bfloat16*)dk,
+    attn_bwd_kernel<false><<<grid, kThreads, C::kSmem, st>>>(mq, mk, mv, mdo, mdq, lse2, delta, dq_acc, (__nv_bfloat16*)dk,
                                                          (__nv_bfloat16*)dv, S, scale, scale_log2, dk_t);
   const long long n4 = rows * HD / 4;
   f32_to_bf16_kernel<<<(unsigned)std::min<long long>((n4 + 255) / 256, 148 * 8), 256, 0, st>>>(dq_acc, (__nv_bfloat16*)dq, n4);
