@@ -262,13 +262,15 @@ struct Gen {
     std::string base;
     int lane = 0;
     bool al4 = false;
+    bool exact = true;       // the string's value is base + lane (false: clamped at the row's end)
   };
   std::unordered_map<std::string, LaneIx> lane_ix;
+  bool lanes_clamped = false;   // padded ragged rows: lanes past the end hold the last index
   bool LaneInfo(const std::string& s, LaneIx* out) const {
     if (!vec) return false;
     if (s.size() == vinner.size() + 2 && s.compare(0, vinner.size() + 1, vinner + "_") == 0 && s.back() >= '0' &&
         s.back() <= '3') {
-      *out = LaneIx{vinner + "_0", s.back() - '0', shift_dims.empty()};
+      *out = LaneIx{vinner + "_0", s.back() - '0', shift_dims.empty(), !lanes_clamped};
       return true;
     }
     auto it = lane_ix.find(s);
@@ -325,7 +327,23 @@ struct Gen {
     return Var(dt, dt == DT::kBF16 ? "bf2f(" + half + ")" : "h2f(" + half + ")");
   }
   std::vector<int64_t> cur_dims;   // dims of the leaf being vector-loaded (set by the caller)
-  std::string LinearDims(const std::vector<std::string>& idx) const { return Linear(idx, cur_dims); }
+  int64_t cur_pitch = 0;           // and its padded row pitch (0: dense)
+  std::string LinearDims(const std::vector<std::string>& idx) const {
+    return cur_pitch ? PitchedLinear(idx, cur_dims, cur_pitch) : Linear(idx, cur_dims);
+  }
+  // slots stored with a padded innermost row pitch (a dot's output whose rows break the 16-byte
+  // rule, or a dot operand stored for in-place use)
+  const std::unordered_map<int, int64_t>* slot_pitch = nullptr;
+  int64_t SlotPitch(int slot) const {
+    if (!slot_pitch) return 0;
+    auto it = slot_pitch->find(slot);
+    return it == slot_pitch->end() ? 0 : it->second;
+  }
+  static std::string PitchedLinear(const std::vector<std::string>& idx, const std::vector<int64_t>& dims, int64_t pitch) {
+    std::vector<std::string> outer(idx.begin(), idx.end() - 1);
+    std::vector<int64_t> od(dims.begin(), dims.end() - 1);
+    return "(" + Linear(outer, od) + ")*" + std::to_string(pitch) + "LL+(" + idx.back() + ")";
+  }
 
   // Row-group mode: values already reduced or computed for the current row live in registers and
   // may only be read at the row's own index (`row_ident`; unit dims may read index 0).
@@ -393,16 +411,19 @@ struct Gen {
       const int lane = branch_depth == 0 ? LaneOf(idx) : -1;
       LaneIx li;
       const bool lane_ok = lane >= 0 && LaneInfo(idx.back(), &li);
+      // a padded row pitch (a multiple of 4 elements) keeps every row 16-byte aligned
+      const int64_t pitch = SlotPitch(slot);
       const bool aligned4 = lane_ok && (shift_dims.empty()
-                                ? li.al4 && !ty.dims.empty() && ty.dims.back() % 4 == 0
-                                : ty.dims == shift_dims && idx.size() == shift_prefix.size() + 1 && li.base == vinner + "_0" &&
+                                ? li.al4 && !ty.dims.empty() && (pitch ? pitch % 4 == 0 : ty.dims.back() % 4 == 0)
+                                : !pitch && ty.dims == shift_dims && idx.size() == shift_prefix.size() + 1 && li.base == vinner + "_0" &&
                                       std::equal(shift_prefix.begin(), shift_prefix.end(), idx.begin()));
       if (lane >= 0 && (ty.dt == DT::kF32 || ty.dt == DT::kBF16 || ty.dt == DT::kF16) && aligned4) {
         cur_dims = ty.dims;
+        cur_pitch = pitch;
         std::string r = VecLoad(ty.dt, slot, idx, lane);
         return ty.dt == DT::kF32 ? Var(ty.dt, r) : r;
       }
-      return Var(ty.dt, LoadExpr(ty.dt, Param(slot), Linear(idx, ty.dims)));
+      return Var(ty.dt, LoadExpr(ty.dt, Param(slot), pitch ? PitchedLinear(idx, ty.dims, pitch) : Linear(idx, ty.dims)));
     }
     const Op* op = v->def;
     if (!op) throw LowerError{"internal: unmaterialized argument"};
@@ -428,7 +449,7 @@ struct Gen {
       const auto& in = op->operands[0]->type.dims;
       LaneIx li;
       if (vec && !idx.empty() && !in.empty() && ty.dims.back() % 4 == 0 && in.back() % 4 == 0 && LaneInfo(idx.back(), &li) &&
-          li.al4) {
+          li.al4 && li.exact) {
         // four consecutive, 4-aligned elements of the result are four consecutive elements of the
         // operand's innermost dim: lane l reads lane 0's operand index with the innermost + l
         std::vector<std::string> idx0 = idx;
@@ -464,7 +485,7 @@ struct Gen {
       for (size_t k = 0; k < idx.size(); ++k)
         j[k] = "(" + std::to_string(st[k]) + "+(" + idx[k] + ")*" + std::to_string(sd[k]) + ")";
       LaneIx li;
-      if (!idx.empty() && sd.back() == 1 && LaneInfo(idx.back(), &li))
+      if (!idx.empty() && sd.back() == 1 && LaneInfo(idx.back(), &li) && li.exact)
         j.back() = DeriveLane("(" + std::to_string(st.back()) + "+(" + li.base + ")*1)", li.lane, li.al4 && st.back() % 4 == 0);
       return opnd(0, j);
     }
@@ -539,7 +560,7 @@ struct Gen {
       const auto& it = op->ints.count("interior") ? op->ints.at("interior") : op->ints.at("interior_padding");
       const auto& ind = op->operands[0]->type.dims;
       LaneIx li;
-      if (vec && branch_depth == 0 && !idx.empty() && LaneInfo(idx.back(), &li) && li.al4 && li.lane == 0 &&
+      if (vec && branch_depth == 0 && !idx.empty() && LaneInfo(idx.back(), &li) && li.al4 && li.exact && li.lane == 0 &&
           lo.back() % 4 == 0 && it.back() == 0 && ind.back() % 4 == 0 && ty.dims.back() % 4 == 0) {
         // the four lanes lie on the same side of every edge: one branch computes all four (their
         // reads inside may then be one vector access) and lanes 1-3 are left in the value cache
@@ -842,6 +863,36 @@ class Lowerer {
         demote_[r->id] = narrow;
         if (pitch_ok) pitch_[r->id] = (r->type.dims.back() + 7) / 8 * 8;
       }
+    }
+    // A tensor-core dot whose result rows break the 16-byte rule (the LM head's f32 logits, 50257
+    // wide) writes them with a padded pitch -- the TMA-store epilogue then applies, and the
+    // generated kernels that read the result get 16-byte aligned rows -- when every reader is such a
+    // kernel (elementwise / index maps other than reshape / reductions).
+    for (auto& opp : g_.ops) {
+      const Op* op = opp.get();
+      if (dead_[op->index] || (op->name != "dot_general" && op->name != "dot") || op->results.size() != 1) continue;
+      const Value* r = op->result();
+      const DT dt = r->type.dt;
+      if (r->type.rank() < 2 || (dt != DT::kF32 && dt != DT::kBF16 && dt != DT::kF16) || outs.count(r->id) ||
+          attn_.count(r->id) || bwd_of_.count(r->id) || pitch_.count(r->id))
+        continue;
+      const int64_t n = r->type.dims.back(), esz = DTBytes(dt);
+      if ((n * esz) % 16 == 0) continue;
+      std::vector<int64_t> bat, fr, ct;
+      DotDims(op, 1, &bat, &fr, &ct);
+      if (fr.size() != 1 || op->operands[1]->type.dims[fr[0]] != n) continue;
+      const DT at = op->operands[0]->type.dt, bt = op->operands[1]->type.dt;
+      if ((at == DT::kF32 || at == DT::kF64) && (bt == DT::kF32 || bt == DT::kF64)) continue;   // SIMT path
+      bool ok = !r->users.empty();
+      for (const Op* u : r->users) {
+        if (dead_[u->index]) continue;
+        const bool gen = (IsElementwise(u) && u->name != "reshape" && u->name != "bitcast_convert") ||
+                         (u->name == "reduce" && u->operands[0] == r && u->results.size() == 1);
+        if (!gen) { ok = false; break; }
+      }
+      bool in_attn = false;
+      for (auto& kv : attn_in_) for (const Value* v : kv.second) in_attn = in_attn || v == r;
+      if (ok && !in_attn) pitch_[r->id] = (n * esz + 15) / 16 * 16 / esz;
     }
   }
   // batch / free / contracting dims of operand `side` (0 lhs, 1 rhs) of a dot
@@ -1472,9 +1523,13 @@ class Lowerer {
     }
   }
 
+  std::unordered_map<int, int64_t> slot_pitch_;   // slot -> padded row pitch (elements)
   int SlotFor(const Value* v) {
     v = Resolve(v);
-    if (slot_of_[v->id] < 0) slot_of_[v->id] = NewSlot(StoredBytes(v));
+    if (slot_of_[v->id] < 0) {
+      slot_of_[v->id] = NewSlot(StoredBytes(v));
+      if (const int64_t p = StoredPitch(v)) slot_pitch_[slot_of_[v->id]] = p;
+    }
     return slot_of_[v->id];
   }
 
@@ -1671,6 +1726,7 @@ class Lowerer {
     }
     Gen gen;
     gen.slot_of = &slot_of_;
+    gen.slot_pitch = &slot_pitch_;
     gen.group_dims = dims;
     std::ostringstream pre;
     std::string ind = "    ";
@@ -1916,6 +1972,7 @@ class Lowerer {
     }
     Gen gen;
     gen.slot_of = &slot_of_;
+    gen.slot_pitch = &slot_pitch_;
     gen.group_dims = X;
     std::ostringstream ob, body;
     gen.row_ident = Delinearize(ob, "row", kept, "a", "    ", wide);
@@ -1965,7 +2022,34 @@ class Lowerer {
     // two loops: four-element groups from the row's first 16-byte aligned element (hd), where the
     // reads and writes of [rows..., L] tensors are vector accesses, and a scalar loop over the at
     // most six elements left at the two ends.
-    const bool shift = !vec && L >= 4 * T && !std::getenv("B200_NO_VEC");
+    // Ragged rows whose full-shape reads all come from buffers with a padded, 16-byte aligned row
+    // pitch (a dot's output): four-element groups from element 0, the padding read but the lanes
+    // past the end masked (clamped indices, ok flags); stores to padded outputs stay vector stores.
+    bool padded = false;
+    if (!vec && L >= 4 * T && !std::getenv("B200_NO_VEC")) {
+      std::set<int> memb;
+      for (const Value* m : members) memb.insert(m->id);
+      int pitched = 0, plain = 0;
+      std::set<int> seen;
+      std::vector<const Value*> st(members.begin(), members.end());
+      while (!st.empty()) {
+        const Value* v = st.back();
+        st.pop_back();
+        if (!seen.insert(v->id).second) continue;
+        if (!memb.count(v->id) && slot_of_[Resolve(v)->id] >= 0) {          // a leaf the kernel reads
+          if (v->type.dims == X) {
+            const int64_t pt = StoredPitch(Resolve(v));
+            if (pt && pt % 4 == 0) ++pitched;
+            else ++plain;
+          }
+          continue;
+        }
+        if (v->def)
+          for (const Value* o : v->def->operands) st.push_back(o);
+      }
+      padded = pitched > 0 && plain == 0;
+    }
+    const bool shift = !vec && !padded && L >= 4 * T && !std::getenv("B200_NO_VEC");
     if (shift)
       ob << "    const int hd = (int)((4 - (int)((row * " << Ls << "LL) & 3)) & 3), nv = (" << Ls << " - hd) >> 2, nrem = " << Ls
          << " - 4 * nv;\n";
@@ -1974,9 +2058,14 @@ class Lowerer {
     const std::string rem_head = "    for (int j = lt; j < nrem; j += " + Ts +
                                  ") {\n      const bool ok_1 = false, ok_2 = false, ok_3 = false;\n"
                                  "      const int j_0 = j < hd ? j : j + 4 * nv, j_1 = j_0, j_2 = j_0, j_3 = j_0;\n";
-    bool cur_vec = vec;        // the walk being emitted has four consecutive elements per thread
-    std::string cur_head = loop_head;
-    auto ok = [&](int l) { return cur_vec || l == 0 ? std::string() : "ok_" + std::to_string(l); };
+    const std::string padded_head = "#pragma unroll 4\n    for (int j = lt * 4; j < " + Ls + "; j += " + std::to_string(4 * T) +
+                                    ") {\n      const bool ok_1 = j + 1 < " + Ls + ", ok_2 = j + 2 < " + Ls + ", ok_3 = j + 3 < " + Ls +
+                                    ";\n      const int j_0 = j, j_1 = ok_1 ? j + 1 : " + last + ", j_2 = ok_2 ? j + 2 : " + last +
+                                    ", j_3 = ok_3 ? j + 3 : " + last + ";\n";
+    bool cur_vec = vec || padded;   // the walk being emitted has four consecutive elements per thread
+    std::string cur_head = padded ? padded_head : loop_head;
+    gen.lanes_clamped = padded;
+    auto ok = [&](int l) { return (cur_vec && !padded) || l == 0 ? std::string() : "ok_" + std::to_string(l); };
     auto elem_index = [&](const Value* m, int l) {
       const int64_t p = StoredPitch(m);
       return "(long long)row * " + (p ? std::to_string(p) : Ls) + "LL + j_" + std::to_string(l);
@@ -2001,12 +2090,12 @@ class Lowerer {
     auto walk = [&](const std::function<std::string()>& lane_code) {
       std::string out;
       for (int pass = 0; pass < (shift ? 2 : 1); ++pass) {
-        cur_vec = shift ? pass == 0 : vec;
-        cur_head = shift ? (pass == 0 ? shift_head : rem_head) : loop_head;
+        cur_vec = shift ? pass == 0 : vec || padded;
+        cur_head = shift ? (pass == 0 ? shift_head : rem_head) : padded ? padded_head : loop_head;
         const std::string tail = lane_code();
         out += cur_head + gen.body.str() + tail + "    }\n";
       }
-      cur_vec = vec;
+      cur_vec = vec || padded;
       return out;
     };
     auto phase_vals = [&](const Value* v) {
@@ -2138,7 +2227,7 @@ class Lowerer {
             DT dt = StoredDt(mq);
             for (auto& x : vals) x = StoreVal(mq, dt, x);
             // vector stores need the row's alignment: with a ragged row only an unpadded output has it
-            const bool vstore = cur_vec && (!shift || StoredPitch(mq) == 0);
+            const bool vstore = padded ? StoredPitch(mq) % 4 == 0 && StoredPitch(mq) > 0 : cur_vec && (!shift || StoredPitch(mq) == 0);
             if (!vstore || (dt != DT::kF32 && dt != DT::kBF16 && dt != DT::kF16)) {
               for (int l = 0; l < 4; ++l)
                 t << "      " << (ok(l).empty() ? "" : "if (" + ok(l) + ") ") << oq << "[" << elem_index(mq, l) << "] = " << StoreExpr(dt, vals[l]) << ";\n";
@@ -2260,6 +2349,7 @@ class Lowerer {
     better += "  if (av != bv) return av " + cmp + " bv;\n  return ai < bi;\n}\n";
     Gen gen;
     gen.slot_of = &slot_of_;
+    gen.slot_pitch = &slot_pitch_;
     gen.indent = "      ";
     std::ostringstream ob, jb;
     auto names_k = Delinearize(ob, inner ? "row" : "o", kept, "a", "    ", wide);
@@ -2348,6 +2438,7 @@ class Lowerer {
     int out_slot = SlotFor(r);
     Gen gen;
     gen.slot_of = &slot_of_;
+    gen.slot_pitch = &slot_pitch_;
     std::ostringstream pre;
     // init value (scalar expression)
     std::string init_expr;
@@ -2786,7 +2877,8 @@ class Lowerer {
     g.b_mn = ob.mn;
     g.ldb = ob.ld;
     g.c = SlotFor(r);
-    if (tc && g.out != DT::kF32 && b200k::GemmSplitK(g.batch, g.M, g.N, g.K, 148) > 1) {
+    g.ldc = StoredPitch(r);                      // 0: dense rows of N
+    if (tc && g.out != DT::kF32 && !g.ldc && b200k::GemmSplitK(g.batch, g.M, g.N, g.K, 148) > 1) {
       g.ws = NewSlot(g.batch * g.M * g.N * 4);   // split-K partial sums
       RecordDt(g.ws, DT::kF32);
     }

@@ -40,6 +40,7 @@ struct GemmStep {
   int a = -1, b = -1, c = -1;  // A[batch,M,K], B[batch,N,K] (K-major), C[batch,M,N] row-major
   int64_t batch = 1, M = 0, N = 0, K = 0;
   int64_t lda = 0, ldb = 0;    // row pitch of A / B in elements (>= K; K rounded up to 8 for TMA)
+  int64_t ldc = 0;             // row pitch of C in elements (0: N; padded to 16 bytes for TMA stores)
   bool a_mn = false, b_mn = false;  // operand stored MN-major: A[batch,K,M] / B[batch,K,N], pitch M / N
   int ws = -1;                 // f32 [batch,M,N] workspace when a 16-bit result is computed split-K
   DT ab = DT::kBF16, out = DT::kF32;

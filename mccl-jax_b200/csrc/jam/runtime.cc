@@ -21,7 +21,7 @@ namespace b200k {
 int Gemm(const void* A, long long lda, const void* B, long long ldb, void* C, int64_t batch, int64_t M, int64_t N,
          int64_t K, int ab_type, int out_type, cudaStream_t st);
 int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C, int64_t batch, int64_t M,
-         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st, float* ws);
+         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st, float* ws, int64_t ldc);
 int AttentionFwd(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D, int causal, float scale,
                  cudaStream_t st);
 int AttentionFwdLse(const void* q, const void* k, const void* v, void* o, float* lse2, int B, int H, int S, int D,
@@ -498,7 +498,7 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
           for (int s : {g.a, g.b, g.c, g.ws}) { err = slot(s); if (!err.empty()) return fail(err); }
           int rc = b200k::Gemm(ptr[g.a], g.lda ? g.lda : (g.a_mn ? g.M : g.K), g.a_mn, ptr[g.b], g.ldb ? g.ldb : (g.b_mn ? g.N : g.K),
                                g.b_mn, ptr[g.c], g.batch, g.M, g.N,
-                               g.K, PjrtType(g.ab), PjrtType(g.out), st, g.ws >= 0 ? (float*)ptr[g.ws] : nullptr);
+                               g.K, PjrtType(g.ab), PjrtType(g.out), st, g.ws >= 0 ? (float*)ptr[g.ws] : nullptr, g.ldc);
           if (rc != 0) return fail("gemm launch failed (" + std::to_string(rc) + ") for " + S.label);
           break;
         }

@@ -87,7 +87,7 @@ template <int BN, int OUT, bool AMN, bool BMN>
 __global__ void __launch_bounds__(192, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, void* __restrict__ C, int M, int N, int K, int batch, int fmt,
-               int splits, float* __restrict__ ws, int tma_store) {
+               int splits, float* __restrict__ ws, int tma_store, long long ldc) {
   using CF = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -210,11 +210,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       tile_coords(r, mb, nb, &m_blk, &n_blk);
       const int row = m_blk * BM + row_in_tile;
       const uint32_t taddr = tmem_base + a * BN + ((uint32_t)(q * 32) << 16);
-      const long long crow = ((long long)b * M + row) * (long long)N;
+      const long long crow = ((long long)b * M + row) * ldc;      // ldc: C's row pitch (>= N)
       // full 32-column chunks of an aligned row go straight out as 16-byte vectors; otherwise (N not
       // a multiple of 8 / 4, or the ragged last chunk) the warp stages 32 rows x 32 columns in shared
       // memory and writes them row by row, coalesced, with bounds checks
-      const bool aligned = OUT == 0 ? (N & 3) == 0 : (N & 7) == 0;
+      const bool aligned = OUT == 0 ? (ldc & 3) == 0 : (ldc & 7) == 0;
       float* stage = stage_base + (warp - 2) * 32 * 33;
       if (tma_store == 2) {
         // split-K partial sums: f32 boxes added into the workspace by TMA reduce-add (L2 atomics
@@ -328,7 +328,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int grow = m_blk * BM + q * 32 + rr;
             if (grow < M && gcol < N) {
               const float x = stage[rr * 33 + lane];
-              const long long o = ((long long)b * M + grow) * (long long)N + gcol;
+              const long long o = ((long long)b * M + grow) * ldc + gcol;
               if (OUT == 0) ((float*)C)[o] = x;
               else if (OUT == 1) ((uint16_t*)C)[o] = (uint16_t)(pack_bf16(x, 0.f) & 0xffff);
               else ((uint16_t*)C)[o] = (uint16_t)(pack_f16(x, 0.f) & 0xffff);
@@ -456,12 +456,12 @@ bool MakeOperandMapMN(CUtensorMap* map, const void* ptr, int K, long long ld, in
 
 // 3-D output map for the TMA-store epilogue: dims {N, M, batch}, box {128 bytes of columns, 32 rows, 1},
 // 128-byte swizzle.  Rows must be 16-byte multiples.
-bool MakeOutputMap(CUtensorMap* map, void* C, int M, int N, int batch, int out) {
+bool MakeOutputMap(CUtensorMap* map, void* C, int M, int N, int batch, int out, long long ldc) {
   EncodeTiledFn enc = GetEncodeTiled();
   if (!enc) return false;
   const int esz = out == 0 ? 4 : 2;
   cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)N * esz, (cuuint64_t)N * esz * M};
+  cuuint64_t strides[2] = {(cuuint64_t)ldc * esz, (cuuint64_t)ldc * esz * M};
   cuuint32_t box[3] = {(cuuint32_t)(128 / esz), 32, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUtensorMapDataType t = out == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : out == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -479,7 +479,7 @@ int NumSMs() {
 
 template <int BN, int OUT, bool AMN, bool BMN>
 static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, void* C, int batch, int M, int N, int K,
-                    int fmt, cudaStream_t st, int splits, float* ws) {
+                    int fmt, cudaStream_t st, int splits, float* ws, long long ldc) {
   using CF = Cfg<BN>;
   static std::once_flag once[8];
   int dev = 0;
@@ -496,25 +496,25 @@ static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, 
   const int esz = OUT == 0 ? 4 : 2;
   int tma_store = 0;
   if (!getenv("B200_GEMM_NO_TMA_STORE")) {
-    if (splits == 1 && ((long long)N * esz) % 16 == 0 && ((uintptr_t)C % 16) == 0)
-      tma_store = MakeOutputMap(&tc, C, M, N, batch, OUT) ? 1 : 0;
+    if (splits == 1 && (ldc * esz) % 16 == 0 && ((uintptr_t)C % 16) == 0)
+      tma_store = MakeOutputMap(&tc, C, M, N, batch, OUT, ldc) ? 1 : 0;
     else if (splits > 1 && ((long long)N * 4) % 16 == 0 && ((uintptr_t)ws % 16) == 0)
-      tma_store = MakeOutputMap(&tc, ws, M, N, batch, 0) ? 2 : 0;
+      tma_store = MakeOutputMap(&tc, ws, M, N, batch, 0, N) ? 2 : 0;
   }
   if (!tma_store) tc = ta;                                  // unused
   int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
   int grid = std::min(tiles * splits, NumSMs());
-  gemm_tc_kernel<BN, OUT, AMN, BMN><<<grid, 192, CF::kSmem, st>>>(ta, tb, tc, C, M, N, K, batch, fmt, splits, ws, tma_store);
+  gemm_tc_kernel<BN, OUT, AMN, BMN><<<grid, 192, CF::kSmem, st>>>(ta, tb, tc, C, M, N, K, batch, fmt, splits, ws, tma_store, ldc);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
 template <int BN, int OUT>
 static int LaunchTcMajor(bool amn, bool bmn, const void* A, long long lda, const void* B, long long ldb, void* C, int batch,
-                         int M, int N, int K, int fmt, cudaStream_t st, int splits, float* ws) {
-  if (amn && bmn) return LaunchTc<BN, OUT, true, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws);
-  if (amn) return LaunchTc<BN, OUT, true, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws);
-  if (bmn) return LaunchTc<BN, OUT, false, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws);
-  return LaunchTc<BN, OUT, false, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws);
+                         int M, int N, int K, int fmt, cudaStream_t st, int splits, float* ws, long long ldc) {
+  if (amn && bmn) return LaunchTc<BN, OUT, true, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc);
+  if (amn) return LaunchTc<BN, OUT, true, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc);
+  if (bmn) return LaunchTc<BN, OUT, false, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc);
+  return LaunchTc<BN, OUT, false, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc);
 }
 
 __global__ void __launch_bounds__(256) ws_to_16bit_kernel(const float* __restrict__ ws, uint16_t* __restrict__ c, long long n,
@@ -596,14 +596,16 @@ int GemmSplitK(int64_t batch, int64_t M, int64_t N, int64_t K, int sms) {
 // may be computed split-K (partials added into ws, then rounded into C); an f32 result splits without
 // it (partials added into C).
 int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C, int64_t batch, int64_t M,
-         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st, float* ws) {
+         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st, float* ws, int64_t ldc) {
   if (batch <= 0 || M <= 0 || N <= 0) return 0;
+  if (ldc <= 0) ldc = N;
+  if (ldc < N) return -1;
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || batch > 65535 || lda < (a_mn ? M : K) || ldb < (b_mn ? N : K))
     return -1;
   int out = out_type == B200_DT_F32 ? 0 : out_type == B200_DT_BF16 ? 1 : out_type == B200_DT_F16 ? 2 : -1;
   if (out < 0) return -1;
   if (K == 0) {
-    size_t bytes = (size_t)batch * M * N * (out == 0 ? 4 : 2);
+    size_t bytes = (size_t)batch * M * ldc * (out == 0 ? 4 : 2);
     return cudaMemsetAsync(C, 0, bytes, st) == cudaSuccess ? 0 : -3;
   }
   bool tc_ok = (ab_type == B200_DT_BF16 || ab_type == B200_DT_F16) && (lda % 8) == 0 && (ldb % 8) == 0 &&
@@ -613,14 +615,15 @@ int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, 
     int b = (int)batch, m = (int)M, n = (int)N, k = (int)K;
     int bn = 256, splits = 1;
     GemmTile(batch, M, N, K, NumSMs(), &bn, &splits);
+    if (ldc != N) splits = 1;                  // partial sums are laid out densely
     float* acc = out == 0 ? (float*)C : ws;
     if (splits > 1 && !acc) splits = 1;
     if (splits > 1 && cudaMemsetAsync(acc, 0, (size_t)batch * M * N * 4, st) != cudaSuccess) return -3;
     auto launch = [&](auto out_c) {
       constexpr int O = decltype(out_c)::value;
-      if (bn == 256) return LaunchTcMajor<256, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc);
-      if (bn == 192) return LaunchTcMajor<192, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc);
-      return LaunchTcMajor<128, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc);
+      if (bn == 256) return LaunchTcMajor<256, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc);
+      if (bn == 192) return LaunchTcMajor<192, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc);
+      return LaunchTcMajor<128, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc);
     };
     int rc = out == 0 ? launch(std::integral_constant<int, 0>{})
            : out == 1 ? launch(std::integral_constant<int, 1>{})
@@ -634,6 +637,7 @@ int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, 
     return rc;
   }
   int b = (int)batch, m = (int)M, n = (int)N, k = (int)K;
+  if (ldc != N) return -1;                     // padded C rows are written by the tensor-core path only
   if (ab_type == B200_DT_F32) return LaunchSimt<float>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, out, st);
   if (ab_type == B200_DT_BF16) return LaunchSimt<__nv_bfloat16>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, out, st);
   if (ab_type == B200_DT_F16) return LaunchSimt<__half>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, out, st);
@@ -641,8 +645,13 @@ int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, 
 }
 
 int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C, int64_t batch, int64_t M,
+         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st, float* ws) {
+  return Gemm(A, lda, a_mn, B, ldb, b_mn, C, batch, M, N, K, ab_type, out_type, st, ws, 0);
+}
+
+int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C, int64_t batch, int64_t M,
          int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st) {
-  return Gemm(A, lda, a_mn, B, ldb, b_mn, C, batch, M, N, K, ab_type, out_type, st, nullptr);
+  return Gemm(A, lda, a_mn, B, ldb, b_mn, C, batch, M, N, K, ab_type, out_type, st, nullptr, 0);
 }
 
 int Gemm(const void* A, long long lda, const void* B, long long ldb, void* C, int64_t batch, int64_t M, int64_t N,

@@ -354,3 +354,28 @@ def test_head_gradients_assembled_into_rows(client, dt):
     refs = oracle_run(text, ins)
     for o, r in zip(outs, refs):
         np.testing.assert_array_equal(np.asarray(o, np.float32), np.asarray(r, np.float32))
+
+
+@pytest.mark.parametrize("V", [1001, 1003, 1024])
+def test_unaligned_dot_output_read_by_fused_kernels(client, V):
+    """A tensor-core dot whose f32 result rows are not 16-byte multiples (the LM head's logits) is
+    written with a padded row pitch; the row kernels (logsumexp, softmax cotangent), a column
+    reduction and an elementwise consumer read it through that pitch."""
+    b = Builder("jit_lm_head")
+    x = b.arg((256, 96), "bf16")
+    w = b.arg((V, 96), "bf16")
+    lg = b.dot_general(x, w, contract=([1], [1]), out_dtype="f32")        # [256, V] f32
+    mx = b.max(lg, 1, keepdims=True)
+    z = lg - b.broadcast_to(mx, lg.shape)
+    lse = b.log(b.sum(b.exp(z), 1, keepdims=True))
+    sm = b.exp(z - b.broadcast_to(lse, lg.shape))
+    col = b.sum(lg, 0)
+    text = b.text([b.reshape(lse, (256,)), b.convert(sm, "bf16"), col, lg * 2.0])
+    rng = np.random.default_rng(V)
+    ins = [(rng.standard_normal((256, 96)) * 0.5).astype(ml_dtypes.bfloat16),
+           (rng.standard_normal((V, 96)) * 0.5).astype(ml_dtypes.bfloat16)]
+    outs = client.run(text, ins)
+    refs = oracle_run(text, ins)
+    for o, r, name, tol in zip(outs, refs, ("lse", "softmax", "colsum", "2*logits"), (1e-4, RTOL_BF16, 1e-4, 1e-4)):
+        assert o.shape == r.shape
+        assert_close(np.asarray(o, np.float32), np.asarray(r, np.float32), tol, name)
