@@ -169,6 +169,13 @@ __device__ __forceinline__ float fsign(float x) { return x > 0.f ? 1.f : (x < 0.
 __device__ __forceinline__ float frne(float x) { return rintf(x); }
 __device__ __forceinline__ float fafz(float x) { return roundf(x); }
 __device__ __forceinline__ float flogistic(float x) { return 1.f / (1.f + expf(-x)); }
+// tanh(u) = 1 - 2 / (e^(2u) + 1) to an absolute error of a few 1e-7 (relative accuracy is lost for
+// |u| << 1), exponential and reciprocal on the SFU; for readers that only form 1 +- tanh(u)
+__device__ __forceinline__ float ftanh_abs(float u) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + ex2a(u * 2.88539008177792681f)));  // 2 log2(e)
+  return fmaf(-2.f, r, 1.f);
+}
 // 1 / (1 + e^(-2u)) = (1 + tanh(u)) / 2, with the exponential and the reciprocal on the SFU
 __device__ __forceinline__ float fsig2(float u) {
   float r;
@@ -367,6 +374,32 @@ struct Gen {
     return out;
   }
 
+  static bool IsSplat(const Value* v) {
+    while (v->def && v->def->name == "broadcast_in_dim") v = v->def->operands[0];
+    return v->def && v->def->name == "constant" && v->def->splat;
+  }
+  // t = tanh(u) read only through sums / differences with constants (1 + t, 1 - t) and its square
+  // t * t, itself read only through such sums: the readers need t to an absolute, not a relative,
+  // accuracy (the tanh-GELU derivative 0.5 (1 + t) + ... (1 - t^2) ...)
+  static bool TanhOnlyNearOne(const Value* t) {
+    if (t->users.empty()) return false;
+    auto const_sum = [](const Op* u, const Value* x) {
+      return (u->name == "add" || u->name == "subtract") && u->operands.size() == 2 &&
+             ((u->operands[0] == x && IsSplat(u->operands[1])) || (u->operands[1] == x && IsSplat(u->operands[0])));
+    };
+    for (const Op* u : t->users) {
+      if (const_sum(u, t)) continue;
+      if (u->name == "multiply" && u->operands.size() == 2 && u->operands[0] == t && u->operands[1] == t) {
+        const Value* sq = u->result();
+        if (sq->users.empty()) return false;
+        for (const Op* w : sq->users)
+          if (!const_sum(w, sq)) return false;
+        continue;
+      }
+      return false;
+    }
+    return true;
+  }
   static bool SplatIs(const Value* v, double want) {
     while (v->def && v->def->name == "broadcast_in_dim") v = v->def->operands[0];
     return v->def && v->def->name == "constant" && v->def->splat && ConstScalar(v->def) == want;
@@ -649,6 +682,11 @@ struct Gen {
       std::vector<std::string> t{row};
       for (size_t k = 0; k < offset_dims.size(); ++k) t.push_back(idx[offset_dims[k]]);
       return Emit(table, t);
+    }
+    if (n == "tanh" && ty.dt == DT::kF32 && TanhOnlyNearOne(v)) {
+      // every reader forms 1 + t, 1 - t, c - t or t * t: an absolute error of a few 1e-7 is all
+      // the result can carry, which tanh(u) = 1 - 2 / (e^(2u) + 1) on the SFU delivers
+      return Var(DT::kF32, "ftanh_abs(" + opnd(0, idx) + ")");
     }
     if (kUnary.count(n)) {
       std::string x = opnd(0, idx);
@@ -1544,7 +1582,12 @@ class Lowerer {
     std::vector<const Value*> pending;   // loop roots of the open group
     std::vector<const Value*> row;       // members of the open row group
     std::vector<int64_t> row_x;          // its row space X = [rows..., L]
+    std::vector<Op*> colred;             // sibling column reductions emitted as one kernel
     auto flush = [&]() {
+      // queued column reductions precede every open row / loop group in program order
+      if (colred.size() == 1) EmitReduce(colred[0]);
+      else if (!colred.empty()) EmitColumnReduceGroup(colred);
+      colred.clear();
       if (!row.empty()) TryRow(row, row_x, false);
       row.clear();
       if (!pending.empty()) EmitLoopGroup(pending);
@@ -1634,6 +1677,18 @@ class Lowerer {
           flush();
           row = {r};
           row_x = X;
+          continue;
+        }
+        if (op->results.size() == 1 && VecColumnReduce(op)) {
+          // reductions of one shape over the same dims, none reading another's result, share a
+          // kernel (and the reads of their common operands: dbeta and dgamma both read dy)
+          if (!colred.empty() && SameColumnReduce(colred[0], op) && !ReadsAny(op->operands[0], colred) && row.empty() &&
+              pending.empty()) {
+            colred.push_back(op);
+            continue;
+          }
+          flush();
+          colred.push_back(op);
           continue;
         }
         flush();
@@ -2401,6 +2456,179 @@ class Lowerer {
   }
 
   // ---------------------------------------------------------------- reductions
+  // a reduction over leading dims whose kept contiguous dim is a multiple of 4 (the vectorised
+  // column path), accumulating in f32
+  bool VecColumnReduce(const Op* op) const {
+    if (op->results.size() != 1 || op->reduce == ReduceKind::kNone || std::getenv("B200_NO_VEC")) return false;
+    const auto& xd = op->operands[0]->type.dims;
+    std::vector<int64_t> rd = op->ints.at("dimensions");
+    if (xd.empty() || rd.empty() || std::find(rd.begin(), rd.end(), (int64_t)xd.size() - 1) != rd.end()) return false;
+    const DT odt = op->result()->type.dt;
+    if (odt != DT::kF32 && odt != DT::kBF16 && odt != DT::kF16) return false;
+    return xd.back() % 4 == 0 && op->result()->type.numel() % 4 == 0;
+  }
+  static bool SameColumnReduce(const Op* a, const Op* b) {
+    std::vector<int64_t> ra = a->ints.at("dimensions"), rb = b->ints.at("dimensions");
+    std::sort(ra.begin(), ra.end());
+    std::sort(rb.begin(), rb.end());
+    return ra == rb && a->operands[0]->type.dims == b->operands[0]->type.dims;
+  }
+  // whether the value v (through the values computed inline) reads the result of any of `ops`
+  bool ReadsAny(const Value* v, const std::vector<Op*>& ops) const {
+    std::set<int> res;
+    for (const Op* o : ops) res.insert(o->result()->id);
+    std::set<int> seen;
+    std::vector<const Value*> st{v};
+    while (!st.empty()) {
+      const Value* x = st.back();
+      st.pop_back();
+      if (!seen.insert(x->id).second) continue;
+      if (res.count(x->id)) return true;
+      if (slot_of_[Resolve(x)->id] >= 0 && !x->def) continue;
+      if (x->def && !IsHeavy(x->def))
+        for (const Value* o : x->def->operands) st.push_back(o);
+    }
+    return false;
+  }
+
+  // Sibling column reductions (same operand shape and reduced dims) as one kernel: a thread owns
+  // four adjacent outputs of every reduction, the reduced range is split over blockIdx.y, and a
+  // second kernel combines the partials of all of them.
+  void EmitColumnReduceGroup(const std::vector<Op*>& ops) {
+    const int K = (int)ops.size();
+    const Value* x0 = ops[0]->operands[0];
+    std::vector<int64_t> rd = ops[0]->ints.at("dimensions");
+    std::sort(rd.begin(), rd.end());
+    const auto& xd = x0->type.dims;
+    std::vector<int64_t> kept, red;
+    std::vector<int> kept_ax, red_ax;
+    for (int k = 0; k < (int)xd.size(); ++k) {
+      if (std::binary_search(rd.begin(), rd.end(), (int64_t)k)) { red.push_back(xd[k]); red_ax.push_back(k); }
+      else { kept.push_back(xd[k]); kept_ax.push_back(k); }
+    }
+    const int64_t n_out = ops[0]->result()->type.numel();
+    int64_t L = 1;
+    for (int64_t d : red) L *= d;
+    const bool wide = x0->type.numel() >= (1LL << 31);
+    auto combine = [&](ReduceKind kind, const std::string& a, const std::string& b) { return Combine(kind, DT::kF32, a, b); };
+    std::vector<std::string> init_expr(K), ident(K);
+    std::vector<int> out_slot(K);
+    std::vector<DT> odt(K);
+    for (int q = 0; q < K; ++q) {
+      init_expr[q] = InitExpr(ops[q]->operands[1], DT::kF32);
+      ident[q] = "(float)(" + IdentityOf(ops[q]->reduce, DT::kF32) + ")";
+      out_slot[q] = SlotFor(ops[q]->result());
+      odt[q] = ops[q]->result()->type.dt;
+    }
+    const int64_t n4 = n_out / 4;
+    int64_t chunks = 1;
+    const int64_t want_threads = 148LL * 2048;
+    if (L > 16) chunks = std::min<int64_t>((want_threads + n4 - 1) / n4, std::max<int64_t>(1, L / 16));
+    chunks = std::max<int64_t>(1, std::min<int64_t>(chunks, 1024));
+    const int64_t per = (L + chunks - 1) / chunks;
+    chunks = (L + per - 1) / per;
+    const int bt = (int)std::min<int64_t>(256, (n4 + 31) / 32 * 32);
+    Gen gen;
+    gen.slot_of = &slot_of_;
+    gen.slot_pitch = &slot_pitch_;
+    gen.indent = "      ";
+    std::ostringstream ob, inner_pre, k;
+    auto names_k = Delinearize(ob, "o4", kept, "a", "  ", wide);
+    auto names_r = Delinearize(inner_pre, "j", red, "b", "      ", wide);
+    const std::string vin = names_k.back();
+    std::vector<std::vector<std::string>> lanes(4, std::vector<std::string>(xd.size()));
+    for (int l = 0; l < 4; ++l) {
+      for (size_t q = 0; q < kept_ax.size(); ++q) lanes[l][kept_ax[q]] = names_k[q];
+      lanes[l][kept_ax.back()] = vin + "_" + std::to_string(l);
+      for (size_t q = 0; q < red_ax.size(); ++q) lanes[l][red_ax[q]] = names_r[q];
+    }
+    gen.vec = true;
+    gen.vinner = vin;
+    gen.lane_identity = lanes;
+    gen.identity = lanes[0];
+    gen.body << inner_pre.str();
+    std::vector<std::vector<std::string>> vals(K);
+    for (int q = 0; q < K; ++q)
+      for (int l = 0; l < 4; ++l) vals[q].push_back(gen.Emit(ops[q]->operands[0], lanes[l]));
+    std::vector<DT> in_dts;
+    for (int s : gen.in_slots) in_dts.push_back(SlotDt(s));
+    const int scratch = chunks > 1 ? NewSlot((int64_t)K * chunks * n_out * 4) : -1;
+    const std::string fn = KName();
+    std::vector<DT> out_dts = chunks > 1 ? std::vector<DT>{DT::kF32} : odt;
+    k << "extern \"C\" __global__ void __launch_bounds__(" << bt << ") " << fn << "("
+      << KernelParams(gen.in_slots, (int)out_dts.size(), false) << ") {\n" << ParamCasts(gen.in_slots, in_dts, out_dts)
+      << "  const long long o = (long long)blockIdx.x * " << bt << " + threadIdx.x;\n  if (o >= " << n4 << "LL) return;\n"
+      << "  const long long o4 = o * 4;\n" << ob.str()
+      << "  const int " << vin << "_0 = " << vin << ", " << vin << "_1 = " << vin << " + 1, " << vin << "_2 = " << vin << " + 2, "
+      << vin << "_3 = " << vin << " + 3;\n";
+    for (int q = 0; q < K; ++q)
+      for (int l = 0; l < 4; ++l)
+        k << "  float acc" << q << "_" << l << " = " << (chunks > 1 ? ident[q] : init_expr[q]) << ";\n";
+    k << "  const long long j0 = (long long)blockIdx.y * " << per << "LL;\n"
+      << "  const long long j1 = j0 + " << per << "LL < " << L << "LL ? j0 + " << per << "LL : " << L << "LL;\n"
+      << "#pragma unroll 4\n  for (long long j = j0; j < j1; ++j) {\n" << gen.body.str();
+    for (int q = 0; q < K; ++q)
+      for (int l = 0; l < 4; ++l) {
+        const std::string a = "acc" + std::to_string(q) + "_" + std::to_string(l);
+        k << "      " << a << " = " << combine(ops[q]->reduce, a, "(float)(" + vals[q][l] + ")") << ";\n";
+      }
+    k << "  }\n";
+    for (int q = 0; q < K; ++q) {
+      const std::string a = "acc" + std::to_string(q) + "_";
+      if (chunks > 1)
+        k << "  *(float4*)(out0 + ((long long)" << q << " * " << chunks << "LL + blockIdx.y) * " << n_out << "LL + o4) = make_float4("
+          << a << "0, " << a << "1, " << a << "2, " << a << "3);\n";
+      else
+        for (int l = 0; l < 4; ++l)
+          k << "  out" << q << "[o4 + " << l << "] = " << StoreExpr(odt[q], FromAcc(odt[q], a + std::to_string(l))) << ";\n";
+    }
+    k << "}\n";
+    Launch L1;
+    L1.fn = fn;
+    L1.in_slots = gen.in_slots;
+    L1.out_slots = chunks > 1 ? std::vector<int>{scratch} : out_slot;
+    L1.block = bt;
+    L1.grid_x = (n4 + bt - 1) / bt;
+    L1.grid_y = chunks;
+    Step st;
+    st.kind = StepKind::kFusion;
+    st.label = "reduce x" + std::to_string(K) + " " + x0->type.str() + " -> " + ops[0]->result()->type.str();
+    st.launches.push_back(L1);
+    if (chunks > 1) {
+      // finish: a warp per (reduction, output), its lanes striding over the chunk partials
+      const std::string fn2 = KName();
+      k << "extern \"C\" __global__ void __launch_bounds__(256) " << fn2 << "(const void* __restrict__ p0";
+      for (int q = 0; q < K; ++q) k << ", void* __restrict__ q" << q;
+      k << ") {\n  const float* part = (const float*)p0;\n  const int lane = threadIdx.x & 31;\n"
+        << "  for (long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); w < " << K * n_out
+        << "LL; w += (long long)gridDim.x * 8) {\n    const int q = (int)(w / " << n_out << "LL);\n    const long long o = w - (long long)q * "
+        << n_out << "LL;\n    const float* pq = part + (long long)q * " << chunks * n_out << "LL;\n";
+      for (int q = 0; q < K; ++q) {
+        k << "    " << (q ? "else " : "") << "if (q == " << q << ") {\n      float acc = " << ident[q] << ";\n"
+          << "#pragma unroll 4\n      for (int c = lane; c < " << chunks << "; c += 32) acc = "
+          << combine(ops[q]->reduce, "acc", "pq[(long long)c * " + std::to_string(n_out) + "LL + o]") << ";\n"
+          << "      for (int s = 16; s; s >>= 1) { float oth = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
+          << combine(ops[q]->reduce, "acc", "oth") << "; }\n"
+          << "      if (lane == 0) ((" << MemType(odt[q]) << "*)q" << q << ")[o] = "
+          << StoreExpr(odt[q], FromAcc(odt[q], combine(ops[q]->reduce, init_expr[q], "acc"))) << ";\n    }\n";
+      }
+      k << "  }\n}\n";
+      Launch L2;
+      L2.fn = fn2;
+      L2.in_slots = {scratch};
+      L2.out_slots = out_slot;
+      L2.block = 256;
+      L2.grid_x = std::max<int64_t>(1, (K * n_out + 7) / 8);
+      L2.grid_stride = true;
+      st.launches.push_back(L2);
+      RecordDt(scratch, DT::kF32);
+    }
+    src_ << k.str();
+    EndKernel();
+    for (int q = 0; q < K; ++q) RecordDt(out_slot[q], odt[q]);
+    p_->steps.push_back(st);
+  }
+
   void EmitReduce(Op* op) {
     if (op->results.size() != 1) throw LowerError{"variadic reduce (argmax/argmin) is not supported yet"};
     const Value* x = op->operands[0];

@@ -379,3 +379,45 @@ def test_unaligned_dot_output_read_by_fused_kernels(client, V):
     for o, r, name, tol in zip(outs, refs, ("lse", "softmax", "colsum", "2*logits"), (1e-4, RTOL_BF16, 1e-4, 1e-4)):
         assert o.shape == r.shape
         assert_close(np.asarray(o, np.float32), np.asarray(r, np.float32), tol, name)
+
+
+def test_tanh_read_only_as_one_plus_minus_t(client):
+    """tanh(u) whose readers only form 1 + t, 1 - t and 1 - t*t (the tanh-GELU derivative) is
+    computed as 1 - 2 / (e^(2u) + 1): those readers agree with the oracle to an absolute 1e-6."""
+    b = Builder("jit_tanh_near_one")
+    u = b.arg((4096,), "f32")
+    t = b.tanh(u)
+    text = b.text([1.0 + t, 1.0 - t * t, 2.0 - t])
+    rng = np.random.default_rng(2)
+    x = np.concatenate([rng.standard_normal(4000) * 3, [0.0, -0.0, 1e-8, -1e-8, 20.0, -20.0, np.inf, -np.inf]]).astype(np.float32)
+    x = np.concatenate([x, rng.standard_normal(4096 - x.size)]).astype(np.float32)
+    outs = client.run(text, [x])
+    refs = oracle_run(text, [x])
+    for o, r in zip(outs, refs):
+        np.testing.assert_allclose(o, r, atol=1e-6, rtol=0)
+
+
+@pytest.mark.parametrize("shape,dims", [((640, 96), [0]), ((3, 50, 48), [0, 1]), ((4096, 768), [0])])
+def test_sibling_column_reductions_share_a_kernel(client, lib_path, shape, dims):
+    """Reductions of one operand shape over the same leading dims (dbeta = sum dy, dgamma =
+    sum dy * xhat, plus a max with a non-identity init) run as one kernel reading dy once."""
+    import ctypes
+    b = Builder("jit_ln_param_grads")
+    dy = b.arg(shape, "bf16")
+    xh = b.arg(shape, "f32")
+    dyf = b.convert(dy, "f32")
+    s1 = b.sum(dyf, dims)
+    s2 = b.sum(dyf * xh, dims)
+    m3 = b.max(xh, dims)
+    text = b.text([s1, s2, m3])
+    lib = ctypes.CDLL(lib_path)
+    buf = ctypes.create_string_buffer(1 << 16)
+    t = text.encode()
+    assert lib.b200_compile_report(t, len(t), 1, 0, buf, len(buf)) == 0
+    assert "reduce x3" in buf.value.decode(), buf.value.decode()
+    rng = np.random.default_rng(len(shape))
+    ins = [rng.standard_normal(shape).astype(ml_dtypes.bfloat16), rng.standard_normal(shape).astype(np.float32)]
+    outs = client.run(text, ins)
+    refs = oracle_run(text, ins)
+    for o, r in zip(outs, refs):
+        assert_close(o, r, RTOL_F32 * 10, "column reductions")
