@@ -1585,8 +1585,7 @@ class Lowerer {
     std::vector<Op*> colred;             // sibling column reductions emitted as one kernel
     auto flush = [&]() {
       // queued column reductions precede every open row / loop group in program order
-      if (colred.size() == 1) EmitReduce(colred[0]);
-      else if (!colred.empty()) EmitColumnReduceGroup(colred);
+      if (!colred.empty()) EmitColumnReduceGroup(colred);
       colred.clear();
       if (!row.empty()) TryRow(row, row_x, false);
       row.clear();
@@ -2491,9 +2490,12 @@ class Lowerer {
     return false;
   }
 
-  // Sibling column reductions (same operand shape and reduced dims) as one kernel: a thread owns
-  // four adjacent outputs of every reduction, the reduced range is split over blockIdx.y, and a
-  // second kernel combines the partials of all of them.
+  // Column reductions (the contiguous dim kept; siblings of one operand shape over the same dims
+  // together) as one kernel: a block is TX column quads x TY row lanes; each thread owns four
+  // adjacent outputs of every reduction and reads them with one vector load per reduced index, the
+  // TY lanes of a block combine in shared memory, and each block writes one partial row per
+  // reduction; a second kernel combines the blocks' partials with coalesced reads (a warp covers
+  // 32 consecutive outputs).
   void EmitColumnReduceGroup(const std::vector<Op*>& ops) {
     const int K = (int)ops.size();
     const Value* x0 = ops[0]->operands[0];
@@ -2521,13 +2523,13 @@ class Lowerer {
       odt[q] = ops[q]->result()->type.dt;
     }
     const int64_t n4 = n_out / 4;
-    int64_t chunks = 1;
-    const int64_t want_threads = 148LL * 2048;
-    if (L > 16) chunks = std::min<int64_t>((want_threads + n4 - 1) / n4, std::max<int64_t>(1, L / 16));
-    chunks = std::max<int64_t>(1, std::min<int64_t>(chunks, 1024));
-    const int64_t per = (L + chunks - 1) / chunks;
+    const int TX = (int)std::min<int64_t>(32, n4), TY = 256 / TX;
+    const int64_t gx = (n4 + TX - 1) / TX;
+    // row chunks: about four blocks per SM, each row lane taking >= 8 reduced indices
+    int64_t chunks = std::max<int64_t>(1, std::min<int64_t>((148 * 4 + gx - 1) / gx, L / (8 * TY)));
+    chunks = std::min<int64_t>(chunks, 1024);
+    const int64_t per = (L + chunks - 1) / chunks;       // reduced indices per block
     chunks = (L + per - 1) / per;
-    const int bt = (int)std::min<int64_t>(256, (n4 + 31) / 32 * 32);
     Gen gen;
     gen.slot_of = &slot_of_;
     gen.slot_pitch = &slot_pitch_;
@@ -2555,71 +2557,86 @@ class Lowerer {
     const int scratch = chunks > 1 ? NewSlot((int64_t)K * chunks * n_out * 4) : -1;
     const std::string fn = KName();
     std::vector<DT> out_dts = chunks > 1 ? std::vector<DT>{DT::kF32} : odt;
-    k << "extern \"C\" __global__ void __launch_bounds__(" << bt << ") " << fn << "("
+    k << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "("
       << KernelParams(gen.in_slots, (int)out_dts.size(), false) << ") {\n" << ParamCasts(gen.in_slots, in_dts, out_dts)
-      << "  const long long o = (long long)blockIdx.x * " << bt << " + threadIdx.x;\n  if (o >= " << n4 << "LL) return;\n"
-      << "  const long long o4 = o * 4;\n" << ob.str()
+      << "  __shared__ float4 red_s[" << K << "][" << TY << "][" << TX << "];\n"
+      << "  const int tx = threadIdx.x % " << TX << ", ty = threadIdx.x / " << TX << ";\n"
+      << "  const long long o = (long long)blockIdx.x * " << TX << " + tx;\n"
+      << "  const bool live = o < " << n4 << "LL;\n"
+      << "  const long long o4 = (live ? o : 0) * 4;\n" << ob.str()
       << "  const int " << vin << "_0 = " << vin << ", " << vin << "_1 = " << vin << " + 1, " << vin << "_2 = " << vin << " + 2, "
       << vin << "_3 = " << vin << " + 3;\n";
     for (int q = 0; q < K; ++q)
-      for (int l = 0; l < 4; ++l)
-        k << "  float acc" << q << "_" << l << " = " << (chunks > 1 ? ident[q] : init_expr[q]) << ";\n";
-    k << "  const long long j0 = (long long)blockIdx.y * " << per << "LL;\n"
-      << "  const long long j1 = j0 + " << per << "LL < " << L << "LL ? j0 + " << per << "LL : " << L << "LL;\n"
-      << "#pragma unroll 4\n  for (long long j = j0; j < j1; ++j) {\n" << gen.body.str();
+      for (int l = 0; l < 4; ++l) k << "  float acc" << q << "_" << l << " = " << ident[q] << ";\n";
+    k << "  const long long jb = (long long)blockIdx.y * " << per << "LL;\n"
+      << "  const long long je = jb + " << per << "LL < " << L << "LL ? jb + " << per << "LL : " << L << "LL;\n"
+      << "#pragma unroll 4\n  for (long long j = jb + ty; j < je; j += " << TY << ") {\n" << gen.body.str();
     for (int q = 0; q < K; ++q)
       for (int l = 0; l < 4; ++l) {
         const std::string a = "acc" + std::to_string(q) + "_" + std::to_string(l);
         k << "      " << a << " = " << combine(ops[q]->reduce, a, "(float)(" + vals[q][l] + ")") << ";\n";
       }
     k << "  }\n";
+    for (int q = 0; q < K; ++q)
+      k << "  red_s[" << q << "][ty][tx] = make_float4(acc" << q << "_0, acc" << q << "_1, acc" << q << "_2, acc" << q << "_3);\n";
+    k << "  __syncthreads();\n  if (ty == 0 && live) {\n";
     for (int q = 0; q < K; ++q) {
       const std::string a = "acc" + std::to_string(q) + "_";
+      k << "    for (int y = 1; y < " << TY << "; ++y) {\n      const float4 t = red_s[" << q << "][y][tx];\n";
+      static const char* c[] = {"x", "y", "z", "w"};
+      for (int l = 0; l < 4; ++l) k << "      " << a << l << " = " << combine(ops[q]->reduce, a + std::to_string(l), std::string("t.") + c[l]) << ";\n";
+      k << "    }\n";
       if (chunks > 1)
-        k << "  *(float4*)(out0 + ((long long)" << q << " * " << chunks << "LL + blockIdx.y) * " << n_out << "LL + o4) = make_float4("
+        k << "    *(float4*)(out0 + ((long long)" << q << " * " << chunks << "LL + blockIdx.y) * " << n_out << "LL + o4) = make_float4("
           << a << "0, " << a << "1, " << a << "2, " << a << "3);\n";
       else
         for (int l = 0; l < 4; ++l)
-          k << "  out" << q << "[o4 + " << l << "] = " << StoreExpr(odt[q], FromAcc(odt[q], a + std::to_string(l))) << ";\n";
+          k << "    out" << q << "[o4 + " << l << "] = "
+            << StoreExpr(odt[q], FromAcc(odt[q], combine(ops[q]->reduce, init_expr[q], a + std::to_string(l)))) << ";\n";
     }
-    k << "}\n";
+    k << "  }\n}\n";
     Launch L1;
     L1.fn = fn;
     L1.in_slots = gen.in_slots;
     L1.out_slots = chunks > 1 ? std::vector<int>{scratch} : out_slot;
-    L1.block = bt;
-    L1.grid_x = (n4 + bt - 1) / bt;
+    L1.block = TX * TY;
+    L1.grid_x = gx;
     L1.grid_y = chunks;
     Step st;
     st.kind = StepKind::kFusion;
-    st.label = "reduce x" + std::to_string(K) + " " + x0->type.str() + " -> " + ops[0]->result()->type.str();
+    st.label = (K > 1 ? "reduce x" + std::to_string(K) + " " : std::string("reduce ")) + x0->type.str() + " -> " +
+               ops[0]->result()->type.str();
     st.launches.push_back(L1);
     if (chunks > 1) {
-      // finish: a warp per (reduction, output), its lanes striding over the chunk partials
+      // finish: a block per 32 consecutive (reduction, output) pairs; its 8 warps take every 8th
+      // partial row (coalesced 128-byte reads), then combine in shared memory in a fixed order
       const std::string fn2 = KName();
       k << "extern \"C\" __global__ void __launch_bounds__(256) " << fn2 << "(const void* __restrict__ p0";
       for (int q = 0; q < K; ++q) k << ", void* __restrict__ q" << q;
-      k << ") {\n  const float* part = (const float*)p0;\n  const int lane = threadIdx.x & 31;\n"
-        << "  for (long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); w < " << K * n_out
-        << "LL; w += (long long)gridDim.x * 8) {\n    const int q = (int)(w / " << n_out << "LL);\n    const long long o = w - (long long)q * "
-        << n_out << "LL;\n    const float* pq = part + (long long)q * " << chunks * n_out << "LL;\n";
-      for (int q = 0; q < K; ++q) {
-        k << "    " << (q ? "else " : "") << "if (q == " << q << ") {\n      float acc = " << ident[q] << ";\n"
-          << "#pragma unroll 4\n      for (int c = lane; c < " << chunks << "; c += 32) acc = "
-          << combine(ops[q]->reduce, "acc", "pq[(long long)c * " + std::to_string(n_out) + "LL + o]") << ";\n"
-          << "      for (int s = 16; s; s >>= 1) { float oth = __shfl_xor_sync(0xffffffffu, acc, s); acc = "
-          << combine(ops[q]->reduce, "acc", "oth") << "; }\n"
-          << "      if (lane == 0) ((" << MemType(odt[q]) << "*)q" << q << ")[o] = "
+      k << ") {\n  const float* part = (const float*)p0;\n  __shared__ float fin_s[8][32];\n"
+        << "  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;\n"
+        << "  const long long w = (long long)blockIdx.x * 32 + tx;\n"
+        << "  const bool live = w < " << K * n_out << "LL;\n"
+        << "  const int q = live ? (int)(w / " << n_out << "LL) : 0;\n"
+        << "  const long long o = live ? w - (long long)q * " << n_out << "LL : 0;\n"
+        << "  const float* pq = part + (long long)q * " << chunks * n_out << "LL + o;\n"
+        << "  float acc = 0.f;\n";
+      for (int q = 0; q < K; ++q)
+        k << "  " << (q ? "else " : "") << "if (q == " << q << ") {\n    acc = " << ident[q] << ";\n"
+          << "#pragma unroll 4\n    for (int c = ty; c < " << chunks << "; c += 8) acc = "
+          << combine(ops[q]->reduce, "acc", "pq[(long long)c * " + std::to_string(n_out) + "LL]") << ";\n  }\n";
+      k << "  fin_s[ty][tx] = acc;\n  __syncthreads();\n  if (ty == 0 && live) {\n";
+      for (int q = 0; q < K; ++q)
+        k << "    " << (q ? "else " : "") << "if (q == " << q << ") {\n      for (int y = 1; y < 8; ++y) acc = "
+          << combine(ops[q]->reduce, "acc", "fin_s[y][tx]") << ";\n      ((" << MemType(odt[q]) << "*)q" << q << ")[o] = "
           << StoreExpr(odt[q], FromAcc(odt[q], combine(ops[q]->reduce, init_expr[q], "acc"))) << ";\n    }\n";
-      }
       k << "  }\n}\n";
       Launch L2;
       L2.fn = fn2;
       L2.in_slots = {scratch};
       L2.out_slots = out_slot;
       L2.block = 256;
-      L2.grid_x = std::max<int64_t>(1, (K * n_out + 7) / 8);
-      L2.grid_stride = true;
+      L2.grid_x = std::max<int64_t>(1, (K * n_out + 31) / 32);
       st.launches.push_back(L2);
       RecordDt(scratch, DT::kF32);
     }
