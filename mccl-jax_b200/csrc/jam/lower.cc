@@ -1992,6 +1992,41 @@ class Lowerer {
     return !probe.conflict && r == "RMAX" && probe.in_slots.empty();
   }
 
+  // reduce-add over the row of select(iota_j == label, x, 0) (either operand order of the compare,
+  // label a row-shaped integer): the cross-entropy's picked logit
+  bool OneHotPick(const Op* op, const std::vector<int64_t>& X, const Value** x, const Value** label) const {
+    if (op->reduce != ReduceKind::kAdd || op->operands.size() != 2 || std::getenv("B200_NO_PICK")) return false;
+    double init = 1;
+    if (!IsScalarConst(op->operands[1], &init) || init != 0) return false;
+    const Value* sel = op->operands[0];
+    if (!sel->def || sel->def->name != "select" || sel->type.dims != X) return false;
+    double z = 1;
+    if (!IsScalarConst(sel->def->operands[2], &z) || z != 0) return false;
+    const Value* c = sel->def->operands[0];
+    if (!c->def || c->def->name != "compare") return false;
+    auto dir = c->def->strs.find("comparison_direction");
+    if (dir == c->def->strs.end() || dir->second != "EQ") return false;
+    const int last = (int)X.size() - 1;
+    auto is_iota_last = [&](const Value* v) {
+      return v->def && v->def->name == "iota" && v->type.dims == X && v->def->ints.at("dim")[0] == last;
+    };
+    auto row_label = [&](const Value* v) -> const Value* {
+      if (!v->def || v->def->name != "broadcast_in_dim" || v->type.dims != X) return nullptr;
+      const Value* s = v->def->operands[0];
+      const auto& bd = v->def->ints.at("dims");
+      for (int64_t d : bd) if (d == last) return nullptr;                  // constant along the row
+      if (!DTIsSigned(s->type.dt) && !DTIsUnsigned(s->type.dt)) return nullptr;
+      return s;
+    };
+    const Value* a = c->def->operands[0];
+    const Value* b = c->def->operands[1];
+    const Value* lab = is_iota_last(a) ? row_label(b) : is_iota_last(b) ? row_label(a) : nullptr;
+    if (!lab) return false;
+    *x = sel->def->operands[1];
+    *label = lab;
+    return true;
+  }
+
   bool TryRow(const std::vector<const Value*>& members, const std::vector<int64_t>& X, bool dry) {
     const std::vector<int64_t> kept(X.begin(), X.end() - 1);
     const int64_t L = X.back();
@@ -2225,6 +2260,36 @@ class Lowerer {
           gen.fixed[members[q]->id] = "r" + std::to_string(q);
         }
         done[k2] = true;
+        continue;
+      }
+      const Value* pick_x = nullptr;
+      const Value* pick_label = nullptr;
+      if (op && op->name == "reduce" && OneHotPick(op, X, &pick_x, &pick_label)) {
+        // sum_j (label == j ? x[j] : 0) is x[label] (+ 0, so -0 comes out +0 as the sum gives it),
+        // or 0 for a label outside the row: one load instead of a walk of the row
+        DT odt = m->type.dt, acc_dt = AccDt(odt);
+        std::string acc_t = CType(acc_dt);
+        std::string init = InitExpr(op->operands[1], acc_dt);
+        gen.cse.clear();
+        gen.body.str("");
+        gen.body.clear();
+        gen.indent = "    ";
+        gen.vec = false;
+        gen.identity = gen.row_ident;
+        const std::string lab = gen.Emit(pick_label, gen.RowIndex(pick_label->type.dims));
+        const std::string li = "pk" + std::to_string(k);
+        body << gen.body.str() << "    const long long " << li << " = (long long)(" << lab << ");\n";
+        gen.body.str("");
+        gen.body.clear();
+        std::vector<std::string> at = gen.row_ident;
+        at.push_back("(int)(" + li + " < 0 || " + li + " >= " + Ls + "LL ? 0 : " + li + ")");
+        const std::string xv = gen.Emit(pick_x, at);
+        body << gen.body.str() << "    const " << CType(odt) << " " << rk << " = "
+             << FromAcc(odt, Combine(op->reduce, acc_dt, init, "((" + li + " < 0 || " + li + " >= " + Ls + "LL) ? (" + acc_t +
+                                                                ")0 : (" + acc_t + ")(" + xv + ") + (" + acc_t + ")0)"))
+             << ";\n";
+        if (!o.empty()) body << "    if (lt == 0) " << o << "[row] = " << StoreExpr(odt, rk) << ";\n";
+        gen.fixed[m->id] = rk;
         continue;
       }
       if (op && op->name == "reduce") {

@@ -421,3 +421,27 @@ def test_sibling_column_reductions_share_a_kernel(client, lib_path, shape, dims)
     refs = oracle_run(text, ins)
     for o, r in zip(outs, refs):
         assert_close(o, r, RTOL_F32 * 10, "column reductions")
+
+
+@pytest.mark.parametrize("V", [1000, 50257])
+def test_one_hot_pick_is_a_gather(client, lib_path, V):
+    """sum_j (label == j ? z[j] : 0) inside a row group (the cross-entropy's picked logit) is read
+    as z[label] -- exact, and 0 for labels outside the row."""
+    rows = 64
+    b = Builder("jit_pick")
+    lg = b.arg((rows, V), "f32")
+    lab = b.arg((rows,), "i32")
+    mx = b.max(lg, 1, keepdims=True)
+    z = lg - b.broadcast_to(mx, lg.shape)
+    onehot = b.compare(b.broadcast_in_dim(lab, (rows, V), [0]), b.iota((rows, V), 1), "EQ")
+    picked = b.sum(b.select(onehot, z, b.const(0.0, "f32", (rows, V))), 1)
+    lse = b.log(b.sum(b.exp(z), 1))
+    text = b.text([picked, lse - picked])
+    rng = np.random.default_rng(V)
+    x = rng.standard_normal((rows, V)).astype(np.float32)
+    labels = rng.integers(0, V, rows).astype(np.int32)
+    labels[:4] = [-1, V, 0, V - 1]
+    outs = client.run(text, [x, labels])
+    refs = oracle_run(text, [x, labels])
+    np.testing.assert_array_equal(outs[0], refs[0])
+    assert_close(outs[1], refs[1], RTOL_F32, "loss")
