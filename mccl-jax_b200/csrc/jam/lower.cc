@@ -831,7 +831,17 @@ class Lowerer {
     dead_.assign(g_.ops.size(), false);
     Retype();
     if (opt_.fuse_attention) MatchAttention();
+    // Two passes: the first decides with recomputation walking down to arguments and heavy results;
+    // the second lets a value be recomputed from what the first pass stored (a LayerNorm's x - mean
+    // and (x - mean) * rstd are then rebuilt by the backward from the stored residual and row
+    // statistics instead of being written and read back as f32 tensors).
     DecideMaterialization();
+    if (!std::getenv("B200_NO_RECOMPUTE")) {
+      const std::vector<bool> first = need_;
+      recompute_stop_ = &first;
+      DecideMaterialization();
+      recompute_stop_ = nullptr;
+    }
     DecideStoredTypes();
     BindLeaves();
     EmitSteps();
@@ -1471,6 +1481,7 @@ class Lowerer {
   // (row statistics, labels, biases).  Each reader then reads that one tensor instead of the stored
   // copy: the same bytes, minus the store.  (exp(z - max) and one-hot(labels) of a cross entropy,
   // x - mean of a LayerNorm, x + bias before an activation.)
+  const std::vector<bool>* recompute_stop_ = nullptr;   // need_ of the first materialisation pass
   bool Recomputable(const Value* v) const {
     if (std::getenv("B200_NO_RECOMPUTE")) return false;
     const int64_t n = v->type.numel();
@@ -1482,9 +1493,11 @@ class Lowerer {
       stack.pop_back();
       if (!seen.insert(x->id).second) continue;
       const Op* op = x->def;
-      const bool leaf = !op || !IsElementwise(op) || op->name == "gather" || (op->name == "constant" && !op->splat);
+      // with a first materialisation pass done, values it stored are read, not recomputed
+      const bool stored = x != v && recompute_stop_ && (*recompute_stop_)[x->id];
+      const bool leaf = stored || !op || !IsElementwise(op) || op->name == "gather" || (op->name == "constant" && !op->splat);
       if (leaf || (op->name == "constant") || op->name == "iota") {
-        if (op && (op->name == "constant" || op->name == "iota")) continue;
+        if (!stored && op && (op->name == "constant" || op->name == "iota")) continue;
         if (x->type.numel() * 16 > n) big.insert(x->id);
         if (big.size() > 1) return false;
         continue;
