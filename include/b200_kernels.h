@@ -52,8 +52,9 @@ B200_API int b200_attention_fwd_lse(const void* q, const void* k, const void* v,
 
 /* dQ, dK, dV of O = softmax(scale * Q K^T [causal]) V from Q, K, V, O, dO (bf16 [B, H, S, D]) and
  * the forward's lse2, D = 64, S a multiple of 128.  Scores are recomputed per 128 x 128 tile on
- * tcgen05; dQ accumulates in the caller's f32 scratch dq_acc [B, H, S, D]; delta [B, H, S] f32 is
- * scratch too.  Allocates nothing.
+ * tcgen05; dQ accumulates in the caller's f32 scratch dq_acc [B, H, S, D] and is rounded into dq
+ * (with dq NULL it stays there, unrounded, for a caller that rounds on read); delta [B, H, S] f32
+ * is scratch too.  Allocates nothing.
  * Replaces: the VJP of the attention chain, which the reference runs as the transposed
  * dot_generals (src/jam/ops/linalg.mm:47-105) and the elementwise softmax VJP ops
  * (src/jam/ops/elementwise.mm:91-191, src/jam/ops/reduce.mm:45-109) over full S x S tensors. */

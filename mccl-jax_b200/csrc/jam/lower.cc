@@ -341,6 +341,7 @@ struct Gen {
   // slots stored with a padded innermost row pitch (a dot's output whose rows break the 16-byte
   // rule, or a dot operand stored for in-place use)
   const std::unordered_map<int, int64_t>* slot_pitch = nullptr;
+  const std::unordered_set<int>* slot_f32 = nullptr;   // slots holding 16-bit values as f32
   int64_t SlotPitch(int slot) const {
     if (!slot_pitch) return 0;
     auto it = slot_pitch->find(slot);
@@ -450,13 +451,17 @@ struct Gen {
                                 ? li.al4 && !ty.dims.empty() && (pitch ? pitch % 4 == 0 : ty.dims.back() % 4 == 0)
                                 : !pitch && ty.dims == shift_dims && idx.size() == shift_prefix.size() + 1 && li.base == vinner + "_0" &&
                                       std::equal(shift_prefix.begin(), shift_prefix.end(), idx.begin()));
+      const bool wide16 = slot_f32 && slot_f32->count(slot) && (ty.dt == DT::kBF16 || ty.dt == DT::kF16);
       if (lane >= 0 && (ty.dt == DT::kF32 || ty.dt == DT::kBF16 || ty.dt == DT::kF16) && aligned4) {
         cur_dims = ty.dims;
         cur_pitch = pitch;
+        if (wide16) return Round(ty.dt, Var(DT::kF32, VecLoad(DT::kF32, slot, idx, lane)));
         std::string r = VecLoad(ty.dt, slot, idx, lane);
         return ty.dt == DT::kF32 ? Var(ty.dt, r) : r;
       }
-      return Var(ty.dt, LoadExpr(ty.dt, Param(slot), pitch ? PitchedLinear(idx, ty.dims, pitch) : Linear(idx, ty.dims)));
+      const std::string lin = pitch ? PitchedLinear(idx, ty.dims, pitch) : Linear(idx, ty.dims);
+      if (wide16) return Round(ty.dt, Var(DT::kF32, LoadExpr(DT::kF32, Param(slot), lin)));
+      return Var(ty.dt, LoadExpr(ty.dt, Param(slot), lin));
     }
     const Op* op = v->def;
     if (!op) throw LowerError{"internal: unmaterialized argument"};
@@ -976,7 +981,28 @@ class Lowerer {
   }
   DT StoredDt(const Value* v) const {
     auto it = demote_.find(v->id);
-    return it == demote_.end() ? v->type.dt : it->second;
+    if (it != demote_.end()) return it->second;
+    return promote_.count(v->id) ? DT::kF32 : v->type.dt;
+  }
+  // 16-bit values kept in f32 storage and rounded where they are read: a split-K dot's f32
+  // accumulator or the attention backward's dQ accumulator needs no separate rounding pass when
+  // every reader is a generated kernel
+  std::unordered_set<int> promote_;
+  std::unordered_set<int> slot_f32_;             // slots holding such values
+  bool PromotableToF32(const Value* v) const {
+    if ((v->type.dt != DT::kBF16 && v->type.dt != DT::kF16) || pitch_.count(v->id) || std::getenv("B200_NO_PROMOTE"))
+      return false;
+    for (const Value* o : g_.outputs) if (o == v) return false;
+    if (v->users.empty()) return false;
+    for (const Op* u : v->users) {
+      if (dead_[u->index]) continue;
+      const bool gen = (IsElementwise(u) && u->name != "reshape" && u->name != "bitcast_convert" && u->name != "gather") ||
+                       (u->name == "reduce" && u->operands[0] == v && u->results.size() == 1);
+      if (!gen) return false;
+    }
+    for (auto& kv : attn_in_) for (const Value* x : kv.second) if (x == v) return false;
+    for (const BwdMatch& m : bwd_) for (const Value* x : {m.Q, m.K, m.V, m.O, m.G}) if (x == v) return false;
+    return true;
   }
   // the value to store for root v into a buffer of type `dt` (rounded when the buffer is narrower)
   static std::string StoreVal(const Value* v, DT dt, const std::string& x) {
@@ -1580,6 +1606,7 @@ class Lowerer {
     if (slot_of_[v->id] < 0) {
       slot_of_[v->id] = NewSlot(StoredBytes(v));
       if (const int64_t p = StoredPitch(v)) slot_pitch_[slot_of_[v->id]] = p;
+      if (promote_.count(v->id)) slot_f32_.insert(slot_of_[v->id]);
     }
     return slot_of_[v->id];
   }
@@ -1794,6 +1821,7 @@ class Lowerer {
     Gen gen;
     gen.slot_of = &slot_of_;
     gen.slot_pitch = &slot_pitch_;
+    gen.slot_f32 = &slot_f32_;
     gen.group_dims = dims;
     std::ostringstream pre;
     std::string ind = "    ";
@@ -2075,6 +2103,7 @@ class Lowerer {
     Gen gen;
     gen.slot_of = &slot_of_;
     gen.slot_pitch = &slot_pitch_;
+    gen.slot_f32 = &slot_f32_;
     gen.group_dims = X;
     std::ostringstream ob, body;
     gen.row_ident = Delinearize(ob, "row", kept, "a", "    ", wide);
@@ -2482,6 +2511,7 @@ class Lowerer {
     Gen gen;
     gen.slot_of = &slot_of_;
     gen.slot_pitch = &slot_pitch_;
+    gen.slot_f32 = &slot_f32_;
     gen.indent = "      ";
     std::ostringstream ob, jb;
     auto names_k = Delinearize(ob, inner ? "row" : "o", kept, "a", "    ", wide);
@@ -2611,6 +2641,7 @@ class Lowerer {
     Gen gen;
     gen.slot_of = &slot_of_;
     gen.slot_pitch = &slot_pitch_;
+    gen.slot_f32 = &slot_f32_;
     gen.indent = "      ";
     std::ostringstream ob, inner_pre, k;
     auto names_k = Delinearize(ob, "o4", kept, "a", "  ", wide);
@@ -2762,6 +2793,7 @@ class Lowerer {
     Gen gen;
     gen.slot_of = &slot_of_;
     gen.slot_pitch = &slot_pitch_;
+    gen.slot_f32 = &slot_f32_;
     std::ostringstream pre;
     // init value (scalar expression)
     std::string init_expr;
@@ -3199,9 +3231,14 @@ class Lowerer {
     g.b = ob.slot;
     g.b_mn = ob.mn;
     g.ldb = ob.ld;
+    const bool split = tc && g.out != DT::kF32 && !StoredPitch(r) && b200k::GemmSplitK(g.batch, g.M, g.N, g.K, 148) > 1;
+    if (split && PromotableToF32(r)) {           // readers round the f32 partial sums themselves
+      promote_.insert(r->id);
+      g.out = DT::kF32;
+    }
     g.c = SlotFor(r);
     g.ldc = StoredPitch(r);                      // 0: dense rows of N
-    if (tc && g.out != DT::kF32 && !g.ldc && b200k::GemmSplitK(g.batch, g.M, g.N, g.K, 148) > 1) {
+    if (split && g.out != DT::kF32) {
       g.ws = NewSlot(g.batch * g.M * g.N * 4);   // split-K partial sums
       RecordDt(g.ws, DT::kF32);
     }
@@ -3211,7 +3248,7 @@ class Lowerer {
     st.label = "gemm b" + std::to_string(g.batch) + " " + std::to_string(g.M) + "x" + std::to_string(g.N) + "x" + std::to_string(g.K) +
                (g.a_mn || g.b_mn ? std::string(" ") + (g.a_mn ? "m" : "k") + (g.b_mn ? "n" : "k") : "");
     p_->steps.push_back(st);
-    RecordDt(g.c, g.out);
+    RecordDt(g.c, StoredDt(r));
   }
 
   void EmitAttention(Op* d2) {
@@ -3252,14 +3289,16 @@ class Lowerer {
     b.dout = SlotFor(m.G);
     b.lse = lse_for_.at(m.d2);
     if (b.lse < 0) throw LowerError{"internal: attention backward before its forward"};
-    b.dq = SlotFor(m.dq);
+    const bool dq_f32 = PromotableToF32(m.dq);   // readers round dQ from its f32 accumulator
+    if (dq_f32) promote_.insert(m.dq->id);
+    b.dq = dq_f32 ? -1 : SlotFor(m.dq);
     b.dk = SlotFor(m.dk);
     b.dv = SlotFor(m.dv);
     const int64_t rows = (int64_t)a.B * a.H * a.S;
-    b.dq_acc = NewSlot(rows * a.D * 4);
+    b.dq_acc = dq_f32 ? SlotFor(m.dq) : NewSlot(rows * a.D * 4);
     b.delta = NewSlot(rows * 4);
     b.dk_t = m.dk_t;                             // the kernel writes dK in the dot's [B, H, D, S] layout
-    for (int s : {b.dq, b.dk, b.dv}) RecordDt(s, DT::kBF16);
+    for (int s : {b.dq, b.dk, b.dv}) if (s >= 0) RecordDt(s, DT::kBF16);
     for (int s : {b.dq_acc, b.delta}) RecordDt(s, DT::kF32);
     Step st;
     st.kind = StepKind::kAttentionBwd;

@@ -517,7 +517,8 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
             err = slot(s);
             if (!err.empty()) return fail(err);
           }
-          int rc = b200k::AttentionBwd(ptr[b.q], ptr[b.k], ptr[b.v], ptr[b.o], ptr[b.dout], (const float*)ptr[b.lse], ptr[b.dq],
+          int rc = b200k::AttentionBwd(ptr[b.q], ptr[b.k], ptr[b.v], ptr[b.o], ptr[b.dout], (const float*)ptr[b.lse],
+                                     b.dq >= 0 ? ptr[b.dq] : nullptr,
                                        ptr[b.dk], ptr[b.dv], (float*)ptr[b.dq_acc], (float*)ptr[b.delta], b.B, b.H, b.S, b.D,
                                        b.causal, b.scale, st, b.dk_t ? 1 : 0);
           if (rc != 0) return fail("attention backward launch failed (" + std::to_string(rc) + ")");

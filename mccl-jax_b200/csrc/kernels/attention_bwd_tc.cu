@@ -467,8 +467,10 @@ int AttentionBwd(const void* q, const void* k, const void* v, const void* o, con
   else
     attn_bwd_kernel<false><<<grid, kThreads, C::kSmem, st>>>(mq, mk, mv, mdo, mdq, lse2, delta, dq_acc, (__nv_bfloat16*)dk,
                                                          (__nv_bfloat16*)dv, S, scale, scale_log2, dk_t);
+  // dq null: the caller reads dQ (rounding it itself) from the f32 accumulator
   const long long n4 = rows * HD / 4;
-  f32_to_bf16_kernel<<<(unsigned)std::min<long long>((n4 + 255) / 256, 148 * 8), 256, 0, st>>>(dq_acc, (__nv_bfloat16*)dq, n4);
+  if (dq)
+    f32_to_bf16_kernel<<<(unsigned)std::min<long long>((n4 + 255) / 256, 148 * 8), 256, 0, st>>>(dq_acc, (__nv_bfloat16*)dq, n4);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

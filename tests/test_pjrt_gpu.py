@@ -445,3 +445,23 @@ def test_one_hot_pick_is_a_gather(client, lib_path, V):
     refs = oracle_run(text, [x, labels])
     np.testing.assert_array_equal(outs[0], refs[0])
     assert_close(outs[1], refs[1], RTOL_F32, "loss")
+
+
+def test_split_k_dot_read_by_a_fused_kernel(client):
+    """A bf16 dot computed split-K whose readers are generated kernels keeps its f32 sums and the
+    readers round them to bf16 (no separate rounding pass): same values as rounding first."""
+    b = Builder("jit_dw_update")
+    x = b.arg((4096, 384), "bf16")
+    dy = b.arg((4096, 512), "bf16")
+    p = b.arg((384, 512), "f32")
+    dw = b.dot_general(x, dy, contract=([0], [0]), out_dtype="bf16")
+    upd = p - 0.5 * b.convert(dw, "f32")
+    text = b.text([upd, b.sum(b.convert(dw, "f32"), [0])])
+    rng = np.random.default_rng(13)
+    ins = [(rng.standard_normal((4096, 384)) * 0.1).astype(ml_dtypes.bfloat16),
+           (rng.standard_normal((4096, 512)) * 0.1).astype(ml_dtypes.bfloat16),
+           rng.standard_normal((384, 512)).astype(np.float32)]
+    outs = client.run(text, ins)
+    refs = oracle_run(text, ins)
+    assert_close(outs[0], refs[0], 1e-2, "update")
+    assert_close(outs[1], refs[1], 1e-2, "column sum")
