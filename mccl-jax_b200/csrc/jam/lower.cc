@@ -1013,9 +1013,22 @@ class Lowerer {
   std::unordered_map<int, std::array<const Value*, 3>> attn_in_;
   std::ostringstream src_;
   // Each finished kernel's source becomes its own unit so NVRTC can compile them in parallel.
+  // Every generated kernel starts with griddepcontrol.wait: launched as a programmatic dependent of
+  // the previous kernel it may be scheduled while that one drains, and waits here (before its first
+  // read) until the previous grid has completed and its writes are visible.  It then lets its own
+  // dependent be scheduled (launch_dependents), which waits the same way.
   void EndKernel() {
     std::string k = src_.str();
-    if (!k.empty()) p_->kernel_sources.push_back(k);
+    if (!k.empty()) {
+      const std::string tag = "extern \"C\" __global__";
+      for (size_t at = k.find(tag); at != std::string::npos; at = k.find(tag, at + 1)) {
+        const size_t open = k.find(") {\n", at);
+        if (open == std::string::npos) break;
+        k.insert(open + 4, "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n"
+                           "  asm volatile(\"griddepcontrol.launch_dependents;\");\n");
+      }
+      p_->kernel_sources.push_back(k);
+    }
     src_.str("");
     src_.clear();
   }

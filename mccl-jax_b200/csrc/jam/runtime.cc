@@ -42,10 +42,12 @@ typedef CUresult (*FnLaunchKernel)(CUfunction, unsigned, unsigned, unsigned, uns
 typedef CUresult (*FnModuleUnload)(CUmodule);
 typedef CUresult (*FnOccupancy)(int*, CUfunction, int, size_t);
 
+typedef CUresult (*FnLaunchKernelEx)(const CUlaunchConfig*, CUfunction, void**, void**);
 struct Driver {
   FnModuleLoadData load = nullptr;
   FnModuleGetFunction get = nullptr;
   FnLaunchKernel launch = nullptr;
+  FnLaunchKernelEx launch_ex = nullptr;      // programmatic dependent launches (optional)
   FnModuleUnload unload = nullptr;
   FnOccupancy occupancy = nullptr;
   bool ok = false;
@@ -65,6 +67,7 @@ const Driver& Drv() {
     d.load = (FnModuleLoadData)sym("cuModuleLoadData");
     d.get = (FnModuleGetFunction)sym("cuModuleGetFunction");
     d.launch = (FnLaunchKernel)sym("cuLaunchKernel");
+    d.launch_ex = (FnLaunchKernelEx)sym("cuLaunchKernelEx");
     d.unload = (FnModuleUnload)sym("cuModuleUnload");
     d.occupancy = (FnOccupancy)sym("cuOccupancyMaxActiveBlocksPerMultiprocessor");
     d.ok = d.load && d.get && d.launch && d.unload && d.occupancy;
@@ -468,6 +471,7 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     if (g) cudaGraphDestroy(g);
     cudaGetLastError();
   };
+  static const bool pdl = std::getenv("B200_NO_PDL") == nullptr;
   auto run_steps = [&]() -> std::string {
     for (size_t i = 0; i < P.steps.size(); ++i) {
       const Step& S = P.steps[i];
@@ -487,8 +491,29 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
               auto w = pd->wave.find(L.fn);
               if (w != pd->wave.end()) gx = std::max<int64_t>(1, std::min(gx, w->second));
             }
-            CUresult r = drv.launch((CUfunction)pd->fns.at(L.fn), (unsigned)gx, (unsigned)L.grid_y, (unsigned)L.grid_z, L.block, 1, 1,
-                                    L.smem, (CUstream)st, params.data(), nullptr);
+            CUresult r;
+            if (drv.launch_ex && pdl) {
+              // may start while the previous kernel drains; the kernel waits (griddepcontrol.wait)
+              // before it reads anything
+              CUlaunchAttribute attr[1];
+              attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+              attr[0].value.programmaticStreamSerializationAllowed = 1;
+              CUlaunchConfig cfg = {};
+              cfg.gridDimX = (unsigned)gx;
+              cfg.gridDimY = (unsigned)L.grid_y;
+              cfg.gridDimZ = (unsigned)L.grid_z;
+              cfg.blockDimX = L.block;
+              cfg.blockDimY = 1;
+              cfg.blockDimZ = 1;
+              cfg.sharedMemBytes = L.smem;
+              cfg.hStream = (CUstream)st;
+              cfg.attrs = attr;
+              cfg.numAttrs = 1;
+              r = drv.launch_ex(&cfg, (CUfunction)pd->fns.at(L.fn), params.data(), nullptr);
+            } else {
+              r = drv.launch((CUfunction)pd->fns.at(L.fn), (unsigned)gx, (unsigned)L.grid_y, (unsigned)L.grid_z, L.block, 1, 1,
+                             L.smem, (CUstream)st, params.data(), nullptr);
+            }
             if (r != CUDA_SUCCESS) return fail("launch of " + L.fn + " failed (" + std::to_string((int)r) + ")");
           }
           break;
