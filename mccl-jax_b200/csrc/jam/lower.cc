@@ -2197,12 +2197,12 @@ class Lowerer {
     if (shift)
       ob << "    const int hd = (int)((4 - (int)((row * " << Ls << "LL) & 3)) & 3), nv = (" << Ls << " - hd) >> 2, nrem = " << Ls
          << " - 4 * nv;\n";
-    const std::string shift_head = "#pragma unroll 4\n    for (int jv = lt; jv < nv; jv += " + Ts +
+    const std::string shift_head = "#pragma unroll 8\n    for (int jv = lt; jv < nv; jv += " + Ts +
                                    ") {\n      const int j = hd + 4 * jv;\n      const int j_0 = j, j_1 = j + 1, j_2 = j + 2, j_3 = j + 3;\n";
     const std::string rem_head = "    for (int j = lt; j < nrem; j += " + Ts +
                                  ") {\n      const bool ok_1 = false, ok_2 = false, ok_3 = false;\n"
                                  "      const int j_0 = j < hd ? j : j + 4 * nv, j_1 = j_0, j_2 = j_0, j_3 = j_0;\n";
-    const std::string padded_head = "#pragma unroll 4\n    for (int j = lt * 4; j < " + Ls + "; j += " + std::to_string(4 * T) +
+    const std::string padded_head = "#pragma unroll 8\n    for (int j = lt * 4; j < " + Ls + "; j += " + std::to_string(4 * T) +
                                     ") {\n      const bool ok_1 = j + 1 < " + Ls + ", ok_2 = j + 2 < " + Ls + ", ok_3 = j + 3 < " + Ls +
                                     ";\n      const int j_0 = j, j_1 = ok_1 ? j + 1 : " + last + ", j_2 = ok_2 ? j + 2 : " + last +
                                     ", j_3 = ok_3 ? j + 3 : " + last + ";\n";
