@@ -851,6 +851,7 @@ class Lowerer {
     BindLeaves();
     EmitSteps();
     BindOutputs();
+    MergeTinyLoops();
     MarkAsyncCollectives();
     ComputeLastUse();
     EndKernel();
@@ -3385,6 +3386,137 @@ class Lowerer {
     st.label = n + " " + x->type.str();
     p_->steps.push_back(st);
     RecordDt(c.out, c.dt);
+  }
+
+  // ---------------------------------------------------------------- horizontal fusion
+  static void StepRW(const Step& S, std::set<int>* r, std::set<int>* w) {
+    auto R = [&](std::initializer_list<int> l) { for (int x : l) if (x >= 0) r->insert(x); };
+    auto W = [&](std::initializer_list<int> l) { for (int x : l) if (x >= 0) w->insert(x); };
+    switch (S.kind) {
+      case StepKind::kFusion:
+        for (const Launch& L : S.launches) {
+          for (int x : L.in_slots) R({x});
+          for (int x : L.out_slots) W({x});
+          W({L.scratch});
+        }
+        break;
+      case StepKind::kGemm: R({S.gemm.a, S.gemm.b}); W({S.gemm.c, S.gemm.ws}); break;
+      case StepKind::kAttention: R({S.attn.q, S.attn.k, S.attn.v}); W({S.attn.o, S.attn.lse}); break;
+      case StepKind::kAttentionBwd:
+        R({S.bwd.q, S.bwd.k, S.bwd.v, S.bwd.o, S.bwd.dout, S.bwd.lse});
+        W({S.bwd.dq, S.bwd.dk, S.bwd.dv, S.bwd.dq_acc, S.bwd.delta});
+        break;
+      case StepKind::kScatterAdd: R({S.scatter.base, S.scatter.idx, S.scatter.upd}); W({S.scatter.out}); break;
+      case StepKind::kCollective: R({S.coll.in}); W({S.coll.out}); break;
+      case StepKind::kCopy: R({S.copy.src}); W({S.copy.dst}); break;
+    }
+  }
+  bool TinyLoop(const Step& S) const {
+    if (S.kind != StepKind::kFusion || S.launches.size() != 1 || S.label.compare(0, 5, "loop ") != 0) return false;
+    const Launch& L = S.launches[0];
+    return L.block == 256 && L.grid_y == 1 && L.grid_z == 1 && L.scratch < 0 && L.smem == 0 && L.grid_x <= 4;
+  }
+  // Loop kernels of at most four CTAs (the optimizer updates of biases and LayerNorm parameters)
+  // that do not depend on each other, nor on the steps they are moved across, run as one launch:
+  // each becomes a device function taking its CTA index and count, and one kernel dispatches its
+  // CTAs to them by range.
+  void MergeTinyLoops() {
+    if (std::getenv("B200_NO_HMERGE")) return;
+    std::vector<Step>& steps = p_->steps;
+    std::vector<Step> out;
+    std::vector<bool> taken(steps.size(), false);
+    for (size_t i = 0; i < steps.size(); ++i) {
+      if (taken[i]) continue;
+      if (!TinyLoop(steps[i])) { out.push_back(steps[i]); continue; }
+      std::vector<size_t> group{i};
+      std::set<int> gr, gw, br, bw;           // group reads / writes, steps passed over
+      StepRW(steps[i], &gr, &gw);
+      size_t params = steps[i].launches[0].in_slots.size() + steps[i].launches[0].out_slots.size();
+      for (size_t j = i + 1; j < steps.size() && j < i + 96 && group.size() < 24; ++j) {
+        if (taken[j]) continue;
+        std::set<int> r, w;
+        StepRW(steps[j], &r, &w);
+        auto meets = [](const std::set<int>& a, const std::set<int>& b) {
+          for (int x : a) if (b.count(x)) return true;
+          return false;
+        };
+        const size_t np = TinyLoop(steps[j]) ? steps[j].launches[0].in_slots.size() + steps[j].launches[0].out_slots.size() : 0;
+        if (TinyLoop(steps[j]) && params + np <= 480 && !meets(r, bw) && !meets(w, br) && !meets(w, bw) && !meets(r, gw) &&
+            !meets(w, gr) && !meets(w, gw)) {
+          group.push_back(j);
+          gr.insert(r.begin(), r.end());
+          gw.insert(w.begin(), w.end());
+          params += np;
+          continue;
+        }
+        br.insert(r.begin(), r.end());
+        bw.insert(w.begin(), w.end());
+      }
+      if (group.size() == 1) { out.push_back(steps[i]); continue; }
+      for (size_t g : group) taken[g] = true;
+      out.push_back(MergeLoopSteps(group));
+    }
+    steps = std::move(out);
+  }
+  Step MergeLoopSteps(const std::vector<size_t>& group) {
+    std::vector<Step>& steps = p_->steps;
+    const std::string fn = KName();
+    std::ostringstream unit, wrap_params, body;
+    Launch M;
+    M.fn = fn;
+    M.block = 256;
+    M.grid_stride = false;
+    int64_t base = 0;
+    std::vector<std::string> in_args, out_args;
+    for (size_t q = 0; q < group.size(); ++q) {
+      const Launch& L = steps[group[q]].launches[0];
+      // move the kernel's source unit, turned into a device function of (CTA index, CTA count)
+      auto& ks = p_->kernel_sources;
+      const std::string head = "extern \"C\" __global__ void __launch_bounds__(256, 4) " + L.fn + "(";
+      size_t u = 0;
+      while (u < ks.size() && ks[u].find(head) == std::string::npos) ++u;
+      if (u == ks.size()) throw LowerError{"internal: kernel " + L.fn + " not found for merging"};
+      std::string src = ks[u];
+      ks.erase(ks.begin() + (long)u);
+      const size_t at = src.find(head);
+      const size_t open = src.find(") {\n", at);
+      std::string kern = src.substr(at, open - at) + ", const unsigned hbx, const unsigned hgx" + src.substr(open);
+      kern.replace(0, head.size() - L.fn.size() - 1, "static __device__ __forceinline__ void ");
+      for (const char* from : {"blockIdx.x", "gridDim.x"}) {
+        const std::string to = std::string(from) == "blockIdx.x" ? "hbx" : "hgx";
+        for (size_t p = kern.find(from); p != std::string::npos; p = kern.find(from, p + to.size())) kern.replace(p, std::strlen(from), to);
+      }
+      unit << src.substr(0, at) << kern;
+      std::vector<std::string> args;
+      for (size_t k = 0; k < L.in_slots.size(); ++k) {
+        const std::string a = "h" + std::to_string(q) + "p" + std::to_string(k);
+        in_args.push_back("const void* __restrict__ " + a);
+        args.push_back(a);
+        M.in_slots.push_back(L.in_slots[k]);
+      }
+      for (size_t k = 0; k < L.out_slots.size(); ++k) {
+        const std::string a = "h" + std::to_string(q) + "q" + std::to_string(k);
+        out_args.push_back("void* __restrict__ " + a);
+        args.push_back(a);
+        M.out_slots.push_back(L.out_slots[k]);
+      }
+      body << "  " << (q ? "else " : "") << "if (b < " << base + L.grid_x << "u) " << L.fn << "(";
+      for (auto& a : args) body << a << ", ";
+      body << "b - " << base << "u, " << L.grid_x << "u);\n";
+      base += L.grid_x;
+    }
+    std::string plist;
+    for (auto& a : in_args) plist += (plist.empty() ? "" : ", ") + a;
+    for (auto& a : out_args) plist += (plist.empty() ? "" : ", ") + a;
+    unit << "extern \"C\" __global__ void __launch_bounds__(256, 4) " << fn << "(" << plist << ") {\n"
+         << "  const unsigned b = blockIdx.x;\n" << body.str() << "}\n";
+    p_->kernel_sources.push_back(unit.str());
+    M.grid_x = base;
+    Step st;
+    st.kind = StepKind::kFusion;
+    st.launches.push_back(M);
+    st.label = "loops x" + std::to_string(group.size()) + " (merged small kernels)";
+    return st;
   }
 
   // ---------------------------------------------------------------- outputs
