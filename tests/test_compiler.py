@@ -123,3 +123,16 @@ def test_generated_kernels_compile_with_nvrtc_for_sm100a(lib_path):
     r0 = b.max(w, 0)
     rc, rep = report(lib_path, b.text([b.convert(w, "bf16"), r1, r0]))
     assert rc == 0, rep
+
+
+def test_small_independent_loops_share_one_launch(lib_path):
+    """Updates of several small parameters (no data flow between them) become one merged kernel
+    whose CTAs are dispatched to each update by range; a dependent one is not merged."""
+    b = Builder("jit_small_updates")
+    ps = [b.arg((n,), "f32") for n in (768, 2304, 96)]
+    gs = [b.arg((n,), "f32") for n in (768, 2304, 96)]
+    outs = [p - 0.1 * g for p, g in zip(ps, gs)]
+    outs.append(b.sum(outs[0], [0]) + 1.0)          # reads an update: after the merged kernel
+    rc, rep = report(lib_path, b.text(outs))
+    assert rc == 0, rep
+    assert "loops x3" in rep, rep
