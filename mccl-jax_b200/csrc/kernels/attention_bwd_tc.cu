@@ -179,12 +179,11 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       const uint32_t k_a = smem_u32(smem + C::kKOff), v_a = smem_u32(smem + C::kVOff);
       const uint32_t p_a = smem_u32(smem + C::kPOff), ds_a = smem_u32(smem + C::kdSOff);
       bool ok = mbar_wait(&bars[kKVFull], 0, kErrTimeoutFull, err);
-      for (int i = 0; i < n_it && ok; ++i) {
-        const int st = i & 1;
-        const uint32_t ph = (i >> 1) & 1;
-        const uint32_t q_a = smem_u32(smem + C::kQOff + st * C::kTile), do_a = smem_u32(smem + C::kdOOff + st * C::kTile);
-        if (!(ok = mbar_wait(&bars[kQFull + st], ph, kErrTimeoutFull, err))) break;
-        if (i > 0 && !(ok = mbar_wait(&bars[kSFree], (i - 1) & 1, kErrTimeoutFull, err))) break;
+      // S^T = K Q^T and dP^T = V dO^T of step j into TMEM columns 0-255
+      auto scores = [&](int j) {
+        const int sj = j & 1;
+        const uint32_t q_a = smem_u32(smem + C::kQOff + sj * C::kTile), do_a = smem_u32(smem + C::kdOOff + sj * C::kTile);
+        if (!mbar_wait(&bars[kQFull + sj], (j >> 1) & 1, kErrTimeoutFull, err)) return false;
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k)
@@ -193,6 +192,19 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         for (int k = 0; k < HD / 16; ++k)
           mma_f16_ss(tmem + 128, sw128_desc(v_a + k * 32), sw128_desc(do_a + k * 32), id_s, k != 0);
         mma_commit(&bars[kSFull]);
+        return true;
+      };
+      if (ok && n_it > 0) ok = scores(0);
+      for (int i = 0; i < n_it && ok; ++i) {
+        const int st = i & 1;
+        const uint32_t q_a = smem_u32(smem + C::kQOff + st * C::kTile), do_a = smem_u32(smem + C::kdOOff + st * C::kTile);
+        // the next step's scores go first: once the P / dS warps have read S^T / dP^T of this step,
+        // the tensor core computes the next ones while those warps finish and this step's gradient
+        // products below follow
+        if (i + 1 < n_it) {
+          if (!(ok = mbar_wait(&bars[kSFree], i & 1, kErrTimeoutFull, err))) break;
+          if (!(ok = scores(i + 1))) break;
+        }
         // dV += P^T dO and dK += dS^T Q: K = 128 queries in steps of 16, issued per 64-query half as
         // soon as that half of P^T / dS^T is in shared memory (the other half is still being written)
         for (int hh = 0; hh < 2 && ok; ++hh) {
@@ -240,7 +252,6 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       // the lse2 / delta slices arrive with the Q / dO tiles of this stage
       if (!(ok = mbar_wait_warp(&bars[kQFull + st], (i >> 1) & 1, kErrTimeoutAcc, err))) break;
       if (!(ok = mbar_wait_warp(&bars[kSFull], i & 1, kErrTimeoutAcc, err))) break;
-      if (i > 0 && !(ok = mbar_wait_warp(&bars[kPdSFree], (i - 1) & 1, kErrTimeoutAcc, err))) break;
       tc_fence_after();
       const bool diag = CAUSAL && q0 == k0;
 #pragma unroll 1
@@ -265,9 +276,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           pp[e >> 1] = pack_bf16x2(p0, p1);
           pd[e >> 1] = pack_bf16x2(d0, d1);
         }
+        // the previous step's P / dS may still be read by its dV / dK / dQ products
+        if (c == half * 64 && i > 0 && !(ok = mbar_wait_warp(&bars[kPdSFree], (i - 1) & 1, kErrTimeoutAcc, err))) break;
         store_row32(p_tile, r, c, pp);
         store_row32(ds_tile, r, c, pd);
       }
+      if (!ok) break;
       tc_fence_before();
       mbar_arrive(&bars[kSFree]);                // S^T / dP^T may be recomputed for the next tile
       fence_async_shared();
