@@ -262,6 +262,10 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         tmem_ld16(tmem + lane_off + 128 + c, *reinterpret_cast<uint32_t(*)[16]>(dv));
         tmem_ld16(tmem + lane_off + 128 + c + 16, *reinterpret_cast<uint32_t(*)[16]>(dv + 16));
         tmem_wait_ld();
+        if (c == half * 64 + 32) {                // last TMEM read of this step: S^T / dP^T may be
+          tc_fence_before();                      // recomputed for the next step
+          mbar_arrive(&bars[kSFree]);
+        }
         uint32_t pp[16], pd[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
@@ -282,8 +286,6 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         store_row32(ds_tile, r, c, pd);
       }
       if (!ok) break;
-      tc_fence_before();
-      mbar_arrive(&bars[kSFree]);                // S^T / dP^T may be recomputed for the next tile
       fence_async_shared();
       mbar_arrive(&bars[kPdSFull + half]);
     }
