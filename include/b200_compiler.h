@@ -14,10 +14,12 @@
 extern "C" {
 #endif
 
-/* Compiles StableHLO MLIR text for `num_processes` ranks.  Writes a NUL-terminated report into
+/* Compiles StableHLO (MLIR text or bytecode) for `num_processes` ranks.  Writes a NUL-terminated report into
  * out[0..out_size): on success the plan dump ("plan: ...\n" then one line per step); on failure
  * "error: <message>".  Returns 0 on success, 1 on a compile error, -1 if `out` is too small.
- * `nvrtc` = 0 skips the NVRTC step (parse + lower only). */
+ * `nvrtc` = 0 skips the NVRTC step (parse + lower only); `nvrtc` = 2 only parses and reports the
+ * parsed op graph (one line per op with its attributes and a checksum of constant data) instead of
+ * the plan.  `text` may also be MLIR bytecode (it starts with "ML\xefR"). */
 __attribute__((visibility("default"))) int b200_compile_report(const char* text, size_t size, int num_processes,
                                                                int nvrtc, char* out, size_t out_size);
 

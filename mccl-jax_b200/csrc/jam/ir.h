@@ -90,6 +90,12 @@ struct Graph {
 // Returns an empty string on success, else an error message (the op or token that failed).
 std::string ParseModule(const char* text, size_t size, Graph* g);
 
+// One line per op of a parsed graph: name, operand / result value ids and types, integer
+// attributes, the attributes the lowering reads as strings, reduce kind and the constant data
+// (splat flag + FNV-1a hash of the bytes).  Two spellings of one program (pretty or generic text,
+// MLIR bytecode) parse to the same dump.
+std::string DumpGraph(const Graph& g);
+
 // Reads the value of a float/int scalar constant as double.
 double ConstScalar(const Op* op);
 

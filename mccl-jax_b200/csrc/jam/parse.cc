@@ -2,13 +2,18 @@
 //
 // Replaces the reference's MLIR deserialization + normalization (src/jam/parse.cc:17-63): the
 // plugin reads the module *text* jax prints (`jit(f).lower(...).as_text()`), in the pretty forms of
-// elementwise / shape / reduce / dot ops and the generic `"stablehlo.x"(...) <{...}> ({...})` form of
-// gather / scatter / collectives.  `func.call`s are inlined while building the graph, which is what
+// elementwise / shape / reduce / dot ops and the generic `"stablehlo.x"(...) <{...}> ({...})` form
+// (which gather / scatter / collectives always use, and which every op takes in MLIR bytecode:
+// bytecode input is first decoded to text by bytecode.cc).  `func.call`s are inlined while building the graph, which is what
 // the reference's lowering walk does (src/jam/lower.mm:245-268); `optimization_barrier`, tuples'
 // absence and the shard_map custom calls are handled by the planner.
 #include "ir.h"
 
+#include "bytecode.h"
+
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <sstream>
@@ -187,6 +192,9 @@ struct FuncAst {
 struct ParseError {
   std::string msg;
 };
+
+std::vector<int64_t> ParseIntsAttr(const std::string& s);
+void ParseDimNumbers(const std::string& s, const std::string& prefix, Op* op);
 
 class Parser {
  public:
@@ -514,7 +522,7 @@ class Parser {
           if (Accept("x")) {
             op.ints[key + ".lhs"] = lhs;
             op.ints[key + ".rhs"] = IntList();
-          } else {
+          } else if (key != "precision") {   // precision = [DEFAULT, DEFAULT]: no shape information
             op.ints[key] = lhs;
           }
         } else {
@@ -607,7 +615,79 @@ class Parser {
     }
     Expect(":");
     FnType(op, op.operands.size());
+    NormalizeGeneric(op);
     return op;
+  }
+
+  // The generic form spells attributes as StableHLO's op definitions name them
+  // (broadcast_dimensions, permutation, #stablehlo.dot<...>, ...); the lowering reads the keys the
+  // pretty form gives (Pretty / Reduce above).  Both forms must give one IR.
+  static void NormalizeGeneric(OpAst& op) {
+    auto take = [&](const char* key, std::string* out) {
+      auto it = op.strs.find(key);
+      if (it == op.strs.end()) return false;
+      *out = it->second;
+      op.strs.erase(it);
+      return true;
+    };
+    auto ints_of = [&](const char* key, const char* as) {
+      std::string v;
+      if (take(key, &v)) op.ints[as] = ParseIntsAttr(v);
+    };
+    // "#stablehlo<comparison_direction GE>" -> "GE"
+    auto enum_word = [](const std::string& v) {
+      std::string s = v;
+      size_t gt = s.rfind('>');
+      if (gt != std::string::npos) s = s.substr(0, gt);
+      size_t sp = s.find_last_of(" <");
+      return sp == std::string::npos ? s : s.substr(sp + 1);
+    };
+    const std::string& n = op.name;
+    std::string v;
+    if (n == "func.call") {
+      if (take("callee", &v)) op.strs["callee"] = v.empty() || v[0] != '@' ? v : v.substr(1);
+    } else if (n == "stablehlo.broadcast_in_dim") {
+      ints_of("broadcast_dimensions", "dims");
+    } else if (n == "stablehlo.transpose") {
+      ints_of("permutation", "dims");
+    } else if (n == "stablehlo.iota") {
+      ints_of("iota_dimension", "dim");
+    } else if (n == "stablehlo.concatenate") {
+      ints_of("dimension", "dim");
+    } else if (n == "stablehlo.reduce") {
+      ints_of("dimensions", "dimensions");
+    } else if (n == "stablehlo.slice") {
+      ints_of("start_indices", "start_indices");
+      ints_of("limit_indices", "limit_indices");
+      ints_of("strides", "strides");
+    } else if (n == "stablehlo.pad") {
+      ints_of("edge_padding_low", "low");
+      ints_of("edge_padding_high", "high");
+      ints_of("interior_padding", "interior");
+    } else if (n == "stablehlo.compare") {
+      if (take("comparison_direction", &v)) op.strs["comparison_direction"] = enum_word(v);
+      if (take("compare_type", &v)) op.strs["compare_type"] = enum_word(v);
+    } else if (n == "stablehlo.constant") {
+      if (take("value", &v)) op.dense = v;
+    } else if (n == "stablehlo.custom_call") {
+      if (take("call_target_name", &v)) {
+        if (v.size() >= 2 && v.front() == '"') v = v.substr(1, v.size() - 2);
+        op.strs["call_target_name"] = v;
+      }
+    } else if (n == "stablehlo.dot_general") {
+      if (take("dot_dimension_numbers", &v)) {
+        Op scratch;
+        ParseDimNumbers(v, "", &scratch);
+        static const char* kMap[][2] = {{"lhs_batching_dimensions", "batching_dims.lhs"},
+                                        {"rhs_batching_dimensions", "batching_dims.rhs"},
+                                        {"lhs_contracting_dimensions", "contracting_dims.lhs"},
+                                        {"rhs_contracting_dimensions", "contracting_dims.rhs"}};
+        for (auto& m : kMap) {
+          auto it = scratch.ints.find(m[0]);
+          if (it != scratch.ints.end()) op.ints[m[1]] = it->second;
+        }
+      }
+    }
   }
 };
 
@@ -728,8 +808,22 @@ ReduceKind KindOfRegion(const std::vector<std::string>& ops) {
 std::vector<int64_t> ParseIntsAttr(const std::string& s) {
   // "array<i64: 1, 768>" or "[1,2]" or "dense<[[0, 1]]> " -> integers
   std::vector<int64_t> out;
+  if (s.rfind("dense<\"0x", 0) == 0) {
+    // hex form (how MLIR prints, and the bytecode reader writes, dense integer data): the integer
+    // attributes read here (replica_groups) are i64, little-endian
+    size_t end = s.find('"', 9);
+    std::string hex = s.substr(9, end == std::string::npos ? std::string::npos : end - 9);
+    if (hex.size() % 16) throw ParseError{"dense integer attribute is not i64: " + s};
+    for (size_t k = 0; k < hex.size(); k += 16) {
+      uint64_t v = 0;
+      for (int b = 7; b >= 0; --b) v = (v << 8) | std::stoul(hex.substr(k + 2 * b, 2), nullptr, 16);
+      out.push_back((int64_t)v);
+    }
+    return out;
+  }
   size_t start = s.find(':');
   if (s.rfind("array<", 0) != 0) start = 0;
+  else if (start == std::string::npos) return out;   // "array<i64>": empty
   std::string cur;
   for (size_t k = (start == std::string::npos ? 0 : start + (s.rfind("array<", 0) == 0 ? 1 : 0)); k < s.size(); ++k) {
     char c = s[k];
@@ -756,9 +850,15 @@ void ParseDimNumbers(const std::string& s, const std::string& prefix, Op* op) {
     key.erase(0, key.find_first_not_of(" ,"));
     key.erase(key.find_last_not_of(' ') + 1);
     size_t v0 = body.find_first_not_of(' ', eq + 1);
+    if (v0 == std::string::npos) throw ParseError{"malformed dimension numbers: " + s};
     size_t v1;
-    if (body[v0] == '[') v1 = body.find(']', v0) + 1;
-    else v1 = body.find(',', v0);
+    if (body[v0] == '[') {
+      v1 = body.find(']', v0);
+      if (v1 == std::string::npos) throw ParseError{"malformed dimension numbers: " + s};
+      ++v1;
+    } else {
+      v1 = body.find(',', v0);
+    }
     if (v1 == std::string::npos) v1 = body.size();
     op->ints[prefix + key] = ParseIntsAttr(body.substr(v0, v1 - v0));
     k = v1;
@@ -843,7 +943,55 @@ class Builder {
 
 }  // namespace
 
+std::string DumpGraph(const Graph& g) {
+  std::ostringstream o;
+  o << "graph partitions=" << g.num_partitions << " replicas=" << g.num_replicas << " args:";
+  for (const Value* v : g.args) o << " %" << v->id << ":" << v->type.str();
+  o << "\n";
+  static const char* kStrKeys[] = {"comparison_direction", "compare_type", "call_target_name", "mhlo.sharding", "region_compare"};
+  for (const auto& op : g.ops) {
+    for (size_t k = 0; k < op->results.size(); ++k) o << (k ? ", " : "") << "%" << op->results[k]->id;
+    o << " = " << op->name << "(";
+    for (size_t k = 0; k < op->operands.size(); ++k) o << (k ? ", " : "") << "%" << op->operands[k]->id;
+    o << ") ->";
+    for (const Value* v : op->results) o << " " << v->type.str();
+    for (const auto& kv : op->ints) {
+      o << " " << kv.first << "=[";
+      for (size_t k = 0; k < kv.second.size(); ++k) o << (k ? "," : "") << kv.second[k];
+      o << "]";
+    }
+    for (const char* key : kStrKeys) {
+      auto it = op->strs.find(key);
+      if (it != op->strs.end()) o << " " << key << "=" << it->second;
+    }
+    if (op->reduce != ReduceKind::kNone) o << " reduce=" << (int)op->reduce;
+    if (op->name == "constant") {
+      uint64_t h = 1469598103934665603ull;
+      for (uint8_t b : op->data) h = (h ^ b) * 1099511628211ull;
+      o << " splat=" << op->splat << " bytes=" << op->data.size() << " fnv=" << std::hex << h << std::dec;
+    }
+    o << "\n";
+  }
+  o << "outputs:";
+  for (const Value* v : g.outputs) o << " %" << v->id;
+  o << "\n";
+  return o.str();
+}
+
 std::string ParseModule(const char* text, size_t size, Graph* g) {
+  std::string decoded;
+  if (IsMlirBytecode(text, size)) {
+    std::string err = MlirBytecodeToText(text, size, &decoded);
+    if (!err.empty()) return err;
+    if (const char* dump = std::getenv("B200_DUMP_BYTECODE_TEXT")) {
+      if (FILE* f = std::fopen(dump, "w")) {
+        std::fwrite(decoded.data(), 1, decoded.size(), f);
+        std::fclose(f);
+      }
+    }
+    text = decoded.data();
+    size = decoded.size();
+  }
   try {
     Lexer lx;
     if (!lx.Run(text, size)) return "lex error: " + lx.err;

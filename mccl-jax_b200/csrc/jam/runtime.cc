@@ -652,7 +652,12 @@ extern "C" int b200_compile_report(const char* text, size_t size, int num_proces
   b200::CompileOptions opt;
   opt.num_processes = num_processes;
   opt.fuse_attention = std::getenv("B200_NO_FLASH") == nullptr;
-  if (nvrtc) {
+  if (nvrtc == 2) {
+    b200::Graph g;
+    std::string err = b200::ParseModule(text, size, &g);
+    if (!err.empty()) { report = "error: " + err; rc = 1; }
+    else report = b200::DumpGraph(g);
+  } else if (nvrtc) {
     std::unique_ptr<b200::Executable> ex;
     std::string err = b200::Executable::Build(text, size, opt, &ex);
     if (!err.empty()) { report = "error: " + err; rc = 1; }

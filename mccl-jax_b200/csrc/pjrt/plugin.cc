@@ -919,9 +919,6 @@ PJRT_Error* ClientCompile(PJRT_Client_Compile_Args* a) {
       std::fclose(f);
     }
   }
-  if (p->code_size >= 4 && std::memcmp(p->code, "ML\xefR", 4) == 0)
-    return Err(PJRT_Error_Code_INVALID_ARGUMENT,
-               "jam compile: MLIR bytecode (VHLO portable artifact) input is not supported yet; pass StableHLO MLIR text");
   b200::CompileOptions opt;
   opt.num_processes = a->client->num_processes;
   opt.fuse_attention = std::getenv("B200_NO_FLASH") == nullptr;

@@ -358,8 +358,9 @@ class Client:
         a = self.api.call("DeviceDescription_Kind", DescStrArgs(description=d))
         return C.string_at(a.s, a.n).decode()
 
-    def compile(self, text: str) -> Executable:
-        code = text.encode()
+    def compile(self, program) -> Executable:
+        """`program`: StableHLO as MLIR text (str) or MLIR bytecode (bytes); format "mlir" covers both."""
+        code = program.encode() if isinstance(program, str) else bytes(program)
         buf = C.create_string_buffer(code, len(code))
         prog = Program(code=C.addressof(buf), code_size=len(code), format=b"mlir", format_size=4)
         prog.struct_size = C.sizeof(prog)
@@ -376,7 +377,7 @@ class Client:
         return Buffer(self, a.buffer)
 
     def run(self, text_or_exe, inputs: Sequence[np.ndarray]) -> List[np.ndarray]:
-        exe = self.compile(text_or_exe) if isinstance(text_or_exe, str) else text_or_exe
+        exe = self.compile(text_or_exe) if isinstance(text_or_exe, (str, bytes)) else text_or_exe
         bufs, outs = [], []
         try:
             bufs = [self.buffer_from_host(x) for x in inputs]

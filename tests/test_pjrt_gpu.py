@@ -83,6 +83,24 @@ def test_mlp_step_config1_vs_oracle(client):
         assert_close(o, r, RTOL_F32, f"mlp out{i}")
 
 
+@pytest.mark.parametrize("version", [6, 0])
+def test_mlp_step_from_mlir_bytecode_vs_oracle(client, version):
+    """The same MLP step given as MLIR bytecode (written by an MLIR 20 writer,
+    tests/golden/make_bytecode.py) runs to the oracle's results on the fixture's text."""
+    fx = os.path.join(G, "bytecode")
+    with open(os.path.join(fx, f"mlp_step.v{version}.mlirbc"), "rb") as f:
+        data = f.read()
+    with open(os.path.join(fx, "mlp_step.mlir")) as f:
+        text = f.read()
+    p = configs.mlp_program()
+    assert p.text == text
+    outs = client.run(data, p.inputs)
+    refs = oracle_run(text, p.inputs)
+    assert len(outs) == len(refs)
+    for i, (o, r) in enumerate(zip(outs, refs)):
+        assert_close(o, r, RTOL_F32, f"mlp (bytecode v{version}) out{i}")
+
+
 @pytest.mark.parametrize("dtype,M,N,K,batch", [("bf16", 1024, 1024, 1024, 0), ("f32", 256, 192, 320, 0),
                                                ("bf16", 256, 256, 256, 4), ("bf16", 96, 80, 64, 0)])
 def test_gemm_vs_oracle(client, dtype, M, N, K, batch):
