@@ -41,10 +41,15 @@ const std::unordered_set<std::string> kBinary = {
 const std::unordered_set<std::string> kUnary = {
     "negate", "exponential", "exponential_minus_one", "log", "log_plus_one", "tanh", "sqrt",
     "rsqrt", "cbrt", "abs", "sine", "cosine", "tan", "floor", "ceil", "sign", "round_nearest_even",
-    "round_nearest_afz", "logistic", "not", "is_finite", "popcnt"};
+    "round_nearest_afz", "logistic", "not", "is_finite", "popcnt", "count_leading_zeros", "erf",
+    "reduce_precision"};
 const std::unordered_set<std::string> kIndexMap = {
     "broadcast_in_dim", "reshape", "transpose", "slice", "concatenate", "pad", "iota",
-    "constant", "convert", "bitcast_convert", "gather", "reverse"};
+    "constant", "convert", "bitcast_convert", "gather", "reverse", "dynamic_slice", "dynamic_update_slice"};
+// index maps whose operand index depends on runtime data (an index tensor or scalar offsets)
+bool DataDependentIndex(const Op* op) {
+  return op->name == "gather" || op->name == "dynamic_slice" || op->name == "dynamic_update_slice";
+}
 const std::unordered_set<std::string> kAliasCustom = {"Sharding", "SPMDFullToShardShape", "SPMDShardToFullShape"};
 
 bool IsElementwise(const Op* op) {
@@ -72,6 +77,23 @@ std::string CType(DT t) {   // register ("compute") type
     default: return "void";
   }
 }
+int DTBits(DT t) { return 8 * DTBytes(t); }
+// all-ones mask of an integer type's width, as an unsigned long long literal
+std::string WidthMask(DT t) {
+  int w = DTBits(t);
+  return w >= 64 ? std::string("0xffffffffffffffffULL") : std::to_string((1ULL << w) - 1) + "ULL";
+}
+// unsigned / signed C types of an integer type's width
+std::string UType(DT t) { return DTBytes(t) == 8 ? "unsigned long long" : "unsigned"; }
+std::string SType(DT t) {
+  switch (DTBytes(t)) {
+    case 1: return "signed char";
+    case 2: return "short";
+    case 4: return "int";
+    default: return "long long";
+  }
+}
+
 std::string MemType(DT t) {  // storage type
   switch (t) {
     case DT::kPred: return "unsigned char";
@@ -511,7 +533,7 @@ struct Gen {
       return opnd(0, j);
     }
     if (n == "reverse") {
-      const auto& dims = op->ints.at("dimensions");
+      const auto& dims = op->ints.count("dims") ? op->ints.at("dims") : op->ints.at("dimensions");
       std::vector<std::string> j = idx;
       for (int64_t d : dims) j[d] = "(" + std::to_string(ty.dims[d] - 1) + "-(" + idx[d] + "))";
       return opnd(0, j);
@@ -526,6 +548,77 @@ struct Gen {
       if (!idx.empty() && sd.back() == 1 && LaneInfo(idx.back(), &li) && li.exact)
         j.back() = DeriveLane("(" + std::to_string(st.back()) + "+(" + li.base + ")*1)", li.lane, li.al4 && st.back() % 4 == 0);
       return opnd(0, j);
+    }
+    if (n == "bitcast_convert") {
+      // same-width reinterpretation of the bits (a 16-bit float register holds an exactly
+      // representable value, so its bits are a shift / exact conversion away)
+      DT from = op->operands[0]->type.dt, to = ty.dt;
+      if (DTBytes(from) != DTBytes(to) || from == DT::kPred || to == DT::kPred || op->operands[0]->type.dims != ty.dims)
+        throw LowerError{std::string("bitcast_convert from ") + DTName(from) + " to " + DTName(to) +
+                         " is not supported (only between element types of the same width)"};
+      std::string x = opnd(0, idx), b;
+      if (from == DT::kF32) b = "(unsigned long long)__float_as_uint(" + x + ")";
+      else if (from == DT::kBF16) b = "(unsigned long long)(__float_as_uint(" + x + ") >> 16)";
+      else if (from == DT::kF16) b = "(unsigned long long)f2h(" + x + ")";
+      else if (from == DT::kF64) b = "(unsigned long long)__double_as_longlong(" + x + ")";
+      else b = "((unsigned long long)(" + x + ") & " + WidthMask(from) + ")";
+      b = Var(DT::kU64, b);
+      std::string e;
+      if (to == DT::kF32) e = "__uint_as_float((unsigned)" + b + ")";
+      else if (to == DT::kBF16) e = "__uint_as_float((unsigned)" + b + " << 16)";
+      else if (to == DT::kF16) e = "h2f((unsigned short)" + b + ")";
+      else if (to == DT::kF64) e = "__longlong_as_double((long long)" + b + ")";
+      else if (DTIsSigned(to)) e = "(" + CType(to) + ")(" + SType(to) + ")" + b;
+      else e = "(" + CType(to) + ")(" + MemType(to) + ")" + b;
+      return Var(to, e);
+    }
+    if (n == "dynamic_slice" || n == "dynamic_update_slice") {
+      // start offsets are runtime scalars, clamped so the window stays inside the operand (the
+      // StableHLO rule): start_k = clamp(start_k, 0, dim_k - window_k)
+      const bool upd = n == "dynamic_update_slice";
+      const auto& in = op->operands[0]->type.dims;
+      const size_t first = upd ? 2 : 1;
+      if (op->operands.size() != first + in.size()) throw LowerError{n + ": expected one scalar start index per dimension"};
+      std::vector<int64_t> win(in.size());
+      for (size_t k = 0; k < in.size(); ++k) {
+        if (upd) win[k] = op->operands[1]->type.dims[k];
+        else win[k] = op->ints.count("sizes") ? op->ints.at("sizes")[k] : ty.dims[k];
+      }
+      std::vector<std::string> st(in.size());
+      for (size_t k = 0; k < in.size(); ++k) {
+        if (!op->operands[first + k]->type.dims.empty()) throw LowerError{n + ": start indices must be scalars"};
+        std::string sv = Emit(op->operands[first + k], {});
+        st[k] = Var(DT::kS64, "imin(imax((long long)(" + sv + "), 0LL), " + std::to_string(in[k] - win[k]) + "LL)");
+      }
+      if (!upd) {
+        std::vector<std::string> j(idx.size());
+        for (size_t k = 0; k < idx.size(); ++k) j[k] = "(" + st[k] + "+(" + idx[k] + "))";
+        return opnd(0, j);
+      }
+      std::string r = "t" + std::to_string(tmp++);
+      body << indent << CType(ty.dt) << " " << r << ";\n";
+      std::string cond = "true";
+      std::vector<std::string> j(idx.size());
+      for (size_t k = 0; k < idx.size(); ++k) {
+        j[k] = "((" + idx[k] + ")-" + st[k] + ")";
+        cond += " && " + j[k] + " >= 0 && " + j[k] + " < " + std::to_string(win[k]) + "LL";
+      }
+      std::string save = indent;
+      for (int side = 0; side < 2; ++side) {
+        body << save << (side == 0 ? "if (" + cond + ") {\n" : std::string("} else {\n"));
+        indent = save + "  ";
+        auto saved = cse;
+        auto saved_r = reindex_cse;
+        ++branch_depth;
+        std::string x = side == 0 ? Emit(op->operands[1], j) : opnd(0, idx);
+        --branch_depth;
+        cse = saved;
+        reindex_cse = saved_r;
+        body << indent << r << " = " << x << ";\n";
+      }
+      indent = save;
+      body << indent << "}\n";
+      return r;
     }
     if (n == "convert") {
       DT from = op->operands[0]->type.dt, to = ty.dt;
@@ -703,7 +796,31 @@ struct Gen {
       else if (n == "not") e = t == DT::kPred ? "!" + x : "~" + x;
       else if (n == "is_finite") e = "isfinite(" + opnd(0, idx) + ")";
       else if (n == "sign") e = d ? "(double)((" + x + " > 0) - (" + x + " < 0))" : f ? "fsign(" + x + ")" : "((" + x + " > 0) - (" + x + " < 0))";
-      else if (n == "popcnt") e = "__popc(" + x + ")";
+      else if (n == "popcnt" || n == "count_leading_zeros") {
+        if (f || t == DT::kPred) throw LowerError{"unsupported op '" + n + "' for " + DTName(t)};
+        // counted over the type's own width (8- / 16-bit values sit sign-extended in registers)
+        const int w = DTBits(t);
+        std::string u = "((unsigned long long)(" + x + ") & " + WidthMask(t) + ")";
+        if (n == "popcnt") e = w == 64 ? "__popcll(" + u + ")" : "__popc((unsigned)" + u + ")";
+        else e = w == 64 ? "__clzll((long long)" + u + ")" : "(__clz((int)(unsigned)" + u + ") - " + std::to_string(32 - w) + ")";
+        e = "(" + CType(t) + ")(" + e + ")";
+      } else if (n == "erf") {
+        if (!f) throw LowerError{std::string("erf of ") + DTName(t) + " is not supported"};
+        e = (d ? "erf(" : "erff(") + x + ")";
+      } else if (n == "reduce_precision") {
+        // the formats of the 16-bit float types (as the reference lowers them, a cast to bf16 / f16
+        // and back) and formats at least as wide as the operand's own (no change)
+        const int eb = (int)op->ints.at("exponent_bits")[0], mb = (int)op->ints.at("mantissa_bits")[0];
+        const int own_e = t == DT::kF64 ? 11 : t == DT::kF32 || t == DT::kBF16 ? 8 : 5;
+        const int own_m = t == DT::kF64 ? 52 : t == DT::kF32 ? 23 : t == DT::kBF16 ? 7 : 10;
+        if (!f) throw LowerError{std::string("reduce_precision of ") + DTName(t)};
+        if (eb >= own_e && mb >= own_m) e = x;
+        else if (eb == 8 && mb == 7 && t != DT::kF64) e = t == DT::kF16 ? "rhf(rbf(" + x + "))" : "rbf(" + x + ")";
+        else if (eb == 5 && mb == 10 && t != DT::kF64) e = t == DT::kBF16 ? "rbf(rhf(" + x + "))" : "rhf(" + x + ")";
+        else
+          throw LowerError{"reduce_precision to e" + std::to_string(eb) + "m" + std::to_string(mb) + " of " + DTName(t) +
+                           " is not supported (e8m7, e5m10 and formats at least as wide as the operand are)"};
+      }
       else {
         static const std::map<std::string, std::pair<std::string, std::string>> fn = {
             {"exponential", {"expf", "exp"}}, {"exponential_minus_one", {"expm1f", "expm1"}},
@@ -746,9 +863,22 @@ struct Gen {
       else if (n == "and") e = t == DT::kPred ? a + " && " + b : a + " & " + b;
       else if (n == "or") e = t == DT::kPred ? a + " || " + b : a + " | " + b;
       else if (n == "xor") e = t == DT::kPred ? a + " != " + b : a + " ^ " + b;
-      else if (n == "shift_left") e = a + " << " + b;
-      else if (n == "shift_right_logical") e = "(" + CType(t) + ")((unsigned" + std::string(DTBytes(t) == 8 ? " long long" : "") + ")" + a + " >> " + b + ")";
-      else if (n == "shift_right_arithmetic") e = a + " >> " + b;
+      else if (n == "shift_left" || n == "shift_right_logical" || n == "shift_right_arithmetic") {
+        // a shift by at least the type's width (the amount read as unsigned) gives 0, or the sign
+        // fill for the arithmetic right shift; 8- / 16-bit values sit sign-extended in registers
+        if (f || t == DT::kPred) throw LowerError{"unsupported op '" + n + "' for " + DTName(t)};
+        const std::string W = std::to_string(DTBits(t));
+        const std::string amt = "((unsigned long long)(" + b + ") & " + WidthMask(t) + ")";
+        const std::string ua = "(((unsigned long long)(" + a + ")) & " + WidthMask(t) + ")";
+        if (n == "shift_left")
+          e = "(" + amt + " >= " + W + " ? (" + CType(t) + ")0 : (" + CType(t) + ")(" + SType(t) + ")(" + UType(t) + ")(" + ua + " << " + amt + "))";
+        else if (n == "shift_right_logical")
+          e = "(" + amt + " >= " + W + " ? (" + CType(t) + ")0 : (" + CType(t) + ")(" + SType(t) + ")(" + UType(t) + ")(" + ua + " >> " + amt + "))";
+        else
+          e = "(" + CType(t) + ")(" + (DTIsSigned(t) ? SType(t) : MemType(t)) + ")((long long)(" + SType(t) + ")(" + UType(t) + ")" + ua +
+              " >> (" + amt + " >= " + W + " ? " + std::to_string(DTBits(t) - 1) + "ULL : " + amt + "))";
+        if (DTIsUnsigned(t)) e = "(" + CType(t) + ")((unsigned long long)(" + e + ") & " + WidthMask(t) + ")";
+      }
       if (e.empty()) throw LowerError{"unsupported op '" + n + "' for " + DTName(t)};
       return Round(t, Var(t, e));
     }
@@ -831,10 +961,29 @@ class Lowerer {
  public:
   Lowerer(Graph& g, const CompileOptions& opt, Plan* p) : g_(g), opt_(opt), p_(p) {}
 
+  // partition_id / replica_id become constants: one process drives one device, so the id is this
+  // process's rank in the dimension the program is partitioned / replicated over, else 0 (the
+  // reference binds both to its rank, src/jam/ops/collectives.mm:16-29)
+  void RankConstants() {
+    for (auto& up : g_.ops) {
+      Op* op = up.get();
+      if (op->name != "partition_id" && op->name != "replica_id") continue;
+      const bool split = op->name == "partition_id" ? g_.num_partitions > 1 : g_.num_replicas > 1;
+      const uint64_t id = split ? (uint64_t)opt_.rank : 0;
+      const Value* r = op->result();
+      if (!r->type.dims.empty() || !DTIsUnsigned(r->type.dt) && !DTIsSigned(r->type.dt))
+        throw LowerError{op->name + " must give an integer scalar"};
+      op->name = "constant";
+      op->splat = true;
+      op->data.assign((const uint8_t*)&id, (const uint8_t*)&id + DTBytes(r->type.dt));
+    }
+  }
+
   void Run() {
     slot_of_.assign(g_.values.size(), -1);
     dead_.assign(g_.ops.size(), false);
     Retype();
+    RankConstants();
     if (opt_.fuse_attention) MatchAttention();
     // Two passes: the first decides with recomputation walking down to arguments and heavy results;
     // the second lets a value be recomputed from what the first pass stored (a LayerNorm's x - mean
@@ -940,7 +1089,7 @@ class Lowerer {
       bool ok = !r->users.empty();
       for (const Op* u : r->users) {
         if (dead_[u->index]) continue;
-        const bool gen = (IsElementwise(u) && u->name != "reshape" && u->name != "bitcast_convert") ||
+        const bool gen = (IsElementwise(u) && u->name != "reshape" && u->name != "bitcast_convert" && !DataDependentIndex(u)) ||
                          (u->name == "reduce" && u->operands[0] == r && u->results.size() == 1);
         if (!gen) { ok = false; break; }
       }
@@ -997,7 +1146,7 @@ class Lowerer {
     if (v->users.empty()) return false;
     for (const Op* u : v->users) {
       if (dead_[u->index]) continue;
-      const bool gen = (IsElementwise(u) && u->name != "reshape" && u->name != "bitcast_convert" && u->name != "gather") ||
+      const bool gen = (IsElementwise(u) && u->name != "reshape" && u->name != "bitcast_convert" && !DataDependentIndex(u)) ||
                        (u->name == "reduce" && u->operands[0] == v && u->results.size() == 1);
       if (!gen) return false;
     }
@@ -1535,7 +1684,7 @@ class Lowerer {
       const Op* op = x->def;
       // with a first materialisation pass done, values it stored are read, not recomputed
       const bool stored = x != v && recompute_stop_ && (*recompute_stop_)[x->id];
-      const bool leaf = stored || !op || !IsElementwise(op) || op->name == "gather" || (op->name == "constant" && !op->splat);
+      const bool leaf = stored || !op || !IsElementwise(op) || DataDependentIndex(op) || (op->name == "constant" && !op->splat);
       if (leaf || (op->name == "constant") || op->name == "iota") {
         if (!stored && op && (op->name == "constant" || op->name == "iota")) continue;
         if (x->type.numel() * 16 > n) big.insert(x->id);
@@ -1752,7 +1901,6 @@ class Lowerer {
       if (n == "scatter") { flush(); EmitScatter(op); continue; }
       if (n == "all_reduce" || n == "all_gather" || n == "reduce_scatter") { flush(); EmitCollective(op); continue; }
       if (n == "custom_call") throw LowerError{"unsupported custom_call @" + op->strs["call_target_name"]};
-      if (n == "partition_id" || n == "replica_id") throw LowerError{"unsupported op '" + n + "'"};
       if (!IsElementwise(op)) throw LowerError{"unsupported op '" + n + "'"};
       if (n == "gather") CheckGather(op);
       if (!need_[r->id]) continue;

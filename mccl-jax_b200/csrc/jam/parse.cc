@@ -417,6 +417,11 @@ class Parser {
       return;
     }
     TensorType t = Type(Next());
+    if (Accept("->")) {        // `: T -> U`, as chlo's unary ops print
+      op.in_types.assign(n_operands, t);
+      op.out_types.push_back(Type(Next()));
+      return;
+    }
     op.out_types.push_back(t);
     op.in_types.assign(n_operands, t);
   }
@@ -650,6 +655,13 @@ class Parser {
       ints_of("broadcast_dimensions", "dims");
     } else if (n == "stablehlo.transpose") {
       ints_of("permutation", "dims");
+    } else if (n == "stablehlo.reverse") {
+      ints_of("dimensions", "dims");
+    } else if (n == "stablehlo.dynamic_slice") {
+      ints_of("slice_sizes", "sizes");
+    } else if (n == "stablehlo.reduce_precision") {
+      ints_of("exponent_bits", "exponent_bits");
+      ints_of("mantissa_bits", "mantissa_bits");
     } else if (n == "stablehlo.iota") {
       ints_of("iota_dimension", "dim");
     } else if (n == "stablehlo.concatenate") {
@@ -911,8 +923,16 @@ class Builder {
         for (size_t k = 0; k < rets.size(); ++k) env[a.results[k]] = rets[k];
         continue;
       }
-      if (a.name.rfind("stablehlo.", 0) != 0) throw ParseError{"unsupported op '" + a.name + "'"};
-      Op* op = g_->NewOp(a.name.substr(10));
+      std::string opname;
+      if (a.name == "chlo.erf") opname = "erf";
+      else if (a.name.rfind("stablehlo.", 0) == 0) opname = a.name.substr(10);
+      else throw ParseError{"unsupported op '" + a.name + "'"};
+      {
+        // custom_call @mhlo.erf carries chlo.erf through a pipeline without the chlo dialect
+        auto t = a.strs.find("call_target_name");
+        if (opname == "custom_call" && t != a.strs.end() && t->second == "mhlo.erf") opname = "erf";
+      }
+      Op* op = g_->NewOp(opname);
       for (auto& n : a.operands) op->operands.push_back(lookup(n));
       op->ints = a.ints;
       op->strs = a.strs;
@@ -925,6 +945,14 @@ class Builder {
         env[a.results[k]] = v;
       }
       if (!a.region_ops.empty()) op->reduce = KindOfRegion(a.region_ops);
+      if (op->name == "reduce_precision" && op->strs.count("format")) {
+        // pretty form: format = e5m10
+        const std::string& f = op->strs["format"];
+        size_t m = f.find('m');
+        if (f.size() < 4 || f[0] != 'e' || m == std::string::npos) throw ParseError{"bad reduce_precision format " + f};
+        op->ints["exponent_bits"] = {std::stoll(f.substr(1, m - 1))};
+        op->ints["mantissa_bits"] = {std::stoll(f.substr(m + 1))};
+      }
       if (op->name == "constant") ParseDense(a.dense, op->result()->type, op);
       if (op->name == "gather") {
         ParseDimNumbers(op->strs["dimension_numbers"], "", op);

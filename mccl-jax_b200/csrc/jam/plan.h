@@ -122,6 +122,7 @@ struct Plan {
 
 struct CompileOptions {
   int num_processes = 1;             // ranks in the communicator (1: collectives are identities)
+  int rank = 0;                      // this process's rank (the value of partition_id / replica_id)
   bool fuse_attention = true;        // B200_NO_FLASH=1 turns the attention pattern match off
 };
 

@@ -921,6 +921,7 @@ PJRT_Error* ClientCompile(PJRT_Client_Compile_Args* a) {
   }
   b200::CompileOptions opt;
   opt.num_processes = a->client->num_processes;
+  opt.rank = a->client->process_index;
   opt.fuse_attention = std::getenv("B200_NO_FLASH") == nullptr;
   std::unique_ptr<b200::Executable> ex;
   std::string err = b200::Executable::Build(p->code, p->code_size, opt, &ex);

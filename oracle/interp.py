@@ -152,6 +152,75 @@ UNARY = {
 }
 
 
+def _uview(x: np.ndarray) -> np.ndarray:
+    """The two's-complement bits of an integer array as uint64 (only the type's own width set)."""
+    return x.view(np.dtype("u%d" % x.dtype.itemsize)).astype(np.uint64)
+
+
+def _from_bits(u: np.ndarray, dt: np.dtype) -> np.ndarray:
+    return u.astype(np.dtype("u%d" % dt.itemsize)).view(dt)
+
+
+def _popcnt(x):
+    """Set bits in each element's own width (StableHLO popcnt)."""
+    b = np.unpackbits(np.ascontiguousarray(x).view(np.uint8).reshape(-1, x.dtype.itemsize), axis=1)
+    return b.sum(axis=1).reshape(x.shape).astype(x.dtype)
+
+
+def _clz(x):
+    """Leading zero bits in each element's own width; clz(0) = width (StableHLO count_leading_zeros)."""
+    v = _uview(x)
+    bl = np.zeros(v.shape, np.int64)
+    for sh in (32, 16, 8, 4, 2, 1):
+        m = v >= (np.uint64(1) << np.uint64(sh))
+        bl += m * sh
+        v = np.where(m, v >> np.uint64(sh), v)
+    bl += (v > 0)
+    return (8 * x.dtype.itemsize - bl).astype(x.dtype)
+
+
+def _shift(name, x, y):
+    """StableHLO shifts: the amount is read as unsigned; an amount >= the width gives 0 (the sign
+    fill for the arithmetic right shift)."""
+    w = 8 * x.dtype.itemsize
+    mask = np.uint64((1 << w) - 1) if w < 64 else np.uint64(0xFFFFFFFFFFFFFFFF)
+    ux, amt = _uview(x), _uview(y)
+    big = amt >= np.uint64(w)
+    a = np.where(big, np.uint64(w - 1), amt)
+    if name == "stablehlo.shift_left":
+        r = np.where(big, np.uint64(0), (ux << a) & mask)
+    elif name == "stablehlo.shift_right_logical":
+        r = np.where(big, np.uint64(0), ux >> a)
+    else:
+        sx = x.view(np.dtype("i%d" % x.dtype.itemsize)).astype(np.int64)
+        r = (sx >> a.astype(np.int64)).astype(np.uint64) & mask
+    return _from_bits(r, x.dtype)
+
+
+def _reduce_precision(x, fmt, out_dtype):
+    """reduce_precision to `eXmY`: the 16-bit float formats (round to bf16 / f16 and back, as the
+    reference lowers it, src/jam/ops/hard_limit.mm:38-52) and formats at least as wide as the
+    operand's own."""
+    m = re.fullmatch(r"e(\d+)m(\d+)", fmt)
+    eb, mb = int(m.group(1)), int(m.group(2))
+    own = {"f64": (11, 52), "f32": (8, 23), "bf16": (8, 7), "f16": (5, 10)}[out_dtype]
+    if eb >= own[0] and mb >= own[1]:
+        return x
+    h = _hi(x).astype(np.float32)
+    if (eb, mb) == (8, 7):
+        h = h.astype(ml_dtypes.bfloat16).astype(np.float32)
+    elif (eb, mb) == (5, 10):
+        with np.errstate(over="ignore"):
+            h = h.astype(np.float16).astype(np.float32)
+    else:
+        raise NotImplementedError(f"reduce_precision {fmt}")
+    return _cast(h, out_dtype)
+
+
+def _dyn_starts(starts, dims, window):
+    return [int(min(max(int(np.asarray(s).reshape(())), 0), d - w)) for s, d, w in zip(starts, dims, window)]
+
+
 def _reducer_kind(block: Block) -> str:
     for op in block.ops:
         for k in ("add", "maximum", "minimum", "multiply", "and", "or"):
@@ -310,6 +379,29 @@ class Interp:
             with np.errstate(all="ignore"):
                 r = UNARY[n](_hi(ins[0]))
             return [_cast(np.asarray(r), ot.dtype)]
+        if n in ("stablehlo.shift_left", "stablehlo.shift_right_logical", "stablehlo.shift_right_arithmetic"):
+            return [_shift(n, ins[0], ins[1])]
+        if n == "stablehlo.popcnt":
+            return [_popcnt(ins[0])]
+        if n == "stablehlo.count_leading_zeros":
+            return [_clz(ins[0])]
+        if n in ("chlo.erf", "stablehlo.erf") or (n == "stablehlo.custom_call" and a.get("call_target_name") == "mhlo.erf"):
+            r = np.vectorize(math.erf, otypes=[np.float64])(_hi(ins[0]).astype(np.float64))
+            return [_cast(r, ot.dtype)]
+        if n == "stablehlo.reduce_precision":
+            return [_reduce_precision(ins[0], a["format"], ot.dtype)]
+        if n == "stablehlo.reverse":
+            return [np.flip(ins[0], axis=tuple(a["dims"])).copy()]
+        if n == "stablehlo.dynamic_slice":
+            x = ins[0]
+            st = _dyn_starts(ins[1:], x.shape, a["sizes"])
+            return [x[tuple(slice(s0, s0 + w) for s0, w in zip(st, a["sizes"]))].copy()]
+        if n == "stablehlo.dynamic_update_slice":
+            x, u = ins[0], ins[1]
+            st = _dyn_starts(ins[2:], x.shape, u.shape)
+            r = x.copy()
+            r[tuple(slice(s0, s0 + w) for s0, w in zip(st, u.shape))] = u
+            return [r]
         if n == "stablehlo.not":
             x = ins[0]
             return [np.logical_not(x) if x.dtype == np.bool_ else np.invert(x)]

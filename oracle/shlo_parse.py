@@ -314,6 +314,8 @@ class Parser:
             self.expect("->")
             return ins, self.result_types()
         ty = parse_type(self.next())
+        if self.accept("->"):                    # `: T -> U`, as chlo's unary ops print
+            return [ty], [parse_type(self.next())]
         return None, [ty]
 
     def result_types(self):

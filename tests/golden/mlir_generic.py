@@ -9,7 +9,7 @@ The attribute names and spellings are StableHLO's own (its op definitions and th
 broadcast_dimensions, permutation, iota_dimension, dimension, dimensions, start_indices /
 limit_indices / strides, edge_padding_low / edge_padding_high / interior_padding,
 #stablehlo<comparison_direction ..>, #stablehlo<comparison_type ..>, #stablehlo.dot<...>,
-call_target_name, value.
+call_target_name, value, dimensions (reverse), slice_sizes, exponent_bits / mantissa_bits.
 
 The tests use it twice: the plugin's parser must give the same plan for both forms, and
 `make_bytecode.py` feeds the generic form to an MLIR bytecode writer to make the bytecode fixtures.
@@ -73,6 +73,9 @@ def _op(res: str, name: str, operands: List[str], attrs: dict, ty: str) -> str:
 def convert_line(line: str) -> str:
     ind = line[: len(line) - len(line.lstrip())]
     s = line.strip()
+    cm = re.match(_RES + r"chlo\.(?P<name>\w+)\s+(?P<x>%[\w.#]+)\s*:\s*(?P<a>tensor<[^>]*>)\s*->\s*(?P<b>tensor<[^>]*>)$", s)
+    if cm:   # chlo unary ops print as `chlo.erf %x : T -> U`
+        return f'{ind}{cm.group("res")} = "chlo.{cm.group("name")}"({cm.group("x")}) : ({cm.group("a")}) -> {cm.group("b")}'
     m = re.match(_RES + r"stablehlo\.(?P<name>\w+)\s*(?P<rest>.*)$", s)
     if not m:
         m2 = re.match(r"stablehlo\.return\s+(?P<ops>[^:]*):\s*(?P<tys>.*)$", s)
@@ -81,6 +84,7 @@ def convert_line(line: str) -> str:
             return f'{ind}"stablehlo.return"({", ".join(ops)}) : ({m2.group("tys").strip()}) -> ()'
         return line
     res, name, rest = m.group("res"), m.group("name"), m.group("rest")
+    rest = " " + rest
     body, ty = rest.rsplit(" : ", 1) if " : " in rest else (rest, "")
     parts = _split_top(body)
     operands = [p for p in parts if p.startswith("%")]
@@ -109,6 +113,14 @@ def convert_line(line: str) -> str:
         return ind + _op(res, name, operands, {"broadcast_dimensions": _arr(kv["dims"])}, ty)
     if name == "transpose":
         return ind + _op(res, name, operands, {"permutation": _arr(kv["dims"])}, ty)
+    if name == "reverse":
+        return ind + _op(res, name, operands, {"dimensions": _arr(kv["dims"])}, _fn_type(ty, 1))
+    if name == "dynamic_slice":
+        return ind + _op(res, name, operands, {"slice_sizes": _arr(kv["sizes"])}, ty)
+    if name == "reduce_precision":
+        fm = re.fullmatch(r"e(\d+)m(\d+)", kv["format"])
+        at = {"exponent_bits": f"{fm.group(1)} : i32", "mantissa_bits": f"{fm.group(2)} : i32"}
+        return ind + _op(res, name, operands, at, _fn_type(ty, 1))
     if name == "concatenate":
         return ind + _op(res, name, operands, {"dimension": f"{kv['dim']} : i64"}, ty)
     if name == "pad":
