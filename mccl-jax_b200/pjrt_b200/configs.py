@@ -146,17 +146,19 @@ def gpt2_param_shapes(layers, d, heads, mlp, vocab, seq):
 
 
 def gpt2_program(layers=12, d=768, heads=12, mlp=3072, vocab=50257, seq=1024, batch=8, world=1,
-                 lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1, seed=0, rank=0, with_inputs=True):
+                 lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1, seed=0, rank=0, with_inputs=True, dtype="bf16"):
     """One data-parallel AdamW step of a GPT-2-style decoder (pre-LN, GELU(tanh) MLP, tied LM head).
 
     Params bf16 (replicated), AdamW moments f32; the batch [world*batch, seq] of token ids is sharded
     over ranks with shard_map (SPMDFullToShardShape); gradients are psum'd (all_reduce) and divided by
     the world size (pmean), as temp/dp_train.py:80-83 does.  Adam bias corrections come in as host
     scalars (dp_train.py:74-76).  Returns (new params..., new m..., new v..., pmean loss).
+    `dtype` is the parameter / activation type (bf16, the config's; "f32" gives the same program
+    without the 16-bit roundings, which tests compare with an independent autograd implementation).
     """
     b = Builder("jit_gpt2_dp_step", num_partitions=world)
     shapes = gpt2_param_shapes(layers, d, heads, mlp, vocab, seq)
-    P = {n: b.arg(s, "bf16") for n, s in shapes}
+    P = {n: b.arg(s, dtype) for n, s in shapes}
     M = {n: b.arg(s, "f32") for n, s in shapes}
     V = {n: b.arg(s, "f32") for n, s in shapes}
     ids_full = b.arg((world * batch, seq), "i32")
@@ -176,16 +178,16 @@ def gpt2_program(layers=12, d=768, heads=12, mlp=3072, vocab=50257, seq=1024, ba
         inv = b.rsqrt(var + 1e-5)
         y = xc * b.broadcast_to(inv, xf.shape) * b.broadcast_to(b.convert(g, "f32"), xf.shape) \
             + b.broadcast_to(b.convert(bias, "f32"), xf.shape)
-        return b.convert(y, "bf16")
+        return b.convert(y, dtype)
 
     def linear(x2, w, bias):                       # x2 [ntok, din] bf16 -> [ntok, dout] bf16
-        y = b.dot_general(x2, w, contract=([1], [0]), out_dtype="bf16")
+        y = b.dot_general(x2, w, contract=([1], [0]), out_dtype=dtype)
         return y + b.broadcast_to(bias, y.shape)
 
     def gelu(x):                                   # tanh approximation, in f32
         xf = b.convert(x, "f32")
         inner = (xf + 0.044715 * (xf * xf * xf)) * math.sqrt(2.0 / math.pi)
-        return b.convert(0.5 * xf * (1.0 + b.tanh(inner)), "bf16")
+        return b.convert(0.5 * xf * (1.0 + b.tanh(inner)), dtype)
 
     x = b.take(P["wte"], ids) + b.broadcast_to(P["wpe"], (batch, seq, d))   # [B, S, d] bf16
     x = b.reshape(x, (ntok, d))
@@ -205,7 +207,7 @@ def gpt2_program(layers=12, d=768, heads=12, mlp=3072, vocab=50257, seq=1024, ba
         m = b.stop_gradient(b.max(s, 3, keepdims=True))
         e = b.exp(s - b.broadcast_to(m, s.shape))
         pr = e / b.broadcast_to(b.sum(e, 3, keepdims=True), s.shape)
-        o = b.dot_general(b.convert(pr, "bf16"), v, batch=([0, 1], [0, 1]), contract=([3], [2]), out_dtype="bf16")
+        o = b.dot_general(b.convert(pr, dtype), v, batch=([0, 1], [0, 1]), contract=([3], [2]), out_dtype=dtype)
         o = b.reshape(b.transpose(o, (0, 2, 1, 3)), (ntok, d))
         x = x + linear(o, p("w_proj"), p("b_proj"))
         h = layernorm(x, p("ln2_g"), p("ln2_b"))
@@ -234,14 +236,14 @@ def gpt2_program(layers=12, d=768, heads=12, mlp=3072, vocab=50257, seq=1024, ba
         vhat = v1 / b.broadcast_to(bc2, v1.shape)
         decay = wd if P[n].ndim == 2 else 0.0
         upd = mhat / (b.sqrt(vhat) + eps) + (decay * pf if decay else 0.0)
-        outs_p.append(b.convert(pf - lr * upd, "bf16"))
+        outs_p.append(b.convert(pf - lr * upd, dtype))
         outs_m.append(m1)
         outs_v.append(v1)
     lo = b.all_reduce(loss, world) * inv_world if world > 1 else loss
     text = b.text(outs_p + outs_m + outs_v + [lo])
     inputs = []
     if with_inputs:
-        inputs = gpt2_inputs(shapes, batch, seq, vocab, seed=seed, rank=rank)
+        inputs = gpt2_inputs(shapes, batch, seq, vocab, seed=seed, rank=rank, dtype=dtype)
     n_params = sum(int(np.prod(s)) for _, s in shapes)
     flops_per_token = 6 * (12 * layers * d * d + d * vocab) + 12 * layers * seq * d
     return Program(b.name, text, inputs, flops=float(flops_per_token) * ntok,
@@ -249,7 +251,7 @@ def gpt2_program(layers=12, d=768, heads=12, mlp=3072, vocab=50257, seq=1024, ba
                              vocab=vocab, seq=seq, batch=batch, world=world))
 
 
-def gpt2_inputs(shapes, batch, seq, vocab, seed=0, rank=0, step=1, b1=0.9, b2=0.95):
+def gpt2_inputs(shapes, batch, seq, vocab, seed=0, rank=0, step=1, b1=0.9, b2=0.95, dtype="bf16"):
     """Params ~N(0, 0.02) bf16 (LN gains 1, biases 0) from `seed` (same on every rank); zero moments;
     token ids / targets uniform in [0, vocab) from seed 1000 + rank (dp_train.py:50)."""
     rng = np.random.default_rng(seed)
@@ -261,7 +263,7 @@ def gpt2_inputs(shapes, batch, seq, vocab, seed=0, rank=0, step=1, b1=0.9, b2=0.
             a = np.zeros(s, np.float32)
         else:
             a = rng.standard_normal(s, dtype=np.float32) * 0.02
-        params.append(a.astype(BF16))
+        params.append(a.astype(np_dtype(dtype)))
         ms.append(np.zeros(s, np.float32))
         vs.append(np.zeros(s, np.float32))
     brng = np.random.default_rng(1000 + rank)

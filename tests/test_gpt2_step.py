@@ -34,6 +34,131 @@ def test_tiny_gpt_step_oracle_dp_equivalence():
             assert_close(np.asarray(a, np.float32), np.asarray(b, np.float32), RTOL_BF16, f"rank {r} out {i}")
 
 
+HP = dict(lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1)
+
+
+def torch_gpt_step(inputs, layers, d, heads, mlp, vocab, seq, lr, b1, b2, eps, wd, gelu_c=0.044715):
+    """The same train step written independently with torch autograd in float64: pre-LN decoder,
+    causal softmax attention, GELU(tanh) MLP, tied LM head, mean cross-entropy, AdamW with decay on
+    the 2-D parameters.  Returns (new params..., new m..., new v..., loss) like the program."""
+    import torch
+    shapes = configs.gpt2_param_shapes(layers, d, heads, mlp, vocab, seq)
+    n = len(shapes)
+    P = {nm: torch.tensor(np.asarray(inputs[i], np.float64), requires_grad=True) for i, (nm, _) in enumerate(shapes)}
+    ids = torch.tensor(np.asarray(inputs[3 * n], np.int64))
+    tgt = torch.tensor(np.asarray(inputs[3 * n + 1], np.int64))
+    bc1, bc2 = float(inputs[3 * n + 2]), float(inputs[3 * n + 3])
+    B, S = ids.shape
+    H, Dh = heads, d // heads
+
+    def ln(x, g, bias):
+        xc = x - x.mean(-1, keepdim=True)
+        return xc * torch.rsqrt((xc * xc).mean(-1, keepdim=True) + 1e-5) * g + bias
+
+    x = (P["wte"][ids] + P["wpe"][None]).reshape(B * S, d)
+    causal = torch.tril(torch.ones(S, S, dtype=torch.bool))
+    for l in range(layers):
+        w = lambda k: P[f"h{l}.{k}"]
+        qkv = ln(x, w("ln1_g"), w("ln1_b")) @ w("w_qkv") + w("b_qkv")
+        q, k, v = [qkv[:, i * d:(i + 1) * d].reshape(B, S, H, Dh).transpose(1, 2) for i in range(3)]
+        s = ((q @ k.transpose(-1, -2)) / np.sqrt(Dh)).masked_fill(~causal, float("-inf"))
+        o = (torch.softmax(s, -1) @ v).transpose(1, 2).reshape(B * S, d)
+        x = x + o @ w("w_proj") + w("b_proj")
+        f = ln(x, w("ln2_g"), w("ln2_b")) @ w("w_fc") + w("b_fc")
+        x = x + (0.5 * f * (1 + torch.tanh(np.sqrt(2 / np.pi) * (f + gelu_c * f ** 3)))) @ w("w_fc2") + w("b_fc2")
+    logits = ln(x, P["lnf_g"], P["lnf_b"]) @ P["wte"].T
+    loss = torch.nn.functional.cross_entropy(logits, tgt.reshape(-1))
+    loss.backward()
+    newp, newm, newv = [], [], []
+    for i, (nm, shp) in enumerate(shapes):
+        g, pv = P[nm].grad, P[nm].detach()
+        m1 = b1 * torch.tensor(np.asarray(inputs[n + i], np.float64)) + (1 - b1) * g
+        v1 = b2 * torch.tensor(np.asarray(inputs[2 * n + i], np.float64)) + (1 - b2) * g * g
+        decay = wd if len(shp) == 2 else 0.0
+        newp.append((pv - lr * ((m1 / bc1) / (torch.sqrt(v1 / bc2) + eps) + decay * pv)).numpy())
+        newm.append(m1.numpy())
+        newv.append(v1.numpy())
+    return newp + newm + newv + [loss.detach().numpy()]
+
+
+def _scaled_f32_inputs(batch, scale, world=1):
+    """Inputs of the f32 program with the weight matrices scaled up, so the attention softmax, GELU
+    and LayerNorm work away from their near-linear regime and a wrong term in any of them shows."""
+    p = configs.gpt2_program(batch=batch * world, dtype="f32", **TINY, **HP)
+    ins = list(p.inputs)
+    for i, (_, shp) in enumerate(configs.gpt2_param_shapes(**TINY)):
+        if len(shp) == 2:
+            ins[i] = ins[i] * np.float32(scale)
+    return ins
+
+
+def _normwise(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def _check_against_torch(outs, ref, ins, tol_grad):
+    n = len(configs.gpt2_param_shapes(**TINY))
+    assert abs(float(outs[-1]) - float(ref[-1])) <= 1e-6 * abs(float(ref[-1]))
+    for i in range(n):          # the moments carry the gradients: m1 = 0.1 g, v1 = 0.05 g^2
+        assert _normwise(outs[n + i], ref[n + i]) <= tol_grad, ("m", i)
+        assert _normwise(outs[2 * n + i], ref[2 * n + i]) <= 2 * tol_grad, ("v", i)
+    # the parameter update is AdamW applied to the program's own moments (elements whose gradient
+    # is near eps make a comparison with the torch parameters themselves noisy)
+    bc1, bc2 = float(ins[3 * n + 2]), float(ins[3 * n + 3])
+    for i, (_, shp) in enumerate(configs.gpt2_param_shapes(**TINY)):
+        p0 = np.asarray(ins[i], np.float64)
+        m1, v1 = np.asarray(outs[n + i], np.float64), np.asarray(outs[2 * n + i], np.float64)
+        decay = HP["wd"] if len(shp) == 2 else 0.0
+        exp = p0 - HP["lr"] * ((m1 / bc1) / (np.sqrt(v1 / bc2) + HP["eps"]) + decay * p0)
+        assert np.abs(np.asarray(outs[i], np.float64) - exp).max() <= 1e-6 * max(np.abs(p0).max(), 1.0), ("p", i)
+
+
+def test_tiny_gpt_f32_step_matches_independent_torch_autograd():
+    """The program the plugin runs (here its f32 form) is the GPT-2 train step: the oracle's loss,
+    gradients (through the AdamW moments) and update agree with a float64 torch autograd step."""
+    ins = _scaled_f32_inputs(batch=2, scale=10.0)
+    text = configs.gpt2_program(batch=2, dtype="f32", with_inputs=False, **TINY, **HP).text
+    _check_against_torch(oracle_run(text, ins), torch_gpt_step(ins, **TINY, **HP), ins, tol_grad=2e-5)
+
+
+def test_tiny_gpt_f32_dp_step_is_pmean_of_the_whole_batch():
+    """Two ranks with half batches each (shard_map + psum / 2) give the whole batch's torch step."""
+    ins = _scaled_f32_inputs(batch=2, scale=10.0, world=2)
+    text = configs.gpt2_program(batch=2, world=2, dtype="f32", with_inputs=False, **TINY, **HP).text
+    ref = torch_gpt_step(ins, **TINY, **HP)
+    ids, tgt = ins[-4], ins[-3]
+    shards = []
+    for r in range(2):
+        part = list(ins)
+        part[-4], part[-3] = ids[2 * r:2 * r + 2], tgt[2 * r:2 * r + 2]
+        shards.append(part)
+    for outs in run_spmd(text, shards):
+        _check_against_torch(outs, ref, ins, tol_grad=2e-5)
+
+
+def test_planted_mistake_in_the_torch_step_is_detected():
+    """Sensitivity of the check above: the same comparison against a torch step whose GELU lacks
+    its cubic term fails by orders of magnitude (the mistake is planted in the CPU reference)."""
+    ins = _scaled_f32_inputs(batch=2, scale=10.0)
+    text = configs.gpt2_program(batch=2, dtype="f32", with_inputs=False, **TINY, **HP).text
+    outs = oracle_run(text, ins)
+    bad = torch_gpt_step(ins, **TINY, **HP, gelu_c=0.0)
+    n = len(configs.gpt2_param_shapes(**TINY))
+    assert max(_normwise(outs[n + i], bad[n + i]) for i in range(n)) > 100 * 2e-5
+
+
+def test_tiny_gpt_bf16_step_near_torch_autograd():
+    """The config's own bf16 program: its gradients stay within bf16 pipeline error of float64."""
+    p = tiny()
+    outs = oracle_run(p.text, p.inputs)
+    ref = torch_gpt_step(p.inputs, **TINY, **HP)
+    n = len(configs.gpt2_param_shapes(**TINY))
+    assert abs(float(outs[-1]) - float(ref[-1])) <= 1e-3 * abs(float(ref[-1]))
+    for i in range(n):
+        assert _normwise(outs[n + i], ref[n + i]) <= 3e-2, i
+
+
 def test_tiny_gpt_loss_is_cross_entropy_of_a_near_uniform_model():
     p = tiny()
     loss = oracle_run(p.text, p.inputs)[-1]
