@@ -90,6 +90,10 @@ struct Graph {
 // Returns an empty string on success, else an error message (the op or token that failed).
 std::string ParseModule(const char* text, size_t size, Graph* g);
 
+// Checks operand counts, shapes and attribute ranges of the supported ops (verify.cc); "" if the
+// graph is well formed, else the first violation.  ParseModule runs it.
+std::string VerifyGraph(const Graph& g);
+
 // One line per op of a parsed graph: name, operand / result value ids and types, integer
 // attributes, the attributes the lowering reads as strings, reduce kind and the constant data
 // (splat flag + FNV-1a hash of the bytes).  Two spellings of one program (pretty or generic text,

@@ -934,6 +934,13 @@ class Builder {
       }
       Op* op = g_->NewOp(opname);
       for (auto& n : a.operands) op->operands.push_back(lookup(n));
+      // the operand types the text states must be the types of the values it names
+      if (a.in_types.size() == a.operands.size()) {
+        for (size_t k = 0; k < a.operands.size(); ++k)
+          if (!(op->operands[k]->type == a.in_types[k]))
+            throw ParseError{"malformed program: operand " + std::to_string(k) + " of " + a.name + " is " +
+                             op->operands[k]->type.str() + " but the op states " + a.in_types[k].str()};
+      }
       op->ints = a.ints;
       op->strs = a.strs;
       if (a.out_types.size() != a.results.size())
@@ -1031,6 +1038,8 @@ std::string ParseModule(const char* text, size_t size, Graph* g) {
     Builder b(p.funcs, g);
     b.BuildMain();
     g->Renumber();
+    std::string bad = VerifyGraph(*g);
+    if (!bad.empty()) return "malformed program: " + bad;
   } catch (const ParseError& e) {
     return e.msg;
   } catch (const std::exception& e) {

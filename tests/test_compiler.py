@@ -136,3 +136,73 @@ def test_small_independent_loops_share_one_launch(lib_path):
     rc, rep = report(lib_path, b.text(outs))
     assert rc == 0, rep
     assert "loops x3" in rep, rep
+
+
+def _one_op(body, ins, out):
+    sig = ", ".join(f"%arg{i}: {t}" for i, t in enumerate(ins))
+    return f"module @m {{\n  func.func public @main({sig}) -> ({out}) {{\n{body}\n    return %0 : {out}\n  }}\n}}\n"
+
+
+A, Bt, C = "tensor<8x128xf32>", "tensor<8x64xf32>", "tensor<128x8xf32>"
+MALFORMED = [
+    ("missing operand", _one_op(f"    %0 = stablehlo.exponential  : {A}", [A], A), "expects 1 operand"),
+    ("operand type stated wrongly", _one_op(f"    %0 = stablehlo.add %arg0, %arg1 : {A}", [A, Bt], A), "operand 1 of stablehlo.add is"),
+    ("binary shapes differ", _one_op(f"    %0 = stablehlo.add %arg0, %arg1 : ({A}, {Bt}) -> {A}", [A, Bt], A), "differs from the result"),
+    ("slice out of range", _one_op(f"    %0 = stablehlo.slice %arg0 [0:8, 100:164] : ({A}) -> {Bt}", [A], Bt), "slice bounds"),
+    ("broadcast dims", _one_op(f"    %0 = stablehlo.broadcast_in_dim %arg0, dims = [0, 2] : ({A}) -> {A}", [A], A), "broadcast"),
+    ("not a permutation", _one_op(f"    %0 = stablehlo.transpose %arg0, dims = [0, 0] : ({A}) -> {C}", [A], C), "permutation"),
+    ("reshape count", _one_op(f"    %0 = stablehlo.reshape %arg0 : ({A}) -> {Bt}", [A], Bt), "element count"),
+    ("dot contracting sizes", _one_op(f"    %0 = stablehlo.dot_general %arg0, %arg1, contracting_dims = [1] x [0] : ({A}, {Bt}) -> tensor<8x64xf32>",
+                                      [A, Bt], "tensor<8x64xf32>"), "contracting dimensions differ"),
+    ("dynamic slice size", _one_op(f"    %0 = stablehlo.dynamic_slice %arg0, %arg1, %arg1, sizes = [16, 64] : ({A}, tensor<i32>, tensor<i32>) -> tensor<16x64xf32>",
+                                   [A, "tensor<i32>"], "tensor<16x64xf32>"), "slice size out of range"),
+]
+
+
+@pytest.mark.parametrize("what,text,msg", MALFORMED, ids=[m[0] for m in MALFORMED])
+def test_malformed_programs_are_rejected_at_compile_time(lib_path, what, text, msg):
+    """Programs MLIR's verifiers would reject fail to compile (never become out-of-bounds kernels)."""
+    rc, rep = report(lib_path, text, nvrtc=0)
+    assert rc == 1 and msg in rep, rep
+
+
+_FUZZ_CHILD = r'''
+import ctypes, json, sys
+lib = ctypes.CDLL(sys.argv[1])
+buf = ctypes.create_string_buffer(1 << 23)
+for t in json.loads(sys.stdin.read()):
+    b = t.encode()
+    assert lib.b200_compile_report(b, len(b), 1, 0, buf, len(buf)) in (0, 1)
+print("ok")
+'''
+
+
+def test_mutated_programs_never_crash_the_compiler(lib_path):
+    """Seeded token-level mutations of real programs (dropped, duplicated and altered tokens):
+    parse + verify + lower end in a plan or an error, never a crash, in a child process."""
+    import json
+    import random
+    import re
+    import subprocess
+    import sys
+    progs = [configs.mlp_program(with_inputs=False).text,
+             configs.attention_program(B=1, H=2, S=256, causal=True, with_inputs=False).text,
+             configs.gpt2_program(layers=1, d=64, heads=2, mlp=128, vocab=96, seq=64, batch=2, with_inputs=False).text]
+    rng = random.Random(2024)
+    tok = re.compile(r"\s+|[^\s]+")
+    items = []
+    for _ in range(300):
+        toks = tok.findall(rng.choice(progs))
+        for _ in range(rng.randint(1, 3)):
+            k = rng.randrange(len(toks))
+            r = rng.random()
+            if r < 0.4:
+                toks[k] = ""
+            elif r < 0.7:
+                toks[k] = toks[rng.randrange(len(toks))]
+            else:
+                toks[k] = re.sub(r"\d+", lambda m: str(rng.choice([0, 1, 7, 65536, 2 ** 31])), toks[k])
+        items.append("".join(toks))
+    r = subprocess.run([sys.executable, "-c", _FUZZ_CHILD, lib_path], input=json.dumps(items).encode(),
+                       capture_output=True, timeout=600)
+    assert r.returncode == 0 and b"ok" in r.stdout, r.stderr[-2000:]
