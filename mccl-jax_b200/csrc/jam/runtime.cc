@@ -14,6 +14,8 @@
 #include <functional>
 #include <thread>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "../../../include/b200_kernels.h"
 #include "../comm/comm.h"
 
@@ -359,7 +361,26 @@ std::string Executable::Load(DeviceState& dev, PerDevice** pd) {
   return "";
 }
 
+namespace {
+// B200_NVTX=1: an NVTX range around each execution and each of its steps (host enqueue side), for
+// profilers that record NVTX; without a profiler attached the calls do nothing.
+bool NvtxOn() {
+  static const bool on = std::getenv("B200_NVTX") != nullptr;
+  return on;
+}
+struct NvtxRange {
+  bool on;
+  NvtxRange(bool enable, const std::string& name) : on(enable) {
+    if (on) nvtxRangePushA(name.c_str());
+  }
+  ~NvtxRange() {
+    if (on) nvtxRangePop();
+  }
+};
+}  // namespace
+
 std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& args, std::vector<void*>* outs, Comm* comm) {
+  NvtxRange run_range(NvtxOn(), "execute " + name_);
   cudaSetDevice(dev.ordinal);
   PerDevice* pd = nullptr;
   std::string err = Load(dev, &pd);
@@ -475,6 +496,7 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
   auto run_steps = [&]() -> std::string {
     for (size_t i = 0; i < P.steps.size(); ++i) {
       const Step& S = P.steps[i];
+      NvtxRange step_range(NvtxOn(), S.label);
       for (int k : S.wait_coll)
         if (coll_done[k]) cudaStreamWaitEvent(st, coll_done[k], 0);
       switch (S.kind) {
