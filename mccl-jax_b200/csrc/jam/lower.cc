@@ -45,7 +45,8 @@ const std::unordered_set<std::string> kUnary = {
     "reduce_precision"};
 const std::unordered_set<std::string> kIndexMap = {
     "broadcast_in_dim", "reshape", "transpose", "slice", "concatenate", "pad", "iota",
-    "constant", "convert", "bitcast_convert", "gather", "reverse", "dynamic_slice", "dynamic_update_slice"};
+    "constant", "convert", "bitcast_convert", "gather", "reverse", "dynamic_slice", "dynamic_update_slice",
+    "broadcast"};
 // index maps whose operand index depends on runtime data (an index tensor or scalar offsets)
 bool DataDependentIndex(const Op* op) {
   return op->name == "gather" || op->name == "dynamic_slice" || op->name == "dynamic_update_slice";
@@ -531,6 +532,11 @@ struct Gen {
       std::vector<std::string> j(perm.size());
       for (size_t k = 0; k < perm.size(); ++k) j[perm[k]] = idx[k];
       return opnd(0, j);
+    }
+    if (n == "broadcast") {
+      // the legacy broadcast prepends dimensions: the operand is indexed by the trailing ones
+      const size_t lead = ty.dims.size() - op->operands[0]->type.dims.size();
+      return opnd(0, std::vector<std::string>(idx.begin() + lead, idx.end()));
     }
     if (n == "reverse") {
       const auto& dims = op->ints.count("dims") ? op->ints.at("dims") : op->ints.at("dimensions");

@@ -655,6 +655,8 @@ class Parser {
       ints_of("broadcast_dimensions", "dims");
     } else if (n == "stablehlo.transpose") {
       ints_of("permutation", "dims");
+    } else if (n == "stablehlo.broadcast") {
+      ints_of("broadcast_sizes", "sizes");
     } else if (n == "stablehlo.reverse") {
       ints_of("dimensions", "dims");
     } else if (n == "stablehlo.dynamic_slice") {

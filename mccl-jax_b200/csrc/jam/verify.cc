@@ -103,6 +103,15 @@ class Verifier {
       }
       return;
     }
+    if (n_ == "broadcast") {
+      Arity(1);
+      const auto& sz = Ints("sizes");
+      std::vector<int64_t> want = sz;
+      want.insert(want.end(), In(0).dims.begin(), In(0).dims.end());
+      if (R().dims != want) Fail("result shape is not broadcast_sizes followed by the operand shape");
+      if (Dt(0) != RDt()) Fail("operand and result types differ");
+      return;
+    }
     if (n_ == "transpose") {
       Arity(1);
       const auto& p = Ints("dims");

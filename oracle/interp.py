@@ -390,6 +390,9 @@ class Interp:
             return [_cast(r, ot.dtype)]
         if n == "stablehlo.reduce_precision":
             return [_reduce_precision(ins[0], a["format"], ot.dtype)]
+        if n == "stablehlo.broadcast":
+            x = ins[0]
+            return [np.broadcast_to(x, tuple(a["sizes"]) + x.shape).copy()]
         if n == "stablehlo.reverse":
             return [np.flip(ins[0], axis=tuple(a["dims"])).copy()]
         if n == "stablehlo.dynamic_slice":

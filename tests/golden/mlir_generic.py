@@ -113,6 +113,8 @@ def convert_line(line: str) -> str:
         return ind + _op(res, name, operands, {"broadcast_dimensions": _arr(kv["dims"])}, ty)
     if name == "transpose":
         return ind + _op(res, name, operands, {"permutation": _arr(kv["dims"])}, ty)
+    if name == "broadcast":
+        return ind + _op(res, name, operands, {"broadcast_sizes": _arr(kv["sizes"])}, ty)
     if name == "reverse":
         return ind + _op(res, name, operands, {"dimensions": _arr(kv["dims"])}, _fn_type(ty, 1))
     if name == "dynamic_slice":

@@ -1,5 +1,5 @@
 """Shape, bit and special-function ops of the reference's lowering beyond the configs' own programs:
-reverse, dynamic_slice, dynamic_update_slice, bitcast_convert (src/jam/ops/shape.mm), popcnt and the
+broadcast (structural.mm), reverse, dynamic_slice, dynamic_update_slice, bitcast_convert (src/jam/ops/shape.mm), popcnt and the
 three shifts (unary.mm, binary.mm), count_leading_zeros and reduce_precision (hard_limit.mm:15-52),
 erf (chlo.erf, or custom_call @mhlo.erf as hard_limit.mm:65-67 reads it) and partition_id
 (collectives.mm:16-29).
@@ -81,6 +81,8 @@ BITCASTS = [("f32", "i32"), ("i32", "f32"), ("bf16", "i16"), ("f16", "ui16"), ("
 
 F = T("f32")
 OTHER = {
+    "broadcast": (prog(f"    %0 = stablehlo.broadcast %arg0, sizes = [3] : ({F}) -> {T('f32', (3, 8, 128))}", [F],
+                       T("f32", (3, 8, 128))), ["f32"]),
     "reverse_1": (prog(f"    %0 = stablehlo.reverse %arg0, dims = [1] : {F}", [F], F), ["f32"]),
     "reverse_01": (prog(f"    %0 = stablehlo.reverse %arg0, dims = [0, 1] : {F}", [F], F), ["f32"]),
     "dynamic_slice": (prog(f"    %0 = stablehlo.dynamic_slice %arg0, %arg1, %arg2, sizes = [4, 64] : "
