@@ -973,6 +973,22 @@ class Lowerer {
   void RankConstants() {
     for (auto& up : g_.ops) {
       Op* op = up.get();
+      if (op->name == "all_to_all" || op->name == "collective_broadcast" || op->name == "collective_permute") {
+        // one process: every rank's data is its own (the reference binds these to their operand,
+        // src/jam/ops/collectives.mm:16-29); across processes they are not lowered
+        if (opt_.num_processes > 1) throw LowerError{op->name + " across processes is not supported"};
+        if (op->operands.size() != 1 || op->results.size() != 1 || !(op->operands[0]->type == op->result()->type))
+          throw LowerError{op->name + ": expected one operand of the result's type"};
+        if (op->name == "collective_permute") {
+          const auto it = op->ints.find("source_target_pairs");
+          bool self = false;
+          if (it != op->ints.end())
+            for (size_t k = 0; k + 1 < it->second.size(); k += 2) self = self || (it->second[k] == 0 && it->second[k + 1] == 0);
+          if (!self) throw LowerError{"collective_permute without a (0, 0) pair at one process (a zero result) is not supported"};
+        }
+        op->name = "optimization_barrier";   // an alias of its operand
+        continue;
+      }
       if (op->name != "partition_id" && op->name != "replica_id") continue;
       const bool split = op->name == "partition_id" ? g_.num_partitions > 1 : g_.num_replicas > 1;
       const uint64_t id = split ? (uint64_t)opt_.rank : 0;

@@ -973,6 +973,7 @@ class Builder {
         if (s != op->strs.end()) op->ints[key] = ParseIntsAttr(s->second);
       }
       if (op->strs.count("replica_groups")) op->ints["replica_groups"] = ParseIntsAttr(op->strs["replica_groups"]);
+      if (op->strs.count("source_target_pairs")) op->ints["source_target_pairs"] = ParseIntsAttr(op->strs["source_target_pairs"]);
     }
     throw ParseError{"function @" + f.name + " has no return"};
   }

@@ -40,7 +40,8 @@ class Verifier {
 
   void Run() {
     const auto& in = op_->operands;
-    if (n_ == "custom_call" || n_ == "all_reduce" || n_ == "all_gather" || n_ == "reduce_scatter") {
+    if (n_ == "custom_call" || n_ == "all_reduce" || n_ == "all_gather" || n_ == "reduce_scatter" || n_ == "all_to_all" ||
+        n_ == "collective_broadcast" || n_ == "collective_permute") {
       if (in.empty()) Fail("needs an operand");
       return;   // shapes follow the sharding / rank count, checked where they are lowered
     }

@@ -206,3 +206,28 @@ def test_mutated_programs_never_crash_the_compiler(lib_path):
     r = subprocess.run([sys.executable, "-c", _FUZZ_CHILD, lib_path], input=json.dumps(items).encode(),
                        capture_output=True, timeout=600)
     assert r.returncode == 0 and b"ok" in r.stdout, r.stderr[-2000:]
+
+
+ONE_RANK = {
+    "all_to_all": '"stablehlo.all_to_all"(%arg0) <{concat_dimension = 0 : i64, replica_groups = dense<[[0]]> : tensor<1x1xi64>, split_count = 1 : i64, split_dimension = 0 : i64}>',
+    "collective_broadcast": '"stablehlo.collective_broadcast"(%arg0) <{replica_groups = dense<[[0]]> : tensor<1x1xi64>}>',
+    "collective_permute": '"stablehlo.collective_permute"(%arg0) <{channel_handle = #stablehlo.channel_handle<handle = 1, type = 1>, source_target_pairs = dense<[[0, 0]]> : tensor<1x2xi64>}>',
+}
+
+
+@pytest.mark.parametrize("name", sorted(ONE_RANK))
+def test_other_collectives_are_identities_at_one_process(lib_path, name):
+    """all_to_all / collective_broadcast / collective_permute at one process return their operand
+    (the reference binds them to it, src/jam/ops/collectives.mm:16-29); across processes they are
+    a compile error naming the op."""
+    text = _one_op(f"    %0 = {ONE_RANK[name]} : ({A}) -> {A}", [A], A)
+    rc, rep = report(lib_path, text, nvrtc=0)
+    assert rc == 0 and "kernel" not in rep and "collective" not in rep.split("\n", 1)[-1], rep
+    rc, rep = report(lib_path, text, nprocs=2, nvrtc=0)
+    assert rc == 1 and name in rep and "across processes" in rep, rep
+
+
+def test_collective_permute_without_self_pair_is_refused_at_one_process(lib_path):
+    text = _one_op(f"    %0 = " + ONE_RANK["collective_permute"].replace("[[0, 0]]", "[[1, 0]]") + f" : ({A}) -> {A}", [A], A)
+    rc, rep = report(lib_path, text, nvrtc=0)
+    assert rc == 1 and "(0, 0) pair" in rep, rep
