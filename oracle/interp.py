@@ -504,7 +504,8 @@ class Interp:
             if tgt in ("Sharding", "SPMDFullToShardShape", "SPMDShardToFullShape"):
                 return [ins[0]]
             raise NotImplementedError(f"custom_call @{tgt}")
-        if n in ("stablehlo.all_reduce", "stablehlo.all_gather", "stablehlo.reduce_scatter"):
+        if n in ("stablehlo.all_reduce", "stablehlo.all_gather", "stablehlo.reduce_scatter", "stablehlo.collective_permute",
+                 "stablehlo.collective_broadcast", "stablehlo.all_to_all"):
             kind = _reducer_kind(op.regions[0]) if op.regions else None
             res = yield (n, kind, ins[0], a)
             return [res]
@@ -555,6 +556,20 @@ def _drive(gens):
                 acc = acc + _hi(x)
             parts = np.split(acc.astype(arrs[0].dtype), n, axis=0)
             sends = parts
+        elif name == "stablehlo.collective_permute":
+            # each (source, target) pair moves source's operand to target; a target without a
+            # source gets zeros
+            nums = [int(v) for v in re.findall(r"-?\d+", str(msgs[0][3].get("source_target_pairs", "")).split(":")[0])]
+            sends = [np.zeros_like(arrs[0]) for _ in range(n)]
+            for k in range(0, len(nums) - 1, 2):
+                sends[nums[k + 1]] = arrs[nums[k]].copy()
+        elif name == "stablehlo.collective_broadcast":
+            sends = [arrs[0].copy() for _ in range(n)]      # one group: rank 0 is the source
+        elif name == "stablehlo.all_to_all":
+            a = msgs[0][3]
+            sd, cd = int(a.get("split_dimension", 0)), int(a.get("concat_dimension", 0))
+            parts = [np.split(x, n, axis=sd) for x in arrs]
+            sends = [np.concatenate([parts[src][dst] for src in range(n)], axis=cd) for dst in range(n)]
         else:
             raise NotImplementedError(name)
 

@@ -114,3 +114,25 @@ module @m {
     assert set(m.funcs) == {"main", "inner"}
     x = np.arange(12, dtype=np.float32).reshape(4, 3)
     np.testing.assert_allclose(run(text, [x])[0], (x * x).sum(1))
+
+
+def test_oracle_permute_broadcast_all_to_all():
+    """collective_permute / collective_broadcast / all_to_all across simulated ranks, and the
+    identity each is at one rank (what the plugin lowers at one process)."""
+    def prog(op_text, n):
+        t = f"tensor<{2 * n}x4xf32>"
+        return ("module @m {\n  func.func public @main(%arg0: " + t + ") -> (" + t + ") {\n"
+                f"    %0 = {op_text} : ({t}) -> {t}\n    return %0 : {t}\n  }}\n}}\n")
+    perm = '"stablehlo.collective_permute"(%arg0) <{channel_handle = #stablehlo.channel_handle<handle = 1, type = 1>, source_target_pairs = dense<PAIRS> : tensor<NPx2xi64>}>'
+    bcast = '"stablehlo.collective_broadcast"(%arg0) <{replica_groups = dense<[[0, 1]]> : tensor<1x2xi64>}>'
+    a2a = '"stablehlo.all_to_all"(%arg0) <{concat_dimension = 0 : i64, replica_groups = dense<[[0, 1]]> : tensor<1x2xi64>, split_count = 2 : i64, split_dimension = 0 : i64}>'
+    x1 = np.arange(8, dtype=np.float32).reshape(2, 4)
+    assert np.array_equal(run(prog(perm.replace("PAIRS", "[[0, 0]]").replace("NP", "1"), 1), [x1])[0], x1)
+    xs = [np.full((4, 4), r + 1, np.float32) + np.arange(4, dtype=np.float32)[:, None] for r in range(2)]
+    res = run_spmd(prog(perm.replace("PAIRS", "[[0, 1]]").replace("NP", "1"), 2), [[x] for x in xs])
+    assert np.array_equal(res[1][0], xs[0]) and np.array_equal(res[0][0], np.zeros_like(xs[0]))
+    res = run_spmd(prog(bcast, 2), [[x] for x in xs])
+    assert all(np.array_equal(r[0], xs[0]) for r in res)
+    res = run_spmd(prog(a2a, 2), [[x] for x in xs])
+    for dst in range(2):
+        assert np.array_equal(res[dst][0], np.concatenate([xs[src][2 * dst:2 * dst + 2] for src in range(2)], axis=0))
