@@ -594,7 +594,15 @@ struct Gen {
       for (size_t k = 0; k < in.size(); ++k) {
         if (!op->operands[first + k]->type.dims.empty()) throw LowerError{n + ": start indices must be scalars"};
         std::string sv = Emit(op->operands[first + k], {});
-        st[k] = Var(DT::kS64, "imin(imax((long long)(" + sv + "), 0LL), " + std::to_string(in[k] - win[k]) + "LL)");
+        const DT it = op->operands[first + k]->type.dt;
+        const std::string hi = std::to_string(in[k] - win[k]);
+        if (it == DT::kU64 || it == DT::kU32 || it == DT::kU16 || it == DT::kU8)
+          // unsigned starts are never below 0; clamp in unsigned arithmetic so a u64 start of 2^63 or
+          // more stays a large value (clamped to dim - window), not a negative one
+          st[k] = Var(DT::kS64, "(long long)((unsigned long long)(" + sv + ") < " + hi + "ULL ? (unsigned long long)(" + sv +
+                                ") : " + hi + "ULL)");
+        else
+          st[k] = Var(DT::kS64, "imin(imax((long long)(" + sv + "), 0LL), " + hi + "LL)");
       }
       if (!upd) {
         std::vector<std::string> j(idx.size());
@@ -3534,6 +3542,21 @@ class Lowerer {
       auto it = op->ints.find(key);
       if (it != op->ints.end() && !it->second.empty() && it->second[0] != 0)
         throw LowerError{n + " only supported along dim 0"};
+    }
+    // Across processes the communicator spans every rank in rank order, so the program's replica
+    // groups must be that one group (a jax shard_map over all devices writes it so); other groupings
+    // would need sub-communicators and are a compile error rather than a silently world-wide
+    // collective.  At one process every collective is the identity, as in the reference.
+    if (opt_.num_processes > 1) {
+      auto g = op->ints.find("replica_groups");
+      auto gc = op->ints.find("replica_groups.count");
+      if (g != op->ints.end() && !g->second.empty()) {
+        const int64_t count = gc == op->ints.end() || gc->second.empty() ? -1 : gc->second[0];
+        bool ok = (int64_t)g->second.size() == opt_.num_processes && (count == 1 || count == -1);
+        for (size_t k = 0; ok && k < g->second.size(); ++k) ok = g->second[k] == (int64_t)k;
+        if (!ok) throw LowerError{n + ": replica_groups other than one group of all " + std::to_string(opt_.num_processes) +
+                                  " ranks in rank order are not supported"};
+      }
     }
     if (opt_.num_processes <= 1 && x->type.dims == r->type.dims) {
       // one rank: identity (the reference does the same, src/jam/lower.mm:346-352)

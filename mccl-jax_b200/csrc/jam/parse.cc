@@ -194,6 +194,7 @@ struct ParseError {
 };
 
 std::vector<int64_t> ParseIntsAttr(const std::string& s);
+int64_t ReplicaGroupCount(const std::string& s);
 void ParseDimNumbers(const std::string& s, const std::string& prefix, Op* op);
 
 class Parser {
@@ -303,7 +304,7 @@ class Parser {
     }
   }
 
-  std::string AttrValue(bool typed) {
+  std::string AttrValue(bool typed, std::string* type_out = nullptr) {
     if (Peek() == "[") {
       auto v = IntList();
       std::string s;
@@ -316,7 +317,11 @@ class Parser {
       const std::string& ty = Peek(1);
       bool is_type = ty.rfind("tensor<", 0) == 0 || ty == "index" ||
                      (ty.size() >= 2 && (ty[0] == 'i' || ty[0] == 'f' || ty[0] == 'u') && std::isdigit((unsigned char)ty.back()));
-      if (is_type) { Next(); Next(); }
+      if (is_type) {
+        Next();
+        const std::string t = Next();
+        if (type_out) *type_out = t;
+      }
     }
     return v;
   }
@@ -327,9 +332,12 @@ class Parser {
     while (!Accept("}")) {
       std::string key = Next();
       if (key == ",") continue;
-      std::string val = "true";
-      if (Accept("=")) val = AttrValue(true);
+      std::string val = "true", ty;
+      if (Accept("=")) val = AttrValue(true, &ty);
       d[key] = val;
+      // the group structure of replica_groups is in its type (tensor<GROUPSxSIZExi64>), which a
+      // hex literal does not show
+      if (key == "replica_groups" && !ty.empty()) d["replica_groups.type"] = ty;
     }
     return d;
   }
@@ -851,6 +859,28 @@ std::vector<int64_t> ParseIntsAttr(const std::string& s) {
   return out;
 }
 
+// Number of groups in a replica_groups attribute: the leading extent of its tensor type when the
+// text carries one ("dense<...> : tensor<2x4xi64>"), else the bracket nesting of the literal
+// ("[[0, 1], [2, 3]]" has 2 groups, a flat "[0, 1]" one); -1 when neither tells.
+int64_t ReplicaGroupCount(const std::string& s) {
+  const size_t t = s.find("tensor<");
+  if (t != std::string::npos) {
+    size_t k = t + 7;
+    int64_t g = 0;
+    bool any = false;
+    while (k < s.size() && std::isdigit((unsigned char)s[k])) { g = g * 10 + (s[k++] - '0'); any = true; }
+    if (any && k < s.size() && s[k] == 'x') return g;
+  }
+  if (s.find("0x") != std::string::npos) return -1;
+  const size_t a = s.find('[');
+  if (a == std::string::npos) return -1;
+  if (a + 1 < s.size() && s.find_first_not_of(" ", a + 1) != std::string::npos && s[s.find_first_not_of(" ", a + 1)] != '[')
+    return 1;
+  int64_t inner = 0;
+  for (size_t k = a + 1; k < s.size(); ++k) if (s[k] == '[') ++inner;
+  return inner;
+}
+
 // "#stablehlo.gather<offset_dims = [1], collapsed_slice_dims = [0], index_vector_dim = 1>"
 void ParseDimNumbers(const std::string& s, const std::string& prefix, Op* op) {
   size_t lt = s.find('<');
@@ -972,7 +1002,13 @@ class Builder {
         auto s = op->strs.find(key);
         if (s != op->strs.end()) op->ints[key] = ParseIntsAttr(s->second);
       }
-      if (op->strs.count("replica_groups")) op->ints["replica_groups"] = ParseIntsAttr(op->strs["replica_groups"]);
+      if (op->strs.count("replica_groups")) {
+        const std::string& rg = op->strs["replica_groups"];
+        op->ints["replica_groups"] = ParseIntsAttr(rg);
+        auto ty = op->strs.find("replica_groups.type");
+        op->ints["replica_groups.count"] = {ReplicaGroupCount(ty == op->strs.end() ? rg : rg + " : " + ty->second)};
+        if (ty != op->strs.end()) op->strs.erase(ty);
+      }
       if (op->strs.count("source_target_pairs")) op->ints["source_target_pairs"] = ParseIntsAttr(op->strs["source_target_pairs"]);
     }
     throw ParseError{"function @" + f.name + " has no return"};

@@ -446,7 +446,10 @@ static bool MapRows64(CUtensorMap* map, const void* ptr, uint64_t rows) {
 }
 
 bool AttentionBwdShapeOk(int B, int H, int S, int D) {
-  return B > 0 && H > 0 && D == HD && S > 0 && S % TB == 0 && (long long)B * H * S <= INT32_MAX;
+  if (!(B > 0 && H > 0 && D == HD && S > 0 && S % TB == 0)) return false;
+  long long bh = 0, rows = 0;   // overflow-checked: huge dimensions must not wrap to a small product
+  return !__builtin_mul_overflow((long long)B, (long long)H, &bh) && !__builtin_mul_overflow(bh, (long long)S, &rows) &&
+         rows <= INT32_MAX;
 }
 
 // Scratch: dq_acc (B*H*S*D f32) and delta (B*H*S f32), caller-owned.  Allocates nothing.

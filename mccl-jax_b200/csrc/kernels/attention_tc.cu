@@ -442,8 +442,13 @@ static int LaunchAttn(const void* q, const void* k, const void* v, void* o, int 
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
+// B * H * S query rows must fit an int (grid and row arithmetic); the product is formed with
+// overflow checks so that huge dimensions cannot wrap around to a small value.
 bool AttentionShapeOk(int B, int H, int S, int D) {
-  return B > 0 && H > 0 && D == 64 && S > 0 && S % (2 * TQ) == 0 && (long long)B * H * S <= INT32_MAX;
+  if (!(B > 0 && H > 0 && D == 64 && S > 0 && S % (2 * TQ) == 0)) return false;
+  long long bh = 0, rows = 0;
+  return !__builtin_mul_overflow((long long)B, (long long)H, &bh) && !__builtin_mul_overflow(bh, (long long)S, &rows) &&
+         rows <= INT32_MAX;
 }
 
 // V read in place (MN-major operand); no scratch memory.
@@ -467,7 +472,7 @@ int AttentionFwdLse(const void* q, const void* k, const void* v, void* o, float*
 // Cross-check variant: V transposed into `vt` (B*H*S*D bf16 scratch) and read K-major.
 int AttentionFwdWithVt(const void* q, const void* k, const void* v, void* vt, void* o, int B, int H, int S, int D,
                        int causal, float scale, cudaStream_t st) {
-  if (!AttentionShapeOk(B, H, S, D)) return -1;
+  if (!AttentionShapeOk(B, H, S, D) || (long long)B * H > 65535) return -1;   // B * H is the transpose's grid.z
   if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)vt | (uintptr_t)o) % 16) return -1;
   dim3 tg(S / 64, D / 64, B * H);
   transpose_v_kernel<<<tg, 256, 0, st>>>((const uint16_t*)v, (uint16_t*)vt, S, D);
@@ -540,7 +545,7 @@ static int NoAllocScratch(void** out) {
 extern "C" int b200_attention_fwd_noalloc(const void* q, const void* k, const void* v, void* o, int B, int H, int S,
                                           int D, int causal, float scale, void* stream) {
   if (B == 0 || H == 0 || S == 0) return 0;
-  if (B < 0 || H < 0 || S < 0 || D <= 0) return -1;
+  if (!b200k::AttentionShapeOk(B, H, S, D)) return -1;   // bounds B * H * S before the size product
   const size_t need = (size_t)B * H * S * D * 2;
   if (need > b200k::kNoAllocScratchBytes) return -5;   // larger than the static scratch
   void* vt = nullptr;

@@ -539,39 +539,68 @@ def _drive(gens):
             sends = list(range(n))
             continue
         kind = msgs[0][1]
+        attrs = msgs[0][3]
         arrs = [m[2] for m in msgs]
-        if name == "stablehlo.all_reduce":
-            acc = _hi(arrs[0]).copy()
-            for x in arrs[1:]:
-                acc = {"add": np.add, "maximum": np.maximum, "minimum": np.minimum,
-                       "multiply": np.multiply}[kind](acc, _hi(x))
-            out = acc.astype(arrs[0].dtype)
-            sends = [out.copy() for _ in range(n)]
-        elif name == "stablehlo.all_gather":
-            out = np.concatenate(arrs, axis=0)
-            sends = [out.copy() for _ in range(n)]
-        elif name == "stablehlo.reduce_scatter":
-            acc = _hi(arrs[0]).copy()
-            for x in arrs[1:]:
-                acc = acc + _hi(x)
-            parts = np.split(acc.astype(arrs[0].dtype), n, axis=0)
-            sends = parts
-        elif name == "stablehlo.collective_permute":
-            # each (source, target) pair moves source's operand to target; a target without a
-            # source gets zeros
-            nums = [int(v) for v in re.findall(r"-?\d+", str(msgs[0][3].get("source_target_pairs", "")).split(":")[0])]
-            sends = [np.zeros_like(arrs[0]) for _ in range(n)]
-            for k in range(0, len(nums) - 1, 2):
-                sends[nums[k + 1]] = arrs[nums[k]].copy()
-        elif name == "stablehlo.collective_broadcast":
-            sends = [arrs[0].copy() for _ in range(n)]      # one group: rank 0 is the source
-        elif name == "stablehlo.all_to_all":
-            a = msgs[0][3]
-            sd, cd = int(a.get("split_dimension", 0)), int(a.get("concat_dimension", 0))
-            parts = [np.split(x, n, axis=sd) for x in arrs]
-            sends = [np.concatenate([parts[src][dst] for src in range(n)], axis=cd) for dst in range(n)]
-        else:
-            raise NotImplementedError(name)
+        sends = [None] * n
+        # every collective acts within each replica group on its own (StableHLO semantics; the
+        # reference forwards whole-world groups only, src/jam/lower.mm:382-436)
+        for grp in _replica_groups(attrs, n, name):
+            sub = _collective(name, kind, attrs, [arrs[r] for r in grp])
+            for r, out in zip(grp, sub):
+                sends[r] = out
+        if any(x is None for x in sends):
+            raise RuntimeError(f"{name}: a rank belongs to no replica group")
+
+
+def _replica_groups(attrs, n, name):
+    """The replica groups of a collective as lists of ranks; an absent or empty attribute means one
+    group of all n ranks.  collective_permute has source_target_pairs instead (one group)."""
+    if name == "stablehlo.collective_permute":
+        return [list(range(n))]
+    txt = str(attrs.get("replica_groups", "")).split(":")[0]
+    groups = [[int(v) for v in re.findall(r"-?\d+", g)] for g in re.findall(r"\[([^\[\]]*)\]", txt)]
+    groups = [g for g in groups if g]
+    if not groups:
+        return [list(range(n))]
+    seen = sorted(r for g in groups for r in g)
+    if seen != list(range(n)):
+        raise ValueError(f"{name}: replica_groups {groups} do not partition ranks 0..{n - 1}")
+    return groups
+
+
+def _collective(name, kind, attrs, arrs):
+    """One collective over the operands of one group, in group order; returns each member's result."""
+    n = len(arrs)
+    if name == "stablehlo.all_reduce":
+        acc = _hi(arrs[0]).copy()
+        for x in arrs[1:]:
+            acc = {"add": np.add, "maximum": np.maximum, "minimum": np.minimum,
+                   "multiply": np.multiply}[kind](acc, _hi(x))
+        out = acc.astype(arrs[0].dtype)
+        return [out.copy() for _ in range(n)]
+    if name == "stablehlo.all_gather":
+        out = np.concatenate(arrs, axis=int(attrs.get("all_gather_dim", 0)))
+        return [out.copy() for _ in range(n)]
+    if name == "stablehlo.reduce_scatter":
+        acc = _hi(arrs[0]).copy()
+        for x in arrs[1:]:
+            acc = acc + _hi(x)
+        return np.split(acc.astype(arrs[0].dtype), n, axis=int(attrs.get("scatter_dimension", 0)))
+    if name == "stablehlo.collective_permute":
+        # each (source, target) pair moves source's operand to target; a target without a source
+        # gets zeros
+        nums = [int(v) for v in re.findall(r"-?\d+", str(attrs.get("source_target_pairs", "")).split(":")[0])]
+        sends = [np.zeros_like(arrs[0]) for _ in range(n)]
+        for k in range(0, len(nums) - 1, 2):
+            sends[nums[k + 1]] = arrs[nums[k]].copy()
+        return sends
+    if name == "stablehlo.collective_broadcast":
+        return [arrs[0].copy() for _ in range(n)]        # the group's first member is the source
+    if name == "stablehlo.all_to_all":
+        sd, cd = int(attrs.get("split_dimension", 0)), int(attrs.get("concat_dimension", 0))
+        parts = [np.split(x, n, axis=sd) for x in arrs]
+        return [np.concatenate([parts[src][dst] for src in range(n)], axis=cd) for dst in range(n)]
+    raise NotImplementedError(name)
 
 
 def run_spmd(text: str, per_rank_inputs: List[List[np.ndarray]]):

@@ -231,3 +231,18 @@ def test_collective_permute_without_self_pair_is_refused_at_one_process(lib_path
     text = _one_op(f"    %0 = " + ONE_RANK["collective_permute"].replace("[[0, 0]]", "[[1, 0]]") + f" : ({A}) -> {A}", [A], A)
     rc, rep = report(lib_path, text, nvrtc=0)
     assert rc == 1 and "(0, 0) pair" in rep, rep
+
+
+@pytest.mark.parametrize("groups,ok", [("[[0, 1]]", True), ("[[1, 0]]", False), ("[[0], [1]]", False)])
+def test_collectives_across_processes_need_one_world_group(lib_path, groups, ok):
+    """The NCCL communicator spans all ranks in rank order: a program whose replica groups split
+    the ranks or reorder them is refused at compile time instead of running world-wide."""
+    p = configs.psum_program(1024, 2, with_inputs=False)
+    n = groups.count("[") - 1
+    text = p.text.replace("dense<[[0, 1]]> : tensor<1x2xi64>", f"dense<{groups}> : tensor<{n}x{2 // n}xi64>")
+    assert text != p.text or groups == "[[0, 1]]"
+    rc, rep = report(lib_path, text, nprocs=2)
+    if ok:
+        assert rc == 0 and "all_reduce" in rep, rep
+    else:
+        assert rc == 1 and "replica_groups" in rep, rep

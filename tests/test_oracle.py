@@ -136,3 +136,42 @@ def test_oracle_permute_broadcast_all_to_all():
     res = run_spmd(prog(a2a, 2), [[x] for x in xs])
     for dst in range(2):
         assert np.array_equal(res[dst][0], np.concatenate([xs[src][2 * dst:2 * dst + 2] for src in range(2)], axis=0))
+
+
+def _coll_prog(op_text, shape_in, shape_out):
+    ti, to = f"tensor<{shape_in}xf32>", f"tensor<{shape_out}xf32>"
+    return ("module @m {\n  func.func public @main(%arg0: " + ti + ") -> (" + to + ") {\n"
+            f"    %0 = {op_text} : ({ti}) -> {to}\n    return %0 : {to}\n  }}\n}}\n")
+
+
+ADD_REGION = ('({\n      ^bb0(%a: tensor<f32>, %b: tensor<f32>):\n        %s = stablehlo.add %a, %b : tensor<f32>\n'
+              '        stablehlo.return %s : tensor<f32>\n      })')
+
+
+def test_oracle_collectives_act_per_replica_group():
+    """StableHLO applies a collective within each replica group: the broadcast source is each
+    group's first member, all_reduce sums only within a group, all_gather concatenates in group
+    order, reduce_scatter hands the group's i-th part to its i-th member."""
+    xs = [np.full((4,), r + 1, np.float32) + np.arange(4, dtype=np.float32) for r in range(4)]
+    bcast = '"stablehlo.collective_broadcast"(%arg0) <{replica_groups = dense<[[1, 0]]> : tensor<1x2xi64>}>'
+    res = run_spmd(_coll_prog(bcast, "4", "4"), [[x] for x in xs[:2]])
+    assert all(np.array_equal(r[0], xs[1]) for r in res)
+    ar = ('"stablehlo.all_reduce"(%arg0) <{replica_groups = dense<[[0, 2], [1, 3]]> : tensor<2x2xi64>}> ' + ADD_REGION)
+    res = run_spmd(_coll_prog(ar, "4", "4"), [[x] for x in xs])
+    for r in range(4):
+        np.testing.assert_array_equal(res[r][0], xs[r % 2] + xs[r % 2 + 2])
+    ag = '"stablehlo.all_gather"(%arg0) <{all_gather_dim = 0 : i64, replica_groups = dense<[[1, 0], [3, 2]]> : tensor<2x2xi64>}>'
+    res = run_spmd(_coll_prog(ag, "4", "8"), [[x] for x in xs])
+    np.testing.assert_array_equal(res[0][0], np.concatenate([xs[1], xs[0]]))
+    np.testing.assert_array_equal(res[3][0], np.concatenate([xs[3], xs[2]]))
+    rs = ('"stablehlo.reduce_scatter"(%arg0) <{replica_groups = dense<[[1, 0]]> : tensor<1x2xi64>, scatter_dimension = 0 : i64}> '
+          + ADD_REGION)
+    res = run_spmd(_coll_prog(rs, "4", "2"), [[x] for x in xs[:2]])
+    np.testing.assert_array_equal(res[1][0], (xs[0] + xs[1])[:2])     # rank 1 is the group's member 0
+    np.testing.assert_array_equal(res[0][0], (xs[0] + xs[1])[2:])
+
+
+def test_oracle_rejects_groups_that_miss_a_rank():
+    ar = ('"stablehlo.all_reduce"(%arg0) <{replica_groups = dense<[[0, 1]]> : tensor<1x2xi64>}> ' + ADD_REGION)
+    with pytest.raises(ValueError):
+        run_spmd(_coll_prog(ar, "4", "4"), [[np.zeros(4, np.float32)] for _ in range(3)])

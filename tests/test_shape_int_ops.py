@@ -88,6 +88,10 @@ OTHER = {
     "dynamic_slice": (prog(f"    %0 = stablehlo.dynamic_slice %arg0, %arg1, %arg2, sizes = [4, 64] : "
                            f"({F}, tensor<i32>, tensor<i32>) -> {T('f32', (4, 64))}",
                            [F, "tensor<i32>", "tensor<i32>"], T("f32", (4, 64))), ["f32", "s", "s"]),
+    # unsigned 64-bit starts: 2^64 - 5 (from -5) is a large value and clamps to dim - window
+    "dynamic_slice_u64": (prog(f"    %0 = stablehlo.dynamic_slice %arg0, %arg1, %arg2, sizes = [4, 64] : "
+                               f"({F}, tensor<ui64>, tensor<ui64>) -> {T('f32', (4, 64))}",
+                               [F, "tensor<ui64>", "tensor<ui64>"], T("f32", (4, 64))), ["f32", "u", "u"]),
     "dynamic_update_slice": (prog(f"    %0 = stablehlo.dynamic_update_slice %arg0, %arg1, %arg2, %arg3 : "
                                   f"({F}, {T('f32', (4, 64))}, tensor<i32>, tensor<i32>) -> {F}",
                                   [F, T("f32", (4, 64)), "tensor<i32>", "tensor<i32>"], F), ["f32", "f32u", "s", "s"]),
@@ -109,6 +113,9 @@ def other_inputs(kinds, seed, starts=(3, 100)):
     for kind in kinds:
         if kind == "s":
             out.append(np.array(starts[k], np.int32))
+            k += 1
+        elif kind == "u":
+            out.append(np.array(starts[k] % 2 ** 64, np.uint64))
             k += 1
         elif kind == "f32u":
             out.append(rng.standard_normal((4, 64)).astype(np.float32) + 10)
@@ -172,6 +179,11 @@ def test_oracle_reduce_precision_erf_and_dynamic_slices():
         exp = ins[0].copy()
         exp[clamped[0]:clamped[0] + 4, clamped[1]:clamped[1] + 64] = ins[1]
         np.testing.assert_array_equal(r, exp)
+    # unsigned starts never count as negative: 2^64 - 5 clamps to the last window, 2^63 + 1 too
+    for starts, clamped in [((2 ** 64 - 5, 7), (4, 7)), ((1, 2 ** 63 + 1), (1, 64))]:
+        ins = other_inputs(OTHER["dynamic_slice_u64"][1], 5, starts)
+        r = oracle_run(OTHER["dynamic_slice_u64"][0], ins)[0]
+        np.testing.assert_array_equal(r, ins[0][clamped[0]:clamped[0] + 4, clamped[1]:clamped[1] + 64])
 
 
 @pytest.fixture(scope="module")
@@ -251,5 +263,5 @@ def test_shape_and_special_ops_vs_oracle(client, name):
             assert_close(got, ref, RTOL_BF16 if name == "erf_bf16" else RTOL_F32, name)
         else:
             np.testing.assert_array_equal(got, ref)
-        if "s" not in kinds:
+        if "s" not in kinds and "u" not in kinds:
             break
