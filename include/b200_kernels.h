@@ -14,6 +14,7 @@
 #ifndef B200_KERNELS_H_
 #define B200_KERNELS_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -34,6 +35,19 @@ extern "C" {
  * Replaces: DotGeneral's matmulWithPrimaryTensor, src/jam/ops/linalg.mm:47-105 (call at :98). */
 B200_API int b200_gemm(const void* A, const void* B, void* C, int64_t batch, int64_t M, int64_t N, int64_t K,
               int ab_type, int out_type, void* stream);
+
+/* f32-accurate C[b] = A[b] . B[b]^T on the bf16 tensor cores, for f32 operands or an f32 operand
+ * with a bf16 / f16 one (A [batch, M, K] of a_type, B [batch, N, K] of b_type, K contiguous; C
+ * [batch, M, N] of out_type).  Each f32 / f16 operand is split into three bf16 pieces that sum to it
+ * exactly; the product keeps the terms down to 2^-16 relative (six for two f32 operands, three for
+ * f32 x bf16) in one f32 accumulator: the f32 arithmetic of a dot_general, within the f32 bar
+ * (normwise 1e-5), at bf16 tensor-core throughput.  `scratch` (256-byte aligned device memory of
+ * b200_gemm_split_scratch_bytes(...) bytes) holds the pieces; A and B must be 16-byte aligned.  Returns 0, -1 (bad arguments), -4 (scratch too small or misaligned), or a launch
+ * failure code.
+ * Replaces: DotGeneral's matmul for f32 operands, src/jam/ops/linalg.mm:47-105 (call at :98). */
+B200_API size_t b200_gemm_split_scratch_bytes(int64_t batch, int64_t M, int64_t N, int64_t K, int a_type, int b_type);
+B200_API int b200_gemm_split(const void* A, int a_type, const void* B, int b_type, void* C, int64_t batch, int64_t M,
+                             int64_t N, int64_t K, int out_type, void* scratch, size_t scratch_bytes, void* stream);
 
 /* O = softmax(scale * Q K^T [causal mask]) V, fp32 softmax, for bf16 Q, K, V, O of shape [B, H, S, D]
  * (D contiguous), D = 64, S a multiple of 256.  Fused flash-style kernel on tcgen05; allocates nothing.
@@ -93,6 +107,17 @@ B200_API int b200_scatter_add_rows(const void* idx, const void* upd, void* out, 
 /* Returns and clears the first error code recorded by a bounded wait inside a tensor-core kernel on
  * the current device (0 = none).  Synchronizes the device. */
 B200_API int b200_take_device_error(void);
+
+/* Runs the tensor-core kernels' bounded mbarrier wait on a barrier whose arrival never comes, with a
+ * budget of `budget_cycles` SM clock cycles: the wait gives up, records its error code (1, a timed-out
+ * pipeline wait) for b200_take_device_error and the kernel returns, leaving the context usable.
+ * `waited_out` (device int, may be NULL) receives 1 when the wait gave up.  For tests of the timeout
+ * path; no counterpart in the reference.  Returns 0 or a launch failure code. */
+B200_API int b200_selftest_wait_timeout(long long budget_cycles, int* waited_out, void* stream);
+
+/* Number of kernel launches this library has issued since it was loaded: its hand-written kernels,
+ * the generated fusion kernels of PJRT executions, and the kernels of each CUDA-graph replay. */
+B200_API long long b200_kernel_launches(void);
 
 #ifdef __cplusplus
 }

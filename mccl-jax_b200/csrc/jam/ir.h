@@ -23,6 +23,18 @@ bool DTIsSigned(DT t);
 bool DTIsUnsigned(DT t);
 DT DTFromMlir(const std::string& s);
 
+// PJRT_Buffer_Type code of an element type as the kernel entry points take it (B200_DT_*), or -1.
+inline int KernelTypeCode(DT t) {
+  switch (t) {
+    case DT::kF32: return 11;
+    case DT::kBF16: return 13;
+    case DT::kF16: return 10;
+    case DT::kS32: return 4;
+    case DT::kS64: return 5;
+    default: return -1;
+  }
+}
+
 struct TensorType {
   DT dt = DT::kInvalid;
   std::vector<int64_t> dims;

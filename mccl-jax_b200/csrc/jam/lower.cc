@@ -22,10 +22,8 @@
 #include <unordered_set>
 
 #include "plan.h"
+#include "../kernels/kernels.h"
 
-namespace b200k {
-int GemmSplitK(int64_t batch, int64_t M, int64_t N, int64_t K, int sms);
-}
 
 namespace b200 {
 namespace {
@@ -1051,8 +1049,10 @@ class Lowerer {
   std::vector<std::set<int>> cons_;        // materialized consumers of each value
   std::unordered_map<int, DT> demote_;     // value id -> narrower type its buffer holds
 
-  // An f32 value read only by dots whose other operand is 16-bit is rounded to that type when the
-  // dot runs; its producing kernel stores it rounded instead (half the bytes, no conversion pass).
+  // An f32 value read only by dots whose other operand is 16-bit and whose result is 16-bit is
+  // rounded to that type when the dot runs (such a dot rounds its f32 operand once, an error of the
+  // size of its own result's rounding); its producing kernel stores it rounded instead (half the
+  // bytes, no conversion pass).  A dot with an f32 result keeps its f32 operand exact.
   void DecideStoredTypes() {
     if (std::getenv("B200_DOT_MIXED_F32")) return;
     std::unordered_set<int> outs;
@@ -1079,6 +1079,7 @@ class Lowerer {
         if (u->operands[0] == r && u->operands[1] == r) { ok = false; break; }
         DT t = other->type.dt;
         if (t != DT::kBF16 && t != DT::kF16) { ok = false; break; }
+        if (u->results.size() != 1 || u->result()->type.dt != t) { ok = false; break; }
         if (narrow != DT::kF32 && narrow != t) { ok = false; break; }
         narrow = t;
         std::vector<int64_t> bat, fr, ct;
@@ -3365,25 +3366,41 @@ class Lowerer {
     g.K = prod(a, lc);
     DT at = StoredDt(a), bt = StoredDt(b);
     if (!DTIsFloat(at) || !DTIsFloat(bt)) throw LowerError{"dot_general on non-float operands is not supported"};
-    // Operand type of the GEMM: both f32 (or f64) -> f32 SIMT (the f32 precision bar); otherwise a
-    // 16-bit type on the tensor cores.  A 16-bit operand times an f32 one (the cotangent of an f32
-    // dot result meeting bf16 weights in a backward pass) runs in the 16-bit type: the f32 operand is
-    // rounded once, the result keeps f32 accumulation (B200_DOT_MIXED_F32=1 keeps such dots in f32).
-    auto wide = [](DT t) { return t == DT::kF32 || t == DT::kF64; };
-    DT ab;
-    if (wide(at) && wide(bt)) ab = DT::kF32;
-    else if (!wide(at) && !wide(bt)) ab = at == bt ? at : DT::kBF16;
-    else ab = std::getenv("B200_DOT_MIXED_F32") ? DT::kF32 : (wide(at) ? bt : at);
-    if (ab != DT::kF16 && ab != DT::kBF16 && ab != DT::kF32) ab = DT::kF32;
-    g.ab = ab;
+    if (at == DT::kF64 || bt == DT::kF64) throw LowerError{"dot_general on f64 operands is not supported"};
     g.out = r->type.dt;
     if (g.out != DT::kF32 && g.out != DT::kBF16 && g.out != DT::kF16) throw LowerError{"dot_general result type not supported"};
+    // Arithmetic of the GEMM:
+    //  * two 16-bit operands: the tensor cores in that type (bf16 for a bf16 x f16 pair);
+    //  * an f32 operand with an f32 result: f32-accurate, each f32 operand split into three bf16
+    //    pieces on the tensor cores (b200k::GemmSplit) -- f32 x f32 when it is large enough to
+    //    gain from that, else the SIMT f32 kernel;
+    //  * an f32 operand with a 16-bit result and a 16-bit other operand (the cotangent of an f32 dot
+    //    result meeting bf16 weights in a backward pass): the f32 operand is rounded to the 16-bit
+    //    type once, an error of the size of the result's own rounding; B200_DOT_MIXED_F32=1 makes
+    //    these f32-accurate too.
+    auto wide = [](DT t) { return t == DT::kF32; };
+    DT ab;
+    bool split = false;
+    if (!wide(at) && !wide(bt)) {
+      ab = at == bt ? at : DT::kBF16;
+    } else if (wide(at) && wide(bt)) {
+      ab = DT::kF32;
+      split = (double)prod(a, lb) * prod(a, lf) * prod(b, rf) * prod(a, lc) >= (double)(1LL << 26) &&
+              !std::getenv("B200_GEMM_F32_SIMT");
+    } else if (g.out == DT::kF32 || std::getenv("B200_DOT_MIXED_F32")) {
+      ab = DT::kF32;
+      split = true;
+    } else {
+      ab = wide(at) ? bt : at;
+    }
+    g.ab = ab;
+    g.split = split;
     // Each operand is used where it lies when its dims are [batch, rows, K] (K-major) or [batch, K,
     // rows] (MN-major) in order; otherwise it is copied K-major.  The tensor cores read either form
     // through TMA, which needs 16-byte row strides: rows % 8 == 0 for MN-major, and a 16-bit K-major
     // copy with K % 8 != 0 gets a padded pitch.
     const bool tc = ab != DT::kF32;
-    struct Opnd { int slot; bool mn; int64_t ld; };
+    struct Opnd { int slot; bool mn; int64_t ld; DT dt; };
     auto identity = [](const std::vector<int64_t>& o) {
       for (size_t k = 0; k < o.size(); ++k) if (o[k] != (int64_t)k) return false;
       return true;
@@ -3399,22 +3416,31 @@ class Lowerer {
       const DT held = StoredDt(v);
       if (const int64_t p = StoredPitch(v)) {      // stored with a padded pitch for exactly this use
         const std::vector<int64_t> last{v->type.rank() - 1};
-        if (identity(kord) && ct == last) return {SlotFor(v), false, p};
-        if (identity(mord) && fr == last) return {SlotFor(v), true, p};
+        if (identity(kord) && ct == last) return {SlotFor(v), false, p, held};
+        if (identity(mord) && fr == last) return {SlotFor(v), true, p, held};
         throw LowerError{"internal: padded operand used out of place"};
       }
-      if (identity(kord) && held == ab && !(tc && g.K % 8)) return {SlotFor(v), false, g.K};
+      if (split) {
+        // the split kernel reads either form in its stored type (f32 / bf16 / f16)
+        if (identity(kord)) return {SlotFor(v), false, g.K, held};
+        if (identity(mord)) return {SlotFor(v), true, rows, held};
+        std::vector<int> perm(kord.begin(), kord.end());
+        std::vector<int64_t> od;
+        for (int q : perm) od.push_back(v->type.dims[q]);
+        return {EmitPermute(v, perm, od, held), false, g.K, held};
+      }
+      if (identity(kord) && held == ab && !(tc && g.K % 8)) return {SlotFor(v), false, g.K, held};
       if (identity(mord) && (!tc || rows % 8 == 0) && !std::getenv("B200_GEMM_NO_MN")) {
-        if (held == ab) return {SlotFor(v), true, rows};
+        if (held == ab) return {SlotFor(v), true, rows, held};
         std::vector<int> same(v->type.rank());
         for (int k = 0; k < v->type.rank(); ++k) same[k] = k;
-        return {EmitPermute(v, same, v->type.dims, ab), true, rows};   // convert only
+        return {EmitPermute(v, same, v->type.dims, ab), true, rows, ab};   // convert only
       }
       const int64_t pitch = (tc && g.K % 8 != 0) ? (g.K + 7) / 8 * 8 : 0;
       std::vector<int> perm(kord.begin(), kord.end());
       std::vector<int64_t> od;
       for (int q : perm) od.push_back(v->type.dims[q]);
-      return {EmitPermute(v, perm, od, ab, pitch), false, pitch ? pitch : g.K};
+      return {EmitPermute(v, perm, od, ab, pitch), false, pitch ? pitch : g.K, ab};
     };
     Opnd oa = operand(a, lb, lf, lc, g.M), ob = operand(b, rb, rf, rc, g.N);
     g.a = oa.slot;
@@ -3423,22 +3449,34 @@ class Lowerer {
     g.b = ob.slot;
     g.b_mn = ob.mn;
     g.ldb = ob.ld;
-    const bool split = tc && g.out != DT::kF32 && !StoredPitch(r) && b200k::GemmSplitK(g.batch, g.M, g.N, g.K, 148) > 1;
-    if (split && PromotableToF32(r)) {           // readers round the f32 partial sums themselves
+    g.a_dt = oa.dt;
+    g.b_dt = ob.dt;
+    const bool split_k = tc && g.out != DT::kF32 && !StoredPitch(r) && b200k::GemmSplitK(g.batch, g.M, g.N, g.K, 148) > 1;
+    if (split_k && PromotableToF32(r)) {         // readers round the f32 partial sums themselves
       promote_.insert(r->id);
       g.out = DT::kF32;
     }
     g.c = SlotFor(r);
     g.ldc = StoredPitch(r);                      // 0: dense rows of N
-    if (split && g.out != DT::kF32) {
+    if (split_k && g.out != DT::kF32) {
       g.ws = NewSlot(g.batch * g.M * g.N * 4);   // split-K partial sums
       RecordDt(g.ws, DT::kF32);
+    }
+    if (split) {                                 // bf16 pieces of the f32 operands
+      const size_t bytes = b200k::GemmSplitScratchBytes(g.batch, g.M, g.N, g.K, KernelTypeCode(g.a_dt), KernelTypeCode(g.b_dt),
+                                                        g.a_mn, g.b_mn, g.lda, g.ldb);
+      if (bytes) {
+        g.split_ws = NewSlot((int64_t)bytes);
+        g.split_ws_bytes = (int64_t)bytes;
+        RecordDt(g.split_ws, DT::kBF16);
+      }
     }
     Step st;
     st.kind = StepKind::kGemm;
     st.gemm = g;
     st.label = "gemm b" + std::to_string(g.batch) + " " + std::to_string(g.M) + "x" + std::to_string(g.N) + "x" + std::to_string(g.K) +
-               (g.a_mn || g.b_mn ? std::string(" ") + (g.a_mn ? "m" : "k") + (g.b_mn ? "n" : "k") : "");
+               (g.a_mn || g.b_mn ? std::string(" ") + (g.a_mn ? "m" : "k") + (g.b_mn ? "n" : "k") : "") +
+               (g.split ? " f32-split" : g.ab == DT::kF32 ? " f32-simt" : "");
     p_->steps.push_back(st);
     RecordDt(g.c, StoredDt(r));
   }
@@ -3593,7 +3631,7 @@ class Lowerer {
           W({L.scratch});
         }
         break;
-      case StepKind::kGemm: R({S.gemm.a, S.gemm.b}); W({S.gemm.c, S.gemm.ws}); break;
+      case StepKind::kGemm: R({S.gemm.a, S.gemm.b}); W({S.gemm.c, S.gemm.ws, S.gemm.split_ws}); break;
       case StepKind::kAttention: R({S.attn.q, S.attn.k, S.attn.v}); W({S.attn.o, S.attn.lse}); break;
       case StepKind::kAttentionBwd:
         R({S.bwd.q, S.bwd.k, S.bwd.v, S.bwd.o, S.bwd.dout, S.bwd.lse});
@@ -3794,7 +3832,9 @@ class Lowerer {
             touch(L.scratch, i);
           }
           break;
-        case StepKind::kGemm: touch(st.gemm.a, i); touch(st.gemm.b, i); touch(st.gemm.c, i); touch(st.gemm.ws, i); break;
+        case StepKind::kGemm:
+          touch(st.gemm.a, i); touch(st.gemm.b, i); touch(st.gemm.c, i); touch(st.gemm.ws, i); touch(st.gemm.split_ws, i);
+          break;
         case StepKind::kAttention:
           touch(st.attn.q, i); touch(st.attn.k, i); touch(st.attn.v, i); touch(st.attn.o, i); touch(st.attn.lse, i);
           break;

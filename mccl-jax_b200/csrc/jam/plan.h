@@ -44,6 +44,12 @@ struct GemmStep {
   bool a_mn = false, b_mn = false;  // operand stored MN-major: A[batch,K,M] / B[batch,K,N], pitch M / N
   int ws = -1;                 // f32 [batch,M,N] workspace when a 16-bit result is computed split-K
   DT ab = DT::kBF16, out = DT::kF32;
+  // f32-accurate product of f32 operands on the tensor cores (b200k::GemmSplit): the operands keep
+  // their stored types a_dt / b_dt; split_ws holds their bf16 pieces
+  bool split = false;
+  DT a_dt = DT::kBF16, b_dt = DT::kBF16;
+  int split_ws = -1;
+  int64_t split_ws_bytes = 0;
 };
 
 struct AttentionStep {

@@ -18,20 +18,8 @@
 
 #include "../../../include/b200_kernels.h"
 #include "../comm/comm.h"
+#include "../kernels/kernels.h"
 
-namespace b200k {
-int Gemm(const void* A, long long lda, const void* B, long long ldb, void* C, int64_t batch, int64_t M, int64_t N,
-         int64_t K, int ab_type, int out_type, cudaStream_t st);
-int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C, int64_t batch, int64_t M,
-         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st, float* ws, int64_t ldc);
-int AttentionFwd(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D, int causal, float scale,
-                 cudaStream_t st);
-int AttentionFwdLse(const void* q, const void* k, const void* v, void* o, float* lse2, int B, int H, int S, int D,
-                    int causal, float scale, cudaStream_t st);
-int AttentionBwd(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse2,
-                 void* dq, void* dk, void* dv, float* dq_acc, float* delta, int B, int H, int S, int D, int causal,
-                 float scale, cudaStream_t st, int dk_t);
-}
 
 namespace b200 {
 namespace {
@@ -100,16 +88,7 @@ std::string Nvrtc(const std::string& src, std::vector<char>* cubin) {
   return "";
 }
 
-int PjrtType(DT t) {
-  switch (t) {
-    case DT::kF32: return B200_DT_F32;
-    case DT::kBF16: return B200_DT_BF16;
-    case DT::kF16: return B200_DT_F16;
-    case DT::kS32: return B200_DT_S32;
-    case DT::kS64: return B200_DT_S64;
-    default: return -1;
-  }
-}
+int PjrtType(DT t) { return KernelTypeCode(t); }
 
 struct StepTimer {
   bool on = std::getenv("B200_TIME") != nullptr;
@@ -245,7 +224,7 @@ static void StepSlots(const Step& S, std::vector<int>* out) {
         add({L.scratch});
       }
       break;
-    case StepKind::kGemm: add({S.gemm.a, S.gemm.b, S.gemm.c, S.gemm.ws}); break;
+    case StepKind::kGemm: add({S.gemm.a, S.gemm.b, S.gemm.c, S.gemm.ws, S.gemm.split_ws}); break;
     case StepKind::kAttention: add({S.attn.q, S.attn.k, S.attn.v, S.attn.o, S.attn.lse}); break;
     case StepKind::kAttentionBwd:
       add({S.bwd.q, S.bwd.k, S.bwd.v, S.bwd.o, S.bwd.dout, S.bwd.lse, S.bwd.dq, S.bwd.dk, S.bwd.dv, S.bwd.dq_acc, S.bwd.delta});
@@ -448,6 +427,7 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     if (ge && ge->exec) {
       if (cudaGraphLaunch(ge->exec, st) != cudaSuccess) return fail("graph launch failed");
       g_graph_launches.fetch_add(1);
+      b200k::CountLaunches(ge->kernels);
       ge->last = ++pd->graph_clock;
       outs->clear();
       for (int s : P.out_slots) outs->push_back(ptr[s]);
@@ -537,15 +517,20 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
                              L.smem, (CUstream)st, params.data(), nullptr);
             }
             if (r != CUDA_SUCCESS) return fail("launch of " + L.fn + " failed (" + std::to_string((int)r) + ")");
+            b200k::CountLaunches();
           }
           break;
         }
         case StepKind::kGemm: {
           const GemmStep& g = S.gemm;
-          for (int s : {g.a, g.b, g.c, g.ws}) { err = slot(s); if (!err.empty()) return fail(err); }
-          int rc = b200k::Gemm(ptr[g.a], g.lda ? g.lda : (g.a_mn ? g.M : g.K), g.a_mn, ptr[g.b], g.ldb ? g.ldb : (g.b_mn ? g.N : g.K),
-                               g.b_mn, ptr[g.c], g.batch, g.M, g.N,
-                               g.K, PjrtType(g.ab), PjrtType(g.out), st, g.ws >= 0 ? (float*)ptr[g.ws] : nullptr, g.ldc);
+          for (int s : {g.a, g.b, g.c, g.ws, g.split_ws}) { err = slot(s); if (!err.empty()) return fail(err); }
+          const long long lda = g.lda ? g.lda : (g.a_mn ? g.M : g.K), ldb = g.ldb ? g.ldb : (g.b_mn ? g.N : g.K);
+          int rc = g.split
+              ? b200k::GemmSplit(ptr[g.a], lda, g.a_mn, PjrtType(g.a_dt), ptr[g.b], ldb, g.b_mn, PjrtType(g.b_dt), ptr[g.c],
+                                 g.batch, g.M, g.N, g.K, PjrtType(g.out), st, g.split_ws >= 0 ? ptr[g.split_ws] : nullptr,
+                                 (size_t)g.split_ws_bytes, g.ldc)
+              : b200k::Gemm(ptr[g.a], lda, g.a_mn, ptr[g.b], ldb, g.b_mn, ptr[g.c], g.batch, g.M, g.N, g.K, PjrtType(g.ab),
+                            PjrtType(g.out), st, g.ws >= 0 ? (float*)ptr[g.ws] : nullptr, g.ldc);
           if (rc != 0) return fail("gemm launch failed (" + std::to_string(rc) + ") for " + S.label);
           break;
         }
@@ -617,8 +602,10 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     }
     return std::string();
   };
+  const long long launches0 = b200k::g_kernel_launches.load();
   err = run_steps();
   if (!err.empty()) return err;
+  if (capture) ge->kernels = b200k::g_kernel_launches.load() - launches0;
   if (capture) {
     end_capture();
     if (ge->exec) {

@@ -48,6 +48,7 @@ class Executable {
     cudaGraphExec_t exec = nullptr;          // null until the second execution with these addresses
     uint64_t last = 0;
     bool no_graph = false;                   // capture failed once: run eagerly
+    long long kernels = 0;                   // kernel launches the captured execution recorded
   };
   struct PerDevice {
     std::vector<void*> modules;              // CUmodule per NVRTC group

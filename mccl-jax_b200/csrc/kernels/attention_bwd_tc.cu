@@ -28,6 +28,7 @@
 #include <cuda_bf16.h>
 #include <mutex>
 
+#include "kernels.h"
 #include "tc_common.cuh"
 #include "../../../include/b200_kernels.h"
 
@@ -478,6 +479,7 @@ int AttentionBwd(const void* q, const void* k, const void* v, const void* o, con
   if (cudaMemsetAsync(dq_acc, 0, (size_t)rows * HD * 4, st) != cudaSuccess) return -3;
   attn_bwd_delta_kernel<<<(unsigned)std::min<long long>((rows + 31) / 32, 148 * 8), 256, 0, st>>>(
       (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, delta, rows);
+  CountLaunches();
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid((unsigned)(B * H * (S / TB)));
   if (causal)
@@ -486,10 +488,13 @@ int AttentionBwd(const void* q, const void* k, const void* v, const void* o, con
   else
     attn_bwd_kernel<false><<<grid, kThreads, C::kSmem, st>>>(mq, mk, mv, mdo, mdq, lse2, delta, dq_acc, (__nv_bfloat16*)dk,
                                                          (__nv_bfloat16*)dv, S, scale, scale_log2, dk_t);
+  CountLaunches();
   // dq null: the caller reads dQ (rounding it itself) from the f32 accumulator
   const long long n4 = rows * HD / 4;
-  if (dq)
+  if (dq) {
     f32_to_bf16_kernel<<<(unsigned)std::min<long long>((n4 + 255) / 256, 148 * 8), 256, 0, st>>>(dq_acc, (__nv_bfloat16*)dq, n4);
+    CountLaunches();
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

@@ -25,6 +25,7 @@
 #include <cuda_bf16.h>
 #include <mutex>
 
+#include "kernels.h"
 #include "tc_common.cuh"
 #include "../../../include/b200_kernels.h"
 
@@ -439,6 +440,7 @@ static int LaunchAttn(const void* q, const void* k, const void* v, void* o, int 
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid((unsigned)(B * H * (S / (2 * TQ))));
   attn_fwd_kernel<D, CAUSAL, VT><<<grid, 320, Cf::kSmem, st>>>(mq, mk, mv, (__nv_bfloat16*)o, lse2, H, S, scale_log2);
+  CountLaunches();
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -476,6 +478,7 @@ int AttentionFwdWithVt(const void* q, const void* k, const void* v, void* vt, vo
   if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)vt | (uintptr_t)o) % 16) return -1;
   dim3 tg(S / 64, D / 64, B * H);
   transpose_v_kernel<<<tg, 256, 0, st>>>((const uint16_t*)v, (uint16_t*)vt, S, D);
+  CountLaunches();
   if (causal) return LaunchAttn<64, true, true>(q, k, vt, o, B, H, S, scale, st);
   return LaunchAttn<64, false, true>(q, k, vt, o, B, H, S, scale, st);
 }

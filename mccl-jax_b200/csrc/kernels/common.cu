@@ -6,9 +6,13 @@
 
 #include <mutex>
 
+#include "kernels.h"
+#include "tc_common.cuh"
 #include "../../../include/b200_kernels.h"
 
 namespace b200k {
+
+std::atomic<long long> g_kernel_launches{0};
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -29,9 +33,26 @@ EncodeTiledFn GetEncodeTiled() {
   return fn;
 }
 
-int TakeGemmError();
-int TakeAttnError();
-int TakeAttnBwdError();
+static __device__ int g_tc_error_selftest;
+
+// The bounded mbarrier wait of the tensor-core kernels, run on a barrier whose one expected arrival
+// never comes: after `budget` cycles the wait gives up, records kErrTimeoutFull in the device flag
+// and the kernel returns (the recovery path every pipeline wait takes).
+__global__ void wait_timeout_selftest_kernel(long long budget, int* waited_out) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  const bool ok = mbar_wait_budget(&bar, 0, kErrTimeoutFull, &g_tc_error_selftest, budget);
+  if (waited_out) *waited_out = ok ? 0 : 1;
+}
+
+static int TakeSelftestError() {
+  int v = 0, z = 0;
+  cudaMemcpyFromSymbol(&v, g_tc_error_selftest, sizeof(int));
+  if (v) cudaMemcpyToSymbol(g_tc_error_selftest, &z, sizeof(int));
+  return v;
+}
 
 template <typename T, typename I>
 __global__ void __launch_bounds__(256) scatter_add_rows_kernel(const I* __restrict__ idx, const T* __restrict__ upd, T* __restrict__ out,
@@ -52,8 +73,18 @@ extern "C" int b200_take_device_error(void) {
   int e = b200k::TakeGemmError();
   int a = b200k::TakeAttnError();
   int b = b200k::TakeAttnBwdError();
-  return e ? e : a ? a : b;
+  int t = b200k::TakeSelftestError();
+  return e ? e : a ? a : b ? b : t;
 }
+
+extern "C" int b200_selftest_wait_timeout(long long budget_cycles, int* waited_out, void* stream) {
+  if (budget_cycles <= 0) return -1;
+  b200k::wait_timeout_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(budget_cycles, waited_out);
+  b200k::CountLaunches();
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+extern "C" long long b200_kernel_launches(void) { return b200k::g_kernel_launches.load(); }
 
 extern "C" int b200_scatter_add_rows(const void* idx, const void* upd, void* out, int64_t n_upd, int64_t row_len,
                                      int64_t rows, int dtype, int idx_type, void* stream) {
@@ -71,5 +102,6 @@ extern "C" int b200_scatter_add_rows(const void* idx, const void* upd, void* out
     b200k::scatter_add_rows_kernel<__nv_bfloat16, long long><<<grid, block, 0, st>>>((const long long*)idx, (const __nv_bfloat16*)upd, (__nv_bfloat16*)out, n_upd, row_len, rows);
   else
     return -1;
+  b200k::CountLaunches();
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

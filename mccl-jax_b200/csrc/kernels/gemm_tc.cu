@@ -20,6 +20,7 @@
 #include <mutex>
 #include <type_traits>
 
+#include "kernels.h"
 #include "tc_common.cuh"
 #include "../../../include/b200_kernels.h"
 
@@ -87,7 +88,8 @@ template <int BN, int OUT, bool AMN, bool BMN>
 __global__ void __launch_bounds__(192, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, void* __restrict__ C, int M, int N, int K, int batch, int fmt,
-               int splits, float* __restrict__ ws, int tma_store, long long ldc) {
+               int splits, float* __restrict__ ws, int tma_store, long long ldc, int terms, uint32_t piece_a,
+               uint32_t piece_b) {
   using CF = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -101,7 +103,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mb = (M + BM - 1) / BM, nb = (N + BN - 1) / BN;
   const int per_batch = mb * nb, num_tiles = per_batch * batch;
-  const int kbs = (K + BK - 1) / BK;
+  // `terms` products accumulate into one result (the f32-accurate split form; 1 otherwise): term t
+  // reads A's K piece (piece_a >> 4t) & 15 and B's (piece_b >> 4t) & 15, pieces sitting kbt K
+  // blocks apart along K.  The K loop runs over terms x kbt blocks.
+  const int kbt = (K + BK - 1) / BK;
+  const int kbs = kbt * terms;
   // split-K: work unit u = (tile u / splits, K slice u % splits); slices are non-empty by construction
   // (host side), partial sums go to the f32 workspace through atomics
   const int kps = (kbs + splits - 1) / splits;
@@ -143,18 +149,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (!mbar_wait(&empty[s], ph ^ 1, kErrTimeoutEmpty, &g_tc_error_gemm)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], CF::kStage);
           uint8_t* sa = smem + s * CF::kStage;
+          const int term = kb / kbt, kk = (kb - term * kbt) * BK;
+          const int ka = (int)((piece_a >> (4 * term)) & 15u) * kbt * BK + kk;
+          const int kb_ = (int)((piece_b >> (4 * term)) & 15u) * kbt * BK + kk;
           if (AMN) {
 #pragma unroll
-            for (int i = 0; i < BM / 64; ++i) tma_load_3d(&tmA, &full[s], sa + i * 8192, m_blk * BM + 64 * i, kb * BK, b);
+            for (int i = 0; i < BM / 64; ++i) tma_load_3d(&tmA, &full[s], sa + i * 8192, m_blk * BM + 64 * i, ka, b);
           } else {
-            tma_load_3d(&tmA, &full[s], sa, kb * BK, m_blk * BM, b);
+            tma_load_3d(&tmA, &full[s], sa, ka, m_blk * BM, b);
           }
           if (BMN) {
 #pragma unroll
             for (int i = 0; i < BN / 64; ++i)
-              tma_load_3d(&tmB, &full[s], sa + CF::kABytes + i * 8192, n_blk * BN + 64 * i, kb * BK, b);
+              tma_load_3d(&tmB, &full[s], sa + CF::kABytes + i * 8192, n_blk * BN + 64 * i, kb_, b);
           } else {
-            tma_load_3d(&tmB, &full[s], sa + CF::kABytes, kb * BK, n_blk * BN, b);
+            tma_load_3d(&tmB, &full[s], sa + CF::kABytes, kb_, n_blk * BN, b);
           }
           issued |= 1u << s;
           fill_par = (fill_par & ~(1u << s)) | (ph << s);
@@ -477,9 +486,17 @@ int NumSMs() {
   return n;
 }
 
+// Operand K extents of the tensor maps and the term table of a launch (see gemm_tc_kernel): plain
+// products read one piece per operand whose map spans K; the split form reads pieces side by side.
+struct Terms {
+  int n = 1;
+  uint32_t a = 0, b = 0;     // 4 bits per term: the piece index of A / B
+  long long ka = -1, kb = -1;  // K extent of A's / B's map (-1: K)
+};
+
 template <int BN, int OUT, bool AMN, bool BMN>
 static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, void* C, int batch, int M, int N, int K,
-                    int fmt, cudaStream_t st, int splits, float* ws, long long ldc) {
+                    int fmt, cudaStream_t st, int splits, float* ws, long long ldc, const Terms& tm) {
   using CF = Cfg<BN>;
   static std::once_flag once[8];
   int dev = 0;
@@ -488,8 +505,9 @@ static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, 
     cudaFuncSetAttribute(gemm_tc_kernel<BN, OUT, AMN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kSmem);
   });
   CUtensorMap ta, tb, tc;
-  bool ok = AMN ? MakeOperandMapMN(&ta, A, K, lda, M, batch, fmt == 0) : MakeOperandMap(&ta, A, K, lda, M, batch, BM, fmt == 0);
-  ok = ok && (BMN ? MakeOperandMapMN(&tb, B, K, ldb, N, batch, fmt == 0) : MakeOperandMap(&tb, B, K, ldb, N, batch, BN, fmt == 0));
+  const int ka = tm.ka < 0 ? K : (int)tm.ka, kb = tm.kb < 0 ? K : (int)tm.kb;
+  bool ok = AMN ? MakeOperandMapMN(&ta, A, ka, lda, M, batch, fmt == 0) : MakeOperandMap(&ta, A, ka, lda, M, batch, BM, fmt == 0);
+  ok = ok && (BMN ? MakeOperandMapMN(&tb, B, kb, ldb, N, batch, fmt == 0) : MakeOperandMap(&tb, B, kb, ldb, N, batch, BN, fmt == 0));
   if (!ok) return -2;
   // TMA-store epilogue when C's rows are 16-byte multiples (else the bounds-checked staged path);
   // split-K partials go to the f32 workspace by TMA reduce-add under the same condition
@@ -504,17 +522,20 @@ static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, 
   if (!tma_store) tc = ta;                                  // unused
   int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
   int grid = std::min(tiles * splits, NumSMs());
-  gemm_tc_kernel<BN, OUT, AMN, BMN><<<grid, 192, CF::kSmem, st>>>(ta, tb, tc, C, M, N, K, batch, fmt, splits, ws, tma_store, ldc);
+  gemm_tc_kernel<BN, OUT, AMN, BMN><<<grid, 192, CF::kSmem, st>>>(ta, tb, tc, C, M, N, K, batch, fmt, splits, ws, tma_store, ldc,
+                                                                   tm.n, tm.a, tm.b);
+  CountLaunches();
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
 template <int BN, int OUT>
 static int LaunchTcMajor(bool amn, bool bmn, const void* A, long long lda, const void* B, long long ldb, void* C, int batch,
-                         int M, int N, int K, int fmt, cudaStream_t st, int splits, float* ws, long long ldc) {
-  if (amn && bmn) return LaunchTc<BN, OUT, true, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc);
-  if (amn) return LaunchTc<BN, OUT, true, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc);
-  if (bmn) return LaunchTc<BN, OUT, false, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc);
-  return LaunchTc<BN, OUT, false, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc);
+                         int M, int N, int K, int fmt, cudaStream_t st, int splits, float* ws, long long ldc,
+                         const Terms& tm) {
+  if (amn && bmn) return LaunchTc<BN, OUT, true, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm);
+  if (amn) return LaunchTc<BN, OUT, true, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm);
+  if (bmn) return LaunchTc<BN, OUT, false, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm);
+  return LaunchTc<BN, OUT, false, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm);
 }
 
 __global__ void __launch_bounds__(256) ws_to_16bit_kernel(const float* __restrict__ ws, uint16_t* __restrict__ c, long long n,
@@ -530,6 +551,7 @@ static int LaunchSimtT(const void* A, long long lda, const void* B, long long ld
   if (out == 0) gemm_simt_kernel<T, 0, AMN, BMN><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K, lda, ldb);
   else if (out == 1) gemm_simt_kernel<T, 1, AMN, BMN><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K, lda, ldb);
   else gemm_simt_kernel<T, 2, AMN, BMN><<<grid, 256, 0, st>>>((const T*)A, (const T*)B, C, M, N, K, lda, ldb);
+  CountLaunches();
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -591,6 +613,41 @@ int GemmSplitK(int64_t batch, int64_t M, int64_t N, int64_t K, int sms) {
   return s;
 }
 
+// Runs one tensor-core launch (tile width and K slices from the wave model over `k_eff` = the K
+// blocks every output tile walks), plus the split-K zeroing and rounding passes.
+static int RunTc(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C, int64_t batch,
+                 int64_t M, int64_t N, int64_t K, int64_t k_eff, int fmt, int out, cudaStream_t st, float* ws, int64_t ldc,
+                 const Terms& tm) {
+  int b = (int)batch, m = (int)M, n = (int)N, k = (int)K;
+  int bn = 256, splits = 1;
+  GemmTile(batch, M, N, k_eff, NumSMs(), &bn, &splits);
+  if (ldc != N) splits = 1;                  // partial sums are laid out densely
+  float* acc = out == 0 ? (float*)C : ws;
+  if (splits > 1 && !acc) splits = 1;
+  if (splits > 1 && cudaMemsetAsync(acc, 0, (size_t)batch * M * N * 4, st) != cudaSuccess) return -3;
+  auto launch = [&](auto out_c) {
+    constexpr int O = decltype(out_c)::value;
+    if (bn == 256) return LaunchTcMajor<256, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm);
+    if (bn == 192) return LaunchTcMajor<192, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm);
+    return LaunchTcMajor<128, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm);
+  };
+  int rc = out == 0 ? launch(std::integral_constant<int, 0>{})
+         : out == 1 ? launch(std::integral_constant<int, 1>{})
+                    : launch(std::integral_constant<int, 2>{});
+  if (rc == 0 && splits > 1 && out != 0) {
+    const long long total = (long long)batch * M * N;
+    ws_to_16bit_kernel<<<(unsigned)std::min<long long>((total + 255) / 256, 148 * 8), 256, 0, st>>>(acc, (uint16_t*)C, total,
+                                                                                                   out == 2);
+    CountLaunches();
+    rc = cudaGetLastError() == cudaSuccess ? 0 : -3;
+  }
+  return rc;
+}
+
+static int OutCode(int out_type) {
+  return out_type == B200_DT_F32 ? 0 : out_type == B200_DT_BF16 ? 1 : out_type == B200_DT_F16 ? 2 : -1;
+}
+
 // C[b] = A[b] . B[b]^T.  A is [batch, M, >=K] (K-major, row pitch lda) or, with a_mn, [batch, K, >=M]
 // (MN-major, pitch lda); B likewise with N, ldb and b_mn.  With `ws` (batch*M*N f32) a 16-bit result
 // may be computed split-K (partials added into ws, then rounded into C); an f32 result splits without
@@ -602,7 +659,7 @@ int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, 
   if (ldc < N) return -1;
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || batch > 65535 || lda < (a_mn ? M : K) || ldb < (b_mn ? N : K))
     return -1;
-  int out = out_type == B200_DT_F32 ? 0 : out_type == B200_DT_BF16 ? 1 : out_type == B200_DT_F16 ? 2 : -1;
+  const int out = OutCode(out_type);
   if (out < 0) return -1;
   if (K == 0) {
     size_t bytes = (size_t)batch * M * ldc * (out == 0 ? 4 : 2);
@@ -610,32 +667,8 @@ int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, 
   }
   bool tc_ok = (ab_type == B200_DT_BF16 || ab_type == B200_DT_F16) && (lda % 8) == 0 && (ldb % 8) == 0 &&
                ((uintptr_t)A % 16) == 0 && ((uintptr_t)B % 16) == 0 && !getenv("B200_GEMM_SIMT");
-  if (tc_ok) {
-    int fmt = ab_type == B200_DT_BF16 ? 1 : 0;
-    int b = (int)batch, m = (int)M, n = (int)N, k = (int)K;
-    int bn = 256, splits = 1;
-    GemmTile(batch, M, N, K, NumSMs(), &bn, &splits);
-    if (ldc != N) splits = 1;                  // partial sums are laid out densely
-    float* acc = out == 0 ? (float*)C : ws;
-    if (splits > 1 && !acc) splits = 1;
-    if (splits > 1 && cudaMemsetAsync(acc, 0, (size_t)batch * M * N * 4, st) != cudaSuccess) return -3;
-    auto launch = [&](auto out_c) {
-      constexpr int O = decltype(out_c)::value;
-      if (bn == 256) return LaunchTcMajor<256, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc);
-      if (bn == 192) return LaunchTcMajor<192, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc);
-      return LaunchTcMajor<128, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc);
-    };
-    int rc = out == 0 ? launch(std::integral_constant<int, 0>{})
-           : out == 1 ? launch(std::integral_constant<int, 1>{})
-                      : launch(std::integral_constant<int, 2>{});
-    if (rc == 0 && splits > 1 && out != 0) {
-      const long long total = (long long)batch * M * N;
-      ws_to_16bit_kernel<<<(unsigned)std::min<long long>((total + 255) / 256, 148 * 8), 256, 0, st>>>(acc, (uint16_t*)C, total,
-                                                                                                     out == 2);
-      rc = cudaGetLastError() == cudaSuccess ? 0 : -3;
-    }
-    return rc;
-  }
+  if (tc_ok)
+    return RunTc(A, lda, a_mn, B, ldb, b_mn, C, batch, M, N, K, K, ab_type == B200_DT_BF16 ? 1 : 0, out, st, ws, ldc, Terms{});
   int b = (int)batch, m = (int)M, n = (int)N, k = (int)K;
   if (ldc != N) return -1;                     // padded C rows are written by the tensor-core path only
   if (ab_type == B200_DT_F32) return LaunchSimt<float>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, out, st);
@@ -644,19 +677,160 @@ int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, 
   return -1;
 }
 
-int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C, int64_t batch, int64_t M,
-         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st, float* ws) {
-  return Gemm(A, lda, a_mn, B, ldb, b_mn, C, batch, M, N, K, ab_type, out_type, st, ws, 0);
-}
-
-int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C, int64_t batch, int64_t M,
-         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st) {
-  return Gemm(A, lda, a_mn, B, ldb, b_mn, C, batch, M, N, K, ab_type, out_type, st, nullptr, 0);
-}
-
 int Gemm(const void* A, long long lda, const void* B, long long ldb, void* C, int64_t batch, int64_t M, int64_t N,
          int64_t K, int ab_type, int out_type, cudaStream_t st) {
-  return Gemm(A, lda, false, B, ldb, false, C, batch, M, N, K, ab_type, out_type, st, nullptr);
+  return Gemm(A, lda, false, B, ldb, false, C, batch, M, N, K, ab_type, out_type, st, nullptr, 0);
+}
+
+// ---------------------------------------------------------------------------- f32-accurate products
+namespace {
+
+__device__ __forceinline__ float load_as_f32(const float* p) { return *p; }
+__device__ __forceinline__ float load_as_f32(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ float load_as_f32(const __half* p) { return __half2float(*p); }
+
+// bf16 pieces of an operand: element (b, k, r) of the logical [batch, K, rows] operand (src stored
+// K-major [batch, rows, ld] or, with src_mn, MN-major [batch, K, ld]) gives `pieces` bf16 values
+// h_j = bf16_rn(x - h_0 - ... - h_{j-1}) (each difference exact in f32), written to
+//   dst_mn = 0: dst[b][r][j * Kp + k]      (K-major, pieces side by side along K)
+//   dst_mn = 1: dst[b][j * Kp + k][r]      (MN-major)
+// with zeros for k in [K, Kp).  Threads walk the destination (coalesced stores), 4 elements each.
+template <typename T>
+__global__ void __launch_bounds__(256) split_pieces_kernel(const T* __restrict__ src, long long ld, int src_mn, int dst_mn,
+                                                           int batch, int rows, int K, int Kp, int pieces,
+                                                           uint16_t* __restrict__ dst) {
+  const long long outer = dst_mn ? (long long)pieces * Kp : rows;      // destination rows per batch
+  const long long inner = dst_mn ? rows : (long long)pieces * Kp;      // destination row length
+  const long long quads = inner / 4;                                   // inner % 4 == 0 (host-checked)
+  const long long total = (long long)batch * outer * quads;
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x) {
+    const long long q = e % quads, t = e / quads;
+    const long long o = t % outer, b = t / outer;
+    uint16_t h[4];
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const long long i = q * 4 + v;
+      // destination element -> (piece j, k, r)
+      long long j, k, r;
+      if (dst_mn) { j = o / Kp; k = o - j * Kp; r = i; }
+      else { j = i / Kp; k = i - j * Kp; r = o; }
+      float x = 0.f;
+      if (k < K) x = load_as_f32(src + (src_mn ? (b * K + k) * ld + r : (b * rows + r) * ld + k));
+      // peel pieces 0..j (each a round-to-nearest-even bf16 of the remainder)
+      __nv_bfloat16 piece = __float2bfloat16_rn(x);
+      for (long long p = 0; p < j; ++p) {
+        x -= __bfloat162float(piece);
+        piece = __float2bfloat16_rn(x);
+      }
+      h[v] = __bfloat16_as_ushort(piece);
+    }
+    *(uint2*)(dst + (b * outer + o) * inner + q * 4) =
+        make_uint2((uint32_t)h[0] | ((uint32_t)h[1] << 16), (uint32_t)h[2] | ((uint32_t)h[3] << 16));
+  }
+}
+
+// How an operand enters the split product: in place (a bf16 operand TMA can read) or as `pieces`
+// bf16 pieces in scratch, K-major or MN-major.
+struct SplitOperand {
+  int pieces = 1;
+  bool in_place = false;
+  bool dst_mn = false;
+  size_t bytes = 0;                            // scratch bytes
+};
+
+SplitOperand PlanOperand(int type, bool mn, long long ld, const void* ptr, int64_t batch, int64_t rows, int64_t Kp) {
+  SplitOperand o;
+  o.pieces = type == B200_DT_BF16 ? 1 : 3;     // f16 and f32 take three bf16 pieces
+  o.in_place = type == B200_DT_BF16 && ld % 8 == 0 && ((uintptr_t)ptr % 16) == 0 && (!mn || rows % 8 == 0);
+  o.dst_mn = mn && rows % 8 == 0;
+  if (!o.in_place) o.bytes = ((size_t)batch * rows * o.pieces * Kp * 2 + 255) / 256 * 256;
+  return o;
+}
+
+template <typename T>
+int LaunchSplit(const void* src, long long ld, bool src_mn, const SplitOperand& o, int64_t batch, int64_t rows, int64_t K,
+                int64_t Kp, void* dst, cudaStream_t st) {
+  const long long total = (long long)batch * rows * o.pieces * Kp / 4;
+  const int grid = (int)std::min<long long>((total + 255) / 256, (long long)NumSMs() * 8);
+  split_pieces_kernel<T><<<grid, 256, 0, st>>>((const T*)src, ld, src_mn ? 1 : 0, o.dst_mn ? 1 : 0, (int)batch, (int)rows,
+                                               (int)K, (int)Kp, o.pieces, (uint16_t*)dst);
+  CountLaunches();
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int Split(int type, const void* src, long long ld, bool src_mn, const SplitOperand& o, int64_t batch, int64_t rows, int64_t K,
+          int64_t Kp, void* dst, cudaStream_t st) {
+  if (type == B200_DT_F32) return LaunchSplit<float>(src, ld, src_mn, o, batch, rows, K, Kp, dst, st);
+  if (type == B200_DT_BF16) return LaunchSplit<__nv_bfloat16>(src, ld, src_mn, o, batch, rows, K, Kp, dst, st);
+  if (type == B200_DT_F16) return LaunchSplit<__half>(src, ld, src_mn, o, batch, rows, K, Kp, dst, st);
+  return -1;
+}
+
+}  // namespace
+
+size_t GemmSplitScratchBytes(int64_t batch, int64_t M, int64_t N, int64_t K, int a_type, int b_type, bool a_mn, bool b_mn,
+                             long long lda, long long ldb) {
+  const int64_t Kp = (K + BK - 1) / BK * BK;
+  // alignment of the caller's pointers is unknown here: size for a copy of a bf16 operand too
+  SplitOperand a = PlanOperand(a_type, a_mn, lda, nullptr, batch, M, Kp);
+  SplitOperand b = PlanOperand(b_type, b_mn, ldb, nullptr, batch, N, Kp);
+  if (a.in_place) a.bytes = 0;
+  if (b.in_place) b.bytes = 0;
+  return a.bytes + b.bytes;
+}
+
+int GemmSplit(const void* A, long long lda, bool a_mn, int a_type, const void* B, long long ldb, bool b_mn, int b_type,
+              void* C, int64_t batch, int64_t M, int64_t N, int64_t K, int out_type, cudaStream_t st, void* scratch,
+              size_t scratch_bytes, int64_t ldc) {
+  if (batch <= 0 || M <= 0 || N <= 0) return 0;
+  if (ldc <= 0) ldc = N;
+  const int out = OutCode(out_type);
+  auto ok_type = [](int t) { return t == B200_DT_F32 || t == B200_DT_BF16 || t == B200_DT_F16; };
+  if (out < 0 || ldc < N || !ok_type(a_type) || !ok_type(b_type)) return -1;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX / 8 || batch > 65535 || lda < (a_mn ? M : K) || ldb < (b_mn ? N : K))
+    return -1;
+  if (K == 0) return cudaMemsetAsync(C, 0, (size_t)batch * M * ldc * (out == 0 ? 4 : 2), st) == cudaSuccess ? 0 : -3;
+  const int64_t Kp = (K + BK - 1) / BK * BK;
+  const SplitOperand pa = PlanOperand(a_type, a_mn, lda, A, batch, M, Kp);
+  const SplitOperand pb = PlanOperand(b_type, b_mn, ldb, B, batch, N, Kp);
+  if (pa.bytes + pb.bytes > scratch_bytes || (pa.bytes + pb.bytes && ((uintptr_t)scratch % 256))) return -4;
+  // terms (i, j) with i + j <= 2 over the pieces both operands have, smallest first: the f32
+  // accumulator then adds the large products last
+  Terms tm;
+  tm.n = 0;
+  for (int sum = 2; sum >= 0; --sum)
+    for (int i = sum; i >= 0; --i) {
+      const int j = sum - i;
+      if (i < pa.pieces && j < pb.pieces) {
+        tm.a |= (uint32_t)i << (4 * tm.n);
+        tm.b |= (uint32_t)j << (4 * tm.n);
+        ++tm.n;
+      }
+    }
+  const void* a_op = A;
+  const void* b_op = B;
+  long long a_ld = lda, b_ld = ldb;
+  bool a_opmn = a_mn, b_opmn = b_mn;
+  uint8_t* next = (uint8_t*)scratch;
+  if (!pa.in_place) {
+    if (int rc = Split(a_type, A, lda, a_mn, pa, batch, M, K, Kp, next, st)) return rc;
+    a_op = next;
+    a_opmn = pa.dst_mn;
+    a_ld = pa.dst_mn ? M : pa.pieces * Kp;
+    tm.ka = pa.pieces * Kp;
+    next += pa.bytes;
+  }
+  if (!pb.in_place) {
+    if (int rc = Split(b_type, B, ldb, b_mn, pb, batch, N, K, Kp, next, st)) return rc;
+    b_op = next;
+    b_opmn = pb.dst_mn;
+    b_ld = pb.dst_mn ? N : pb.pieces * Kp;
+    tm.kb = pb.pieces * Kp;
+  }
+  // 16-bit results are not split along K here (no f32 workspace): the terms already give every
+  // output tile a long K walk
+  return RunTc(a_op, a_ld, a_opmn, b_op, b_ld, b_opmn, C, batch, M, N, K, (int64_t)tm.n * Kp, /*bf16*/ 1, out, st,
+               out == 0 ? (float*)C : nullptr, ldc, tm);
 }
 
 }  // namespace b200k
@@ -664,4 +838,15 @@ int Gemm(const void* A, long long lda, const void* B, long long ldb, void* C, in
 extern "C" int b200_gemm(const void* A, const void* B, void* C, int64_t batch, int64_t M, int64_t N, int64_t K,
                          int ab_type, int out_type, void* stream) {
   return b200k::Gemm(A, K, B, K, C, batch, M, N, K, ab_type, out_type, (cudaStream_t)stream);
+}
+
+extern "C" size_t b200_gemm_split_scratch_bytes(int64_t batch, int64_t M, int64_t N, int64_t K, int a_type, int b_type) {
+  if (batch <= 0 || M <= 0 || N <= 0 || K <= 0) return 0;
+  return b200k::GemmSplitScratchBytes(batch, M, N, K, a_type, b_type, false, false, K, K);
+}
+
+extern "C" int b200_gemm_split(const void* A, int a_type, const void* B, int b_type, void* C, int64_t batch, int64_t M,
+                               int64_t N, int64_t K, int out_type, void* scratch, size_t scratch_bytes, void* stream) {
+  return b200k::GemmSplit(A, K, false, a_type, B, K, false, b_type, C, batch, M, N, K, out_type, (cudaStream_t)stream,
+                          scratch, scratch_bytes, 0);
 }

@@ -53,19 +53,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
 }
 
 // Waits until the phase with the given parity has completed.  Returns false (and records `code`)
-// if the budget runs out or another thread already recorded an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code, int* flag) {
+// if `budget` clock cycles pass or another thread already recorded an error.
+__device__ __forceinline__ bool mbar_wait_budget(uint64_t* bar, uint32_t parity, int code, int* flag, long long budget) {
   uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(addr, parity)) return true;
     if (*(volatile int*)flag != 0) return false;
-    if (clock64() - t0 > kWaitBudget) {
+    if (clock64() - t0 > budget) {
       atomicCAS(flag, 0, code);
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code, int* flag) {
+  return mbar_wait_budget(bar, parity, code, flag, kWaitBudget);
 }
 
 // Warp-uniform form of mbar_wait for warps that go on to warp-collective (.sync.aligned) tcgen05

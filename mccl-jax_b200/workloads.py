@@ -1,11 +1,21 @@
-"""The non-headline workloads of bench.py (`--workload dp | gemm | psum`), each printing one JSON line.
+"""The measured workloads behind bench.py, one function per BASELINE configuration, each returning a
+dict (bench.py assembles them into its JSON line).
 
-  dp    GPT-2-small data-parallel AdamW step through the PJRT C API: params,
-        moments and the token batch stay on the device, step outputs feed the next step; device
-        time from CUDA events the executor records (b200_exec_timer), max over ranks; tokens/s for
-        the whole job, MFU against the measured dense bf16 peak (854.4 MFLOP/token, PaLM counting).
-  gemm  dot_general sweep (config 3) through b200_gemm on HBM-resident operands.
-  psum  all_reduce sweep (config 5) through the PJRT plugin, bus GB/s = bytes * 2(n-1)/n / time.
+  run_dp        config 4: the GPT-2-small data-parallel AdamW train step through the PJRT C API (one
+                process per GPU, gradients all-reduced over NCCL).  Params, moments and the token
+                batch stay on the device and each step's outputs feed the next; device time from the
+                CUDA events the executor records (b200_exec_timer), max over ranks.  The end-to-end
+                loop uploads each step's token batch from pinned host memory and reads the loss back.
+  run_attention config 2: the fused attention kernel (b200_attention_fwd) on HBM-resident inputs,
+                the sequence-length sweep, and the same metric through PJRT with host buffers.
+  run_gemm      config 3: dot_general through b200_gemm (bf16) and b200_gemm_split (f32 inputs).
+  run_fused     the HBM-bound chains of the train step (AdamW, LayerNorm, bias+GELU, logsumexp)
+                through PJRT, GB/s against the measured copy bandwidth.
+  run_attn_bwd  the flash backward through the C ABI.
+  run_psum      config 5: the all_reduce sweep through PJRT (NCCL), bus GB/s.
+  cpu_*         the CPU baselines (oracle/torch_ref.py: torch on all host cores, f32), rank 0 only.
+Device time is measured with CUDA events on the stream the kernels run on; L2 is flushed (a
+256 MiB write) before timed kernel calls whose inputs fit in L2.
 """
 from __future__ import annotations
 
@@ -14,7 +24,9 @@ import datetime
 import json
 import math
 import os
-import sys
+import statistics
+import subprocess
+import tempfile
 import time
 
 import numpy as np
@@ -23,16 +35,85 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "lib", "libpjrt_b200.so")
 
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-def _peaks():
+
+def peaks():
+    """(peaks, "measured" | "fallback"): the pool's measured HBM copy and dense bf16 GEMM rates."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             return json.load(f), "measured"
     except Exception:
-        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+        return dict(FALLBACK_PEAKS), "fallback"
 
 
-def _client(world, rank, local):
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count()
+
+
+def lib():
+    l = ctypes.CDLL(LIB)
+    l.b200_exec_timer.restype = ctypes.c_double
+    l.b200_graph_stats.restype = ctypes.c_longlong
+    l.b200_kernel_launches.restype = ctypes.c_longlong
+    l.b200_gemm.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 4 + [ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    l.b200_gemm_split_scratch_bytes.argtypes = [ctypes.c_int64] * 4 + [ctypes.c_int, ctypes.c_int]
+    l.b200_gemm_split_scratch_bytes.restype = ctypes.c_size_t
+    l.b200_gemm_split.argtypes = ([ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p] +
+                                  [ctypes.c_int64] * 4 + [ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p])
+    l.b200_attention_fwd.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_void_p]
+    l.b200_attention_fwd_lse.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_void_p]
+    l.b200_attention_bwd.argtypes = [ctypes.c_void_p] * 11 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_void_p]
+    return l
+
+
+class Clocks:
+    """nvidia-smi samples (SM clock, throttle reasons) while a timed region runs."""
+
+    def __init__(self, index):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.strip() == "Active":
+                        reasons.add(n)
+            except Exception:
+                pass
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_client(world, rank, local):
+    """A PJRT client for this rank; with world > 1 the NCCL unique id travels through a TCP store
+    (the kv_put / kv_get callbacks of PJRT_Client_Create)."""
     from pjrt_b200 import pjrt
     api = pjrt.Api(LIB)
     if world == 1:
@@ -51,7 +132,7 @@ def _client(world, rank, local):
     return pjrt.Client(api, node_id=rank, num_nodes=world, device_ordinal=local, kv_put=put, kv_get=get), store
 
 
-def _max_over_ranks(x, world):
+def max_over_ranks(x, world):
     if world == 1:
         return x
     import torch
@@ -61,115 +142,275 @@ def _max_over_ranks(x, world):
     return float(t.item())
 
 
+def barrier(world):
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def pinned(x):
+    """A copy of numpy array `x` in page-locked host memory (torch's pinned allocator)."""
+    import torch
+    t = torch.empty(x.nbytes, dtype=torch.uint8).pin_memory()
+    a = t.numpy().view(x.dtype).reshape(x.shape)     # the view's base keeps `t` alive
+    a[...] = x
+    return a
+
+
+# ============================================================================ config 4: DP step
 def run_dp(a, world, rank, local):
     import torch
     from pjrt_b200 import configs
-    lib = ctypes.CDLL(LIB)
-    lib.b200_exec_timer.restype = ctypes.c_double
+    L = lib()
     cfg = dict(configs.GPT2_SMALL, layers=a.layers)
     batch = 8
     t0 = time.time()
     prog = configs.gpt2_program(batch=batch, world=world, rank=rank, **cfg)
-    client, store = _client(world, rank, local)
+    client, store = make_client(world, rank, local)
     exe = client.compile(prog.text)
     compile_s = time.time() - t0
     n = prog.meta["n_tensors"]
-    bufs = [client.buffer_from_host(x) for x in prog.inputs[:3 * n + 2]]
-    state, data = bufs[:3 * n], bufs[3 * n:]
+    state = [client.buffer_from_host(x) for x in prog.inputs[:3 * n]]
+    # token batches (this rank's shard [batch, seq]; shard_map retypes the argument): a few distinct
+    # ones, seeded per rank, in pinned host memory; the device-resident loop reuses uploaded copies
+    brng = np.random.default_rng(1000 + rank)
+    host_batches = [[pinned(brng.integers(0, cfg["vocab"], (batch, cfg["seq"])).astype(np.int32)) for _ in range(2)]
+                    for _ in range(4)]
+    dev_batches = [[client.buffer_from_host(x) for x in hb] for hb in host_batches]
+    bc_host = [pinned(np.zeros((), np.float32)), pinned(np.zeros((), np.float32))]
 
-    def step(s):
-        # the bias-correction scalars and last step's buffers are released once this step is
-        # enqueued (stream-ordered frees), so steady-state steps reuse the same addresses
-        bc = [client.buffer_from_host(np.array(1 - 0.9 ** s, np.float32)),
-              client.buffer_from_host(np.array(1 - 0.95 ** s, np.float32))]
-        outs = exe.execute(state + data + bc, wait=False)
-        for b in bc + state:
+    def step(s, upload):
+        """One train step s >= 1.  `upload`: the token batch comes from pinned host memory now (else
+        from its device copy).  Argument buffers are released once the step is enqueued (the frees
+        are stream-ordered); the step's new state replaces the old."""
+        bc_host[0][...] = 1 - 0.9 ** s          # Adam bias corrections, host scalars per step
+        bc_host[1][...] = 1 - 0.95 ** s
+        bc = [client.buffer_from_host(x) for x in bc_host]     # returns once the host copy is read
+        toks = [client.buffer_from_host(x) for x in host_batches[s % 4]] if upload else dev_batches[s % 4]
+        outs = exe.execute(state + toks + bc, wait=False)
+        for b in bc + state + (toks if upload else []):
             b.delete()
         state[:] = outs[:3 * n]
         return outs[-1]
 
-    lib.b200_graph_stats.restype = ctypes.c_longlong
-    losses = []
     s = 1
+    losses = []
     for _ in range(a.warmup):
-        loss = step(s)
+        loss = step(s, False)
         s += 1
         losses.append(float(loss.to_numpy()))
         loss.delete()
-    if world > 1:
-        torch.distributed.barrier()
-    replays0 = lib.b200_graph_stats(1)
-    lib.b200_exec_timer(0)
-    t_wall = time.perf_counter()
+    barrier(world)
+    clk = Clocks(local) if rank == 0 else None
+    replays0 = L.b200_graph_stats(1)
+    launches0 = L.b200_kernel_launches()
+    L.b200_exec_timer(0)
     loss = None
     for _ in range(a.steps):
         if loss is not None:
             loss.delete()
-        loss = step(s)
+        loss = step(s, False)
         s += 1
+    dev_ms = L.b200_exec_timer(1)            # waits for the last execution
+    barrier(world)
+    clocks = clk.stop() if clk else None
+    launches = L.b200_kernel_launches() - launches0
+    replays = L.b200_graph_stats(1) - replays0
     last_loss = float(loss.to_numpy())
     loss.delete()
-    replays = lib.b200_graph_stats(1) - replays0
-    dev_ms = lib.b200_exec_timer(1)
-    wall_ms = (time.perf_counter() - t_wall) * 1e3
-    ms = _max_over_ranks(dev_ms / a.steps, world)
-    tokens = batch * cfg["seq"] * world
-    pk, src = _peaks()
-    fl_tok = prog.flops / (batch * cfg["seq"])
-    tps = tokens / (ms * 1e-3)
-    mfu = fl_tok * tps / world / (pk["bf16_tflops"] * 1e12)
-    if rank == 0:
-        print(json.dumps({
-            "metric": "DP train-step tokens/s (GPT-2 small, per-GPU batch 8 x 1024, AdamW)", "value": tps,
-            "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded ids, N(0,0.02) params)",
-            "config": {"workload": "gpt2-small DP step", "layers": cfg["layers"], "d_model": cfg["d"],
-                       "heads": cfg["heads"], "vocab": cfg["vocab"], "seq_len": cfg["seq"], "per_gpu_batch": batch,
-                       "global_batch": batch * world, "parallelism": f"dp{world}", "params": prog.meta["n_params"]},
-            "roofline": {"bound": "tensor", "achieved": fl_tok * tps / world / 1e12, "peak": pk["bf16_tflops"],
-                         "unit": "TFLOP/s", "frac": mfu, "peak_source": src + " dense bf16 (burst)",
-                         "flops_per_token": fl_tok},
-            "wall_ms_per_step": wall_ms / a.steps, "compile_s": compile_s, "graph_replays": replays,
-            "loss_first": losses[0], "loss_last": last_loss}))
-    for b in state + data:
+    ms = max_over_ranks(dev_ms / a.steps, world)
+    # ---- end to end: per step, token batch + scalars H2D from pinned memory, loss D2H
+    e2e_steps = max(3, a.steps // 2)
+    loss_host = pinned(np.zeros((), np.float32))
+    for k in range(2 + e2e_steps):
+        if k == 2:
+            barrier(world)
+            t_e = time.perf_counter()
+        lb = step(s, True)
+        lb.to_numpy(loss_host)
+        lb.delete()
+        s += 1
+    e2e_ms = max_over_ranks((time.perf_counter() - t_e) * 1e3 / e2e_steps, world)
+    h2d = sum(x.nbytes for x in host_batches[0]) + 8
+    for b in state + [x for db in dev_batches for x in db]:
         b.delete()
     exe.destroy()
     client.close()
-    return 0
+    tokens = batch * cfg["seq"] * world
+    pk, src = peaks()
+    fl_tok = prog.flops / (batch * cfg["seq"])
+    tps = tokens / (ms * 1e-3)
+    per_gpu_tflops = fl_tok * tps / world / 1e12
+    return {
+        "ms": ms, "tokens_per_s": tps, "tokens_per_step": tokens, "compile_s": compile_s, "graph_replays": replays,
+        "launches": launches, "loss_first": losses[0] if losses else None, "loss_last": last_loss, "clocks": clocks,
+        "flops_per_token": fl_tok, "n_params": prog.meta["n_params"], "cfg": cfg, "batch": batch,
+        "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": per_gpu_tflops / pk["bf16_tflops_sustained"], "traffic": None,
+                     "kernel": "whole train step (model FLOPs utilisation: 854.4 MFLOP/token, PaLM counting with "
+                               "attention as non-causal)",
+                     "peak_source": f"{src} dense bf16, sustained (a kernel mix timed inside a long step)"},
+        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": 4,
+                "path": "PJRT C API per step: BufferFromHostBuffer(ids, targets, 2 scalars; pinned host) + Execute + "
+                        "ToHostBuffer(loss), host wall clock, max over ranks"},
+    }
 
 
-def run_gemm(a, world, rank, local):
-    import torch
-    lib = ctypes.CDLL(LIB)
-    lib.b200_gemm.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 4 + [ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
-    torch.cuda.set_device(local)
+# ============================================================================ config 2: attention
+def attn_flops(B, H, S, D, causal):
+    return 4.0 * B * H * S * S * D * (0.5 if causal else 1.0)
+
+
+def time_attention(torch, L, cfg, steps, warmup, flush):
+    """Device ms per b200_attention_fwd call (CUDA events on the launching stream, L2 flushed)."""
+    B, H, S, D, causal = cfg["B"], cfg["H"], cfg["S"], cfg["D"], cfg["causal"]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q, k, v = (torch.randn(B, H, S, D, device="cuda", generator=g).to(torch.bfloat16) for _ in range(3))
+    o = torch.empty_like(q)
     st = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(st.cuda_stream)
+
+    def call():
+        rc = L.b200_attention_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, H, S, D, int(causal),
+                                  1.0 / math.sqrt(D), sp)
+        if rc != 0:
+            raise RuntimeError(f"b200_attention_fwd failed ({rc})")
+
+    for _ in range(warmup):
+        flush.zero_()
+        call()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        call()
+        e1.record(st)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    torch.cuda.synchronize()
+    if L.b200_take_device_error() != 0:
+        raise RuntimeError("attention kernel reported a timed-out wait")
+    return sum(times) / len(times)
+
+
+def attention_e2e(cfg, steps, warmup, device):
+    """The attention metric through the PJRT C API with host buffers (pinned): 3 H2D + Execute +
+    1 D2H per step, host wall clock around the synchronous calls."""
+    import ml_dtypes
+    from pjrt_b200 import configs, pjrt
+    p = configs.attention_program(with_inputs=True, **{k: cfg[k] for k in ("B", "H", "S", "D", "causal")})
+    hosts = [pinned(x) for x in p.inputs]
+    out_host = pinned(np.zeros(p.inputs[0].shape, ml_dtypes.bfloat16))
+    client = pjrt.Client(pjrt.Api(LIB), device_ordinal=device)
+    exe = client.compile(p.text)
+
+    def step():
+        bufs = [client.buffer_from_host(x) for x in hosts]
+        outs = exe.execute(bufs)
+        outs[0].to_numpy(out_host)
+        for b in bufs + outs:
+            b.delete()
+
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    ms = (time.perf_counter() - t0) * 1e3 / steps
+    exe.destroy()
+    client.close()
+    return ms, sum(x.nbytes for x in hosts), out_host.nbytes
+
+
+def run_attention(a, local, sweep=True, e2e=True, cpu=True, traffic=None):
+    import torch
+    L = lib()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    pk, src = peaks()
+    head = dict(B=a.B, H=a.H, S=a.S, D=64, causal=a.causal)
+    ms = time_attention(torch, L, head, a.steps, a.warmup, flush)
+    fl = attn_flops(**head)
+    tf = fl / (ms * 1e-3) / 1e12
+    r = {"value": tf, "unit": "TFLOP/s", "ms_per_call": ms,
+         "config": {"workload": f"attention B={a.B} H={a.H} S={a.S} d=64 {'causal' if a.causal else 'non-causal'}",
+                    "dtype": "bf16 in/out, fp32 softmax", "l2": "flushed (256 MiB write) before every timed call"},
+         "roofline": {"bound": "tensor", "achieved": tf, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                      "frac": tf / pk["bf16_tflops"], "traffic": traffic,
+                      "peak_source": f"{src} dense bf16 (burst: one kernel timed alone)",
+                      "algorithmic_flops_per_call": fl, "algorithmic_bytes_per_call": 4.0 * a.B * a.H * a.S * 64 * 2}}
+    if sweep:
+        rows = []
+        for S in (512, 1024, 2048, 4096, 8192, 16384):
+            for causal in (False, True):
+                cfg = dict(B=4, H=16, S=S, D=64, causal=causal)
+                m = time_attention(torch, L, cfg, max(3, a.steps // 2), 3, flush)
+                rows.append({"S": S, "causal": causal, "ms": round(m, 4),
+                             "tflops": round(attn_flops(**cfg) / (m * 1e-3) / 1e12, 1)})
+        r["sweep"] = rows
+    del flush
+    torch.cuda.empty_cache()
+    if e2e:
+        e_ms, h2d, d2h = attention_e2e(head, max(3, a.steps // 2), 2, local)
+        r["e2e"] = {"value": fl / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e_ms, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "path": "PJRT C API: BufferFromHostBuffer x3 + Execute + ToHostBuffer (pinned)"}
+    if cpu:
+        r["cpu_baseline"] = cpu_attention(head)
+    return r
+
+
+def cpu_attention(cfg):
+    """torch-CPU scaled_dot_product_attention in f32 on all host cores, on the whole input."""
+    import torch
+    from oracle import torch_ref
+    torch.set_num_threads(torch_ref.host_threads())
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(cfg["B"], cfg["H"], cfg["S"], cfg["D"], generator=g).to(torch.bfloat16).float() for _ in range(3))
+    torch_ref.attention(q[:1, :1], k[:1, :1], v[:1, :1], cfg["causal"])          # warm-up
+    t0 = time.perf_counter()
+    torch_ref.attention(q, k, v, cfg["causal"])
+    dt = time.perf_counter() - t0
+    return {"value": attn_flops(**cfg) / dt / 1e12, "unit": "TFLOP/s", "cores": torch_ref.host_threads(), "kind": "port",
+            "sample": f"torch-CPU f32 scaled_dot_product_attention on the whole [{cfg['B']},{cfg['H']},{cfg['S']},64] "
+                      f"input, one call ({dt:.2f} s)"}
+
+
+# ============================================================================ config 3: GEMM
+def run_gemm(a, local, only=""):
+    import torch
+    L = lib()
+    st = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(st.cuda_stream)
     flush = torch.empty(64 * 1024 * 1024, device="cuda")
-    pk, src = _peaks()
+    pk, src = peaks()
     rows = []
-    shapes = [(1, 1024, 13), (1, 4096, 13), (1, 8192, 13), (16, 2048, 13), (1, 1024, 11), (1, 4096, 11), (1, 8192, 11)]
-    only = getattr(a, "only", "")
-    custom = None
-    if only.startswith("m"):                      # e.g. m8192n3072k768: one rectangular bf16 shape
-        import re
-        mm = re.fullmatch(r"m(\d+)n(\d+)k(\d+)", only)
-        custom = tuple(int(x) for x in mm.groups())
-        shapes = [(1, custom, 13)]
-    for batch, n, ab in shapes:
-        if only and custom is None and only != f"b{batch}-{n}-{'bf16' if ab == 13 else 'f32'}":
+    shapes = [(1, 1024, "bf16"), (1, 4096, "bf16"), (1, 8192, "bf16"), (16, 2048, "bf16"), (1, 1024, "f32"),
+              (1, 4096, "f32"), (1, 8192, "f32")]
+    for batch, n, dt in shapes:
+        name = f"b{batch}-{n}-{dt}"
+        if only and only != name:
             continue
-        M, N, K = n if custom else (n, n, n)
-        dt = torch.bfloat16 if ab == 13 else torch.float32
-        A = (torch.randn(batch, M, K, device="cuda") / math.sqrt(K)).to(dt)
-        B = (torch.randn(batch, N, K, device="cuda") / math.sqrt(K)).to(dt)
-        C = torch.empty(batch, M, N, device="cuda")
-        f = lambda: lib.b200_gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), batch, M, N, K, ab, 11,
-                                  ctypes.c_void_p(st.cuda_stream))
+        tdt = torch.bfloat16 if dt == "bf16" else torch.float32
+        A = (torch.randn(batch, n, n, device="cuda") / math.sqrt(n)).to(tdt)
+        B = (torch.randn(batch, n, n, device="cuda") / math.sqrt(n)).to(tdt)
+        C = torch.empty(batch, n, n, device="cuda")
+        if dt == "bf16":
+            f = lambda: L.b200_gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), batch, n, n, n, 13, 11, sp)
+            path = "b200_gemm (tcgen05, bf16 x bf16 -> f32)"
+        else:
+            nb = L.b200_gemm_split_scratch_bytes(batch, n, n, n, 11, 11)
+            scratch = torch.empty(nb, dtype=torch.uint8, device="cuda")
+            f = lambda: L.b200_gemm_split(A.data_ptr(), 11, B.data_ptr(), 11, C.data_ptr(), batch, n, n, n, 11,
+                                          scratch.data_ptr(), nb, sp)
+            path = "b200_gemm_split (f32 operands as 3 bf16 pieces, 6 tcgen05 products, f32 accumulation)"
         for _ in range(a.warmup):
-            f()
+            assert f() == 0
         ts = []
-        for _ in range(a.steps if ab == 13 else max(2, a.steps // 4)):
+        for _ in range(a.steps):
             flush.zero_()
             e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
             e0.record(st)
@@ -178,94 +419,31 @@ def run_gemm(a, world, rank, local):
             e1.synchronize()
             ts.append(e0.elapsed_time(e1))
         ms = sorted(ts)[len(ts) // 2]
-        tf = 2.0 * batch * M * N * K / (ms * 1e-3) / 1e12
-        rows.append({"batch": batch, "M=N=K": n if not custom else f"{M}x{N}x{K}", "inputs": "bf16" if ab == 13 else "f32",
-                     "ms": round(ms, 4), "tflops": round(tf, 1), "frac_of_peak": round(tf / pk["bf16_tflops"], 3)})
+        tf = 2.0 * batch * n ** 3 / (ms * 1e-3) / 1e12
+        rows.append({"shape": name, "path": path, "ms": round(ms, 4), "tflops": round(tf, 1),
+                     "frac_of_bf16_peak": round(tf / pk["bf16_tflops"], 3)})
         del A, B, C
-    heads = [r for r in rows if r["M=N=K"] == 8192 and r["inputs"] == "bf16"]
-    head = heads[0] if heads else rows[0]
-    print(json.dumps({"metric": "dot_general TFLOP/s (bf16 -> f32, 8192^3)", "value": head["tflops"], "unit": "TFLOP/s",
-                      "n_gpus": 1, "higher_is_better": True, "dtype": "bf16", "data": "synthetic N(0,1)/sqrt(K)",
-                      "config": {"workload": "gemm sweep", "l2": "flushed before every timed call"},
-                      "roofline": {"bound": "tensor", "achieved": head["tflops"], "peak": pk["bf16_tflops"],
-                                   "frac": head["frac_of_peak"], "peak_source": src + " dense bf16 (burst)"},
-                      "sweep": rows}))
-    return 0
+    if L.b200_take_device_error() != 0:
+        raise RuntimeError("GEMM kernel reported a timed-out wait")
+    del flush
+    torch.cuda.empty_cache()
+    head = next((r for r in rows if r["shape"] == "b1-8192-bf16"), rows[0])
+    return {"value": head["tflops"], "unit": "TFLOP/s", "shape": head["shape"],
+            "roofline": {"bound": "tensor", "achieved": head["tflops"], "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": head["frac_of_bf16_peak"], "peak_source": f"{src} dense bf16 (burst)"},
+            "config": {"workload": "dot_general sweep, A[M,K] B[N,K] ~ N(0,1)/sqrt(K), f32 result",
+                       "l2": "flushed before every timed call", "timing": "median of CUDA-event spans"},
+            "sweep": rows}
 
 
-def _pipelined(exe, bufs, steps):
-    """Execute `steps` times back to back: each step's outputs are released (stream-ordered, back to
-    the pool) after the next step has been enqueued, and the last step is read back.  Warm-up and
-    timed loops both use this, so the allocator pool holds two steps' outputs before timing starts."""
-    prev = []
-    for _ in range(steps):
-        outs = exe.execute(bufs, wait=False)
-        for o in prev:
-            o.delete()
-        prev = outs
-    if prev:
-        prev[-1].to_numpy()
-    for o in prev:
-        o.delete()
-
-
-def run_psum(a, world, rank, local):
-    import torch
-    from pjrt_b200 import configs
-    lib = ctypes.CDLL(LIB)
-    lib.b200_exec_timer.restype = ctypes.c_double
-    client, store = _client(world, rank, local)
-    rows = []
-    for kb in (4, 16, 64, 256, 1024, 4096, 16384, 65536, 262144, 1048576):
-        n = kb * 1024 // 4
-        p = configs.psum_program(n, world, seed_rank=rank)
-        exe = client.compile(p.text)
-        buf = client.buffer_from_host(p.inputs[0])
-        _pipelined(exe, [buf], a.warmup)
-        if world > 1:
-            torch.distributed.barrier()
-        lib.b200_exec_timer(0)
-        _pipelined(exe, [buf], a.steps)
-        ms = _max_over_ranks(lib.b200_exec_timer(1) / a.steps, world)
-        buf.delete()
-        exe.destroy()
-        algbw = n * 4 / (ms * 1e-3) / 1e9
-        row = {"bytes": n * 4, "ms": round(ms, 5), "algbw_GBs": round(algbw, 2),
-               "busbw_GBs": round(algbw * 2 * (world - 1) / world, 2)}
-        if world > 1:
-            # the same all_reduce through torch.distributed (NCCL) for comparison
-            t = torch.randn(n, device="cuda")
-            for _ in range(a.warmup):
-                torch.distributed.all_reduce(t)
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
-            e0.record()
-            for _ in range(a.steps):
-                torch.distributed.all_reduce(t)
-            e1.record()
-            e1.synchronize()
-            tms = _max_over_ranks(e0.elapsed_time(e1) / a.steps, world)
-            row["torch_nccl_busbw_GBs"] = round(n * 4 / (tms * 1e-3) / 1e9 * 2 * (world - 1) / world, 2)
-            del t
-        rows.append(row)
-    client.close()
-    if rank == 0:
-        big = rows[-1]
-        print(json.dumps({"metric": "all_reduce (psum) bus GB/s at 1 GiB f32", "value": big["busbw_GBs"], "unit": "GB/s",
-                          "n_gpus": world, "higher_is_better": True, "dtype": "f32", "data": "synthetic N(0,1) per rank",
-                          "config": {"workload": "psum sweep 4 KiB .. 1 GiB through PJRT (NCCL)",
-                                     "nvlink_peak_GBs_per_direction": 900},
-                          "sweep": rows}))
-    return 0
-
-
+# ============================================================================ fused HBM-bound chains
 def fused_programs():
     """Memory-bound chains of the train step as standalone programs, with their algorithmic bytes
     (unique inputs read + outputs written once)."""
     from pjrt_b200.shlo import Builder
+    import ml_dtypes
     progs = []
     rng = np.random.default_rng(0)
-    import ml_dtypes
     bf = ml_dtypes.bfloat16
     # AdamW over the flattened GPT-2-small parameters: bf16 p, g; f32 m, v
     n = 124_439_808
@@ -312,21 +490,35 @@ def fused_programs():
     return progs
 
 
-def run_fused(a, world, rank, local):
-    lib = ctypes.CDLL(LIB)
-    lib.b200_exec_timer.restype = ctypes.c_double
-    client, _ = _client(1, 0, local)
-    pk, src = _peaks()
+def _pipelined(exe, bufs, steps):
+    """Execute `steps` times back to back: each step's outputs are released (stream-ordered, back to
+    the pool) after the next step has been enqueued, and the last step is read back."""
+    prev = []
+    for _ in range(steps):
+        outs = exe.execute(bufs, wait=False)
+        for o in prev:
+            o.delete()
+        prev = outs
+    if prev:
+        prev[-1].to_numpy()
+    for o in prev:
+        o.delete()
+
+
+def run_fused(a, local, only=""):
+    L = lib()
+    client, _ = make_client(1, 0, local)
+    pk, src = peaks()
     rows = []
     for name, text, ins, nbytes in fused_programs():
-        if getattr(a, "only", "") and a.only not in name:
+        if only and only not in name:
             continue
         exe = client.compile(text)
         bufs = [client.buffer_from_host(x) for x in ins]
         _pipelined(exe, bufs, a.warmup)
-        lib.b200_exec_timer(2)          # each execution's own device span: host enqueue gaps left out
+        L.b200_exec_timer(2)          # each execution's own device span: host enqueue gaps left out
         _pipelined(exe, bufs, a.steps)
-        ms = lib.b200_exec_timer(1) / a.steps
+        ms = L.b200_exec_timer(1) / a.steps
         for o in bufs:
             o.delete()
         exe.destroy()
@@ -335,31 +527,26 @@ def run_fused(a, world, rank, local):
                      "frac_of_hbm": round(gbs / pk["hbm_gbs"], 3)})
     client.close()
     worst = min(r["frac_of_hbm"] for r in rows)
-    print(json.dumps({"metric": "fused elementwise/reduce kernels, fraction of HBM bandwidth (min over the set)",
-                      "value": worst, "unit": "fraction", "n_gpus": 1, "higher_is_better": True, "dtype": "bf16/f32",
-                      "data": "synthetic", "config": {"workload": "fused chains through PJRT, device time",
-                                                       "timing": "sum of per-execution CUDA-event spans; inputs > L2",
-                                                       "hbm_peak_GBs": pk["hbm_gbs"], "peak_source": src},
-                      "kernels": rows}))
-    return 0
+    return {"value": worst, "unit": "fraction of measured HBM copy bandwidth (min over the set)",
+            "config": {"workload": "fused chains through PJRT, device time (per-execution CUDA-event spans)",
+                       "l2": "inputs larger than L2", "hbm_peak_GBs": pk["hbm_gbs"], "peak_source": src},
+            "kernels": rows}
 
 
-def run_attn_bwd(a, world, rank, local):
+# ============================================================================ attention backward
+def run_attn_bwd(a, local, only=""):
     """Flash-attention training kernels through the C ABI: forward with lse2, then the backward
     (delta, dQ/dK/dV, dQ rounding), device time with CUDA events, L2 flushed before each step."""
     import torch
-    lib = ctypes.CDLL(LIB)
-    lib.b200_attention_fwd_lse.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_void_p]
-    lib.b200_attention_bwd.argtypes = [ctypes.c_void_p] * 11 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_void_p]
-    torch.cuda.set_device(local)
+    L = lib()
     st = torch.cuda.current_stream()
     sp = ctypes.c_void_p(st.cuda_stream)
     flush = torch.empty(64 * 1024 * 1024, device="cuda")
-    pk, src = _peaks()
+    pk, src = peaks()
     rows = []
     for B, H, S, causal in [(8, 12, 1024, True), (4, 16, 4096, True), (4, 16, 4096, False)]:
         name = f"{B}x{H}x{S}-{'causal' if causal else 'full'}"
-        if getattr(a, "only", "") and a.only != name:
+        if only and only != name:
             continue
         g = torch.Generator(device="cuda").manual_seed(S)
         q, k, v, do = (torch.randn(B, H, S, 64, device="cuda", generator=g).to(torch.bfloat16) for _ in range(4))
@@ -367,11 +554,11 @@ def run_attn_bwd(a, world, rank, local):
         lse = torch.empty(B, H, S, device="cuda")
         dq_acc = torch.empty(B, H, S, 64, device="cuda")
         delta = torch.empty(B, H, S, device="cuda")
-        fwd = lambda: lib.b200_attention_fwd_lse(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
-                                                 B, H, S, 64, int(causal), 0.125, sp)
-        bwd = lambda: lib.b200_attention_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(),
-                                             lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dq_acc.data_ptr(),
-                                             delta.data_ptr(), B, H, S, 64, int(causal), 0.125, sp)
+        fwd = lambda: L.b200_attention_fwd_lse(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+                                               B, H, S, 64, int(causal), 0.125, sp)
+        bwd = lambda: L.b200_attention_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(),
+                                           lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dq_acc.data_ptr(),
+                                           delta.data_ptr(), B, H, S, 64, int(causal), 0.125, sp)
         for _ in range(a.warmup):
             assert fwd() == 0 and bwd() == 0
         tf, tb = [], []
@@ -387,32 +574,86 @@ def run_attn_bwd(a, world, rank, local):
             tf.append(e[0].elapsed_time(e[1]))
             tb.append(e[1].elapsed_time(e[2]))
         mf, mb = sorted(tf)[len(tf) // 2], sorted(tb)[len(tb) // 2]
-        fl = 4.0 * B * H * S * S * 64 * (0.5 if causal else 1.0)      # forward; the backward is 2.5x
+        fl = attn_flops(B, H, S, 64, causal)     # forward; the backward is 2.5x
         rows.append({"shape": name, "fwd_ms": round(mf, 4), "fwd_tflops": round(fl / mf / 1e9, 1),
                      "bwd_ms": round(mb, 4), "bwd_tflops": round(2.5 * fl / mb / 1e9, 1)})
+    if L.b200_take_device_error() != 0:
+        raise RuntimeError("attention backward reported a timed-out wait")
+    del flush
+    torch.cuda.empty_cache()
     head = rows[0]
-    print(json.dumps({"metric": "attention backward TFLOP/s (bf16 [8,12,1024,64] causal, GPT-2 training shape)",
-                      "value": head["bwd_tflops"], "unit": "TFLOP/s", "n_gpus": 1, "higher_is_better": True,
-                      "dtype": "bf16", "data": "synthetic N(0,1)",
-                      "config": {"workload": "flash attention fwd(+lse2) and bwd", "l2": "flushed before every step",
-                                 "flops": "bwd = 2.5 x fwd = 10 B H S^2 d (half causal)"},
-                      "roofline": {"bound": "tensor", "achieved": head["bwd_tflops"], "peak": pk["bf16_tflops"],
-                                   "frac": round(head["bwd_tflops"] / pk["bf16_tflops"], 3), "peak_source": src},
-                      "sweep": rows}))
-    return 0
+    return {"value": head["bwd_tflops"], "unit": "TFLOP/s", "shape": head["shape"],
+            "roofline": {"bound": "tensor", "achieved": head["bwd_tflops"], "peak": pk["bf16_tflops"],
+                         "frac": round(head["bwd_tflops"] / pk["bf16_tflops"], 3), "peak_source": src},
+            "config": {"workload": "flash attention fwd(+lse2) and bwd through the C ABI", "l2": "flushed before every step",
+                       "flops": "bwd = 2.5 x fwd = 10 B H S^2 d (half causal)"},
+            "sweep": rows}
 
 
-def run(a, world, rank, local):
+# ============================================================================ config 5: psum
+def run_psum(a, world, rank, local):
     import torch
-    torch.cuda.set_device(local)
-    if world > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
-    try:
-        return {"dp": run_dp, "gemm": run_gemm, "psum": run_psum, "fused": run_fused,
-                "attn_bwd": run_attn_bwd}[a.workload](a, world, rank, local)
-    finally:
+    from pjrt_b200 import configs
+    L = lib()
+    client, store = make_client(world, rank, local)
+    rows = []
+    for kb in (4, 16, 64, 256, 1024, 4096, 16384, 65536, 262144, 1048576):
+        n = kb * 1024 // 4
+        p = configs.psum_program(n, world, seed_rank=rank)
+        exe = client.compile(p.text)
+        buf = client.buffer_from_host(p.inputs[0])
+        _pipelined(exe, [buf], a.warmup)
+        barrier(world)
+        L.b200_exec_timer(0)
+        _pipelined(exe, [buf], a.steps)
+        ms = max_over_ranks(L.b200_exec_timer(1) / a.steps, world)
+        buf.delete()
+        exe.destroy()
+        algbw = n * 4 / (ms * 1e-3) / 1e9
+        row = {"bytes": n * 4, "ms": round(ms, 5), "algbw_GBs": round(algbw, 2),
+               "busbw_GBs": round(algbw * 2 * (world - 1) / world, 2)}
         if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-            dist.destroy_process_group()
+            # the same all_reduce through torch.distributed (NCCL) for comparison
+            t = torch.randn(n, device="cuda")
+            for _ in range(a.warmup):
+                torch.distributed.all_reduce(t)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            for _ in range(a.steps):
+                torch.distributed.all_reduce(t)
+            e1.record()
+            e1.synchronize()
+            tms = max_over_ranks(e0.elapsed_time(e1) / a.steps, world)
+            row["torch_nccl_busbw_GBs"] = round(n * 4 / (tms * 1e-3) / 1e9 * 2 * (world - 1) / world, 2)
+            del t
+        rows.append(row)
+    client.close()
+    big = rows[-1]
+    return {"value": big["busbw_GBs"], "unit": "GB/s", "metric": "all_reduce (psum) bus GB/s at 1 GiB f32",
+            "config": {"workload": "psum sweep 4 KiB .. 1 GiB through PJRT (NCCL)", "nvlink_peak_GBs_per_direction": 900,
+                       "nvlink_measured_peer_copy_GBs": 770},
+            "sweep": rows}
+
+
+# ============================================================================ CPU baselines
+def cpu_gpt2_step(layers, steps=1, batch=1, seed=0):
+    """torch-CPU f32 GPT-2 train step (oracle/torch_ref.py) on all host cores: `batch` sequences of
+    1024 tokens per step, timed over `steps` steps after one untimed step.  Returns (tokens/s,
+    seconds per step, threads)."""
+    import torch
+    from oracle import torch_ref
+    from pjrt_b200 import configs
+    threads = torch_ref.host_threads()
+    torch.set_num_threads(threads)
+    cfg = dict(configs.GPT2_SMALL, layers=layers)
+    shapes = torch_ref.gpt2_param_shapes(**{k: cfg[k] for k in ("layers", "d", "heads", "mlp", "vocab", "seq")})
+    ins = configs.gpt2_inputs(shapes, batch, cfg["seq"], cfg["vocab"], seed=seed, dtype="f32")
+    hp = dict(lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1)
+    kw = dict(layers=cfg["layers"], d=cfg["d"], heads=cfg["heads"], mlp=cfg["mlp"], vocab=cfg["vocab"], seq=cfg["seq"], **hp)
+    torch_ref.gpt2_step(ins, dtype="f32", **kw)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        torch_ref.gpt2_step(ins, dtype="f32", **kw)
+    dt = (time.perf_counter() - t0) / steps
+    return batch * cfg["seq"] / dt, dt, threads

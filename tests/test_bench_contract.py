@@ -30,7 +30,7 @@ def _check(line, n_gpus):
 
 
 def test_reference_arm_prints_one_contract_line():
-    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0"],
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0", "--layers", "1"],
                        cwd=ROOT, capture_output=True, timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = _lines(r.stdout)
@@ -45,7 +45,7 @@ def test_reference_arm_under_torchrun_two_ranks():
     env = dict(os.environ, OMP_NUM_THREADS="1")
     r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
                         "--master-addr", "127.0.0.1", "--master-port", str(port), "bench.py", "--impl", "reference",
-                        "--gpus", "2", "--steps", "1", "--warmup", "0"],
+                        "--gpus", "2", "--steps", "1", "--warmup", "0", "--layers", "1"],
                        cwd=ROOT, capture_output=True, timeout=600, env=env)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = _lines(r.stdout)

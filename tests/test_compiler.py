@@ -61,17 +61,29 @@ def test_dot_reads_mn_major_operands_in_place(lib_path):
     assert "transpose" not in rep and "gemm b1 512x384x256 kn" in rep and "gemm b1 256x384x512 mn" in rep, rep
 
 
-def test_f32_dot_operand_is_stored_narrow_and_read_in_place(lib_path):
+@pytest.mark.parametrize("out", ["bf16", "f32"])
+def test_f32_dot_operand_is_stored_narrow_only_for_16bit_results(lib_path, out):
+    """An f32 operand whose dots have bf16 partners and bf16 results is stored rounded and read in
+    place by the tensor cores; with f32 results the dots are f32-accurate split products that read
+    the f32 value in place."""
     b = Builder("jit_cot")
     x = b.arg((256, 96), "bf16")
     w = b.arg((1001, 96), "bf16")
     z = b.arg((256, 1001), "f32")
     g = b.exp(z) - z
-    dx = b.dot_general(g, w, contract=([1], [0]), out_dtype="f32")
-    dw = b.dot_general(g, x, contract=([0], [0]), out_dtype="f32")
+    dx = b.dot_general(g, w, contract=([1], [0]), out_dtype=out)
+    dw = b.dot_general(g, x, contract=([0], [0]), out_dtype=out)
     rc, rep = report(lib_path, b.text([dx, dw]))
     assert rc == 0, rep
     assert "transpose" not in rep and rep.count("gemm") == 2 and "loop" in rep, rep
+    assert (rep.count("f32-split") == 2) == (out == "f32"), rep
+
+
+def test_large_f32_dots_use_the_split_tensor_core_product(lib_path):
+    rc, rep = report(lib_path, configs.gemm_program(1024, 1024, 1024, dtype="f32", with_inputs=False).text)
+    assert rc == 0 and "f32-split" in rep, rep
+    rc, rep = report(lib_path, configs.mlp_program(with_inputs=False).text)   # [128,784] x [784,512]: small
+    assert rc == 0 and "f32-split" not in rep and "f32-simt" in rep, rep
 
 
 def test_psum_is_identity_on_one_rank_and_a_collective_on_many(lib_path):

@@ -5,6 +5,7 @@ import numpy as np
 import pytest
 
 from conftest import RTOL_BF16, RTOL_F32, assert_close, rel_err
+from oracle import torch_ref
 from oracle.interp import run as oracle_run, run_spmd
 from pjrt_b200 import configs
 
@@ -38,47 +39,10 @@ HP = dict(lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1)
 
 
 def torch_gpt_step(inputs, layers, d, heads, mlp, vocab, seq, lr, b1, b2, eps, wd, gelu_c=0.044715):
-    """The same train step written independently with torch autograd in float64: pre-LN decoder,
-    causal softmax attention, GELU(tanh) MLP, tied LM head, mean cross-entropy, AdamW with decay on
-    the 2-D parameters.  Returns (new params..., new m..., new v..., loss) like the program."""
-    import torch
-    shapes = configs.gpt2_param_shapes(layers, d, heads, mlp, vocab, seq)
-    n = len(shapes)
-    P = {nm: torch.tensor(np.asarray(inputs[i], np.float64), requires_grad=True) for i, (nm, _) in enumerate(shapes)}
-    ids = torch.tensor(np.asarray(inputs[3 * n], np.int64))
-    tgt = torch.tensor(np.asarray(inputs[3 * n + 1], np.int64))
-    bc1, bc2 = float(inputs[3 * n + 2]), float(inputs[3 * n + 3])
-    B, S = ids.shape
-    H, Dh = heads, d // heads
-
-    def ln(x, g, bias):
-        xc = x - x.mean(-1, keepdim=True)
-        return xc * torch.rsqrt((xc * xc).mean(-1, keepdim=True) + 1e-5) * g + bias
-
-    x = (P["wte"][ids] + P["wpe"][None]).reshape(B * S, d)
-    causal = torch.tril(torch.ones(S, S, dtype=torch.bool))
-    for l in range(layers):
-        w = lambda k: P[f"h{l}.{k}"]
-        qkv = ln(x, w("ln1_g"), w("ln1_b")) @ w("w_qkv") + w("b_qkv")
-        q, k, v = [qkv[:, i * d:(i + 1) * d].reshape(B, S, H, Dh).transpose(1, 2) for i in range(3)]
-        s = ((q @ k.transpose(-1, -2)) / np.sqrt(Dh)).masked_fill(~causal, float("-inf"))
-        o = (torch.softmax(s, -1) @ v).transpose(1, 2).reshape(B * S, d)
-        x = x + o @ w("w_proj") + w("b_proj")
-        f = ln(x, w("ln2_g"), w("ln2_b")) @ w("w_fc") + w("b_fc")
-        x = x + (0.5 * f * (1 + torch.tanh(np.sqrt(2 / np.pi) * (f + gelu_c * f ** 3)))) @ w("w_fc2") + w("b_fc2")
-    logits = ln(x, P["lnf_g"], P["lnf_b"]) @ P["wte"].T
-    loss = torch.nn.functional.cross_entropy(logits, tgt.reshape(-1))
-    loss.backward()
-    newp, newm, newv = [], [], []
-    for i, (nm, shp) in enumerate(shapes):
-        g, pv = P[nm].grad, P[nm].detach()
-        m1 = b1 * torch.tensor(np.asarray(inputs[n + i], np.float64)) + (1 - b1) * g
-        v1 = b2 * torch.tensor(np.asarray(inputs[2 * n + i], np.float64)) + (1 - b2) * g * g
-        decay = wd if len(shp) == 2 else 0.0
-        newp.append((pv - lr * ((m1 / bc1) / (torch.sqrt(v1 / bc2) + eps) + decay * pv)).numpy())
-        newm.append(m1.numpy())
-        newv.append(v1.numpy())
-    return newp + newm + newv + [loss.detach().numpy()]
+    """The same train step written independently with torch autograd in float64 (oracle/torch_ref.py):
+    pre-LN decoder, causal softmax attention, GELU(tanh) MLP, tied LM head, mean cross-entropy, AdamW
+    with decay on the 2-D parameters."""
+    return torch_ref.gpt2_step(inputs, layers, d, heads, mlp, vocab, seq, lr, b1, b2, eps, wd, gelu_c=gelu_c, dtype="f64")
 
 
 def _scaled_f32_inputs(batch, scale, world=1):

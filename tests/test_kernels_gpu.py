@@ -215,3 +215,92 @@ def test_gemm_split_k_f32(lib, cuda, batch, M, N, K):
     check_device_error(lib)
     ref = torch.bmm(a.float(), b.float().transpose(1, 2))
     assert rel_err(c.cpu().numpy(), ref.cpu().numpy()) <= RTOL_F32 * 10
+
+
+def _split_lib(lib):
+    lib.b200_gemm_split_scratch_bytes.argtypes = [ctypes.c_int64] * 4 + [ctypes.c_int, ctypes.c_int]
+    lib.b200_gemm_split_scratch_bytes.restype = ctypes.c_size_t
+    lib.b200_gemm_split.argtypes = ([ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p] +
+                                    [ctypes.c_int64] * 4 + [ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p])
+    return lib
+
+
+def run_split_gemm(lib, torch, a, b, out_dt):
+    """C = A . B^T through b200_gemm_split for torch operands [batch, M, K] / [batch, N, K]."""
+    code = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
+    batch, M, K = a.shape
+    N = b.shape[1]
+    _split_lib(lib)
+    nbytes = lib.b200_gemm_split_scratch_bytes(batch, M, N, K, code[a.dtype], code[b.dtype])
+    scratch = torch.empty(max(nbytes, 1), dtype=torch.uint8, device="cuda")
+    c = torch.empty(batch, M, N, device="cuda", dtype=out_dt)
+    rc = lib.b200_gemm_split(a.data_ptr(), code[a.dtype], b.data_ptr(), code[b.dtype], c.data_ptr(), batch, M, N, K,
+                             code[out_dt], scratch.data_ptr(), nbytes, stream(torch))
+    assert rc == 0, rc
+    torch.cuda.synchronize()
+    check_device_error(lib)
+    return c
+
+
+@pytest.mark.parametrize("ta,tb", [("f32", "f32"), ("bf16", "f32"), ("f32", "bf16"), ("f16", "f32")])
+@pytest.mark.parametrize("batch,M,N,K", [(1, 128, 256, 64), (1, 300, 200, 100), (2, 1000, 520, 1000), (1, 77, 50, 8),
+                                         (1, 1024, 1024, 1024), (3, 256, 136, 4100)])
+def test_gemm_split_is_f32_accurate(lib, cuda, ta, tb, batch, M, N, K):
+    """f32 (and mixed f32 x 16-bit) products on the bf16 tensor cores through three-piece splits hold
+    the f32 bar against float64, including ragged M / N / K and K % 64 != 0."""
+    torch = cuda
+    dt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
+    g = torch.Generator(device="cuda").manual_seed(M + 3 * N + 7 * K + batch)
+    a = (torch.randn(batch, M, K, device="cuda", generator=g, dtype=torch.float64) / K ** 0.5).to(dt[ta])
+    b = torch.randn(batch, N, K, device="cuda", generator=g, dtype=torch.float64).to(dt[tb])
+    c = run_split_gemm(lib, torch, a, b, torch.float32)
+    ref = torch.bmm(a.double(), b.double().transpose(1, 2))
+    assert rel_err(c.cpu().numpy(), ref.cpu().numpy()) <= RTOL_F32
+
+
+def test_gemm_split_bf16_result_and_wide_range(lib, cuda):
+    """A bf16 result rounds once from the f32-accurate product; operands spanning 2^-30 .. 2^30 keep
+    their small terms (each piece is a bf16 of its own remainder, with f32's exponent range)."""
+    torch = cuda
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.randn(1, 256, 512, device="cuda", generator=g) * torch.exp2(torch.randint(-30, 30, (1, 256, 512), device="cuda",
+                                                                                      generator=g).float())
+    b = torch.randn(1, 192, 512, device="cuda", generator=g)
+    c32 = run_split_gemm(lib, torch, a, b, torch.float32)
+    ref = torch.bmm(a.double(), b.double().transpose(1, 2))
+    assert rel_err(c32.cpu().numpy(), ref.cpu().numpy()) <= RTOL_F32
+    c16 = run_split_gemm(lib, torch, a, b, torch.bfloat16)
+    assert torch.equal(c16, ref.float().to(torch.bfloat16)) or rel_err(c16.float().cpu().numpy(), ref.cpu().numpy()) <= 2 ** -8
+
+
+def test_bounded_wait_runs_out_and_reports_without_faulting(lib, cuda):
+    """The pipelines' bounded mbarrier wait, on a barrier nobody arrives at with a ~1 ms budget, gives
+    up, records its error code and returns: the host reads the code once, and the context keeps
+    working (a GEMM afterwards is correct)."""
+    torch = cuda
+    lib.b200_selftest_wait_timeout.argtypes = [ctypes.c_longlong, ctypes.c_void_p, ctypes.c_void_p]
+    check_device_error(lib)
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert lib.b200_selftest_wait_timeout(2_000_000, flag.data_ptr(), stream(torch)) == 0
+    torch.cuda.synchronize()
+    assert int(flag.item()) == 1
+    assert lib.b200_take_device_error() == 1            # a timed-out pipeline wait
+    assert lib.b200_take_device_error() == 0            # read once, then cleared
+    a = torch.randn(1, 256, 128, device="cuda").to(torch.bfloat16)
+    b = torch.randn(1, 128, 128, device="cuda").to(torch.bfloat16)
+    c = torch.empty(1, 256, 128, device="cuda")
+    assert lib.b200_gemm(a.data_ptr(), b.data_ptr(), c.data_ptr(), 1, 256, 128, 128, BF16, F32, stream(torch)) == 0
+    torch.cuda.synchronize()
+    check_device_error(lib)
+    assert rel_err(c.cpu().numpy(), torch.bmm(a.float(), b.float().transpose(1, 2)).cpu().numpy()) <= RTOL_F32 * 10
+
+
+def test_kernel_launch_counter_counts_this_librarys_launches(lib, cuda):
+    torch = cuda
+    lib.b200_kernel_launches.restype = ctypes.c_longlong
+    a = torch.randn(1, 256, 64, device="cuda").to(torch.bfloat16)
+    c = torch.empty(1, 256, 256, device="cuda")
+    n0 = lib.b200_kernel_launches()
+    for _ in range(3):
+        assert lib.b200_gemm(a.data_ptr(), a.data_ptr(), c.data_ptr(), 1, 256, 256, 64, BF16, F32, stream(torch)) == 0
+    assert lib.b200_kernel_launches() - n0 == 3

@@ -110,10 +110,12 @@ def test_gemm_vs_oracle(client, dtype, M, N, K, batch):
     assert_close(out, ref, RTOL_F32 if dtype == "f32" else RTOL_F32 * 10, "gemm")
 
 
-@pytest.mark.parametrize("K,N,out", [(50, 70, "f32"), (50257 // 41, 333, "bf16"), (768, 1001, "f32")])
+@pytest.mark.parametrize("K,N,out", [(50, 70, "f32"), (50257 // 41, 333, "bf16"), (768, 1001, "f32"), (1000, 520, "bf16")])
 def test_dot_mixed_precision_and_unaligned_shapes(client, K, N, out):
-    """bf16 x f32 operands (a backward-pass cotangent meeting bf16 weights) run on the tensor cores in
-    bf16; K % 8 != 0 takes the padded-pitch operand copy; N % 8 != 0 the staged epilogue."""
+    """bf16 x f32 operands (a backward-pass cotangent meeting bf16 weights).  With an f32 result the
+    dot is f32 arithmetic (the f32 operand split into bf16 pieces on the tensor cores) and holds the
+    f32 bar; with a bf16 result the f32 operand is rounded to bf16 once and the result holds the bf16
+    bar.  K % 8 != 0 takes the padded operand layout; N % 8 != 0 the staged epilogue."""
     b = Builder("jit_mixed_dot")
     x = b.arg((200, K), "bf16")
     w = b.arg((K, N), "f32")
@@ -124,7 +126,8 @@ def test_dot_mixed_precision_and_unaligned_shapes(client, K, N, out):
            rng.standard_normal((K, N)).astype(np.float32)]
     got = client.run(text, ins)[0]
     ref = oracle_run(text, ins)[0]
-    assert_close(np.asarray(got, np.float32), np.asarray(ref, np.float32), 1e-2, "mixed dot")
+    assert_close(np.asarray(got, np.float32), np.asarray(ref, np.float32), RTOL_F32 if out == "f32" else RTOL_BF16,
+                 "mixed dot")
 
 
 @pytest.mark.parametrize("lhs_c,rhs_c", [(1, 0), (0, 0), (1, 1), (0, 1)])
@@ -146,18 +149,20 @@ def test_dot_operand_layouts(client, lhs_c, rhs_c, dtype, M, N, K):
     assert_close(got, ref, RTOL_F32 if dtype == "f32" else RTOL_F32 * 10, "dot layouts")
 
 
+@pytest.mark.parametrize("out", ["bf16", "f32"])
 @pytest.mark.parametrize("V", [1001, 1000, 1024])
-def test_f32_cotangent_feeding_two_dots(client, V):
-    """An f32 value read only by dots with bf16 partners (the logits cotangent of an LM head) is stored
-    rounded to bf16, with a padded row pitch when V % 8 != 0, and both dots (dX = g W^T, dW = x^T g)
-    read it in place."""
+def test_f32_cotangent_feeding_two_dots(client, V, out):
+    """An f32 value read by two dots with bf16 partners (the logits cotangent of an LM head: dX = g W^T,
+    dW = x^T g).  With bf16 results it is stored rounded to bf16 (a padded row pitch when V % 8 != 0)
+    and read in place, the results held to the bf16 bar; with f32 results the dots are f32-accurate
+    (split into bf16 pieces) and held to the f32 bar."""
     b = Builder("jit_cotangent")
     x = b.arg((256, 96), "bf16")
     w = b.arg((V, 96), "bf16")
     z = b.arg((256, V), "f32")
     g = b.exp(z) * 0.5 - z                       # f32 [256, V], produced by a loop kernel
-    dx = b.dot_general(g, w, contract=([1], [0]), out_dtype="f32")
-    dw = b.dot_general(g, x, contract=([0], [0]), out_dtype="f32")
+    dx = b.dot_general(g, w, contract=([1], [0]), out_dtype=out)
+    dw = b.dot_general(g, x, contract=([0], [0]), out_dtype=out)
     text = b.text([dx, dw])
     rng = np.random.default_rng(V)
     ins = [(rng.standard_normal((256, 96)) * 0.3).astype(ml_dtypes.bfloat16),
@@ -166,7 +171,7 @@ def test_f32_cotangent_feeding_two_dots(client, V):
     outs = client.run(text, ins)
     refs = oracle_run(text, ins)
     for o, r, name in zip(outs, refs, ("dx", "dw")):
-        assert_close(o, r, 1e-2, name)
+        assert_close(np.asarray(o, np.float32), np.asarray(r, np.float32), RTOL_F32 if out == "f32" else RTOL_BF16, name)
 
 
 @pytest.mark.parametrize("splitk", [True, False])
