@@ -1,17 +1,29 @@
-// plugin.cc — PJRT C-API v0.55 implementation for B200 (the drop-in boundary).
+// plugin.cc — the PJRT C API (v0.55) over B200 devices: the plugin's drop-in boundary, GetPjrtApi.
 //
-// Mirrors the reference plugin's surface and error behaviour (src/pjrt/api/pjrt_c_api.cc): the same
-// entry points are real, the same ones answer UNIMPLEMENTED (:833-873), errors carry the same codes
-// (INVALID_ARGUMENT for bad arguments and "jam compile: ..." compile failures, RESOURCE_EXHAUSTED for
-// allocation, INTERNAL for execute / communicator failures).  What changes is underneath: buffers
-// live in HBM (stream-ordered CUDA pool), transfers are cudaMemcpyAsync on the device stream, events
-// are CUDA events, Execute enqueues asynchronously and returns events that complete on the GPU.
+// The reference plugin (src/pjrt/api/pjrt_c_api.cc) fixes what a caller sees: which entry points
+// work and which answer UNIMPLEMENTED (its list at :833-873), the error codes (INVALID_ARGUMENT for
+// bad arguments and "jam compile: ..." failures, RESOURCE_EXHAUSTED for allocation, INTERNAL for
+// execution and communicator failures), one addressable device per process, and two memories per
+// device ("device", "pinned_host").  The implementation here is its own:
+//
+//   PJRT_Client   the process's view of a job of `world` processes: one device per process, the local
+//                 one bound to a CUDA ordinal; the NCCL communicator when world > 1.
+//   PJRT_Device   a global device id with its two memory spaces embedded (HBM and page-locked host
+//                 memory) and, for the local device, the executor's CUDA state.
+//   PJRT_Buffer   typed, shaped storage in one memory space -- HBM from the executor's stream-ordered
+//                 pool, or cudaHostAlloc'd host memory -- with a completion for its contents and a
+//                 pin count for external references.
+//   PJRT_Event    a Completion: a CUDA event the host can poll, await or attach callbacks to.
+//   PJRT_(Loaded)Executable   a compiled b200::Executable and its output signature.
+// The API table is bound from small lambdas grouped by object (Bind* below).
 #include <cuda_runtime.h>
 
 #include <atomic>
 #include <condition_variable>
+#include <cstddef>
 #include <cstdlib>
 #include <cstring>
+#include <deque>
 #include <functional>
 #include <memory>
 #include <mutex>
@@ -25,1153 +37,1108 @@
 #include "../jam/runtime.h"
 
 struct PJRT_Error {
-  PJRT_Error_Code code = PJRT_Error_Code_UNKNOWN;
-  std::string message;
+  PJRT_Error_Code code;
+  std::string text;
 };
 
-namespace {
+namespace b200pj {
 
-PJRT_Error* Err(PJRT_Error_Code c, const std::string& m) { return new PJRT_Error{c, m}; }
+PJRT_Error* Fail(PJRT_Error_Code code, std::string text) { return new PJRT_Error{code, std::move(text)}; }
+PJRT_Error* BadArg(std::string text) { return Fail(PJRT_Error_Code_INVALID_ARGUMENT, std::move(text)); }
 
-// Shared completion state: a PJRT_Event and any waiter threads hold it.
-struct EventState {
-  std::mutex mu;
-  std::condition_variable cv;
-  bool ready = false;
-  bool has_error = false;
-  PJRT_Error_Code code = PJRT_Error_Code_UNKNOWN;
-  std::string message;
-  cudaEvent_t ev = nullptr;
-  int device = -1;
-  bool check_kernels = false;   // read the tensor-core kernels' timeout flag on completion
-  std::vector<std::pair<PJRT_Event_OnReadyCallback, void*>> callbacks;
+// Writes a plugin-owned string into a (pointer, size) pair of an Args struct.
+inline void Put(const std::string& s, const char** p, size_t* n) {
+  *p = s.data();
+  *n = s.size();
+}
 
-  ~EventState() {
-    if (ev) cudaEventDestroy(ev);
+const std::string kPlatform = "b200";
+const std::string kPlatformVersion = "pjrt-b200 0.2.0 (PJRT 0.55, sm_100a)";
+
+// ------------------------------------------------------------------------------------ completions
+// The state behind a PJRT_Event: done once the CUDA event it recorded has completed on the GPU (or
+// at once, for host-side work).  Callbacks run when it completes; a completion that follows kernel
+// launches also reads the tensor-core kernels' timed-out-wait flag and turns it into an error.
+class Completion {
+ public:
+  static std::shared_ptr<Completion> Done() {
+    auto c = std::make_shared<Completion>();
+    c->done_ = true;
+    return c;
   }
-  // Blocks until the GPU work is done; idempotent.
-  void Complete() {
-    std::vector<std::pair<PJRT_Event_OnReadyCallback, void*>> cbs;
+  // Records an event on `stream`; falls back to a stream synchronize if that fails.
+  static std::shared_ptr<Completion> After(int ordinal, cudaStream_t stream, bool reads_kernel_flags) {
+    auto c = std::make_shared<Completion>();
+    c->ordinal_ = ordinal;
+    c->reads_kernel_flags_ = reads_kernel_flags;
+    if (cudaEventCreateWithFlags(&c->event_, cudaEventDisableTiming) == cudaSuccess &&
+        cudaEventRecord(c->event_, stream) == cudaSuccess)
+      return c;
+    cudaGetLastError();
+    if (c->event_) cudaEventDestroy(c->event_);
+    c->event_ = nullptr;
+    cudaStreamSynchronize(stream);
+    c->done_ = true;
+    return c;
+  }
+  ~Completion() {
+    if (event_) cudaEventDestroy(event_);
+  }
+
+  // Blocks until done, then runs the callbacks (once).
+  void Wait() {
     {
-      std::unique_lock<std::mutex> lock(mu);
-      if (ready) return;
+      std::lock_guard<std::mutex> g(mu_);
+      if (done_) return;
     }
-    if (ev) {
-      cudaSetDevice(device);
-      cudaError_t e = cudaEventSynchronize(ev);
-      std::lock_guard<std::mutex> lock(mu);
+    PJRT_Error_Code code = PJRT_Error_Code_UNKNOWN;
+    std::string problem;
+    if (event_) {
+      cudaSetDevice(ordinal_);
+      const cudaError_t e = cudaEventSynchronize(event_);
       if (e != cudaSuccess) {
-        has_error = true;
         code = PJRT_Error_Code_INTERNAL;
-        message = std::string("device execution failed: ") + cudaGetErrorString(e);
-      } else if (check_kernels) {
-        int k = b200_take_device_error();
-        if (k) {
-          has_error = true;
+        problem = std::string("device execution failed: ") + cudaGetErrorString(e);
+      } else if (reads_kernel_flags_) {
+        if (const int k = b200_take_device_error()) {
           code = PJRT_Error_Code_DEADLINE_EXCEEDED;
-          message = "a tensor-core kernel gave up waiting on a pipeline barrier (code " + std::to_string(k) + ")";
+          problem = "a tensor-core kernel gave up waiting on a pipeline barrier (code " + std::to_string(k) + ")";
         }
       }
     }
+    std::vector<std::pair<PJRT_Event_OnReadyCallback, void*>> run;
     {
-      std::lock_guard<std::mutex> lock(mu);
-      ready = true;
-      cbs.swap(callbacks);
+      std::lock_guard<std::mutex> g(mu_);
+      if (done_) return;
+      done_ = true;
+      failed_ = !problem.empty();
+      code_ = code;
+      problem_ = problem;
+      run.swap(callbacks_);
     }
-    cv.notify_all();
-    for (auto& cb : cbs) cb.first(MakeError(), cb.second);
+    for (auto& cb : run) cb.first(Status(), cb.second);
   }
-  bool Poll() {
+  bool Ready() {
     {
-      std::lock_guard<std::mutex> lock(mu);
-      if (ready) return true;
+      std::lock_guard<std::mutex> g(mu_);
+      if (done_) return true;
     }
-    if (ev) {
-      cudaSetDevice(device);
-      if (cudaEventQuery(ev) == cudaErrorNotReady) return false;
+    if (event_) {
+      cudaSetDevice(ordinal_);
+      if (cudaEventQuery(event_) == cudaErrorNotReady) return false;
     }
-    Complete();
+    Wait();
     return true;
   }
-  PJRT_Error* MakeError() {
-    return has_error ? Err(code, message) : nullptr;
+  // A new PJRT_Error for a failed completion (the caller owns it), null otherwise.
+  PJRT_Error* Status() {
+    std::lock_guard<std::mutex> g(mu_);
+    return failed_ ? Fail(code_, problem_) : nullptr;
+  }
+  // Runs `cb` now if done, else when done (a helper thread waits for the GPU).
+  void Then(PJRT_Event_OnReadyCallback cb, void* arg, const std::shared_ptr<Completion>& self) {
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      if (!done_) {
+        callbacks_.emplace_back(cb, arg);
+        std::thread([self] { self->Wait(); }).detach();
+        return;
+      }
+    }
+    cb(Status(), arg);
+  }
+
+ private:
+  std::mutex mu_;
+  bool done_ = false, failed_ = false, reads_kernel_flags_ = false;
+  PJRT_Error_Code code_ = PJRT_Error_Code_UNKNOWN;
+  std::string problem_;
+  cudaEvent_t event_ = nullptr;
+  int ordinal_ = 0;
+  std::vector<std::pair<PJRT_Event_OnReadyCallback, void*>> callbacks_;
+};
+
+using CompletionRef = std::shared_ptr<Completion>;
+
+// ------------------------------------------------------------------------------------ element types
+// Bytes per element of each PJRT_Buffer_Type, indexed by the enum value (0: not storable here).
+constexpr uint8_t kElementBytes[] = {
+    /*INVALID*/ 0, /*PRED*/ 1, /*S8*/ 1, /*S16*/ 2, /*S32*/ 4, /*S64*/ 8, /*U8*/ 1, /*U16*/ 2, /*U32*/ 4, /*U64*/ 8,
+    /*F16*/ 2, /*F32*/ 4, /*F64*/ 8, /*BF16*/ 2, /*C64*/ 8, /*C128*/ 16, /*F8E5M2*/ 1, /*F8E4M3FN*/ 1,
+    /*F8E4M3B11FNUZ*/ 1, /*F8E5M2FNUZ*/ 1, /*F8E4M3FNUZ*/ 1, /*S4*/ 0, /*U4*/ 0, /*TOKEN*/ 0, /*S2*/ 0, /*U2*/ 0,
+    /*F8E4M3*/ 1, /*F8E3M4*/ 1};
+
+size_t ElementBytes(PJRT_Buffer_Type t) {
+  const size_t i = (size_t)t;
+  return i < sizeof(kElementBytes) ? kElementBytes[i] : 0;
+}
+
+// The compiler's element types and the PJRT ones (same names, PJRT numbering).
+PJRT_Buffer_Type PjrtTypeOf(b200::DT d) {
+  static const PJRT_Buffer_Type kMap[] = {
+      PJRT_Buffer_Type_PRED, PJRT_Buffer_Type_S8,  PJRT_Buffer_Type_S16,  PJRT_Buffer_Type_S32, PJRT_Buffer_Type_S64,
+      PJRT_Buffer_Type_U8,   PJRT_Buffer_Type_U16, PJRT_Buffer_Type_U32,  PJRT_Buffer_Type_U64, PJRT_Buffer_Type_F16,
+      PJRT_Buffer_Type_BF16, PJRT_Buffer_Type_F32, PJRT_Buffer_Type_F64};
+  const size_t i = (size_t)d;
+  return i < sizeof(kMap) / sizeof(kMap[0]) ? kMap[i] : PJRT_Buffer_Type_INVALID;
+}
+
+std::string ShapeText(PJRT_Buffer_Type t, const std::vector<int64_t>& dims) {
+  std::string s = "type " + std::to_string((int)t) + " [";
+  for (size_t i = 0; i < dims.size(); ++i) s += (i ? "x" : "") + std::to_string(dims[i]);
+  return s + "]";
+}
+
+// The two memory spaces every device has.
+enum class Space : int { kHbm = 0, kPinnedHost = 1 };
+const std::string kSpaceKind[2] = {"device", "pinned_host"};
+
+int EnvInt(const char* name, int fallback) {
+  const char* v = std::getenv(name);
+  return v && *v ? std::atoi(v) : fallback;
+}
+
+// Named values the plugin reports (device attributes); owns the strings the entries point at.
+class Attributes {
+ public:
+  void AddString(const std::string& name, const std::string& value) {
+    Entry& e = Push(name);
+    e.text = value;
+    e.nv.type = PJRT_NamedValue_kString;
+  }
+  void AddInt(const std::string& name, int64_t value) {
+    Entry& e = Push(name);
+    e.nv.type = PJRT_NamedValue_kInt64;
+    e.nv.int64_value = value;
+    e.nv.value_size = 1;
+  }
+  // The PJRT_NamedValue array (pointers into this object; valid while it lives unchanged).
+  const PJRT_NamedValue* Values() {
+    flat_.clear();
+    for (Entry& e : entries_) {
+      e.nv.name = e.name.c_str();
+      e.nv.name_size = e.name.size();
+      if (e.nv.type == PJRT_NamedValue_kString) {
+        e.nv.string_value = e.text.c_str();
+        e.nv.value_size = e.text.size();
+      }
+      flat_.push_back(e.nv);
+    }
+    return flat_.data();
+  }
+  size_t Count() const { return entries_.size(); }
+
+ private:
+  struct Entry {
+    std::string name, text;
+    PJRT_NamedValue nv;
+  };
+  Entry& Push(const std::string& name) {
+    entries_.emplace_back();
+    Entry& e = entries_.back();
+    std::memset(&e.nv, 0, sizeof(e.nv));
+    e.nv.struct_size = sizeof(PJRT_NamedValue);
+    e.name = name;
+    return e;
+  }
+  std::deque<Entry> entries_;
+  std::vector<PJRT_NamedValue> flat_;
+};
+
+// The output signature of a compiled program in the shapes PJRT returns it.
+struct Signature {
+  std::vector<PJRT_Buffer_Type> types;
+  std::vector<size_t> ranks;
+  std::vector<int64_t> dims;                   // all outputs' dims, concatenated
+  std::vector<const char*> kinds;
+  std::vector<size_t> kind_sizes;
+  explicit Signature(const b200::Plan& plan) {
+    for (const b200::TensorType& t : plan.out_types) {
+      types.push_back(PjrtTypeOf(t.dt));
+      ranks.push_back(t.dims.size());
+      dims.insert(dims.end(), t.dims.begin(), t.dims.end());
+      kinds.push_back(kSpaceKind[0].c_str());
+      kind_sizes.push_back(kSpaceKind[0].size());
+    }
   }
 };
 
-std::shared_ptr<EventState> ReadyState() {
-  auto s = std::make_shared<EventState>();
-  s->ready = true;
-  return s;
-}
+}  // namespace b200pj
 
-std::shared_ptr<EventState> RecordState(int device, cudaStream_t st, bool check_kernels = false) {
-  auto s = std::make_shared<EventState>();
-  s->device = device;
-  s->check_kernels = check_kernels;
-  if (cudaEventCreateWithFlags(&s->ev, cudaEventDisableTiming) != cudaSuccess || cudaEventRecord(s->ev, st) != cudaSuccess) {
-    cudaGetLastError();
-    if (s->ev) cudaEventDestroy(s->ev);
-    s->ev = nullptr;
-    cudaStreamSynchronize(st);
-    s->ready = true;
-  }
-  return s;
-}
+using namespace b200pj;
 
-}  // namespace
-
+// ======================================================================================= objects
 struct PJRT_Event {
-  std::shared_ptr<EventState> s;
+  CompletionRef done;
 };
 
 struct PJRT_DeviceDescription {
-  int id = 0;
-  int process_index = 0;
+  int global_id = 0;
+  int process = 0;
   std::string kind = "NVIDIA B200";
-  std::string debug_string;
-  std::string to_string;
-  std::vector<PJRT_NamedValue> attrs;
-  std::vector<std::string> attr_names;
-  std::string cc;
-  int64_t core_count = 0;
-};
+  std::string summary;       // ToString
+  std::string detail;        // DebugString
+  Attributes attributes;
+  const PJRT_NamedValue* attribute_values = nullptr;
 
-struct PJRT_Device {
-  PJRT_DeviceDescription description;
-  PJRT_Client* client = nullptr;
-  int local_hardware_id = -1;
-  bool addressable = false;
-  std::vector<PJRT_Memory*> memories;
-  PJRT_Memory* default_memory = nullptr;
-  b200::DeviceState state;
-  std::mutex exec_mu;
+  // Fills the description of global device `id`; `ordinal` >= 0 reads the local GPU's properties.
+  void Describe(int id, int ordinal) {
+    global_id = id;
+    process = id;                 // one device per process
+    int major = 10, minor = 0, sms = 148;
+    size_t hbm = 0;
+    cudaDeviceProp prop;
+    if (ordinal >= 0 && cudaGetDeviceProperties(&prop, ordinal) == cudaSuccess) {
+      kind = prop.name;
+      major = prop.major;
+      minor = prop.minor;
+      sms = prop.multiProcessorCount;
+      hbm = prop.totalGlobalMem;
+    }
+    summary = "B200(id=" + std::to_string(id) + ", process=" + std::to_string(process) + ")";
+    detail = "b200 device " + std::to_string(id) + (ordinal >= 0 ? " on cuda:" + std::to_string(ordinal) : " (remote)") +
+             ", sm_" + std::to_string(major) + std::to_string(minor) + "a, " + std::to_string(sms) + " SMs";
+    attributes.AddString("compute_capability", std::to_string(major) + "." + std::to_string(minor));
+    attributes.AddInt("core_count", sms);
+    attributes.AddString("device_vendor", "NVIDIA");
+    if (hbm) attributes.AddInt("hbm_bytes", (int64_t)hbm);
+    attribute_values = attributes.Values();
+  }
 };
 
 struct PJRT_Memory {
+  Space space = Space::kHbm;
   int id = 0;
-  std::string kind;
-  int kind_id = 0;
-  std::string debug_string;
-  std::string to_string;
-  std::vector<PJRT_Device*> devices;
+  std::string summary, detail;
+  PJRT_Device* owner[1] = {nullptr};
+  const std::string& kind() const { return kSpaceKind[(int)space]; }
+};
+
+struct PJRT_Device {
+  PJRT_DeviceDescription desc;
+  PJRT_Client* client = nullptr;
+  int ordinal = -1;                     // CUDA device, -1 unless this process's device
+  PJRT_Memory spaces[2];
+  PJRT_Memory* space_list[2] = {nullptr, nullptr};
+  b200::DeviceState cuda;               // executor state of the local device
+  std::mutex launch_mu;                 // serializes Execute's enqueue on this device
+  bool local() const { return ordinal >= 0; }
+  PJRT_Memory* hbm() { return &spaces[(int)Space::kHbm]; }
 };
 
 struct PJRT_TopologyDescription {
-  std::string platform_name = "b200";
-  std::string platform_version;
-  std::vector<std::unique_ptr<PJRT_DeviceDescription>> owned;
   std::vector<PJRT_DeviceDescription*> descriptions;
+  std::deque<PJRT_DeviceDescription> owned;   // only for a topology created without a client
 };
 
 struct PJRT_Client {
-  std::string platform_name = "b200";
-  std::string platform_version;
-  int process_index = 0;
-  int num_processes = 1;
-  std::vector<std::unique_ptr<PJRT_Device>> owned_devices;
-  std::vector<PJRT_Device*> devices;
-  std::vector<PJRT_Device*> addressable_devices;
-  std::vector<std::unique_ptr<PJRT_Memory>> owned_memories;
-  std::vector<PJRT_Memory*> memories;
-  std::unique_ptr<PJRT_TopologyDescription> topology;
+  int rank = 0, world = 1;
+  std::deque<PJRT_Device> fleet;              // every device of the job, by global id
+  std::vector<PJRT_Device*> all, mine;
+  std::vector<PJRT_Memory*> my_memories;
+  PJRT_TopologyDescription topology;
   std::unique_ptr<b200::Comm> comm;
+
+  PJRT_Device* local() { return mine.front(); }
   ~PJRT_Client() {
-    // drain the compute and communication streams before the communicator goes away
-    for (PJRT_Device* d : addressable_devices) {
-      cudaSetDevice(d->state.ordinal);
-      if (d->state.stream) cudaStreamSynchronize(d->state.stream);
-      if (d->state.comm_stream) cudaStreamSynchronize(d->state.comm_stream);
+    for (PJRT_Device* d : mine) {                 // let queued work drain before the communicator goes
+      cudaSetDevice(d->ordinal);
+      if (d->cuda.stream) cudaStreamSynchronize(d->cuda.stream);
+      if (d->cuda.comm_stream) cudaStreamSynchronize(d->cuda.comm_stream);
     }
     comm.reset();
-    for (PJRT_Device* d : addressable_devices) {
-      cudaSetDevice(d->state.ordinal);
-      if (d->state.stream) cudaStreamDestroy(d->state.stream);
-      if (d->state.comm_stream) cudaStreamDestroy(d->state.comm_stream);
+    for (PJRT_Device* d : mine) {
+      cudaSetDevice(d->ordinal);
+      if (d->cuda.stream) cudaStreamDestroy(d->cuda.stream);
+      if (d->cuda.comm_stream) cudaStreamDestroy(d->cuda.comm_stream);
     }
   }
 };
 
 struct PJRT_Buffer {
+  enum class Life { kLive, kFreeWhenUnpinned, kFreed };
   PJRT_Client* client = nullptr;
-  PJRT_Device* device = nullptr;
-  PJRT_Memory* memory = nullptr;
-  PJRT_Buffer_Type type = PJRT_Buffer_Type_INVALID;
+  PJRT_Memory* where = nullptr;               // memory space, and through it the device
+  PJRT_Buffer_Type etype = PJRT_Buffer_Type_INVALID;
   std::vector<int64_t> dims;
-  size_t nbytes = 0;
-  void* data = nullptr;
-  std::shared_ptr<EventState> ready;
-  int external_refs = 0;
-  bool delete_requested = false;
-  bool deleted = false;
+  size_t bytes = 0;
+  void* ptr = nullptr;                         // device pointer (HBM) or host pointer (pinned host)
+  CompletionRef ready;                         // contents are written once this completes
+  int pins = 0;                                // external references
+  Life life = Life::kLive;
+
+  PJRT_Device* device() const { return where->owner[0]; }
+  bool on_host() const { return where->space == Space::kPinnedHost; }
+  bool usable() const { return life == Life::kLive && (ptr || bytes == 0); }
 };
 
 struct PJRT_ExecuteContext {};
 
 struct PJRT_Executable {
   std::shared_ptr<b200::Executable> program;
-  std::string name;
-  std::vector<PJRT_Buffer_Type> out_types;
-  std::vector<int64_t> out_dims_flat;
-  std::vector<size_t> out_dim_sizes;
-  std::vector<std::string> out_mem_kinds;
-  std::vector<const char*> out_mem_kind_ptrs;
-  std::vector<size_t> out_mem_kind_sizes;
+  Signature outputs;
+  explicit PJRT_Executable(std::shared_ptr<b200::Executable> p) : program(std::move(p)), outputs(program->plan()) {}
 };
 
 struct PJRT_LoadedExecutable {
   PJRT_Client* client = nullptr;
-  std::shared_ptr<b200::Executable> program;
+  std::shared_ptr<b200::Executable> program;   // null once deleted
   std::vector<PJRT_Device*> devices;
-  bool deleted = false;
 };
 
 namespace {
 
-const char* kVersion = "pjrt-b200 0.1.0 (PJRT 0.55, sm_100a)";
-
-size_t ByteWidth(PJRT_Buffer_Type t) {
-  switch (t) {
-    case PJRT_Buffer_Type_PRED: case PJRT_Buffer_Type_S8: case PJRT_Buffer_Type_U8:
-    case PJRT_Buffer_Type_F8E5M2: case PJRT_Buffer_Type_F8E4M3FN: case PJRT_Buffer_Type_F8E4M3B11FNUZ:
-    case PJRT_Buffer_Type_F8E5M2FNUZ: case PJRT_Buffer_Type_F8E4M3FNUZ: case PJRT_Buffer_Type_F8E4M3:
-    case PJRT_Buffer_Type_F8E3M4:
-      return 1;
-    case PJRT_Buffer_Type_S16: case PJRT_Buffer_Type_U16: case PJRT_Buffer_Type_F16: case PJRT_Buffer_Type_BF16:
-      return 2;
-    case PJRT_Buffer_Type_S32: case PJRT_Buffer_Type_U32: case PJRT_Buffer_Type_F32:
-      return 4;
-    case PJRT_Buffer_Type_S64: case PJRT_Buffer_Type_U64: case PJRT_Buffer_Type_F64: case PJRT_Buffer_Type_C64:
-      return 8;
-    case PJRT_Buffer_Type_C128:
-      return 16;
-    default:
-      return 0;
-  }
-}
-
-PJRT_Buffer_Type ToPjrt(b200::DT d) {
-  using b200::DT;
-  switch (d) {
-    case DT::kPred: return PJRT_Buffer_Type_PRED;
-    case DT::kS8: return PJRT_Buffer_Type_S8;
-    case DT::kS16: return PJRT_Buffer_Type_S16;
-    case DT::kS32: return PJRT_Buffer_Type_S32;
-    case DT::kS64: return PJRT_Buffer_Type_S64;
-    case DT::kU8: return PJRT_Buffer_Type_U8;
-    case DT::kU16: return PJRT_Buffer_Type_U16;
-    case DT::kU32: return PJRT_Buffer_Type_U32;
-    case DT::kU64: return PJRT_Buffer_Type_U64;
-    case DT::kF16: return PJRT_Buffer_Type_F16;
-    case DT::kBF16: return PJRT_Buffer_Type_BF16;
-    case DT::kF32: return PJRT_Buffer_Type_F32;
-    case DT::kF64: return PJRT_Buffer_Type_F64;
-    default: return PJRT_Buffer_Type_INVALID;
-  }
-}
-
-std::string DimsStr(const std::vector<int64_t>& d) {
-  std::string s = "[";
-  for (size_t i = 0; i < d.size(); ++i) s += (i ? "," : "") + std::to_string(d[i]);
-  return s + "]";
-}
-
-PJRT_Error* MakeUnimplemented(const char* name) {
-  return Err(PJRT_Error_Code_UNIMPLEMENTED, std::string(name) + " is not implemented by the B200 plugin");
-}
-
-int GetIntEnv(const char* n, int dflt) {
-  const char* v = std::getenv(n);
-  return v && *v ? std::atoi(v) : dflt;
-}
-
-// ------------------------------------------------------------------------------------------ errors
-void ErrorDestroy(PJRT_Error_Destroy_Args* a) { delete a->error; }
-void ErrorMessage(PJRT_Error_Message_Args* a) {
-  a->message = a->error->message.c_str();
-  a->message_size = a->error->message.size();
-}
-PJRT_Error* ErrorGetCode(PJRT_Error_GetCode_Args* a) {
-  a->code = a->error->code;
-  return nullptr;
-}
-
-// ------------------------------------------------------------------------------------------ events
-PJRT_Event* NewEvent(std::shared_ptr<EventState> s) { return new PJRT_Event{std::move(s)}; }
-
-PJRT_Error* EventDestroy(PJRT_Event_Destroy_Args* a) {
-  delete a->event;
-  return nullptr;
-}
-PJRT_Error* EventIsReady(PJRT_Event_IsReady_Args* a) {
-  a->is_ready = a->event->s->Poll();
-  return nullptr;
-}
-PJRT_Error* EventError(PJRT_Event_Error_Args* a) {
-  std::lock_guard<std::mutex> lock(a->event->s->mu);
-  return a->event->s->MakeError();
-}
-PJRT_Error* EventAwait(PJRT_Event_Await_Args* a) {
-  a->event->s->Complete();
-  std::lock_guard<std::mutex> lock(a->event->s->mu);
-  return a->event->s->MakeError();
-}
-PJRT_Error* EventOnReady(PJRT_Event_OnReady_Args* a) {
-  std::shared_ptr<EventState> s = a->event->s;
-  {
-    std::unique_lock<std::mutex> lock(s->mu);
-    if (!s->ready) {
-      s->callbacks.emplace_back(a->callback, a->user_arg);
-      lock.unlock();
-      std::thread([s] { s->Complete(); }).detach();
-      return nullptr;
-    }
-  }
-  a->callback(s->MakeError(), a->user_arg);
-  return nullptr;
-}
-
-// ------------------------------------------------------------------------------------------ plugin
-PJRT_Error* PluginInitialize(PJRT_Plugin_Initialize_Args*) { return nullptr; }
-PJRT_Error* PluginAttributes(PJRT_Plugin_Attributes_Args* a) {
-  a->attributes = nullptr;
-  a->num_attributes = 0;
-  return nullptr;
-}
-
-// ------------------------------------------------------------------------------------------ client
-void FillDescription(PJRT_DeviceDescription* d, int id, int ordinal, bool local) {
-  d->id = id;
-  d->process_index = id;
-  d->to_string = "B200Device(id=" + std::to_string(id) + ")";
-  d->debug_string = "b200:" + std::to_string(id);
-  int major = 10, minor = 0, sms = 148;
-  if (local) {
-    cudaDeviceProp p;
-    if (cudaGetDeviceProperties(&p, ordinal) == cudaSuccess) {
-      d->kind = p.name;
-      major = p.major;
-      minor = p.minor;
-      sms = p.multiProcessorCount;
-    }
-  }
-  d->cc = std::to_string(major) + "." + std::to_string(minor);
-  d->core_count = sms;
-  d->attr_names = {"compute_capability", "core_count", "device_vendor"};
-  d->attrs.resize(3);
-  for (auto& nv : d->attrs) {
-    std::memset(&nv, 0, sizeof(nv));
-    nv.struct_size = sizeof(PJRT_NamedValue);
-  }
-  static const char* vendor = "NVIDIA";
-  d->attrs[0].name = d->attr_names[0].c_str();
-  d->attrs[0].name_size = d->attr_names[0].size();
-  d->attrs[0].type = PJRT_NamedValue_kString;
-  d->attrs[0].string_value = d->cc.c_str();
-  d->attrs[0].value_size = d->cc.size();
-  d->attrs[1].name = d->attr_names[1].c_str();
-  d->attrs[1].name_size = d->attr_names[1].size();
-  d->attrs[1].type = PJRT_NamedValue_kInt64;
-  d->attrs[1].int64_value = d->core_count;
-  d->attrs[1].value_size = 1;
-  d->attrs[2].name = d->attr_names[2].c_str();
-  d->attrs[2].name_size = d->attr_names[2].size();
-  d->attrs[2].type = PJRT_NamedValue_kString;
-  d->attrs[2].string_value = vendor;
-  d->attrs[2].value_size = 6;
-}
-
-// Builds `num_nodes` devices of which `node_id` is addressable (the reference's process model,
-// src/pjrt/api/pjrt_c_api.cc:129-171), bound to CUDA device `ordinal`.
-PJRT_Client* CreateClient(int num_nodes, int node_id, int ordinal) {
-  auto client = std::make_unique<PJRT_Client>();
-  client->process_index = node_id;
-  client->num_processes = num_nodes;
-  client->platform_version = kVersion;
-  for (int k = 0; k < num_nodes; ++k) {
-    const std::string ks = std::to_string(k);
-    auto device = std::make_unique<PJRT_Device>();
-    device->client = client.get();
-    device->addressable = (k == node_id);
-    device->local_hardware_id = device->addressable ? ordinal : -1;
-    FillDescription(&device->description, k, ordinal, device->addressable);
-    PJRT_Device* dev = device.get();
-    auto hbm = std::make_unique<PJRT_Memory>();
-    hbm->id = k * 2;
-    hbm->kind = "device";
-    hbm->kind_id = 0;
-    hbm->debug_string = "hbm:" + ks;
-    hbm->to_string = "HbmMemory(id=" + ks + ")";
-    hbm->devices.push_back(dev);
-    auto host = std::make_unique<PJRT_Memory>();
-    host->id = k * 2 + 1;
-    host->kind = "pinned_host";
-    host->kind_id = 1;
-    host->debug_string = "host:" + ks;
-    host->to_string = "PinnedHostMemory(id=" + ks + ")";
-    host->devices.push_back(dev);
-    dev->memories = {hbm.get(), host.get()};
-    dev->default_memory = hbm.get();
-    if (dev->addressable) {
-      client->memories = {hbm.get(), host.get()};
-      client->addressable_devices.push_back(dev);
-      dev->state.ordinal = ordinal;
-    }
-    client->owned_memories.push_back(std::move(hbm));
-    client->owned_memories.push_back(std::move(host));
-    client->devices.push_back(dev);
-    client->owned_devices.push_back(std::move(device));
-  }
-  auto topo = std::make_unique<PJRT_TopologyDescription>();
-  topo->platform_version = kVersion;
-  for (PJRT_Device* d : client->devices) topo->descriptions.push_back(&d->description);
-  client->topology = std::move(topo);
-  return client.release();
-}
-
-PJRT_Error* ClientCreate(PJRT_Client_Create_Args* a) {
-  int node_id = 0, num_nodes = 1, ordinal = -1;
-  for (size_t i = 0; i < a->num_options; ++i) {
-    const PJRT_NamedValue& nv = a->create_options[i];
-    const std::string name(nv.name, nv.name_size);
-    if (nv.type == PJRT_NamedValue_kInt64) {
-      if (name == "node_id") node_id = (int)nv.int64_value;
-      else if (name == "num_nodes") num_nodes = (int)nv.int64_value;
-      else if (name == "device_ordinal") ordinal = (int)nv.int64_value;
-    }
-  }
-  if (num_nodes < 1) num_nodes = 1;
-  if (node_id < 0 || node_id >= num_nodes) node_id = 0;
-  int count = 0;
-  cudaError_t ce = cudaGetDeviceCount(&count);
-  if (ce != cudaSuccess || count == 0) {
+// ======================================================================================= storage
+// Allocates `bytes` in memory space `m`: HBM from the executor's stream-ordered pool on the owning
+// device's stream, pinned host memory with cudaHostAlloc.
+std::string Allocate(PJRT_Memory* m, size_t bytes, void** out) {
+  *out = nullptr;
+  PJRT_Device* d = m->owner[0];
+  cudaSetDevice(d->ordinal);
+  if (m->space == Space::kHbm) return b200::DeviceAlloc(bytes, d->cuda.stream, out);
+  if (bytes == 0) return "";
+  if (cudaHostAlloc(out, bytes, cudaHostAllocPortable) != cudaSuccess) {
     cudaGetLastError();
-    return Err(PJRT_Error_Code_FAILED_PRECONDITION, "no CUDA device is visible to the B200 plugin");
+    *out = nullptr;
+    return "pinned host allocation of " + std::to_string(bytes) + " bytes failed";
   }
-  if (ordinal < 0) ordinal = GetIntEnv("LOCAL_RANK", node_id % count);
-  if (ordinal >= count) return Err(PJRT_Error_Code_INVALID_ARGUMENT, "device_ordinal " + std::to_string(ordinal) + " out of range");
-  std::unique_ptr<PJRT_Client> client(CreateClient(num_nodes, node_id, ordinal));
-  PJRT_Device* local = client->addressable_devices[0];
-  cudaSetDevice(ordinal);
-  if (cudaStreamCreateWithFlags(&local->state.stream, cudaStreamNonBlocking) != cudaSuccess)
-    return Err(PJRT_Error_Code_INTERNAL, "cudaStreamCreate failed");
-  // keep freed pool memory cached (stream-ordered reuse instead of returning it to the driver)
-  cudaMemPool_t pool;
-  if (cudaDeviceGetDefaultMemPool(&pool, ordinal) == cudaSuccess) {
-    uint64_t thr = UINT64_MAX;
-    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
-  }
-  if (num_nodes > 1) {
-    b200::KvStore kv;
-    if (a->kv_put_callback && a->kv_get_callback) {
-      auto put_cb = a->kv_put_callback;
-      void* put_arg = a->kv_put_user_arg;
-      auto get_cb = a->kv_get_callback;
-      void* get_arg = a->kv_get_user_arg;
-      kv.put = [put_cb, put_arg](const std::string& k, const std::string& v) -> std::string {
-        PJRT_KeyValuePutCallback_Args pa;
-        std::memset(&pa, 0, sizeof(pa));
-        pa.struct_size = sizeof(pa);
-        pa.key = k.data();
-        pa.key_size = k.size();
-        pa.value = v.data();
-        pa.value_size = v.size();
-        pa.user_arg = put_arg;
-        PJRT_Error* e = put_cb(&pa);
-        if (!e) return "";
-        std::string m = "kv_put callback failed";
-        return m;
-      };
-      kv.get = [get_cb, get_arg](const std::string& k, int timeout_ms, std::string* out) -> std::string {
-        PJRT_KeyValueGetCallback_Args ga;
-        std::memset(&ga, 0, sizeof(ga));
-        ga.struct_size = sizeof(ga);
-        ga.key = k.data();
-        ga.key_size = k.size();
-        ga.timeout_in_ms = timeout_ms;
-        ga.user_arg = get_arg;
-        PJRT_Error* e = get_cb(&ga);
-        if (e) return "kv_get callback failed";
-        out->assign(ga.value, ga.value_size);
-        if (ga.value_deleter_callback) ga.value_deleter_callback(ga.value);
-        return "";
-      };
-    }
-    std::string err;
-    client->comm = b200::Comm::Create(num_nodes, node_id, ordinal, kv, GetIntEnv("B200_COMM_TIMEOUT_MS", 120000), &err);
-    if (!client->comm) return Err(err.find("timed out") != std::string::npos ? PJRT_Error_Code_DEADLINE_EXCEEDED : PJRT_Error_Code_INTERNAL,
-                                  "NCCL communicator init failed: " + err);
-  }
-  a->client = client.release();
-  return nullptr;
+  return "";
 }
 
-PJRT_Error* ClientDestroy(PJRT_Client_Destroy_Args* a) {
-  delete a->client;
-  return nullptr;
-}
-PJRT_Error* ClientPlatformName(PJRT_Client_PlatformName_Args* a) {
-  a->platform_name = a->client->platform_name.c_str();
-  a->platform_name_size = a->client->platform_name.size();
-  return nullptr;
-}
-PJRT_Error* ClientPlatformVersion(PJRT_Client_PlatformVersion_Args* a) {
-  a->platform_version = a->client->platform_version.c_str();
-  a->platform_version_size = a->client->platform_version.size();
-  return nullptr;
-}
-PJRT_Error* ClientProcessIndex(PJRT_Client_ProcessIndex_Args* a) {
-  a->process_index = a->client->process_index;
-  return nullptr;
-}
-PJRT_Error* ClientDevices(PJRT_Client_Devices_Args* a) {
-  a->devices = a->client->devices.data();
-  a->num_devices = a->client->devices.size();
-  return nullptr;
-}
-PJRT_Error* ClientAddressableDevices(PJRT_Client_AddressableDevices_Args* a) {
-  a->addressable_devices = a->client->addressable_devices.data();
-  a->num_addressable_devices = a->client->addressable_devices.size();
-  return nullptr;
-}
-PJRT_Error* ClientAddressableMemories(PJRT_Client_AddressableMemories_Args* a) {
-  a->addressable_memories = a->client->memories.data();
-  a->num_addressable_memories = a->client->memories.size();
-  return nullptr;
-}
-PJRT_Error* ClientLookupDevice(PJRT_Client_LookupDevice_Args* a) {
-  for (PJRT_Device* d : a->client->devices)
-    if (d->description.id == a->id) { a->device = d; return nullptr; }
-  return Err(PJRT_Error_Code_INVALID_ARGUMENT, "no device with that id");
-}
-PJRT_Error* ClientLookupAddressableDevice(PJRT_Client_LookupAddressableDevice_Args* a) {
-  for (PJRT_Device* d : a->client->addressable_devices)
-    if (d->local_hardware_id == a->local_hardware_id) { a->addressable_device = d; return nullptr; }
-  return Err(PJRT_Error_Code_INVALID_ARGUMENT, "no addressable device with that local hardware id");
-}
-PJRT_Error* ClientDefaultDeviceAssignment(PJRT_Client_DefaultDeviceAssignment_Args* a) {
-  const size_t n = (size_t)a->num_replicas * (size_t)a->num_partitions;
-  const size_t nd = a->client->devices.size();
-  for (size_t i = 0; i < n && i < a->default_assignment_size; ++i) a->default_assignment[i] = (int)(i % nd);
-  return nullptr;
-}
-PJRT_Error* ClientTopologyDescription(PJRT_Client_TopologyDescription_Args* a) {
-  a->topology = a->client->topology.get();
-  return nullptr;
-}
-
-// ------------------------------------------------------------------------------------------ devices
-PJRT_Error* DeviceGetDescription(PJRT_Device_GetDescription_Args* a) {
-  a->device_description = &a->device->description;
-  return nullptr;
-}
-PJRT_Error* DeviceIsAddressable(PJRT_Device_IsAddressable_Args* a) {
-  a->is_addressable = a->device->addressable;
-  return nullptr;
-}
-PJRT_Error* DeviceLocalHardwareId(PJRT_Device_LocalHardwareId_Args* a) {
-  a->local_hardware_id = a->device->local_hardware_id;
-  return nullptr;
-}
-PJRT_Error* DeviceAddressableMemories(PJRT_Device_AddressableMemories_Args* a) {
-  a->memories = a->device->memories.data();
-  a->num_memories = a->device->memories.size();
-  return nullptr;
-}
-PJRT_Error* DeviceDefaultMemory(PJRT_Device_DefaultMemory_Args* a) {
-  a->memory = a->device->default_memory;
-  return nullptr;
-}
-PJRT_Error* DeviceMemoryStats(PJRT_Device_MemoryStats_Args* a) {
-  size_t free_b = 0, total = 0;
-  if (a->device->addressable) {
-    cudaSetDevice(a->device->state.ordinal);
-    cudaMemGetInfo(&free_b, &total);
-  }
-  a->bytes_in_use = (int64_t)(total - free_b);
-  a->peak_bytes_in_use_is_set = false;
-  a->num_allocs_is_set = false;
-  a->largest_alloc_size_is_set = false;
-  a->bytes_limit = (int64_t)total;
-  a->bytes_limit_is_set = total != 0;
-  a->bytes_reserved_is_set = false;
-  a->peak_bytes_reserved_is_set = false;
-  a->bytes_reservable_limit_is_set = false;
-  a->largest_free_block_bytes_is_set = false;
-  a->pool_bytes_is_set = false;
-  a->peak_pool_bytes_is_set = false;
-  return nullptr;
-}
-
-PJRT_Error* DescId(PJRT_DeviceDescription_Id_Args* a) {
-  a->id = a->device_description->id;
-  return nullptr;
-}
-PJRT_Error* DescProcessIndex(PJRT_DeviceDescription_ProcessIndex_Args* a) {
-  a->process_index = a->device_description->process_index;
-  return nullptr;
-}
-PJRT_Error* DescAttributes(PJRT_DeviceDescription_Attributes_Args* a) {
-  a->num_attributes = a->device_description->attrs.size();
-  a->attributes = a->device_description->attrs.data();
-  return nullptr;
-}
-PJRT_Error* DescKind(PJRT_DeviceDescription_Kind_Args* a) {
-  a->device_kind = a->device_description->kind.c_str();
-  a->device_kind_size = a->device_description->kind.size();
-  return nullptr;
-}
-PJRT_Error* DescDebugString(PJRT_DeviceDescription_DebugString_Args* a) {
-  a->debug_string = a->device_description->debug_string.c_str();
-  a->debug_string_size = a->device_description->debug_string.size();
-  return nullptr;
-}
-PJRT_Error* DescToString(PJRT_DeviceDescription_ToString_Args* a) {
-  a->to_string = a->device_description->to_string.c_str();
-  a->to_string_size = a->device_description->to_string.size();
-  return nullptr;
-}
-
-// ------------------------------------------------------------------------------------------ memories
-PJRT_Error* MemoryId(PJRT_Memory_Id_Args* a) { a->id = a->memory->id; return nullptr; }
-PJRT_Error* MemoryKind(PJRT_Memory_Kind_Args* a) {
-  a->kind = a->memory->kind.c_str();
-  a->kind_size = a->memory->kind.size();
-  return nullptr;
-}
-PJRT_Error* MemoryKindId(PJRT_Memory_Kind_Id_Args* a) { a->kind_id = a->memory->kind_id; return nullptr; }
-PJRT_Error* MemoryDebugString(PJRT_Memory_DebugString_Args* a) {
-  a->debug_string = a->memory->debug_string.c_str();
-  a->debug_string_size = a->memory->debug_string.size();
-  return nullptr;
-}
-PJRT_Error* MemoryToString(PJRT_Memory_ToString_Args* a) {
-  a->to_string = a->memory->to_string.c_str();
-  a->to_string_size = a->memory->to_string.size();
-  return nullptr;
-}
-PJRT_Error* MemoryAddressableByDevices(PJRT_Memory_AddressableByDevices_Args* a) {
-  a->devices = a->memory->devices.data();
-  a->num_devices = a->memory->devices.size();
-  return nullptr;
-}
-
-// ------------------------------------------------------------------------------------------ topology
-PJRT_Error* TopologyCreate(PJRT_TopologyDescription_Create_Args* a) {
-  auto* t = new PJRT_TopologyDescription();
-  t->platform_version = kVersion;
-  auto d = std::make_unique<PJRT_DeviceDescription>();
-  FillDescription(d.get(), 0, 0, false);
-  t->descriptions.push_back(d.get());
-  t->owned.push_back(std::move(d));
-  a->topology = t;
-  return nullptr;
-}
-PJRT_Error* TopologyDestroy(PJRT_TopologyDescription_Destroy_Args* a) {
-  delete a->topology;
-  return nullptr;
-}
-PJRT_Error* TopologyPlatformName(PJRT_TopologyDescription_PlatformName_Args* a) {
-  a->platform_name = a->topology->platform_name.c_str();
-  a->platform_name_size = a->topology->platform_name.size();
-  return nullptr;
-}
-PJRT_Error* TopologyPlatformVersion(PJRT_TopologyDescription_PlatformVersion_Args* a) {
-  a->platform_version = a->topology->platform_version.c_str();
-  a->platform_version_size = a->topology->platform_version.size();
-  return nullptr;
-}
-PJRT_Error* TopologyGetDeviceDescriptions(PJRT_TopologyDescription_GetDeviceDescriptions_Args* a) {
-  a->descriptions = a->topology->descriptions.data();
-  a->num_descriptions = a->topology->descriptions.size();
-  return nullptr;
-}
-PJRT_Error* TopologyAttributes(PJRT_TopologyDescription_Attributes_Args* a) {
-  a->attributes = nullptr;
-  a->num_attributes = 0;
-  return nullptr;
-}
-
-PJRT_Error* ExecuteContextCreate(PJRT_ExecuteContext_Create_Args* a) {
-  a->context = new PJRT_ExecuteContext();
-  return nullptr;
-}
-PJRT_Error* ExecuteContextDestroy(PJRT_ExecuteContext_Destroy_Args* a) {
-  delete a->context;
-  return nullptr;
-}
-
-// ------------------------------------------------------------------------------------------ buffers
-PJRT_Error* ClientBufferFromHostBuffer(PJRT_Client_BufferFromHostBuffer_Args* a) {
-  const size_t width = ByteWidth(a->type);
-  if (width == 0) return Err(PJRT_Error_Code_UNIMPLEMENTED, "BufferFromHostBuffer: unsupported element type");
-  size_t count = 1;
-  for (size_t i = 0; i < a->num_dims; ++i) {
-    if (a->dims[i] < 0) return Err(PJRT_Error_Code_INVALID_ARGUMENT, "BufferFromHostBuffer: negative dimension");
-    count *= (size_t)a->dims[i];
-  }
-  const size_t nbytes = count * width;
-  if (a->num_byte_strides) {
-    // only dense row-major host layouts (the reference assumes the same, pjrt_c_api.cc:492-522)
-    int64_t expect = (int64_t)width;
-    for (int i = (int)a->num_dims - 1; i >= 0; --i) {
-      if (a->dims[i] > 1 && a->byte_strides[i] != expect)
-        return Err(PJRT_Error_Code_UNIMPLEMENTED, "BufferFromHostBuffer: non-dense host strides");
-      expect *= a->dims[i];
-    }
-  }
-  PJRT_Device* device = a->device;
-  PJRT_Memory* memory = a->memory;
-  if (!device && memory && !memory->devices.empty()) device = memory->devices.front();
-  if (!device) device = a->client->addressable_devices.front();
-  if (!memory) memory = device->default_memory;
-  if (!device->addressable) return Err(PJRT_Error_Code_INVALID_ARGUMENT, "BufferFromHostBuffer: device is not addressable");
-  cudaSetDevice(device->state.ordinal);
-  cudaStream_t st = device->state.stream;
-  void* d = nullptr;
-  std::string e = b200::DeviceAlloc(nbytes, st, &d);
-  if (!e.empty()) return Err(PJRT_Error_Code_RESOURCE_EXHAUSTED, "BufferFromHostBuffer: " + e);
-  if (nbytes && cudaMemcpyAsync(d, a->data, nbytes, cudaMemcpyHostToDevice, st) != cudaSuccess) {
-    cudaGetLastError();
-    b200::DeviceFree(d, st);
-    return Err(PJRT_Error_Code_INTERNAL, "BufferFromHostBuffer: host to device copy failed");
-  }
-  auto ev = RecordState(device->state.ordinal, st);
-  if (a->host_buffer_semantics == PJRT_HostBufferSemantics_kImmutableOnlyDuringCall) ev->Complete();
-  auto* buf = new PJRT_Buffer();
-  buf->client = a->client;
-  buf->device = device;
-  buf->memory = memory;
-  buf->type = a->type;
-  buf->dims.assign(a->dims, a->dims + a->num_dims);
-  buf->nbytes = nbytes;
-  buf->data = d;
-  buf->ready = ev;
-  a->done_with_host_buffer = NewEvent(ev);
-  a->buffer = buf;
-  return nullptr;
-}
-
-PJRT_Error* BufferToHostBuffer(PJRT_Buffer_ToHostBuffer_Args* a) {
-  PJRT_Buffer* b = a->src;
-  if (a->dst == nullptr) {
-    a->dst_size = b->nbytes;
-    a->event = NewEvent(ReadyState());
-    return nullptr;
-  }
-  if (b->deleted || !b->data) return Err(PJRT_Error_Code_INVALID_ARGUMENT, "ToHostBuffer: buffer has been deleted");
-  if (a->dst_size < b->nbytes) return Err(PJRT_Error_Code_INVALID_ARGUMENT, "ToHostBuffer: dst_size too small");
-  cudaSetDevice(b->device->state.ordinal);
-  cudaStream_t st = b->device->state.stream;
-  if (b->nbytes && cudaMemcpyAsync(a->dst, b->data, b->nbytes, cudaMemcpyDeviceToHost, st) != cudaSuccess) {
-    cudaGetLastError();
-    return Err(PJRT_Error_Code_INTERNAL, "ToHostBuffer: device to host copy failed");
-  }
-  a->event = NewEvent(RecordState(b->device->state.ordinal, st, true));
-  return nullptr;
-}
-
-PJRT_Buffer* CopyBuffer(PJRT_Buffer* src, PJRT_Device* dev, PJRT_Memory* mem, std::string* err) {
-  if (!dev || !dev->addressable) { *err = "destination device is not addressable"; return nullptr; }
-  cudaSetDevice(dev->state.ordinal);
-  void* d = nullptr;
-  *err = b200::DeviceAlloc(src->nbytes, dev->state.stream, &d);
-  if (!err->empty()) return nullptr;
-  if (src->device == dev) {
-    cudaMemcpyAsync(d, src->data, src->nbytes, cudaMemcpyDeviceToDevice, dev->state.stream);
+// Returns a buffer's storage.  HBM goes back to the pool stream-ordered; pinned host memory is freed
+// once the device's stream has finished any copy that may still touch it.
+void Release(PJRT_Buffer* b) {
+  if (!b->ptr) return;
+  PJRT_Device* d = b->device();
+  cudaSetDevice(d->ordinal);
+  if (b->on_host()) {
+    cudaStreamSynchronize(d->cuda.stream);
+    cudaFreeHost(b->ptr);
   } else {
-    src->ready->Complete();
-    cudaMemcpyPeerAsync(d, dev->state.ordinal, src->data, src->device->state.ordinal, src->nbytes, dev->state.stream);
+    b200::DeviceFree(b->ptr, d->cuda.stream);
   }
+  b->ptr = nullptr;
+  b->life = PJRT_Buffer::Life::kFreed;
+}
+
+PJRT_Buffer* NewBuffer(PJRT_Client* c, PJRT_Memory* m, PJRT_Buffer_Type t, std::vector<int64_t> dims, size_t bytes,
+                       void* ptr, CompletionRef ready) {
   auto* b = new PJRT_Buffer();
-  b->client = src->client;
-  b->device = dev;
-  b->memory = mem ? mem : dev->default_memory;
-  b->type = src->type;
-  b->dims = src->dims;
-  b->nbytes = src->nbytes;
-  b->data = d;
-  b->ready = RecordState(dev->state.ordinal, dev->state.stream);
+  b->client = c;
+  b->where = m;
+  b->etype = t;
+  b->dims = std::move(dims);
+  b->bytes = bytes;
+  b->ptr = ptr;
+  b->ready = std::move(ready);
   return b;
 }
 
-PJRT_Error* BufferCopyToMemory(PJRT_Buffer_CopyToMemory_Args* a) {
-  if (a->buffer->deleted) return Err(PJRT_Error_Code_INVALID_ARGUMENT, "CopyToMemory: deleted buffer");
-  PJRT_Memory* mem = a->dst_memory;
-  PJRT_Device* dev = (mem && !mem->devices.empty()) ? mem->devices.front() : a->buffer->device;
-  std::string err;
-  PJRT_Buffer* nb = CopyBuffer(a->buffer, dev, mem, &err);
-  if (!nb) return Err(PJRT_Error_Code_RESOURCE_EXHAUSTED, "CopyToMemory: " + err);
-  a->dst_buffer = nb;
-  return nullptr;
-}
-PJRT_Error* BufferCopyToDevice(PJRT_Buffer_CopyToDevice_Args* a) {
-  if (a->buffer->deleted) return Err(PJRT_Error_Code_INVALID_ARGUMENT, "CopyToDevice: deleted buffer");
-  std::string err;
-  PJRT_Buffer* nb = CopyBuffer(a->buffer, a->dst_device, nullptr, &err);
-  if (!nb) return Err(PJRT_Error_Code_RESOURCE_EXHAUSTED, "CopyToDevice: " + err);
-  a->dst_buffer = nb;
-  return nullptr;
-}
-
-void ReleaseStorage(PJRT_Buffer* b) {
-  if (b->data) {
-    cudaSetDevice(b->device->state.ordinal);
-    b200::DeviceFree(b->data, b->device->state.stream);
-    b->data = nullptr;
+// A copy of `src` in memory space `dst` (same or another device, either space).
+PJRT_Error* CopyInto(PJRT_Buffer* src, PJRT_Memory* dst, PJRT_Buffer** out) {
+  if (!src->usable()) return BadArg("copy of a deleted buffer");
+  PJRT_Device* to = dst->owner[0];
+  if (!to->local()) return BadArg("copy to a device this process does not address");
+  void* p = nullptr;
+  std::string e = Allocate(dst, src->bytes, &p);
+  if (!e.empty()) return Fail(PJRT_Error_Code_RESOURCE_EXHAUSTED, "buffer copy: " + e);
+  PJRT_Device* from = src->device();
+  cudaStream_t st = to->cuda.stream;
+  if (from != to) src->ready->Wait();          // another device's stream: wait on the host
+  cudaError_t ce = cudaSuccess;
+  if (src->bytes) {
+    if (from != to && !src->on_host() && dst->space == Space::kHbm)
+      ce = cudaMemcpyPeerAsync(p, to->ordinal, src->ptr, from->ordinal, src->bytes, st);
+    else
+      ce = cudaMemcpyAsync(p, src->ptr, src->bytes, cudaMemcpyDefault, st);   // UVA: any space to any space
   }
-}
-
-PJRT_Error* BufferDestroy(PJRT_Buffer_Destroy_Args* a) {
-  ReleaseStorage(a->buffer);
-  delete a->buffer;
-  return nullptr;
-}
-PJRT_Error* BufferDelete(PJRT_Buffer_Delete_Args* a) {
-  a->buffer->deleted = true;
-  if (a->buffer->external_refs == 0) ReleaseStorage(a->buffer);
-  else a->buffer->delete_requested = true;
-  return nullptr;
-}
-PJRT_Error* BufferIsDeleted(PJRT_Buffer_IsDeleted_Args* a) {
-  a->is_deleted = a->buffer->deleted;
-  return nullptr;
-}
-PJRT_Error* BufferElementType(PJRT_Buffer_ElementType_Args* a) {
-  a->type = a->buffer->type;
-  return nullptr;
-}
-PJRT_Error* BufferDimensions(PJRT_Buffer_Dimensions_Args* a) {
-  a->dims = a->buffer->dims.data();
-  a->num_dims = a->buffer->dims.size();
-  return nullptr;
-}
-PJRT_Error* BufferUnpaddedDimensions(PJRT_Buffer_UnpaddedDimensions_Args* a) {
-  a->unpadded_dims = a->buffer->dims.data();
-  a->num_dims = a->buffer->dims.size();
-  return nullptr;
-}
-PJRT_Error* BufferDynamicDimensionIndices(PJRT_Buffer_DynamicDimensionIndices_Args* a) {
-  a->dynamic_dim_indices = nullptr;
-  a->num_dynamic_dims = 0;
-  return nullptr;
-}
-PJRT_Error* BufferOnDeviceSizeInBytes(PJRT_Buffer_OnDeviceSizeInBytes_Args* a) {
-  a->on_device_size_in_bytes = a->buffer->nbytes;
-  return nullptr;
-}
-PJRT_Error* BufferDevice(PJRT_Buffer_Device_Args* a) {
-  a->device = a->buffer->device;
-  return nullptr;
-}
-PJRT_Error* BufferMemory(PJRT_Buffer_Memory_Args* a) {
-  a->memory = a->buffer->memory;
-  return nullptr;
-}
-PJRT_Error* BufferIsOnCpu(PJRT_Buffer_IsOnCpu_Args* a) {
-  a->is_on_cpu = false;
-  return nullptr;
-}
-PJRT_Error* BufferReadyEvent(PJRT_Buffer_ReadyEvent_Args* a) {
-  a->event = NewEvent(a->buffer->ready ? a->buffer->ready : ReadyState());
-  return nullptr;
-}
-PJRT_Error* BufferUnsafePointer(PJRT_Buffer_UnsafePointer_Args* a) {
-  a->buffer_pointer = reinterpret_cast<uintptr_t>(a->buffer->data);
-  return nullptr;
-}
-PJRT_Error* BufferOpaqueDeviceMemoryDataPointer(PJRT_Buffer_OpaqueDeviceMemoryDataPointer_Args* a) {
-  a->device_memory_ptr = a->buffer->data;
-  return nullptr;
-}
-PJRT_Error* BufferIncreaseExternalReferenceCount(PJRT_Buffer_IncreaseExternalReferenceCount_Args* a) {
-  ++a->buffer->external_refs;
-  return nullptr;
-}
-PJRT_Error* BufferDecreaseExternalReferenceCount(PJRT_Buffer_DecreaseExternalReferenceCount_Args* a) {
-  if (a->buffer->external_refs > 0) --a->buffer->external_refs;
-  if (a->buffer->external_refs == 0 && a->buffer->delete_requested) ReleaseStorage(a->buffer);
-  return nullptr;
-}
-
-// ------------------------------------------------------------------------------------------ compile / execute
-void CacheExecutableOutputs(PJRT_Executable* e) {
-  const b200::Plan& p = e->program->plan();
-  for (const auto& t : p.out_types) {
-    e->out_types.push_back(ToPjrt(t.dt));
-    e->out_dim_sizes.push_back(t.dims.size());
-    for (int64_t d : t.dims) e->out_dims_flat.push_back(d);
-    e->out_mem_kinds.push_back("device");
+  if (ce != cudaSuccess) {
+    cudaGetLastError();
+    PJRT_Buffer failed;
+    failed.where = dst;
+    failed.ptr = p;
+    Release(&failed);
+    return Fail(PJRT_Error_Code_INTERNAL, std::string("buffer copy failed: ") + cudaGetErrorString(ce));
   }
-  for (const auto& k : e->out_mem_kinds) {
-    e->out_mem_kind_ptrs.push_back(k.c_str());
-    e->out_mem_kind_sizes.push_back(k.size());
-  }
+  CompletionRef done = Completion::After(to->ordinal, st, false);
+  if (dst->space == Space::kPinnedHost) done->Wait();
+  *out = NewBuffer(src->client, dst, src->etype, src->dims, src->bytes, p, done);
+  return nullptr;
 }
 
-PJRT_Error* ClientCompile(PJRT_Client_Compile_Args* a) {
+// ======================================================================================= client
+// Builds the job's devices: `world` of them, device `rank` local on CUDA device `ordinal`.  Memory
+// ids: HBM of device k is k, its pinned host memory world + k.
+std::unique_ptr<PJRT_Client> MakeClient(int world, int rank, int ordinal) {
+  auto c = std::make_unique<PJRT_Client>();
+  c->rank = rank;
+  c->world = world;
+  for (int k = 0; k < world; ++k) {
+    c->fleet.emplace_back();
+    PJRT_Device& d = c->fleet.back();
+    d.client = c.get();
+    d.ordinal = k == rank ? ordinal : -1;
+    d.desc.Describe(k, d.ordinal);
+    for (int s = 0; s < 2; ++s) {
+      PJRT_Memory& m = d.spaces[s];
+      m.space = (Space)s;
+      m.id = s * world + k;
+      m.owner[0] = &d;
+      m.summary = (s == 0 ? "HBM(device=" : "PinnedHost(device=") + std::to_string(k) + ")";
+      m.detail = m.kind() + " memory " + std::to_string(m.id) + " of b200 device " + std::to_string(k);
+      d.space_list[s] = &m;
+    }
+    d.cuda.ordinal = d.local() ? ordinal : 0;
+    c->all.push_back(&d);
+    c->topology.descriptions.push_back(&d.desc);
+    if (d.local()) {
+      c->mine.push_back(&d);
+      c->my_memories = {&d.spaces[0], &d.spaces[1]};
+    }
+  }
+  return c;
+}
+
+// The kv_put / kv_get callbacks of PJRT_Client_Create as the communicator's key-value store.
+b200::KvStore StoreFrom(const PJRT_Client_Create_Args* a) {
+  b200::KvStore kv;
+  if (!a->kv_put_callback || !a->kv_get_callback) return kv;
+  PJRT_KeyValuePutCallback put = a->kv_put_callback;
+  PJRT_KeyValueGetCallback get = a->kv_get_callback;
+  void* put_arg = a->kv_put_user_arg;
+  void* get_arg = a->kv_get_user_arg;
+  kv.put = [put, put_arg](const std::string& key, const std::string& value) -> std::string {
+    PJRT_KeyValuePutCallback_Args x;
+    std::memset(&x, 0, sizeof(x));
+    x.struct_size = sizeof(x);
+    x.key = key.data();
+    x.key_size = key.size();
+    x.value = value.data();
+    x.value_size = value.size();
+    x.user_arg = put_arg;
+    return put(&x) ? "the kv_put callback reported an error" : "";
+  };
+  kv.get = [get, get_arg](const std::string& key, int timeout_ms, std::string* value) -> std::string {
+    PJRT_KeyValueGetCallback_Args x;
+    std::memset(&x, 0, sizeof(x));
+    x.struct_size = sizeof(x);
+    x.key = key.data();
+    x.key_size = key.size();
+    x.timeout_in_ms = timeout_ms;
+    x.user_arg = get_arg;
+    if (get(&x)) return "the kv_get callback reported an error";
+    value->assign(x.value, x.value_size);
+    if (x.value_deleter_callback) x.value_deleter_callback(x.value);
+    return "";
+  };
+  return kv;
+}
+
+PJRT_Error* CreateClient(PJRT_Client_Create_Args* a) {
+  // recognised int64 options; anything else is ignored, as jax passes options for other backends
+  int64_t rank = 0, world = 1, ordinal = -1;
+  struct Known { const char* name; int64_t* slot; } known[] = {{"node_id", &rank}, {"num_nodes", &world},
+                                                                {"device_ordinal", &ordinal}};
+  for (size_t i = 0; i < a->num_options; ++i) {
+    const PJRT_NamedValue& nv = a->create_options[i];
+    if (nv.type != PJRT_NamedValue_kInt64) continue;
+    for (const Known& k : known)
+      if (nv.name_size == std::strlen(k.name) && std::memcmp(nv.name, k.name, nv.name_size) == 0) *k.slot = nv.int64_value;
+  }
+  world = std::max<int64_t>(world, 1);
+  if (rank < 0 || rank >= world) rank = 0;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return Fail(PJRT_Error_Code_FAILED_PRECONDITION, "no CUDA device is visible to the B200 plugin");
+  }
+  if (ordinal < 0) ordinal = EnvInt("LOCAL_RANK", (int)(rank % count));
+  if (ordinal >= count) return BadArg("device_ordinal " + std::to_string(ordinal) + " out of range");
+  std::unique_ptr<PJRT_Client> c = MakeClient((int)world, (int)rank, (int)ordinal);
+  PJRT_Device* d = c->local();
+  cudaSetDevice((int)ordinal);
+  if (cudaStreamCreateWithFlags(&d->cuda.stream, cudaStreamNonBlocking) != cudaSuccess)
+    return Fail(PJRT_Error_Code_INTERNAL, "cudaStreamCreate failed");
+  // freed pool memory stays cached for stream-ordered reuse instead of going back to the driver
+  cudaMemPool_t pool;
+  if (cudaDeviceGetDefaultMemPool(&pool, (int)ordinal) == cudaSuccess) {
+    uint64_t keep = UINT64_MAX;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  }
+  if (world > 1) {
+    std::string err;
+    c->comm = b200::Comm::Create((int)world, (int)rank, (int)ordinal, StoreFrom(a), EnvInt("B200_COMM_TIMEOUT_MS", 120000),
+                                 &err);
+    if (!c->comm)
+      return Fail(err.find("timed out") != std::string::npos ? PJRT_Error_Code_DEADLINE_EXCEEDED : PJRT_Error_Code_INTERNAL,
+                  "NCCL communicator init failed: " + err);
+  }
+  a->client = c.release();
+  return nullptr;
+}
+
+// ======================================================================================= transfers
+PJRT_Error* FromHost(PJRT_Client_BufferFromHostBuffer_Args* a) {
+  const size_t width = ElementBytes(a->type);
+  if (width == 0) return Fail(PJRT_Error_Code_UNIMPLEMENTED, "BufferFromHostBuffer: unsupported element type");
+  size_t count = 1;
+  for (size_t i = 0; i < a->num_dims; ++i) {
+    if (a->dims[i] < 0) return BadArg("BufferFromHostBuffer: negative dimension");
+    count *= (size_t)a->dims[i];
+  }
+  if (a->num_byte_strides) {
+    // dense row-major host data only: each stride is the bytes of the dimensions after it
+    size_t dense = width;
+    for (size_t i = a->num_dims; i-- > 0;) {
+      if (a->dims[i] > 1 && a->byte_strides[i] != (int64_t)dense)
+        return Fail(PJRT_Error_Code_UNIMPLEMENTED, "BufferFromHostBuffer: non-dense host strides");
+      dense *= (size_t)a->dims[i];
+    }
+  }
+  PJRT_Memory* m = a->memory;
+  if (!m) m = (a->device ? a->device : a->client->local())->hbm();
+  if (a->device && m->owner[0] != a->device) return BadArg("BufferFromHostBuffer: memory is not on the given device");
+  PJRT_Device* d = m->owner[0];
+  if (!d->local()) return BadArg("BufferFromHostBuffer: device is not addressable");
+  const size_t bytes = count * width;
+  void* p = nullptr;
+  std::string e = Allocate(m, bytes, &p);
+  if (!e.empty()) return Fail(PJRT_Error_Code_RESOURCE_EXHAUSTED, "BufferFromHostBuffer: " + e);
+  CompletionRef done;
+  if (m->space == Space::kPinnedHost) {
+    if (bytes) std::memcpy(p, a->data, bytes);
+    done = Completion::Done();
+  } else {
+    if (bytes && cudaMemcpyAsync(p, a->data, bytes, cudaMemcpyHostToDevice, d->cuda.stream) != cudaSuccess) {
+      cudaGetLastError();
+      b200::DeviceFree(p, d->cuda.stream);
+      return Fail(PJRT_Error_Code_INTERNAL, "BufferFromHostBuffer: host to device copy failed");
+    }
+    done = Completion::After(d->ordinal, d->cuda.stream, false);
+    // the caller may reuse its host memory when this call returns
+    if (a->host_buffer_semantics == PJRT_HostBufferSemantics_kImmutableOnlyDuringCall) done->Wait();
+  }
+  a->buffer = NewBuffer(a->client, m, a->type, std::vector<int64_t>(a->dims, a->dims + a->num_dims), bytes, p, done);
+  a->done_with_host_buffer = new PJRT_Event{done};
+  return nullptr;
+}
+
+PJRT_Error* ToHost(PJRT_Buffer_ToHostBuffer_Args* a) {
+  PJRT_Buffer* b = a->src;
+  if (!a->dst) {                                 // size query
+    a->dst_size = b->bytes;
+    a->event = new PJRT_Event{Completion::Done()};
+    return nullptr;
+  }
+  if (!b->usable()) return BadArg("ToHostBuffer: buffer has been deleted");
+  if (a->dst_size < b->bytes) return BadArg("ToHostBuffer: dst_size too small");
+  PJRT_Device* d = b->device();
+  if (b->on_host()) {
+    b->ready->Wait();
+    if (b->bytes) std::memcpy(a->dst, b->ptr, b->bytes);
+    a->event = new PJRT_Event{Completion::Done()};
+    return nullptr;
+  }
+  cudaSetDevice(d->ordinal);
+  if (b->bytes && cudaMemcpyAsync(a->dst, b->ptr, b->bytes, cudaMemcpyDeviceToHost, d->cuda.stream) != cudaSuccess) {
+    cudaGetLastError();
+    return Fail(PJRT_Error_Code_INTERNAL, "ToHostBuffer: device to host copy failed");
+  }
+  a->event = new PJRT_Event{Completion::After(d->ordinal, d->cuda.stream, true)};
+  return nullptr;
+}
+
+// ======================================================================================= execute
+PJRT_Error* Execute(PJRT_LoadedExecutable_Execute_Args* a) {
+  PJRT_LoadedExecutable* le = a->executable;
+  if (!le->program) return BadArg("Execute: deleted executable");
+  const b200::Plan& plan = le->program->plan();
+  if (a->num_args != plan.arg_types.size())
+    return BadArg("Execute: expected " + std::to_string(plan.arg_types.size()) + " arguments, got " +
+                  std::to_string(a->num_args));
+  if (a->num_devices < 1) return BadArg("Execute: no devices");
+  for (size_t k = 0; k < a->num_devices; ++k) {
+    PJRT_Device* dev = a->execute_device ? a->execute_device : le->devices[k % le->devices.size()];
+    if (!dev->local()) return BadArg("Execute: device is not addressable");
+    std::vector<const void*> args(a->num_args);
+    for (size_t i = 0; i < a->num_args; ++i) {
+      PJRT_Buffer* b = a->argument_lists[k][i];
+      const b200::TensorType& want = plan.arg_types[i];
+      if (!b || !b->usable()) return BadArg("Execute: argument " + std::to_string(i) + " is deleted");
+      if (b->etype != PjrtTypeOf(want.dt) || b->dims != want.dims)
+        return BadArg("Execute: argument " + std::to_string(i) + " is " + ShapeText(b->etype, b->dims) + ", expected " +
+                      want.str());
+      if (b->on_host())
+        return BadArg("Execute: argument " + std::to_string(i) +
+                      " is in pinned_host memory; executables read device memory (copy it there first)");
+      if (b->device() != dev) b->ready->Wait();   // written on another device's stream
+      args[i] = b->ptr;
+    }
+    std::vector<void*> outs;
+    {
+      std::lock_guard<std::mutex> g(dev->launch_mu);
+      cudaSetDevice(dev->ordinal);
+      std::string err = le->program->Run(dev->cuda, args, &outs, le->client->comm.get());
+      if (!err.empty()) return Fail(PJRT_Error_Code_INTERNAL, err);
+    }
+    CompletionRef done = Completion::After(dev->ordinal, dev->cuda.stream, true);
+    for (size_t i = 0; i < outs.size(); ++i) {
+      const b200::TensorType& t = plan.out_types[i];
+      a->output_lists[k][i] = NewBuffer(le->client, dev->hbm(), PjrtTypeOf(t.dt), t.dims, (size_t)t.bytes(), outs[i], done);
+    }
+    if (a->device_complete_events) a->device_complete_events[k] = new PJRT_Event{done};
+  }
+  return nullptr;
+}
+
+PJRT_Error* CompileProgram(PJRT_Client_Compile_Args* a) {
   const PJRT_Program* p = a->program;
-  if (!p || !p->code) return Err(PJRT_Error_Code_INVALID_ARGUMENT, "jam compile: empty program");
-  std::string fmt(p->format ? p->format : "", p->format_size);
-  if (!fmt.empty() && fmt != "mlir") return Err(PJRT_Error_Code_INVALID_ARGUMENT, "jam compile: unsupported program format '" + fmt + "'");
-  if (const char* dump = std::getenv("JAM_DUMP_ARTIFACT")) {
-    if (FILE* f = std::fopen(dump, "wb")) {
+  if (!p || !p->code) return BadArg("jam compile: empty program");
+  const std::string format(p->format ? p->format : "", p->format_size);
+  if (!format.empty() && format != "mlir") return BadArg("jam compile: unsupported program format '" + format + "'");
+  if (const char* path = std::getenv("JAM_DUMP_ARTIFACT")) {   // the reference's artifact dump switch
+    if (FILE* f = std::fopen(path, "wb")) {
       std::fwrite(p->code, 1, p->code_size, f);
       std::fclose(f);
     }
   }
   b200::CompileOptions opt;
-  opt.num_processes = a->client->num_processes;
-  opt.rank = a->client->process_index;
+  opt.num_processes = a->client->world;
+  opt.rank = a->client->rank;
   opt.fuse_attention = std::getenv("B200_NO_FLASH") == nullptr;
   std::unique_ptr<b200::Executable> ex;
-  std::string err = b200::Executable::Build(p->code, p->code_size, opt, &ex);
-  if (!err.empty()) return Err(PJRT_Error_Code_INVALID_ARGUMENT, "jam compile: " + err);
-  auto le = std::make_unique<PJRT_LoadedExecutable>();
+  const std::string err = b200::Executable::Build(p->code, p->code_size, opt, &ex);
+  if (!err.empty()) return BadArg("jam compile: " + err);
+  auto* le = new PJRT_LoadedExecutable();
   le->client = a->client;
-  le->program = std::shared_ptr<b200::Executable>(std::move(ex));
-  le->devices = a->client->addressable_devices;
-  a->executable = le.release();
+  le->program = std::move(ex);
+  le->devices = a->client->mine;
+  a->executable = le;
   return nullptr;
 }
 
-PJRT_Error* LoadedGetExecutable(PJRT_LoadedExecutable_GetExecutable_Args* a) {
-  if (!a->loaded_executable->program) return Err(PJRT_Error_Code_INVALID_ARGUMENT, "GetExecutable: deleted executable");
-  auto* e = new PJRT_Executable();
-  e->program = a->loaded_executable->program;
-  e->name = e->program->name();
-  CacheExecutableOutputs(e);
-  a->executable = e;
-  return nullptr;
-}
-PJRT_Error* ExecutableDestroy(PJRT_Executable_Destroy_Args* a) {
-  delete a->executable;
-  return nullptr;
-}
-PJRT_Error* ExecutableName(PJRT_Executable_Name_Args* a) {
-  a->executable_name = a->executable->name.c_str();
-  a->executable_name_size = a->executable->name.size();
-  return nullptr;
-}
-PJRT_Error* ExecutableNumReplicas(PJRT_Executable_NumReplicas_Args* a) {
-  a->num_replicas = 1;
-  return nullptr;
-}
-PJRT_Error* ExecutableNumPartitions(PJRT_Executable_NumPartitions_Args* a) {
-  a->num_partitions = (size_t)a->executable->program->plan().num_partitions;
-  return nullptr;
-}
-PJRT_Error* ExecutableNumOutputs(PJRT_Executable_NumOutputs_Args* a) {
-  a->num_outputs = a->executable->program->plan().out_types.size();
-  return nullptr;
-}
-PJRT_Error* ExecutableOutputElementTypes(PJRT_Executable_OutputElementTypes_Args* a) {
-  a->output_types = a->executable->out_types.data();
-  a->num_output_types = a->executable->out_types.size();
-  return nullptr;
-}
-PJRT_Error* ExecutableOutputDimensions(PJRT_Executable_OutputDimensions_Args* a) {
-  auto* e = a->executable;
-  a->num_outputs = e->out_dim_sizes.size();
-  a->dims = e->out_dims_flat.data();
-  a->dim_sizes = e->out_dim_sizes.data();
-  return nullptr;
-}
-PJRT_Error* ExecutableOutputMemoryKinds(PJRT_Executable_OutputMemoryKinds_Args* a) {
-  auto* e = a->executable;
-  a->num_outputs = e->out_mem_kind_ptrs.size();
-  a->memory_kinds = e->out_mem_kind_ptrs.data();
-  a->memory_kind_sizes = e->out_mem_kind_sizes.data();
-  return nullptr;
-}
-PJRT_Error* LoadedDestroy(PJRT_LoadedExecutable_Destroy_Args* a) {
-  delete a->executable;
-  return nullptr;
-}
-PJRT_Error* LoadedDelete(PJRT_LoadedExecutable_Delete_Args* a) {
-  a->executable->deleted = true;
-  a->executable->program.reset();
-  return nullptr;
-}
-PJRT_Error* LoadedIsDeleted(PJRT_LoadedExecutable_IsDeleted_Args* a) {
-  a->is_deleted = a->executable->deleted;
-  return nullptr;
-}
-PJRT_Error* LoadedAddressableDevices(PJRT_LoadedExecutable_AddressableDevices_Args* a) {
-  a->addressable_devices = a->executable->devices.data();
-  a->num_addressable_devices = a->executable->devices.size();
-  return nullptr;
+// ======================================================================================= the table
+PJRT_Error* NotProvided(const char* what) {
+  return Fail(PJRT_Error_Code_UNIMPLEMENTED, std::string(what) + " is not implemented by the B200 plugin");
 }
 
-PJRT_Error* LoadedExecute(PJRT_LoadedExecutable_Execute_Args* a) {
-  PJRT_LoadedExecutable* le = a->executable;
-  if (!le->program) return Err(PJRT_Error_Code_INVALID_ARGUMENT, "Execute: deleted executable");
-  const b200::Plan& plan = le->program->plan();
-  if (a->num_args != plan.arg_types.size())
-    return Err(PJRT_Error_Code_INVALID_ARGUMENT, "Execute: expected " + std::to_string(plan.arg_types.size()) +
-                                                     " arguments, got " + std::to_string(a->num_args));
-  if (a->num_devices < 1) return Err(PJRT_Error_Code_INVALID_ARGUMENT, "Execute: no devices");
-  for (size_t d = 0; d < a->num_devices; ++d) {
-    PJRT_Device* dev = a->execute_device;
-    if (!dev) dev = le->devices[d % le->devices.size()];
-    if (!dev->addressable) return Err(PJRT_Error_Code_INVALID_ARGUMENT, "Execute: device is not addressable");
-    std::vector<const void*> args;
-    for (size_t i = 0; i < a->num_args; ++i) {
-      PJRT_Buffer* b = a->argument_lists[d][i];
-      const b200::TensorType& want = plan.arg_types[i];
-      if (!b || b->deleted || (!b->data && b->nbytes))
-        return Err(PJRT_Error_Code_INVALID_ARGUMENT, "Execute: argument " + std::to_string(i) + " is deleted");
-      if (b->type != ToPjrt(want.dt) || b->dims != want.dims)
-        return Err(PJRT_Error_Code_INVALID_ARGUMENT, "Execute: argument " + std::to_string(i) + " has shape " +
-                                                         DimsStr(b->dims) + ", expected " + want.str());
-      if (b->device != dev) {
-        if (b->ready) b->ready->Complete();
+void BindErrorsAndEvents(PJRT_Api& t) {
+  t.PJRT_Error_Destroy = [](PJRT_Error_Destroy_Args* a) { delete a->error; };
+  t.PJRT_Error_Message = [](PJRT_Error_Message_Args* a) { Put(a->error->text, &a->message, &a->message_size); };
+  t.PJRT_Error_GetCode = [](PJRT_Error_GetCode_Args* a) -> PJRT_Error* {
+    a->code = a->error->code;
+    return nullptr;
+  };
+  t.PJRT_Event_Destroy = [](PJRT_Event_Destroy_Args* a) -> PJRT_Error* {
+    delete a->event;
+    return nullptr;
+  };
+  t.PJRT_Event_IsReady = [](PJRT_Event_IsReady_Args* a) -> PJRT_Error* {
+    a->is_ready = a->event->done->Ready();
+    return nullptr;
+  };
+  t.PJRT_Event_Error = [](PJRT_Event_Error_Args* a) -> PJRT_Error* { return a->event->done->Status(); };
+  t.PJRT_Event_Await = [](PJRT_Event_Await_Args* a) -> PJRT_Error* {
+    a->event->done->Wait();
+    return a->event->done->Status();
+  };
+  t.PJRT_Event_OnReady = [](PJRT_Event_OnReady_Args* a) -> PJRT_Error* {
+    a->event->done->Then(a->callback, a->user_arg, a->event->done);
+    return nullptr;
+  };
+  t.PJRT_Plugin_Initialize = [](PJRT_Plugin_Initialize_Args*) -> PJRT_Error* { return nullptr; };
+  t.PJRT_Plugin_Attributes = [](PJRT_Plugin_Attributes_Args* a) -> PJRT_Error* {
+    a->attributes = nullptr;
+    a->num_attributes = 0;
+    return nullptr;
+  };
+}
+
+void BindClient(PJRT_Api& t) {
+  t.PJRT_Client_Create = CreateClient;
+  t.PJRT_Client_Destroy = [](PJRT_Client_Destroy_Args* a) -> PJRT_Error* {
+    delete a->client;
+    return nullptr;
+  };
+  t.PJRT_Client_PlatformName = [](PJRT_Client_PlatformName_Args* a) -> PJRT_Error* {
+    Put(kPlatform, &a->platform_name, &a->platform_name_size);
+    return nullptr;
+  };
+  t.PJRT_Client_PlatformVersion = [](PJRT_Client_PlatformVersion_Args* a) -> PJRT_Error* {
+    Put(kPlatformVersion, &a->platform_version, &a->platform_version_size);
+    return nullptr;
+  };
+  t.PJRT_Client_ProcessIndex = [](PJRT_Client_ProcessIndex_Args* a) -> PJRT_Error* {
+    a->process_index = a->client->rank;
+    return nullptr;
+  };
+  t.PJRT_Client_Devices = [](PJRT_Client_Devices_Args* a) -> PJRT_Error* {
+    a->devices = a->client->all.data();
+    a->num_devices = a->client->all.size();
+    return nullptr;
+  };
+  t.PJRT_Client_AddressableDevices = [](PJRT_Client_AddressableDevices_Args* a) -> PJRT_Error* {
+    a->addressable_devices = a->client->mine.data();
+    a->num_addressable_devices = a->client->mine.size();
+    return nullptr;
+  };
+  t.PJRT_Client_AddressableMemories = [](PJRT_Client_AddressableMemories_Args* a) -> PJRT_Error* {
+    a->addressable_memories = a->client->my_memories.data();
+    a->num_addressable_memories = a->client->my_memories.size();
+    return nullptr;
+  };
+  t.PJRT_Client_LookupDevice = [](PJRT_Client_LookupDevice_Args* a) -> PJRT_Error* {
+    if (a->id < 0 || a->id >= (int)a->client->all.size()) return BadArg("no device with id " + std::to_string(a->id));
+    a->device = a->client->all[a->id];
+    return nullptr;
+  };
+  t.PJRT_Client_LookupAddressableDevice = [](PJRT_Client_LookupAddressableDevice_Args* a) -> PJRT_Error* {
+    for (PJRT_Device* d : a->client->mine)
+      if (d->ordinal == a->local_hardware_id) {
+        a->addressable_device = d;
+        return nullptr;
       }
-      args.push_back(b->data);
-    }
-    std::vector<void*> outs;
-    {
-      std::lock_guard<std::mutex> lock(dev->exec_mu);
-      cudaSetDevice(dev->state.ordinal);
-      std::string err = le->program->Run(dev->state, args, &outs, le->client->comm.get());
-      if (!err.empty()) return Err(PJRT_Error_Code_INTERNAL, err);
-    }
-    auto ev = RecordState(dev->state.ordinal, dev->state.stream, true);
-    for (size_t i = 0; i < outs.size(); ++i) {
-      auto* ob = new PJRT_Buffer();
-      ob->client = le->client;
-      ob->device = dev;
-      ob->memory = dev->default_memory;
-      ob->type = ToPjrt(plan.out_types[i].dt);
-      ob->dims = plan.out_types[i].dims;
-      ob->nbytes = (size_t)plan.out_types[i].bytes();
-      ob->data = outs[i];
-      ob->ready = ev;
-      a->output_lists[d][i] = ob;
-    }
-    if (a->device_complete_events) a->device_complete_events[d] = NewEvent(ev);
-  }
-  return nullptr;
+    return BadArg("no addressable device with local hardware id " + std::to_string(a->local_hardware_id));
+  };
+  t.PJRT_Client_DefaultDeviceAssignment = [](PJRT_Client_DefaultDeviceAssignment_Args* a) -> PJRT_Error* {
+    // replica-major over the job's devices, wrapping when the program asks for more than exist
+    const size_t want = (size_t)a->num_replicas * (size_t)a->num_partitions;
+    for (size_t i = 0; i < want && i < a->default_assignment_size; ++i)
+      a->default_assignment[i] = a->client->all[i % a->client->all.size()]->desc.global_id;
+    return nullptr;
+  };
+  t.PJRT_Client_TopologyDescription = [](PJRT_Client_TopologyDescription_Args* a) -> PJRT_Error* {
+    a->topology = &a->client->topology;
+    return nullptr;
+  };
+  t.PJRT_Client_BufferFromHostBuffer = FromHost;
+  t.PJRT_Client_Compile = CompileProgram;
 }
 
-#define B200_UNIMPLEMENTED(X)                                                                      \
-  X(Executable_SizeOfGeneratedCodeInBytes) X(Executable_GetCostAnalysis) X(Executable_OptimizedProgram) \
-  X(Executable_Serialize) X(Executable_DeserializeAndLoad) X(LoadedExecutable_Fingerprint)           \
-  X(Buffer_GetMemoryLayout) X(CopyToDeviceStream_Destroy) X(CopyToDeviceStream_AddChunk)              \
-  X(CopyToDeviceStream_TotalBytes) X(CopyToDeviceStream_GranuleSize) X(CopyToDeviceStream_CurrentBytes) \
-  X(TopologyDescription_Serialize) X(Compile) X(Client_CreateViewOfDeviceBuffer) X(Executable_Fingerprint) \
-  X(Executable_GetCompiledMemoryStats)
+void BindDevicesAndMemories(PJRT_Api& t) {
+  t.PJRT_Device_GetDescription = [](PJRT_Device_GetDescription_Args* a) -> PJRT_Error* {
+    a->device_description = &a->device->desc;
+    return nullptr;
+  };
+  t.PJRT_Device_IsAddressable = [](PJRT_Device_IsAddressable_Args* a) -> PJRT_Error* {
+    a->is_addressable = a->device->local();
+    return nullptr;
+  };
+  t.PJRT_Device_LocalHardwareId = [](PJRT_Device_LocalHardwareId_Args* a) -> PJRT_Error* {
+    a->local_hardware_id = a->device->ordinal;
+    return nullptr;
+  };
+  t.PJRT_Device_AddressableMemories = [](PJRT_Device_AddressableMemories_Args* a) -> PJRT_Error* {
+    a->memories = a->device->space_list;
+    a->num_memories = 2;
+    return nullptr;
+  };
+  t.PJRT_Device_DefaultMemory = [](PJRT_Device_DefaultMemory_Args* a) -> PJRT_Error* {
+    a->memory = a->device->hbm();
+    return nullptr;
+  };
+  t.PJRT_Device_MemoryStats = [](PJRT_Device_MemoryStats_Args* a) -> PJRT_Error* {
+    // what the driver reports for the whole GPU; the per-allocator statistics are left unset
+    size_t free_bytes = 0, total = 0;
+    if (a->device->local()) {
+      cudaSetDevice(a->device->ordinal);
+      cudaMemGetInfo(&free_bytes, &total);
+    }
+    // every output field (and its *_is_set flag) starts cleared
+    std::memset(reinterpret_cast<char*>(a) + offsetof(PJRT_Device_MemoryStats_Args, bytes_in_use), 0,
+                sizeof(PJRT_Device_MemoryStats_Args) - offsetof(PJRT_Device_MemoryStats_Args, bytes_in_use));
+    a->bytes_in_use = (int64_t)(total - free_bytes);
+    a->bytes_limit = (int64_t)total;
+    a->bytes_limit_is_set = total != 0;
+    return nullptr;
+  };
+  t.PJRT_DeviceDescription_Id = [](PJRT_DeviceDescription_Id_Args* a) -> PJRT_Error* {
+    a->id = a->device_description->global_id;
+    return nullptr;
+  };
+  t.PJRT_DeviceDescription_ProcessIndex = [](PJRT_DeviceDescription_ProcessIndex_Args* a) -> PJRT_Error* {
+    a->process_index = a->device_description->process;
+    return nullptr;
+  };
+  t.PJRT_DeviceDescription_Attributes = [](PJRT_DeviceDescription_Attributes_Args* a) -> PJRT_Error* {
+    a->attributes = a->device_description->attribute_values;
+    a->num_attributes = a->device_description->attributes.Count();
+    return nullptr;
+  };
+  t.PJRT_DeviceDescription_Kind = [](PJRT_DeviceDescription_Kind_Args* a) -> PJRT_Error* {
+    Put(a->device_description->kind, &a->device_kind, &a->device_kind_size);
+    return nullptr;
+  };
+  t.PJRT_DeviceDescription_DebugString = [](PJRT_DeviceDescription_DebugString_Args* a) -> PJRT_Error* {
+    Put(a->device_description->detail, &a->debug_string, &a->debug_string_size);
+    return nullptr;
+  };
+  t.PJRT_DeviceDescription_ToString = [](PJRT_DeviceDescription_ToString_Args* a) -> PJRT_Error* {
+    Put(a->device_description->summary, &a->to_string, &a->to_string_size);
+    return nullptr;
+  };
+  t.PJRT_Memory_Id = [](PJRT_Memory_Id_Args* a) -> PJRT_Error* {
+    a->id = a->memory->id;
+    return nullptr;
+  };
+  t.PJRT_Memory_Kind = [](PJRT_Memory_Kind_Args* a) -> PJRT_Error* {
+    Put(a->memory->kind(), &a->kind, &a->kind_size);
+    return nullptr;
+  };
+  t.PJRT_Memory_Kind_Id = [](PJRT_Memory_Kind_Id_Args* a) -> PJRT_Error* {
+    a->kind_id = (int)a->memory->space;
+    return nullptr;
+  };
+  t.PJRT_Memory_DebugString = [](PJRT_Memory_DebugString_Args* a) -> PJRT_Error* {
+    Put(a->memory->detail, &a->debug_string, &a->debug_string_size);
+    return nullptr;
+  };
+  t.PJRT_Memory_ToString = [](PJRT_Memory_ToString_Args* a) -> PJRT_Error* {
+    Put(a->memory->summary, &a->to_string, &a->to_string_size);
+    return nullptr;
+  };
+  t.PJRT_Memory_AddressableByDevices = [](PJRT_Memory_AddressableByDevices_Args* a) -> PJRT_Error* {
+    a->devices = a->memory->owner;
+    a->num_devices = 1;
+    return nullptr;
+  };
+}
 
-#define B200_DEFINE_STUB(name) \
-  PJRT_Error* name##_Stub(PJRT_##name##_Args*) { return MakeUnimplemented(#name); }
-B200_UNIMPLEMENTED(B200_DEFINE_STUB)
-#undef B200_DEFINE_STUB
+void BindTopology(PJRT_Api& t) {
+  t.PJRT_TopologyDescription_Create = [](PJRT_TopologyDescription_Create_Args* a) -> PJRT_Error* {
+    // a topology without a client: one (remote-described) B200
+    auto* topo = new PJRT_TopologyDescription();
+    topo->owned.emplace_back();
+    topo->owned.back().Describe(0, -1);
+    topo->descriptions.push_back(&topo->owned.back());
+    a->topology = topo;
+    return nullptr;
+  };
+  t.PJRT_TopologyDescription_Destroy = [](PJRT_TopologyDescription_Destroy_Args* a) -> PJRT_Error* {
+    delete a->topology;
+    return nullptr;
+  };
+  t.PJRT_TopologyDescription_PlatformName = [](PJRT_TopologyDescription_PlatformName_Args* a) -> PJRT_Error* {
+    Put(kPlatform, &a->platform_name, &a->platform_name_size);
+    return nullptr;
+  };
+  t.PJRT_TopologyDescription_PlatformVersion = [](PJRT_TopologyDescription_PlatformVersion_Args* a) -> PJRT_Error* {
+    Put(kPlatformVersion, &a->platform_version, &a->platform_version_size);
+    return nullptr;
+  };
+  t.PJRT_TopologyDescription_GetDeviceDescriptions = [](PJRT_TopologyDescription_GetDeviceDescriptions_Args* a)
+      -> PJRT_Error* {
+    a->descriptions = a->topology->descriptions.data();
+    a->num_descriptions = a->topology->descriptions.size();
+    return nullptr;
+  };
+  t.PJRT_TopologyDescription_Attributes = [](PJRT_TopologyDescription_Attributes_Args* a) -> PJRT_Error* {
+    a->attributes = nullptr;
+    a->num_attributes = 0;
+    return nullptr;
+  };
+  t.PJRT_ExecuteContext_Create = [](PJRT_ExecuteContext_Create_Args* a) -> PJRT_Error* {
+    a->context = new PJRT_ExecuteContext();
+    return nullptr;
+  };
+  t.PJRT_ExecuteContext_Destroy = [](PJRT_ExecuteContext_Destroy_Args* a) -> PJRT_Error* {
+    delete a->context;
+    return nullptr;
+  };
+}
+
+void BindBuffers(PJRT_Api& t) {
+  t.PJRT_Buffer_Destroy = [](PJRT_Buffer_Destroy_Args* a) -> PJRT_Error* {
+    Release(a->buffer);
+    delete a->buffer;
+    return nullptr;
+  };
+  t.PJRT_Buffer_Delete = [](PJRT_Buffer_Delete_Args* a) -> PJRT_Error* {
+    PJRT_Buffer* b = a->buffer;
+    if (b->life != PJRT_Buffer::Life::kLive) return nullptr;
+    if (b->pins > 0) b->life = PJRT_Buffer::Life::kFreeWhenUnpinned;   // freed by the last unpin
+    else Release(b);
+    return nullptr;
+  };
+  t.PJRT_Buffer_IsDeleted = [](PJRT_Buffer_IsDeleted_Args* a) -> PJRT_Error* {
+    a->is_deleted = a->buffer->life != PJRT_Buffer::Life::kLive;
+    return nullptr;
+  };
+  t.PJRT_Buffer_ElementType = [](PJRT_Buffer_ElementType_Args* a) -> PJRT_Error* {
+    a->type = a->buffer->etype;
+    return nullptr;
+  };
+  t.PJRT_Buffer_Dimensions = [](PJRT_Buffer_Dimensions_Args* a) -> PJRT_Error* {
+    a->dims = a->buffer->dims.data();
+    a->num_dims = a->buffer->dims.size();
+    return nullptr;
+  };
+  t.PJRT_Buffer_UnpaddedDimensions = [](PJRT_Buffer_UnpaddedDimensions_Args* a) -> PJRT_Error* {
+    a->unpadded_dims = a->buffer->dims.data();            // buffers are dense: no padding
+    a->num_dims = a->buffer->dims.size();
+    return nullptr;
+  };
+  t.PJRT_Buffer_DynamicDimensionIndices = [](PJRT_Buffer_DynamicDimensionIndices_Args* a) -> PJRT_Error* {
+    a->dynamic_dim_indices = nullptr;                      // static shapes only
+    a->num_dynamic_dims = 0;
+    return nullptr;
+  };
+  t.PJRT_Buffer_OnDeviceSizeInBytes = [](PJRT_Buffer_OnDeviceSizeInBytes_Args* a) -> PJRT_Error* {
+    a->on_device_size_in_bytes = a->buffer->bytes;
+    return nullptr;
+  };
+  t.PJRT_Buffer_Device = [](PJRT_Buffer_Device_Args* a) -> PJRT_Error* {
+    a->device = a->buffer->device();
+    return nullptr;
+  };
+  t.PJRT_Buffer_Memory = [](PJRT_Buffer_Memory_Args* a) -> PJRT_Error* {
+    a->memory = a->buffer->where;
+    return nullptr;
+  };
+  t.PJRT_Buffer_IsOnCpu = [](PJRT_Buffer_IsOnCpu_Args* a) -> PJRT_Error* {
+    a->is_on_cpu = a->buffer->on_host();
+    return nullptr;
+  };
+  t.PJRT_Buffer_ReadyEvent = [](PJRT_Buffer_ReadyEvent_Args* a) -> PJRT_Error* {
+    a->event = new PJRT_Event{a->buffer->ready ? a->buffer->ready : Completion::Done()};
+    return nullptr;
+  };
+  t.PJRT_Buffer_ToHostBuffer = ToHost;
+  t.PJRT_Buffer_CopyToMemory = [](PJRT_Buffer_CopyToMemory_Args* a) -> PJRT_Error* {
+    return CopyInto(a->buffer, a->dst_memory ? a->dst_memory : a->buffer->where, &a->dst_buffer);
+  };
+  t.PJRT_Buffer_CopyToDevice = [](PJRT_Buffer_CopyToDevice_Args* a) -> PJRT_Error* {
+    if (!a->dst_device) return BadArg("CopyToDevice: no destination device");
+    return CopyInto(a->buffer, a->dst_device->hbm(), &a->dst_buffer);
+  };
+  t.PJRT_Buffer_UnsafePointer = [](PJRT_Buffer_UnsafePointer_Args* a) -> PJRT_Error* {
+    a->buffer_pointer = reinterpret_cast<uintptr_t>(a->buffer->ptr);
+    return nullptr;
+  };
+  t.PJRT_Buffer_OpaqueDeviceMemoryDataPointer = [](PJRT_Buffer_OpaqueDeviceMemoryDataPointer_Args* a) -> PJRT_Error* {
+    a->device_memory_ptr = a->buffer->ptr;
+    return nullptr;
+  };
+  t.PJRT_Buffer_IncreaseExternalReferenceCount = [](PJRT_Buffer_IncreaseExternalReferenceCount_Args* a) -> PJRT_Error* {
+    ++a->buffer->pins;
+    return nullptr;
+  };
+  t.PJRT_Buffer_DecreaseExternalReferenceCount = [](PJRT_Buffer_DecreaseExternalReferenceCount_Args* a) -> PJRT_Error* {
+    PJRT_Buffer* b = a->buffer;
+    if (b->pins == 0) return BadArg("DecreaseExternalReferenceCount: the buffer has no external references");
+    if (--b->pins == 0 && b->life == PJRT_Buffer::Life::kFreeWhenUnpinned) Release(b);
+    return nullptr;
+  };
+}
+
+void BindExecutables(PJRT_Api& t) {
+  t.PJRT_LoadedExecutable_GetExecutable = [](PJRT_LoadedExecutable_GetExecutable_Args* a) -> PJRT_Error* {
+    if (!a->loaded_executable->program) return BadArg("GetExecutable: deleted executable");
+    a->executable = new PJRT_Executable(a->loaded_executable->program);
+    return nullptr;
+  };
+  t.PJRT_LoadedExecutable_Destroy = [](PJRT_LoadedExecutable_Destroy_Args* a) -> PJRT_Error* {
+    delete a->executable;
+    return nullptr;
+  };
+  t.PJRT_LoadedExecutable_Delete = [](PJRT_LoadedExecutable_Delete_Args* a) -> PJRT_Error* {
+    a->executable->program.reset();
+    return nullptr;
+  };
+  t.PJRT_LoadedExecutable_IsDeleted = [](PJRT_LoadedExecutable_IsDeleted_Args* a) -> PJRT_Error* {
+    a->is_deleted = !a->executable->program;
+    return nullptr;
+  };
+  t.PJRT_LoadedExecutable_AddressableDevices = [](PJRT_LoadedExecutable_AddressableDevices_Args* a) -> PJRT_Error* {
+    a->addressable_devices = a->executable->devices.data();
+    a->num_addressable_devices = a->executable->devices.size();
+    return nullptr;
+  };
+  t.PJRT_LoadedExecutable_Execute = Execute;
+  t.PJRT_Executable_Destroy = [](PJRT_Executable_Destroy_Args* a) -> PJRT_Error* {
+    delete a->executable;
+    return nullptr;
+  };
+  t.PJRT_Executable_Name = [](PJRT_Executable_Name_Args* a) -> PJRT_Error* {
+    Put(a->executable->program->name(), &a->executable_name, &a->executable_name_size);
+    return nullptr;
+  };
+  t.PJRT_Executable_NumReplicas = [](PJRT_Executable_NumReplicas_Args* a) -> PJRT_Error* {
+    a->num_replicas = 1;
+    return nullptr;
+  };
+  t.PJRT_Executable_NumPartitions = [](PJRT_Executable_NumPartitions_Args* a) -> PJRT_Error* {
+    a->num_partitions = (size_t)a->executable->program->plan().num_partitions;
+    return nullptr;
+  };
+  t.PJRT_Executable_NumOutputs = [](PJRT_Executable_NumOutputs_Args* a) -> PJRT_Error* {
+    a->num_outputs = a->executable->outputs.types.size();
+    return nullptr;
+  };
+  t.PJRT_Executable_OutputElementTypes = [](PJRT_Executable_OutputElementTypes_Args* a) -> PJRT_Error* {
+    a->output_types = a->executable->outputs.types.data();
+    a->num_output_types = a->executable->outputs.types.size();
+    return nullptr;
+  };
+  t.PJRT_Executable_OutputDimensions = [](PJRT_Executable_OutputDimensions_Args* a) -> PJRT_Error* {
+    const Signature& s = a->executable->outputs;
+    a->num_outputs = s.ranks.size();
+    a->dims = s.dims.data();
+    a->dim_sizes = s.ranks.data();
+    return nullptr;
+  };
+  t.PJRT_Executable_OutputMemoryKinds = [](PJRT_Executable_OutputMemoryKinds_Args* a) -> PJRT_Error* {
+    const Signature& s = a->executable->outputs;
+    a->num_outputs = s.kinds.size();
+    a->memory_kinds = s.kinds.data();
+    a->memory_kind_sizes = s.kind_sizes.data();
+    return nullptr;
+  };
+}
+
+// The entry points the reference also leaves UNIMPLEMENTED (src/pjrt/api/pjrt_c_api.cc:833-873).
+#define B200_NOT_PROVIDED(slot) \
+  t.PJRT_##slot = [](PJRT_##slot##_Args*) -> PJRT_Error* { return NotProvided(#slot); };
+
+void BindUnimplemented(PJRT_Api& t) {
+  B200_NOT_PROVIDED(Executable_SizeOfGeneratedCodeInBytes)
+  B200_NOT_PROVIDED(Executable_GetCostAnalysis)
+  B200_NOT_PROVIDED(Executable_OptimizedProgram)
+  B200_NOT_PROVIDED(Executable_Serialize)
+  B200_NOT_PROVIDED(Executable_DeserializeAndLoad)
+  B200_NOT_PROVIDED(Executable_Fingerprint)
+  B200_NOT_PROVIDED(Executable_GetCompiledMemoryStats)
+  B200_NOT_PROVIDED(LoadedExecutable_Fingerprint)
+  B200_NOT_PROVIDED(Buffer_GetMemoryLayout)
+  B200_NOT_PROVIDED(CopyToDeviceStream_Destroy)
+  B200_NOT_PROVIDED(CopyToDeviceStream_AddChunk)
+  B200_NOT_PROVIDED(CopyToDeviceStream_TotalBytes)
+  B200_NOT_PROVIDED(CopyToDeviceStream_GranuleSize)
+  B200_NOT_PROVIDED(CopyToDeviceStream_CurrentBytes)
+  B200_NOT_PROVIDED(TopologyDescription_Serialize)
+  B200_NOT_PROVIDED(Compile)
+  B200_NOT_PROVIDED(Client_CreateViewOfDeviceBuffer)
+}
+#undef B200_NOT_PROVIDED
 
 }  // namespace
 
 extern "C" __attribute__((visibility("default"))) const PJRT_Api* GetPjrtApi(void) {
-  static PJRT_Api api = [] {
-    PJRT_Api a;
-    std::memset(&a, 0, sizeof(a));
-    a.struct_size = sizeof(PJRT_Api);
-    a.pjrt_api_version.struct_size = sizeof(PJRT_Api_Version);
-    a.pjrt_api_version.major_version = PJRT_API_MAJOR;
-    a.pjrt_api_version.minor_version = PJRT_API_MINOR;
-
-    a.PJRT_Error_Destroy = ErrorDestroy;
-    a.PJRT_Error_Message = ErrorMessage;
-    a.PJRT_Error_GetCode = ErrorGetCode;
-    a.PJRT_Event_Destroy = EventDestroy;
-    a.PJRT_Event_IsReady = EventIsReady;
-    a.PJRT_Event_Error = EventError;
-    a.PJRT_Event_Await = EventAwait;
-    a.PJRT_Event_OnReady = EventOnReady;
-    a.PJRT_Plugin_Initialize = PluginInitialize;
-    a.PJRT_Plugin_Attributes = PluginAttributes;
-
-    a.PJRT_Client_Create = ClientCreate;
-    a.PJRT_Client_Destroy = ClientDestroy;
-    a.PJRT_Client_PlatformName = ClientPlatformName;
-    a.PJRT_Client_PlatformVersion = ClientPlatformVersion;
-    a.PJRT_Client_ProcessIndex = ClientProcessIndex;
-    a.PJRT_Client_Devices = ClientDevices;
-    a.PJRT_Client_AddressableDevices = ClientAddressableDevices;
-    a.PJRT_Client_AddressableMemories = ClientAddressableMemories;
-    a.PJRT_Client_LookupDevice = ClientLookupDevice;
-    a.PJRT_Client_LookupAddressableDevice = ClientLookupAddressableDevice;
-    a.PJRT_Client_DefaultDeviceAssignment = ClientDefaultDeviceAssignment;
-    a.PJRT_Client_TopologyDescription = ClientTopologyDescription;
-    a.PJRT_Client_BufferFromHostBuffer = ClientBufferFromHostBuffer;
-    a.PJRT_Client_Compile = ClientCompile;
-
-    a.PJRT_Device_GetDescription = DeviceGetDescription;
-    a.PJRT_Device_IsAddressable = DeviceIsAddressable;
-    a.PJRT_Device_LocalHardwareId = DeviceLocalHardwareId;
-    a.PJRT_Device_AddressableMemories = DeviceAddressableMemories;
-    a.PJRT_Device_DefaultMemory = DeviceDefaultMemory;
-    a.PJRT_Device_MemoryStats = DeviceMemoryStats;
-    a.PJRT_DeviceDescription_Id = DescId;
-    a.PJRT_DeviceDescription_ProcessIndex = DescProcessIndex;
-    a.PJRT_DeviceDescription_Attributes = DescAttributes;
-    a.PJRT_DeviceDescription_Kind = DescKind;
-    a.PJRT_DeviceDescription_DebugString = DescDebugString;
-    a.PJRT_DeviceDescription_ToString = DescToString;
-
-    a.PJRT_Memory_Id = MemoryId;
-    a.PJRT_Memory_Kind = MemoryKind;
-    a.PJRT_Memory_Kind_Id = MemoryKindId;
-    a.PJRT_Memory_DebugString = MemoryDebugString;
-    a.PJRT_Memory_ToString = MemoryToString;
-    a.PJRT_Memory_AddressableByDevices = MemoryAddressableByDevices;
-
-    a.PJRT_TopologyDescription_Create = TopologyCreate;
-    a.PJRT_TopologyDescription_Destroy = TopologyDestroy;
-    a.PJRT_TopologyDescription_PlatformName = TopologyPlatformName;
-    a.PJRT_TopologyDescription_PlatformVersion = TopologyPlatformVersion;
-    a.PJRT_TopologyDescription_GetDeviceDescriptions = TopologyGetDeviceDescriptions;
-    a.PJRT_TopologyDescription_Attributes = TopologyAttributes;
-
-    a.PJRT_ExecuteContext_Create = ExecuteContextCreate;
-    a.PJRT_ExecuteContext_Destroy = ExecuteContextDestroy;
-
-    a.PJRT_Buffer_Destroy = BufferDestroy;
-    a.PJRT_Buffer_Delete = BufferDelete;
-    a.PJRT_Buffer_IsDeleted = BufferIsDeleted;
-    a.PJRT_Buffer_ElementType = BufferElementType;
-    a.PJRT_Buffer_Dimensions = BufferDimensions;
-    a.PJRT_Buffer_UnpaddedDimensions = BufferUnpaddedDimensions;
-    a.PJRT_Buffer_DynamicDimensionIndices = BufferDynamicDimensionIndices;
-    a.PJRT_Buffer_OnDeviceSizeInBytes = BufferOnDeviceSizeInBytes;
-    a.PJRT_Buffer_Device = BufferDevice;
-    a.PJRT_Buffer_Memory = BufferMemory;
-    a.PJRT_Buffer_IsOnCpu = BufferIsOnCpu;
-    a.PJRT_Buffer_ReadyEvent = BufferReadyEvent;
-    a.PJRT_Buffer_ToHostBuffer = BufferToHostBuffer;
-    a.PJRT_Buffer_CopyToMemory = BufferCopyToMemory;
-    a.PJRT_Buffer_CopyToDevice = BufferCopyToDevice;
-    a.PJRT_Buffer_UnsafePointer = BufferUnsafePointer;
-    a.PJRT_Buffer_OpaqueDeviceMemoryDataPointer = BufferOpaqueDeviceMemoryDataPointer;
-    a.PJRT_Buffer_IncreaseExternalReferenceCount = BufferIncreaseExternalReferenceCount;
-    a.PJRT_Buffer_DecreaseExternalReferenceCount = BufferDecreaseExternalReferenceCount;
-
-    a.PJRT_Executable_Destroy = ExecutableDestroy;
-    a.PJRT_Executable_Name = ExecutableName;
-    a.PJRT_Executable_NumReplicas = ExecutableNumReplicas;
-    a.PJRT_Executable_NumPartitions = ExecutableNumPartitions;
-    a.PJRT_Executable_NumOutputs = ExecutableNumOutputs;
-    a.PJRT_Executable_OutputElementTypes = ExecutableOutputElementTypes;
-    a.PJRT_Executable_OutputDimensions = ExecutableOutputDimensions;
-    a.PJRT_Executable_OutputMemoryKinds = ExecutableOutputMemoryKinds;
-    a.PJRT_LoadedExecutable_Destroy = LoadedDestroy;
-    a.PJRT_LoadedExecutable_GetExecutable = LoadedGetExecutable;
-    a.PJRT_LoadedExecutable_AddressableDevices = LoadedAddressableDevices;
-    a.PJRT_LoadedExecutable_Delete = LoadedDelete;
-    a.PJRT_LoadedExecutable_IsDeleted = LoadedIsDeleted;
-    a.PJRT_LoadedExecutable_Execute = LoadedExecute;
-
-#define B200_BIND_STUB(name) a.PJRT_##name = name##_Stub;
-    B200_UNIMPLEMENTED(B200_BIND_STUB)
-#undef B200_BIND_STUB
-    return a;
+  static const PJRT_Api table = [] {
+    PJRT_Api t;
+    std::memset(&t, 0, sizeof(t));
+    t.struct_size = sizeof(PJRT_Api);
+    t.pjrt_api_version.struct_size = sizeof(PJRT_Api_Version);
+    t.pjrt_api_version.major_version = PJRT_API_MAJOR;
+    t.pjrt_api_version.minor_version = PJRT_API_MINOR;
+    BindErrorsAndEvents(t);
+    BindClient(t);
+    BindDevicesAndMemories(t);
+    BindTopology(t);
+    BindBuffers(t);
+    BindExecutables(t);
+    BindUnimplemented(t);
+    return t;
   }();
-  return &api;
+  return &table;
 }

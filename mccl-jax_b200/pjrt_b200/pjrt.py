@@ -126,6 +126,12 @@ DeviceIntArgs = _args("DeviceIntArgs", [("device", P), ("value", C.c_int)])
 DeviceMemsArgs = _args("DeviceMemsArgs", [("device", P), ("memories", C.POINTER(P)), ("n", SZ)])
 MemoryStrArgs = _args("MemoryStrArgs", [("memory", P), ("s", P), ("n", SZ)])
 MemoryIntArgs = _args("MemoryIntArgs", [("memory", P), ("value", C.c_int)])
+BufferMemArgs = _args("BufferMemArgs", [("buffer", P), ("memory", P)])
+BufferBoolArgs = _args("BufferBoolArgs", [("buffer", P), ("value", C.c_bool)])
+CopyToMemoryArgs = _args("CopyToMemoryArgs", [("buffer", P), ("dst_memory", P), ("dst_buffer", P)])
+LookupDeviceArgs = _args("LookupDeviceArgs", [("client", P), ("id", C.c_int), ("device", P)])
+AssignArgs = _args("AssignArgs", [("client", P), ("num_replicas", C.c_int), ("num_partitions", C.c_int),
+                                  ("size", SZ), ("assignment", C.POINTER(C.c_int))])
 
 
 class PjrtError(RuntimeError):
@@ -228,6 +234,28 @@ class Buffer:
         a = self.api.call("Buffer_ToHostBuffer", ToHostArgs(src=self.h, dst=out.ctypes.data, dst_size=out.nbytes))
         self.api.await_event(a.event)
         return out
+
+    def memory(self):
+        return self.api.call("Buffer_Memory", BufferMemArgs(buffer=self.h)).memory
+
+    def is_on_cpu(self) -> bool:
+        return bool(self.api.call("Buffer_IsOnCpu", BufferBoolArgs(buffer=self.h)).value)
+
+    def is_deleted(self) -> bool:
+        return bool(self.api.call("Buffer_IsDeleted", BufferBoolArgs(buffer=self.h)).value)
+
+    def copy_to_memory(self, memory) -> "Buffer":
+        a = self.api.call("Buffer_CopyToMemory", CopyToMemoryArgs(buffer=self.h, dst_memory=memory))
+        return Buffer(self.client, a.dst_buffer)
+
+    def add_external_ref(self, delta: int):
+        name = "Buffer_IncreaseExternalReferenceCount" if delta > 0 else "Buffer_DecreaseExternalReferenceCount"
+        self.api.call(name, BufferArgs(buffer=self.h))
+
+    def mark_deleted(self):
+        """PJRT_Buffer_Delete: storage released (now, or at the last external reference's release);
+        the handle stays valid until destroyed."""
+        self.api.call("Buffer_Delete", BufferArgs(buffer=self.h))
 
     def delete(self):
         # a buffer outliving its client is dropped without a call: the client freed the device
@@ -358,6 +386,27 @@ class Client:
         a = self.api.call("DeviceDescription_Kind", DescStrArgs(description=d))
         return C.string_at(a.s, a.n).decode()
 
+    def memories(self):
+        a = self.api.call("Client_AddressableMemories", ClientListArgs(client=self.h))
+        return [a.items[i] for i in range(a.n)]
+
+    def memory_kind(self, mem) -> str:
+        a = self.api.call("Memory_Kind", MemoryStrArgs(memory=mem))
+        return C.string_at(a.s, a.n).decode()
+
+    def memory_id(self, mem) -> int:
+        return self.api.call("Memory_Id", MemoryIntArgs(memory=mem)).value
+
+    def lookup_device(self, global_id: int):
+        return self.api.call("Client_LookupDevice", LookupDeviceArgs(client=self.h, id=global_id)).device
+
+    def default_device_assignment(self, replicas: int, partitions: int):
+        out = (C.c_int * (replicas * partitions))()
+        self.api.call("Client_DefaultDeviceAssignment", AssignArgs(client=self.h, num_replicas=replicas,
+                                                                   num_partitions=partitions,
+                                                                   size=replicas * partitions, assignment=out))
+        return list(out)
+
     def compile(self, program) -> Executable:
         """`program`: StableHLO as MLIR text (str) or MLIR bytecode (bytes); format "mlir" covers both."""
         code = program.encode() if isinstance(program, str) else bytes(program)
@@ -367,12 +416,13 @@ class Client:
         a = self.api.call("Client_Compile", CompileArgs(client=self.h, program=C.pointer(prog)))
         return Executable(self, a.executable)
 
-    def buffer_from_host(self, x: np.ndarray, device=None, semantics: int = 1) -> Buffer:
+    def buffer_from_host(self, x: np.ndarray, device=None, semantics: int = 1, memory=None) -> Buffer:
         x = np.ascontiguousarray(x).reshape(np.shape(x))   # (ascontiguousarray turns 0-d into 1-d)
         dims = (C.c_int64 * max(1, x.ndim))(*x.shape)
         a = self.api.call("Client_BufferFromHostBuffer", FromHostArgs(
             client=self.h, data=x.ctypes.data, type=np_type_code(x), dims=dims, num_dims=x.ndim,
-            host_buffer_semantics=semantics, device=device or self.devices(True)[0]))
+            host_buffer_semantics=semantics, device=device if device or memory else self.devices(True)[0],
+            memory=memory))
         self.api.await_event(a.done_with_host_buffer)
         return Buffer(self, a.buffer)
 

@@ -488,3 +488,54 @@ def test_split_k_dot_read_by_a_fused_kernel(client):
     refs = oracle_run(text, ins)
     assert_close(outs[0], refs[0], 1e-2, "update")
     assert_close(outs[1], refs[1], 1e-2, "column sum")
+
+
+def test_memory_spaces_and_placement(client):
+    """Each device has HBM ("device", default) and page-locked host memory ("pinned_host"): a buffer
+    placed in pinned_host lives in host memory (IsOnCpu), copies between the spaces keep the bytes,
+    and an executable refuses a pinned_host argument instead of reading host memory as if it were HBM."""
+    mems = client.memories()
+    kinds = [client.memory_kind(m) for m in mems]
+    assert kinds == ["device", "pinned_host"]
+    hbm, host = mems
+    assert client.memory_id(hbm) != client.memory_id(host)
+    x = (np.arange(4 * 257) % 13 - 6).astype(np.float32).reshape(4, 257)
+    hb = client.buffer_from_host(x, memory=host)
+    assert hb.is_on_cpu() and hb.memory() == host
+    np.testing.assert_array_equal(hb.to_numpy(), x)
+    db = hb.copy_to_memory(hbm)
+    assert not db.is_on_cpu() and db.memory() == hbm
+    np.testing.assert_array_equal(db.to_numpy(), x)
+    back = db.copy_to_memory(host)
+    assert back.is_on_cpu()
+    np.testing.assert_array_equal(back.to_numpy(), x)
+    b = Builder("jit_neg")
+    y = b.arg((4, 257), "f32")
+    exe = client.compile(b.text([-y]))
+    np.testing.assert_array_equal(exe.execute([db])[0].to_numpy(), -x)
+    with pytest.raises(pjrt.PjrtError) as e:
+        exe.execute([hb])
+    assert e.value.code_name == "INVALID_ARGUMENT" and "pinned_host" in e.value.message
+    for buf in (hb, db, back):
+        buf.delete()
+    exe.destroy()
+
+
+def test_external_references_defer_the_free(client):
+    x = np.arange(64, dtype=np.int32)
+    b = client.buffer_from_host(x)
+    b.add_external_ref(+1)
+    b.mark_deleted()
+    assert b.is_deleted()
+    b.add_external_ref(-1)                      # the last reference releases the storage
+    with pytest.raises(pjrt.PjrtError):
+        b.add_external_ref(-1)                  # no references left
+    b.delete()
+
+
+def test_device_lookup_and_default_assignment(client):
+    devs = client.devices()
+    assert client.lookup_device(0) == devs[0]
+    with pytest.raises(pjrt.PjrtError):
+        client.lookup_device(len(devs))
+    assert client.default_device_assignment(1, 1) == [0]
