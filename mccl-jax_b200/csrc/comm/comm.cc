@@ -102,40 +102,117 @@ std::unique_ptr<Comm> Comm::Create(int world, int rank, int device, const KvStor
   c->comm_ = comm;
   c->rank_ = rank;
   c->world_ = world;
+  c->kv_ = kv;
+  c->enqueue_timeout_ms_ = timeout_ms;
   return c;
 }
 
 Comm::~Comm() {
-  if (comm_) ncclCommDestroy((ncclComm_t)comm_);
+  if (comm_) ncclCommDestroy((ncclComm_t)comm_);     // an aborted communicator has none left
 }
 
-static std::string Wait(ncclComm_t comm, ncclResult_t r, const char* what) {
-  // non-blocking communicator: enqueue may return ncclInProgress
+void Comm::AbortLocked(const std::string& why) {
+  if (!broken_.empty()) return;
+  broken_ = why.empty() ? "communicator aborted" : why;
+  if (comm_) ncclCommAbort((ncclComm_t)comm_);
+  comm_ = nullptr;
+}
+
+void Comm::Abort(const std::string& why) {
+  std::lock_guard<std::mutex> g(mu_);
+  AbortLocked(why);
+}
+
+bool Comm::broken() {
+  std::lock_guard<std::mutex> g(mu_);
+  return !broken_.empty();
+}
+
+std::string Comm::broken_reason() {
+  std::lock_guard<std::mutex> g(mu_);
+  return broken_;
+}
+
+// Non-blocking communicator: an enqueue may return ncclInProgress until NCCL has taken the call.
+// The wait is bounded; past the bound the communicator is aborted.
+std::string Comm::Finish(int result, const char* what) {
+  ncclResult_t r = (ncclResult_t)result;
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(enqueue_timeout_ms_);
   while (r == ncclInProgress) {
-    ncclCommGetAsyncError(comm, &r);
-    if (r == ncclInProgress) std::this_thread::yield();
+    ncclCommGetAsyncError((ncclComm_t)comm_, &r);
+    if (r != ncclInProgress) break;
+    if (std::chrono::steady_clock::now() > deadline) {
+      AbortLocked(std::string(what) + " timed out after " + std::to_string(enqueue_timeout_ms_) + " ms");
+      return broken_;
+    }
+    std::this_thread::yield();
   }
   return r == ncclSuccess ? std::string() : std::string(what) + ": " + ncclGetErrorString(r);
 }
 
 std::string Comm::AllReduce(const void* send, void* recv, size_t count, DT dt, ReduceKind op, cudaStream_t st) {
+  std::lock_guard<std::mutex> g(mu_);
+  if (!broken_.empty()) return broken_;
   ncclDataType_t t;
   ncclRedOp_t o;
   if (!NcclType(dt, &t) || !NcclOp(op, &o)) return "all_reduce: unsupported dtype or reducer";
-  return Wait((ncclComm_t)comm_, ncclAllReduce(send, recv, count, t, o, (ncclComm_t)comm_, st), "ncclAllReduce");
+  return Finish(ncclAllReduce(send, recv, count, t, o, (ncclComm_t)comm_, st), "ncclAllReduce");
 }
 
 std::string Comm::AllGather(const void* send, void* recv, size_t send_count, DT dt, cudaStream_t st) {
+  std::lock_guard<std::mutex> g(mu_);
+  if (!broken_.empty()) return broken_;
   ncclDataType_t t;
   if (!NcclType(dt, &t)) return "all_gather: unsupported dtype";
-  return Wait((ncclComm_t)comm_, ncclAllGather(send, recv, send_count, t, (ncclComm_t)comm_, st), "ncclAllGather");
+  return Finish(ncclAllGather(send, recv, send_count, t, (ncclComm_t)comm_, st), "ncclAllGather");
 }
 
 std::string Comm::ReduceScatter(const void* send, void* recv, size_t recv_count, DT dt, ReduceKind op, cudaStream_t st) {
+  std::lock_guard<std::mutex> g(mu_);
+  if (!broken_.empty()) return broken_;
   ncclDataType_t t;
   ncclRedOp_t o;
   if (!NcclType(dt, &t) || !NcclOp(op, &o)) return "reduce_scatter: unsupported dtype or reducer";
-  return Wait((ncclComm_t)comm_, ncclReduceScatter(send, recv, recv_count, t, o, (ncclComm_t)comm_, st), "ncclReduceScatter");
+  return Finish(ncclReduceScatter(send, recv, recv_count, t, o, (ncclComm_t)comm_, st), "ncclReduceScatter");
+}
+
+std::string Comm::GroupStart() {
+  std::lock_guard<std::mutex> g(mu_);
+  if (!broken_.empty()) return broken_;
+  const ncclResult_t r = ncclGroupStart();
+  return r == ncclSuccess ? std::string() : std::string("ncclGroupStart: ") + ncclGetErrorString(r);
+}
+
+std::string Comm::GroupEnd() {
+  std::lock_guard<std::mutex> g(mu_);
+  if (!broken_.empty()) {
+    ncclGroupEnd();                                  // close the host-side group either way
+    return broken_;
+  }
+  return Finish(ncclGroupEnd(), "ncclGroupEnd");
+}
+
+std::string Comm::Handshake(int timeout_ms) {
+  if (broken()) return broken_reason();
+  if (!kv_.put || !kv_.get) return "";
+  const long long n = ++handshakes_;
+  const std::string base = "b200_pjrt/execution/" + std::to_string(n) + "/";
+  std::string e = kv_.put(base + std::to_string(rank_), "1");
+  if (!e.empty()) {
+    Abort("execution handshake: " + e);
+    return broken_reason();
+  }
+  for (int r = 0; r < world_; ++r) {
+    if (r == rank_) continue;
+    std::string v;
+    e = kv_.get(base + std::to_string(r), timeout_ms, &v);
+    if (!e.empty()) {
+      Abort("execution handshake timed out after " + std::to_string(timeout_ms) + " ms: rank " + std::to_string(r) +
+            " did not arrive at execution " + std::to_string(n) + " (" + e + ")");
+      return broken_reason();
+    }
+  }
+  return "";
 }
 
 }  // namespace b200

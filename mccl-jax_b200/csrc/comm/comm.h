@@ -11,6 +11,7 @@
 
 #include <functional>
 #include <memory>
+#include <mutex>
 #include <string>
 
 #include "../jam/ir.h"
@@ -37,10 +38,38 @@ class Comm {
   std::string AllGather(const void* send, void* recv, size_t send_count, DT dt, cudaStream_t st);
   std::string ReduceScatter(const void* send, void* recv, size_t recv_count, DT dt, ReduceKind op, cudaStream_t st);
 
+  // Collectives enqueued between GroupStart and GroupEnd go to NCCL as one group (one launch for
+  // the set instead of one per call).
+  std::string GroupStart();
+  std::string GroupEnd();
+
+  // Host-side rendezvous before an execution that runs collectives: this rank posts its arrival at
+  // the next execution through the key-value store and waits up to `timeout_ms` for every other
+  // rank's.  A rank that has left makes it fail ("timed out") before any collective is enqueued; the
+  // communicator is then aborted, with no NCCL work of this rank in flight.
+  std::string Handshake(int timeout_ms);
+
+  // Ends the communicator (ncclCommAbort: NCCL kernels still waiting on it return); later calls fail
+  // with `why`.  Used when a rank is gone or a collective ran past its deadline.
+  // Safe to call from another thread while this one is enqueueing (the calls are serialized).
+  void Abort(const std::string& why);
+  bool broken();
+  std::string broken_reason();
+
+  // Bound on the host-side waits of one enqueue (ncclInProgress on the non-blocking communicator).
+  void set_enqueue_timeout_ms(int ms) { enqueue_timeout_ms_ = ms; }
+
  private:
   Comm() = default;
+  std::string Finish(int result, const char* what);   // waits out ncclInProgress, bounded (mu_ held)
+  void AbortLocked(const std::string& why);
+  std::mutex mu_;         // serializes NCCL calls on comm_ with Abort
   void* comm_ = nullptr;  // ncclComm_t
   int rank_ = 0, world_ = 1;
+  KvStore kv_;
+  long long handshakes_ = 0;
+  int enqueue_timeout_ms_ = 120000;
+  std::string broken_;
 };
 
 }  // namespace b200

@@ -1029,6 +1029,7 @@ class Lowerer {
     EmitSteps();
     BindOutputs();
     MergeTinyLoops();
+    GroupSmallCollectives();
     MarkAsyncCollectives();
     ComputeLastUse();
     EndKernel();
@@ -3798,6 +3799,61 @@ class Lowerer {
     }
     return r;
   }
+  // Small all-reduces (at most 256 KiB each: bias, LayerNorm-parameter and loss gradients) are held
+  // back from where hoisting put them and issued together, as one NCCL group, with the next large
+  // collective, or just before the first step that needs one of their results or writes one of
+  // their operands -- or when the held ones reach 4 MiB.  The reference buckets the same in-place
+  // all-reduces of <= 256 KiB into one call through a packed buffer (src/jam/jam_run.mm:186-248);
+  // an NCCL group does it without the packing copies.
+  void GroupSmallCollectives() {
+    if (opt_.num_processes <= 1 || std::getenv("B200_NO_COLL_GROUPS")) return;
+    constexpr int64_t kSmall = 256 << 10, kFlushBytes = 4 << 20;
+    std::vector<Step> out, held;
+    std::set<int> held_out, held_in;
+    int64_t held_bytes = 0;
+    int next_group = 0;
+    auto flush = [&]() {
+      if (held.empty()) return;
+      const int g = held.size() > 1 ? next_group++ : -1;
+      for (Step& h : held) {
+        h.coll.group = g;
+        if (g >= 0) h.label += " [group " + std::to_string(g) + "]";
+        out.push_back(std::move(h));
+      }
+      held.clear();
+      held_out.clear();
+      held_in.clear();
+      held_bytes = 0;
+    };
+    for (Step& st : p_->steps) {
+      const bool coll = st.kind == StepKind::kCollective;
+      const int64_t bytes = coll ? st.coll.send_count * DTBytes(st.coll.dt) : 0;
+      if (coll && st.coll.op == CollKind::kAllReduce && bytes <= kSmall) {
+        held_out.insert(st.coll.out);
+        held_in.insert(st.coll.in);
+        held_bytes += bytes;
+        held.push_back(std::move(st));
+        if (held_bytes >= kFlushBytes) flush();
+        continue;
+      }
+      if (coll) {
+        // a large collective takes the held ones along in its group (their operands are older)
+        held.push_back(std::move(st));
+        flush();
+        continue;
+      }
+      std::set<int> r, w;
+      StepRW(st, &r, &w);
+      bool conflict = false;
+      for (int x : r) conflict = conflict || held_out.count(x);
+      for (int x : w) conflict = conflict || held_in.count(x) || held_out.count(x);
+      if (conflict) flush();
+      out.push_back(std::move(st));
+    }
+    flush();
+    p_->steps = std::move(out);
+  }
+
   // Collectives of a multi-process program run on the communication stream; the first step that
   // reads a collective's result waits for it (later readers are ordered behind that step).
   std::vector<int> coll_until_;   // step index -> step that waits for it (async collectives)

@@ -86,6 +86,7 @@ struct CollectiveStep {
   int in = -1, out = -1;
   int64_t send_count = 0, recv_count = 0;
   DT dt = DT::kF32;
+  int group = -1;              // consecutive steps with one group id go to NCCL as one group
 };
 
 struct CopyStep {

@@ -387,6 +387,17 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
       if (owned[s]) DeviceFree(ptr[s], st);
     return e;
   };
+  bool has_coll = false;
+  for (const Step& S : P.steps) has_coll = has_coll || S.kind == StepKind::kCollective;
+  if (has_coll && comm) {
+    if (comm->broken()) return "the communicator is unusable: " + comm->broken_reason();
+    // optional host-side rendezvous of all ranks before any collective of this execution is enqueued
+    static const int handshake_ms = std::getenv("B200_EXEC_HANDSHAKE_MS") ? std::atoi(std::getenv("B200_EXEC_HANDSHAKE_MS")) : 0;
+    if (handshake_ms > 0) {
+      std::string e = comm->Handshake(handshake_ms);
+      if (!e.empty()) return e;
+    }
+  }
   ExecTimerMarkStart(dev.ordinal, st);
   static StepTimer timer;
   const auto host_t0 = std::chrono::steady_clock::now();
@@ -406,8 +417,6 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
   // of an earlier execution (intermediates are at fixed arena offsets) replays that execution's
   // launches as one graph.  The first execution with a set of addresses runs eagerly (lazy set-up
   // happens there), the second is captured, later ones launch the graph.
-  bool has_coll = false;
-  for (const Step& S : P.steps) has_coll = has_coll || S.kind == StepKind::kCollective;
   // (a program of a few launches gains nothing from a graph and pays its launch latency)
   size_t n_launch = 0;
   for (const Step& S : P.steps) n_launch += S.kind == StepKind::kFusion ? S.launches.size() : 1;
@@ -570,25 +579,45 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
           const CollectiveStep& c = S.coll;
           for (int q : {c.in, c.out}) { err = slot(q); if (!err.empty()) return fail(err); }
           if (!comm) return fail("collective in a single-process program without a communicator");
+          // a group is a run of consecutive collective steps with one group id: one NCCL group
+          auto same_group = [&](size_t j) {
+            return j < P.steps.size() && P.steps[j].kind == StepKind::kCollective && P.steps[j].coll.group == c.group;
+          };
+          const bool opens = c.group < 0 || i == 0 || !same_group(i - 1);
+          const bool closes = c.group < 0 || !same_group(i + 1);
           cudaStream_t cs = st;
           if (S.async) {
             // on the communication stream, after everything enqueued so far on the compute stream
             if (!dev.comm_stream && cudaStreamCreateWithFlags(&dev.comm_stream, cudaStreamNonBlocking) != cudaSuccess)
               return fail("cannot create the communication stream");
-            cudaEvent_t ready;
-            cudaEventCreateWithFlags(&ready, cudaEventDisableTiming);
-            cudaEventRecord(ready, st);
-            cudaStreamWaitEvent(dev.comm_stream, ready, 0);
-            cudaEventDestroy(ready);
+            if (opens) {
+              cudaEvent_t ready;
+              cudaEventCreateWithFlags(&ready, cudaEventDisableTiming);
+              cudaEventRecord(ready, st);
+              cudaStreamWaitEvent(dev.comm_stream, ready, 0);
+              cudaEventDestroy(ready);
+            }
             cs = dev.comm_stream;
+          }
+          if (c.group >= 0 && opens) {
+            err = comm->GroupStart();
+            if (!err.empty()) { release_events(); return fail(err); }
           }
           if (c.op == CollKind::kAllReduce) err = comm->AllReduce(ptr[c.in], ptr[c.out], c.send_count, c.dt, c.reduce, cs);
           else if (c.op == CollKind::kAllGather) err = comm->AllGather(ptr[c.in], ptr[c.out], c.send_count, c.dt, cs);
           else err = comm->ReduceScatter(ptr[c.in], ptr[c.out], c.recv_count, c.dt, c.reduce, cs);
+          if (c.group >= 0 && (closes || !err.empty())) {
+            const std::string e2 = comm->GroupEnd();
+            if (err.empty()) err = e2;
+          }
           if (!err.empty()) { release_events(); return fail(err); }
-          if (S.async) {
-            cudaEventCreateWithFlags(&coll_done[i], cudaEventDisableTiming);
-            cudaEventRecord(coll_done[i], cs);
+          if (S.async && closes) {
+            // every member of the group completes with the group
+            for (size_t k = i; ; --k) {
+              cudaEventCreateWithFlags(&coll_done[k], cudaEventDisableTiming);
+              cudaEventRecord(coll_done[k], cs);
+              if (c.group < 0 || k == 0 || !same_group(k - 1)) break;
+            }
           }
           break;
         }

@@ -577,9 +577,11 @@ int TakeGemmError() {
 // launch is the number of rounds of work units over the SMs times the time of one unit, which grows
 // with the tile width (BN = 256, 192 or 128 columns) and the unit's K blocks plus about two blocks of
 // fill and epilogue; narrower tiles pay a little for feeding the tensor cores more operand bytes
-// per FLOP.  K is split (at most 8 slices of >= 16 K blocks, none empty) only when the tiles leave
-// more than half the SMs idle: the f32 partials cost a zeroing pass, L2 reductions and a rounding
-// pass.  Shared by the compiler (which sizes the workspace) and the launcher.
+// per FLOP.  K is split (at most 8 slices of >= 16 K blocks, none empty) when that shortens the
+// model's time including the f32 partials' cost (a zeroing pass, L2 reductions and, for 16-bit
+// results, a rounding pass): when the tiles leave SMs idle, or when a long K walk makes the last
+// round of tiles a large fraction of the launch.  Shared by the compiler (which sizes the workspace)
+// and the launcher.
 void GemmTile(int64_t batch, int64_t M, int64_t N, int64_t K, int sms, int* bn_out, int* splits_out) {
   const int64_t kbs = std::max<int64_t>(1, (K + BK - 1) / BK), mb = (M + BM - 1) / BM;
   const bool no_split = std::getenv("B200_GEMM_NO_SPLITK") != nullptr || K <= 0;
@@ -592,7 +594,7 @@ void GemmTile(int64_t batch, int64_t M, int64_t N, int64_t K, int sms, int* bn_o
     const int64_t tiles = mb * ((N + bn - 1) / bn) * batch;
     const double width = bn / 256.0 * (bn == 128 ? 1.3 : bn == 192 ? 1.08 : 1.0);   // measured on B200
     for (int64_t s = 1; s <= 8; ++s) {
-      if (s > 1 && (no_split || tiles * 2 > sms || kbs / s < 16)) break;
+      if (s > 1 && (no_split || kbs / s < 16 || (tiles * 2 > sms && kbs < 128))) break;
       const int64_t kps = (kbs + s - 1) / s;
       if (s > 1 && (s - 1) * kps >= kbs) continue;        // would leave an empty slice
       const int64_t rounds = (tiles * s + sms - 1) / sms;
@@ -698,7 +700,7 @@ __device__ __forceinline__ float load_as_f32(const __half* p) { return __half2fl
 template <typename T>
 __global__ void __launch_bounds__(256) split_pieces_kernel(const T* __restrict__ src, long long ld, int src_mn, int dst_mn,
                                                            int batch, int rows, int K, int Kp, int pieces,
-                                                           uint16_t* __restrict__ dst) {
+                                                           uint16_t* __restrict__ dst, int vec_ok) {
   const long long outer = dst_mn ? (long long)pieces * Kp : rows;      // destination rows per batch
   const long long inner = dst_mn ? rows : (long long)pieces * Kp;      // destination row length
   const long long quads = inner / 4;                                   // inner % 4 == 0 (host-checked)
@@ -707,6 +709,32 @@ __global__ void __launch_bounds__(256) split_pieces_kernel(const T* __restrict__
     const long long q = e % quads, t = e / quads;
     const long long o = t % outer, b = t / outer;
     uint16_t h[4];
+    if (sizeof(T) == 4 && vec_ok && src_mn == dst_mn) {
+      // same layout on both sides: the quad is 4 consecutive source elements of one piece, read as
+      // one 16-byte load when they are all inside the operand
+      const long long i = q * 4;
+      long long j, k, r;
+      if (dst_mn) { j = o / Kp; k = o - j * Kp; r = i; }
+      else { j = i / Kp; k = i - j * Kp; r = o; }
+      const bool inside = dst_mn ? (k < K) : (k + 3 < K);
+      if (inside) {
+        const float4 x4 = *reinterpret_cast<const float4*>(src + (src_mn ? (b * K + k) * ld + r : (b * rows + r) * ld + k));
+        float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          float x = xs[v];
+          __nv_bfloat16 piece = __float2bfloat16_rn(x);
+          for (long long p = 0; p < j; ++p) {
+            x -= __bfloat162float(piece);
+            piece = __float2bfloat16_rn(x);
+          }
+          h[v] = __bfloat16_as_ushort(piece);
+        }
+        *(uint2*)(dst + (b * outer + o) * inner + q * 4) =
+            make_uint2((uint32_t)h[0] | ((uint32_t)h[1] << 16), (uint32_t)h[2] | ((uint32_t)h[3] << 16));
+        continue;
+      }
+    }
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
       const long long i = q * 4 + v;
@@ -752,8 +780,10 @@ int LaunchSplit(const void* src, long long ld, bool src_mn, const SplitOperand& 
                 int64_t Kp, void* dst, cudaStream_t st) {
   const long long total = (long long)batch * rows * o.pieces * Kp / 4;
   const int grid = (int)std::min<long long>((total + 255) / 256, (long long)NumSMs() * 8);
+  // 16-byte source loads need a 16-byte aligned base and rows of a multiple of 4 elements
+  const int vec_ok = ((uintptr_t)src % 16) == 0 && (ld % 4) == 0;
   split_pieces_kernel<T><<<grid, 256, 0, st>>>((const T*)src, ld, src_mn ? 1 : 0, o.dst_mn ? 1 : 0, (int)batch, (int)rows,
-                                               (int)K, (int)Kp, o.pieces, (uint16_t*)dst);
+                                               (int)K, (int)Kp, o.pieces, (uint16_t*)dst, vec_ok);
   CountLaunches();
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

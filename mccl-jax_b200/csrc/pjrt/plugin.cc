@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <cstddef>
 #include <cstdlib>
@@ -84,6 +85,13 @@ class Completion {
   ~Completion() {
     if (event_) cudaEventDestroy(event_);
   }
+  // For work that includes collectives: if it has not completed `ms` after a wait starts, run
+  // `on_expiry` (which aborts the communicator, so the NCCL kernels waiting on it return) and report
+  // DEADLINE_EXCEEDED.
+  void SetDeadline(int ms, std::function<void()> on_expiry) {
+    deadline_ms_ = ms;
+    on_expiry_ = std::move(on_expiry);
+  }
 
   // Blocks until done, then runs the callbacks (once).
   void Wait() {
@@ -95,8 +103,27 @@ class Completion {
     std::string problem;
     if (event_) {
       cudaSetDevice(ordinal_);
+      bool expired = false;
+      if (deadline_ms_ > 0) {
+        const auto until = std::chrono::steady_clock::now() + std::chrono::milliseconds(deadline_ms_);
+        const auto spin_until = std::chrono::steady_clock::now() + std::chrono::milliseconds(5);
+        while (cudaEventQuery(event_) == cudaErrorNotReady) {
+          const auto now = std::chrono::steady_clock::now();
+          if (now > until) {
+            expired = true;
+            if (on_expiry_) on_expiry_();
+            break;
+          }
+          if (now < spin_until) std::this_thread::yield();     // short waits: no sleep latency
+          else std::this_thread::sleep_for(std::chrono::microseconds(100));
+        }
+      }
       const cudaError_t e = cudaEventSynchronize(event_);
-      if (e != cudaSuccess) {
+      if (expired) {
+        code = PJRT_Error_Code_DEADLINE_EXCEEDED;
+        problem = "the execution's collectives did not complete within " + std::to_string(deadline_ms_) +
+                  " ms; the communicator was aborted";
+      } else if (e != cudaSuccess) {
         code = PJRT_Error_Code_INTERNAL;
         problem = std::string("device execution failed: ") + cudaGetErrorString(e);
       } else if (reads_kernel_flags_) {
@@ -155,6 +182,8 @@ class Completion {
   std::string problem_;
   cudaEvent_t event_ = nullptr;
   int ordinal_ = 0;
+  int deadline_ms_ = 0;
+  std::function<void()> on_expiry_;
   std::vector<std::pair<PJRT_Event_OnReadyCallback, void*>> callbacks_;
 };
 
@@ -679,9 +708,19 @@ PJRT_Error* Execute(PJRT_LoadedExecutable_Execute_Args* a) {
       std::lock_guard<std::mutex> g(dev->launch_mu);
       cudaSetDevice(dev->ordinal);
       std::string err = le->program->Run(dev->cuda, args, &outs, le->client->comm.get());
-      if (!err.empty()) return Fail(PJRT_Error_Code_INTERNAL, err);
+      if (!err.empty())
+        return Fail(err.find("timed out") != std::string::npos ? PJRT_Error_Code_DEADLINE_EXCEEDED : PJRT_Error_Code_INTERNAL,
+                    err);
     }
     CompletionRef done = Completion::After(dev->ordinal, dev->cuda.stream, true);
+    if (b200::Comm* comm = le->client->comm.get()) {
+      bool collectives = false;
+      for (const b200::Step& st : plan.steps) collectives = collectives || st.kind == b200::StepKind::kCollective;
+      if (collectives)
+        done->SetDeadline(EnvInt("B200_COLLECTIVE_TIMEOUT_MS", 600000), [comm] {
+          comm->Abort("a collective did not complete within its deadline");
+        });
+    }
     for (size_t i = 0; i < outs.size(); ++i) {
       const b200::TensorType& t = plan.out_types[i];
       a->output_lists[k][i] = NewBuffer(le->client, dev->hbm(), PjrtTypeOf(t.dt), t.dims, (size_t)t.bytes(), outs[i], done);

@@ -55,6 +55,63 @@ def main():
     client = pjrt.Client(api, node_id=rank, num_nodes=world, device_ordinal=rank, kv_put=put, kv_get=get)
     out = {"rank": rank}
     ok = True
+    if case == "peer_leaves":
+        # both ranks run one psum; rank 1 then leaves (client closed, process gone) between executions;
+        # rank 0's next execution must end in DEADLINE_EXCEEDED from the execution handshake (run with
+        # B200_EXEC_HANDSHAKE_MS set) before any collective is enqueued, and its client must close
+        p = configs.psum_program(1024, world, with_inputs=False)
+        exe = client.compile(p.text)
+        r = client.run(exe, [np.full(1024, rank + 1, np.float32)])[0]
+        ok &= bool(np.all(r == world * (world + 1) / 2))
+        store.set(f"step1_done/{rank}", b"1")
+        store.wait([f"step1_done/{q}" for q in range(world)], datetime.timedelta(seconds=60))
+        if rank == 1:
+            exe.destroy()
+            client.close()
+            out.update(ok=bool(ok), left=True)
+            print(json.dumps(out))
+            return 0 if ok else 1
+        time.sleep(1.0)
+        t0 = time.time()
+        try:
+            client.run(exe, [np.full(1024, 1.0, np.float32)])
+            out["error"] = "the execution ran without its peer"
+            ok = False
+        except pjrt.PjrtError as e:
+            out.update(code=e.code_name, msg=e.message[:300], s=time.time() - t0)
+            ok &= e.code_name == "DEADLINE_EXCEEDED"
+        # the communicator is gone: a further execution fails at once with the same cause
+        try:
+            client.run(exe, [np.full(1024, 1.0, np.float32)])
+            ok = False
+        except pjrt.PjrtError as e:
+            out["again"] = e.message[:200]
+        exe.destroy()
+        t1 = time.time()
+        client.close()
+        out["close_s"] = time.time() - t1
+        out["ok"] = bool(ok)
+        print(json.dumps(out))
+        return 0 if ok else 1
+    if case == "dp_step":
+        # the GPT-2 DP train step (tiny widths, with its ~40 gradient all-reduces, small ones grouped)
+        # on `world` ranks against the oracle's run of all ranks
+        from oracle.interp import run_spmd
+        tiny = dict(layers=2, d=64, heads=2, mlp=128, vocab=96, seq=64)
+        progs = [configs.gpt2_program(batch=2, world=world, rank=q, **tiny) for q in range(world)]
+        outs = client.run(progs[rank].text, progs[rank].inputs)
+        refs = run_spmd(progs[0].text, [pq.inputs for pq in progs])[rank]
+        n = progs[0].meta["n_tensors"]
+        errs = []
+        for i, (o, r) in enumerate(zip(outs, refs)):
+            o32, r32 = np.asarray(o, np.float32), np.asarray(r, np.float32)
+            if i < n:
+                ok &= bool(np.all(np.abs(o32 - r32) <= 2.2 * 3e-4 + np.abs(r32) * 2.0 ** -7 + 1e-30))
+            else:
+                e = float(np.max(np.abs(o32 - r32)) / max(float(np.max(np.abs(r32))), 1e-30))
+                errs.append(e)
+                ok &= e <= (1e-3 if i == len(outs) - 1 else 5e-2)
+        out["max_moment_err"] = max(errs)
     if case == "collectives":
         # smoke_multi.cc:32-48 known answer: rank r contributes r+1 in 1024 floats -> n(n+1)/2
         p = configs.psum_program(1024, world, with_inputs=False)

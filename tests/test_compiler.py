@@ -258,3 +258,16 @@ def test_collectives_across_processes_need_one_world_group(lib_path, groups, ok)
         assert rc == 0 and "all_reduce" in rep, rep
     else:
         assert rc == 1 and "replica_groups" in rep, rep
+
+
+def test_small_all_reduces_are_issued_as_nccl_groups(lib_path):
+    """Across processes, the DP step's small gradient all-reduces (<= 256 KiB) are held back and
+    issued together as NCCL groups; large ones keep their hoisted places."""
+    p = configs.gpt2_program(batch=2, world=2, layers=2, d=64, heads=2, mlp=128, vocab=96, seq=64, with_inputs=False)
+    rc, rep = report(lib_path, p.text, nprocs=2)
+    assert rc == 0, rep
+    colls = [l for l in rep.splitlines() if "all_reduce" in l]
+    grouped = [l for l in colls if "[group" in l]
+    assert len(colls) > 10 and len(grouped) >= len(colls) // 2, rep
+    rc, rep1 = report(lib_path, p.text, nprocs=1)
+    assert rc == 0 and "[group" not in rep1

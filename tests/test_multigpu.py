@@ -59,6 +59,31 @@ def test_nccl_collectives_through_pjrt(lib_path, world):
 
 
 @pytest.mark.gpu
+def test_dp_step_on_two_ranks_matches_the_oracle(lib_path):
+    """The tiny GPT-2 DP step (shard_map + psum of ~40 gradients, small ones as NCCL groups) on two
+    GPUs against the oracle's two-rank run."""
+    if gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    for rc, o, e in run_ranks("dp_step", 2):
+        assert rc == 0, (o, e[-2000:])
+        assert json.loads(o.strip().splitlines()[-1])["ok"]
+
+
+@pytest.mark.gpu
+def test_rank_that_leaves_between_steps_gives_deadline_error(lib_path):
+    """A rank that leaves between executions: the survivor's next execution fails with
+    DEADLINE_EXCEEDED from the host-side execution handshake -- no collective is enqueued, so nothing
+    waits on the GPU for the missing rank -- and its client still closes."""
+    if gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    outs = run_ranks("peer_leaves", 2, {"B200_EXEC_HANDSHAKE_MS": "3000"}, timeout=120)
+    for rc, o, e in outs:
+        assert rc == 0, (o, e[-2000:])
+    res = json.loads(outs[0][1].strip().splitlines()[-1])
+    assert res["code"] == "DEADLINE_EXCEEDED" and res["s"] < 30 and res["close_s"] < 30, res
+
+
+@pytest.mark.gpu
 def test_rank_that_never_joins_gives_deadline_error(lib_path):
     if gpu_count() < 2:
         pytest.skip("needs 2 GPUs")
