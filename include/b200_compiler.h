@@ -23,6 +23,14 @@ extern "C" {
 __attribute__((visibility("default"))) int b200_compile_report(const char* text, size_t size, int num_processes,
                                                                int nvrtc, char* out, size_t out_size);
 
+/* Decodes the partitioning fields of an xla.CompileOptionsProto (the compile_options bytes of
+ * PJRT_Client_Compile) the way PJRT_Client_Compile does, without a client: writes
+ * "replicas=R partitions=P assignment=RxC devices=d,d;d,d" (-1 for fields not present) or
+ * "error: <message>".  Returns 0, 1 on malformed input, -1 if `out` is too small.  No counterpart in
+ * the reference (which ignores compile_options, src/pjrt/api/pjrt_c_api.cc:681-697). */
+__attribute__((visibility("default"))) int b200_compile_options_report(const void* data, size_t size, char* out,
+                                                                       size_t out_size);
+
 /* Device-time measurement of PJRT executions (no counterpart in the reference, whose runner timed
  * segments with host clocks under MCCL_JAX_TIME, src/jam/jam_run.mm:114-126).
  * b200_exec_timer(0): reset — the next LoadedExecutable_Execute records a CUDA event on the device

@@ -713,6 +713,27 @@ extern "C" int b200_compile_report(const char* text, size_t size, int num_proces
   return rc;
 }
 
+#include "../pjrt/compile_options.h"
+
+extern "C" int b200_compile_options_report(const void* data, size_t size, char* out, size_t out_size) {
+  b200::CompileOptionsInfo co;
+  const std::string e = b200::ParseCompileOptions((const uint8_t*)data, size, &co);
+  std::string r;
+  if (!e.empty()) {
+    r = "error: " + e;
+  } else {
+    r = "replicas=" + std::to_string(co.num_replicas) + " partitions=" + std::to_string(co.num_partitions) +
+        " assignment=" + std::to_string(co.da_replicas) + "x" + std::to_string(co.da_computations) + " devices=";
+    for (size_t c = 0; c < co.da_devices.size(); ++c) {
+      r += c ? ";" : "";
+      for (size_t k = 0; k < co.da_devices[c].size(); ++k) r += (k ? "," : "") + std::to_string(co.da_devices[c][k]);
+    }
+  }
+  if (!out || r.size() + 1 > out_size) return -1;
+  std::memcpy(out, r.c_str(), r.size() + 1);
+  return e.empty() ? 0 : 1;
+}
+
 extern "C" long long b200_graph_stats(int which) {
   return which == 0 ? b200::g_graph_captures.load() : b200::g_graph_launches.load();
 }

@@ -48,8 +48,8 @@ struct ACfg {
   static constexpr int kKOff = 2 * kQBytes;
   static constexpr int kVOff = kKOff + 2 * kKBytes;
   static constexpr int kPOff = kVOff + 2 * kVBytes;
-  static constexpr int kBarOff = kPOff + 2 * kPBytes;
-  static constexpr int kSmem = kBarOff + 256 + 1024;
+  static constexpr int kBarOff = kPOff + 4 * kPBytes;  // two P buffers per query tile
+  static constexpr int kSmem = kBarOff + 256 + 1024;   // 225.25 KB for D = 64 (limit 227 KB)
   static constexpr int kOCol = 256;
 };
 
@@ -123,8 +123,10 @@ __device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t addr) {
   return d;
 }
 
-enum { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kSFree = 11, kPFull = 13, kPVFull = 15,
-       kNumBars = 17 };
+// kPFull / kPVFull: one barrier per (query tile t, P buffer b) at index 2 t + b; KV tile j uses
+// buffer j & 1, so each of them completes once every second KV tile.
+enum { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kSFree = 11, kPFull = 13, kPVFull = 17,
+       kNumBars = 21 };
 
 // 320 threads: the compiler caps registers at 168 per thread (one CTA per SM); 200 does not launch.
 template <int D, bool CAUSAL, bool VT>
@@ -159,6 +161,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       mbar_init(&bars[kVEmpty + i], 1);
       mbar_init(&bars[kSFull + i], 1);
       mbar_init(&bars[kSFree + i], 128);
+    }
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&bars[kPFull + i], 128);
       mbar_init(&bars[kPVFull + i], 1);
     }
@@ -228,7 +232,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       };
       auto issue_pv = [&](int t, int j) {
         const int st = j & 1;
-        const uint32_t pa = p_addr + t * C::kPBytes, va = v_addr + st * C::kVBytes;
+        const uint32_t pa = p_addr + (2 * t + (j & 1)) * C::kPBytes, va = v_addr + st * C::kVBytes;
 #pragma unroll
         for (int k = 0; k < TK / 16; ++k) {
           const uint32_t off_p = (k / 4) * (TQ * 128) + (k % 4) * 32;
@@ -236,7 +240,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                                     : sw128_mn_desc(va + k * 16 * 128);
           mma_f16_ss(tmem + C::kOCol + t * D, sw128_desc(pa + off_p), bdesc, id_pv, (j | k) != 0);
         }
-        mma_commit(&bars[kPVFull + t]);
+        mma_commit(&bars[kPVFull + 2 * t + (j & 1)]);
       };
       bool ok = mbar_wait(&bars[kQFull], 0, kErrTimeoutFull, err);
       if (ok) ok = mbar_wait(&bars[kKFull + 0], 0, kErrTimeoutFull, err);
@@ -246,24 +250,31 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         issue_s(1, 0);
         mma_commit(&bars[kKEmpty + 0]);
       }
+      // Per KV tile j: both tiles' next scores S_t(j+1) as soon as their softmax has read S_t(j),
+      // then both P V products.  A softmax group therefore never waits behind the other group's P,
+      // and with two P buffers per tile it writes P(j+1) while P V(j) still reads P(j).
       for (int j = 0; j < n_kv && ok; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         const int ns = (j + 1) & 1;
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (j + 1 < n_kv) {
-            if (t == 0 && !mbar_wait(&bars[kKFull + ns], ((j + 1) >> 1) & 1, kErrTimeoutFull, err)) { ok = false; break; }
+        if (j + 1 < n_kv) {
+          if (!mbar_wait(&bars[kKFull + ns], ((j + 1) >> 1) & 1, kErrTimeoutFull, err)) { ok = false; break; }
+          for (int t = 0; t < 2 && ok; ++t) {
             if (!mbar_wait(&bars[kSFree + t], j & 1, kErrTimeoutFull, err)) { ok = false; break; }
             tc_fence_after();
             issue_s(t, j + 1);
-            if (t == 1) mma_commit(&bars[kKEmpty + ns]);
           }
-          if (t == 0 && !mbar_wait(&bars[kVFull + st], ph, kErrTimeoutFull, err)) { ok = false; break; }
-          if (!mbar_wait(&bars[kPFull + t], j & 1, kErrTimeoutFull, err)) { ok = false; break; }
+          if (!ok) break;
+          mma_commit(&bars[kKEmpty + ns]);
+        }
+        if (!mbar_wait(&bars[kVFull + st], ph, kErrTimeoutFull, err)) { ok = false; break; }
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!mbar_wait(&bars[kPFull + 2 * t + (j & 1)], (j >> 1) & 1, kErrTimeoutFull, err)) { ok = false; break; }
           tc_fence_after();
           issue_pv(t, j);
-          if (t == 1) mma_commit(&bars[kVEmpty + st]);
         }
+        if (!ok) break;
+        mma_commit(&bars[kVEmpty + st]);
       }
     }
   } else {
@@ -275,7 +286,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t s_col = tmem + t * 128 + lane_off;
     const uint32_t o_col = tmem + C::kOCol + t * D + lane_off;
-    uint8_t* p_row = smem + C::kPOff + t * C::kPBytes + r * 128;
+    uint8_t* const p_rows = smem + C::kPOff + 2 * t * C::kPBytes + r * 128;   // buffer b at + b * kPBytes
     float m_use = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
@@ -299,16 +310,25 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       for (int e = 1; e + 1 < TK; e += 2) mx = fmax3(mx, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
       mx = fmaxf(mx, __uint_as_float(sv[TK - 1]));
       mx *= scale_log2;
-      // P smem and the O accumulator are free once the previous P V product has completed
-      if (j > 0 && !mbar_wait_warp(&bars[kPVFull + t], (j - 1) & 1, kErrTimeoutAcc, err)) { ok = false; break; }
+      // This iteration writes P buffer j & 1, last read by P V(j - 2): wait for that product.
+      uint8_t* const p_row = p_rows + (j & 1) * C::kPBytes;
+      if (j >= 2 && !mbar_wait_warp(&bars[kPVFull + 2 * t + (j & 1)], ((j >> 1) - 1) & 1, kErrTimeoutAcc, err)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       // Lazy rescale.  The decision is per row, but tcgen05.ld / st are warp-collective
       // (.sync.aligned): the whole warp takes the TMEM path when any of its rows needs it, and rows
-      // that do not rescale multiply by 1.
+      // that do not rescale multiply by 1.  Rescaling O needs every earlier P V product done.
       const bool mine = mx > m_use + kRescaleThreshold;
       if (__any_sync(0xffffffffu, mine)) {
         const float m_new = mine ? mx : m_use;
         if (j > 0) {
+          if (!mbar_wait_warp(&bars[kPVFull + 2 * t + ((j - 1) & 1)], ((j - 1) >> 1) & 1, kErrTimeoutAcc, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
           const float f = mine ? ex2(m_use - m_new) : 1.f;
           l *= f;
 #pragma unroll
@@ -350,7 +370,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       fence_async_smem();
       mbar_arrive(&bars[kPFull + t]);
     }
-    if (ok && mbar_wait_warp(&bars[kPVFull + t], (n_kv - 1) & 1, kErrTimeoutAcc, err)) {
+    if (ok && mbar_wait_warp(&bars[kPVFull + 2 * t + ((n_kv - 1) & 1)], ((n_kv - 1) >> 1) & 1, kErrTimeoutAcc, err)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = O + (row_base + qrow) * D;

@@ -18,6 +18,7 @@
 // The API table is bound from small lambdas grouped by object (Bind* below).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <chrono>
 #include <condition_variable>
@@ -36,6 +37,7 @@
 #include "../../../include/pjrt_b200.h"
 #include "../comm/comm.h"
 #include "../jam/runtime.h"
+#include "compile_options.h"
 
 struct PJRT_Error {
   PJRT_Error_Code code;
@@ -741,6 +743,20 @@ PJRT_Error* CompileProgram(PJRT_Client_Compile_Args* a) {
       std::fclose(f);
     }
   }
+  // the partitioning jax asks for (xla.CompileOptionsProto), checked against this client's job
+  b200::CompileOptionsInfo co;
+  if (a->compile_options && a->compile_options_size) {
+    const std::string e = b200::ParseCompileOptions((const uint8_t*)a->compile_options, a->compile_options_size, &co);
+    if (!e.empty()) return BadArg("jam compile: compile_options: " + e);
+  }
+  const int64_t want = std::max<int64_t>(co.num_replicas, 1) * std::max<int64_t>(co.num_partitions, 1);
+  if (want > a->client->world)
+    return BadArg("jam compile: the compile options ask for " + std::to_string(want) +
+                  " devices (num_replicas x num_partitions); this job has " + std::to_string(a->client->world));
+  for (const auto& ids : co.da_devices)
+    for (int64_t id : ids)
+      if (id < 0 || id >= a->client->world)
+        return BadArg("jam compile: the device assignment names device " + std::to_string(id) + ", outside the job");
   b200::CompileOptions opt;
   opt.num_processes = a->client->world;
   opt.rank = a->client->rank;
@@ -748,6 +764,10 @@ PJRT_Error* CompileProgram(PJRT_Client_Compile_Args* a) {
   std::unique_ptr<b200::Executable> ex;
   const std::string err = b200::Executable::Build(p->code, p->code_size, opt, &ex);
   if (!err.empty()) return BadArg("jam compile: " + err);
+  const int module_parts = ex->plan().num_partitions;
+  if (co.num_partitions > 1 && module_parts > 1 && co.num_partitions != module_parts)
+    return BadArg("jam compile: compile options say num_partitions = " + std::to_string(co.num_partitions) +
+                  ", the module says " + std::to_string(module_parts));
   auto* le = new PJRT_LoadedExecutable();
   le->client = a->client;
   le->program = std::move(ex);

@@ -271,3 +271,36 @@ def test_small_all_reduces_are_issued_as_nccl_groups(lib_path):
     assert len(colls) > 10 and len(grouped) >= len(colls) // 2, rep
     rc, rep1 = report(lib_path, p.text, nprocs=1)
     assert rc == 0 and "[group" not in rep1
+
+
+def _options_report(lib_path, data):
+    lib = ctypes.CDLL(lib_path)
+    buf = ctypes.create_string_buffer(4096)
+    rc = lib.b200_compile_options_report(data, len(data), buf, len(buf))
+    return rc, buf.value.decode()
+
+
+def test_compile_options_proto_fields_decode_like_the_protobuf_library(lib_path):
+    """PJRT_Client_Compile's compile_options bytes (xla.CompileOptionsProto) as the protobuf library
+    writes them (tests/golden/make_compile_options.py): the plugin reads num_replicas /
+    num_partitions and the device assignment, and skips every other field."""
+    import json
+    with open(os.path.join(os.path.dirname(__file__), "golden", "compile_options.json")) as f:
+        cases = json.load(f)
+    assert len(cases) >= 4
+    for c in cases:
+        rc, rep = _options_report(lib_path, bytes.fromhex(c["hex"]))
+        assert rc == 0 and rep == c["expect"], (c["name"], rep)
+
+
+def test_malformed_compile_options_are_rejected(lib_path):
+    import json
+    with open(os.path.join(os.path.dirname(__file__), "golden", "compile_options.json")) as f:
+        good = bytes.fromhex(next(c for c in json.load(f) if c["name"] == "shard_map_8")["hex"])
+    for cut in range(1, len(good)):
+        rc, rep = _options_report(lib_path, good[:cut])
+        assert rc in (0, 1) and (rc == 0 or rep.startswith("error:"))
+    rc, rep = _options_report(lib_path, b"\x1a\xff\xff\xff\xff\x0f")     # field 3 claiming 4 GB
+    assert rc == 1 and "past the end" in rep, rep
+    rc, rep = _options_report(lib_path, b"\x1f")                          # wire type 7
+    assert rc == 1, rep
