@@ -280,12 +280,45 @@ static int64_t LayoutArena(const Plan& P, std::vector<int64_t>* off) {
   return total;
 }
 
+const std::vector<Executable::Piece>& Executable::Pieces() {
+  std::call_once(pieces_once_, [this] {
+    const std::vector<Step>& steps = plan_.steps;
+    auto launches = [](const Step& S) { return S.kind == StepKind::kFusion ? (int)S.launches.size() : 1; };
+    Piece cur;
+    auto close = [&](int at) {
+      if (at > cur.begin) {
+        cur.end = at;
+        pieces_.push_back(cur);
+      }
+      cur = Piece();
+      cur.begin = at;
+    };
+    for (int i = 0; i < (int)steps.size(); ++i) {
+      if (steps[i].kind == StepKind::kCollective) {
+        close(i);
+        Piece c;
+        c.begin = i;
+        c.end = i + 1;
+        c.coll = true;
+        pieces_.push_back(c);
+        cur.begin = i + 1;
+        continue;
+      }
+      if (!steps[i].wait_coll.empty()) close(i);     // the wait goes in front of a piece
+      cur.launches += launches(steps[i]);
+    }
+    close((int)steps.size());
+  });
+  return pieces_;
+}
+
 Executable::~Executable() {
   const Driver& d = Drv();
   for (auto& kv : per_dev_) {
     cudaSetDevice(kv.first);
     for (auto& g : kv.second.graphs)
-      if (g.exec) cudaGraphExecDestroy(g.exec);
+      for (cudaGraphExec_t x : g.execs)
+        if (x) cudaGraphExecDestroy(x);
     if (kv.second.arena) cudaFree(kv.second.arena);
     for (void* p : kv.second.consts) cudaFree(p);
     if (d.ok)
@@ -413,16 +446,21 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     for (auto& e : coll_done)
       if (e) { cudaEventDestroy(e); e = nullptr; }
   };
-  // CUDA graphs: a program without collectives whose arguments and outputs sit at the addresses
-  // of an earlier execution (intermediates are at fixed arena offsets) replays that execution's
-  // launches as one graph.  The first execution with a set of addresses runs eagerly (lazy set-up
-  // happens there), the second is captured, later ones launch the graph.
-  // (a program of a few launches gains nothing from a graph and pays its launch latency)
+  // CUDA graphs.  An execution is a sequence of pieces: runs of steps between collectives (cut
+  // again where a step waits for an earlier collective, that wait being done before the piece),
+  // and the collective steps themselves.  When the arguments and outputs sit at the addresses of an
+  // earlier execution (intermediates are at fixed arena offsets), each piece of two or more
+  // launches replays as one graph: the first execution with a set of addresses runs eagerly (lazy
+  // set-up happens there), the second captures, later ones launch the graphs.  Collectives always
+  // run eagerly on the communication stream, so every rank issues the same NCCL calls in the same
+  // way whether or not its pieces replay; a program without collectives is one piece.
+  const std::vector<Piece>& pieces = Pieces();
   size_t n_launch = 0;
   for (const Step& S : P.steps) n_launch += S.kind == StepKind::kFusion ? S.launches.size() : 1;
-  const bool graphs = !has_coll && n_launch >= 8 && !timer.on && !std::getenv("B200_NO_GRAPHS");
+  const bool graphs = n_launch >= 8 && !timer.on && !std::getenv("B200_NO_GRAPHS") &&
+                      !(has_coll && std::getenv("B200_NO_COLL_GRAPHS"));
   GraphEntry* ge = nullptr;
-  bool capture = false;
+  bool capturing = false;          // this execution captures its pieces' graphs
   if (graphs) {
     for (int s : P.out_slots) {
       err = slot(s);
@@ -433,46 +471,22 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     for (int s : P.out_slots) key.push_back(ptr[s]);
     for (auto& g : pd->graphs)
       if (g.key == key) ge = &g;
-    if (ge && ge->exec) {
-      if (cudaGraphLaunch(ge->exec, st) != cudaSuccess) return fail("graph launch failed");
-      g_graph_launches.fetch_add(1);
-      b200k::CountLaunches(ge->kernels);
-      ge->last = ++pd->graph_clock;
-      outs->clear();
-      for (int s : P.out_slots) outs->push_back(ptr[s]);
-      ExecTimerMarkEnd(dev.ordinal, st);
-      cudaError_t ce = cudaGetLastError();
-      return ce == cudaSuccess ? std::string() : std::string("CUDA error during execute: ") + cudaGetErrorString(ce);
-    }
     if (ge) {
-      if (!ge->no_graph) {
-        capture = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
-        if (!capture) cudaGetLastError();
-      }
+      capturing = !ge->captured && !ge->no_graph;
+      ge->last = ++pd->graph_clock;
     } else {
       if (pd->graphs.size() >= 4) {   // forget the least recently used address set
         auto old = std::min_element(pd->graphs.begin(), pd->graphs.end(),
                                     [](const GraphEntry& a, const GraphEntry& b) { return a.last < b.last; });
-        if (old->exec) cudaGraphExecDestroy(old->exec);
+        for (cudaGraphExec_t x : old->execs)
+          if (x) cudaGraphExecDestroy(x);
         pd->graphs.erase(old);
       }
-      pd->graphs.push_back(GraphEntry{key, nullptr, ++pd->graph_clock});
+      pd->graphs.push_back(GraphEntry{key});
+      pd->graphs.back().last = ++pd->graph_clock;
     }
   }
-  auto end_capture = [&]() {
-    if (!capture) return;
-    capture = false;
-    cudaGraph_t g = nullptr;
-    if (cudaStreamEndCapture(st, &g) == cudaSuccess && g) {
-      cudaGraphExec_t ex = nullptr;
-      if (cudaGraphInstantiate(&ex, g, 0) == cudaSuccess) {
-        ge->exec = ex;
-        g_graph_captures.fetch_add(1);
-      }
-      cudaGraphDestroy(g);
-    }
-    cudaGetLastError();
-  };
+  bool capture = false;            // a piece is being captured right now
   abort_capture = [&]() {
     if (!capture) return;
     capture = false;
@@ -482,12 +496,17 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     cudaGetLastError();
   };
   static const bool pdl = std::getenv("B200_NO_PDL") == nullptr;
-  auto run_steps = [&]() -> std::string {
-    for (size_t i = 0; i < P.steps.size(); ++i) {
+  auto wait_for_collectives = [&](const Step& S) {
+    for (int k : S.wait_coll)
+      if (coll_done[k]) cudaStreamWaitEvent(st, coll_done[k], 0);
+  };
+  // enqueues steps [begin, end); `waits`: also the waits for earlier collectives (a captured piece
+  // has them done before the capture starts)
+  auto run_steps = [&](int begin, int end, bool waits) -> std::string {
+    for (int i = begin; i < end; ++i) {
       const Step& S = P.steps[i];
       NvtxRange step_range(NvtxOn(), S.label);
-      for (int k : S.wait_coll)
-        if (coll_done[k]) cudaStreamWaitEvent(st, coll_done[k], 0);
+      if (waits) wait_for_collectives(S);
       switch (S.kind) {
         case StepKind::kFusion: {
           for (const Launch& L : S.launches) {
@@ -631,19 +650,52 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     }
     return std::string();
   };
-  const long long launches0 = b200k::g_kernel_launches.load();
-  err = run_steps();
-  if (!err.empty()) return err;
-  if (capture) ge->kernels = b200k::g_kernel_launches.load() - launches0;
-  if (capture) {
-    end_capture();
-    if (ge->exec) {
-      if (cudaGraphLaunch(ge->exec, st) != cudaSuccess) return fail("graph launch failed");
-    } else {
-      ge->no_graph = true;             // capture failed: this address set runs eagerly from now on
-      err = run_steps();
-      if (!err.empty()) return err;
+  for (size_t k = 0; k < pieces.size(); ++k) {
+    const Piece& pc = pieces[k];
+    const bool graphable = ge && !pc.coll && pc.launches >= 2;
+    if (graphable && ge->captured && k < ge->execs.size() && ge->execs[k]) {
+      wait_for_collectives(P.steps[pc.begin]);
+      if (cudaGraphLaunch(ge->execs[k], st) != cudaSuccess) return fail("graph launch failed");
+      b200k::CountLaunches(ge->kernels[k]);
+      continue;
     }
+    if (graphable && capturing) {
+      wait_for_collectives(P.steps[pc.begin]);
+      capture = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+      if (!capture) cudaGetLastError();
+      const long long launches0 = b200k::g_kernel_launches.load();
+      err = run_steps(pc.begin, pc.end, false);
+      if (!err.empty()) return err;
+      if (capture) {
+        capture = false;
+        cudaGraph_t g = nullptr;
+        cudaGraphExec_t ex = nullptr;
+        if (cudaStreamEndCapture(st, &g) == cudaSuccess && g && cudaGraphInstantiate(&ex, g, 0) == cudaSuccess) {
+          ge->execs.resize(pieces.size(), nullptr);
+          ge->kernels.resize(pieces.size(), 0);
+          ge->execs[k] = ex;
+          ge->kernels[k] = b200k::g_kernel_launches.load() - launches0;
+          g_graph_captures.fetch_add(1);
+        }
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        if (ex) {
+          if (cudaGraphLaunch(ex, st) != cudaSuccess) return fail("graph launch failed");
+          continue;
+        }
+        ge->no_graph = true;             // capture failed: this address set runs eagerly from now on
+        capturing = false;
+      }
+      err = run_steps(pc.begin, pc.end, false);     // the captured launches did not run: run them now
+      if (!err.empty()) return err;
+      continue;
+    }
+    err = run_steps(pc.begin, pc.end, true);
+    if (!err.empty()) return err;
+  }
+  if (ge) {
+    if (capturing) ge->captured = true;
+    else if (ge->captured) g_graph_launches.fetch_add(1);
   }
   abort_capture = nullptr;
   outs->clear();

@@ -43,12 +43,21 @@ class Executable {
   std::string Run(DeviceState& dev, const std::vector<const void*>& args, std::vector<void*>* outs, Comm* comm);
 
  private:
+  // A run of steps enqueued as a unit: steps [begin, end) between collectives (replayable as one
+  // CUDA graph), or one collective step (always eager).
+  struct Piece {
+    int begin = 0, end = 0;
+    bool coll = false;
+    int launches = 0;                        // kernel launches of the piece (graphs need >= 2)
+  };
+  const std::vector<Piece>& Pieces();
   struct GraphEntry {
     std::vector<void*> key;                  // argument then output addresses
-    cudaGraphExec_t exec = nullptr;          // null until the second execution with these addresses
-    uint64_t last = 0;
+    std::vector<cudaGraphExec_t> execs;      // per piece; null for pieces run eagerly
+    std::vector<long long> kernels;          // kernel launches each captured piece recorded
+    bool captured = false;                   // set by the second execution with these addresses
     bool no_graph = false;                   // capture failed once: run eagerly
-    long long kernels = 0;                   // kernel launches the captured execution recorded
+    uint64_t last = 0;
   };
   struct PerDevice {
     std::vector<void*> modules;              // CUmodule per NVRTC group
@@ -66,6 +75,8 @@ class Executable {
   std::string Load(DeviceState& dev, PerDevice** pd);
 
   Plan plan_;
+  std::vector<Piece> pieces_;
+  std::once_flag pieces_once_;
   std::string name_;
   std::vector<std::vector<char>> cubins_;
   std::mutex mu_;
