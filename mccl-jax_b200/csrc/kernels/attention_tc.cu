@@ -368,7 +368,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       l += lo_f(sum2) + hi_f(sum2);
       tc_fence_before();
       fence_async_smem();
-      mbar_arrive(&bars[kPFull + t]);
+      mbar_arrive(&bars[kPFull + 2 * t + (j & 1)]);
     }
     if (ok && mbar_wait_warp(&bars[kPVFull + 2 * t + ((n_kv - 1) & 1)], ((n_kv - 1) >> 1) & 1, kErrTimeoutAcc, err)) {
       tc_fence_after();
