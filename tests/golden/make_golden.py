@@ -2,7 +2,7 @@
 implementation.
 
 The reference ships no golden vectors for its compute ops (its 125-case jax-CPU oracle was never
-committed, /root/reference/docs/ops.md:7-10) and jax is not installed here, so the expected outputs
+committed, docs/ops.md:7-10 of the reference) and jax is not installed here, so the expected outputs
 come from PyTorch's CPU kernels, computed from the same seeded inputs the StableHLO programs take:
   attention  : torch.nn.functional.scaled_dot_product_attention in fp32 on the bf16 inputs
   MLP step   : torch autograd of the same 2-layer ReLU / softmax-CE model, one SGD step

@@ -255,8 +255,8 @@ def test_elementwise_and_reductions_vs_oracle(client):
 
 
 def test_tanh_f32_within_4_ulp(client):
-    # the generated kernels' tanh (series below |x| = 0.55, SFU exponential above) over every
-    # binade from 2^-30 to 2^6, signed zeros, infinities and NaN
+    # a tanh whose result is used as such (not only through 1 +- tanh) compiles to CUDA's tanhf:
+    # every binade from 2^-30 to 2^6, signed zeros, infinities and NaN, within 4 ulp of float64
     rng = np.random.default_rng(5)
     mag = np.exp2(rng.uniform(-30, 6, 1 << 20))
     x = (mag * rng.choice([-1.0, 1.0], mag.size)).astype(np.float32)
