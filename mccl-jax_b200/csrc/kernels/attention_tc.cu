@@ -10,19 +10,24 @@
 //   warps 4-7   softmax warpgroup for query tile 1
 //   warp 8      TMA loads: Q0, Q1 once; K_j and V_j through two-stage rings
 //   warp 9      allocates 512 TMEM columns; one thread issues every tcgen05.mma
-// TMEM: S_t (128 x 128 f32) at column 128 t, O_t (128 x D f32) at column 256 + D t.
+// TMEM: S_t (128 x 128 f32) at column 128 t, O_t (128 x D f32) at column 256 + D t, and P_t
+// (128 x 128 bf16, two per 32-bit column) at column 256 + 2 D + 64 t.
 // Per KV tile j and query tile t:
-//   S_t = Q_t K_j^T (tensor core)  ->  softmax warps load their S row once (one wait), release S_t,
-//   update the running max, write P_t = exp2(s - m) as bf16 into 128-byte-swizzled shared memory
-//   ->  O_t += P_t V_j (tensor core, accumulating in TMEM).
+//   S_t = Q_t K_j^T (tensor core)  ->  the softmax warps load their S row once, release S_t, take
+//   the row max (four independent chains), write P_t = exp2(s - m) as bf16 into tensor memory
+//   (tcgen05.st; the row sums in four independent packed accumulators)  ->  O_t += P_t V_j (tensor
+//   core, A operand read from tensor memory, accumulating in TMEM).
 // The running max used for P only moves when the true row max exceeds it by more than 2^8
 // (lazy rescaling): then the warp rescales its O row in TMEM (ld / scale / st) before the next
 // P V product; otherwise O is never touched by the CUDA cores until the final 1 / l.
-// The MMA thread issues S_t(j+1) as soon as warpgroup t has read S_t(j), before PV_t(j), so the
-// tensor core computes the next scores while the softmax runs.
+// Per KV tile the MMA thread issues both tiles' S_t(j+1) as soon as their softmax has read S_t(j),
+// then both P V(j) products: the tensor core computes the next scores while the softmax runs, and
+// neither softmax group waits behind the other's P.
 // V is read in place ([B*H, S, D], D contiguous) as the MN-major B operand of the P V product; the
-// VT variant (V pre-transposed to [B*H, D, S], K-major) is kept as a cross-check.
+// VT variant (V pre-transposed to [B*H, D, S], K-major) and P in shared memory (PT = false, two
+// buffers per tile, 128-byte swizzled, read through a descriptor) are kept as cross-checks.
 #include <cuda_bf16.h>
+#include <cstdlib>
 #include <mutex>
 
 #include "kernels.h"
@@ -51,6 +56,8 @@ struct ACfg {
   static constexpr int kBarOff = kPOff + 4 * kPBytes;  // two P buffers per query tile
   static constexpr int kSmem = kBarOff + 256 + 1024;   // 225.25 KB for D = 64 (limit 227 KB)
   static constexpr int kOCol = 256;
+  static constexpr int kPCol = kOCol + 2 * D;          // PT: P of tile t at columns kPCol + 64 t
+  static_assert(kPCol + 2 * (TK / 2) <= 512, "TMEM columns");
 };
 
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1) {
@@ -129,7 +136,9 @@ enum { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9,
        kNumBars = 21 };
 
 // 320 threads: the compiler caps registers at 168 per thread (one CTA per SM); 200 does not launch.
-template <int D, bool CAUSAL, bool VT>
+// PT: P goes to tensor memory (64 columns per query tile) and P V reads its A operand from there,
+// instead of P in shared memory (two buffers per tile) read through a descriptor.
+template <int D, bool CAUSAL, bool VT, bool PT>
 __global__ void __launch_bounds__(320, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, float* __restrict__ lse2, int H,
@@ -242,6 +251,17 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         }
         mma_commit(&bars[kPVFull + 2 * t + (j & 1)]);
       };
+      auto issue_pv_tmem = [&](int t, int j) {
+        const uint32_t va = v_addr + (j & 1) * C::kVBytes;
+#pragma unroll
+        for (int k = 0; k < TK / 16; ++k) {
+          const uint64_t bdesc = VT ? sw128_desc(va + (k / 4) * (D * 128) + (k % 4) * 32)
+                                    : sw128_mn_desc(va + k * 16 * 128);
+          // 16 keys of P = 8 columns (two bf16 per 32-bit column)
+          mma_f16_ts(tmem + C::kOCol + t * D, tmem + C::kPCol + t * (TK / 2) + k * 8, bdesc, id_pv, (j | k) != 0);
+        }
+        mma_commit(&bars[kPVFull + 2 * t + (j & 1)]);
+      };
       bool ok = mbar_wait(&bars[kQFull], 0, kErrTimeoutFull, err);
       if (ok) ok = mbar_wait(&bars[kKFull + 0], 0, kErrTimeoutFull, err);
       if (ok) {
@@ -271,7 +291,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         for (int t = 0; t < 2 && ok; ++t) {
           if (!mbar_wait(&bars[kPFull + 2 * t + (j & 1)], (j >> 1) & 1, kErrTimeoutFull, err)) { ok = false; break; }
           tc_fence_after();
-          issue_pv(t, j);
+          if (PT) issue_pv_tmem(t, j);
+          else issue_pv(t, j);
         }
         if (!ok) break;
         mma_commit(&bars[kVEmpty + st]);
@@ -304,15 +325,27 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         for (int e = 0; e < TK; ++e)
           if (key0 + e > qrow) sv[e] = 0xff800000u;
       }
-      // row max of the raw scores (scale > 0 commutes with max), three at a time
-      float mx = __uint_as_float(sv[0]);
+      // row max of the raw scores (scale > 0 commutes with max): four independent chains of
+      // three-way maxima, so consecutive instructions do not wait on each other
+      float mc[4];
 #pragma unroll
-      for (int e = 1; e + 1 < TK; e += 2) mx = fmax3(mx, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
-      mx = fmaxf(mx, __uint_as_float(sv[TK - 1]));
+      for (int i = 0; i < 4; ++i) mc[i] = fmaxf(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1]));
+#pragma unroll
+      for (int e = 8; e < TK; e += 8)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          mc[i] = fmax3(mc[i], __uint_as_float(sv[e + 2 * i]), __uint_as_float(sv[e + 2 * i + 1]));
+      float mx = fmax3(fmaxf(mc[0], mc[1]), mc[2], mc[3]);
       mx *= scale_log2;
-      // This iteration writes P buffer j & 1, last read by P V(j - 2): wait for that product.
+      // The shared-memory form writes P buffer j & 1, last read by P V(j - 2); the tensor-memory form
+      // has one P per tile, last read by P V(j - 1).  Wait for that product.
       uint8_t* const p_row = p_rows + (j & 1) * C::kPBytes;
-      if (j >= 2 && !mbar_wait_warp(&bars[kPVFull + 2 * t + (j & 1)], ((j >> 1) - 1) & 1, kErrTimeoutAcc, err)) {
+      if (!PT && j >= 2 && !mbar_wait_warp(&bars[kPVFull + 2 * t + (j & 1)], ((j >> 1) - 1) & 1, kErrTimeoutAcc, err)) {
+        ok = false;
+        break;
+      }
+      if (PT && j >= 1 &&
+          !mbar_wait_warp(&bars[kPVFull + 2 * t + ((j - 1) & 1)], ((j - 1) >> 1) & 1, kErrTimeoutAcc, err)) {
         ok = false;
         break;
       }
@@ -347,27 +380,36 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       const float mu = m_use == -INFINITY ? 0.f : m_use;   // a row masked so far contributes p = 0
       // p = 2^(s * scale_log2 - m): one packed FMA per two scores, packed adds for the row sum
       const uint64_t sc2 = pack2(scale_log2, scale_log2), nm2 = pack2(-mu, -mu);
-      uint64_t sum2 = pack2(0.f, 0.f);
+      uint64_t sum2[4] = {pack2(0.f, 0.f), pack2(0.f, 0.f), pack2(0.f, 0.f), pack2(0.f, 0.f)};   // independent sums
+      const uint32_t p_col = tmem + C::kPCol + t * (TK / 2) + lane_off;
 #pragma unroll
-      for (int c = 0; c < TK; c += 16) {
-        uint32_t pk[8];
+      for (int c = 0; c < TK; c += 32) {
+        uint32_t pk[16];                     // keys c .. c+31, two bf16 per word
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
+        for (int e = 0; e < 16; ++e) {
           const uint64_t x2 = ffma2(pack2u(sv[c + 2 * e], sv[c + 2 * e + 1]), sc2, nm2);
           const float p0 = ex2(lo_f(x2)), p1 = ex2(hi_f(x2));
-          sum2 = fadd2(sum2, pack2(p0, p1));
+          sum2[e & 3] = fadd2(sum2[e & 3], pack2(p0, p1));
           pk[e] = pack_bf16(p0, p1);
         }
-        // keys c .. c+15 = two 16-byte chunks of row r in the 64-key block c / 64 (128-byte swizzle)
-        const int blk = c >> 6;
-        const int ch0 = (c & 63) >> 3;
-        uint8_t* rowp = p_row + blk * (TQ * 128);
-        *(uint4*)(rowp + ((ch0 ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *(uint4*)(rowp + (((ch0 + 1) ^ (r & 7)) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        if (PT) {
+          tmem_st16(p_col + c / 2, pk);      // 32 keys = 16 columns of this row's lane
+        } else {
+          // keys c .. c+31 = four 16-byte chunks of row r in the 64-key block c / 64 (128-byte swizzle)
+          const int blk = c >> 6;
+          const int ch0 = (c & 63) >> 3;
+          uint8_t* rowp = p_row + blk * (TQ * 128);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *(uint4*)(rowp + (((ch0 + q) ^ (r & 7)) << 4)) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        }
       }
-      l += lo_f(sum2) + hi_f(sum2);
+      const uint64_t s01 = fadd2(sum2[0], sum2[1]), s23 = fadd2(sum2[2], sum2[3]);
+      const uint64_t stot = fadd2(s01, s23);
+      l += lo_f(stot) + hi_f(stot);
+      if (PT) tmem_wait_st();
       tc_fence_before();
-      fence_async_smem();
+      if (!PT) fence_async_smem();
       mbar_arrive(&bars[kPFull + 2 * t + (j & 1)]);
     }
     if (ok && mbar_wait_warp(&bars[kPVFull + 2 * t + ((n_kv - 1) & 1)], ((n_kv - 1) >> 1) & 1, kErrTimeoutAcc, err)) {
@@ -439,15 +481,15 @@ static bool Map2D(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t ou
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int D, bool CAUSAL, bool VT>
-static int LaunchAttn(const void* q, const void* k, const void* v, void* o, int B, int H, int S, float scale, cudaStream_t st,
-                      float* lse2 = nullptr) {
+template <int D, bool CAUSAL, bool VT, bool PT>
+static int LaunchAttnP(const void* q, const void* k, const void* v, void* o, int B, int H, int S, float scale, cudaStream_t st,
+                       float* lse2) {
   using Cf = ACfg<D>;
   static std::once_flag once[8];
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 7], [] {
-    cudaFuncSetAttribute(attn_fwd_kernel<D, CAUSAL, VT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmem);
+    cudaFuncSetAttribute(attn_fwd_kernel<D, CAUSAL, VT, PT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmem);
   });
   CUtensorMap mq, mk, mv;
   const uint64_t rows = (uint64_t)B * H * S;
@@ -459,9 +501,19 @@ static int LaunchAttn(const void* q, const void* k, const void* v, void* o, int 
   }
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid((unsigned)(B * H * (S / (2 * TQ))));
-  attn_fwd_kernel<D, CAUSAL, VT><<<grid, 320, Cf::kSmem, st>>>(mq, mk, mv, (__nv_bfloat16*)o, lse2, H, S, scale_log2);
+  attn_fwd_kernel<D, CAUSAL, VT, PT><<<grid, 320, Cf::kSmem, st>>>(mq, mk, mv, (__nv_bfloat16*)o, lse2, H, S, scale_log2);
   CountLaunches();
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+// P in tensor memory by default (measured 645 against 624 TFLOP/s at [4,16,4096,64]);
+// B200_ATTN_P_SMEM=1 selects the shared-memory form as a cross-check.
+template <int D, bool CAUSAL, bool VT>
+static int LaunchAttn(const void* q, const void* k, const void* v, void* o, int B, int H, int S, float scale, cudaStream_t st,
+                      float* lse2 = nullptr) {
+  static const bool p_smem = std::getenv("B200_ATTN_P_SMEM") != nullptr && std::atoi(std::getenv("B200_ATTN_P_SMEM")) != 0;
+  if (p_smem) return LaunchAttnP<D, CAUSAL, VT, false>(q, k, v, o, B, H, S, scale, st, lse2);
+  return LaunchAttnP<D, CAUSAL, VT, true>(q, k, v, o, B, H, S, scale, st, lse2);
 }
 
 // B * H * S query rows must fit an int (grid and row arithmetic); the product is formed with
