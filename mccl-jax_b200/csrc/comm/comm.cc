@@ -57,7 +57,8 @@ bool Unhex(const std::string& s, void* p, size_t n) {
 
 }  // namespace
 
-std::unique_ptr<Comm> Comm::Create(int world, int rank, int device, const KvStore& kv, int timeout_ms, std::string* err) {
+std::unique_ptr<Comm> Comm::Create(int world, int rank, int device, const KvStore& kv, int timeout_ms, std::string* err,
+                                   int max_ctas) {
   if (!kv.put || !kv.get) {
     *err = "no key-value store to exchange the NCCL id (pass kv_put / kv_get callbacks to PJRT_Client_Create)";
     return nullptr;
@@ -78,6 +79,7 @@ std::unique_ptr<Comm> Comm::Create(int world, int rank, int device, const KvStor
   cudaSetDevice(device);
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
   cfg.blocking = 0;
+  if (max_ctas > 0) cfg.maxCTAs = max_ctas;
   ncclComm_t comm = nullptr;
   ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &cfg);
   auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);

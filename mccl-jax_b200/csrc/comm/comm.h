@@ -27,8 +27,11 @@ class Comm {
  public:
   // Creates the communicator of `world` ranks; every rank must call it.  `timeout_ms` bounds the
   // wait for the other ranks.  On failure returns null and sets *err.
+  // `max_ctas` > 0 caps the CTAs (SMs) an NCCL collective may occupy: gradients all-reduced while
+  // the backward pass runs need little bandwidth, and every SM a collective holds is one the
+  // persistent one-CTA-per-SM kernels running beside it cannot use.
   static std::unique_ptr<Comm> Create(int world, int rank, int device, const KvStore& kv, int timeout_ms,
-                                      std::string* err);
+                                      std::string* err, int max_ctas = 0);
   ~Comm();
 
   int rank() const { return rank_; }

@@ -567,9 +567,10 @@ b200::KvStore StoreFrom(const PJRT_Client_Create_Args* a) {
 
 PJRT_Error* CreateClient(PJRT_Client_Create_Args* a) {
   // recognised int64 options; anything else is ignored, as jax passes options for other backends
-  int64_t rank = 0, world = 1, ordinal = -1;
+  int64_t rank = 0, world = 1, ordinal = -1, nccl_max_ctas = 0;
   struct Known { const char* name; int64_t* slot; } known[] = {{"node_id", &rank}, {"num_nodes", &world},
-                                                                {"device_ordinal", &ordinal}};
+                                                                {"device_ordinal", &ordinal},
+                                                                {"nccl_max_ctas", &nccl_max_ctas}};
   for (size_t i = 0; i < a->num_options; ++i) {
     const PJRT_NamedValue& nv = a->create_options[i];
     if (nv.type != PJRT_NamedValue_kInt64) continue;
@@ -599,7 +600,7 @@ PJRT_Error* CreateClient(PJRT_Client_Create_Args* a) {
   if (world > 1) {
     std::string err;
     c->comm = b200::Comm::Create((int)world, (int)rank, (int)ordinal, StoreFrom(a), EnvInt("B200_COMM_TIMEOUT_MS", 120000),
-                                 &err);
+                                 &err, (int)nccl_max_ctas);
     if (!c->comm)
       return Fail(err.find("timed out") != std::string::npos ? PJRT_Error_Code_DEADLINE_EXCEEDED : PJRT_Error_Code_INTERNAL,
                   "NCCL communicator init failed: " + err);

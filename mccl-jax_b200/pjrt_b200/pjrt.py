@@ -317,11 +317,13 @@ class Client:
 
     def __init__(self, api: Optional[Api] = None, node_id: int = 0, num_nodes: int = 1,
                  device_ordinal: Optional[int] = None, kv_put: Optional[Callable[[str, bytes], None]] = None,
-                 kv_get: Optional[Callable[[str, int], bytes]] = None):
+                 kv_get: Optional[Callable[[str, int], bytes]] = None, nccl_max_ctas: int = 0):
         self.api = api or Api()
         opts = [("node_id", node_id), ("num_nodes", num_nodes)]
         if device_ordinal is not None:
             opts.append(("device_ordinal", device_ordinal))
+        if nccl_max_ctas:
+            opts.append(("nccl_max_ctas", nccl_max_ctas))
         arr = (NamedValue * len(opts))()
         self._names = []
         for i, (k, v) in enumerate(opts):

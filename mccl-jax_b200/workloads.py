@@ -111,7 +111,7 @@ class Clocks:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_client(world, rank, local):
+def make_client(world, rank, local, nccl_max_ctas=0, port_offset=17):
     """A PJRT client for this rank; with world > 1 the NCCL unique id travels through a TCP store
     (the kv_put / kv_get callbacks of PJRT_Client_Create)."""
     from pjrt_b200 import pjrt
@@ -119,7 +119,7 @@ def make_client(world, rank, local):
     if world == 1:
         return pjrt.Client(api, device_ordinal=local), None
     import torch.distributed as dist
-    port = int(os.environ.get("MASTER_PORT", "29500")) + 17
+    port = int(os.environ.get("MASTER_PORT", "29500")) + port_offset
     store = dist.TCPStore(os.environ.get("MASTER_ADDR", "127.0.0.1"), port, world, rank == 0,
                           timeout=datetime.timedelta(seconds=120))
 
@@ -129,7 +129,8 @@ def make_client(world, rank, local):
     def get(k, ms):
         store.wait([k], datetime.timedelta(milliseconds=max(ms, 1)))
         return store.get(k)
-    return pjrt.Client(api, node_id=rank, num_nodes=world, device_ordinal=local, kv_put=put, kv_get=get), store
+    return pjrt.Client(api, node_id=rank, num_nodes=world, device_ordinal=local, kv_put=put, kv_get=get,
+                       nccl_max_ctas=nccl_max_ctas), store
 
 
 def max_over_ranks(x, world):
@@ -168,7 +169,7 @@ def run_dp(a, world, rank, local):
     batch = 8
     t0 = time.time()
     prog = configs.gpt2_program(batch=batch, world=world, rank=rank, **cfg)
-    client, store = make_client(world, rank, local)
+    client, store = make_client(world, rank, local, nccl_max_ctas=getattr(a, "nccl_max_ctas", 0))
     exe = client.compile(prog.text)
     compile_s = time.time() - t0
     n = prog.meta["n_tensors"]
@@ -597,7 +598,7 @@ def run_psum(a, world, rank, local):
     import torch
     from pjrt_b200 import configs
     L = lib()
-    client, store = make_client(world, rank, local)
+    client, store = make_client(world, rank, local, port_offset=23)
     rows = []
     for kb in (4, 16, 64, 256, 1024, 4096, 16384, 65536, 262144, 1048576):
         n = kb * 1024 // 4
