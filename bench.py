@@ -56,7 +56,8 @@ def config_of(dp, world):
             "model": "gpt2-small (random init N(0,0.02))", "layers": c["layers"], "d_model": c["d"], "heads": c["heads"],
             "mlp": c["mlp"], "vocab": c["vocab"], "seq_len": c["seq"], "per_gpu_batch": dp["batch"],
             "global_batch": dp["batch"] * world, "parallelism": f"dp{world}", "params": dp["n_params"],
-            "l2": "working set (249 MB params + 1 GB moments + activations) far larger than L2"}
+            "l2": "working set (249 MB params + 1 GB moments + activations) far larger than L2",
+            "donation": "params and AdamW moments donated, updated in place" if dp.get("donate") else "none"}
 
 
 def reference_arm(a, world, rank):
@@ -95,6 +96,7 @@ def main():
     ap.add_argument("--layers", type=int, default=12, help="decoder layers of the DP step")
     ap.add_argument("--nccl-max-ctas", type=int, default=0,
                     help="DP step: cap on the SMs one NCCL collective occupies (client option nccl_max_ctas; 0 = NCCL's choice)")
+    ap.add_argument("--donate", action="store_true", help="DP step: params and moments donated (updated in place)")
     ap.add_argument("--no-sub", action="store_true", help="headline only (no sub-benchmarks, no CPU baseline)")
     ap.add_argument("--no-sweep", action="store_true", help="attention: no sequence-length sweep")
     ap.add_argument("--only", default="", help="gemm / fused / attn_bwd: one case by name")

@@ -880,7 +880,11 @@ class Decoder {
     if (func_body) {
       // the caller left "func.func @f(" open: finish the signature
       std::string sig;
-      for (size_t k = 0; k < args.size(); ++k) sig += (k ? ", " : "") + args[k] + ": " + arg_types[k];
+      for (size_t k = 0; k < args.size(); ++k) {
+        sig += (k ? ", " : "") + args[k] + ": " + arg_types[k];
+        if (k < func_arg_attrs_.size() && !func_arg_attrs_[k].empty()) sig += " " + func_arg_attrs_[k];
+      }
+      func_arg_attrs_.clear();
       out_ += sig + func_sig_tail_ + " {\n";
     } else {
       out_ += "{\n";
@@ -895,6 +899,7 @@ class Decoder {
     PopRegion(nv);
   }
   std::string func_sig_tail_;
+  std::vector<std::string> func_arg_attrs_;   // per argument of the func.func being written: "{...}" or ""
 
   const AttrV* Find(const Props& p, const char* name) {
     for (auto& kv : p)
@@ -949,6 +954,15 @@ class Decoder {
       func_sig_tail_ = ") -> (";
       for (size_t k = 0; k < ft.results.size(); ++k) func_sig_tail_ += (k ? ", " : "") + Type(ft.results[k]).text;
       func_sig_tail_ += ")";
+      func_arg_attrs_.clear();
+      if (const AttrV* aa = Find(all, "arg_attrs")) {
+        if (aa->kind != AttrV::kArray) Bad("func.func arg_attrs is not an array");
+        for (size_t e : aa->elems) {
+          const AttrV& d = Attr(e);
+          if (d.kind != AttrV::kDict) Bad("func.func arg_attrs entry is not a dictionary");
+          func_arg_attrs_.push_back(d.dict.empty() ? std::string() : d.text);
+        }
+      }
       if (op.num_regions != 1) Bad("external func.func declarations are not supported");
       ReadRegions(c, op, ind, true);
       out_ += "\n";

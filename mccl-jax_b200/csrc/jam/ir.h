@@ -83,6 +83,10 @@ struct Graph {
   std::vector<std::unique_ptr<Op>> ops;      // program order
   std::vector<Value*> args;
   std::vector<Value*> outputs;
+  // per @main argument: the result its buffer may become (`tf.aliasing_output`, -1: none), and
+  // whether the caller may give up its buffer at all (an alias, or `jax.buffer_donor`)
+  std::vector<int> arg_alias_output;
+  std::vector<bool> arg_donor;
 
   Value* NewValue(const TensorType& t) {
     values.emplace_back(new Value());

@@ -219,6 +219,7 @@ struct Gen {
   std::vector<std::string> identity;      // loop index names of the current group shape
   std::vector<int64_t> group_dims;
   bool conflict = false;
+  std::set<int> nonident;                 // slots some load reads away from the element being computed
   std::ostringstream body;
   int tmp = 0;
   std::string indent = "    ";
@@ -473,6 +474,8 @@ struct Gen {
                                 : !pitch && ty.dims == shift_dims && idx.size() == shift_prefix.size() + 1 && li.base == vinner + "_0" &&
                                       std::equal(shift_prefix.begin(), shift_prefix.end(), idx.begin()));
       const bool wide16 = slot_f32 && slot_f32->count(slot) && (ty.dt == DT::kBF16 || ty.dt == DT::kF16);
+      if (ty.dims != group_dims || (idx != identity && std::find(lane_identity.begin(), lane_identity.end(), idx) == lane_identity.end()))
+        nonident.insert(slot);
       if (lane >= 0 && (ty.dt == DT::kF32 || ty.dt == DT::kBF16 || ty.dt == DT::kF16) && aligned4) {
         cur_dims = ty.dims;
         cur_pitch = pitch;
@@ -930,20 +933,28 @@ struct Gen {
   }
 };
 
-std::string KernelParams(const std::vector<int>& ins, int n_out, bool scratch) {
+// `shared_in` / `shared_out`: parameters that may point at the same memory (an output written in
+// place of a donated input) and so are declared without __restrict__.
+std::string KernelParams(const std::vector<int>& ins, int n_out, bool scratch, const std::set<int>& shared_in = {},
+                         const std::set<int>& shared_out = {}) {
   std::string s;
-  for (size_t k = 0; k < ins.size(); ++k) s += (k ? ", " : "") + std::string("const void* __restrict__ p") + std::to_string(k);
-  for (int k = 0; k < n_out; ++k) s += (s.empty() ? "" : ", ") + std::string("void* __restrict__ q") + std::to_string(k);
+  for (size_t k = 0; k < ins.size(); ++k)
+    s += (k ? ", " : "") + std::string(shared_in.count((int)k) ? "const void* p" : "const void* __restrict__ p") + std::to_string(k);
+  for (int k = 0; k < n_out; ++k)
+    s += (s.empty() ? "" : ", ") + std::string(shared_out.count(k) ? "void* q" : "void* __restrict__ q") + std::to_string(k);
   if (scratch) s += (s.empty() ? "" : ", ") + std::string("void* __restrict__ scratch");
   return s;
 }
 
-std::string ParamCasts(const std::vector<int>& ins, const std::vector<DT>& in_dts, const std::vector<DT>& out_dts) {
+std::string ParamCasts(const std::vector<int>& ins, const std::vector<DT>& in_dts, const std::vector<DT>& out_dts,
+                       const std::set<int>& shared_in = {}, const std::set<int>& shared_out = {}) {
   std::ostringstream o;
   for (size_t k = 0; k < ins.size(); ++k)
-    o << "  const " << MemType(in_dts[k]) << "* __restrict__ in" << k << " = (const " << MemType(in_dts[k]) << "*)p" << k << ";\n";
+    o << "  const " << MemType(in_dts[k]) << (shared_in.count((int)k) ? "* in" : "* __restrict__ in") << k << " = (const "
+      << MemType(in_dts[k]) << "*)p" << k << ";\n";
   for (size_t k = 0; k < out_dts.size(); ++k)
-    o << "  " << MemType(out_dts[k]) << "* __restrict__ out" << k << " = (" << MemType(out_dts[k]) << "*)q" << k << ";\n";
+    o << "  " << MemType(out_dts[k]) << (shared_out.count((int)k) ? "* out" : "* __restrict__ out") << k << " = ("
+      << MemType(out_dts[k]) << "*)q" << k << ";\n";
   return o.str();
 }
 
@@ -1026,12 +1037,14 @@ class Lowerer {
     }
     DecideStoredTypes();
     BindLeaves();
+    FindAliases();
     EmitSteps();
     BindOutputs();
     MergeTinyLoops();
     GroupSmallCollectives();
     MarkAsyncCollectives();
     ComputeLastUse();
+    DecideInPlace();
     EndKernel();
     p_->cuda_prelude = kPrelude;
     p_->cuda_source = kPrelude;
@@ -1795,6 +1808,68 @@ class Lowerer {
     }
   }
 
+  // ---------------------------------------------------------------- buffer donation
+  // `tf.aliasing_output = k` on argument i (jax.jit's donate_argnums) lets result k live in argument
+  // i's buffer.  alias_arg_slot_ maps the value result k is computed as to argument i's slot, so the
+  // loop kernel that writes it can be generated for running in place.
+  std::unordered_map<int, int> alias_arg_slot_;
+  void FindAliases() {
+    const size_t n = g_.args.size();
+    if (g_.arg_alias_output.size() != n) return;
+    std::set<int> seen;
+    for (size_t i = 0; i < n; ++i) {
+      const int k = g_.arg_alias_output[i];
+      if (k < 0) continue;
+      if (k >= (int)g_.outputs.size())
+        throw LowerError{"argument " + std::to_string(i) + ": tf.aliasing_output = " + std::to_string(k) + ", but @main has " +
+                         std::to_string(g_.outputs.size()) + " results"};
+      if (!seen.insert(k).second) throw LowerError{"result " + std::to_string(k) + " is the tf.aliasing_output of two arguments"};
+      const TensorType& at = p_->arg_types[i];
+      const TensorType& rt = g_.outputs[k]->type;
+      if (at.dt != rt.dt || at.dims != rt.dims)
+        throw LowerError{"argument " + std::to_string(i) + " (" + at.str() + ") cannot alias result " + std::to_string(k) +
+                         " (" + rt.str() + ")"};
+      const Value* v = Resolve(g_.outputs[k]);
+      if (v->arg_index < 0) alias_arg_slot_[v->id] = p_->arg_slots[i];
+    }
+  }
+  // Which aliased results can be written in place: the one step that writes the result's slot is the
+  // output copy of the argument itself, or a loop kernel that reads the argument only at the element
+  // it writes, and no later step reads the argument.  Other aliased results get fresh buffers (the
+  // donated argument's buffer is then released after the execution).
+  void DecideInPlace() {
+    const size_t n = p_->arg_slots.size();
+    p_->arg_alias.assign(n, -1);
+    p_->arg_donor.assign(n, false);
+    p_->out_inplace_arg.assign(p_->out_slots.size(), -1);
+    if (g_.arg_alias_output.size() != n) return;
+    for (size_t i = 0; i < n; ++i) {
+      p_->arg_alias[i] = g_.arg_alias_output[i];
+      p_->arg_donor[i] = g_.arg_donor[i];
+      const int k = g_.arg_alias_output[i];
+      if (k < 0) continue;
+      const int sa = p_->arg_slots[i], so = p_->out_slots[k];
+      int writer = -1, writers = 0;
+      for (int j = 0; j < (int)p_->steps.size(); ++j) {
+        std::set<int> r, w;
+        StepRW(p_->steps[j], &r, &w);
+        if (w.count(so)) writer = j, ++writers;
+      }
+      if (writers != 1) continue;
+      const Step& st = p_->steps[writer];
+      bool ok = false;
+      if (st.kind == StepKind::kCopy) {
+        ok = st.copy.src == sa;                // the result is the argument itself
+      } else if (st.kind == StepKind::kFusion && st.launches.size() == 1 && p_->slots[sa].last_use <= writer) {
+        const Launch& L = st.launches[0];
+        const bool pair = std::find(L.inplace.begin(), L.inplace.end(), std::make_pair(sa, so)) != L.inplace.end();
+        // in a merged launch the argument must be read by the writing kernel alone
+        ok = pair && std::count(L.in_slots.begin(), L.in_slots.end(), sa) <= 1;
+      }
+      if (ok) p_->out_inplace_arg[k] = (int)i;
+    }
+  }
+
   std::unordered_map<int, int64_t> slot_pitch_;   // slot -> padded row pitch (elements)
   int SlotFor(const Value* v) {
     v = Resolve(v);
@@ -2069,17 +2144,34 @@ class Lowerer {
     if (gen.conflict) throw LowerError{"internal: fusion conflict"};
     std::vector<DT> in_dts;
     for (int s : gen.in_slots) in_dts.push_back(SlotDt(s));
+    // results that a donated argument's buffer may hold (tf.aliasing_output): written in place when
+    // this kernel reads the argument only at the element it writes
+    std::vector<std::pair<int, int>> inplace;
+    std::set<int> shared_in, shared_out;
+    for (size_t k = 0; k < roots.size(); ++k) {
+      auto al = alias_arg_slot_.find(roots[k]->id);
+      if (al == alias_arg_slot_.end()) continue;
+      const int sa = al->second;
+      if (p_->slots[sa].bytes != p_->slots[out_slots[k]].bytes || slot_pitch_.count(out_slots[k])) continue;
+      auto pi = gen.param_of.find(sa);
+      if (pi != gen.param_of.end()) {
+        if (gen.nonident.count(sa)) continue;
+        shared_in.insert(pi->second);
+      }
+      shared_out.insert((int)k);
+      inplace.push_back({sa, out_slots[k]});
+    }
     std::string fn = KName();
     // The per-element body is an inlined device function; the grid-stride loop calls it for four
     // independent elements per iteration so each thread keeps four loads in flight (one 4-byte load
     // per thread cannot cover HBM latency: Little's law caps that near 1.5 TB/s on 148 SMs).
     std::string args_decl, args_use;
     for (size_t k = 0; k < gen.in_slots.size(); ++k) {
-      args_decl += ", const " + MemType(in_dts[k]) + "* __restrict__ in" + std::to_string(k);
+      args_decl += ", const " + MemType(in_dts[k]) + (shared_in.count((int)k) ? "* in" : "* __restrict__ in") + std::to_string(k);
       args_use += ", in" + std::to_string(k);
     }
     for (size_t k = 0; k < out_dts.size(); ++k) {
-      args_decl += ", " + MemType(out_dts[k]) + "* __restrict__ out" + std::to_string(k);
+      args_decl += ", " + MemType(out_dts[k]) + (shared_out.count((int)k) ? "* out" : "* __restrict__ out") + std::to_string(k);
       args_use += ", out" + std::to_string(k);
     }
     // In vector mode the element function's argument is the vector index t (elements 4t .. 4t+3).
@@ -2105,8 +2197,8 @@ class Lowerer {
     }
     src_ << "}\n";
     src_ << "extern \"C\" __global__ void __launch_bounds__(256, 4) " << fn << "("
-         << KernelParams(gen.in_slots, (int)out_slots.size(), false) << ") {\n"
-         << ParamCasts(gen.in_slots, in_dts, out_dts)
+         << KernelParams(gen.in_slots, (int)out_slots.size(), false, shared_in, shared_out) << ") {\n"
+         << ParamCasts(gen.in_slots, in_dts, out_dts, shared_in, shared_out)
          << "  const long long st = (long long)gridDim.x * 256;\n"
          << "  long long i = (long long)blockIdx.x * 256 + threadIdx.x;\n"
          << "  for (; i + 3 * st < " << trip << "LL; i += 4 * st) {\n"
@@ -2125,6 +2217,7 @@ class Lowerer {
     L.block = 256;
     L.grid_x = std::max<int64_t>(1, (trip + 255) / 256);
     L.grid_stride = true;
+    L.inplace = inplace;
     Step st;
     st.kind = StepKind::kFusion;
     st.launches.push_back(L);
@@ -3720,18 +3813,24 @@ class Lowerer {
       }
       unit << src.substr(0, at) << kern;
       std::vector<std::string> args;
+      auto shared = [&](int slot, bool in) {
+        for (auto& pr : L.inplace)
+          if ((in ? pr.first : pr.second) == slot) return true;
+        return false;
+      };
       for (size_t k = 0; k < L.in_slots.size(); ++k) {
         const std::string a = "h" + std::to_string(q) + "p" + std::to_string(k);
-        in_args.push_back("const void* __restrict__ " + a);
+        in_args.push_back((shared(L.in_slots[k], true) ? "const void* " : "const void* __restrict__ ") + a);
         args.push_back(a);
         M.in_slots.push_back(L.in_slots[k]);
       }
       for (size_t k = 0; k < L.out_slots.size(); ++k) {
         const std::string a = "h" + std::to_string(q) + "q" + std::to_string(k);
-        out_args.push_back("void* __restrict__ " + a);
+        out_args.push_back((shared(L.out_slots[k], false) ? "void* " : "void* __restrict__ ") + a);
         args.push_back(a);
         M.out_slots.push_back(L.out_slots[k]);
       }
+      M.inplace.insert(M.inplace.end(), L.inplace.begin(), L.inplace.end());
       body << "  " << (q ? "else " : "") << "if (b < " << base + L.grid_x << "u) " << L.fn << "(";
       for (auto& a : args) body << a << ", ";
       body << "b - " << base << "u, " << L.grid_x << "u);\n";
@@ -3922,6 +4021,14 @@ std::string Plan::dump() const {
     o << "  [" << i << "] " << steps[i].label;
     for (size_t k = 0; k < steps[i].launches.size(); ++k) o << (k ? ", " : "  {") << steps[i].launches[k].fn;
     o << (steps[i].launches.empty() ? "" : "}") << "\n";
+  }
+  for (size_t i = 0; i < arg_alias.size(); ++i) {
+    if (arg_alias[i] < 0 && !arg_donor[i]) continue;
+    o << "  donated argument " << i;
+    if (arg_alias[i] >= 0)
+      o << " -> result " << arg_alias[i]
+        << (out_inplace_arg[arg_alias[i]] == (int)i ? " (written in place)" : " (fresh buffer; argument released)");
+    o << "\n";
   }
   return o.str();
 }

@@ -185,6 +185,7 @@ struct OpAst {
 struct FuncAst {
   std::string name;
   std::vector<std::pair<std::string, TensorType>> args;
+  std::vector<std::map<std::string, std::string>> arg_attrs;   // per argument (empty if none)
   std::vector<TensorType> results;
   std::vector<OpAst> ops;
 };
@@ -365,7 +366,7 @@ class Parser {
       std::string a = Next();
       Expect(":");
       TensorType ty = Type(Next());
-      if (Peek() == "{") AttrDict();
+      f.arg_attrs.push_back(Peek() == "{" ? AttrDict() : std::map<std::string, std::string>());
       f.args.push_back({a, ty});
     }
     if (Accept("->")) {
@@ -923,6 +924,21 @@ class Builder {
       v->arg_index = (int)k;
       g_->args.push_back(v);
       env[it->second.args[k].first] = v;
+      // buffer donation as jax marks it (jit's donate_argnums): `tf.aliasing_output = k` when the
+      // argument's buffer may become result k, `jax.buffer_donor` when it may be reused freely
+      const auto& at = it->second.arg_attrs[k];
+      int alias = -1;
+      auto al = at.find("tf.aliasing_output");
+      if (al != at.end()) {
+        char* end = nullptr;
+        const long x = std::strtol(al->second.c_str(), &end, 10);
+        if (end == al->second.c_str() || *end || x < 0 || x > INT32_MAX)
+          throw ParseError{"argument " + std::to_string(k) + ": bad tf.aliasing_output " + al->second};
+        alias = (int)x;
+      }
+      auto dn = at.find("jax.buffer_donor");
+      g_->arg_alias_output.push_back(alias);
+      g_->arg_donor.push_back(alias >= 0 || (dn != at.end() && dn->second == "true"));
     }
     g_->outputs = Walk(it->second, env, 0);
   }

@@ -34,6 +34,10 @@ struct Launch {
   int block = 256;
   int smem = 0;
   bool grid_stride = false;    // any grid size is correct: launched with at most one wave of CTAs
+  // (input slot, output slot) pairs this kernel may run with the output in the input's memory: the
+  // input is read only at the element the same thread then writes (or not at all), and the kernel
+  // declares those two pointers without __restrict__
+  std::vector<std::pair<int, int>> inplace;
 };
 
 struct GemmStep {
@@ -123,6 +127,12 @@ struct Plan {
   std::vector<TensorType> arg_types; // after shard_map retyping
   std::vector<int> out_slots;        // per @main result
   std::vector<TensorType> out_types;
+  // buffer donation: per argument, the result its buffer may become (-1: none) and whether the
+  // caller gives the buffer up at all; per result, the argument whose memory it is written into when
+  // that argument is donated (-1: a fresh buffer)
+  std::vector<int> arg_alias;
+  std::vector<bool> arg_donor;
+  std::vector<int> out_inplace_arg;
   int num_partitions = 1;
   std::string dump() const;
 };

@@ -320,6 +320,7 @@ Executable::~Executable() {
       for (cudaGraphExec_t x : g.execs)
         if (x) cudaGraphExecDestroy(x);
     if (kv.second.arena) cudaFree(kv.second.arena);
+    if (kv.second.gemm_counters) cudaFree(kv.second.gemm_counters);
     for (void* p : kv.second.consts) cudaFree(p);
     if (d.ok)
       for (void* m : kv.second.modules) d.unload((CUmodule)m);
@@ -362,6 +363,18 @@ std::string Executable::Load(DeviceState& dev, PerDevice** pd) {
     cudaGetLastError();
     return "device allocation of the " + std::to_string(arena_bytes) + "-byte intermediate arena failed";
   }
+  // one work-unit counter per GEMM step, zeroed at the start of every execution
+  p.gemm_slot.assign(plan_.steps.size(), -1);
+  int n_gemm = 0;
+  for (size_t i = 0; i < plan_.steps.size(); ++i)
+    if (plan_.steps[i].kind == StepKind::kGemm) p.gemm_slot[i] = n_gemm++;
+  if (n_gemm > 0 && !std::getenv("B200_GEMM_STATIC_UNITS")) {
+    if (cudaMalloc(&p.gemm_counters, (size_t)n_gemm * sizeof(int)) != cudaSuccess) {
+      cudaGetLastError();
+      return "device allocation of the GEMM work-unit counters failed";
+    }
+    p.n_gemm = n_gemm;
+  }
   for (const ConstBlob& c : plan_.consts) {
     void* ptr = nullptr;
     if (cudaMalloc(&ptr, c.bytes.empty() ? 16 : c.bytes.size()) != cudaSuccess) return "constant upload: out of memory";
@@ -391,7 +404,8 @@ struct NvtxRange {
 };
 }  // namespace
 
-std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& args, std::vector<void*>* outs, Comm* comm) {
+std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& args, std::vector<void*>* outs, Comm* comm,
+                            const std::vector<bool>* donated, std::vector<bool>* taken) {
   NvtxRange run_range(NvtxOn(), "execute " + name_);
   cudaSetDevice(dev.ordinal);
   PerDevice* pd = nullptr;
@@ -406,6 +420,15 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     if (P.slots[s].const_index >= 0) ptr[s] = pd->consts[P.slots[s].const_index];
     else if (pd->arena_off[s] >= 0) ptr[s] = (char*)pd->arena + pd->arena_off[s];
   }
+  // results written in place of donated arguments
+  if (taken) taken->assign(args.size(), false);
+  if (donated && donated->size() == args.size())
+    for (size_t k = 0; k < P.out_inplace_arg.size(); ++k) {
+      const int i = P.out_inplace_arg[k];
+      if (i < 0 || !(*donated)[i] || !args[i]) continue;
+      ptr[P.out_slots[k]] = const_cast<void*>(args[i]);
+      if (taken) (*taken)[i] = true;
+    }
   cudaStream_t st = dev.stream;
   auto slot = [&](int s) -> std::string {
     if (s < 0 || ptr[s]) return "";
@@ -432,6 +455,8 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     }
   }
   ExecTimerMarkStart(dev.ordinal, st);
+  if (pd->gemm_counters && cudaMemsetAsync(pd->gemm_counters, 0, (size_t)pd->n_gemm * sizeof(int), st) != cudaSuccess)
+    return fail("zeroing the GEMM work-unit counters failed");
   static StepTimer timer;
   const auto host_t0 = std::chrono::steady_clock::now();
   std::vector<cudaEvent_t> evs;
@@ -553,12 +578,13 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
           const GemmStep& g = S.gemm;
           for (int s : {g.a, g.b, g.c, g.ws, g.split_ws}) { err = slot(s); if (!err.empty()) return fail(err); }
           const long long lda = g.lda ? g.lda : (g.a_mn ? g.M : g.K), ldb = g.ldb ? g.ldb : (g.b_mn ? g.N : g.K);
+          int* counter = pd->gemm_counters ? pd->gemm_counters + pd->gemm_slot[i] : nullptr;
           int rc = g.split
               ? b200k::GemmSplit(ptr[g.a], lda, g.a_mn, PjrtType(g.a_dt), ptr[g.b], ldb, g.b_mn, PjrtType(g.b_dt), ptr[g.c],
                                  g.batch, g.M, g.N, g.K, PjrtType(g.out), st, g.split_ws >= 0 ? ptr[g.split_ws] : nullptr,
-                                 (size_t)g.split_ws_bytes, g.ldc)
+                                 (size_t)g.split_ws_bytes, g.ldc, counter)
               : b200k::Gemm(ptr[g.a], lda, g.a_mn, ptr[g.b], ldb, g.b_mn, ptr[g.c], g.batch, g.M, g.N, g.K, PjrtType(g.ab),
-                            PjrtType(g.out), st, g.ws >= 0 ? (float*)ptr[g.ws] : nullptr, g.ldc);
+                            PjrtType(g.out), st, g.ws >= 0 ? (float*)ptr[g.ws] : nullptr, g.ldc, counter);
           if (rc != 0) return fail("gemm launch failed (" + std::to_string(rc) + ") for " + S.label);
           break;
         }
@@ -642,7 +668,9 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
         }
         case StepKind::kCopy: {
           for (int q : {S.copy.src, S.copy.dst}) { err = slot(q); if (!err.empty()) return fail(err); }
-          cudaMemcpyAsync(ptr[S.copy.dst], ptr[S.copy.src], (size_t)S.copy.bytes, cudaMemcpyDeviceToDevice, st);
+          // a result that is a donated argument itself is already in place
+          if (ptr[S.copy.dst] != ptr[S.copy.src])
+            cudaMemcpyAsync(ptr[S.copy.dst], ptr[S.copy.src], (size_t)S.copy.bytes, cudaMemcpyDeviceToDevice, st);
           break;
         }
       }

@@ -40,7 +40,11 @@ class Executable {
   // Enqueues one execution on `dev`.  `args` are device pointers of the argument buffers (sizes were
   // checked against plan().arg_types by the caller); on success `outs` receives newly allocated
   // device buffers (stream-ordered on dev.stream) that the caller owns.
-  std::string Run(DeviceState& dev, const std::vector<const void*>& args, std::vector<void*>* outs, Comm* comm);
+  // `donated` (per argument, may be null): the caller gives up these argument buffers.  A result the
+  // plan writes in place of a donated argument is written into that argument's memory; `taken`
+  // reports which donated buffers became results this way (the caller releases the others).
+  std::string Run(DeviceState& dev, const std::vector<const void*>& args, std::vector<void*>* outs, Comm* comm,
+                  const std::vector<bool>* donated = nullptr, std::vector<bool>* taken = nullptr);
 
  private:
   // A run of steps enqueued as a unit: steps [begin, end) between collectives (replayable as one
@@ -70,6 +74,9 @@ class Executable {
     void* arena = nullptr;
     std::vector<int64_t> arena_off;          // per slot, -1 when not in the arena
     std::vector<GraphEntry> graphs;          // captured executions by argument / output addresses
+    int* gemm_counters = nullptr;            // per GEMM step: its launch's work-unit counter
+    int n_gemm = 0;
+    std::vector<int> gemm_slot;              // step index -> its counter (-1: not a GEMM)
     uint64_t graph_clock = 0;
   };
   std::string Load(DeviceState& dev, PerDevice** pd);

@@ -31,6 +31,7 @@ static __device__ int g_tc_error_gemm;
 namespace {
 
 constexpr int BM = 128, BK = 64;
+constexpr int kUnitRing = 4;   // work units published ahead by the TMA warp
 
 template <int BN>
 struct Cfg {
@@ -89,7 +90,7 @@ __global__ void __launch_bounds__(192, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, void* __restrict__ C, int M, int N, int K, int batch, int fmt,
                int splits, float* __restrict__ ws, int tma_store, long long ldc, int terms, uint32_t piece_a,
-               uint32_t piece_b) {
+               uint32_t piece_b, int* __restrict__ unit_counter) {
   using CF = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -97,7 +98,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint64_t* empty = full + CF::kStages;
   uint64_t* acc_full = empty + CF::kStages;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
+  uint64_t* unit_full = acc_empty + 2;         // ring of the work units this CTA processes
+  uint64_t* unit_empty = unit_full + kUnitRing;
+  int* unit_ring = (int*)(unit_empty + kUnitRing);
+  uint32_t* tmem_slot = (uint32_t*)(unit_ring + kUnitRing);
   float* stage_base = (float*)(smem + CF::kStages * CF::kStage + 1024);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -122,6 +126,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 128);
     }
+    for (int q = 0; q < kUnitRing; ++q) {
+      mbar_init(&unit_full[q], 1);
+      mbar_init(&unit_empty[q], 1 + 4);       // the MMA thread and the four epilogue warps
+    }
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, CF::kTmemCols);
@@ -139,7 +147,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t issued = 0;  // bit s: stage s has a fill in flight of parity (ph_of_fill[s])
       uint32_t fill_par = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      // Work units come from the launch's counter when there is one: a CTA that starts late (its
+      // SM held by another kernel, e.g. a collective) finds the units taken and leaves at once
+      // instead of holding the launch back; the next unit is claimed while this one's loads are
+      // issued, so the atomic's latency stays off the critical path.  Without a counter a CTA takes
+      // every gridDim.x-th unit.  Each unit index, and finally one past the end, is published to
+      // the MMA and epilogue warps through the ring.
+      int next = unit_counter ? atomicAdd(unit_counter, 1) : (int)blockIdx.x;
+      for (int iu = 0;; ++iu) {
+        const int u = ok ? next : num_units;
+        const int rq = iu % kUnitRing;
+        if (!mbar_wait(&unit_empty[rq], ((iu / kUnitRing) & 1) ^ 1, kErrTimeoutEmpty, &g_tc_error_gemm)) break;
+        *(volatile int*)&unit_ring[rq] = u;
+        mbar_arrive(&unit_full[rq]);
+        if (u >= num_units) break;
+        next = unit_counter ? atomicAdd(unit_counter, 1) : u + (int)gridDim.x;
         const int t = u / splits, sp = u % splits;
         const int b = t / per_batch, r = t % per_batch;
         int m_blk, n_blk;
@@ -179,9 +201,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const uint32_t idesc = idesc_f16(fmt, BM, BN, BMN, AMN);
       int s = 0;
       uint32_t ph = 0;
-      int local = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
+      for (int local = 0; ok; ++local) {
+        const int rq = local % kUnitRing;
+        if (!mbar_wait(&unit_full[rq], (local / kUnitRing) & 1, kErrTimeoutFull, &g_tc_error_gemm)) break;
+        const int u = *(volatile int*)&unit_ring[rq];
+        mbar_arrive(&unit_empty[rq]);
+        if (u >= num_units) break;
         const int a = local & 1;
         const uint32_t aph = (local >> 1) & 1;
         if (!mbar_wait(&acc_empty[a], aph ^ 1, kErrTimeoutAccEmpty, &g_tc_error_gemm)) break;
@@ -207,8 +233,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
-    int local = 0;
-    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
+    for (int local = 0;; ++local) {
+      const int rq = local % kUnitRing;
+      if (!mbar_wait_warp(&unit_full[rq], (local / kUnitRing) & 1, kErrTimeoutAcc, &g_tc_error_gemm)) break;
+      const int u = *(volatile int*)&unit_ring[rq];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&unit_empty[rq]);
+      if (u >= num_units) break;
       const int t = u / splits;
       const int a = local & 1;
       const uint32_t aph = (local >> 1) & 1;
@@ -496,7 +527,7 @@ struct Terms {
 
 template <int BN, int OUT, bool AMN, bool BMN>
 static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, void* C, int batch, int M, int N, int K,
-                    int fmt, cudaStream_t st, int splits, float* ws, long long ldc, const Terms& tm) {
+                    int fmt, cudaStream_t st, int splits, float* ws, long long ldc, const Terms& tm, int* counter) {
   using CF = Cfg<BN>;
   static std::once_flag once[8];
   int dev = 0;
@@ -523,7 +554,7 @@ static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, 
   int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
   int grid = std::min(tiles * splits, NumSMs());
   gemm_tc_kernel<BN, OUT, AMN, BMN><<<grid, 192, CF::kSmem, st>>>(ta, tb, tc, C, M, N, K, batch, fmt, splits, ws, tma_store, ldc,
-                                                                   tm.n, tm.a, tm.b);
+                                                                   tm.n, tm.a, tm.b, counter);
   CountLaunches();
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
@@ -531,11 +562,11 @@ static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, 
 template <int BN, int OUT>
 static int LaunchTcMajor(bool amn, bool bmn, const void* A, long long lda, const void* B, long long ldb, void* C, int batch,
                          int M, int N, int K, int fmt, cudaStream_t st, int splits, float* ws, long long ldc,
-                         const Terms& tm) {
-  if (amn && bmn) return LaunchTc<BN, OUT, true, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm);
-  if (amn) return LaunchTc<BN, OUT, true, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm);
-  if (bmn) return LaunchTc<BN, OUT, false, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm);
-  return LaunchTc<BN, OUT, false, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm);
+                         const Terms& tm, int* counter) {
+  if (amn && bmn) return LaunchTc<BN, OUT, true, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm, counter);
+  if (amn) return LaunchTc<BN, OUT, true, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm, counter);
+  if (bmn) return LaunchTc<BN, OUT, false, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm, counter);
+  return LaunchTc<BN, OUT, false, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm, counter);
 }
 
 __global__ void __launch_bounds__(256) ws_to_16bit_kernel(const float* __restrict__ ws, uint16_t* __restrict__ c, long long n,
@@ -619,7 +650,7 @@ int GemmSplitK(int64_t batch, int64_t M, int64_t N, int64_t K, int sms) {
 // blocks every output tile walks), plus the split-K zeroing and rounding passes.
 static int RunTc(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C, int64_t batch,
                  int64_t M, int64_t N, int64_t K, int64_t k_eff, int fmt, int out, cudaStream_t st, float* ws, int64_t ldc,
-                 const Terms& tm) {
+                 const Terms& tm, int* counter) {
   int b = (int)batch, m = (int)M, n = (int)N, k = (int)K;
   int bn = 256, splits = 1;
   GemmTile(batch, M, N, k_eff, NumSMs(), &bn, &splits);
@@ -629,9 +660,11 @@ static int RunTc(const void* A, long long lda, bool a_mn, const void* B, long lo
   if (splits > 1 && cudaMemsetAsync(acc, 0, (size_t)batch * M * N * 4, st) != cudaSuccess) return -3;
   auto launch = [&](auto out_c) {
     constexpr int O = decltype(out_c)::value;
-    if (bn == 256) return LaunchTcMajor<256, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm);
-    if (bn == 192) return LaunchTcMajor<192, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm);
-    return LaunchTcMajor<128, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm);
+    if (bn == 256) return LaunchTcMajor<256, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm,
+                                                  counter);
+    if (bn == 192) return LaunchTcMajor<192, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm,
+                                                  counter);
+    return LaunchTcMajor<128, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm, counter);
   };
   int rc = out == 0 ? launch(std::integral_constant<int, 0>{})
          : out == 1 ? launch(std::integral_constant<int, 1>{})
@@ -655,7 +688,7 @@ static int OutCode(int out_type) {
 // may be computed split-K (partials added into ws, then rounded into C); an f32 result splits without
 // it (partials added into C).
 int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C, int64_t batch, int64_t M,
-         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st, float* ws, int64_t ldc) {
+         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st, float* ws, int64_t ldc, int* counter) {
   if (batch <= 0 || M <= 0 || N <= 0) return 0;
   if (ldc <= 0) ldc = N;
   if (ldc < N) return -1;
@@ -670,7 +703,8 @@ int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, 
   bool tc_ok = (ab_type == B200_DT_BF16 || ab_type == B200_DT_F16) && (lda % 8) == 0 && (ldb % 8) == 0 &&
                ((uintptr_t)A % 16) == 0 && ((uintptr_t)B % 16) == 0 && !getenv("B200_GEMM_SIMT");
   if (tc_ok)
-    return RunTc(A, lda, a_mn, B, ldb, b_mn, C, batch, M, N, K, K, ab_type == B200_DT_BF16 ? 1 : 0, out, st, ws, ldc, Terms{});
+    return RunTc(A, lda, a_mn, B, ldb, b_mn, C, batch, M, N, K, K, ab_type == B200_DT_BF16 ? 1 : 0, out, st, ws, ldc, Terms{},
+                 counter);
   int b = (int)batch, m = (int)M, n = (int)N, k = (int)K;
   if (ldc != N) return -1;                     // padded C rows are written by the tensor-core path only
   if (ab_type == B200_DT_F32) return LaunchSimt<float>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, out, st);
@@ -681,7 +715,7 @@ int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, 
 
 int Gemm(const void* A, long long lda, const void* B, long long ldb, void* C, int64_t batch, int64_t M, int64_t N,
          int64_t K, int ab_type, int out_type, cudaStream_t st) {
-  return Gemm(A, lda, false, B, ldb, false, C, batch, M, N, K, ab_type, out_type, st, nullptr, 0);
+  return Gemm(A, lda, false, B, ldb, false, C, batch, M, N, K, ab_type, out_type, st, nullptr, 0, nullptr);
 }
 
 // ---------------------------------------------------------------------------- f32-accurate products
@@ -811,7 +845,7 @@ size_t GemmSplitScratchBytes(int64_t batch, int64_t M, int64_t N, int64_t K, int
 
 int GemmSplit(const void* A, long long lda, bool a_mn, int a_type, const void* B, long long ldb, bool b_mn, int b_type,
               void* C, int64_t batch, int64_t M, int64_t N, int64_t K, int out_type, cudaStream_t st, void* scratch,
-              size_t scratch_bytes, int64_t ldc) {
+              size_t scratch_bytes, int64_t ldc, int* counter) {
   if (batch <= 0 || M <= 0 || N <= 0) return 0;
   if (ldc <= 0) ldc = N;
   const int out = OutCode(out_type);
@@ -860,7 +894,7 @@ int GemmSplit(const void* A, long long lda, bool a_mn, int a_type, const void* B
   // 16-bit results are not split along K here (no f32 workspace): the terms already give every
   // output tile a long K walk
   return RunTc(a_op, a_ld, a_opmn, b_op, b_ld, b_opmn, C, batch, M, N, K, (int64_t)tm.n * Kp, /*bf16*/ 1, out, st,
-               out == 0 ? (float*)C : nullptr, ldc, tm);
+               out == 0 ? (float*)C : nullptr, ldc, tm, counter);
 }
 
 }  // namespace b200k

@@ -22,9 +22,11 @@ int NumSMs();
 // C[b] = A[b] . B[b]^T.  A is [batch, M, >=K] (K-major, row pitch lda) or, with a_mn, [batch, K, >=M]
 // (MN-major, pitch lda); B likewise with N, ldb and b_mn.  ab_type: PJRT type code of both operands
 // (bf16 / f16 on the tensor cores, f32 on the SIMT kernel).  With `ws` (batch*M*N f32) a 16-bit result
-// may be computed split-K; ldc is C's row pitch (0 = N).
+// may be computed split-K; ldc is C's row pitch (0 = N).  `counter` (device int, zero before the
+// launch, used by this one launch only; may be null): the CTAs draw their work units from it instead
+// of taking every gridDim.x-th, so CTAs that start late take fewer.
 int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* C, int64_t batch, int64_t M,
-         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st, float* ws, int64_t ldc);
+         int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st, float* ws, int64_t ldc, int* counter = nullptr);
 int Gemm(const void* A, long long lda, const void* B, long long ldb, void* C, int64_t batch, int64_t M, int64_t N,
          int64_t K, int ab_type, int out_type, cudaStream_t st);
 void GemmTile(int64_t batch, int64_t M, int64_t N, int64_t K, int sms, int* bn_out, int* splits_out);
@@ -43,7 +45,7 @@ size_t GemmSplitScratchBytes(int64_t batch, int64_t M, int64_t N, int64_t K, int
                              long long lda, long long ldb);
 int GemmSplit(const void* A, long long lda, bool a_mn, int a_type, const void* B, long long ldb, bool b_mn, int b_type,
               void* C, int64_t batch, int64_t M, int64_t N, int64_t K, int out_type, cudaStream_t st, void* scratch,
-              size_t scratch_bytes, int64_t ldc);
+              size_t scratch_bytes, int64_t ldc, int* counter = nullptr);
 
 // ---- attention (attention_tc.cu, attention_bwd_tc.cu) -------------------------------------------
 bool AttentionShapeOk(int B, int H, int S, int D);

@@ -689,6 +689,15 @@ PJRT_Error* Execute(PJRT_LoadedExecutable_Execute_Args* a) {
     return BadArg("Execute: expected " + std::to_string(plan.arg_types.size()) + " arguments, got " +
                   std::to_string(a->num_args));
   if (a->num_devices < 1) return BadArg("Execute: no devices");
+  // donation: an argument the program marks donatable (tf.aliasing_output / jax.buffer_donor) is
+  // given up unless the options list it as non-donatable
+  std::vector<bool> donatable(a->num_args, false);
+  for (size_t i = 0; i < a->num_args && i < plan.arg_donor.size(); ++i) donatable[i] = plan.arg_donor[i];
+  if (a->options && a->options->non_donatable_input_indices)
+    for (size_t j = 0; j < a->options->num_non_donatable_input_indices; ++j) {
+      const int64_t i = a->options->non_donatable_input_indices[j];
+      if (i >= 0 && (size_t)i < donatable.size()) donatable[i] = false;
+    }
   for (size_t k = 0; k < a->num_devices; ++k) {
     PJRT_Device* dev = a->execute_device ? a->execute_device : le->devices[k % le->devices.size()];
     if (!dev->local()) return BadArg("Execute: device is not addressable");
@@ -706,11 +715,24 @@ PJRT_Error* Execute(PJRT_LoadedExecutable_Execute_Args* a) {
       if (b->device() != dev) b->ready->Wait();   // written on another device's stream
       args[i] = b->ptr;
     }
+    std::vector<bool> donated(a->num_args, false);
+    for (size_t i = 0; i < a->num_args; ++i) {
+      if (!donatable[i]) continue;
+      PJRT_Buffer* b = a->argument_lists[k][i];
+      if (b->pins > 0)
+        return BadArg("Execute: argument " + std::to_string(i) + " is donated but has external references");
+      for (size_t j = 0; j < a->num_args; ++j)
+        if (j != i && a->argument_lists[k][j] == b)
+          return BadArg("Execute: argument " + std::to_string(i) + " is donated and also passed as argument " +
+                        std::to_string(j));
+      donated[i] = b->device() == dev;           // a buffer on another device is copied, not given up
+    }
     std::vector<void*> outs;
+    std::vector<bool> taken;
     {
       std::lock_guard<std::mutex> g(dev->launch_mu);
       cudaSetDevice(dev->ordinal);
-      std::string err = le->program->Run(dev->cuda, args, &outs, le->client->comm.get());
+      std::string err = le->program->Run(dev->cuda, args, &outs, le->client->comm.get(), &donated, &taken);
       if (!err.empty())
         return Fail(err.find("timed out") != std::string::npos ? PJRT_Error_Code_DEADLINE_EXCEEDED : PJRT_Error_Code_INTERNAL,
                     err);
@@ -727,6 +749,18 @@ PJRT_Error* Execute(PJRT_LoadedExecutable_Execute_Args* a) {
     for (size_t i = 0; i < outs.size(); ++i) {
       const b200::TensorType& t = plan.out_types[i];
       a->output_lists[k][i] = NewBuffer(le->client, dev->hbm(), PjrtTypeOf(t.dt), t.dims, (size_t)t.bytes(), outs[i], done);
+    }
+    // donated arguments are deleted: their memory is now a result's, or goes back to the pool once
+    // the execution is done with it (stream-ordered)
+    for (size_t i = 0; i < a->num_args; ++i) {
+      if (!donated[i]) continue;
+      PJRT_Buffer* b = a->argument_lists[k][i];
+      if (i < taken.size() && taken[i]) {
+        b->ptr = nullptr;
+        b->life = PJRT_Buffer::Life::kFreed;
+      } else {
+        Release(b);
+      }
     }
     if (a->device_complete_events) a->device_complete_events[k] = new PJRT_Event{done};
   }

@@ -146,7 +146,8 @@ def gpt2_param_shapes(layers, d, heads, mlp, vocab, seq):
 
 
 def gpt2_program(layers=12, d=768, heads=12, mlp=3072, vocab=50257, seq=1024, batch=8, world=1,
-                 lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1, seed=0, rank=0, with_inputs=True, dtype="bf16"):
+                 lr=3e-4, b1=0.9, b2=0.95, eps=1e-8, wd=0.1, seed=0, rank=0, with_inputs=True, dtype="bf16",
+                 donate=False):
     """One data-parallel AdamW step of a GPT-2-style decoder (pre-LN, GELU(tanh) MLP, tied LM head).
 
     Params bf16 (replicated), AdamW moments f32; the batch [world*batch, seq] of token ids is sharded
@@ -155,6 +156,8 @@ def gpt2_program(layers=12, d=768, heads=12, mlp=3072, vocab=50257, seq=1024, ba
     scalars (dp_train.py:74-76).  Returns (new params..., new m..., new v..., pmean loss).
     `dtype` is the parameter / activation type (bf16, the config's; "f32" gives the same program
     without the 16-bit roundings, which tests compare with an independent autograd implementation).
+    `donate`: params and moments are donated, each aliased to its updated value (what
+    jax.jit(step, donate_argnums=(params, opt_state)) emits), so the update runs in place.
     """
     b = Builder("jit_gpt2_dp_step", num_partitions=world)
     shapes = gpt2_param_shapes(layers, d, heads, mlp, vocab, seq)
@@ -240,7 +243,8 @@ def gpt2_program(layers=12, d=768, heads=12, mlp=3072, vocab=50257, seq=1024, ba
         outs_m.append(m1)
         outs_v.append(v1)
     lo = b.all_reduce(loss, world) * inv_world if world > 1 else loss
-    text = b.text(outs_p + outs_m + outs_v + [lo])
+    n_state = 3 * len(shapes)
+    text = b.text(outs_p + outs_m + outs_v + [lo], aliases={k: k for k in range(n_state)} if donate else None)
     inputs = []
     if with_inputs:
         inputs = gpt2_inputs(shapes, batch, seq, vocab, seed=seed, rank=rank, dtype=dtype)

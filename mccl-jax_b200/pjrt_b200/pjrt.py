@@ -280,7 +280,10 @@ class Executable:
         self.name = C.string_at(n.name, n.name_size).decode()
         api.call("Executable_Destroy", LoadedArgs(executable=g.executable))
 
-    def execute(self, args: Sequence[Buffer], wait: bool = True) -> List[Buffer]:
+    def execute(self, args: Sequence[Buffer], wait: bool = True, non_donatable: Sequence[int] = ()) -> List[Buffer]:
+        """LoadedExecutable_Execute on one device.  Arguments the program marks donated
+        (tf.aliasing_output / jax.buffer_donor) are given up -- deleted after the call, their memory
+        reused by the aliased result where the plan allows -- unless listed in `non_donatable`."""
         api = self.client.api
         arg_arr = (P * max(1, len(args)))(*[b.h for b in args])
         arg_lists = (C.POINTER(P) * 1)(C.cast(arg_arr, C.POINTER(P)))
@@ -289,6 +292,10 @@ class Executable:
         evs = (P * 1)()
         opts = ExecuteOptions()
         opts.struct_size = C.sizeof(opts)
+        nd = (C.c_int64 * max(1, len(non_donatable)))(*non_donatable)
+        if non_donatable:
+            opts.non_donatable_input_indices = C.cast(nd, P)
+            opts.num_non_donatable_input_indices = len(non_donatable)
         api.call("LoadedExecutable_Execute", ExecuteArgs(executable=self.h, options=C.pointer(opts), argument_lists=arg_lists,
                                                           num_devices=1, num_args=len(args), output_lists=out_lists,
                                                           device_complete_events=evs))

@@ -448,7 +448,12 @@ class Builder:
         shape = np.broadcast_shapes(a.shape, c.shape)
         return self.broadcast_to(a, shape), self.broadcast_to(c, shape)
 
-    def text(self, outputs: Sequence[T]) -> str:
+    def text(self, outputs: Sequence[T], aliases=None, donors=()) -> str:
+        """The module text.  `aliases` {argument index: result index} marks donated arguments whose
+        buffer may become that result (`tf.aliasing_output`, what jax.jit(donate_argnums=...) emits
+        when a result matches the argument's type); `donors` marks donated arguments without one
+        (`jax.buffer_donor`)."""
+        aliases = dict(aliases or {})
         outs = list(outputs)
         live = set()
         stack = list(outs)
@@ -458,7 +463,11 @@ class Builder:
                 continue
             live.add(id(t))
             stack.extend(t.inputs)
-        sig = ", ".join(f"{a.name}: {a.type}" for a in self.args)
+        def arg_attr(k):
+            if k in aliases:
+                return f" {{tf.aliasing_output = {aliases[k]} : i32}}"
+            return " {jax.buffer_donor = true}" if k in donors else ""
+        sig = ", ".join(f"{a.name}: {a.type}{arg_attr(k)}" for k, a in enumerate(self.args))
         res = ", ".join(f"{o.type}" for o in outs)
         attrs = f"mhlo.num_partitions = {self.num_partitions} : i32, mhlo.num_replicas = {self.num_replicas} : i32"
         body = [f"    {self.lines[id(t)]}".replace("\n", "\n    ") for t in self.ops if id(t) in live and id(t) in self.lines]

@@ -168,7 +168,9 @@ def run_dp(a, world, rank, local):
     cfg = dict(configs.GPT2_SMALL, layers=a.layers)
     batch = 8
     t0 = time.time()
-    prog = configs.gpt2_program(batch=batch, world=world, rank=rank, **cfg)
+    # params and moments donated (jax.jit(step, donate_argnums=...)): AdamW updates them in place
+    donate = bool(getattr(a, "donate", False))
+    prog = configs.gpt2_program(batch=batch, world=world, rank=rank, donate=donate, **cfg)
     client, store = make_client(world, rank, local, nccl_max_ctas=getattr(a, "nccl_max_ctas", 0))
     exe = client.compile(prog.text)
     compile_s = time.time() - t0
@@ -248,6 +250,7 @@ def run_dp(a, world, rank, local):
     per_gpu_tflops = fl_tok * tps / world / 1e12
     return {
         "ms": ms, "tokens_per_s": tps, "tokens_per_step": tokens, "compile_s": compile_s, "graph_replays": replays,
+        "donate": donate,
         "launches": launches, "loss_first": losses[0] if losses else None, "loss_last": last_loss, "clocks": clocks,
         "flops_per_token": fl_tok, "n_params": prog.meta["n_params"], "cfg": cfg, "batch": batch,
         "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
@@ -391,23 +394,28 @@ def run_gemm(a, local, only=""):
     flush = torch.empty(64 * 1024 * 1024, device="cuda")
     pk, src = peaks()
     rows = []
-    shapes = [(1, 1024, "bf16"), (1, 4096, "bf16"), (1, 8192, "bf16"), (16, 2048, "bf16"), (1, 1024, "f32"),
-              (1, 4096, "f32"), (1, 8192, "f32")]
-    for batch, n, dt in shapes:
-        name = f"b{batch}-{n}-{dt}"
+    # (name, batch, M, N, K, operand type, result type): config 3's square sweep, then the GPT-2
+    # train step's forward products (tokens x d_model -> qkv / proj / fc1 / fc2, bf16 results)
+    shapes = [(f"b{b}-{n}-{dt}", b, n, n, n, dt, "f32") for b, n, dt in
+              [(1, 1024, "bf16"), (1, 4096, "bf16"), (1, 8192, "bf16"), (16, 2048, "bf16"), (1, 1024, "f32"),
+               (1, 4096, "f32"), (1, 8192, "f32")]]
+    shapes += [("gpt2-qkv", 1, 8192, 2304, 768, "bf16", "bf16"), ("gpt2-proj", 1, 8192, 768, 768, "bf16", "bf16"),
+               ("gpt2-fc1", 1, 8192, 3072, 768, "bf16", "bf16"), ("gpt2-fc2", 1, 8192, 768, 3072, "bf16", "bf16")]
+    for name, batch, m, n, k, dt, odt in shapes:
         if only and only != name:
             continue
         tdt = torch.bfloat16 if dt == "bf16" else torch.float32
-        A = (torch.randn(batch, n, n, device="cuda") / math.sqrt(n)).to(tdt)
-        B = (torch.randn(batch, n, n, device="cuda") / math.sqrt(n)).to(tdt)
-        C = torch.empty(batch, n, n, device="cuda")
+        A = (torch.randn(batch, m, k, device="cuda") / math.sqrt(k)).to(tdt)
+        B = (torch.randn(batch, n, k, device="cuda") / math.sqrt(k)).to(tdt)
+        C = torch.empty(batch, m, n, device="cuda", dtype=torch.bfloat16 if odt == "bf16" else torch.float32)
+        oc = 13 if odt == "bf16" else 11
         if dt == "bf16":
-            f = lambda: L.b200_gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), batch, n, n, n, 13, 11, sp)
-            path = "b200_gemm (tcgen05, bf16 x bf16 -> f32)"
+            f = lambda: L.b200_gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), batch, m, n, k, 13, oc, sp)
+            path = f"b200_gemm (tcgen05, bf16 x bf16 -> {odt})"
         else:
-            nb = L.b200_gemm_split_scratch_bytes(batch, n, n, n, 11, 11)
+            nb = L.b200_gemm_split_scratch_bytes(batch, m, n, k, 11, 11)
             scratch = torch.empty(nb, dtype=torch.uint8, device="cuda")
-            f = lambda: L.b200_gemm_split(A.data_ptr(), 11, B.data_ptr(), 11, C.data_ptr(), batch, n, n, n, 11,
+            f = lambda: L.b200_gemm_split(A.data_ptr(), 11, B.data_ptr(), 11, C.data_ptr(), batch, m, n, k, oc,
                                           scratch.data_ptr(), nb, sp)
             path = "b200_gemm_split (f32 operands as 3 bf16 pieces, 6 tcgen05 products, f32 accumulation)"
         for _ in range(a.warmup):
@@ -422,7 +430,7 @@ def run_gemm(a, local, only=""):
             e1.synchronize()
             ts.append(e0.elapsed_time(e1))
         ms = sorted(ts)[len(ts) // 2]
-        tf = 2.0 * batch * n ** 3 / (ms * 1e-3) / 1e12
+        tf = 2.0 * batch * m * n * k / (ms * 1e-3) / 1e12
         rows.append({"shape": name, "path": path, "ms": round(ms, 4), "tflops": round(tf, 1),
                      "frac_of_bf16_peak": round(tf / pk["bf16_tflops"], 3)})
         del A, B, C
@@ -434,7 +442,7 @@ def run_gemm(a, local, only=""):
     return {"value": head["tflops"], "unit": "TFLOP/s", "shape": head["shape"],
             "roofline": {"bound": "tensor", "achieved": head["tflops"], "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": head["frac_of_bf16_peak"], "peak_source": f"{src} dense bf16 (burst)"},
-            "config": {"workload": "dot_general sweep, A[M,K] B[N,K] ~ N(0,1)/sqrt(K), f32 result",
+            "config": {"workload": "dot_general sweep, A[M,K] B[N,K] ~ N(0,1)/sqrt(K), f32 result (gpt2-*: bf16)",
                        "l2": "flushed before every timed call", "timing": "median of CUDA-event spans"},
             "sweep": rows}
 

@@ -73,6 +73,15 @@ def argmax_text():
     return b.text([v, i])
 
 
+def donated_text():
+    """An optimizer-style update with donated arguments: two results aliased to their arguments
+    (tf.aliasing_output) and one argument donated without an alias (jax.buffer_donor)."""
+    b = Builder("jit_donated_update")
+    p, g, m = b.arg((64, 64), "f32"), b.arg((64, 64), "f32"), b.arg((64, 64), "f32")
+    m1 = m * 0.9 + g
+    return b.text([p - m1 * 0.01, m1], aliases={0: 0, 2: 1}, donors=(1,))
+
+
 def programs():
     """(name, pretty text, ranks, versions)"""
     all_versions = list(range(7))
@@ -87,6 +96,7 @@ def programs():
                                                world=2, with_inputs=False).text, 2, all_versions),
         ("argmax", argmax_text(), 1, [6]),
         ("misc", MISC, 1, [0, 4, 6]),
+        ("donated_update", donated_text(), 1, [0, 6]),
     ]
 
 

@@ -304,3 +304,64 @@ def test_malformed_compile_options_are_rejected(lib_path):
     assert rc == 1 and "past the end" in rep, rep
     rc, rep = _options_report(lib_path, b"\x1f")                          # wire type 7
     assert rc == 1, rep
+
+
+# ---------------------------------------------------------------------------- buffer donation
+def _donated_lines(rep):
+    return {int(l.split()[2]): l for l in rep.splitlines() if l.startswith("  donated argument")}
+
+
+def test_donated_optimizer_state_is_updated_in_place(lib_path):
+    """jax.jit(step, donate_argnums=...) marks each donated parameter / moment with
+    tf.aliasing_output; the AdamW update kernels read them only at the element they write, after
+    every other reader, so every result goes into its argument's buffer (also across processes)."""
+    for world in (1, 2):
+        p = configs.gpt2_program(batch=2, world=world, layers=2, d=64, heads=2, mlp=128, vocab=96, seq=64,
+                                 with_inputs=False, donate=True)
+        rc, rep = report(lib_path, p.text, nprocs=world)
+        assert rc == 0, rep
+        lines = _donated_lines(rep)
+        n_state = 3 * p.meta["n_tensors"]
+        assert len(lines) == n_state and all("written in place" in l for l in lines.values()), rep
+
+
+def _alias_program(make, aliases, donors=()):
+    b = Builder("jit_alias")
+    x, y = b.arg((64, 128), "f32"), b.arg((64, 128), "f32")
+    return b.text(make(b, x, y), aliases=aliases, donors=donors)
+
+
+def test_donation_in_place_only_where_it_is_safe(lib_path):
+    # elementwise: in place
+    rc, rep = report(lib_path, _alias_program(lambda b, x, y: [x * 2.0 + y], {0: 0}))
+    assert rc == 0 and "written in place" in _donated_lines(rep)[0], rep
+    # the result is the argument itself: in place (the output copy becomes a no-op)
+    rc, rep = report(lib_path, _alias_program(lambda b, x, y: [x, y + 1.0], {0: 0}))
+    assert rc == 0 and "written in place" in _donated_lines(rep)[0], rep
+    # a row kernel (softmax over the rows of the donated argument): a fresh buffer
+    def softmax(b, x, y):
+        e = b.exp(x - b.broadcast_to(b.max(x, -1, keepdims=True), x.shape))
+        return [e / b.broadcast_to(b.sum(e, -1, keepdims=True), x.shape)]
+    rc, rep = report(lib_path, _alias_program(softmax, {0: 0}))
+    assert rc == 0 and "fresh buffer" in _donated_lines(rep)[0], rep
+    # the donated argument read at another element (its transpose): a fresh buffer
+    b = Builder("jit_alias_t")
+    x, y = b.arg((64, 64), "f32"), b.arg((64, 64), "f32")
+    rc, rep = report(lib_path, b.text([b.transpose(x, (1, 0)) + y], aliases={0: 0}))
+    assert rc == 0 and "fresh buffer" in _donated_lines(rep)[0], rep
+    # a buffer donor without an alias is listed, no result is tied to it
+    rc, rep = report(lib_path, _alias_program(lambda b, x, y: [x + y], {}, donors=(1,)))
+    assert rc == 0 and _donated_lines(rep)[1].strip() == "donated argument 1", rep
+
+
+@pytest.mark.parametrize("aliases,err", [({0: 1}, "has 1 results"), ({0: 0, 1: 0}, "of two arguments")])
+def test_bad_aliasing_is_a_compile_error(lib_path, aliases, err):
+    rc, rep = report(lib_path, _alias_program(lambda b, x, y: [x + y], aliases))
+    assert rc == 1 and err in rep, rep
+
+
+def test_alias_between_different_types_is_a_compile_error(lib_path):
+    b = Builder("jit_alias")
+    x = b.arg((64, 128), "f32")
+    rc, rep = report(lib_path, b.text([b.convert(x, "bf16")], aliases={0: 0}))
+    assert rc == 1 and "cannot alias result 0" in rep, rep
