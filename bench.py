@@ -96,7 +96,7 @@ def main():
     ap.add_argument("--layers", type=int, default=12, help="decoder layers of the DP step")
     ap.add_argument("--nccl-max-ctas", type=int, default=0,
                     help="DP step: cap on the SMs one NCCL collective occupies (client option nccl_max_ctas; 0 = NCCL's choice)")
-    ap.add_argument("--donate", action="store_true", help="DP step: params and moments donated (updated in place)")
+    ap.add_argument("--no-donate", action="store_true", help="DP step: params and moments not donated (fresh buffers)")
     ap.add_argument("--no-sub", action="store_true", help="headline only (no sub-benchmarks, no CPU baseline)")
     ap.add_argument("--no-sweep", action="store_true", help="attention: no sequence-length sweep")
     ap.add_argument("--only", default="", help="gemm / fused / attn_bwd: one case by name")

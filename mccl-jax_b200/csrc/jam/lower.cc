@@ -2712,11 +2712,30 @@ class Lowerer {
     for (size_t k = 0; k < members.size(); ++k) slot_of_[members[k]->id] = member_slot[k];
     std::vector<DT> in_dts;
     for (int s : gen.in_slots) in_dts.push_back(SlotDt(s));
+    // a row loop of elementwise members only is one walk over each row: a result aliased to a
+    // donated argument that the walk reads only at the element it writes can be written in place
+    std::vector<std::pair<int, int>> inplace;
+    std::set<int> shared_in, shared_out;
+    bool one_walk = !any_reduce;
+    for (const Value* m : members) one_walk = one_walk && m->type.dims == X;
+    for (size_t k = 0; one_walk && k < members.size(); ++k) {
+      auto al = alias_arg_slot_.find(members[k]->id);
+      if (al == alias_arg_slot_.end() || out_of[k] < 0) continue;
+      const int sa = al->second, so = out_slots[out_of[k]];
+      if (p_->slots[sa].bytes != p_->slots[so].bytes || slot_pitch_.count(so)) continue;
+      auto pi = gen.param_of.find(sa);
+      if (pi != gen.param_of.end()) {
+        if (gen.nonident.count(sa)) continue;
+        shared_in.insert(pi->second);
+      }
+      shared_out.insert(out_of[k]);
+      inplace.push_back({sa, so});
+    }
     std::string fn = KName();
     const int threads = block_mode ? 512 : 256;
     src_ << "extern \"C\" __global__ void __launch_bounds__(" << threads << ", " << (block_mode ? 2 : 4) << ") " << fn << "("
-         << KernelParams(gen.in_slots, (int)out_slots.size(), false) << ") {\n"
-         << ParamCasts(gen.in_slots, in_dts, out_dts);
+         << KernelParams(gen.in_slots, (int)out_slots.size(), false, shared_in, shared_out) << ") {\n"
+         << ParamCasts(gen.in_slots, in_dts, out_dts, shared_in, shared_out);
     for (const auto& s : shared) src_ << "  __shared__ " << s.first << " " << s.second << "[32];\n";
     if (block_mode)
       src_ << "  const int lt = threadIdx.x;\n"
@@ -2739,6 +2758,7 @@ class Lowerer {
     Lc.block = threads;
     Lc.grid_x = block_mode ? std::max<int64_t>(1, rows) : std::max<int64_t>(1, (rows * nseg + 7) / 8);
     Lc.grid_stride = true;
+    Lc.inplace = inplace;
     Step st;
     st.kind = StepKind::kFusion;
     st.launches.push_back(Lc);

@@ -213,6 +213,9 @@ std::string Executable::Build(const char* text, size_t n, const CompileOptions& 
 }
 
 // The slots a step reads or writes.
+// Arguments and results up to this size are staged at fixed addresses (PerDevice::stage).
+constexpr int64_t kStageMax = 256;
+
 static void StepSlots(const Step& S, std::vector<int>* out) {
   out->clear();
   auto add = [&](std::initializer_list<int> l) { for (int s : l) if (s >= 0) out->push_back(s); };
@@ -321,6 +324,7 @@ Executable::~Executable() {
         if (x) cudaGraphExecDestroy(x);
     if (kv.second.arena) cudaFree(kv.second.arena);
     if (kv.second.gemm_counters) cudaFree(kv.second.gemm_counters);
+    if (kv.second.stage) cudaFree(kv.second.stage);
     for (void* p : kv.second.consts) cudaFree(p);
     if (d.ok)
       for (void* m : kv.second.modules) d.unload((CUmodule)m);
@@ -362,6 +366,22 @@ std::string Executable::Load(DeviceState& dev, PerDevice** pd) {
   if (arena_bytes > 0 && cudaMalloc(&p.arena, (size_t)arena_bytes) != cudaSuccess) {
     cudaGetLastError();
     return "device allocation of the " + std::to_string(arena_bytes) + "-byte intermediate arena failed";
+  }
+  // fixed homes for small arguments and results (see PerDevice::stage)
+  p.stage_off.assign(plan_.slots.size(), -1);
+  int64_t stage_bytes = 0;
+  auto stage_slot = [&](int s) {
+    const int64_t b = plan_.slots[s].bytes;
+    if (b <= 0 || b > kStageMax || p.stage_off[s] >= 0) return;
+    p.stage_off[s] = stage_bytes;
+    stage_bytes += (b + 255) & ~(int64_t)255;
+  };
+  for (int s : plan_.arg_slots) stage_slot(s);
+  for (int s : plan_.out_slots)
+    if (plan_.slots[s].arg_index < 0 && plan_.slots[s].const_index < 0) stage_slot(s);
+  if (stage_bytes > 0 && cudaMalloc(&p.stage, (size_t)stage_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return "device allocation of the small-value stage failed";
   }
   // one work-unit counter per GEMM step, zeroed at the start of every execution
   p.gemm_slot.assign(plan_.steps.size(), -1);
@@ -421,14 +441,15 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     else if (pd->arena_off[s] >= 0) ptr[s] = (char*)pd->arena + pd->arena_off[s];
   }
   // results written in place of donated arguments
-  if (taken) taken->assign(args.size(), false);
+  std::vector<bool> in_place(args.size(), false);
   if (donated && donated->size() == args.size())
     for (size_t k = 0; k < P.out_inplace_arg.size(); ++k) {
       const int i = P.out_inplace_arg[k];
       if (i < 0 || !(*donated)[i] || !args[i]) continue;
       ptr[P.out_slots[k]] = const_cast<void*>(args[i]);
-      if (taken) (*taken)[i] = true;
+      in_place[i] = true;
     }
+  if (taken) *taken = in_place;
   cudaStream_t st = dev.stream;
   auto slot = [&](int s) -> std::string {
     if (s < 0 || ptr[s]) return "";
@@ -486,6 +507,22 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
                       !(has_coll && std::getenv("B200_NO_COLL_GRAPHS"));
   GraphEntry* ge = nullptr;
   bool capturing = false;          // this execution captures its pieces' graphs
+  std::vector<int> staged_outs;    // results computed in the stage, copied out at the end
+  if (graphs && pd->stage) {
+    for (size_t k = 0; k < args.size(); ++k) {
+      const int s = P.arg_slots[k];
+      if (pd->stage_off[s] < 0 || !args[k] || in_place[k]) continue;
+      void* home = (char*)pd->stage + pd->stage_off[s];
+      if (cudaMemcpyAsync(home, args[k], (size_t)P.slots[s].bytes, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return fail("staging a small argument failed");
+      ptr[s] = home;
+    }
+    for (int s : P.out_slots) {
+      if (pd->stage_off[s] < 0 || ptr[s]) continue;
+      ptr[s] = (char*)pd->stage + pd->stage_off[s];
+      staged_outs.push_back(s);
+    }
+  }
   if (graphs) {
     for (int s : P.out_slots) {
       err = slot(s);
@@ -726,16 +763,27 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     else if (ge->captured) g_graph_launches.fetch_add(1);
   }
   abort_capture = nullptr;
-  outs->clear();
-  for (int s : P.out_slots) {
-    if (!ptr[s]) { err = slot(s); if (!err.empty()) return fail(err); }
-    outs->push_back(ptr[s]);
-    owned[s] = false;
-  }
   // the execution completes on the compute stream only after its collectives
   for (auto& e : coll_done)
     if (e) cudaStreamWaitEvent(st, e, 0);
   release_events();
+  outs->clear();
+  for (int s : P.out_slots) {
+    if (std::find(staged_outs.begin(), staged_outs.end(), s) != staged_outs.end()) {
+      void* own = nullptr;
+      err = DeviceAlloc((size_t)P.slots[s].bytes, st, &own);
+      if (!err.empty()) return fail(err);
+      if (cudaMemcpyAsync(own, ptr[s], (size_t)P.slots[s].bytes, cudaMemcpyDeviceToDevice, st) != cudaSuccess) {
+        DeviceFree(own, st);
+        return fail("copying a small result out of the stage failed");
+      }
+      outs->push_back(own);
+      continue;
+    }
+    if (!ptr[s]) { err = slot(s); if (!err.empty()) return fail(err); }
+    outs->push_back(ptr[s]);
+    owned[s] = false;
+  }
   for (size_t s = 0; s < P.slots.size(); ++s)
     if (owned[s]) DeviceFree(ptr[s], st);
   ExecTimerMarkEnd(dev.ordinal, st);

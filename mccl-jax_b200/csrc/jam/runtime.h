@@ -74,6 +74,12 @@ class Executable {
     void* arena = nullptr;
     std::vector<int64_t> arena_off;          // per slot, -1 when not in the arena
     std::vector<GraphEntry> graphs;          // captured executions by argument / output addresses
+    // Small arguments and results (scalars: step counters, bias corrections, a loss) live at fixed
+    // offsets of `stage` inside executions that may replay CUDA graphs: arguments are copied in
+    // first, results copied out into their own buffers last, so the graphs' addresses -- and the
+    // cache key -- do not change with the fresh small buffers a caller passes every step.
+    void* stage = nullptr;
+    std::vector<int64_t> stage_off;          // per slot, -1 when not staged
     int* gemm_counters = nullptr;            // per GEMM step: its launch's work-unit counter
     int n_gemm = 0;
     std::vector<int> gemm_slot;              // step index -> its counter (-1: not a GEMM)

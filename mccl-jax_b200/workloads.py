@@ -80,9 +80,15 @@ class Clocks:
              "clocks_event_reasons.sw_power_cap")
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.p = None
+        # nvidia-smi takes a moment to start: the timed region begins once it is sampling
+        t0 = time.time()
+        while self.p is not None and time.time() - t0 < 5:
+            if os.path.getsize(self.f.name) > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self):
         if self.p is None:
@@ -169,7 +175,7 @@ def run_dp(a, world, rank, local):
     batch = 8
     t0 = time.time()
     # params and moments donated (jax.jit(step, donate_argnums=...)): AdamW updates them in place
-    donate = bool(getattr(a, "donate", False))
+    donate = not getattr(a, "no_donate", False)
     prog = configs.gpt2_program(batch=batch, world=world, rank=rank, donate=donate, **cfg)
     client, store = make_client(world, rank, local, nccl_max_ctas=getattr(a, "nccl_max_ctas", 0))
     exe = client.compile(prog.text)

@@ -353,6 +353,37 @@ def test_repeated_executions_replay_a_cuda_graph(client, lib_path):
     exe.destroy()
 
 
+def test_fresh_scalar_arguments_still_replay_the_graph(client, lib_path):
+    """A training loop passes new scalar buffers every step (a step count, bias corrections) and
+    gets a new scalar loss back: those small values are staged at fixed addresses, so the
+    executions keep replaying one captured graph -- and each replay sees its own scalars."""
+    import ctypes
+    lib = ctypes.CDLL(lib_path)
+    lib.b200_graph_stats.restype = ctypes.c_longlong
+    b = Builder("jit_scalar_step")
+    x, w, c = b.arg((512, 256), "f32"), b.arg((256, 256), "f32"), b.arg((), "f32")
+    h = x
+    for _ in range(4):                                   # enough launches for graph capture
+        h = b.tanh(b.matmul(h, w)) * b.broadcast_to(c, (512, 256))
+    text = b.text([h, b.sum(b.sum(h, 1), 0)])
+    rng = np.random.default_rng(0)
+    xs, ws = rng.standard_normal((512, 256), dtype=np.float32), rng.standard_normal((256, 256), dtype=np.float32) / 16
+    exe = client.compile(text)
+    bx, bw = client.buffer_from_host(xs), client.buffer_from_host(ws)
+    rep0 = lib.b200_graph_stats(1)
+    for step in range(8):
+        cv = np.array(0.5 + 0.25 * step, np.float32)
+        bc = client.buffer_from_host(cv)
+        h_out, loss = exe.execute([bx, bw, bc])
+        ref = oracle_run(text, [xs, ws, cv])
+        assert_close(h_out.to_numpy(), ref[0], RTOL_F32 * 10, f"step {step}")
+        assert abs(float(loss.to_numpy()) - float(ref[1])) <= 1e-4 * max(1.0, abs(float(ref[1])))
+        for o in (h_out, loss, bc):
+            o.delete()
+    assert lib.b200_graph_stats(1) - rep0 >= 5
+    exe.destroy()
+
+
 @pytest.mark.parametrize("dt", ["bf16", "f32"])
 def test_head_gradients_assembled_into_rows(client, dt):
     """The attention backward's dq / dk / dv ([B, H, S, D]) transposed to [B*S, H*D] and placed side
