@@ -151,12 +151,14 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qblk = S / (2 * TQ);
-  // query-block-major order: for the causal case every (batch, head)'s heaviest (last) query block
-  // is dispatched before any lighter one, so the last wave holds short CTAs
+  // causal: query-block-major order, every (batch, head)'s heaviest (last) query block dispatched
+  // before any lighter one, so the last wave holds short CTAs.  Non-causal (equal CTAs): head-major
+  // order, the query blocks of one (batch, head) in flight together, so its K and V are read from
+  // HBM once and from L2 by the others.
   const int n_bh = (int)(gridDim.x / n_qblk);
-  const int qi = (int)(blockIdx.x / n_bh);
+  const int qi = CAUSAL ? (int)(blockIdx.x / n_bh) : (int)(blockIdx.x % n_qblk);
   const int qb = CAUSAL ? (n_qblk - 1 - qi) : qi;
-  const int bh = (int)(blockIdx.x % n_bh);
+  const int bh = CAUSAL ? (int)(blockIdx.x % n_bh) : (int)(blockIdx.x / n_qblk);
   const int q0 = qb * 2 * TQ;
   const int n_kv = CAUSAL ? (q0 + 2 * TQ) / TK : S / TK;
   const long long row_base = (long long)bh * S;  // row of (bh, 0) in the [B*H*S, D] views

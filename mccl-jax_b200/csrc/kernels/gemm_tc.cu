@@ -33,11 +33,15 @@ namespace {
 constexpr int BM = 128, BK = 64;
 constexpr int kUnitRing = 4;   // work units published ahead by the TMA warp
 
-template <int BN>
+// PAIR: the CTA is one of a pair (cluster of two) that computes 256 x BN tiles with M = 256
+// tcgen05.mma over both CTAs (cta_group::2): each CTA loads 128 rows of A and BN / 2 rows of B, and
+// holds its 128 x BN half of the accumulator in its own tensor memory.
+template <int BN, bool PAIR = false>
 struct Cfg {
-  static constexpr int kStages = BN == 256 ? 4 : BN == 192 ? 5 : 6;
+  static constexpr int kBRows = PAIR ? BN / 2 : BN;        // B rows this CTA loads per stage
+  static constexpr int kStages = BN == 256 ? (PAIR ? 6 : 4) : BN == 192 ? 5 : 6;
   static constexpr int kABytes = BM * BK * 2;
-  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kBBytes = kBRows * BK * 2;
   static constexpr int kStage = kABytes + kBBytes;
   // epilogue staging (1024-byte aligned): 4 warps x 32 x 33 f32 for the bounds-checked path, or 4 x
   // 4 KB swizzled boxes for the TMA-store path
@@ -84,14 +88,15 @@ __device__ __forceinline__ void tile_coords(int r, int mb, int nb, int* m_blk, i
   *n_blk = q / rows;
 }
 
-// OUT: 0 f32, 1 bf16, 2 f16; AMN / BMN: operand stored MN-major
-template <int BN, int OUT, bool AMN, bool BMN>
+// OUT: 0 f32, 1 bf16, 2 f16; AMN / BMN: operand stored MN-major; PAIR: see Cfg
+template <int BN, int OUT, bool AMN, bool BMN, bool PAIR>
 __global__ void __launch_bounds__(192, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, void* __restrict__ C, int M, int N, int K, int batch, int fmt,
                int splits, float* __restrict__ ws, int tma_store, long long ldc, int terms, uint32_t piece_a,
                uint32_t piece_b, int* __restrict__ unit_counter) {
-  using CF = Cfg<BN>;
+  using CF = Cfg<BN, PAIR>;
+  constexpr int TM = PAIR ? 2 * BM : BM;       // output rows per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(smem + CF::kStages * CF::kStage);
@@ -105,7 +110,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   float* stage_base = (float*)(smem + CF::kStages * CF::kStage + 1024);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mb = (M + BM - 1) / BM, nb = (N + BN - 1) / BN;
+  // in a pair the even CTA (rank 0) issues the MMAs and owns the full / acc_empty barriers
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int unit_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int mb = (M + TM - 1) / TM, nb = (N + BN - 1) / BN;
   const int per_batch = mb * nb, num_tiles = per_batch * batch;
   // `terms` products accumulate into one result (the f32-accurate split form; 1 otherwise): term t
   // reads A's K piece (piece_a >> 4t) & 15 and B's (piece_b >> 4t) & 15, pieces sitting kbt K
@@ -124,7 +133,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 128);
+      mbar_init(&acc_empty[a], PAIR ? 256 : 128);   // every epilogue thread (of both CTAs in a pair)
     }
     for (int q = 0; q < kUnitRing; ++q) {
       mbar_init(&unit_full[q], 1);
@@ -132,9 +141,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, CF::kTmemCols);
+  if (warp == 1) {
+    if (PAIR) tmem_alloc_pair(tmem_slot, CF::kTmemCols);
+    else tmem_alloc(tmem_slot, CF::kTmemCols);
+  }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR) cluster_sync();                    // the peer's barriers exist before anything signals them
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -153,7 +166,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       // issued, so the atomic's latency stays off the critical path.  Without a counter a CTA takes
       // every gridDim.x-th unit.  Each unit index, and finally one past the end, is published to
       // the MMA and epilogue warps through the ring.
-      int next = unit_counter ? atomicAdd(unit_counter, 1) : (int)blockIdx.x;
+      // (a pair walks the units statically: both CTAs must take the same ones)
+      if (PAIR) unit_counter = nullptr;
+      int next = unit_counter ? atomicAdd(unit_counter, 1) : unit0;
       for (int iu = 0;; ++iu) {
         const int u = ok ? next : num_units;
         const int rq = iu % kUnitRing;
@@ -161,7 +176,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         *(volatile int*)&unit_ring[rq] = u;
         mbar_arrive(&unit_full[rq]);
         if (u >= num_units) break;
-        next = unit_counter ? atomicAdd(unit_counter, 1) : u + (int)gridDim.x;
+        next = unit_counter ? atomicAdd(unit_counter, 1) : u + unit_step;
         const int t = u / splits, sp = u % splits;
         const int b = t / per_batch, r = t % per_batch;
         int m_blk, n_blk;
@@ -169,36 +184,46 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int kb1 = min(kbs, (sp + 1) * kps);
         for (int kb = sp * kps; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, kErrTimeoutEmpty, &g_tc_error_gemm)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[s], CF::kStage);
+          // a pair's loads all complete on the even CTA's full barrier, armed there for both
+          if (!PAIR) mbar_arrive_expect_tx(&full[s], CF::kStage);
+          else if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * CF::kStage);
+          const uint32_t fbar = PAIR ? cluster_addr(&full[s], 0) : 0u;
+          auto load = [&](const CUtensorMap* map, void* dst, int c0, int c1) {
+            if (PAIR) tma_load_3d_pair(map, fbar, dst, c0, c1, b);
+            else tma_load_3d(map, &full[s], dst, c0, c1, b);
+          };
           uint8_t* sa = smem + s * CF::kStage;
           const int term = kb / kbt, kk = (kb - term * kbt) * BK;
           const int ka = (int)((piece_a >> (4 * term)) & 15u) * kbt * BK + kk;
           const int kb_ = (int)((piece_b >> (4 * term)) & 15u) * kbt * BK + kk;
+          const int a_row = m_blk * TM + (int)rank * BM, b_row = n_blk * BN + (int)rank * CF::kBRows;
           if (AMN) {
 #pragma unroll
-            for (int i = 0; i < BM / 64; ++i) tma_load_3d(&tmA, &full[s], sa + i * 8192, m_blk * BM + 64 * i, ka, b);
+            for (int i = 0; i < BM / 64; ++i) load(&tmA, sa + i * 8192, a_row + 64 * i, ka);
           } else {
-            tma_load_3d(&tmA, &full[s], sa, ka, m_blk * BM, b);
+            load(&tmA, sa, ka, a_row);
           }
           if (BMN) {
 #pragma unroll
-            for (int i = 0; i < BN / 64; ++i)
-              tma_load_3d(&tmB, &full[s], sa + CF::kABytes + i * 8192, n_blk * BN + 64 * i, kb_, b);
+            for (int i = 0; i < CF::kBRows / 64; ++i) load(&tmB, sa + CF::kABytes + i * 8192, b_row + 64 * i, kb_);
           } else {
-            tma_load_3d(&tmB, &full[s], sa + CF::kABytes, kb_, n_blk * BN, b);
+            load(&tmB, sa + CF::kABytes, kb_, b_row);
           }
           issued |= 1u << s;
           fill_par = (fill_par & ~(1u << s)) | (ph << s);
           if (++s == CF::kStages) { s = 0; ph ^= 1; }
         }
       }
-      // never leave with TMA writes in flight: wait (bounded) for the last fill of every stage
-      for (int q = 0; q < CF::kStages; ++q)
-        if (issued & (1u << q)) mbar_wait(&full[q], (fill_par >> q) & 1, kErrTimeoutOther, &g_tc_error_gemm);
+      // never leave with TMA writes in flight: wait (bounded) for the last fill of every stage (in a
+      // pair the even CTA's full barriers count both CTAs' loads; the odd CTA stays until the pair's
+      // final cluster barrier, which the even CTA reaches after this wait)
+      if (rank == 0)
+        for (int q = 0; q < CF::kStages; ++q)
+          if (issued & (1u << q)) mbar_wait(&full[q], (fill_par >> q) & 1, kErrTimeoutOther, &g_tc_error_gemm);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(fmt, BM, BN, BMN, AMN);
+      const uint32_t idesc = idesc_f16(fmt, TM, BN, BMN, AMN);
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
@@ -208,6 +233,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int u = *(volatile int*)&unit_ring[rq];
         mbar_arrive(&unit_empty[rq]);
         if (u >= num_units) break;
+        if (rank != 0) continue;                 // the odd CTA of a pair issues no MMAs
         const int a = local & 1;
         const uint32_t aph = (local >> 1) & 1;
         if (!mbar_wait(&acc_empty[a], aph ^ 1, kErrTimeoutAccEmpty, &g_tc_error_gemm)) break;
@@ -220,19 +246,31 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const uint32_t a_addr = smem_u32(smem + s * CF::kStage);
           const uint32_t b_addr = a_addr + CF::kABytes;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            mma_f16_ss(d, AMN ? sw128_mn_desc_lbo(a_addr + k * 2048, 8192) : sw128_desc(a_addr + k * 32),
-                       BMN ? sw128_mn_desc_lbo(b_addr + k * 2048, 8192) : sw128_desc(b_addr + k * 32), idesc,
-                       ((kb - kb0) | k) != 0);
-          mma_commit(&empty[s]);
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t da = AMN ? sw128_mn_desc_lbo(a_addr + k * 2048, 8192) : sw128_desc(a_addr + k * 32);
+            const uint64_t db = BMN ? sw128_mn_desc_lbo(b_addr + k * 2048, 8192) : sw128_desc(b_addr + k * 32);
+            if (PAIR) mma_f16_ss_pair(d, da, db, idesc, ((kb - kb0) | k) != 0);
+            else mma_f16_ss(d, da, db, idesc, ((kb - kb0) | k) != 0);
+          }
+          if (PAIR) mma_commit_pair(&empty[s]);  // frees the stage in both CTAs
+          else mma_commit(&empty[s]);
           if (++s == CF::kStages) { s = 0; ph ^= 1; }
         }
-        if (ok) mma_commit(&acc_full[a]);
+        if (ok) {
+          if (PAIR) mma_commit_pair(&acc_full[a]);
+          else mma_commit(&acc_full[a]);
+        }
       }
     }
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
+    // the accumulator buffer is free again once every epilogue thread (of both CTAs in a pair) has
+    // read its part; a pair's MMAs wait on the even CTA's barrier
+    auto release_acc = [&](int a) {
+      if (PAIR && rank != 0) mbar_arrive_remote(cluster_addr(&acc_empty[a], 0));
+      else mbar_arrive(&acc_empty[a]);
+    };
     for (int local = 0;; ++local) {
       const int rq = local % kUnitRing;
       if (!mbar_wait_warp(&unit_full[rq], (local / kUnitRing) & 1, kErrTimeoutAcc, &g_tc_error_gemm)) break;
@@ -248,7 +286,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int b = t / per_batch, r = t % per_batch;
       int m_blk, n_blk;
       tile_coords(r, mb, nb, &m_blk, &n_blk);
-      const int row = m_blk * BM + row_in_tile;
+      const int m0 = m_blk * TM + (int)rank * BM;   // first output row of this CTA's accumulator half
+      const int row = m0 + row_in_tile;
       const uint32_t taddr = tmem_base + a * BN + ((uint32_t)(q * 32) << 16);
       const long long crow = ((long long)b * M + row) * ldc;      // ldc: C's row pitch (>= N)
       // full 32-column chunks of an aligned row go straight out as 16-byte vectors; otherwise (N not
@@ -276,12 +315,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_reduce_add_3d(&tmC, box, col, m_blk * BM + q * 32, b);
+            tma_reduce_add_3d(&tmC, box, col, m0 + q * 32, b);
             bulk_commit();
           }
         }
         tc_fence_before();
-        mbar_arrive(&acc_empty[a]);
+        release_acc(a);
         continue;
       }
       if (tma_store) {
@@ -311,12 +350,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(&tmC, box, col, m_blk * BM + q * 32, b);
+            tma_store_3d(&tmC, box, col, m0 + q * 32, b);
             bulk_commit();
           }
         }
         tc_fence_before();
-        mbar_arrive(&acc_empty[a]);
+        release_acc(a);
         continue;
       }
 #pragma unroll 1
@@ -335,7 +374,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const int gcol = col + lane;
 #pragma unroll 4
           for (int rr = 0; rr < 32; ++rr) {
-            const int grow = m_blk * BM + q * 32 + rr;
+            const int grow = m0 + q * 32 + rr;
             if (grow < M && gcol < N) atomicAdd(ws + ((long long)b * M + grow) * (long long)N + gcol, stage[rr * 33 + lane]);
           }
           __syncwarp();
@@ -365,7 +404,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const int gcol = col + lane;
 #pragma unroll 4
           for (int rr = 0; rr < 32; ++rr) {
-            const int grow = m_blk * BM + q * 32 + rr;
+            const int grow = m0 + q * 32 + rr;
             if (grow < M && gcol < N) {
               const float x = stage[rr * 33 + lane];
               const long long o = ((long long)b * M + grow) * ldc + gcol;
@@ -378,15 +417,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[a]);
+      release_acc(a);
     }
   }
   if (warp >= 2 && lane == 0) bulk_wait_all();    // TMA stores complete before the CTA's smem goes away
   tc_fence_before();
-  __syncthreads();
+  if (PAIR) cluster_sync();                      // neither CTA leaves while the pair's MMAs may read it
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, CF::kTmemCols);
+    if (PAIR) tmem_dealloc_pair(tmem_base, CF::kTmemCols);
+    else tmem_dealloc(tmem_base, CF::kTmemCols);
   }
 }
 
@@ -525,20 +566,50 @@ struct Terms {
   long long ka = -1, kb = -1;  // K extent of A's / B's map (-1: K)
 };
 
+// CTA pairs (clusters of two) of the pair kernel that fit on the device at once; 0 if none.
 template <int BN, int OUT, bool AMN, bool BMN>
+static int MaxPairs() {
+  static int pairs[8] = {-1, -1, -1, -1, -1, -1, -1, -1};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& p = pairs[dev & 7];
+  if (p < 0) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * NumSMs());
+    cfg.blockDim = dim3(192);
+    cfg.dynamicSmemBytes = Cfg<BN, true>::kSmem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<BN, OUT, AMN, BMN, true>, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    p = n;
+  }
+  return p;
+}
+
+template <int BN, int OUT, bool AMN, bool BMN, bool PAIR>
 static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, void* C, int batch, int M, int N, int K,
                     int fmt, cudaStream_t st, int splits, float* ws, long long ldc, const Terms& tm, int* counter) {
-  using CF = Cfg<BN>;
+  using CF = Cfg<BN, PAIR>;
   static std::once_flag once[8];
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 7], [] {
-    cudaFuncSetAttribute(gemm_tc_kernel<BN, OUT, AMN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kSmem);
+    cudaFuncSetAttribute(gemm_tc_kernel<BN, OUT, AMN, BMN, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kSmem);
   });
   CUtensorMap ta, tb, tc;
   const int ka = tm.ka < 0 ? K : (int)tm.ka, kb = tm.kb < 0 ? K : (int)tm.kb;
   bool ok = AMN ? MakeOperandMapMN(&ta, A, ka, lda, M, batch, fmt == 0) : MakeOperandMap(&ta, A, ka, lda, M, batch, BM, fmt == 0);
-  ok = ok && (BMN ? MakeOperandMapMN(&tb, B, kb, ldb, N, batch, fmt == 0) : MakeOperandMap(&tb, B, kb, ldb, N, batch, BN, fmt == 0));
+  ok = ok && (BMN ? MakeOperandMapMN(&tb, B, kb, ldb, N, batch, fmt == 0)
+                  : MakeOperandMap(&tb, B, kb, ldb, N, batch, CF::kBRows, fmt == 0));
   if (!ok) return -2;
   // TMA-store epilogue when C's rows are 16-byte multiples (else the bounds-checked staged path);
   // split-K partials go to the f32 workspace by TMA reduce-add under the same condition
@@ -551,22 +622,44 @@ static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, 
       tma_store = MakeOutputMap(&tc, ws, M, N, batch, 0, N) ? 2 : 0;
   }
   if (!tma_store) tc = ta;                                  // unused
-  int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
-  int grid = std::min(tiles * splits, NumSMs());
-  gemm_tc_kernel<BN, OUT, AMN, BMN><<<grid, 192, CF::kSmem, st>>>(ta, tb, tc, C, M, N, K, batch, fmt, splits, ws, tma_store, ldc,
-                                                                   tm.n, tm.a, tm.b, counter);
+  constexpr int TM = PAIR ? 2 * BM : BM;
+  const int tiles = ((M + TM - 1) / TM) * ((N + BN - 1) / BN) * batch;
+  if constexpr (!PAIR) {
+    const int grid = std::min(tiles * splits, NumSMs());
+    gemm_tc_kernel<BN, OUT, AMN, BMN, false><<<grid, 192, CF::kSmem, st>>>(ta, tb, tc, C, M, N, K, batch, fmt, splits, ws,
+                                                                           tma_store, ldc, tm.n, tm.a, tm.b, counter);
+  } else {
+    const int pairs = std::min(tiles * splits, MaxPairs<BN, OUT, AMN, BMN>());
+    if (pairs < 1) return -3;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(192);
+    cfg.dynamicSmemBytes = CF::kSmem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int* no_counter = nullptr;                 // a pair walks its units statically
+    if (cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, OUT, AMN, BMN, true>, ta, tb, tc, C, M, N, K, batch, fmt, splits, ws,
+                           tma_store, ldc, tm.n, tm.a, tm.b, no_counter) != cudaSuccess)
+      return -3;
+  }
   CountLaunches();
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
-template <int BN, int OUT>
+template <int BN, int OUT, bool PAIR>
 static int LaunchTcMajor(bool amn, bool bmn, const void* A, long long lda, const void* B, long long ldb, void* C, int batch,
                          int M, int N, int K, int fmt, cudaStream_t st, int splits, float* ws, long long ldc,
                          const Terms& tm, int* counter) {
-  if (amn && bmn) return LaunchTc<BN, OUT, true, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm, counter);
-  if (amn) return LaunchTc<BN, OUT, true, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm, counter);
-  if (bmn) return LaunchTc<BN, OUT, false, true>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm, counter);
-  return LaunchTc<BN, OUT, false, false>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm, counter);
+  if (amn && bmn) return LaunchTc<BN, OUT, true, true, PAIR>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm, counter);
+  if (amn) return LaunchTc<BN, OUT, true, false, PAIR>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm, counter);
+  if (bmn) return LaunchTc<BN, OUT, false, true, PAIR>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm, counter);
+  return LaunchTc<BN, OUT, false, false, PAIR>(A, lda, B, ldb, C, batch, M, N, K, fmt, st, splits, ws, ldc, tm, counter);
 }
 
 __global__ void __launch_bounds__(256) ws_to_16bit_kernel(const float* __restrict__ ws, uint16_t* __restrict__ c, long long n,
@@ -611,33 +704,44 @@ int TakeGemmError() {
 // per FLOP.  K is split (at most 8 slices of >= 16 K blocks, none empty) when that shortens the
 // model's time including the f32 partials' cost (a zeroing pass, L2 reductions and, for 16-bit
 // results, a rounding pass): when the tiles leave SMs idle, or when a long K walk makes the last
-// round of tiles a large fraction of the launch.  Shared by the compiler (which sizes the workspace)
-// and the launcher.
-void GemmTile(int64_t batch, int64_t M, int64_t N, int64_t K, int sms, int* bn_out, int* splits_out) {
-  const int64_t kbs = std::max<int64_t>(1, (K + BK - 1) / BK), mb = (M + BM - 1) / BM;
+// round of tiles a large fraction of the launch.  256-column tiles may also run on CTA pairs (256 x
+// 256 tiles on two SMs, half the shared-memory operand traffic per SM: measured 12-19 % faster per
+// tile on B200), which halves the tile count and the units' slots.  Shared by the compiler (which
+// sizes the workspace) and the launcher.  B200_GEMM_PAIR=0 / 1 turns pairs off / forces them for
+// every 256-column choice.
+void GemmTile(int64_t batch, int64_t M, int64_t N, int64_t K, int sms, int* bn_out, int* splits_out, bool* pair_out) {
+  const int64_t kbs = std::max<int64_t>(1, (K + BK - 1) / BK);
   const bool no_split = std::getenv("B200_GEMM_NO_SPLITK") != nullptr || K <= 0;
   const char* force = std::getenv("B200_GEMM_BN");
+  const char* pair_env = std::getenv("B200_GEMM_PAIR");
+  const bool pair_off = pair_env && pair_env[0] == '0', pair_forced = pair_env && pair_env[0] == '1';
   double best = 1e300;
   int best_bn = 256, best_s = 1;
+  bool best_pair = false;
   for (int bn : {256, 192, 128}) {
     if (force && std::atoi(force) != bn) continue;
     if (!force && bn > 128 && N < bn) continue;
-    const int64_t tiles = mb * ((N + bn - 1) / bn) * batch;
-    const double width = bn / 256.0 * (bn == 128 ? 1.3 : bn == 192 ? 1.08 : 1.0);   // measured on B200
-    for (int64_t s = 1; s <= 8; ++s) {
-      if (s > 1 && (no_split || kbs / s < 16 || (tiles * 2 > sms && kbs < 128))) break;
-      const int64_t kps = (kbs + s - 1) / s;
-      if (s > 1 && (s - 1) * kps >= kbs) continue;        // would leave an empty slice
-      const int64_t rounds = (tiles * s + sms - 1) / sms;
-      double t = (double)rounds * width * (double)(kps + 2);
-      // splitting: zero + reduce + round the f32 partials, ~10 bytes per output at HBM speed, in
-      // units of one 128 x 256 x 64 block step (~0.45 us)
-      if (s > 1) t += (double)batch * M * N * 10.0 / 6.5e12 / 0.45e-6;
-      if (t < best * 0.999) { best = t; best_bn = bn; best_s = (int)s; }
+    for (int pair = 0; pair <= (bn == 256 ? 1 : 0); ++pair) {
+      if (pair ? (pair_off || M < 2 * BM) : (pair_forced && bn == 256 && M >= 2 * BM)) continue;
+      const int64_t tm = pair ? 2 * BM : BM, slots = pair ? sms / 2 : sms;
+      const int64_t tiles = ((M + tm - 1) / tm) * ((N + bn - 1) / bn) * batch;
+      const double width = pair ? 0.85 : bn / 256.0 * (bn == 128 ? 1.3 : bn == 192 ? 1.08 : 1.0);   // measured on B200
+      for (int64_t s = 1; s <= 8; ++s) {
+        if (s > 1 && (no_split || kbs / s < 16 || (tiles * 2 > slots && kbs < 128))) break;
+        const int64_t kps = (kbs + s - 1) / s;
+        if (s > 1 && (s - 1) * kps >= kbs) continue;        // would leave an empty slice
+        const int64_t rounds = (tiles * s + slots - 1) / slots;
+        double t = (double)rounds * width * (double)(kps + 2);
+        // splitting: zero + reduce + round the f32 partials, ~10 bytes per output at HBM speed, in
+        // units of one 128 x 256 x 64 block step (~0.45 us)
+        if (s > 1) t += (double)batch * M * N * 10.0 / 6.5e12 / 0.45e-6;
+        if (t < best * 0.999) { best = t; best_bn = bn; best_s = (int)s; best_pair = pair != 0; }
+      }
     }
   }
   *bn_out = best_bn;
   *splits_out = best_s;
+  if (pair_out) *pair_out = best_pair;
 }
 
 int GemmSplitK(int64_t batch, int64_t M, int64_t N, int64_t K, int sms) {
@@ -653,18 +757,21 @@ static int RunTc(const void* A, long long lda, bool a_mn, const void* B, long lo
                  const Terms& tm, int* counter) {
   int b = (int)batch, m = (int)M, n = (int)N, k = (int)K;
   int bn = 256, splits = 1;
-  GemmTile(batch, M, N, k_eff, NumSMs(), &bn, &splits);
+  bool pair = false;
+  GemmTile(batch, M, N, k_eff, NumSMs(), &bn, &splits, &pair);
   if (ldc != N) splits = 1;                  // partial sums are laid out densely
   float* acc = out == 0 ? (float*)C : ws;
   if (splits > 1 && !acc) splits = 1;
   if (splits > 1 && cudaMemsetAsync(acc, 0, (size_t)batch * M * N * 4, st) != cudaSuccess) return -3;
   auto launch = [&](auto out_c) {
     constexpr int O = decltype(out_c)::value;
-    if (bn == 256) return LaunchTcMajor<256, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm,
-                                                  counter);
-    if (bn == 192) return LaunchTcMajor<192, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm,
-                                                  counter);
-    return LaunchTcMajor<128, O>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm, counter);
+    if (bn == 256 && pair)
+      return LaunchTcMajor<256, O, true>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm, counter);
+    if (bn == 256) return LaunchTcMajor<256, O, false>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm,
+                                                         counter);
+    if (bn == 192) return LaunchTcMajor<192, O, false>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm,
+                                                         counter);
+    return LaunchTcMajor<128, O, false>(a_mn, b_mn, A, lda, B, ldb, C, b, m, n, k, fmt, st, splits, acc, ldc, tm, counter);
   };
   int rc = out == 0 ? launch(std::integral_constant<int, 0>{})
          : out == 1 ? launch(std::integral_constant<int, 1>{})

@@ -29,7 +29,8 @@ int Gemm(const void* A, long long lda, bool a_mn, const void* B, long long ldb, 
          int64_t N, int64_t K, int ab_type, int out_type, cudaStream_t st, float* ws, int64_t ldc, int* counter = nullptr);
 int Gemm(const void* A, long long lda, const void* B, long long ldb, void* C, int64_t batch, int64_t M, int64_t N,
          int64_t K, int ab_type, int out_type, cudaStream_t st);
-void GemmTile(int64_t batch, int64_t M, int64_t N, int64_t K, int sms, int* bn_out, int* splits_out);
+void GemmTile(int64_t batch, int64_t M, int64_t N, int64_t K, int sms, int* bn_out, int* splits_out,
+              bool* pair_out = nullptr);
 int GemmSplitK(int64_t batch, int64_t M, int64_t N, int64_t K, int sms);
 
 // f32-accurate products of f32 (or mixed f32 x 16-bit) operands on the bf16 tensor cores.  Each wide
