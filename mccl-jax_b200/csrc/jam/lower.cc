@@ -1893,6 +1893,38 @@ class Lowerer {
     std::vector<const Value*> row;       // members of the open row group
     std::vector<int64_t> row_x;          // its row space X = [rows..., L]
     std::vector<Op*> colred;             // sibling column reductions emitted as one kernel
+    // Reductions of the open row group's per-row results (a loss summed over the rows) and the loop
+    // roots computed from them are held back behind the group, so that later full-row members (the
+    // loss gradient over the same rows) can still join it: one walk of the rows instead of two.
+    // `tainted` holds the values computed from held-back results; an op that needs one closes the
+    // group first.  Collectives of held-back values wait with them.
+    std::vector<Op*> deferred;
+    std::unordered_set<int> tainted;
+    std::vector<Op*> held_colls;
+    std::unordered_set<const Op*> hoisted;
+    auto emit_deferred = [&]() {
+      std::vector<const Value*> roots;
+      auto flush_roots = [&]() {
+        if (!roots.empty()) EmitLoopGroup(roots);
+        roots.clear();
+      };
+      for (Op* d : deferred) {
+        if (d->name == "reduce") {
+          flush_roots();
+          if (d->results.size() == 2) EmitArgReduce(d);
+          else EmitReduce(d);
+        } else {
+          const Value* r = d->result();
+          if (!roots.empty() && roots[0]->type.dims != r->type.dims) flush_roots();
+          roots.push_back(r);
+        }
+      }
+      flush_roots();
+      deferred.clear();
+      tainted.clear();
+      for (Op* c : held_colls) EmitCollective(c);
+      held_colls.clear();
+    };
     auto flush = [&]() {
       // queued column reductions precede every open row / loop group in program order
       if (!colred.empty()) EmitColumnReduceGroup(colred);
@@ -1901,7 +1933,15 @@ class Lowerer {
       row.clear();
       if (!pending.empty()) EmitLoopGroup(pending);
       pending.clear();
+      emit_deferred();
     };
+    auto reads_tainted = [&](const Op* op) {
+      if (tainted.empty()) return false;
+      for (const Value* o : op->operands)
+        if (tainted.count(o->id) || tainted.count(Resolve(o)->id)) return true;
+      return false;
+    };
+    const bool defer_ok = !std::getenv("B200_NO_DEFER");
     // true if r joined the open row group
     auto join_row = [&](const Value* r) {
       if (row.empty()) return false;
@@ -1915,7 +1955,6 @@ class Lowerer {
     // Collectives are issued as soon as their operand exists (the reference hoists them too,
     // src/jam/lower.mm:438-458): a gradient's all_reduce then overlaps the rest of the backward pass.
     std::vector<std::pair<int, Op*>> hoist;   // (index of the operand's producer, collective)
-    std::unordered_set<const Op*> hoisted;
     if (opt_.num_processes > 1 && !std::getenv("B200_NO_HOIST")) {
       for (auto& opp : g_.ops) {
         Op* op = opp.get();
@@ -1932,12 +1971,23 @@ class Lowerer {
       while (next_hoist < hoist.size() && hoist[next_hoist].first < op->index) {
         Op* c = hoist[next_hoist++].second;
         if (c->index <= op->index || hoisted.count(c)) continue;
+        hoisted.insert(c);
+        if (reads_tainted(c)) { held_colls.push_back(c); continue; }
         flush();
         EmitCollective(c);
-        hoisted.insert(c);
       }
       if (dead_[op->index] || hoisted.count(op)) continue;
       const std::string& n = op->name;
+      if (reads_tainted(op)) {
+        // values computed inline carry the taint; a held-back loop root joins the held-back ops;
+        // anything else waits until the held-back ops are emitted
+        if (IsElementwise(op) && !IsAlias(op) && op->results.size() == 1 && n != "gather") {
+          Value* r = op->result();
+          if (!need_[r->id]) { tainted.insert(r->id); continue; }
+          if (!row.empty() && !deferred.empty()) { deferred.push_back(op); tainted.insert(r->id); continue; }
+        }
+        flush();
+      }
       if (IsAlias(op)) {
         for (size_t k = 0; k < op->results.size(); ++k) {
           const Value* src = Resolve(op->results[k]);
@@ -1986,6 +2036,13 @@ class Lowerer {
           flush();
           row = {r};
           row_x = X;
+          continue;
+        }
+        // a reduction of the open group's per-row results waits behind the group (see `deferred`)
+        if (defer_ok && !row.empty() && op->results.size() == 1 && RowShaped(op->operands[0]->type.dims, row_x) &&
+            op->operands[0]->type.dims != row_x) {
+          deferred.push_back(op);
+          tainted.insert(r->id);
           continue;
         }
         if (op->results.size() == 1 && VecColumnReduce(op)) {
