@@ -557,7 +557,9 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
     if (g) cudaGraphDestroy(g);
     cudaGetLastError();
   };
-  static const bool pdl = std::getenv("B200_NO_PDL") == nullptr;
+  // programmatic dependent launch of generated kernels: off unless asked for (B200_PDL=1); on the
+  // DP step it measured 0.07 ms slower per step than plain stream order
+  static const bool pdl = std::getenv("B200_PDL") != nullptr;
   auto wait_for_collectives = [&](const Step& S) {
     for (int k : S.wait_coll)
       if (coll_done[k]) cudaStreamWaitEvent(st, coll_done[k], 0);
