@@ -383,12 +383,19 @@ std::string Executable::Load(DeviceState& dev, PerDevice** pd) {
     cudaGetLastError();
     return "device allocation of the small-value stage failed";
   }
-  // one work-unit counter per GEMM step, zeroed at the start of every execution
+  // one work-unit counter per GEMM step, zeroed at the start of every execution -- in programs with
+  // collectives only: there NCCL kernels hold SMs while GEMMs run, and CTAs that start late should
+  // find their units taken; alone on the GPU the static walk is faster (no atomic before the first
+  // tile: 0.25 ms per DP step)
   p.gemm_slot.assign(plan_.steps.size(), -1);
   int n_gemm = 0;
-  for (size_t i = 0; i < plan_.steps.size(); ++i)
+  bool coll = false;
+  for (size_t i = 0; i < plan_.steps.size(); ++i) {
     if (plan_.steps[i].kind == StepKind::kGemm) p.gemm_slot[i] = n_gemm++;
-  if (n_gemm > 0 && !std::getenv("B200_GEMM_STATIC_UNITS")) {
+    coll = coll || plan_.steps[i].kind == StepKind::kCollective;
+  }
+  const char* units = std::getenv("B200_GEMM_STATIC_UNITS");
+  if (n_gemm > 0 && (units ? units[0] == '0' : coll)) {
     if (cudaMalloc(&p.gemm_counters, (size_t)n_gemm * sizeof(int)) != cudaSuccess) {
       cudaGetLastError();
       return "device allocation of the GEMM work-unit counters failed";

@@ -114,6 +114,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const uint32_t rank = PAIR ? cluster_rank() : 0u;
   const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
   const int unit_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  // A pair drawing units from the counter: the even CTA claims them and writes each into both CTAs'
+  // rings; the odd CTA's ring readers (its producer, MMA thread and epilogue warps) wait on their own
+  // ring barrier (arrived on by the even CTA) and release the slot on the even CTA's barrier.
+  const bool handoff = PAIR && unit_counter != nullptr;
+  const bool ring_remote = handoff && rank != 0;
+  auto ring_wait = [&](int rq, uint32_t parity, int code) {
+    return ring_remote ? mbar_wait_cluster(&unit_full[rq], parity, code, &g_tc_error_gemm)
+                       : mbar_wait(&unit_full[rq], parity, code, &g_tc_error_gemm);
+  };
+  auto ring_release = [&](int rq) {
+    if (ring_remote) mbar_arrive_remote(cluster_addr(&unit_empty[rq], 0));
+    else mbar_arrive(&unit_empty[rq]);
+  };
   const int mb = (M + TM - 1) / TM, nb = (N + BN - 1) / BN;
   const int per_batch = mb * nb, num_tiles = per_batch * batch;
   // `terms` products accumulate into one result (the f32-accurate split form; 1 otherwise): term t
@@ -137,7 +150,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int q = 0; q < kUnitRing; ++q) {
       mbar_init(&unit_full[q], 1);
-      mbar_init(&unit_empty[q], 1 + 4);       // the MMA thread and the four epilogue warps
+      // the MMA thread and the four epilogue warps (with a handoff: of both CTAs, and the odd CTA's
+      // producer)
+      mbar_init(&unit_empty[q], handoff ? 2 * (1 + 4) + 1 : 1 + 4);
     }
     fence_barrier_init();
   }
@@ -166,17 +181,32 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       // issued, so the atomic's latency stays off the critical path.  Without a counter a CTA takes
       // every gridDim.x-th unit.  Each unit index, and finally one past the end, is published to
       // the MMA and epilogue warps through the ring.
-      // (a pair walks the units statically: both CTAs must take the same ones)
-      if (PAIR) unit_counter = nullptr;
-      int next = unit_counter ? atomicAdd(unit_counter, 1) : unit0;
+      // (without a counter a pair walks the units statically: both CTAs take the same ones)
+      int next = unit_counter ? (ring_remote ? 0 : atomicAdd(unit_counter, 1)) : unit0;
       for (int iu = 0;; ++iu) {
-        const int u = ok ? next : num_units;
         const int rq = iu % kUnitRing;
-        if (!mbar_wait(&unit_empty[rq], ((iu / kUnitRing) & 1) ^ 1, kErrTimeoutEmpty, &g_tc_error_gemm)) break;
-        *(volatile int*)&unit_ring[rq] = u;
-        mbar_arrive(&unit_full[rq]);
-        if (u >= num_units) break;
-        next = unit_counter ? atomicAdd(unit_counter, 1) : u + unit_step;
+        int u;
+        if (ring_remote) {
+          if (!ring_wait(rq, (iu / kUnitRing) & 1, kErrTimeoutEmpty)) break;
+          u = *(volatile int*)&unit_ring[rq];
+          ring_release(rq);
+          if (u >= num_units) break;
+        } else {
+          u = ok ? next : num_units;
+          if (handoff) {
+            if (!mbar_wait_cluster(&unit_empty[rq], ((iu / kUnitRing) & 1) ^ 1, kErrTimeoutEmpty, &g_tc_error_gemm)) break;
+            *(volatile int*)&unit_ring[rq] = u;
+            st_cluster_u32(cluster_addr(&unit_ring[rq], 1), (uint32_t)u);
+            mbar_arrive(&unit_full[rq]);
+            mbar_arrive_remote(cluster_addr(&unit_full[rq], 1));
+          } else {
+            if (!mbar_wait(&unit_empty[rq], ((iu / kUnitRing) & 1) ^ 1, kErrTimeoutEmpty, &g_tc_error_gemm)) break;
+            *(volatile int*)&unit_ring[rq] = u;
+            mbar_arrive(&unit_full[rq]);
+          }
+          if (u >= num_units) break;
+          next = unit_counter ? atomicAdd(unit_counter, 1) : u + unit_step;
+        }
         const int t = u / splits, sp = u % splits;
         const int b = t / per_batch, r = t % per_batch;
         int m_blk, n_blk;
@@ -229,9 +259,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       bool ok = true;
       for (int local = 0; ok; ++local) {
         const int rq = local % kUnitRing;
-        if (!mbar_wait(&unit_full[rq], (local / kUnitRing) & 1, kErrTimeoutFull, &g_tc_error_gemm)) break;
+        if (!ring_wait(rq, (local / kUnitRing) & 1, kErrTimeoutFull)) break;
         const int u = *(volatile int*)&unit_ring[rq];
-        mbar_arrive(&unit_empty[rq]);
+        ring_release(rq);
         if (u >= num_units) break;
         if (rank != 0) continue;                 // the odd CTA of a pair issues no MMAs
         const int a = local & 1;
@@ -273,10 +303,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     };
     for (int local = 0;; ++local) {
       const int rq = local % kUnitRing;
-      if (!mbar_wait_warp(&unit_full[rq], (local / kUnitRing) & 1, kErrTimeoutAcc, &g_tc_error_gemm)) break;
+      if (!__all_sync(0xffffffffu, ring_wait(rq, (local / kUnitRing) & 1, kErrTimeoutAcc))) break;
       const int u = *(volatile int*)&unit_ring[rq];
       __syncwarp();
-      if (lane == 0) mbar_arrive(&unit_empty[rq]);
+      if (lane == 0) ring_release(rq);
       if (u >= num_units) break;
       const int t = u / splits;
       const int a = local & 1;
@@ -643,9 +673,8 @@ static int LaunchTc(const void* A, long long lda, const void* B, long long ldb, 
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    int* no_counter = nullptr;                 // a pair walks its units statically
     if (cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, OUT, AMN, BMN, true>, ta, tb, tc, C, M, N, K, batch, fmt, splits, ws,
-                           tma_store, ldc, tm.n, tm.a, tm.b, no_counter) != cudaSuccess)
+                           tma_store, ldc, tm.n, tm.a, tm.b, counter) != cudaSuccess)
       return -3;
   }
   CountLaunches();

@@ -187,6 +187,36 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// mbar_wait for a barrier whose arrivals come from other CTAs of the cluster that wrote shared memory
+// this thread then reads (acquire at cluster scope).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int code, int* flag) {
+  const uint32_t addr = smem_u32(bar);
+  auto try_wait = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+  };
+  if (try_wait()) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (try_wait()) return true;
+    if (*(volatile int*)flag != 0) return false;
+    if (clock64() - t0 > kWaitBudget) {
+      atomicCAS(flag, 0, code);
+      return false;
+    }
+  }
+}
+// Stores a 32-bit value into another CTA's shared memory (a shared::cluster address).
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
 // Arrives on an mbarrier in another CTA of the cluster (a shared::cluster address from cluster_addr).
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");

@@ -110,6 +110,25 @@ def test_gemm_vs_oracle(client, dtype, M, N, K, batch):
     assert_close(out, ref, RTOL_F32 if dtype == "f32" else RTOL_F32 * 10, "gemm")
 
 
+@pytest.mark.parametrize("pair", ["0", "1"])
+@pytest.mark.parametrize("dtype,M,N,K", [("bf16", 2048, 1536, 768), ("bf16", 768, 2304, 8192), ("f32", 1024, 1024, 1024)])
+def test_gemm_units_from_a_counter(client, monkeypatch, pair, dtype, M, N, K):
+    """Programs with collectives draw GEMM work units from a per-launch counter (CTAs that start late
+    take fewer); forced here on one GPU, on one-SM tiles and on CTA pairs (whose even CTA hands each
+    unit to its peer), including split-K and the f32 split form."""
+    monkeypatch.setenv("B200_GEMM_STATIC_UNITS", "0")
+    monkeypatch.setenv("B200_GEMM_PAIR", pair)
+    p = configs.gemm_program(M, N, K, dtype=dtype, seed=M + N)
+    exe = client.compile(p.text)
+    bufs = [client.buffer_from_host(x) for x in p.inputs]
+    ref = oracle_run(p.text, p.inputs)[0]
+    for _ in range(3):                                  # the counters are zeroed again every execution
+        out = exe.execute(bufs)[0]
+        assert_close(out.to_numpy(), ref, RTOL_F32 if dtype == "f32" else RTOL_F32 * 10, "gemm with unit counter")
+        out.delete()
+    exe.destroy()
+
+
 @pytest.mark.parametrize("K,N,out", [(50, 70, "f32"), (50257 // 41, 333, "bf16"), (768, 1001, "f32"), (1000, 520, "bf16")])
 def test_dot_mixed_precision_and_unaligned_shapes(client, K, N, out):
     """bf16 x f32 operands (a backward-pass cotangent meeting bf16 weights).  With an f32 result the
