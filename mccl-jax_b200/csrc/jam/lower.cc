@@ -3981,9 +3981,14 @@ class Lowerer {
   // their operands -- or when the held ones reach 4 MiB.  The reference buckets the same in-place
   // all-reduces of <= 256 KiB into one call through a packed buffer (src/jam/jam_run.mm:186-248);
   // an NCCL group does it without the packing copies.
+  // B200_COLL_BUCKET=all holds every all-reduce, whatever its size, until a step needs one of their
+  // results: the gradients of a train step then go to NCCL as one group after the backward pass,
+  // instead of overlapping it (NCCL kernels then share no SMs with the backward's kernels).
   void GroupSmallCollectives() {
     if (opt_.num_processes <= 1 || std::getenv("B200_NO_COLL_GROUPS")) return;
-    constexpr int64_t kSmall = 256 << 10, kFlushBytes = 4 << 20;
+    const char* bucket = std::getenv("B200_COLL_BUCKET");
+    const bool all = bucket && std::strcmp(bucket, "all") == 0;
+    const int64_t kSmall = all ? INT64_MAX : 256 << 10, kFlushBytes = all ? INT64_MAX : 4 << 20;
     std::vector<Step> out, held;
     std::set<int> held_out, held_in;
     int64_t held_bytes = 0;

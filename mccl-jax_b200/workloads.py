@@ -74,6 +74,10 @@ class Clocks:
     """nvidia-smi samples (SM clock, throttle reasons) while a timed region runs."""
 
     def __init__(self, index):
+        # nvidia-smi numbers the physical GPUs: map this process's device through CUDA_VISIBLE_DEVICES
+        vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+        if index < len(vis):
+            index = vis[index]
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
