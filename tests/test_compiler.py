@@ -365,3 +365,18 @@ def test_alias_between_different_types_is_a_compile_error(lib_path):
     x = b.arg((64, 128), "f32")
     rc, rep = report(lib_path, b.text([b.convert(x, "bf16")], aliases={0: 0}))
     assert rc == 1 and "cannot alias result 0" in rep, rep
+
+
+def test_cross_entropy_backward_joins_its_forward_row_walk(lib_path, monkeypatch):
+    """The mean cross-entropy sums the per-row losses between the forward row kernel (max, sum of
+    exponentials, picked logit) and the backward (softmax - one-hot): that sum is held back behind
+    the row group, so the backward becomes a second walk of the same kernel instead of a separate
+    pass over the logits."""
+    p = configs.gpt2_program(batch=2, world=1, layers=1, d=64, heads=2, mlp=128, vocab=1000, seq=64, with_inputs=False)
+    rc, rep = report(lib_path, p.text)
+    assert rc == 0, rep
+    over_logits = [l for l in rep.splitlines() if "tensor<128x1000xf32>" in l]
+    assert len(over_logits) == 1 and "row" in over_logits[0] and "x4" in over_logits[0], rep
+    monkeypatch.setenv("B200_NO_DEFER", "1")
+    rc, rep = report(lib_path, p.text)
+    assert rc == 0 and len([l for l in rep.splitlines() if "tensor<128x1000xf32>" in l]) == 2, rep
