@@ -1042,6 +1042,7 @@ class Lowerer {
     BindOutputs();
     MergeTinyLoops();
     GroupSmallCollectives();
+    PackAllReduces();
     MarkAsyncCollectives();
     ComputeLastUse();
     DecideInPlace();
@@ -3809,7 +3810,12 @@ class Lowerer {
         W({S.bwd.dq, S.bwd.dk, S.bwd.dv, S.bwd.dq_acc, S.bwd.delta});
         break;
       case StepKind::kScatterAdd: R({S.scatter.base, S.scatter.idx, S.scatter.upd}); W({S.scatter.out}); break;
-      case StepKind::kCollective: R({S.coll.in}); W({S.coll.out}); break;
+      case StepKind::kCollective:
+        R({S.coll.in});
+        W({S.coll.out});
+        for (int x : S.coll.packed_in) R({x});
+        for (int x : S.coll.packed_out) W({x});
+        break;
       case StepKind::kCopy: R({S.copy.src}); W({S.copy.dst}); break;
     }
   }
@@ -3970,7 +3976,10 @@ class Lowerer {
       case StepKind::kAttention: r = {st.attn.q, st.attn.k, st.attn.v}; break;
       case StepKind::kAttentionBwd: r = {st.bwd.q, st.bwd.k, st.bwd.v, st.bwd.o, st.bwd.dout, st.bwd.lse}; break;
       case StepKind::kScatterAdd: r = {st.scatter.base, st.scatter.idx, st.scatter.upd}; break;
-      case StepKind::kCollective: r = {st.coll.in}; break;
+      case StepKind::kCollective:
+        r = {st.coll.in};
+        r.insert(r.end(), st.coll.packed_in.begin(), st.coll.packed_in.end());
+        break;
       case StepKind::kCopy: r = {st.copy.src}; break;
     }
     return r;
@@ -4035,6 +4044,78 @@ class Lowerer {
     p_->steps = std::move(out);
   }
 
+  // A run of grouped all-reduces of one type and reduction becomes one all-reduce over a bucket:
+  // each member's input and output slots live at the same offset inside the bucket (the producers
+  // write straight into it, the reduction is in place, the readers read from it), so NCCL runs one
+  // large operation instead of one per gradient (~20 us of latency each on NVLink).  A member
+  // qualifies when nothing but its all-reduce reads its input, its output is not a program output,
+  // and neither slot is an argument, a constant or row-padded.  B200_NO_PACK=1 turns this off.
+  void PackAllReduces() {
+    if (opt_.num_processes <= 1 || std::getenv("B200_NO_PACK")) return;
+    std::vector<Step>& steps = p_->steps;
+    std::vector<int> readers(p_->slots.size(), 0), writers(p_->slots.size(), 0);
+    for (const Step& st : steps) {
+      std::set<int> r, w;
+      StepRW(st, &r, &w);
+      for (int x : r) ++readers[x];
+      for (int x : w) ++writers[x];
+    }
+    auto plain = [&](int s) {
+      const Slot& sl = p_->slots[s];
+      return sl.arg_index < 0 && sl.const_index < 0 && !sl.output && sl.alias_of < 0 && !slot_pitch_.count(s);
+    };
+    std::vector<Step> out;
+    for (size_t i = 0; i < steps.size();) {
+      if (steps[i].kind != StepKind::kCollective || steps[i].coll.group < 0) { out.push_back(std::move(steps[i++])); continue; }
+      size_t j = i;
+      while (j < steps.size() && steps[j].kind == StepKind::kCollective && steps[j].coll.group == steps[i].coll.group) ++j;
+      // members by (type, reduction)
+      std::map<std::pair<int, int>, std::vector<size_t>> by_kind;
+      for (size_t k = i; k < j; ++k) {
+        const CollectiveStep& c = steps[k].coll;
+        if (c.op != CollKind::kAllReduce || c.in == c.out || !plain(c.in) || !plain(c.out)) continue;
+        if (readers[c.in] != 1 || writers[c.out] != 1 || p_->slots[c.in].bytes != p_->slots[c.out].bytes) continue;
+        by_kind[{(int)c.dt, (int)c.reduce}].push_back(k);
+      }
+      std::vector<bool> packed(j - i, false);
+      std::vector<Step> buckets;
+      for (auto& kv : by_kind) {
+        if (kv.second.size() < 2) continue;
+        int64_t total = 0;
+        for (size_t k : kv.second) total += (p_->slots[steps[k].coll.in].bytes + 255) / 256 * 256;
+        const int bucket = NewSlot(total);
+        Step b;
+        b.kind = StepKind::kCollective;
+        b.coll = steps[kv.second[0]].coll;
+        b.coll.in = b.coll.out = bucket;
+        b.coll.packed_in.clear();
+        b.coll.packed_out.clear();
+        int64_t off = 0;
+        for (size_t k : kv.second) {
+          const CollectiveStep& c = steps[k].coll;
+          for (int x : {c.in, c.out}) {
+            p_->slots[x].alias_of = bucket;
+            p_->slots[x].alias_off = off;
+          }
+          b.coll.packed_in.push_back(c.in);
+          b.coll.packed_out.push_back(c.out);
+          off += (p_->slots[c.in].bytes + 255) / 256 * 256;
+          packed[k - i] = true;
+        }
+        const int64_t esz = DTBytes(b.coll.dt);
+        b.coll.send_count = b.coll.recv_count = total / esz;
+        b.label = "all_reduce packed x" + std::to_string(kv.second.size()) + " (" + std::to_string(total) + " bytes)" +
+                  (b.coll.group >= 0 ? " [group " + std::to_string(b.coll.group) + "]" : "");
+        buckets.push_back(std::move(b));
+      }
+      for (size_t k = i; k < j; ++k)
+        if (!packed[k - i]) out.push_back(std::move(steps[k]));
+      for (Step& b : buckets) out.push_back(std::move(b));
+      i = j;
+    }
+    steps = std::move(out);
+  }
+
   // Collectives of a multi-process program run on the communication stream; the first step that
   // reads a collective's result waits for it (later readers are ordered behind that step).
   std::vector<int> coll_until_;   // step index -> step that waits for it (async collectives)
@@ -4047,7 +4128,9 @@ class Lowerer {
       c.async = true;
       for (int j = k + 1; j < (int)p_->steps.size(); ++j) {
         const std::vector<int> rd = StepReads(p_->steps[j]);
-        if (std::find(rd.begin(), rd.end(), c.coll.out) != rd.end()) {
+        bool reads = std::find(rd.begin(), rd.end(), c.coll.out) != rd.end();
+        for (int x : c.coll.packed_out) reads = reads || std::find(rd.begin(), rd.end(), x) != rd.end();
+        if (reads) {
           p_->steps[j].wait_coll.push_back(k);
           coll_until_[k] = j;
           break;
@@ -4086,6 +4169,8 @@ class Lowerer {
           const int until = st.async && i < (int)coll_until_.size() ? std::max(i, coll_until_[i]) : i;
           touch(st.coll.in, until);
           touch(st.coll.out, until);
+          for (int x : st.coll.packed_in) touch(x, until);
+          for (int x : st.coll.packed_out) touch(x, until);
           break;
         }
         case StepKind::kCopy: touch(st.copy.src, i); touch(st.copy.dst, i); break;

@@ -20,6 +20,8 @@ struct Slot {
   int const_index = -1;        // bound to uploaded constant k (owned by the executable)
   bool output = false;         // handed to the caller as an output buffer
   int last_use = -1;           // index of the last step that reads it (-1: never read)
+  int alias_of = -1;           // lives inside slot alias_of, at byte offset alias_off (a packed bucket)
+  int64_t alias_off = 0;
 };
 
 enum class StepKind { kFusion, kGemm, kAttention, kAttentionBwd, kScatterAdd, kCollective, kCopy };
@@ -91,6 +93,9 @@ struct CollectiveStep {
   int64_t send_count = 0, recv_count = 0;
   DT dt = DT::kF32;
   int group = -1;              // consecutive steps with one group id go to NCCL as one group
+  // a packed all-reduce: in = out = a bucket slot holding these members' inputs (reduced in place
+  // into their outputs, which alias the same bytes)
+  std::vector<int> packed_in, packed_out;
 };
 
 struct CopyStep {

@@ -233,7 +233,11 @@ static void StepSlots(const Step& S, std::vector<int>* out) {
       add({S.bwd.q, S.bwd.k, S.bwd.v, S.bwd.o, S.bwd.dout, S.bwd.lse, S.bwd.dq, S.bwd.dk, S.bwd.dv, S.bwd.dq_acc, S.bwd.delta});
       break;
     case StepKind::kScatterAdd: add({S.scatter.base, S.scatter.idx, S.scatter.upd, S.scatter.out}); break;
-    case StepKind::kCollective: add({S.coll.in, S.coll.out}); break;
+    case StepKind::kCollective:
+      add({S.coll.in, S.coll.out});
+      for (int s : S.coll.packed_in) add({s});
+      for (int s : S.coll.packed_out) add({s});
+      break;
     case StepKind::kCopy: add({S.copy.src, S.copy.dst}); break;
   }
 }
@@ -253,10 +257,19 @@ static int64_t LayoutArena(const Plan& P, std::vector<int64_t>* off) {
     }
   }
   off->assign(n, -1);
+  // a slot living inside a bucket (alias_of) takes no space of its own; the bucket lives from the
+  // first to the last step touching any of its members
+  for (size_t s = 0; s < n; ++s) {
+    const int b = P.slots[s].alias_of;
+    if (b < 0 || first[s] < 0) continue;
+    last[s] = std::max(last[s], P.slots[s].last_use);
+    first[b] = first[b] < 0 ? first[s] : std::min(first[b], first[s]);
+    last[b] = std::max(last[b], last[s]);
+  }
   std::vector<int> order;
   for (size_t s = 0; s < n; ++s) {
     const Slot& sl = P.slots[s];
-    if (sl.arg_index >= 0 || sl.const_index >= 0 || sl.output || first[s] < 0) continue;
+    if (sl.arg_index >= 0 || sl.const_index >= 0 || sl.output || sl.alias_of >= 0 || first[s] < 0) continue;
     last[s] = std::max(last[s], sl.last_use);
     order.push_back((int)s);
   }
@@ -446,6 +459,17 @@ std::string Executable::Run(DeviceState& dev, const std::vector<const void*>& ar
   for (size_t s = 0; s < P.slots.size(); ++s) {
     if (P.slots[s].const_index >= 0) ptr[s] = pd->consts[P.slots[s].const_index];
     else if (pd->arena_off[s] >= 0) ptr[s] = (char*)pd->arena + pd->arena_off[s];
+  }
+  // slots that live inside a packed bucket
+  for (size_t s = 0; s < P.slots.size(); ++s) {
+    const int b = P.slots[s].alias_of;
+    if (b < 0) continue;
+    if (!ptr[b]) {
+      std::string e = DeviceAlloc((size_t)P.slots[b].bytes, dev.stream, &ptr[b]);
+      if (!e.empty()) return e;
+      owned[b] = true;
+    }
+    ptr[s] = (char*)ptr[b] + P.slots[s].alias_off;
   }
   // results written in place of donated arguments
   std::vector<bool> in_place(args.size(), false);

@@ -31,6 +31,7 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <tuple>
 #include <vector>
 
 #include "../../../include/b200_kernels.h"
@@ -345,6 +346,22 @@ struct PJRT_Memory {
   const std::string& kind() const { return kSpaceKind[(int)space]; }
 };
 
+// Pinned host staging for small host-to-device uploads: the caller's bytes are copied here at once,
+// so the call can release the caller's memory without waiting for the device stream to reach the
+// copy (which queues behind every execution already enqueued).  A ring of 16 MiB; a range is
+// reused once the copy that last read it has completed.
+struct UploadStaging {
+  static constexpr size_t kCap = 16u << 20, kMaxItem = 1u << 20;
+  std::mutex mu;
+  uint8_t* base = nullptr;
+  size_t head = 0;
+  std::deque<std::tuple<size_t, size_t, cudaEvent_t>> busy;   // (offset, bytes, copy done)
+  ~UploadStaging() {
+    for (auto& b : busy) cudaEventDestroy(std::get<2>(b));
+    if (base) cudaFreeHost(base);
+  }
+};
+
 struct PJRT_Device {
   PJRT_DeviceDescription desc;
   PJRT_Client* client = nullptr;
@@ -353,6 +370,7 @@ struct PJRT_Device {
   PJRT_Memory* space_list[2] = {nullptr, nullptr};
   b200::DeviceState cuda;               // executor state of the local device
   std::mutex launch_mu;                 // serializes Execute's enqueue on this device
+  UploadStaging staging;
   bool local() const { return ordinal >= 0; }
   PJRT_Memory* hbm() { return &spaces[(int)Space::kHbm]; }
 };
@@ -610,6 +628,55 @@ PJRT_Error* CreateClient(PJRT_Client_Create_Args* a) {
 }
 
 // ======================================================================================= transfers
+// Copies `bytes` of host data into device d's staging ring (waiting, rarely, for the copy that last
+// read the range) and returns its address in *src; the ring stays locked until StagedCopyIssued
+// records the completion of the copy that reads it.
+bool Stage(PJRT_Device* d, const void* data, size_t bytes, const void** src) {
+  UploadStaging& g = d->staging;
+  g.mu.lock();
+  if (!g.base) {
+    void* b = nullptr;
+    if (cudaHostAlloc(&b, UploadStaging::kCap, cudaHostAllocPortable) != cudaSuccess) {
+      cudaGetLastError();
+      g.mu.unlock();
+      return false;
+    }
+    g.base = (uint8_t*)b;
+  }
+  size_t off = (g.head + 255) & ~(size_t)255;
+  if (off + bytes > UploadStaging::kCap) off = 0;
+  // wait for (and forget) the earlier copies that read any byte of [off, off + bytes)
+  for (auto it = g.busy.begin(); it != g.busy.end();) {
+    const size_t o = std::get<0>(*it), n = std::get<1>(*it);
+    if (o < off + bytes && off < o + n) {
+      cudaEventSynchronize(std::get<2>(*it));
+      cudaEventDestroy(std::get<2>(*it));
+      it = g.busy.erase(it);
+    } else {
+      ++it;
+    }
+  }
+  std::memcpy(g.base + off, data, bytes);
+  g.head = off + bytes;
+  g.busy.push_back({off, bytes, nullptr});
+  *src = g.base + off;
+  return true;
+}
+
+void StagedCopyIssued(PJRT_Device* d) {
+  UploadStaging& g = d->staging;
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess) {
+    cudaEventRecord(e, d->cuda.stream);
+    std::get<2>(g.busy.back()) = e;
+  } else {
+    cudaGetLastError();
+    cudaStreamSynchronize(d->cuda.stream);    // no event: let the copy finish before the range is reused
+    g.busy.pop_back();
+  }
+  g.mu.unlock();
+}
+
 PJRT_Error* FromHost(PJRT_Client_BufferFromHostBuffer_Args* a) {
   const size_t width = ElementBytes(a->type);
   if (width == 0) return Fail(PJRT_Error_Code_UNIMPLEMENTED, "BufferFromHostBuffer: unsupported element type");
@@ -641,12 +708,25 @@ PJRT_Error* FromHost(PJRT_Client_BufferFromHostBuffer_Args* a) {
     if (bytes) std::memcpy(p, a->data, bytes);
     done = Completion::Done();
   } else {
-    if (bytes && cudaMemcpyAsync(p, a->data, bytes, cudaMemcpyHostToDevice, d->cuda.stream) != cudaSuccess) {
+    const void* src = a->data;
+    bool staged = false;
+    if (bytes && bytes <= UploadStaging::kMaxItem) staged = Stage(d, a->data, bytes, &src);
+    if (bytes && cudaMemcpyAsync(p, src, bytes, cudaMemcpyHostToDevice, d->cuda.stream) != cudaSuccess) {
       cudaGetLastError();
+      if (staged) {
+        d->staging.busy.pop_back();
+        d->staging.mu.unlock();
+      }
       b200::DeviceFree(p, d->cuda.stream);
       return Fail(PJRT_Error_Code_INTERNAL, "BufferFromHostBuffer: host to device copy failed");
     }
     done = Completion::After(d->ordinal, d->cuda.stream, false);
+    if (staged) {
+      StagedCopyIssued(d);
+      a->buffer = NewBuffer(a->client, m, a->type, std::vector<int64_t>(a->dims, a->dims + a->num_dims), bytes, p, done);
+      a->done_with_host_buffer = new PJRT_Event{Completion::Done()};   // the caller's bytes are copied
+      return nullptr;
+    }
     // the caller may reuse its host memory when this call returns
     if (a->host_buffer_semantics == PJRT_HostBufferSemantics_kImmutableOnlyDuringCall) done->Wait();
   }

@@ -260,9 +260,10 @@ def test_collectives_across_processes_need_one_world_group(lib_path, groups, ok)
         assert rc == 1 and "replica_groups" in rep, rep
 
 
-def test_small_all_reduces_are_issued_as_nccl_groups(lib_path):
+def test_small_all_reduces_are_issued_as_nccl_groups(lib_path, monkeypatch):
     """Across processes, the DP step's small gradient all-reduces (<= 256 KiB) are held back and
     issued together as NCCL groups; large ones keep their hoisted places."""
+    monkeypatch.setenv("B200_NO_PACK", "1")
     p = configs.gpt2_program(batch=2, world=2, layers=2, d=64, heads=2, mlp=128, vocab=96, seq=64, with_inputs=False)
     rc, rep = report(lib_path, p.text, nprocs=2)
     assert rc == 0, rep
@@ -380,3 +381,23 @@ def test_cross_entropy_backward_joins_its_forward_row_walk(lib_path, monkeypatch
     monkeypatch.setenv("B200_NO_DEFER", "1")
     rc, rep = report(lib_path, p.text)
     assert rc == 0 and len([l for l in rep.splitlines() if "tensor<128x1000xf32>" in l]) == 2, rep
+
+
+@pytest.mark.parametrize("bucket", ["", "all"])
+def test_grouped_all_reduces_are_packed_into_one_bucket(lib_path, monkeypatch, bucket):
+    """The all-reduces of one NCCL group (one type, one reduction) become a single all-reduce over a
+    bucket that their inputs and outputs live in; with B200_COLL_BUCKET=all every gradient of the
+    step is held for it.  Every gradient is still reduced exactly once: the packed members' bytes
+    (each rounded up to 256) add up to the buckets."""
+    import re
+    if bucket:
+        monkeypatch.setenv("B200_COLL_BUCKET", bucket)
+    p = configs.gpt2_program(batch=2, world=2, layers=2, d=64, heads=2, mlp=128, vocab=96, seq=64, with_inputs=False)
+    rc, rep = report(lib_path, p.text, nprocs=2)
+    assert rc == 0, rep
+    colls = [l for l in rep.splitlines() if "all_reduce" in l]
+    packed = [l for l in colls if "packed" in l]
+    members = sum(int(re.search(r"packed x(\d+)", l).group(1)) for l in packed)
+    assert packed and members + len(colls) - len(packed) == 29, rep   # 28 gradients + the loss
+    if bucket == "all":
+        assert len(colls) <= 8, rep
