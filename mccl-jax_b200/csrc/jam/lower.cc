@@ -2077,10 +2077,29 @@ class Lowerer {
         if (join_row(r)) continue;
         flush();
       }
+      // a value computed from the open column reductions' results alone (a gradient rounded to bf16
+      // for its all_reduce) waits behind them, so a later sibling reduction still joins their kernel
+      if (defer_ok && !colred.empty() && pending.empty() && FromColumnReductions(op, colred, tainted)) {
+        deferred.push_back(op);
+        tainted.insert(r->id);
+        continue;
+      }
       if (!pending.empty() && (pending[0]->type.dims != r->type.dims)) flush();
       pending.push_back(r);
     }
     flush();
+  }
+
+  // True if every operand of `op` is the result of one of `group`'s reductions or a value already
+  // held back behind them.
+  bool FromColumnReductions(const Op* op, const std::vector<Op*>& group, const std::unordered_set<int>& held) const {
+    if (op->operands.empty()) return false;
+    for (const Value* o : op->operands) {
+      if (held.count(o->id) || held.count(Resolve(o)->id)) continue;
+      const Op* d = Resolve(o)->def;
+      if (!d || std::find(group.begin(), group.end(), d) == group.end()) return false;
+    }
+    return true;
   }
 
   void CheckGather(const Op* op) {

@@ -401,3 +401,19 @@ def test_grouped_all_reduces_are_packed_into_one_bucket(lib_path, monkeypatch, b
     assert packed and members + len(colls) - len(packed) == 29, rep   # 28 gradients + the loss
     if bucket == "all":
         assert len(colls) <= 8, rep
+
+
+def test_sibling_column_reductions_stay_merged_when_rounded_for_all_reduce(lib_path, monkeypatch):
+    """Across processes each LayerNorm's two parameter gradients (column sums over the same rows) are
+    rounded to bf16 for their all_reduce.  The roundings wait behind the open column-reduction group,
+    so the second sum still joins the first one's kernel (one read of the shared dy) and the two
+    roundings share a launch; without the hold-back every sum runs alone."""
+    p = configs.gpt2_program(batch=2, world=2, layers=2, d=64, heads=2, mlp=128, vocab=96, seq=64, with_inputs=False)
+    rc, rep = report(lib_path, p.text, nprocs=2)
+    assert rc == 0, rep
+    sums = [l for l in rep.splitlines() if "-> tensor<64xf32>" in l and "all_reduce" not in l]
+    assert len(sums) == 5 and all("reduce x2" in l for l in sums), rep
+    monkeypatch.setenv("B200_NO_DEFER", "1")
+    rc, rep = report(lib_path, p.text, nprocs=2)
+    sums = [l for l in rep.splitlines() if "-> tensor<64xf32>" in l and "all_reduce" not in l]
+    assert rc == 0 and len(sums) == 10 and not any("reduce x2" in l for l in sums), rep

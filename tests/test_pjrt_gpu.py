@@ -589,3 +589,28 @@ def test_device_lookup_and_default_assignment(client):
     with pytest.raises(pjrt.PjrtError):
         client.lookup_device(len(devs))
     assert client.default_device_assignment(1, 1) == [0]
+
+
+@pytest.mark.parametrize("rows,cols", [(8192, 768), (300, 72)])
+def test_rounded_sibling_column_sums(client, lib_path, rows, cols):
+    """Two column sums over the same rows, each rounded to bf16 as a program output (a LayerNorm's
+    parameter gradients as the all_reduce receives them): one merged reduction kernel and one launch
+    for both roundings, results against the oracle at the bf16 bar."""
+    import ctypes
+    b = Builder("jit_rounded_sums")
+    dy = b.arg((rows, cols), "f32")
+    xh = b.arg((rows, cols), "f32")
+    g = b.convert(b.reduce(dy * xh, [0]), "bf16")
+    s = b.convert(b.reduce(dy, [0]), "bf16")
+    text = b.text([g, s])
+    lib = ctypes.CDLL(lib_path)
+    buf = ctypes.create_string_buffer(1 << 16)
+    assert lib.b200_compile_report(text.encode(), len(text), 1, 0, buf, len(buf)) == 0
+    rep = buf.value.decode()
+    assert "reduce x2" in rep and f"loop tensor<{cols}xbf16> x2" in rep, rep
+    rng = np.random.default_rng(rows + cols)
+    ins = [rng.standard_normal((rows, cols)).astype(np.float32), rng.standard_normal((rows, cols)).astype(np.float32)]
+    outs = client.run(text, ins)
+    refs = oracle_run(text, ins)
+    for o, r, name in zip(outs, refs, ("dgamma", "dbeta")):
+        assert_close(np.asarray(o, np.float32), np.asarray(r, np.float32), RTOL_BF16, name)
